@@ -1,0 +1,408 @@
+#!/usr/bin/env python3
+"""Benchmark of the emmy B200 backend on BASELINE.json's configurations.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config c2|c3|c4|c5]
+
+One JSON line on stdout (rank 0).  A "step" is one pass of the hot path over
+one batch: one launch of the KernelOp compiled from the config's IR, on
+inputs already resident in HBM (``value``), and the same call through the
+C ABI on pinned host buffers with the copies inside the timed region
+(``e2e``).  The default workload is BASELINE configs[1] (the metric's
+HBM-bound pointwise chain, y = GELU_tanh(x*s + t) on f32 [16384, 16384]).
+Under torchrun every rank runs its own full-size shard (weak scaling, no
+data-path collective) and the slowest rank's device time is reported.
+
+``--impl reference`` times the reference's CPU restatement (oracle/) on
+the host cores, for the same metric, on a bounded sample per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+CASES = REPO / "tests" / "golden" / "cases"
+METRIC = "HBM GB/s (pointwise/reduce), GEMM TFLOP/s; % of B200 roofline at 1/2/4/8 GPU"
+sys.path.insert(0, str(REPO))
+
+CONFIGS = {
+    # name: (case dir, unit, bound, algorithmic units per launch, workload text)
+    "c2": ("c2_gelu_full", "GB/s", "hbm", 2 * (1 << 28) * 4 + 2 * 16384 * 4,
+           "BASELINE configs[1]: y = GELU_tanh(x*s + t), x f32 [16384, 16384], s,t f32 [16384]"),
+    "c3": ("c3_rowsummax_full", "GB/s", "hbm", (1 << 31) + 2 * 8192 * 4,
+           "BASELINE configs[2]: row sum and max of f32 [8192, 65536]"),
+    "c4": ("c4_sum_full", "GB/s", "hbm", (1 << 33) + 4,
+           "BASELINE configs[3]: sum of f32 [2^31]"),
+    "c5": ("c5_gemm_full", "TFLOP/s", "tensor", 2 * 16384 * 16384 * 8192,
+           "BASELINE configs[4]: relu(A@B + bias), A bf16 [16384, 8192], B bf16 [8192, 16384]"),
+}
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def peaks() -> tuple[dict, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.is_file():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except json.JSONDecodeError:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.QUERY}", "--format=csv,noheader",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+
+    def summary(self) -> dict:
+        sm, smax, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1].split()[0]))
+                smax = max(smax, float(parts[2].split()[0]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------- inputs
+
+
+def make_inputs(cfg: str, spec, rank: int, device: str):
+    """Seeded synthetic inputs with the config's shapes and distributions
+    (generated on the device; per-rank seeds for weak scaling)."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(1234 + 7919 * rank)
+    out = {}
+    for name in spec.arg_order:
+        a = spec.args[name]
+        shape = tuple(a["shape"]) or (1,)
+        dt = {"f32": torch.float32, "bf16": torch.bfloat16}[a.get("dtype", "f32")]
+        if a.get("output"):
+            out[name] = torch.empty(shape, dtype=dt, device=device)
+            continue
+        init = a.get("init", {"kind": "normal", "std": 1.0, "mean": 0.0})
+        if init["kind"] == "uniform":
+            t = torch.empty(shape, dtype=torch.float32, device=device)
+            t.uniform_(init["low"], init["high"], generator=g)
+        else:
+            t = torch.randn(shape, dtype=torch.float32, device=device, generator=g)
+            t.mul_(init.get("std", 1.0)).add_(init.get("mean", 0.0))
+        out[name] = t.to(dt)
+    return out
+
+
+# ---------------------------------------------------------------------------- our arm
+
+
+def run_ours(args, rank: int, world: int, local: int) -> dict | None:
+    import torch
+    from emmy_ptx_compiler_b200 import compiler, harness, runtime
+
+    device = f"cuda:{local}"
+    torch.cuda.set_device(local)
+    case_id, unit, bound, units, workload = CONFIGS[args.config]
+    spec = harness.load_case(CASES / case_id)
+    bundle = compiler.compile_bundle(spec.ir_path, want_cubin=True)
+    runtime.init(local)
+    mod = runtime.Module(bundle["cubin"], spec.entry, local)
+    bufs = make_inputs(args.config, spec, rank, device)
+    order = [bufs[n] for n in spec.arg_order]
+    stream = torch.cuda.current_stream(local).cuda_stream
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    for _ in range(args.warmup):
+        mod.launch(order, stream=stream)
+    torch.cuda.synchronize(local)
+    st = mod.status()
+    if st:
+        raise RuntimeError(f"kernel status 0x{st:x} during warm-up")
+    barrier()
+    torch.cuda.synchronize(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            mod.launch(order, stream=stream)
+        e1.record()
+        torch.cuda.synchronize(local)
+    barrier()
+    ms = e0.elapsed_time(e1)
+    ms_t = torch.tensor([ms], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    per_launch_ms = ms_max / args.steps
+    value = units * world * args.steps / (ms_max / 1e3) / (1e9 if unit == "GB/s" else 1e12)
+    achieved = units / (per_launch_ms / 1e3) / (1e9 if unit == "GB/s" else 1e12)
+    pk, pk_kind = peaks()
+    peak = pk["hbm_gbs"] if bound == "hbm" else pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+    traffic = None
+    tfile = REPO / "profiles" / "traffic.json"
+    if tfile.is_file():
+        traffic = json.loads(tfile.read_text()).get(case_id)
+
+    # e2e: the C-ABI host-buffer call, copies in the timed region
+    host = {}
+    nbytes, roles, ptrs = [], [], []
+    for name in spec.arg_order:
+        t = bufs[name]
+        h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+        if not spec.args[name].get("output"):
+            h.copy_(t)
+        host[name] = h
+        ptrs.append(h.data_ptr())
+        nbytes.append(h.numel() * h.element_size())
+        roles.append(runtime.EMMY_ROLE_OUT if spec.args[name].get("output") else runtime.EMMY_ROLE_IN)
+    e2e_steps = max(1, min(args.steps, 5))
+    mod.run_host(ptrs, nbytes, roles, stream=stream)  # warm the module's device buffers
+    barrier()
+    torch.cuda.synchronize(local)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        mod.run_host(ptrs, nbytes, roles, stream=stream)
+    e2e_s = time.perf_counter() - t0
+    e2e_t = torch.tensor([e2e_s], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(e2e_t, op=torch.distributed.ReduceOp.MAX)
+    e2e_s = float(e2e_t.item())
+    h2d = sum(b for b, r in zip(nbytes, roles) if r == runtime.EMMY_ROLE_IN)
+    d2h = sum(b for b, r in zip(nbytes, roles) if r == runtime.EMMY_ROLE_OUT)
+    e2e_value = units * world * e2e_steps / e2e_s / (1e9 if unit == "GB/s" else 1e12)
+
+    ref_ptx = None
+    if rank == 0 and world == 1 and args.config == "c2" and not args.no_ref_ptx:
+        ref_ptx = time_reference_ptx(spec, bufs, local, units, unit)
+
+    mod.close()
+    if rank != 0:
+        return None
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32" if args.config != "c5" else "bf16",
+        "data": "synthetic (seeded on device, BASELINE distributions)",
+        "config": {"workload": workload, "case": case_id, "rows_per_rank": spec.args[spec.arg_order[0]]["shape"][0],
+                   "parallelism": f"{world} ranks, each its own full-size shard; no collective",
+                   "l2": "inputs larger than L2 (126 MB), no flush needed",
+                   "launch": bundle["launch"]},
+        "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": peak,
+                     "unit": unit, "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "peak_source": f"{pk_kind} ({'hbm_gbs' if bound == 'hbm' else 'bf16_tflops'})",
+                     "units_per_launch": units},
+        "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                "path": "emmy_run_host (C ABI) on pinned host buffers"},
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+    }
+    if ref_ptx is not None:
+        line["reference_ptx_gpu"] = ref_ptx
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.config, seconds=args.cpu_seconds)
+    return line
+
+
+def time_reference_ptx(spec, bufs, local: int, units: int, unit: str) -> dict:
+    """The reference compiler's own PTX for the same IR on the same B200
+    (JIT-loaded, meta.json launch), on the same device buffers."""
+    import torch
+    from emmy_ptx_compiler_b200 import runtime
+    ref = spec.root / "ref.ptx"
+    if not ref.is_file():
+        return {"unavailable": "no reference PTX for this IR"}
+    mod = runtime.Module(ref.read_bytes(), spec.entry, local)
+    g, b = spec.kernel["grid"], spec.kernel["block"]
+    order = [bufs[n] for n in spec.arg_order]
+    stream = torch.cuda.current_stream(local).cuda_stream
+    for _ in range(3):
+        mod.launch(order, stream=stream, grid=g, block=b)
+    torch.cuda.synchronize(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 5
+    e0.record()
+    for _ in range(n):
+        mod.launch(order, stream=stream, grid=g, block=b)
+    e1.record()
+    torch.cuda.synchronize(local)
+    ms = e0.elapsed_time(e1) / n
+    mod.close()
+    return {"value": round(units / (ms / 1e3) / (1e9 if unit == "GB/s" else 1e12), 2), "unit": unit,
+            "ms_per_launch": round(ms, 4), "launch": {"grid": g, "block": b}}
+
+
+# ---------------------------------------------------------------------------- CPU arms
+
+
+def _oracle_sample(cfg: str, rows: int):
+    """(callable, algorithmic units it processes) for a bounded CPU sample."""
+    import numpy as np
+    sys.path.insert(0, str(REPO / "oracle"))
+    import interp
+    case_id, unit, bound, units, _ = CONFIGS[cfg]
+    kop, meta, mk, shapes, dtypes = interp.load_case(CASES / case_id)
+    rng = np.random.default_rng(0)
+    if cfg == "c2":
+        cols = 16384
+        shp = dict(shapes, x=(rows, cols), y=(rows, cols))
+        ins = {"x": rng.standard_normal((rows, cols), dtype=np.float32),
+               "s": rng.uniform(0.5, 1.5, cols).astype(np.float32),
+               "t": rng.uniform(-0.1, 0.1, cols).astype(np.float32)}
+        body = list(kop.body)[0]
+        import copy
+        tile = copy.copy(body)
+        from emmy._core import Axis, Dim
+        tile.axes = (Axis("a0", Dim(rows)), Axis("a1", Dim(cols)))
+        kop2 = copy.copy(kop)
+        kop2.body = (tile,)
+        fn = lambda: interp.evaluate(kop2, shp, dtypes, ins, {"y": (rows, cols)})  # noqa: E731
+        return fn, rows * cols * 8 + 2 * cols * 4
+    raise ValueError(f"no CPU sample defined for {cfg}")
+
+
+def cpu_baseline(cfg: str, seconds: float = 10.0) -> dict:
+    """The oracle port on the host cores: rows split over a thread pool
+    (numpy and the oracle's C loops release the GIL)."""
+    if cfg != "c2":
+        return {"unavailable": f"CPU baseline for {cfg} not wired"}
+    threads = len(os.sched_getaffinity(0))
+    rows_per_task = 16
+    fn, units = _oracle_sample(cfg, rows_per_task)
+    fn()  # warm
+    done_units = 0
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        while time.perf_counter() - t0 < seconds:
+            list(ex.map(lambda _: fn(), range(threads)))
+            done_units += units * threads
+    el = time.perf_counter() - t0
+    return {"value": round(done_units / el / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"oracle/interp.py GELU chain, {threads} threads x {rows_per_task} rows of 16384 "
+                      f"per round, {el:.1f} s of rounds"}
+
+
+def run_reference(args, rank: int) -> dict | None:
+    if rank != 0:
+        return None
+    case_id, unit, bound, units, workload = CONFIGS[args.config]
+    if args.config != "c2":
+        return {"impl": "reference", "unavailable": f"reference CPU arm not wired for {args.config}"}
+    threads = len(os.sched_getaffinity(0))
+    rows_per_task = 16
+    fn, units_task = _oracle_sample(args.config, rows_per_task)
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        for _ in range(args.warmup):
+            list(ex.map(lambda _: fn(), range(threads)))
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            list(ex.map(lambda _: fn(), range(threads)))
+        el = time.perf_counter() - t0
+    value = units_task * threads * args.steps / el / 1e9
+    return {"metric": METRIC, "value": round(value, 3), "unit": unit, "n_gpus": 0, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": workload, "case": case_id},
+            "cpu_baseline": {"value": round(value, 3), "unit": unit, "cores": threads, "kind": "port",
+                             "sample": f"{threads} threads x {rows_per_task} rows of 16384 per step"},
+            "e2e": {"value": round(value, 3), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ref-ptx", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return 0
+    if world > 1:
+        import datetime
+        import torch
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device(f"cuda:{local}"))
+    try:
+        line = run_ours(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch
+            torch.distributed.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,171 @@
+"""Drop-in compiler surface: ``compile_ir``, ``compile_bundle``, ``Compiler``, ``main``.
+
+Mirrors the reference's L1 entry points (compile.py:3164-3227):
+
+* ``python compile.py kernel.ir.json > out.ptx`` prints one PTX module,
+  ASCII only, with one ``.visible .entry <KernelOp.name>`` whose parameters
+  are the ``meta.json`` ``arg_order`` buffers (``.u64`` pointers, or typed
+  scalars for ``args[i].scalar``), now ``.target sm_100a``;
+* wrong usage prints the usage line and exits 2; an IR this backend cannot
+  lower prints ``unsupported ...`` on stderr and exits 2 (compile.py:1516-1518);
+* ``compile_bundle`` returns the reference's keys (``ptx, entry, args, shapes,
+  dtypes, smem_bytes, dynamic_smem, block, virt_regs, stats, ops, ir_txt,
+  meta, bytes``) plus ``family``, ``launch`` (the geometry the module is
+  tuned for), ``source`` (generated CUDA) and ``notes``.
+
+Lowering replaces the reference's PTX printer (compile.py:342-3161): the
+KernelOp is classified into one of three hand-written sm_100a families,
+which emit specialised CUDA C++ that nvcc compiles.
+"""
+
+from __future__ import annotations
+
+import json
+import sys
+from dataclasses import dataclass
+from pathlib import Path
+
+from . import frontend, ir, toolchain
+from .errors import ToolchainError, UnsupportedIR
+from .families import gemm, pointwise, reduction
+from .families.common import KernelSource
+
+
+@dataclass
+class Lowered:
+    kernel: KernelSource
+    args: list[str]
+    shapes: dict
+    dtypes: dict
+    meta: dict
+
+
+def _scalars(meta: dict | None, dtypes: dict) -> dict[str, str]:
+    out: dict[str, str] = {}
+    for arg in (meta or {}).get("args") or []:
+        if arg.get("scalar"):
+            dt = ir.canon_dtype(arg.get("dtype") or dtypes.get(arg.get("name")))
+            out[arg["name"]] = "f32" if dt == "f32" else "i32"
+    return out
+
+
+def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: dict | None) -> Lowered:
+    """Classify ``kop`` into a family and generate its specialised source."""
+    meta = meta or {}
+    written = {s.output for s in ir.walk(kop.body) if isinstance(s, ir.Write)}
+    scalars = _scalars(meta, dtypes)
+    for name in args:
+        if name not in scalars and name not in shapes and name not in dtypes:
+            raise UnsupportedIR(f"parameter {name!r} has no shape or dtype")
+    plan = gemm.match(kop, shapes, dtypes)
+    if plan is not None:
+        ks = gemm.generate(kop, plan, shapes, dtypes, args, scalars, written)
+        return Lowered(ks, args, shapes, dtypes, meta)
+    plan = reduction.match(kop, shapes, dtypes)
+    if plan is not None:
+        ks = reduction.generate(kop, plan, shapes, dtypes, args, scalars, written)
+        return Lowered(ks, args, shapes, dtypes, meta)
+    plan = pointwise.match(kop)
+    if plan is not None:
+        ks = pointwise.generate(kop, plan, shapes, dtypes, args, scalars, written)
+        return Lowered(ks, args, shapes, dtypes, meta)
+    kinds = sorted({type(s).__name__ for s in ir.walk(kop.body)})
+    raise UnsupportedIR(f"KernelOp {kop.name!r} is not a pointwise, reduction or GEMM kernel "
+                        f"(nodes: {', '.join(kinds)})")
+
+
+class Compiler:
+    """``Compiler(kop, shapes, dtypes, args, meta).run() -> ptx``, the
+    constructor the reference's tests use (compile.py:410-411, 823)."""
+
+    def __init__(self, kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str],
+                 meta: dict | None = None):
+        self.kop = kop
+        self.shapes = {k: tuple(int(x) for x in v) for k, v in shapes.items()}
+        self.dtypes = dict(dtypes)
+        self.args = list(args)
+        self.meta = meta or {}
+        self.lowered: Lowered | None = None
+
+    def lower(self) -> Lowered:
+        if self.lowered is None:
+            self.lowered = lower(self.kop, self.shapes, self.dtypes, self.args, self.meta)
+        return self.lowered
+
+    def run(self) -> str:
+        ks = self.lower().kernel
+        return toolchain.build(ks.source, "ptx", name=ks.entry).decode("ascii")
+
+    def cubin(self) -> bytes:
+        ks = self.lower().kernel
+        return toolchain.build(ks.source, "cubin", name=ks.entry)
+
+
+def _bundle_from(kop: ir.KernelOp, raw: dict | None, meta_k: dict | None, path: Path | None,
+                 want_cubin: bool = False) -> dict:
+    args = frontend.arg_order_for(kop, meta_k)
+    shapes, dtypes = frontend.load_shapes(raw, kop, meta_k)
+    comp = Compiler(kop, shapes, dtypes, args, meta_k)
+    low = comp.lower()
+    ks = low.kernel
+    ptx = comp.run()
+    ir_txt = ""
+    if path is not None:
+        for cand in (path.with_suffix(".txt"), path.parent / (path.stem + ".ir.txt")):
+            if cand.is_file():
+                ir_txt = cand.read_text(encoding="utf-8")
+                break
+    mix: dict[str, int] = {}
+    out = {
+        "ptx": ptx,
+        "entry": kop.name,
+        "args": args,
+        "shapes": {k: list(v) for k, v in shapes.items()},
+        "dtypes": dtypes,
+        "smem_bytes": ks.launch.smem,
+        "dynamic_smem": ks.launch.smem > 48 * 1024,
+        "block": ks.launch.block[0] * ks.launch.block[1] * ks.launch.block[2],
+        "virt_regs": {},
+        "stats": {"family": ks.family, **{k: v for k, v in ks.notes.items() if isinstance(v, (int, bool))}},
+        "ops": mix,
+        "ir_txt": ir_txt,
+        "meta": meta_k or {},
+        "bytes": len(ptx.encode("ascii", "replace")),
+        "family": ks.family,
+        "launch": {"grid": list(ks.launch.grid), "block": list(ks.launch.block), "smem": ks.launch.smem},
+        "params": [{"name": p.name, "kind": p.kind, "dtype": p.dtype} for p in ks.params],
+        "source": ks.source,
+        "notes": ks.notes,
+    }
+    if want_cubin:
+        out["cubin"] = comp.cubin()
+    return out
+
+
+def compile_bundle(path, want_cubin: bool = False) -> dict:
+    path = Path(path)
+    raw = json.loads(path.read_text(encoding="utf-8"))
+    info = frontend.load_graph(raw)
+    meta_k = frontend.load_meta_kernel(path, info.kop.name)
+    return _bundle_from(info.kop, raw, meta_k, path, want_cubin)
+
+
+def compile_ir(path) -> str:
+    return compile_bundle(path)["ptx"]
+
+
+def main(argv: list[str] | None = None) -> int:
+    argv = list(sys.argv if argv is None else argv)
+    if len(argv) != 2:
+        print("usage: python compile.py path/to/kernel.ir.json", file=sys.stderr)
+        return 2
+    try:
+        ptx = compile_ir(Path(argv[1]))
+    except UnsupportedIR as exc:
+        print(f"unsupported: {exc}", file=sys.stderr)
+        return 2
+    except ToolchainError as exc:
+        print(f"toolchain error: {exc}", file=sys.stderr)
+        return 3
+    sys.stdout.write(ptx)
+    return 0

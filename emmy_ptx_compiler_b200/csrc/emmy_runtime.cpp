@@ -1,0 +1,795 @@
+// libemmy_b200: module loading, launching, host-buffer runs, timing and NCCL
+// collectives behind the C ABI declared in include/emmy_b200.h.
+//
+// The CUDA driver and NCCL are opened with dlopen on first use, so the
+// library loads (and its symbols can be inspected) on machines without a GPU
+// driver.  Every entry point returns a status code and records a message
+// for emmy_last_error(); nothing aborts.
+
+#include "emmy_b200.h"
+#include "emmy_launch_record.h"
+
+#include <cuda.h>
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <chrono>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <unordered_map>
+#include <vector>
+
+namespace {
+
+// ------------------------------------------------------------------ errors
+
+thread_local std::string g_err;
+thread_local int g_err_code = EMMY_OK;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    g_err_code = code;
+    return code;
+}
+
+// ------------------------------------------------------------------ driver table
+
+struct Driver {
+    void *lib = nullptr;
+    bool ok = false;
+#define EMMY_DRV(name) decltype(&::name) name = nullptr;
+    EMMY_DRV(cuInit)
+    EMMY_DRV(cuDeviceGetCount)
+    EMMY_DRV(cuDeviceGet)
+    EMMY_DRV(cuDevicePrimaryCtxRetain)
+    EMMY_DRV(cuCtxSetCurrent)
+    EMMY_DRV(cuCtxSynchronize)
+    EMMY_DRV(cuModuleLoadDataEx)
+    EMMY_DRV(cuModuleUnload)
+    EMMY_DRV(cuModuleGetFunction)
+    EMMY_DRV(cuModuleGetGlobal)
+    EMMY_DRV(cuFuncSetAttribute)
+    EMMY_DRV(cuFuncGetParamInfo)
+    EMMY_DRV(cuLaunchKernel)
+    EMMY_DRV(cuLaunchKernelEx)
+    EMMY_DRV(cuMemAlloc)
+    EMMY_DRV(cuMemFree)
+    EMMY_DRV(cuMemAllocHost)
+    EMMY_DRV(cuMemFreeHost)
+    EMMY_DRV(cuMemcpyHtoD)
+    EMMY_DRV(cuMemcpyDtoH)
+    EMMY_DRV(cuMemcpyHtoDAsync)
+    EMMY_DRV(cuMemcpyDtoHAsync)
+    EMMY_DRV(cuMemsetD8Async)
+    EMMY_DRV(cuStreamQuery)
+    EMMY_DRV(cuStreamSynchronize)
+    EMMY_DRV(cuEventCreate)
+    EMMY_DRV(cuEventRecord)
+    EMMY_DRV(cuEventSynchronize)
+    EMMY_DRV(cuEventElapsedTime)
+    EMMY_DRV(cuEventDestroy)
+    EMMY_DRV(cuGetErrorString)
+    EMMY_DRV(cuTensorMapEncodeTiled)
+#undef EMMY_DRV
+};
+
+Driver g_drv;
+std::mutex g_mu;
+std::vector<CUcontext> g_ctx;  // primary context per device
+bool g_init = false;
+
+typedef CUresult (*GetProcAddressFn)(const char *, void **, int, cuuint64_t,
+                                     CUdriverProcAddressQueryResult *);
+
+int load_driver() {
+    if (g_drv.ok) return EMMY_OK;
+    if (!g_drv.lib) g_drv.lib = dlopen("libcuda.so.1", RTLD_NOW | RTLD_GLOBAL);
+    if (!g_drv.lib) return fail(EMMY_ERR_NO_DRIVER, "cannot open libcuda.so.1: %s", dlerror());
+    auto gpa = reinterpret_cast<GetProcAddressFn>(dlsym(g_drv.lib, "cuGetProcAddress_v2"));
+    if (!gpa) return fail(EMMY_ERR_NO_DRIVER, "libcuda.so.1 has no cuGetProcAddress_v2");
+    bool missing = false;
+    std::string which;
+    auto get = [&](const char *name, void **slot, bool required) {
+        CUdriverProcAddressQueryResult st;
+        if (gpa(name, slot, 12090, CU_GET_PROC_ADDRESS_DEFAULT, &st) != CUDA_SUCCESS || !*slot) {
+            *slot = nullptr;
+            if (required) {
+                missing = true;
+                which += std::string(" ") + name;
+            }
+        }
+    };
+#define EMMY_GET(name, req) get(#name, reinterpret_cast<void **>(&g_drv.name), req);
+    EMMY_GET(cuInit, true)
+    EMMY_GET(cuDeviceGetCount, true)
+    EMMY_GET(cuDeviceGet, true)
+    EMMY_GET(cuDevicePrimaryCtxRetain, true)
+    EMMY_GET(cuCtxSetCurrent, true)
+    EMMY_GET(cuCtxSynchronize, true)
+    EMMY_GET(cuModuleLoadDataEx, true)
+    EMMY_GET(cuModuleUnload, true)
+    EMMY_GET(cuModuleGetFunction, true)
+    EMMY_GET(cuModuleGetGlobal, true)
+    EMMY_GET(cuFuncSetAttribute, true)
+    EMMY_GET(cuFuncGetParamInfo, false)
+    EMMY_GET(cuLaunchKernel, true)
+    EMMY_GET(cuLaunchKernelEx, false)
+    EMMY_GET(cuMemAlloc, true)
+    EMMY_GET(cuMemFree, true)
+    EMMY_GET(cuMemAllocHost, true)
+    EMMY_GET(cuMemFreeHost, true)
+    EMMY_GET(cuMemcpyHtoD, true)
+    EMMY_GET(cuMemcpyDtoH, true)
+    EMMY_GET(cuMemcpyHtoDAsync, true)
+    EMMY_GET(cuMemcpyDtoHAsync, true)
+    EMMY_GET(cuMemsetD8Async, true)
+    EMMY_GET(cuStreamQuery, true)
+    EMMY_GET(cuStreamSynchronize, true)
+    EMMY_GET(cuEventCreate, true)
+    EMMY_GET(cuEventRecord, true)
+    EMMY_GET(cuEventSynchronize, true)
+    EMMY_GET(cuEventElapsedTime, true)
+    EMMY_GET(cuEventDestroy, true)
+    EMMY_GET(cuGetErrorString, true)
+    EMMY_GET(cuTensorMapEncodeTiled, false)
+#undef EMMY_GET
+    if (missing) return fail(EMMY_ERR_NO_DRIVER, "driver lacks:%s", which.c_str());
+    g_drv.ok = true;
+    return EMMY_OK;
+}
+
+int cu_fail(CUresult r, const char *what) {
+    const char *s = nullptr;
+    if (g_drv.cuGetErrorString) g_drv.cuGetErrorString(r, &s);
+    return fail(EMMY_ERR_CUDA, "%s failed: %s (%d)", what, s ? s : "?", static_cast<int>(r));
+}
+
+#define CU(call, what)                                      \
+    do {                                                    \
+        CUresult _r = (call);                               \
+        if (_r != CUDA_SUCCESS) return cu_fail(_r, what);   \
+    } while (0)
+
+int set_device(int dev) {
+    if (!g_init) return fail(EMMY_ERR_NOT_INIT, "emmy_init has not been called");
+    if (dev < 0 || dev >= static_cast<int>(g_ctx.size()) || !g_ctx[dev])
+        return fail(EMMY_ERR_NOT_FOUND, "device %d is not initialised", dev);
+    CU(g_drv.cuCtxSetCurrent(g_ctx[dev]), "cuCtxSetCurrent");
+    return EMMY_OK;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ modules
+
+struct emmy_module {
+    int dev = 0;
+    CUmodule mod = nullptr;
+    CUfunction fn = nullptr;
+    EmmyLaunchRecord rec{};
+    bool has_rec = false;
+    CUdeviceptr status = 0;
+    std::vector<size_t> param_size;  // from cuFuncGetParamInfo (may be empty)
+    // tensor-map cache: encoded for these source pointers
+    std::vector<CUtensorMap> tmaps;
+    std::vector<uint64_t> tmap_src;
+    // emmy_run_host device buffers
+    std::vector<CUdeviceptr> dbuf;
+    std::vector<size_t> dbuf_bytes;
+};
+
+namespace {
+
+int encode_tmaps(emmy_module *m, const uint64_t *args, int nargs) {
+    const uint32_t n = m->has_rec ? m->rec.ntmaps : 0;
+    if (n == 0) return EMMY_OK;
+    if (!g_drv.cuTensorMapEncodeTiled)
+        return fail(EMMY_ERR_NO_DRIVER, "driver lacks cuTensorMapEncodeTiled (needed by the GEMM family)");
+    m->tmaps.resize(n);
+    m->tmap_src.resize(n, ~0ull);
+    for (uint32_t i = 0; i < n; ++i) {
+        const EmmyTmapSpec &t = m->rec.tmaps[i];
+        if (t.src_param >= static_cast<uint32_t>(nargs))
+            return fail(EMMY_ERR_INVALID, "tensor map %u reads parameter %u of %d", i, t.src_param, nargs);
+        const uint64_t base = args[t.src_param];
+        if (m->tmap_src[i] == base) continue;
+        if (base & 15ull) return fail(EMMY_ERR_INVALID, "TMA operand %u is not 16-byte aligned", t.src_param);
+        cuuint64_t dims[5], strides[4];
+        cuuint32_t box[5], estr[5];
+        for (uint32_t d = 0; d < t.rank; ++d) {
+            dims[d] = t.dims[d];
+            box[d] = t.box[d];
+            estr[d] = 1;
+        }
+        for (uint32_t d = 0; d + 1 < t.rank; ++d) strides[d] = t.strides[d];
+        CUresult r = g_drv.cuTensorMapEncodeTiled(
+            &m->tmaps[i], static_cast<CUtensorMapDataType>(t.dtype), t.rank,
+            reinterpret_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            static_cast<CUtensorMapSwizzle>(t.swizzle), static_cast<CUtensorMapL2promotion>(t.l2_promotion),
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return cu_fail(r, "cuTensorMapEncodeTiled");
+        m->tmap_src[i] = base;
+    }
+    return EMMY_OK;
+}
+
+int launch_locked(emmy_module *m, const uint64_t *args, int nargs, const uint32_t *grid,
+                  const uint32_t *block, uint64_t stream) {
+    int rc = set_device(m->dev);
+    if (rc) return rc;
+    uint32_t g[3], b[3], smem = 0;
+    if (grid && block) {
+        for (int i = 0; i < 3; ++i) {
+            g[i] = grid[i] ? grid[i] : 1;
+            b[i] = block[i] ? block[i] : 1;
+        }
+        smem = m->has_rec ? m->rec.dyn_smem : 0;
+    } else if (m->has_rec) {
+        for (int i = 0; i < 3; ++i) {
+            g[i] = m->rec.grid[i];
+            b[i] = m->rec.block[i];
+        }
+        smem = m->rec.dyn_smem;
+    } else {
+        return fail(EMMY_ERR_INVALID, "module has no launch record: pass grid and block");
+    }
+    if (m->has_rec && static_cast<uint32_t>(nargs) != m->rec.nparams)
+        return fail(EMMY_ERR_INVALID, "entry takes %u parameters, got %d", m->rec.nparams, nargs);
+    if ((rc = encode_tmaps(m, args, nargs))) return rc;
+    const size_t ntm = m->has_rec ? m->rec.ntmaps : 0;
+    std::vector<void *> kp(static_cast<size_t>(nargs) + ntm);
+    std::vector<uint32_t> narrow(static_cast<size_t>(nargs));
+    for (int i = 0; i < nargs; ++i) {
+        size_t sz = 8;
+        if (m->has_rec) sz = m->rec.param_kind[i] == EMMY_PARAM_PTR ? 8 : 4;
+        else if (i < static_cast<int>(m->param_size.size())) sz = m->param_size[i];
+        if (sz == 4) {
+            narrow[i] = static_cast<uint32_t>(args[i]);
+            kp[i] = &narrow[i];
+        } else if (sz == 8) {
+            kp[i] = const_cast<uint64_t *>(&args[i]);
+        } else {
+            return fail(EMMY_ERR_INVALID, "parameter %d has unsupported size %zu", i, sz);
+        }
+    }
+    for (size_t i = 0; i < ntm; ++i) kp[static_cast<size_t>(nargs) + i] = &m->tmaps[i];
+    const bool cluster = m->has_rec && (m->rec.flags & 0xFFu) > 1u;
+    if (cluster) {
+        if (!g_drv.cuLaunchKernelEx) return fail(EMMY_ERR_NO_DRIVER, "driver lacks cuLaunchKernelEx");
+        CUlaunchAttribute attr[1];
+        attr[0].id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+        attr[0].value.clusterDim.x = m->rec.flags & 0xFFu;
+        attr[0].value.clusterDim.y = 1;
+        attr[0].value.clusterDim.z = 1;
+        CUlaunchConfig cfg{};
+        cfg.gridDimX = g[0];
+        cfg.gridDimY = g[1];
+        cfg.gridDimZ = g[2];
+        cfg.blockDimX = b[0];
+        cfg.blockDimY = b[1];
+        cfg.blockDimZ = b[2];
+        cfg.sharedMemBytes = smem;
+        cfg.hStream = reinterpret_cast<CUstream>(stream);
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        CU(g_drv.cuLaunchKernelEx(&cfg, m->fn, kp.data(), nullptr), "cuLaunchKernelEx");
+    } else {
+        CU(g_drv.cuLaunchKernel(m->fn, g[0], g[1], g[2], b[0], b[1], b[2], smem,
+                                reinterpret_cast<CUstream>(stream), kp.data(), nullptr),
+           "cuLaunchKernel");
+    }
+    return EMMY_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *emmy_version(void) { return "emmy_b200 1.0 (sm_100a)"; }
+
+int emmy_last_error(char *buf, size_t len) {
+    if (buf && len) {
+        std::strncpy(buf, g_err.c_str(), len - 1);
+        buf[len - 1] = '\0';
+    }
+    return g_err_code;
+}
+
+int emmy_init(int ndev) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = load_driver();
+    if (rc) return rc;
+    CUresult r = g_drv.cuInit(0);
+    if (r != CUDA_SUCCESS) return cu_fail(r, "cuInit");
+    int count = 0;
+    CU(g_drv.cuDeviceGetCount(&count), "cuDeviceGetCount");
+    if (count <= 0) return fail(EMMY_ERR_NOT_FOUND, "no CUDA devices");
+    const int n = (ndev <= 0 || ndev > count) ? count : ndev;
+    if (static_cast<int>(g_ctx.size()) < n) g_ctx.resize(n, nullptr);
+    for (int i = 0; i < n; ++i) {
+        if (g_ctx[i]) continue;
+        CUdevice d;
+        CU(g_drv.cuDeviceGet(&d, i), "cuDeviceGet");
+        CU(g_drv.cuDevicePrimaryCtxRetain(&g_ctx[i], d), "cuDevicePrimaryCtxRetain");
+    }
+    g_init = true;
+    return EMMY_OK;
+}
+
+int emmy_device_count(int *count) {
+    if (!count) return fail(EMMY_ERR_INVALID, "count is NULL");
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = load_driver();
+    if (rc) return rc;
+    CUresult r = g_drv.cuInit(0);
+    if (r != CUDA_SUCCESS) return cu_fail(r, "cuInit");
+    CU(g_drv.cuDeviceGetCount(count), "cuDeviceGetCount");
+    return EMMY_OK;
+}
+
+int emmy_load(int dev, const void *image, size_t len, const char *entry, emmy_module_t *out) {
+    if (!image || !len || !entry || !out) return fail(EMMY_ERR_INVALID, "emmy_load: NULL argument");
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = set_device(dev);
+    if (rc) return rc;
+    // PTX must be NUL-terminated; cubin (ELF) is passed through.
+    std::vector<char> buf(static_cast<const char *>(image), static_cast<const char *>(image) + len);
+    const bool elf = len >= 4 && std::memcmp(image, "\x7f" "ELF", 4) == 0;
+    if (!elf) buf.push_back('\0');
+    char log[8192] = {0};
+    CUjit_option opts[2] = {CU_JIT_ERROR_LOG_BUFFER, CU_JIT_ERROR_LOG_BUFFER_SIZE_BYTES};
+    void *vals[2] = {log, reinterpret_cast<void *>(static_cast<uintptr_t>(sizeof log))};
+    auto *m = new emmy_module();
+    m->dev = dev;
+    CUresult r = g_drv.cuModuleLoadDataEx(&m->mod, buf.data(), 2, opts, vals);
+    if (r != CUDA_SUCCESS) {
+        delete m;
+        const char *s = nullptr;
+        g_drv.cuGetErrorString(r, &s);
+        return fail(EMMY_ERR_CUDA, "cuModuleLoadDataEx: %s: %s", s ? s : "?", log);
+    }
+    r = g_drv.cuModuleGetFunction(&m->fn, m->mod, entry);
+    if (r != CUDA_SUCCESS) {
+        g_drv.cuModuleUnload(m->mod);
+        delete m;
+        return fail(EMMY_ERR_NOT_FOUND, "entry '%s' not found in module", entry);
+    }
+    CUdeviceptr rec_ptr = 0;
+    size_t rec_bytes = 0;
+    if (g_drv.cuModuleGetGlobal(&rec_ptr, &rec_bytes, m->mod, "emmy_launch_record") == CUDA_SUCCESS &&
+        rec_bytes == sizeof(EmmyLaunchRecord)) {
+        r = g_drv.cuMemcpyDtoH(&m->rec, rec_ptr, sizeof m->rec);
+        if (r != CUDA_SUCCESS) {
+            g_drv.cuModuleUnload(m->mod);
+            delete m;
+            return cu_fail(r, "reading emmy_launch_record");
+        }
+        if (m->rec.magic == EMMY_LR_MAGIC && m->rec.version == EMMY_LR_VERSION) m->has_rec = true;
+    }
+    size_t st_bytes = 0;
+    if (g_drv.cuModuleGetGlobal(&m->status, &st_bytes, m->mod, "emmy_status") != CUDA_SUCCESS)
+        m->status = 0;
+    if (g_drv.cuFuncGetParamInfo) {
+        for (size_t i = 0; i < 256; ++i) {
+            size_t off = 0, sz = 0;
+            if (g_drv.cuFuncGetParamInfo(m->fn, i, &off, &sz) != CUDA_SUCCESS) break;
+            m->param_size.push_back(sz);
+        }
+    }
+    if (m->has_rec) {
+        const size_t want = m->rec.nparams + m->rec.ntmaps;
+        if (!m->param_size.empty() && m->param_size.size() != want) {
+            g_drv.cuModuleUnload(m->mod);
+            delete m;
+            return fail(EMMY_ERR_INVALID, "entry has %zu parameters, launch record says %zu",
+                        m->param_size.size(), want);
+        }
+        if (m->rec.dyn_smem > 48 * 1024) {
+            r = g_drv.cuFuncSetAttribute(m->fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
+                                         static_cast<int>(m->rec.dyn_smem));
+            if (r != CUDA_SUCCESS) {
+                g_drv.cuModuleUnload(m->mod);
+                delete m;
+                return cu_fail(r, "cuFuncSetAttribute(max dynamic smem)");
+            }
+        }
+    }
+    *out = m;
+    return EMMY_OK;
+}
+
+int emmy_unload(emmy_module_t m) {
+    if (!m) return EMMY_OK;
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = set_device(m->dev);
+    if (rc) return rc;
+    for (CUdeviceptr p : m->dbuf)
+        if (p) g_drv.cuMemFree(p);
+    CUresult r = g_drv.cuModuleUnload(m->mod);
+    delete m;
+    if (r != CUDA_SUCCESS) return cu_fail(r, "cuModuleUnload");
+    return EMMY_OK;
+}
+
+int emmy_module_info(emmy_module_t m, uint32_t *family, uint32_t grid[3], uint32_t block[3],
+                     uint32_t *dyn_smem, uint32_t *nparams) {
+    if (!m) return fail(EMMY_ERR_INVALID, "module is NULL");
+    if (family) *family = m->has_rec ? m->rec.family : 0;
+    for (int i = 0; i < 3; ++i) {
+        if (grid) grid[i] = m->has_rec ? m->rec.grid[i] : 0;
+        if (block) block[i] = m->has_rec ? m->rec.block[i] : 0;
+    }
+    if (dyn_smem) *dyn_smem = m->has_rec ? m->rec.dyn_smem : 0;
+    if (nparams)
+        *nparams = m->has_rec ? m->rec.nparams : static_cast<uint32_t>(m->param_size.size());
+    return EMMY_OK;
+}
+
+int emmy_launch(emmy_module_t m, const uint64_t *args, int nargs, const uint32_t *grid,
+                const uint32_t *block, uint64_t stream) {
+    if (!m || (nargs > 0 && !args)) return fail(EMMY_ERR_INVALID, "emmy_launch: NULL argument");
+    std::lock_guard<std::mutex> lk(g_mu);
+    return launch_locked(m, args, nargs, grid, block, stream);
+}
+
+int emmy_module_status(emmy_module_t m, uint32_t *status) {
+    if (!m || !status) return fail(EMMY_ERR_INVALID, "emmy_module_status: NULL argument");
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = set_device(m->dev);
+    if (rc) return rc;
+    *status = 0;
+    if (!m->status) return EMMY_OK;
+    CU(g_drv.cuCtxSynchronize(), "cuCtxSynchronize");
+    CU(g_drv.cuMemcpyDtoH(status, m->status, sizeof(uint32_t)), "reading emmy_status");
+    if (*status) {
+        const uint32_t zero = 0;
+        CU(g_drv.cuMemcpyHtoD(m->status, &zero, sizeof zero), "clearing emmy_status");
+    }
+    return EMMY_OK;
+}
+
+int emmy_sync(int dev, uint64_t stream, int timeout_ms) {
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        int rc = set_device(dev);
+        if (rc) return rc;
+    }
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        CUresult r = g_drv.cuStreamQuery(reinterpret_cast<CUstream>(stream));
+        if (r == CUDA_SUCCESS) return EMMY_OK;
+        if (r != CUDA_ERROR_NOT_READY) return cu_fail(r, "cuStreamQuery");
+        if (timeout_ms > 0) {
+            const auto el = std::chrono::duration_cast<std::chrono::milliseconds>(
+                std::chrono::steady_clock::now() - t0);
+            if (el.count() > timeout_ms)
+                return fail(EMMY_ERR_TIMEOUT, "stream not idle after %d ms", timeout_ms);
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+int emmy_alloc(int dev, size_t bytes, uint64_t *dptr) {
+    if (!dptr) return fail(EMMY_ERR_INVALID, "dptr is NULL");
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = set_device(dev);
+    if (rc) return rc;
+    CUdeviceptr p = 0;
+    CU(g_drv.cuMemAlloc(&p, bytes ? bytes : 1), "cuMemAlloc");
+    *dptr = p;
+    return EMMY_OK;
+}
+
+int emmy_free(int dev, uint64_t dptr) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = set_device(dev);
+    if (rc) return rc;
+    if (dptr) CU(g_drv.cuMemFree(dptr), "cuMemFree");
+    return EMMY_OK;
+}
+
+int emmy_memcpy_htod(int dev, uint64_t dst, const void *src, size_t bytes, uint64_t stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = set_device(dev);
+    if (rc) return rc;
+    CU(g_drv.cuMemcpyHtoDAsync(dst, src, bytes, reinterpret_cast<CUstream>(stream)), "cuMemcpyHtoDAsync");
+    return EMMY_OK;
+}
+
+int emmy_memcpy_dtoh(int dev, void *dst, uint64_t src, size_t bytes, uint64_t stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = set_device(dev);
+    if (rc) return rc;
+    CU(g_drv.cuMemcpyDtoHAsync(dst, src, bytes, reinterpret_cast<CUstream>(stream)), "cuMemcpyDtoHAsync");
+    CU(g_drv.cuStreamSynchronize(reinterpret_cast<CUstream>(stream)), "cuStreamSynchronize");
+    return EMMY_OK;
+}
+
+int emmy_memset_d8(int dev, uint64_t dst, uint8_t value, size_t bytes, uint64_t stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = set_device(dev);
+    if (rc) return rc;
+    CU(g_drv.cuMemsetD8Async(dst, value, bytes, reinterpret_cast<CUstream>(stream)), "cuMemsetD8Async");
+    return EMMY_OK;
+}
+
+int emmy_host_alloc(size_t bytes, void **ptr) {
+    if (!ptr) return fail(EMMY_ERR_INVALID, "ptr is NULL");
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = set_device(0);
+    if (rc) return rc;
+    CU(g_drv.cuMemAllocHost(ptr, bytes ? bytes : 1), "cuMemAllocHost");
+    return EMMY_OK;
+}
+
+int emmy_host_free(void *ptr) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = set_device(0);
+    if (rc) return rc;
+    if (ptr) CU(g_drv.cuMemFreeHost(ptr), "cuMemFreeHost");
+    return EMMY_OK;
+}
+
+int emmy_run_host(emmy_module_t m, void *const *host_ptrs, const size_t *bytes, const uint8_t *roles,
+                  int nargs, uint64_t stream) {
+    if (!m || (nargs > 0 && (!host_ptrs || !bytes || !roles)))
+        return fail(EMMY_ERR_INVALID, "emmy_run_host: NULL argument");
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = set_device(m->dev);
+    if (rc) return rc;
+    CUstream s = reinterpret_cast<CUstream>(stream);
+    if (static_cast<int>(m->dbuf.size()) < nargs) {
+        m->dbuf.resize(nargs, 0);
+        m->dbuf_bytes.resize(nargs, 0);
+    }
+    std::vector<uint64_t> args(nargs);
+    for (int i = 0; i < nargs; ++i) {
+        if (roles[i] == EMMY_ROLE_SCALAR) {
+            uint32_t v = 0;
+            std::memcpy(&v, host_ptrs[i], 4);
+            args[i] = v;
+            continue;
+        }
+        if (m->dbuf_bytes[i] < bytes[i]) {
+            if (m->dbuf[i]) g_drv.cuMemFree(m->dbuf[i]);
+            m->dbuf[i] = 0;
+            m->dbuf_bytes[i] = 0;
+            CU(g_drv.cuMemAlloc(&m->dbuf[i], bytes[i] ? bytes[i] : 1), "cuMemAlloc (run_host)");
+            m->dbuf_bytes[i] = bytes[i];
+        }
+        args[i] = m->dbuf[i];
+        if (roles[i] == EMMY_ROLE_IN || roles[i] == EMMY_ROLE_INOUT)
+            CU(g_drv.cuMemcpyHtoDAsync(m->dbuf[i], host_ptrs[i], bytes[i], s), "cuMemcpyHtoDAsync");
+        else if (roles[i] == EMMY_ROLE_OUT_ZEROED)
+            CU(g_drv.cuMemsetD8Async(m->dbuf[i], 0, bytes[i], s), "cuMemsetD8Async");
+    }
+    if ((rc = launch_locked(m, args.data(), nargs, nullptr, nullptr, stream))) return rc;
+    for (int i = 0; i < nargs; ++i) {
+        if (roles[i] == EMMY_ROLE_OUT || roles[i] == EMMY_ROLE_INOUT || roles[i] == EMMY_ROLE_OUT_ZEROED)
+            CU(g_drv.cuMemcpyDtoHAsync(host_ptrs[i], m->dbuf[i], bytes[i], s), "cuMemcpyDtoHAsync");
+    }
+    CU(g_drv.cuStreamSynchronize(s), "cuStreamSynchronize");
+    return EMMY_OK;
+}
+
+int emmy_time_launch(emmy_module_t m, const uint64_t *args, int nargs, int iters, uint64_t stream,
+                     float *ms_total) {
+    if (!m || !ms_total || iters <= 0) return fail(EMMY_ERR_INVALID, "emmy_time_launch: bad argument");
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = set_device(m->dev);
+    if (rc) return rc;
+    CUevent e0, e1;
+    CU(g_drv.cuEventCreate(&e0, CU_EVENT_DEFAULT), "cuEventCreate");
+    CU(g_drv.cuEventCreate(&e1, CU_EVENT_DEFAULT), "cuEventCreate");
+    CUstream s = reinterpret_cast<CUstream>(stream);
+    CU(g_drv.cuEventRecord(e0, s), "cuEventRecord");
+    for (int i = 0; i < iters && rc == EMMY_OK; ++i) rc = launch_locked(m, args, nargs, nullptr, nullptr, stream);
+    CU(g_drv.cuEventRecord(e1, s), "cuEventRecord");
+    CU(g_drv.cuEventSynchronize(e1), "cuEventSynchronize");
+    CU(g_drv.cuEventElapsedTime(ms_total, e0, e1), "cuEventElapsedTime");
+    g_drv.cuEventDestroy(e0);
+    g_drv.cuEventDestroy(e1);
+    return rc;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ NCCL
+
+namespace {
+
+struct Nccl {
+    void *lib = nullptr;
+    bool ok = false;
+    decltype(&::ncclGetUniqueId) GetUniqueId = nullptr;
+    decltype(&::ncclCommInitRankConfig) CommInitRankConfig = nullptr;
+    decltype(&::ncclCommGetAsyncError) CommGetAsyncError = nullptr;
+    decltype(&::ncclCommDestroy) CommDestroy = nullptr;
+    decltype(&::ncclCommAbort) CommAbort = nullptr;
+    decltype(&::ncclAllReduce) AllReduce = nullptr;
+    decltype(&::ncclAllGather) AllGather = nullptr;
+    decltype(&::ncclGetErrorString) GetErrorString = nullptr;
+};
+Nccl g_nccl;
+
+int load_nccl() {
+    if (g_nccl.ok) return EMMY_OK;
+    if (!g_nccl.lib) g_nccl.lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!g_nccl.lib) return fail(EMMY_ERR_NCCL, "cannot open libnccl.so.2: %s", dlerror());
+#define EMMY_NC(field, sym)                                                                 \
+    g_nccl.field = reinterpret_cast<decltype(g_nccl.field)>(dlsym(g_nccl.lib, sym));        \
+    if (!g_nccl.field) return fail(EMMY_ERR_NCCL, "libnccl.so.2 lacks %s", sym);
+    EMMY_NC(GetUniqueId, "ncclGetUniqueId")
+    EMMY_NC(CommInitRankConfig, "ncclCommInitRankConfig")
+    EMMY_NC(CommGetAsyncError, "ncclCommGetAsyncError")
+    EMMY_NC(CommDestroy, "ncclCommDestroy")
+    EMMY_NC(CommAbort, "ncclCommAbort")
+    EMMY_NC(AllReduce, "ncclAllReduce")
+    EMMY_NC(AllGather, "ncclAllGather")
+    EMMY_NC(GetErrorString, "ncclGetErrorString")
+#undef EMMY_NC
+    g_nccl.ok = true;
+    return EMMY_OK;
+}
+
+}  // namespace
+
+struct emmy_comm {
+    int dev = 0;
+    ncclComm_t comm = nullptr;
+};
+
+namespace {
+
+// Poll a nonblocking communicator until its pending operation settles.
+int nccl_wait(emmy_comm *c, int timeout_ms, const char *what) {
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        ncclResult_t st = ncclSuccess;
+        ncclResult_t r = g_nccl.CommGetAsyncError(c->comm, &st);
+        if (r != ncclSuccess) return fail(EMMY_ERR_NCCL, "%s: ncclCommGetAsyncError: %s", what, g_nccl.GetErrorString(r));
+        if (st == ncclSuccess) return EMMY_OK;
+        if (st != ncclInProgress) return fail(EMMY_ERR_NCCL, "%s: %s", what, g_nccl.GetErrorString(st));
+        if (timeout_ms > 0) {
+            const auto el = std::chrono::duration_cast<std::chrono::milliseconds>(
+                std::chrono::steady_clock::now() - t0);
+            if (el.count() > timeout_ms) {
+                g_nccl.CommAbort(c->comm);
+                c->comm = nullptr;
+                return fail(EMMY_ERR_TIMEOUT, "%s: no progress after %d ms; communicator aborted", what, timeout_ms);
+            }
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
+
+int stream_wait(emmy_comm *c, uint64_t stream, int timeout_ms, const char *what) {
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        CUresult r = g_drv.cuStreamQuery(reinterpret_cast<CUstream>(stream));
+        if (r == CUDA_SUCCESS) return EMMY_OK;
+        if (r != CUDA_ERROR_NOT_READY) return cu_fail(r, what);
+        int rc = EMMY_OK;
+        ncclResult_t st = ncclSuccess;
+        if (g_nccl.CommGetAsyncError(c->comm, &st) == ncclSuccess && st != ncclSuccess && st != ncclInProgress)
+            rc = fail(EMMY_ERR_NCCL, "%s: %s", what, g_nccl.GetErrorString(st));
+        if (!rc && timeout_ms > 0) {
+            const auto el = std::chrono::duration_cast<std::chrono::milliseconds>(
+                std::chrono::steady_clock::now() - t0);
+            if (el.count() > timeout_ms)
+                rc = fail(EMMY_ERR_TIMEOUT, "%s: collective not complete after %d ms; communicator aborted",
+                          what, timeout_ms);
+        }
+        if (rc) {
+            g_nccl.CommAbort(c->comm);
+            c->comm = nullptr;
+            return rc;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(10));
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int emmy_comm_unique_id(uint8_t id[128]) {
+    if (!id) return fail(EMMY_ERR_INVALID, "id is NULL");
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = load_nccl();
+    if (rc) return rc;
+    ncclUniqueId uid;
+    ncclResult_t r = g_nccl.GetUniqueId(&uid);
+    if (r != ncclSuccess) return fail(EMMY_ERR_NCCL, "ncclGetUniqueId: %s", g_nccl.GetErrorString(r));
+    static_assert(sizeof(uid) == 128, "ncclUniqueId is 128 bytes");
+    std::memcpy(id, &uid, 128);
+    return EMMY_OK;
+}
+
+int emmy_comm_init(int dev, int nranks, int rank, const uint8_t id[128], int timeout_ms, emmy_comm_t *out) {
+    if (!id || !out || nranks <= 0 || rank < 0 || rank >= nranks)
+        return fail(EMMY_ERR_INVALID, "emmy_comm_init: bad argument");
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = load_nccl();
+    if (rc) return rc;
+    if ((rc = set_device(dev))) return rc;
+    ncclUniqueId uid;
+    std::memcpy(&uid, id, 128);
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    auto *c = new emmy_comm();
+    c->dev = dev;
+    ncclResult_t r = g_nccl.CommInitRankConfig(&c->comm, nranks, uid, rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress) {
+        delete c;
+        return fail(EMMY_ERR_NCCL, "ncclCommInitRankConfig: %s", g_nccl.GetErrorString(r));
+    }
+    if ((rc = nccl_wait(c, timeout_ms, "ncclCommInitRankConfig"))) {
+        delete c;
+        return rc;
+    }
+    *out = c;
+    return EMMY_OK;
+}
+
+int emmy_allreduce_f32(emmy_comm_t c, uint64_t send, uint64_t recv, size_t count, uint64_t stream,
+                       int timeout_ms) {
+    if (!c || !c->comm) return fail(EMMY_ERR_INVALID, "communicator is not live");
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = set_device(c->dev);
+    if (rc) return rc;
+    ncclResult_t r = g_nccl.AllReduce(reinterpret_cast<const void *>(send), reinterpret_cast<void *>(recv),
+                                      count, ncclFloat32, ncclSum, c->comm,
+                                      reinterpret_cast<cudaStream_t>(stream));
+    if (r != ncclSuccess && r != ncclInProgress)
+        return fail(EMMY_ERR_NCCL, "ncclAllReduce: %s", g_nccl.GetErrorString(r));
+    if ((rc = nccl_wait(c, timeout_ms, "ncclAllReduce"))) return rc;
+    return stream_wait(c, stream, timeout_ms, "ncclAllReduce");
+}
+
+int emmy_allgather_f32(emmy_comm_t c, uint64_t send, uint64_t recv, size_t count_per_rank,
+                       uint64_t stream, int timeout_ms) {
+    if (!c || !c->comm) return fail(EMMY_ERR_INVALID, "communicator is not live");
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = set_device(c->dev);
+    if (rc) return rc;
+    ncclResult_t r = g_nccl.AllGather(reinterpret_cast<const void *>(send), reinterpret_cast<void *>(recv),
+                                      count_per_rank, ncclFloat32, c->comm,
+                                      reinterpret_cast<cudaStream_t>(stream));
+    if (r != ncclSuccess && r != ncclInProgress)
+        return fail(EMMY_ERR_NCCL, "ncclAllGather: %s", g_nccl.GetErrorString(r));
+    if ((rc = nccl_wait(c, timeout_ms, "ncclAllGather"))) return rc;
+    return stream_wait(c, stream, timeout_ms, "ncclAllGather");
+}
+
+int emmy_comm_destroy(emmy_comm_t c) {
+    if (!c) return EMMY_OK;
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = EMMY_OK;
+    if (c->comm) {
+        set_device(c->dev);
+        ncclResult_t r = g_nccl.CommDestroy(c->comm);
+        if (r != ncclSuccess) rc = fail(EMMY_ERR_NCCL, "ncclCommDestroy: %s", g_nccl.GetErrorString(r));
+    }
+    delete c;
+    return rc;
+}
+
+int emmy_comm_abort(emmy_comm_t c) {
+    if (!c) return EMMY_OK;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (c->comm) g_nccl.CommAbort(c->comm);
+    delete c;
+    return EMMY_OK;
+}
+
+}  // extern "C"

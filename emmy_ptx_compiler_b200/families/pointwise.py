@@ -1,0 +1,356 @@
+"""Pointwise family: one Tile cell = one independent element computation.
+
+Replaces the reference's Tile lowering (compile.py:1520-1629), which runs one
+cell per thread, guards leftover threads with ``bra SKIP`` and issues scalar
+4-byte loads/stores unless the IR itself groups elements.  Here:
+
+* cells are walked by a grid-stride loop sized to the machine (148 SMs), so
+  any launch geometry computes the same result and no thread idles;
+* when every Load/Write addresses the Tile axes directly (``x[a0, a1]``,
+  broadcast forms like ``s[a1]`` or ``bias[a0]``, or a constant index) and
+  the innermost extent is a multiple of 4, each thread moves 2 x 4
+  consecutive cells per trip with 128-bit (f32) vector loads/stores, loads
+  streamed with ``ld.global.cs``/``st.global.cs``;
+* the fused op chain runs in registers through :mod:`..cgen`, with the
+  reference's exact op semantics and FMA contraction sites;
+* indices are 64-bit, so a Tile of 2^31 cells or more is one launch.
+
+Anything else in the cell body (Conds with memory ops, multi-element Loads,
+non-axis indices) takes the scalar grid-stride path with the same cell code.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+from .. import ir
+from ..cgen import DEVICE_PRELUDE, Emitter, ctype, load_to_kind, store_from
+from ..errors import UnsupportedIR
+from .common import KernelSource, LaunchPlan, ParamSpec, SM_COUNT, launch_record_source
+
+BLOCK = 256
+UNROLL = 2
+VEC = 4
+_CELL_STMTS = (ir.Load, ir.Write, ir.Let, ir.Init, ir.Assign, ir.Accum, ir.Cond, ir.Select)
+
+
+@dataclass
+class PointwisePlan:
+    tile: ir.Tile
+    prelude: tuple  # statements before the Tile (none allowed today)
+    axes: list[tuple[str, int]]
+    ncells: int
+    vector: bool
+    reasons: list[str] = field(default_factory=list)
+
+
+def _is_cell_body(body) -> bool:
+    for s in ir.walk(body):
+        if not isinstance(s, _CELL_STMTS):
+            return False
+        if isinstance(s, ir.Write) and s.atomic:
+            return False
+    return True
+
+
+def match(kop: ir.KernelOp) -> PointwisePlan | None:
+    body = ir.body_stmts(kop.body)
+    tiles = [s for s in body if isinstance(s, ir.Tile)]
+    if len(tiles) != 1 or len(body) != 1:
+        return None
+    tile = tiles[0]
+    if not _is_cell_body(tile.body):
+        return None
+    if int(tile.aux_threads or 0):
+        return None
+    axes = [(a.name, a.size) for a in tile.axes]
+    n = 1
+    for _, e in axes:
+        n *= e
+    return PointwisePlan(tile=tile, prelude=(), axes=axes, ncells=n, vector=False)
+
+
+def _axis_aligned(index, axes: list[tuple[str, int]]) -> list[int] | None:
+    """Positions of the tile axes an index names, if it is exactly a tuple of
+    axis variables in increasing axis order; None otherwise."""
+    pos = {name: i for i, (name, _) in enumerate(axes)}
+    out: list[int] = []
+    for ix in index:
+        if not isinstance(ix, ir.Var) or ix.name not in pos:
+            return None
+        p = pos[ix.name]
+        if out and p <= out[-1]:
+            return None
+        out.append(p)
+    return out
+
+
+def _const_index(index) -> bool:
+    return len(index) > 0 and all(isinstance(ix, ir.Literal) and not isinstance(ix.value, float)
+                                  for ix in index)
+
+
+def vector_eligible(plan: PointwisePlan, shapes: dict, dtypes: dict) -> tuple[bool, list[str]]:
+    why: list[str] = []
+    axes = plan.axes
+    inner = axes[-1][1] if axes else 1
+    if not axes or inner % VEC != 0:
+        why.append(f"innermost extent {inner} is not a multiple of {VEC}")
+    top = list(ir.body_stmts(plan.tile.body))
+    for s in ir.walk(plan.tile.body):
+        if isinstance(s, ir.Cond):
+            for t in list(ir.walk(s.body)) + list(ir.walk(s.else_body)):
+                if isinstance(t, (ir.Load, ir.Write)):
+                    why.append("memory access under a Cond")
+        if isinstance(s, ir.Load):
+            if len(s.names) != 1:
+                why.append(f"multi-element Load of {s.input}")
+            elif not _const_index(s.index):
+                pos = _axis_aligned(s.index, axes)
+                shp = shapes.get(s.input)
+                if pos is None:
+                    why.append(f"Load {s.input} index is not a tile-axis tuple")
+                elif shp is not None and tuple(shp) != tuple(axes[p][1] for p in pos):
+                    why.append(f"Load {s.input} shape {shp} does not match its axes")
+        if isinstance(s, ir.Write):
+            pos = _axis_aligned(s.index, axes)
+            shp = shapes.get(s.output)
+            if len(s.values) != 1:
+                why.append(f"multi-element Write of {s.output}")
+            elif pos != list(range(len(axes))):
+                why.append(f"Write {s.output} does not index every tile axis in order")
+            elif shp is not None and tuple(shp) != tuple(e for _, e in axes):
+                why.append(f"Write {s.output} shape {shp} does not match the tile")
+    for s in top:
+        if isinstance(s, (ir.Load, ir.Write)):
+            dt = ir.canon_dtype((s.dtype if isinstance(s, ir.Load) else s.value_dtype)
+                                or dtypes.get(s.input if isinstance(s, ir.Load) else s.output))
+            if dt not in ("f32", "bf16", "f16"):
+                why.append(f"element type {dt} has no vector form")
+    return (not why), why
+
+
+def _axis_strides(axes) -> list[int]:
+    strides = [1] * len(axes)
+    acc = 1
+    for i in range(len(axes) - 1, -1, -1):
+        strides[i] = acc
+        acc *= axes[i][1]
+    return strides
+
+
+def _decode_axes(em: Emitter, axes, cell: str, prefix: str) -> None:
+    strides = _axis_strides(axes)
+    for i, ((name, ext), st) in enumerate(zip(axes, strides)):
+        var = f"{prefix}{i}"
+        q = cell if st == 1 else f"({cell} / {st}LL)"
+        expr = q if i == 0 else f"({q} % {ext}LL)"
+        if ext == 1:
+            expr = "0LL"
+        em.emit(f"const long long {var} = {expr};")
+        em.bind_const(name, "int", var)
+
+
+def generate(kop: ir.KernelOp, plan: PointwisePlan, shapes: dict, dtypes: dict, args: list[str],
+             scalars: dict[str, str], written: set[str]) -> KernelSource:
+    vec_ok, why = vector_eligible(plan, shapes, dtypes)
+    plan.vector = vec_ok
+    plan.reasons = why
+    params: list[ParamSpec] = []
+    ptrs: dict[str, str] = {}
+    sig: list[str] = []
+    for name in args:
+        if name in scalars:
+            dt = scalars[name]
+            sig.append(f"{ctype(dt)} p_{_c(name)}")
+            params.append(ParamSpec(name, "scalar", dt))
+            continue
+        dt = ir.canon_dtype(dtypes.get(name))
+        cty = ctype(dt)
+        if name in written:
+            sig.append(f"{cty}* __restrict__ p_{_c(name)}")
+        else:
+            sig.append(f"const {cty}* __restrict__ p_{_c(name)}")
+        ptrs[name] = f"p_{_c(name)}"
+        params.append(ParamSpec(name, "ptr", dt))
+    ncell = plan.ncells
+    axes = plan.axes
+    lines: list[str] = []
+    w = lines.append
+    w(DEVICE_PRELUDE)
+    w(_VEC_HELPERS)
+    w(f'extern "C" __global__ void __launch_bounds__({BLOCK}) {kop.name}(' + ", ".join(sig) + ") {")
+    w(f"    constexpr long long NCELL = {ncell}LL;")
+    w("    const long long gstride = (long long)gridDim.x * blockDim.x;")
+    w("    const long long gtid = (long long)blockIdx.x * blockDim.x + threadIdx.x;")
+    scalar_env = {name: (("f32", f"p_{_c(name)}") if scalars[name] == "f32" else
+                         ("int", f"(long long)p_{_c(name)}")) for name in scalars}
+    if vec_ok:
+        align_terms = [f"(uintptr_t)p_{_c(n)}" for n in ptrs]
+        w("    const bool aligned = ((" + (" | ".join(align_terms) if align_terms else "0") + ") & 15u) == 0;")
+        w("    if (aligned) {")
+        w(f"        constexpr long long NVEC = NCELL / {VEC};")
+        w("        long long v = gtid;")
+        w(f"        for (; v + gstride < NVEC; v += {UNROLL} * gstride) {{")
+        lines.extend(_vector_trip(plan, shapes, dtypes, ptrs, scalar_env, ["v", "v + gstride"],
+                                  "            "))
+        w("        }")
+        w("        if (v < NVEC) {")
+        lines.extend(_vector_trip(plan, shapes, dtypes, ptrs, scalar_env, ["v"], "            "))
+        w("        }")
+        w("        return;")
+        w("    }")
+    w("    for (long long cell = gtid; cell < NCELL; cell += gstride) {")
+    em = Emitter(shapes, dtypes, ptrs, indent="        ")
+    em.env.update(scalar_env)
+    _decode_axes(em, axes, "cell", "ax")
+    em.run(plan.tile.body)
+    lines.extend(em.lines)
+    w("    }")
+    w("}")
+    nvec = ncell // VEC if vec_ok else ncell
+    per_block = BLOCK * (UNROLL if vec_ok else 1)
+    grid = max(1, min((nvec + per_block - 1) // per_block, SM_COUNT * 8))
+    launch = LaunchPlan(grid=(grid, 1, 1), block=(BLOCK, 1, 1), smem=0)
+    lines.append(launch_record_source("pointwise", launch, params))
+    return KernelSource(entry=kop.name, source="\n".join(lines), launch=launch, params=params,
+                        family="pointwise",
+                        notes={"vector": vec_ok, "scalar_reasons": why, "ncells": ncell})
+
+
+def _c(name: str) -> str:
+    import re
+    return re.sub(r"[^A-Za-z0-9_]", "_", name)
+
+
+def _vector_trip(plan: PointwisePlan, shapes, dtypes, ptrs, scalar_env, vexprs: list[str],
+                 ind: str) -> list[str]:
+    """One trip: load U vectors of every input, run the cell body per lane,
+    store U vectors of every output."""
+    axes = plan.axes
+    out: list[str] = []
+    loads = [s for s in ir.walk(plan.tile.body) if isinstance(s, ir.Load)]
+    writes = [s for s in ir.walk(plan.tile.body) if isinstance(s, ir.Write)]
+    strides = _axis_strides(axes)
+    for u, vx in enumerate(vexprs):
+        out.append(f"{ind}const long long c{u} = ({vx}) * {VEC}LL;")
+        for i, ((name, ext), st) in enumerate(zip(axes, strides)):
+            q = f"c{u}" if st == 1 else f"(c{u} / {st}LL)"
+            expr = q if i == 0 else f"({q} % {ext}LL)"
+            if ext == 1:
+                expr = "0LL"
+            out.append(f"{ind}const long long u{u}_ax{i} = {expr};")
+    # fetch every load for every trip vector before any compute
+    fetched: dict[tuple[int, int], tuple[str, bool, str]] = {}
+    for li, s in enumerate(loads):
+        dt = ir.canon_dtype(s.dtype or dtypes.get(s.input))
+        ptr = ptrs[s.input]
+        for u in range(len(vexprs)):
+            var = f"ld{li}_{u}"
+            if _const_index(s.index):
+                off = "+".join(str(int(ix.value)) for ix in s.index) if len(s.index) == 1 else \
+                    _const_flat(s, shapes)
+                out.append(f"{ind}const {ctype(dt)} {var} = {ptr}[{off}];")
+                fetched[(li, u)] = (var, False, dt)
+                continue
+            pos = _axis_aligned(s.index, axes)
+            bstrides = _axis_strides([axes[p] for p in pos])
+            off = " + ".join(f"u{u}_ax{p} * {bs}LL" for p, bs in zip(pos, bstrides)) or "0LL"
+            contiguous = bool(pos) and pos[-1] == len(axes) - 1
+            if contiguous:
+                out.append(f"{ind}const auto {var} = emmy_ld{VEC}_{dt}({ptr} + ({off}), "
+                           f"{'true' if _streamed(s, plan) else 'false'});")
+                fetched[(li, u)] = (var, True, dt)
+            else:
+                out.append(f"{ind}const {ctype(dt)} {var} = {ptr}[{off}];")
+                fetched[(li, u)] = (var, False, dt)
+    outs: dict[tuple[int, int], list[str]] = {}
+    for u in range(len(vexprs)):
+        for wi, s in enumerate(writes):
+            dt = ir.canon_dtype(s.value_dtype or dtypes.get(s.output))
+            outs[(wi, u)] = [f"st{wi}_{u}_{lane}" for lane in range(VEC)]
+            for lane in range(VEC):
+                out.append(f"{ind}{ctype(dt)} st{wi}_{u}_{lane};")
+    for u in range(len(vexprs)):
+        for lane in range(VEC):
+            load_idx = {id(s): li for li, s in enumerate(loads)}
+            write_idx = {id(s): wi for wi, s in enumerate(writes)}
+
+            def load_hook(s, k, u=u, lane=lane):
+                var, is_vec, dt = fetched[(load_idx[id(s)], u)]
+                code = f"{var}.v[{lane}]" if is_vec else var
+                return load_to_kind(code, dt)
+
+            def write_hook(s, k, kind, code, u=u, lane=lane):
+                dt = ir.canon_dtype(s.value_dtype or dtypes.get(s.output))
+                return f"st{write_idx[id(s)]}_{u}_{lane} = {store_from(kind, code, dt)};"
+
+            em = Emitter(shapes, dtypes, ptrs, load_hook=load_hook, write_hook=write_hook,
+                         indent=ind + "    ")
+            em.env.update(scalar_env)
+            for i, (name, ext) in enumerate(axes):
+                code = f"u{u}_ax{i}" if i < len(axes) - 1 else f"(u{u}_ax{i} + {lane})"
+                em.bind_const(name, "int", code)
+            em.run(plan.tile.body)
+            out.append(f"{ind}{{")
+            out.extend(em.lines)
+            out.append(f"{ind}}}")
+    for u in range(len(vexprs)):
+        for wi, s in enumerate(writes):
+            dt = ir.canon_dtype(s.value_dtype or dtypes.get(s.output))
+            vals = ", ".join(outs[(wi, u)])
+            out.append(f"{ind}emmy_st{VEC}_{dt}({ptrs[s.output]} + c{u}, {vals});")
+    return out
+
+
+def _const_flat(s: ir.Load, shapes) -> str:
+    shape = shapes.get(s.input)
+    vals = [int(ix.value) for ix in s.index]
+    if not shape or len(shape) != len(vals):
+        return str(sum(vals))
+    acc = 0
+    for v, st in zip(vals, _axis_strides([(None, int(e)) for e in shape])):
+        acc += v * st
+    return str(acc)
+
+
+def _streamed(s: ir.Load, plan: PointwisePlan) -> bool:
+    """Full-tile operands are read once: stream them past L1/L2 residency."""
+    pos = _axis_aligned(s.index, plan.axes)
+    return pos is not None and len(pos) == len(plan.axes)
+
+
+_VEC_HELPERS = r"""
+template <class T, int N> struct EmmyVec { T v[N]; };
+static __device__ __forceinline__ EmmyVec<float, 4> emmy_ld4_f32(const float* p, bool stream) {
+    float4 t = stream ? __ldcs(reinterpret_cast<const float4*>(p))
+                      : __ldg(reinterpret_cast<const float4*>(p));
+    return EmmyVec<float, 4>{{t.x, t.y, t.z, t.w}};
+}
+static __device__ __forceinline__ void emmy_st4_f32(float* p, float a, float b, float c, float d) {
+    __stcs(reinterpret_cast<float4*>(p), make_float4(a, b, c, d));
+}
+static __device__ __forceinline__ EmmyVec<__nv_bfloat16, 4> emmy_ld4_bf16(const __nv_bfloat16* p, bool stream) {
+    uint2 t = stream ? __ldcs(reinterpret_cast<const uint2*>(p)) : __ldg(reinterpret_cast<const uint2*>(p));
+    EmmyVec<__nv_bfloat16, 4> r;
+    memcpy(&r, &t, 8);
+    return r;
+}
+static __device__ __forceinline__ void emmy_st4_bf16(__nv_bfloat16* p, __nv_bfloat16 a, __nv_bfloat16 b,
+                                                     __nv_bfloat16 c, __nv_bfloat16 d) {
+    EmmyVec<__nv_bfloat16, 4> r{{a, b, c, d}};
+    uint2 t; memcpy(&t, &r, 8);
+    __stcs(reinterpret_cast<uint2*>(p), t);
+}
+static __device__ __forceinline__ EmmyVec<__half, 4> emmy_ld4_f16(const __half* p, bool stream) {
+    uint2 t = stream ? __ldcs(reinterpret_cast<const uint2*>(p)) : __ldg(reinterpret_cast<const uint2*>(p));
+    EmmyVec<__half, 4> r;
+    memcpy(&r, &t, 8);
+    return r;
+}
+static __device__ __forceinline__ void emmy_st4_f16(__half* p, __half a, __half b, __half c, __half d) {
+    EmmyVec<__half, 4> r{{a, b, c, d}};
+    uint2 t; memcpy(&t, &r, 8);
+    __stcs(reinterpret_cast<uint2*>(p), t);
+}
+"""

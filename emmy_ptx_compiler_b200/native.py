@@ -1,0 +1,45 @@
+"""Build recipe for the in-tree native library ``lib/libemmy_b200.so``.
+
+The library is plain C++ over the CUDA driver API; libcuda and libnccl are
+opened at run time, so it builds and loads on machines without a GPU.
+"""
+
+from __future__ import annotations
+
+import os
+import subprocess
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+REPO = PKG.parent
+LIB_DIR = PKG / "lib"
+RUNTIME_SO = LIB_DIR / "libemmy_b200.so"
+SOURCES = [PKG / "csrc" / "emmy_runtime.cpp"]
+HEADERS = [REPO / "include" / "emmy_b200.h", REPO / "include" / "emmy_launch_record.h"]
+CUDA_INC = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda")) / "include"
+
+
+def _stale(target: Path, deps: list[Path]) -> bool:
+    if not target.is_file():
+        return True
+    t = target.stat().st_mtime
+    return any(d.stat().st_mtime > t for d in deps if d.exists())
+
+
+def build_runtime(force: bool = False) -> Path:
+    if not force and not _stale(RUNTIME_SO, SOURCES + HEADERS):
+        return RUNTIME_SO
+    LIB_DIR.mkdir(parents=True, exist_ok=True)
+    tmp = RUNTIME_SO.with_suffix(f".so.tmp{os.getpid()}")
+    cmd = ["g++", "-O2", "-g", "-std=c++17", "-fPIC", "-shared", "-Wall", "-Wextra",
+           f"-I{REPO / 'include'}", f"-I{CUDA_INC}", "-I/usr/include",
+           *[str(s) for s in SOURCES], "-o", str(tmp), "-ldl", "-lpthread"]
+    proc = subprocess.run(cmd, capture_output=True, text=True, check=False)
+    if proc.returncode != 0:
+        raise RuntimeError(f"building libemmy_b200.so failed:\n{proc.stderr[-4000:]}")
+    os.replace(tmp, RUNTIME_SO)
+    return RUNTIME_SO
+
+
+if __name__ == "__main__":
+    print(build_runtime(force=True))

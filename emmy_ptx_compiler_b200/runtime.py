@@ -1,0 +1,223 @@
+"""ctypes binding of ``libemmy_b200.so`` (C ABI: include/emmy_b200.h).
+
+This is the launch side the reference leaves to its external runner
+(README.md:170-182): load the module for a KernelOp, launch its entry on
+device buffers in ``arg_order``, read back the kernel status word.  There is
+no CPU fallback: if the library or a GPU is missing, calls raise
+:class:`EmmyError`.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import struct
+import threading
+from pathlib import Path
+
+from . import native
+
+EMMY_ROLE_IN, EMMY_ROLE_OUT, EMMY_ROLE_INOUT, EMMY_ROLE_OUT_ZEROED, EMMY_ROLE_SCALAR = 0, 1, 2, 3, 4
+FAMILY_NAMES = {0: "foreign", 1: "pointwise", 2: "reduction", 3: "gemm"}
+
+_lock = threading.Lock()
+_lib = None
+_initialised: set[int] = set()
+
+
+class EmmyError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"emmy error {code}: {msg}")
+        self.code = code
+
+
+def _declare(lib) -> None:
+    u64, u32, i32, vp, sz = C.c_uint64, C.c_uint32, C.c_int, C.c_void_p, C.c_size_t
+    P = C.POINTER
+    sigs = {
+        "emmy_version": ([], C.c_char_p),
+        "emmy_last_error": ([C.c_char_p, sz], i32),
+        "emmy_init": ([i32], i32),
+        "emmy_device_count": ([P(i32)], i32),
+        "emmy_load": ([i32, vp, sz, C.c_char_p, P(vp)], i32),
+        "emmy_unload": ([vp], i32),
+        "emmy_module_info": ([vp, P(u32), P(u32), P(u32), P(u32), P(u32)], i32),
+        "emmy_launch": ([vp, P(u64), i32, P(u32), P(u32), u64], i32),
+        "emmy_module_status": ([vp, P(u32)], i32),
+        "emmy_sync": ([i32, u64, i32], i32),
+        "emmy_alloc": ([i32, sz, P(u64)], i32),
+        "emmy_free": ([i32, u64], i32),
+        "emmy_memcpy_htod": ([i32, u64, vp, sz, u64], i32),
+        "emmy_memcpy_dtoh": ([i32, vp, u64, sz, u64], i32),
+        "emmy_memset_d8": ([i32, u64, C.c_uint8, sz, u64], i32),
+        "emmy_host_alloc": ([sz, P(vp)], i32),
+        "emmy_host_free": ([vp], i32),
+        "emmy_run_host": ([vp, P(vp), P(sz), P(C.c_uint8), i32, u64], i32),
+        "emmy_time_launch": ([vp, P(u64), i32, i32, u64, P(C.c_float)], i32),
+        "emmy_comm_unique_id": ([P(C.c_uint8)], i32),
+        "emmy_comm_init": ([i32, i32, i32, P(C.c_uint8), i32, P(vp)], i32),
+        "emmy_allreduce_f32": ([vp, u64, u64, sz, u64, i32], i32),
+        "emmy_allgather_f32": ([vp, u64, u64, sz, u64, i32], i32),
+        "emmy_comm_destroy": ([vp], i32),
+        "emmy_comm_abort": ([vp], i32),
+    }
+    for name, (argtypes, restype) in sigs.items():
+        fn = getattr(lib, name)
+        fn.argtypes = argtypes
+        fn.restype = restype
+
+
+EXPORTED = ("emmy_version", "emmy_last_error", "emmy_init", "emmy_device_count", "emmy_load",
+            "emmy_unload", "emmy_module_info", "emmy_launch", "emmy_module_status", "emmy_sync",
+            "emmy_alloc", "emmy_free", "emmy_memcpy_htod", "emmy_memcpy_dtoh", "emmy_memset_d8",
+            "emmy_host_alloc", "emmy_host_free", "emmy_run_host", "emmy_time_launch",
+            "emmy_comm_unique_id", "emmy_comm_init", "emmy_allreduce_f32", "emmy_allgather_f32",
+            "emmy_comm_destroy", "emmy_comm_abort")
+
+
+def library_path() -> Path:
+    return native.RUNTIME_SO
+
+
+def lib():
+    """Load (building first if needed) the native library."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            path = native.build_runtime()
+            handle = C.CDLL(str(path), mode=C.RTLD_GLOBAL)
+            _declare(handle)
+            _lib = handle
+        return _lib
+
+
+def _check(rc: int) -> None:
+    if rc != 0:
+        buf = C.create_string_buffer(2048)
+        lib().emmy_last_error(buf, len(buf))
+        raise EmmyError(rc, buf.value.decode(errors="replace"))
+
+
+def init(device: int = 0) -> None:
+    """Initialise devices [0, device] (their primary contexts)."""
+    if device in _initialised:
+        return
+    _check(lib().emmy_init(device + 1))
+    _initialised.update(range(device + 1))
+
+
+def device_count() -> int:
+    n = C.c_int(0)
+    _check(lib().emmy_device_count(C.byref(n)))
+    return n.value
+
+
+def arg_word(value) -> int:
+    """One 64-bit launch word: device pointer, torch tensor, f32 or i32 scalar."""
+    if hasattr(value, "data_ptr"):
+        return int(value.data_ptr())
+    if isinstance(value, float):
+        return struct.unpack("<I", struct.pack("<f", value))[0]
+    if isinstance(value, int):
+        return value & 0xFFFFFFFFFFFFFFFF
+    if isinstance(value, tuple) and len(value) == 2 and value[0] == "i32":
+        return int(value[1]) & 0xFFFFFFFF
+    raise TypeError(f"cannot pass {type(value).__name__} as a kernel argument")
+
+
+class Module:
+    """One loaded entry on one device."""
+
+    def __init__(self, image: bytes, entry: str, device: int = 0):
+        init(device)
+        self.device = device
+        self.entry = entry
+        self._image = image
+        h = C.c_void_p()
+        _check(lib().emmy_load(device, image, len(image), entry.encode(), C.byref(h)))
+        self._h = h
+        fam, nparams, smem = C.c_uint32(), C.c_uint32(), C.c_uint32()
+        grid, block = (C.c_uint32 * 3)(), (C.c_uint32 * 3)()
+        _check(lib().emmy_module_info(h, C.byref(fam), grid, block, C.byref(smem), C.byref(nparams)))
+        self.family = FAMILY_NAMES.get(fam.value, str(fam.value))
+        self.grid = tuple(grid)
+        self.block = tuple(block)
+        self.smem = smem.value
+        self.nparams = nparams.value
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _check(lib().emmy_unload(self._h))
+            self._h = None
+
+    def __del__(self):  # best effort; explicit close() is preferred
+        try:
+            if getattr(self, "_h", None) and _lib is not None:
+                _lib.emmy_unload(self._h)
+        except Exception:
+            pass
+
+    def _words(self, args) -> C.Array:
+        return (C.c_uint64 * max(1, len(args)))(*[arg_word(a) for a in args])
+
+    def launch(self, args, stream: int = 0, grid=None, block=None) -> None:
+        words = self._words(args)
+        g = (C.c_uint32 * 3)(*(list(grid) + [1, 1])[:3]) if grid is not None else None
+        b = (C.c_uint32 * 3)(*(list(block) + [1, 1])[:3]) if block is not None else None
+        _check(lib().emmy_launch(self._h, words, len(args), g, b, C.c_uint64(stream)))
+
+    def status(self) -> int:
+        st = C.c_uint32(0)
+        _check(lib().emmy_module_status(self._h, C.byref(st)))
+        return st.value
+
+    def time(self, args, iters: int, stream: int = 0) -> float:
+        """Total device milliseconds of ``iters`` back-to-back launches."""
+        words = self._words(args)
+        ms = C.c_float(0.0)
+        _check(lib().emmy_time_launch(self._h, words, len(args), iters, C.c_uint64(stream), C.byref(ms)))
+        return ms.value
+
+    def run_host(self, host_ptrs: list[int], nbytes: list[int], roles: list[int], stream: int = 0) -> None:
+        n = len(host_ptrs)
+        ptrs = (C.c_void_p * n)(*host_ptrs)
+        sizes = (C.c_size_t * n)(*nbytes)
+        rl = (C.c_uint8 * n)(*roles)
+        _check(lib().emmy_run_host(self._h, ptrs, sizes, rl, n, C.c_uint64(stream)))
+
+
+def sync(device: int = 0, stream: int = 0, timeout_ms: int = 0) -> None:
+    _check(lib().emmy_sync(device, C.c_uint64(stream), timeout_ms))
+
+
+class Comm:
+    """NCCL communicator for the per-GPU partial combine of full reductions."""
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = (C.c_uint8 * 128)()
+        _check(lib().emmy_comm_unique_id(buf))
+        return bytes(buf)
+
+    def __init__(self, device: int, nranks: int, rank: int, uid: bytes, timeout_ms: int = 60000):
+        init(device)
+        self.device = device
+        h = C.c_void_p()
+        idbuf = (C.c_uint8 * 128)(*uid)
+        _check(lib().emmy_comm_init(device, nranks, rank, idbuf, timeout_ms, C.byref(h)))
+        self._h = h
+
+    def allreduce_f32(self, send: int, recv: int, count: int, stream: int = 0, timeout_ms: int = 60000) -> None:
+        _check(lib().emmy_allreduce_f32(self._h, send, recv, count, C.c_uint64(stream), timeout_ms))
+
+    def allgather_f32(self, send: int, recv: int, count: int, stream: int = 0, timeout_ms: int = 60000) -> None:
+        _check(lib().emmy_allgather_f32(self._h, send, recv, count, C.c_uint64(stream), timeout_ms))
+
+    def close(self) -> None:
+        if self._h:
+            _check(lib().emmy_comm_destroy(self._h))
+            self._h = None
+
+    def abort(self) -> None:
+        if self._h:
+            lib().emmy_comm_abort(self._h)
+            self._h = None

@@ -1,0 +1,131 @@
+/*
+ * libemmy_b200 - C ABI of the emmy B200 execution backend.
+ *
+ * The reference (vedantgpt/emmy-ptx-compiler) stops at printing PTX; an
+ * external runner (the starter kit's submit.py and a hosted GPU service,
+ * reference README.md:170-182) assembled that PTX, launched the entry under
+ * meta.json's grid/block/smem_bytes on device buffers, and compared the
+ * outputs.  This library is that missing launch layer, for modules produced
+ * by our compiler (compile_bundle, reference compile.py:3168-3215) and for
+ * any other PTX/cubin module, such as the reference's own output.
+ *
+ * Conventions: every function returns 0 (EMMY_OK) or a negative EMMY_ERR_*
+ * code and never aborts the process; emmy_last_error() gives the message of
+ * the calling thread's last failure.  Device pointers and streams are plain
+ * 64-bit integers (CUdeviceptr / CUstream of the device's primary context,
+ * which is also the context the CUDA runtime and PyTorch use).  The caller
+ * owns device buffers; the library owns modules and communicators.
+ * libcuda and libnccl are opened at run time, so the library itself loads on
+ * machines without a GPU driver.
+ */
+#ifndef EMMY_B200_H
+#define EMMY_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EMMY_OK 0
+#define EMMY_ERR_NO_DRIVER (-1)     /* libcuda.so.1 could not be opened or cuInit failed */
+#define EMMY_ERR_CUDA (-2)          /* a driver call failed; see emmy_last_error */
+#define EMMY_ERR_INVALID (-3)       /* bad argument */
+#define EMMY_ERR_NOT_FOUND (-4)     /* entry / symbol / device not found */
+#define EMMY_ERR_KERNEL_STATUS (-5) /* a kernel raised EMMY_STATUS_* bits */
+#define EMMY_ERR_TIMEOUT (-6)       /* a bounded host wait ran out */
+#define EMMY_ERR_NCCL (-7)          /* NCCL missing or a collective failed */
+#define EMMY_ERR_NOT_INIT (-8)      /* emmy_init has not succeeded */
+
+typedef struct emmy_module *emmy_module_t;
+typedef struct emmy_comm *emmy_comm_t;
+
+/* Library version string, e.g. "emmy_b200 1.0 (sm_100a)". */
+const char *emmy_version(void);
+
+/* Thread-local message of the last failed call; returns the code of that call. */
+int emmy_last_error(char *buf, size_t len);
+
+/* Open libcuda, cuInit, retain the primary context of devices [0, ndev)
+ * (ndev <= 0: every device).  Replaces the runner's device setup. */
+int emmy_init(int ndev);
+
+int emmy_device_count(int *count);
+
+/* Load a PTX (NUL-terminated text) or cubin image on device `dev` and resolve
+ * `entry` (the reference's `.visible .entry <KernelOp.name>`,
+ * compile.py:862).  Modules from our compiler also carry a launch record
+ * (include/emmy_launch_record.h), read here. */
+int emmy_load(int dev, const void *image, size_t len, const char *entry, emmy_module_t *out);
+
+int emmy_unload(emmy_module_t m);
+
+/* The module's launch record: family (0 when the module has none), tuned
+ * grid/block, dynamic shared memory and IR parameter count. */
+int emmy_module_info(emmy_module_t m, uint32_t *family, uint32_t grid[3], uint32_t block[3],
+                     uint32_t *dyn_smem, uint32_t *nparams);
+
+/* Launch the entry.  `args` holds one 64-bit word per IR parameter in
+ * meta.json arg_order (compile.py:314-317, 854-864): a device pointer, or
+ * the bits of an f32 / i32 scalar in the low 32 bits.  grid/block NULL
+ * means the module's launch record; modules without one need both.  Tensor
+ * maps the record describes are encoded and appended after the IR
+ * parameters.  Asynchronous on `stream` (0 = the legacy default stream). */
+int emmy_launch(emmy_module_t m, const uint64_t *args, int nargs, const uint32_t *grid,
+                const uint32_t *block, uint64_t stream);
+
+/* Read and clear the module's device status word (EMMY_STATUS_* bits from
+ * include/emmy_launch_record.h).  Synchronises the device first. */
+int emmy_module_status(emmy_module_t m, uint32_t *status);
+
+/* Wait for `stream` on `dev`, polling, for at most timeout_ms (<= 0: no limit). */
+int emmy_sync(int dev, uint64_t stream, int timeout_ms);
+
+/* Device memory and copies, for hosts without another CUDA runtime. */
+int emmy_alloc(int dev, size_t bytes, uint64_t *dptr);
+int emmy_free(int dev, uint64_t dptr);
+int emmy_memcpy_htod(int dev, uint64_t dst, const void *src, size_t bytes, uint64_t stream);
+int emmy_memcpy_dtoh(int dev, void *dst, uint64_t src, size_t bytes, uint64_t stream);
+int emmy_memset_d8(int dev, uint64_t dst, uint8_t value, size_t bytes, uint64_t stream);
+int emmy_host_alloc(size_t bytes, void **ptr);  /* pinned host memory */
+int emmy_host_free(void *ptr);
+
+/* Argument roles of emmy_run_host. */
+#define EMMY_ROLE_IN 0          /* host -> device before the launch */
+#define EMMY_ROLE_OUT 1         /* device -> host after the launch */
+#define EMMY_ROLE_INOUT 2       /* both */
+#define EMMY_ROLE_OUT_ZEROED 3  /* zero-filled on the device, then device -> host (meta zero_outputs) */
+#define EMMY_ROLE_SCALAR 4      /* host_ptrs[i] points at the 4-byte scalar value */
+
+/* Run the entry on host buffers - the whole job the reference's runner did
+ * per problem (README.md:170-182): copy inputs in, zero `zero_outputs`,
+ * launch with the module's record, copy outputs back.  Device buffers are
+ * owned by the module and reused across calls; everything is ordered on
+ * `stream`, and the call returns after the outputs are on the host. */
+int emmy_run_host(emmy_module_t m, void *const *host_ptrs, const size_t *bytes,
+                  const uint8_t *roles, int nargs, uint64_t stream);
+
+/* Launch `iters` times back to back on `stream` between two CUDA events and
+ * return the elapsed milliseconds (device time). */
+int emmy_time_launch(emmy_module_t m, const uint64_t *args, int nargs, int iters, uint64_t stream,
+                     float *ms_total);
+
+/* NCCL over NVLink/NVSwitch for the one collective of the path: combining
+ * per-GPU partials of a full-array reduction.  No reference counterpart
+ * (the reference is single-GPU). */
+int emmy_comm_unique_id(uint8_t id[128]);
+int emmy_comm_init(int dev, int nranks, int rank, const uint8_t id[128], int timeout_ms,
+                   emmy_comm_t *out);
+int emmy_allreduce_f32(emmy_comm_t c, uint64_t send, uint64_t recv, size_t count, uint64_t stream,
+                       int timeout_ms);
+int emmy_allgather_f32(emmy_comm_t c, uint64_t send, uint64_t recv, size_t count_per_rank,
+                       uint64_t stream, int timeout_ms);
+int emmy_comm_destroy(emmy_comm_t c);
+int emmy_comm_abort(emmy_comm_t c);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

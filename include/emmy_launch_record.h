@@ -1,0 +1,75 @@
+/*
+ * Launch record and status word embedded in every module the emmy B200
+ * compiler emits.
+ *
+ * The reference compiler's modules carry no launch information: the external
+ * runner launched them with meta.json's grid/block/smem_bytes (the contract
+ * in the reference README, "Correct under the launch in meta.json").  Our
+ * kernels are correct under any 1-D launch, but they are fastest under the
+ * geometry the lowering chose, and the GEMM family needs TMA tensor maps
+ * encoded on the host.  So each module exports:
+ *
+ *   extern "C" __device__ const EmmyLaunchRecord emmy_launch_record;
+ *   extern "C" __device__ unsigned int emmy_status;
+ *
+ * libemmy_b200 (emmy_load) reads the record with cuModuleGetGlobal, and
+ * emmy_launch appends the tensor maps it describes after the arg_order
+ * parameters - the same "arg_order, then tensor-map params" layout the
+ * reference uses for its own TMA descriptors (compile.py:854-864).
+ * Kernels report failures (a bounded wait that ran out, a launch geometry
+ * they cannot run under) by OR-ing EMMY_STATUS_* bits into emmy_status;
+ * emmy_module_status() reads and clears it.
+ *
+ * This header is shared by device code (generated .cu files) and host code
+ * (emmy_runtime.cpp), so the layout is plain fixed-width integers.
+ */
+#ifndef EMMY_LAUNCH_RECORD_H
+#define EMMY_LAUNCH_RECORD_H
+
+#include <stdint.h>
+
+#define EMMY_LR_MAGIC 0x31594D45u /* "EMY1" little-endian */
+#define EMMY_LR_VERSION 1u
+#define EMMY_LR_MAX_PARAMS 32
+#define EMMY_LR_MAX_TMAPS 4
+
+enum EmmyFamily { EMMY_FAMILY_POINTWISE = 1, EMMY_FAMILY_REDUCTION = 2, EMMY_FAMILY_GEMM = 3 };
+
+enum EmmyParamKind { EMMY_PARAM_PTR = 0, EMMY_PARAM_F32 = 1, EMMY_PARAM_I32 = 2 };
+
+/* Status bits a kernel may raise (never a trap or a fault). */
+#define EMMY_STATUS_TIMEOUT_PRODUCER 0x1u /* TMA producer gave up waiting for a free stage */
+#define EMMY_STATUS_TIMEOUT_MMA 0x2u      /* MMA issuer gave up waiting for data/accumulator */
+#define EMMY_STATUS_TIMEOUT_EPILOGUE 0x4u /* epilogue gave up waiting for an accumulator */
+#define EMMY_STATUS_BAD_LAUNCH 0x8u       /* block shape or smem the kernel cannot run under */
+#define EMMY_STATUS_TMEM_ALLOC 0x10u      /* tensor-memory allocation did not fit */
+#define EMMY_STATUS_TIMEOUT_REDUCE 0x20u  /* cross-block combine waited too long */
+
+typedef struct EmmyTmapSpec {
+    uint32_t src_param; /* index into arg_order of the global buffer */
+    uint32_t dtype;     /* CUtensorMapDataType */
+    uint32_t rank;
+    uint32_t swizzle;   /* CUtensorMapSwizzle */
+    uint64_t dims[5];   /* innermost first, elements */
+    uint64_t strides[4];/* bytes, for dims 1..rank-1 */
+    uint32_t box[5];
+    uint32_t l2_promotion; /* CUtensorMapL2promotion */
+    uint32_t reserved[3];
+} EmmyTmapSpec;
+
+typedef struct EmmyLaunchRecord {
+    uint32_t magic;
+    uint32_t version;
+    uint32_t family;
+    uint32_t flags;
+    uint32_t grid[3];
+    uint32_t block[3];
+    uint32_t dyn_smem;
+    uint32_t nparams;
+    uint32_t param_kind[EMMY_LR_MAX_PARAMS];
+    uint32_t ntmaps;
+    uint32_t reserved;
+    EmmyTmapSpec tmaps[EMMY_LR_MAX_TMAPS];
+} EmmyLaunchRecord;
+
+#endif

@@ -1,0 +1,36 @@
+.version 8.0
+.target sm_89
+.address_size 64
+
+.visible .entry k_multiply_pointwise(
+        .param .u64 param_x0,
+        .param .u64 param_x1,
+        .param .u64 param_out
+)
+.reqntid 128
+{
+        .reg .pred      %p<2>;
+        .reg .f32       %f<4>;
+        .reg .b32       %r<6>;
+        .reg .b64       %rd<7>;
+
+        ld.param.u64    %rd1, [param_x0];
+        cvta.to.global.u64     %rd1, %rd1;
+        ld.param.u64    %rd2, [param_x1];
+        cvta.to.global.u64     %rd2, %rd2;
+        ld.param.u64    %rd3, [param_out];
+        cvta.to.global.u64     %rd3, %rd3;
+        mov.u32         %r1, %tid.x;
+        mov.u32         %r2, %ntid.x;
+        mov.u32         %r3, %ctaid.x;
+        mad.lo.s32      %r4, %r3, %r2, %r1;
+        mov.u32         %r5, %nctaid.x;
+        mad.wide.s32    %rd4, %r4, 4, %rd1;
+        ld.global.nc.f32   %f1, [%rd4];
+        mad.wide.s32    %rd5, %r4, 4, %rd2;
+        ld.global.nc.f32   %f2, [%rd5];
+        mul.f32         %f3, %f1, %f2;
+        mad.wide.s32    %rd6, %r4, 4, %rd3;
+        st.global.f32   [%rd6], %f3;
+        ret;
+}

@@ -1,0 +1,40 @@
+.version 8.0
+.target sm_89
+.address_size 64
+
+.visible .entry k_add_v4(
+        .param .u64 param_x0,
+        .param .u64 param_x1,
+        .param .u64 param_out
+)
+.reqntid 128
+{
+        .reg .pred      %p<2>;
+        .reg .f32       %f<13>;
+        .reg .b32       %r<7>;
+        .reg .b64       %rd<7>;
+
+        ld.param.u64    %rd1, [param_x0];
+        cvta.to.global.u64     %rd1, %rd1;
+        ld.param.u64    %rd2, [param_x1];
+        cvta.to.global.u64     %rd2, %rd2;
+        ld.param.u64    %rd3, [param_out];
+        cvta.to.global.u64     %rd3, %rd3;
+        mov.u32         %r1, %tid.x;
+        mov.u32         %r2, %ntid.x;
+        mov.u32         %r3, %ctaid.x;
+        mad.lo.s32      %r4, %r3, %r2, %r1;
+        mov.u32         %r5, %nctaid.x;
+        shl.b32         %r6, %r4, 2;
+        mad.wide.s32    %rd4, %r6, 4, %rd1;
+        ld.global.nc.v4.f32 {%f1, %f2, %f3, %f4}, [%rd4];
+        mad.wide.s32    %rd5, %r6, 4, %rd2;
+        ld.global.nc.v4.f32 {%f5, %f6, %f7, %f8}, [%rd5];
+        add.f32         %f9, %f1, %f5;
+        add.f32         %f10, %f2, %f6;
+        add.f32         %f11, %f3, %f7;
+        add.f32         %f12, %f4, %f8;
+        mad.wide.s32    %rd6, %r6, 4, %rd3;
+        st.global.v4.f32 [%rd6], {%f9, %f10, %f11, %f12};
+        ret;
+}

@@ -1,0 +1,29 @@
+.version 8.0
+.target sm_89
+.address_size 64
+
+.visible .entry k_atomic_sum(
+        .param .u64 param_x,
+        .param .u64 param_sum_1
+)
+.reqntid 128
+{
+        .reg .pred      %p<2>;
+        .reg .f32       %f<2>;
+        .reg .b32       %r<6>;
+        .reg .b64       %rd<4>;
+
+        ld.param.u64    %rd1, [param_x];
+        cvta.to.global.u64     %rd1, %rd1;
+        ld.param.u64    %rd2, [param_sum_1];
+        cvta.to.global.u64     %rd2, %rd2;
+        mov.u32         %r1, %tid.x;
+        mov.u32         %r2, %ntid.x;
+        mov.u32         %r3, %ctaid.x;
+        mad.lo.s32      %r4, %r3, %r2, %r1;
+        mov.u32         %r5, %nctaid.x;
+        mad.wide.s32    %rd3, %r4, 4, %rd1;
+        ld.global.nc.f32   %f1, [%rd3];
+        red.global.add.f32 [%rd2], %f1;
+        ret;
+}

@@ -1,0 +1,690 @@
+#!/usr/bin/env python3
+"""Generate the golden Kernel-IR fixtures and the reference compiler's PTX.
+
+Run in a container that has the reference checkout (read-only) and the test
+shim ``oracle/emmy_shim`` (it stands in for the absent ``emmy-ml`` package):
+
+    python tests/golden/make_golden.py --reference /path/to/emmy-ptx-compiler
+
+For every case this writes ``tests/golden/cases/<case>/``:
+
+* ``<entry>.ir.json`` - an Emmy Graph whose KernelOp body is ``repr(body)``,
+  exactly the layout the reference's fixture tools write
+  (tools/make_proxy_set.py:42-55);
+* ``meta.json`` - launch geometry, ``arg_order`` and per-argument input
+  recipes, in the reference's meta schema (tools/make_proxy_set.py:75-86),
+  plus an ``init`` recipe per input and a ``check`` block (tolerances);
+* ``ref.ptx`` - what the unmodified reference ``compile.py`` prints for that
+  IR (its ``compile_bundle``, compile.py:3168), when the reference can lower
+  it.  bf16 GEMM IRs cannot be lowered by the reference (ptxas rejects its
+  ``ld.global.nc.bf16`` form), so those cases carry a sibling ``ref_f32/``
+  case: the same IR on fp32 copies of the operands, the oracle route for
+  GEMM parity.
+
+The IR shapes follow the reference's own generators: pointwise bodies
+(make_proxy_set.py:89-213), the strided warp/tree reduction schedule
+(make_proxy_set.py:215-336), the naive matmul (make_proxy_set.py:338-365) and
+the extra op mixes of make_world_set.py:68-291.  They are rebuilt here with
+our own code; nothing of the reference is copied into the repository except
+the PTX its compiler prints for these inputs.
+
+The GPU box has no reference checkout, so everything the tests need is
+committed under ``tests/golden/cases``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import math
+import shutil
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+CASES = HERE / "cases"
+BT = 128
+
+sys.path.insert(0, str(REPO / "oracle" / "emmy_shim"))
+
+import numpy as np  # noqa: E402
+from emmy.compiler.dim import Dim  # noqa: E402
+from emmy.compiler.ir.elementwise import ElementwiseImpl as EW  # noqa: E402
+from emmy.compiler.ir.expr import BinaryExpr, Literal, Var  # noqa: E402
+from emmy.compiler.ir.kernel.ir import (  # noqa: E402
+    Axis, DataType, Smem, Sync, Tile, TreeHalve, WarpShuffle,
+)
+from emmy.compiler.ir.stmt import Accum, Assign, Cond, Init, Let, Load, Loop, StridedLoop, Write  # noqa: E402
+from emmy.compiler.ir.stmt.leaves import Select, SelectBranch  # noqa: E402
+
+F32 = DataType("f32", np.dtype("float32"), 4)
+BF16 = DataType("bf16", None, 2)
+
+
+def _dt(dt: DataType) -> str:
+    return dt.name
+
+
+# ----------------------------------------------------------------- graph helpers
+
+
+def _input(name: str, shape: list[int], dtype: str = "f32") -> dict:
+    return {"op": "InputOp", "op_fields": {}, "inputs": [],
+            "outputs": [{"name": name, "shape": shape, "dtype": dtype}]}
+
+
+def _const(name: str, value: float) -> dict:
+    return {"op": "ConstantOp",
+            "op_fields": {"name": name, "value": value, "context_value": None, "load_ops": [],
+                          "source_path": None, "source_parts": [], "source_shape": None,
+                          "source_dtype": None, "source_graph": None},
+            "inputs": [], "outputs": [{"name": name, "shape": [1], "dtype": "f32"}]}
+
+
+def _kernel(entry: str, body, inputs: list[str], outputs: list[tuple[str, list[int], str]]) -> dict:
+    return {"op": "KernelOp",
+            "op_fields": {"body": [repr(body)], "name": entry, "zero_delegated": [], "serial": []},
+            "inputs": inputs,
+            "outputs": [{"name": n, "shape": s, "dtype": d} for n, s, d in outputs]}
+
+
+def _launch(n: int, block: int = BT) -> tuple[list[int], list[int]]:
+    return [max(1, math.ceil(n / block)), 1, 1], [block, 1, 1]
+
+
+class Case:
+    """One fixture directory."""
+
+    def __init__(self, cid: str, entry: str, graph: dict, kernel: dict, *, family: str,
+                 config: str | None = None, check: dict | None = None, ref: bool = True,
+                 ref_case: "Case | None" = None, tags: tuple[str, ...] = ()):
+        self.cid = cid
+        self.entry = entry
+        self.graph = graph
+        self.kernel = kernel
+        self.family = family
+        self.config = config
+        self.check = check or {}
+        self.ref = ref
+        self.ref_case = ref_case
+        self.tags = tags
+
+    def write(self, root: Path, compile_bundle) -> dict:
+        d = root / self.cid
+        if d.exists():
+            shutil.rmtree(d)
+        d.mkdir(parents=True)
+        ir_path = d / f"{self.entry}.ir.json"
+        ir_path.write_text(json.dumps(self.graph, indent=1) + "\n")
+        meta = {"id": self.cid, "family": self.family, "config": self.config,
+                "check": self.check, "tags": list(self.tags),
+                "graph_inputs": self.graph["inputs"], "graph_outputs": self.graph["outputs"],
+                "kernels": [self.kernel]}
+        (d / "meta.json").write_text(json.dumps(meta, indent=1) + "\n")
+        rec = {"id": self.cid, "entry": self.entry, "family": self.family, "config": self.config,
+               "tags": list(self.tags), "ir": str(ir_path.relative_to(root)), "ref_ptx": None,
+               "ref_case": None}
+        if self.ref:
+            bundle = compile_bundle(ir_path)
+            (d / "ref.ptx").write_text(bundle["ptx"])
+            rec["ref_ptx"] = str((d / "ref.ptx").relative_to(root))
+        if self.ref_case is not None:
+            sub = self.ref_case.write(d, compile_bundle)
+            rec["ref_case"] = f"{self.cid}/{sub['id']}"
+            rec["ref_ptx"] = f"{self.cid}/{sub['ref_ptx']}"
+        return rec
+
+
+def _arg(name: str, shape: list[int], dtype: str = "f32", *, init: dict | None = None,
+         output: bool = False, seed: int | None = None) -> dict:
+    a = {"name": name, "dtype": dtype, "shape": shape}
+    if output:
+        a["output"] = True
+    else:
+        a["seed"] = seed if seed is not None else 0
+        a["init"] = init or {"kind": "normal", "mean": 0.0, "std": 1.0}
+    return a
+
+
+def _meta_kernel(node: str, entry: str, arg_order: list[str], grid, block, args: list[dict],
+                 zero_outputs: list[str] | None = None) -> dict:
+    return {"node": node, "entry": entry, "arg_order": arg_order, "grid": grid, "block": block,
+            "smem_bytes": 0, "zero_outputs": zero_outputs or [], "args": args, "final": True}
+
+
+UNIF = lambda lo, hi: {"kind": "uniform", "low": lo, "high": hi}  # noqa: E731
+NORM = lambda std=1.0: {"kind": "normal", "mean": 0.0, "std": std}  # noqa: E731
+
+
+# ------------------------------------------------------------------ config 1 / 2
+
+
+def add_case(cid: str, n: int, *, block: int = 256, grid: int | None = None,
+             config: str | None = None) -> Case:
+    """c[i] = a[i] + b[i] (make_proxy_set.py:89-115 shape)."""
+    entry = "k_add_pointwise"
+    body = Tile(axes=(Axis("a0", Dim(n)),), body=(
+        Load(names=("in0",), input="a", index=(Var("a0"),), dtype=F32),
+        Load(names=("in1",), input="b", index=(Var("a0"),), dtype=F32),
+        Assign("v0", EW("add"), ("in0", "in1"), F32),
+        Write(output="c", index=(Var("a0"),), values=("v0",), value_dtype=F32),
+    ))
+    graph = {"inputs": ["a", "b"], "outputs": ["c"], "nodes": {
+        "a": _input("a", [n]), "b": _input("b", [n]),
+        "c": _kernel(entry, body, ["a", "b"], [("c", [n], "f32")])}}
+    g = [grid if grid is not None else max(1, math.ceil(n / block)), 1, 1]
+    kern = _meta_kernel("c", entry, ["a", "b", "c"], g, [block, 1, 1], [
+        _arg("a", [n], init=UNIF(-1.0, 1.0), seed=0),
+        _arg("b", [n], init=UNIF(-1.0, 1.0), seed=1),
+        _arg("c", [n], output=True)])
+    return Case(cid, entry, graph, kern, family="pointwise", config=config,
+                check={"kind": "ulp", "ulp": 0})
+
+
+def gelu_case(cid: str, rows: int, cols: int, *, config: str | None = None) -> Case:
+    """y = GELU_tanh(x*s + t) with per-column s, t.
+
+    GELU-tanh has no IR op of its own, so the body is the Assign chain
+    0.5*z*(1 + tanh(sqrt(2/pi)*(z + 0.044715*z^3))) with z = x*s + t; the
+    reference contracts ``x*s``+``t`` and ``z3*c``+``z`` into fma.rn
+    (compile.py:1285-1303) and lowers tanh through ex2.approx
+    (compile.py:2142-2157).
+    """
+    entry = "k_gelu_tanh_affine"
+    body = Tile(axes=(Axis("a0", Dim(rows)), Axis("a1", Dim(cols))), body=(
+        Load(names=("xv",), input="x", index=(Var("a0"), Var("a1")), dtype=F32),
+        Load(names=("sv",), input="s", index=(Var("a1"),), dtype=F32),
+        Load(names=("tv",), input="t", index=(Var("a1"),), dtype=F32),
+        Assign("xs", EW("multiply"), ("xv", "sv"), F32),
+        Assign("z", EW("add"), ("xs", "tv"), F32),
+        Assign("z2", EW("multiply"), ("z", "z"), F32),
+        Assign("z3", EW("multiply"), ("z2", "z"), F32),
+        Let("c0", Literal(0.044715, "float"), F32),
+        Assign("u0", EW("multiply"), ("z3", "c0"), F32),
+        Assign("u", EW("add"), ("z", "u0"), F32),
+        Let("c1", Literal(math.sqrt(2.0 / math.pi), "float"), F32),
+        Assign("w", EW("multiply"), ("u", "c1"), F32),
+        Assign("th", EW("tanh"), ("w",), F32),
+        Let("one", Literal(1.0, "float"), F32),
+        Assign("th1", EW("add"), ("th", "one"), F32),
+        Let("half", Literal(0.5, "float"), F32),
+        Assign("hz", EW("multiply"), ("z", "half"), F32),
+        Assign("y0", EW("multiply"), ("hz", "th1"), F32),
+        Write(output="y", index=(Var("a0"), Var("a1")), values=("y0",), value_dtype=F32),
+    ))
+    graph = {"inputs": ["x", "s", "t"], "outputs": ["y"], "nodes": {
+        "x": _input("x", [rows, cols]), "s": _input("s", [cols]), "t": _input("t", [cols]),
+        "y": _kernel(entry, body, ["x", "s", "t"], [("y", [rows, cols], "f32")])}}
+    grid, block = _launch(rows * cols)
+    kern = _meta_kernel("y", entry, ["x", "s", "t", "y"], grid, block, [
+        _arg("x", [rows, cols], init=NORM(), seed=0),
+        _arg("s", [cols], init=UNIF(0.5, 1.5), seed=1),
+        _arg("t", [cols], init=UNIF(-0.1, 0.1), seed=2),
+        _arg("y", [rows, cols], output=True)])
+    return Case(cid, entry, graph, kern, family="pointwise", config=config,
+                check={"kind": "ulp", "ulp": 1, "oracle_ulp": 8})
+
+
+# ------------------------------------------------------------------ config 3 / 4
+
+
+def _reduce_body(red_axis: Axis, start: str, index, accs: list[tuple[str, str]],
+                 outs: list[tuple[str, tuple]], post=()) -> tuple:
+    """The reference's strided warp/tree schedule (make_proxy_set.py:226-253),
+    generalised to several accumulators sharing one pass over the input."""
+    loads = (Load(names=("in0",), input="x", index=index, dtype=F32),)
+    accums = tuple(Accum(a, "in0", EW(op), F32, axes=(red_axis.name,)) for a, op in accs)
+    combine = tuple(Assign(a, EW(op), (a, f"{a}__o"), None) for a, op in accs)
+    smems = tuple(Smem(f"{a}_smem", (BT // 32,), "float", 0) for a, _ in accs)
+    lane_writes = tuple(Write(output=f"{a}_smem", index=(Var("warp"),), values=(a,), value_dtype=F32)
+                        for a, _ in accs)
+    final = tuple(Write(output=o, index=idx, values=(a,), value_dtype=F32)
+                  for (a, _), (o, idx) in zip(accs, outs))
+    return (
+        StridedLoop(axis=red_axis, start=Var(start), step=Literal(BT, "int"), body=loads + accums),
+        WarpShuffle(state=tuple(a for a, _ in accs), state_b=tuple(f"{a}__o" for a, _ in accs),
+                    combine_states=combine, length=32, dtype=F32),
+        *smems,
+        Cond(BinaryExpr("==", Var("lane"), Literal(0, "int")), body=lane_writes),
+        Sync(),
+        TreeHalve(bufs=tuple(f"{a}_smem" for a, _ in accs), state=tuple(a for a, _ in accs),
+                  state_b=tuple(f"{a}__o" for a, _ in accs), combine_states=combine,
+                  length=BT // 32, tid_var="warp", dtype=F32),
+        *post,
+        Cond(BinaryExpr("==", Var(start), Literal(0, "int")), body=final),
+    )
+
+
+def rowsummax_case(cid: str, rows: int, cols: int, *, config: str | None = None) -> Case:
+    """row sum and row max of x[rows, cols] in one pass."""
+    entry = "k_row_sum_max_reduce"
+    body = Tile(axes=(Axis("a0", Dim(rows)), Axis("a1_co", Dim(BT))),
+                body=_reduce_body(Axis("a1", Dim(cols)), "a1_co", (Var("a0"), Var("a1")),
+                                  [("acc0", "add"), ("acc1", "maximum")],
+                                  [("sum_1", (Var("a0"),)), ("max_1", (Var("a0"),))]),
+                block_threads=BT)
+    graph = {"inputs": ["x"], "outputs": ["sum_1", "max_1"], "nodes": {
+        "x": _input("x", [rows, cols]),
+        "sum_1": _kernel(entry, body, ["x"], [("sum_1", [rows], "f32"), ("max_1", [rows], "f32")])}}
+    kern = _meta_kernel("sum_1", entry, ["x", "sum_1", "max_1"], [rows, 1, 1], [BT, 1, 1], [
+        _arg("x", [rows, cols], init=NORM(), seed=0),
+        _arg("sum_1", [rows], output=True), _arg("max_1", [rows], output=True)])
+    return Case(cid, entry, graph, kern, family="reduction", config=config,
+                check={"kind": "rtol", "rtol": 1e-5, "atol": 1e-5, "exact_outputs": ["max_1"]})
+
+
+def fullsum_case(cid: str, n: int, *, config: str | None = None, ref: bool = True,
+                 dist: dict | None = None) -> Case:
+    """sum of x[n] (make_proxy_set.py:256-268 schedule, one block)."""
+    entry = "k_sum_1_reduce"
+    body = Tile(axes=(Axis("a0_co", Dim(BT)),),
+                body=_reduce_body(Axis("a0", Dim(n)), "a0_co", (Var("a0"),), [("acc0", "add")],
+                                  [("sum_1", ())]),
+                block_threads=BT)
+    graph = {"inputs": ["x"], "outputs": ["sum_1"], "nodes": {
+        "x": _input("x", [n]), "sum_1": _kernel(entry, body, ["x"], [("sum_1", [], "f32")])}}
+    kern = _meta_kernel("sum_1", entry, ["x", "sum_1"], [1, 1, 1], [BT, 1, 1], [
+        _arg("x", [n], init=dist or UNIF(-1.0, 1.0), seed=0), _arg("sum_1", [1], output=True)])
+    return Case(cid, entry, graph, kern, family="reduction", config=config, ref=ref,
+                check={"kind": "rtol", "rtol": 1e-5, "atol": 1e-4})
+
+
+def mean_case(cid: str, n: int) -> Case:
+    """make_proxy_set.py:293-318: full mean = sum then multiply by 1/n."""
+    entry = "k_mean_reduce"
+    post = (Let("invn", Literal(1.0 / n, "float"), F32),
+            Assign("acc0", EW("multiply"), ("acc0", "invn"), F32))
+    body = Tile(axes=(Axis("a0_co", Dim(BT)),),
+                body=_reduce_body(Axis("a0", Dim(n)), "a0_co", (Var("a0"),), [("acc0", "add")],
+                                  [("mean", ())], post=post),
+                block_threads=BT)
+    graph = {"inputs": ["x"], "outputs": ["mean"], "nodes": {
+        "x": _input("x", [n]), "mean": _kernel(entry, body, ["x"], [("mean", [], "f32")])}}
+    kern = _meta_kernel("mean", entry, ["x", "mean"], [1, 1, 1], [BT, 1, 1], [
+        _arg("x", [n], init=NORM(), seed=0), _arg("mean", [1], output=True)])
+    return Case(cid, entry, graph, kern, family="reduction", check={"kind": "rtol", "rtol": 1e-5,
+                                                                     "atol": 1e-6})
+
+
+def fullmax_case(cid: str, n: int) -> Case:
+    entry = "k_max_1_reduce"
+    body = Tile(axes=(Axis("a0_co", Dim(BT)),),
+                body=_reduce_body(Axis("a0", Dim(n)), "a0_co", (Var("a0"),), [("acc0", "maximum")],
+                                  [("max_1", ())]),
+                block_threads=BT)
+    graph = {"inputs": ["x"], "outputs": ["max_1"], "nodes": {
+        "x": _input("x", [n]), "max_1": _kernel(entry, body, ["x"], [("max_1", [], "f32")])}}
+    kern = _meta_kernel("max_1", entry, ["x", "max_1"], [1, 1, 1], [BT, 1, 1], [
+        _arg("x", [n], init=NORM(), seed=0), _arg("max_1", [1], output=True)])
+    return Case(cid, entry, graph, kern, family="reduction", check={"kind": "exact"})
+
+
+def rowsum_loop_case(cid: str, rows: int, cols: int) -> Case:
+    """One thread per row, a plain ``Loop`` over the columns (no warp/tree stage)."""
+    entry = "k_row_sumsq_loop"
+    body = Tile(axes=(Axis("r", Dim(rows)),), body=(
+        Init("acc", 0.0, dtype=F32),
+        Loop(axis=Axis("c", Dim(cols)), body=(
+            Load(names=("v",), input="x", index=(Var("r"), Var("c")), dtype=F32),
+            Assign("sq", EW("multiply"), ("v", "v"), F32),
+            Accum("acc", "sq", EW("add"), F32, axes=("c",)),
+        )),
+        Write(output="ss", index=(Var("r"),), values=("acc",), value_dtype=F32),
+    ))
+    graph = {"inputs": ["x"], "outputs": ["ss"], "nodes": {
+        "x": _input("x", [rows, cols]), "ss": _kernel(entry, body, ["x"], [("ss", [rows], "f32")])}}
+    grid, block = _launch(rows)
+    kern = _meta_kernel("ss", entry, ["x", "ss"], grid, block, [
+        _arg("x", [rows, cols], init=NORM(), seed=0), _arg("ss", [rows], output=True)])
+    return Case(cid, entry, graph, kern, family="reduction", check={"kind": "rtol", "rtol": 1e-5,
+                                                                     "atol": 1e-5})
+
+
+def atomic_sum_case(cid: str, n: int) -> Case:
+    """make_world_set.py:247-266: every cell red.add's into sum_1[0]."""
+    entry = "k_atomic_sum"
+    body = Tile(axes=(Axis("a0", Dim(n)),), body=(
+        Load(names=("in0",), input="x", index=(Var("a0"),), dtype=F32),
+        Write(output="sum_1", index=(), values=("in0",), value_dtype=F32, atomic=True),
+    ))
+    graph = {"inputs": ["x"], "outputs": ["sum_1"], "nodes": {
+        "x": _input("x", [n]), "sum_1": _kernel(entry, body, ["x"], [("sum_1", [], "f32")])}}
+    grid, block = _launch(n)
+    kern = _meta_kernel("sum_1", entry, ["x", "sum_1"], grid, block, [
+        _arg("x", [n], init=NORM(), seed=0), _arg("sum_1", [1], output=True)],
+        zero_outputs=["sum_1"])
+    return Case(cid, entry, graph, kern, family="reduction", check={"kind": "rtol", "rtol": 1e-5,
+                                                                     "atol": 1e-4})
+
+
+# ------------------------------------------------------------------ config 5
+
+
+def gemm_case(cid: str, m: int, k: int, n: int, *, dtype: DataType = BF16, epilogue: bool = True,
+              config: str | None = None, with_ref: bool = True) -> Case:
+    """C = relu(A@B + bias), the naive matmul IR
+    (make_proxy_set.py:338-365) plus a bias/ReLU epilogue.  bf16 operands and
+    output, fp32 accumulate."""
+    entry = "k_matmul_bias_relu" if epilogue else "k_matmul"
+    out_dt = dtype
+    tail: tuple = ()
+    res = "acc0"
+    if epilogue:
+        tail = (Load(names=("bj",), input="bias", index=(Var("j"),), dtype=F32),
+                Assign("v0", EW("add"), ("acc0", "bj"), F32),
+                Assign("v1", EW("relu"), ("v0",), F32))
+        res = "v1"
+    body = Tile(axes=(Axis("i", Dim(m)), Axis("j", Dim(n))), body=(
+        Init("acc0", 0.0, dtype=F32),
+        Loop(axis=Axis("kk", Dim(k)), body=(
+            Load(names=("a",), input="A", index=(Var("i"), Var("kk")), dtype=dtype),
+            Load(names=("b",), input="B", index=(Var("kk"), Var("j")), dtype=dtype),
+            Assign("p", EW("multiply"), ("a", "b"), F32),
+            Accum("acc0", "p", EW("add"), F32, axes=("kk",)),
+        )),
+        *tail,
+        Write(output="C", index=(Var("i"), Var("j")), values=(res,), value_dtype=out_dt),
+    ))
+    ins = ["A", "B"] + (["bias"] if epilogue else [])
+    nodes = {"A": _input("A", [m, k], _dt(dtype)), "B": _input("B", [k, n], _dt(dtype))}
+    if epilogue:
+        nodes["bias"] = _input("bias", [n], "f32")
+    nodes["C"] = _kernel(entry, body, ins, [("C", [m, n], _dt(out_dt))])
+    graph = {"inputs": ins, "outputs": ["C"], "nodes": nodes}
+    grid, block = _launch(m * n)
+    std = 0.02 if epilogue else 1.0
+    args = [_arg("A", [m, k], _dt(dtype), init=NORM(std), seed=0),
+            _arg("B", [k, n], _dt(dtype), init=NORM(std), seed=1)]
+    if epilogue:
+        args.append(_arg("bias", [n], "f32", init=NORM(std), seed=2))
+    args.append(_arg("C", [m, n], _dt(out_dt), output=True))
+    kern = _meta_kernel("C", entry, ins + ["C"], grid, block, args)
+    ref_case = None
+    ref = True
+    if dtype.name == "bf16":
+        ref = False
+        if with_ref:
+            ref_case = gemm_case("ref_f32", m, k, n, dtype=F32, epilogue=epilogue, with_ref=False)
+            ref_case.check = {"kind": "oracle_route",
+                              "note": "fp32 copies of the bf16 operands; output rounded to bf16 RNE"}
+    check = {"kind": "rtol", "rtol": 1e-2, "atol": 1e-2}
+    if dtype.name == "f32":
+        check = {"kind": "rtol", "rtol": 1e-5, "atol": 1e-5}
+    return Case(cid, entry, graph, kern, family="gemm", config=config, check=check, ref=ref,
+                ref_case=ref_case)
+
+
+# ------------------------------------------------------------ reference op catalog
+
+
+def unary_case(cid: str, op: str, n: int, *, prep_abs: float | None = None, extra=()) -> Case:
+    """make_proxy_set.py:118-142 / make_world_set.py:68-99 shapes."""
+    entry = f"k_{op}_pointwise"
+    pre: tuple = ()
+    src = "in0"
+    if prep_abs is not None:
+        pre = (Assign("ab", EW("abs"), ("in0",), F32),
+               Let("eps", Literal(prep_abs, "float"), F32),
+               Assign("pz", EW("add"), ("ab", "eps"), F32))
+        src = "pz"
+    lets = tuple(Let(e, Literal(0.01, "float"), F32) for e in extra)
+    body = Tile(axes=(Axis("a0", Dim(n)),), body=lets + (
+        Load(names=("in0",), input="x", index=(Var("a0"),), dtype=F32),
+        *pre,
+        Assign("v0", EW(op), (src,) + tuple(extra), F32),
+        Write(output="out", index=(Var("a0"),), values=("v0",), value_dtype=F32),
+    ))
+    graph = {"inputs": ["x"], "outputs": ["out"], "nodes": {
+        "x": _input("x", [n]), "out": _kernel(entry, body, ["x"], [("out", [n], "f32")])}}
+    grid, block = _launch(n)
+    kern = _meta_kernel("out", entry, ["x", "out"], grid, block, [
+        _arg("x", [n], init=NORM(), seed=0), _arg("out", [n], output=True)])
+    return Case(cid, entry, graph, kern, family="pointwise",
+                check={"kind": "ulp", "ulp": 0, "oracle_ulp": 8}, tags=("catalog",))
+
+
+def binary_case(cid: str, op: str, n: int) -> Case:
+    entry = f"k_{op}_pointwise"
+    body = Tile(axes=(Axis("a0", Dim(n)),), body=(
+        Load(names=("in0",), input="x0", index=(Var("a0"),), dtype=F32),
+        Load(names=("in1",), input="x1", index=(Var("a0"),), dtype=F32),
+        Assign("v0", EW(op), ("in0", "in1"), F32),
+        Write(output="out", index=(Var("a0"),), values=("v0",), value_dtype=F32),
+    ))
+    graph = {"inputs": ["x0", "x1"], "outputs": ["out"], "nodes": {
+        "x0": _input("x0", [n]), "x1": _input("x1", [n]),
+        "out": _kernel(entry, body, ["x0", "x1"], [("out", [n], "f32")])}}
+    grid, block = _launch(n)
+    kern = _meta_kernel("out", entry, ["x0", "x1", "out"], grid, block, [
+        _arg("x0", [n], seed=0), _arg("x1", [n], seed=1), _arg("out", [n], output=True)])
+    return Case(cid, entry, graph, kern, family="pointwise", check={"kind": "ulp", "ulp": 0},
+                tags=("catalog",))
+
+
+def chain_case(cid: str, n: int, which: str) -> Case:
+    """Multi-statement pointwise mixes: relu_mul, scale_shift, leaky, clamp,
+    where, select, cond_else, 2-D add, square_scale (make_proxy_set.py:145-213,
+    367-390; make_world_set.py:164-245, 294-341)."""
+    x = Load(names=("in0",), input="x", index=(Var("a0"),), dtype=F32)
+    y = Load(names=("in1",), input="y", index=(Var("a0"),), dtype=F32)
+    two_inputs = which in ("relu_mul", "where")
+    if which == "relu_mul":
+        stmts = (x, Assign("v0", EW("relu"), ("in0",), F32), y,
+                 Assign("r", EW("multiply"), ("v0", "in1"), F32))
+    elif which == "scale_shift":
+        stmts = (x, Let("s", Literal(2.0, "float"), F32), Let("b", Literal(1.0, "float"), F32),
+                 Assign("v0", EW("multiply"), ("in0", "s"), F32),
+                 Assign("r", EW("add"), ("v0", "b"), F32))
+    elif which == "leaky":
+        stmts = (x, Let("z", Literal(0.0, "float"), F32), Let("s", Literal(0.01, "float"), F32),
+                 Assign("p", EW("greater"), ("in0", "z"), F32),
+                 Assign("sc", EW("multiply"), ("in0", "s"), F32),
+                 Assign("r", EW("where"), ("p", "in0", "sc"), F32))
+    elif which == "clamp":
+        stmts = (x, Let("lo", Literal(-0.5, "float"), F32), Let("hi", Literal(0.5, "float"), F32),
+                 Assign("t0", EW("maximum"), ("in0", "lo"), F32),
+                 Assign("r", EW("minimum"), ("t0", "hi"), F32))
+    elif which == "where":
+        stmts = (x, y, Assign("p", EW("greater"), ("in0", "in1"), F32),
+                 Assign("r", EW("where"), ("p", "in0", "in1"), F32))
+    elif which == "select":
+        stmts = (x, Let("z", Literal(0.0, "float"), F32),
+                 Select("r", (SelectBranch("in0", BinaryExpr(">", Var("in0"), Var("z"))),
+                              SelectBranch("z", Literal(1, "int")))))
+    elif which == "cond_else":
+        stmts = (x, Init("r", 0.0, dtype=F32),
+                 Cond(BinaryExpr(">", Var("a0"), Literal(n // 2, "int")),
+                      body=(Assign("r", EW("relu"), ("in0",), F32),),
+                      else_body=(Assign("r", EW("negative"), ("in0",), F32),)))
+    elif which == "square_scale":
+        stmts = (x, Assign("v0", EW("square"), ("in0",), F32), Let("s", Literal(0.5, "float"), F32),
+                 Assign("r", EW("multiply"), ("v0", "s"), F32))
+    elif which == "silu_sigmoid":
+        stmts = (x, Assign("sg", EW("sigmoid"), ("in0",), F32),
+                 Assign("sl", EW("silu"), ("in0",), F32),
+                 Assign("r", EW("add"), ("sg", "sl"), F32))
+    elif which == "exp_log_sqrt":
+        stmts = (x, Assign("ab", EW("abs"), ("in0",), F32), Let("e", Literal(1e-3, "float"), F32),
+                 Assign("p", EW("add"), ("ab", "e"), F32), Assign("l", EW("log"), ("p",), F32),
+                 Assign("q", EW("sqrt"), ("p",), F32), Assign("rq", EW("rsqrt"), ("p",), F32),
+                 Assign("ex", EW("exp"), ("l",), F32), Assign("m", EW("multiply"), ("q", "rq"), F32),
+                 Assign("d", EW("divide"), ("ex", "m"), F32), Assign("r", EW("add"), ("d", "l"), F32))
+    else:
+        raise ValueError(which)
+    entry = f"k_{which}"
+    body = Tile(axes=(Axis("a0", Dim(n)),), body=stmts + (
+        Write(output="out", index=(Var("a0"),), values=("r",), value_dtype=F32),))
+    ins = ["x", "y"] if two_inputs else ["x"]
+    nodes = {i: _input(i, [n]) for i in ins}
+    nodes["out"] = _kernel(entry, body, ins, [("out", [n], "f32")])
+    graph = {"inputs": ins, "outputs": ["out"], "nodes": nodes}
+    grid, block = _launch(n)
+    args = [_arg(i, [n], seed=k) for k, i in enumerate(ins)] + [_arg("out", [n], output=True)]
+    kern = _meta_kernel("out", entry, ins + ["out"], grid, block, args)
+    approx = which in ("silu_sigmoid", "exp_log_sqrt")
+    return Case(cid, entry, graph, kern, family="pointwise",
+                check={"kind": "ulp", "ulp": 0, "oracle_ulp": 16 if approx else 0},
+                tags=("catalog",))
+
+
+def add2d_case(cid: str, h: int, w: int) -> Case:
+    """make_proxy_set.py:186-212: 2-D add, one cell per (a0, a1)."""
+    entry = "k_add2d_pointwise"
+    body = Tile(axes=(Axis("a0", Dim(h)), Axis("a1", Dim(w))), body=(
+        Load(names=("in0",), input="x0", index=(Var("a0"), Var("a1")), dtype=F32),
+        Load(names=("in1",), input="x1", index=(Var("a0"), Var("a1")), dtype=F32),
+        Load(names=("rb",), input="rowb", index=(Var("a0"),), dtype=F32),
+        Assign("v0", EW("add"), ("in0", "in1"), F32),
+        Assign("v1", EW("subtract"), ("v0", "rb"), F32),
+        Write(output="out", index=(Var("a0"), Var("a1")), values=("v1",), value_dtype=F32),
+    ))
+    graph = {"inputs": ["x0", "x1", "rowb"], "outputs": ["out"], "nodes": {
+        "x0": _input("x0", [h, w]), "x1": _input("x1", [h, w]), "rowb": _input("rowb", [h]),
+        "out": _kernel(entry, body, ["x0", "x1", "rowb"], [("out", [h, w], "f32")])}}
+    grid, block = _launch(h * w)
+    kern = _meta_kernel("out", entry, ["x0", "x1", "rowb", "out"], grid, block, [
+        _arg("x0", [h, w], seed=0), _arg("x1", [h, w], seed=1), _arg("rowb", [h], seed=2),
+        _arg("out", [h, w], output=True)])
+    return Case(cid, entry, graph, kern, family="pointwise", check={"kind": "ulp", "ulp": 0},
+                tags=("catalog",))
+
+
+def vec4_case(cid: str, n: int) -> Case:
+    """make_world_set.py:102-131: the IR groups four consecutive cells."""
+    entry = "k_add_v4"
+    tiles = n // 4
+    idx = lambda k: BinaryExpr("+", BinaryExpr("*", Var("a0"), Literal(4, "int")), Literal(k, "int"))  # noqa: E731
+    stmts = []
+    for k in range(4):
+        stmts += [Load(names=(f"l{k}",), input="x0", index=(idx(k),), dtype=F32),
+                  Load(names=(f"r{k}",), input="x1", index=(idx(k),), dtype=F32),
+                  Assign(f"v{k}", EW("add"), (f"l{k}", f"r{k}"), F32)]
+    body = Tile(axes=(Axis("a0", Dim(tiles)),), body=tuple(stmts) + (
+        Write(output="out", index=(idx(0),), values=("v0", "v1", "v2", "v3"), value_dtype=F32),))
+    graph = {"inputs": ["x0", "x1"], "outputs": ["out"], "nodes": {
+        "x0": _input("x0", [n]), "x1": _input("x1", [n]),
+        "out": _kernel(entry, body, ["x0", "x1"], [("out", [n], "f32")])}}
+    grid, block = _launch(tiles)
+    kern = _meta_kernel("out", entry, ["x0", "x1", "out"], grid, block, [
+        _arg("x0", [n], seed=0), _arg("x1", [n], seed=1), _arg("out", [n], output=True)])
+    return Case(cid, entry, graph, kern, family="pointwise", check={"kind": "ulp", "ulp": 0},
+                tags=("catalog",))
+
+
+def const_scale_case(cid: str, n: int) -> Case:
+    """make_world_set.py:134-161: ConstantOp inputs read at index 0."""
+    entry = "k_const_scale"
+    body = Tile(axes=(Axis("a0", Dim(n)),), body=(
+        Load(names=("c0",), input="mul_c", index=(Literal(0, "int"),), dtype=F32),
+        Load(names=("c1",), input="add_c", index=(Literal(0, "int"),), dtype=F32),
+        Load(names=("in0",), input="x", index=(Var("a0"),), dtype=F32),
+        Assign("v0", EW("multiply"), ("in0", "c0"), F32),
+        Assign("v1", EW("add"), ("v0", "c1"), F32),
+        Write(output="out", index=(Var("a0"),), values=("v1",), value_dtype=F32),
+    ))
+    graph = {"inputs": ["x"], "outputs": ["out"], "nodes": {
+        "mul_c": _const("mul_c", 3.0), "add_c": _const("add_c", -0.5), "x": _input("x", [n]),
+        "out": _kernel(entry, body, ["mul_c", "add_c", "x"], [("out", [n], "f32")])}}
+    grid, block = _launch(n)
+    kern = _meta_kernel("out", entry, ["mul_c", "add_c", "x", "out"], grid, block, [
+        {"name": "mul_c", "dtype": "f32", "shape": [1], "data": [3.0]},
+        {"name": "add_c", "dtype": "f32", "shape": [1], "data": [-0.5]},
+        _arg("x", [n], seed=0), _arg("out", [n], output=True)])
+    return Case(cid, entry, graph, kern, family="pointwise", check={"kind": "ulp", "ulp": 0},
+                tags=("catalog",))
+
+
+def launch3d_case(cid: str, n: int = 64) -> Case:
+    """make_world_set.py:269-291: a 3-D block launch of a 1-D Tile."""
+    c = binary_case(cid, "add", n)
+    c.entry = "k_add_3d"
+    c.kernel["entry"] = "k_add_3d"
+    body_node = c.graph["nodes"]["out"]
+    body_node["op_fields"]["name"] = "k_add_3d"
+    c.kernel["grid"] = [1, 1, 1]
+    c.kernel["block"] = [8, 4, 2]
+    return c
+
+
+# ------------------------------------------------------------------ registry
+
+
+def all_cases() -> list[Case]:
+    cases: list[Case] = []
+    # config 1
+    cases.append(add_case("c1_add_64", 64, block=256, grid=1, config="c1"))
+    cases.append(add_case("c1_add_1000", 1000))
+    # config 2
+    cases.append(gelu_case("c2_gelu_full", 16384, 16384, config="c2"))
+    cases.append(gelu_case("c2_gelu_256x4096", 256, 4096))
+    cases.append(gelu_case("c2_gelu_64x1000", 64, 1000))
+    cases.append(gelu_case("c2_gelu_3x7", 3, 7))
+    cases.append(gelu_case("c2_gelu_1x1", 1, 1))
+    # config 3
+    cases.append(rowsummax_case("c3_rowsummax_full", 8192, 65536, config="c3"))
+    cases.append(rowsummax_case("c3_rowsummax_64x5000", 64, 5000))
+    cases.append(rowsummax_case("c3_rowsummax_16x65536", 16, 65536))
+    cases.append(rowsummax_case("c3_rowsummax_300x200", 300, 200))
+    cases.append(rowsummax_case("c3_rowsummax_5x64", 5, 64))
+    # config 4 (the reference indexes in s32, so it cannot lower n = 2^31 as one launch;
+    # its oracle route is 2^28-element chunks)
+    cases.append(fullsum_case("c4_sum_full", 1 << 31, config="c4", ref=False))
+    cases.append(fullsum_case("c4_sum_chunk_2p28", 1 << 28))
+    cases.append(fullsum_case("c4_sum_1048579", (1 << 20) + 3))
+    cases.append(fullsum_case("c4_sum_1000", 1000))
+    cases.append(fullsum_case("c4_sum_1", 1))
+    cases.append(mean_case("r_mean_777", 777))
+    cases.append(fullmax_case("r_max_1024", 1024))
+    cases.append(rowsum_loop_case("r_rowsumsq_loop_33x250", 33, 250))
+    cases.append(atomic_sum_case("r_atomic_sum_512", 512))
+    # config 5
+    cases.append(gemm_case("c5_gemm_full", 16384, 8192, 16384, config="c5", with_ref=False))
+    cases.append(gemm_case("c5_gemm_128x64x256", 128, 64, 256))
+    cases.append(gemm_case("c5_gemm_256x512x512", 256, 512, 512))
+    cases.append(gemm_case("c5_gemm_384x1024x768", 384, 1024, 768))
+    cases.append(gemm_case("c5_gemm_200x136x300", 200, 136, 300))
+    cases.append(gemm_case("m_matmul_f32_17x33x19", 17, 33, 19, dtype=F32, epilogue=False))
+    cases.append(gemm_case("m_matmul_f32_64x64x64", 64, 64, 64, dtype=F32, epilogue=False))
+    cases.append(gemm_case("m_matmul_f32_bias_96x160x80", 96, 160, 80, dtype=F32))
+    # the reference generators' pointwise catalog
+    for op, n in (("add", 333), ("subtract", 512), ("multiply", 768), ("maximum", 4096),
+                  ("minimum", 256), ("divide", 200)):
+        cases.append(binary_case(f"p_{op}_{n}", op, n))
+    for op, n, pa in (("relu", 1000, None), ("exp", 256, None), ("tanh", 512, None),
+                      ("sigmoid", 384, None), ("abs", 222, None), ("negative", 111, None),
+                      ("sqrt", 256, 1e-6), ("rsqrt", 192, 1e-3), ("log", 160, 1e-3),
+                      ("silu", 200, None), ("copy", 96, None), ("square", 300, None),
+                      ("reciprocal", 130, None), ("exp2", 64, None), ("log2", 70, 1e-3)):
+        cases.append(unary_case(f"p_{op}_{n}", op, n, prep_abs=pa))
+    for which, n in (("relu_mul", 300), ("scale_shift", 1536), ("leaky", 180), ("clamp", 240),
+                     ("where", 384), ("select", 256), ("cond_else", 300), ("square_scale", 512),
+                     ("silu_sigmoid", 4100), ("exp_log_sqrt", 2051)):
+        cases.append(chain_case(f"p_{which}_{n}", n, which))
+    cases.append(add2d_case("p_add2d_7x13", 7, 13))
+    cases.append(add2d_case("p_add2d_32x64", 32, 64))
+    cases.append(vec4_case("p_vec4_1024", 1024))
+    cases.append(const_scale_case("p_const_scale_777", 777))
+    cases.append(launch3d_case("p_launch3d_64"))
+    return cases
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, help="path of the reference checkout")
+    args = ap.parse_args()
+    sys.path.insert(0, str(Path(args.reference).resolve()))
+    sys.dont_write_bytecode = True
+    ref = importlib.import_module("compile")
+    CASES.mkdir(parents=True, exist_ok=True)
+    index = []
+    for case in all_cases():
+        index.append(case.write(CASES, ref.compile_bundle))
+    (CASES / "INDEX.json").write_text(json.dumps({"cases": index}, indent=1) + "\n")
+    print(f"wrote {len(index)} cases under {CASES}", file=sys.stderr)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
