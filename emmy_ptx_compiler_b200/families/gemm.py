@@ -1,9 +1,526 @@
-"""GEMM family (placeholder while the tcgen05 kernel is written)."""
+"""GEMM family: ``C[i, j] = epilogue(sum_k A[i, k] * B[k, j])``.
+
+Recognises the reference's naive matmul schedule (tools/make_proxy_set.py:
+338-365): a Tile over (i, j), ``Init acc``, ``Loop(kk)`` with two Loads, a
+``multiply`` and an ``Accum add`` (the reference lowers it to one thread per
+output running ``fma.rn.f32`` over k, compile.py:1813-1864, 1263-1283),
+followed by per-output epilogue statements (bias add, ReLU, ... ) and the
+Write of C.
+
+Two kernels:
+
+* ``tcgen05`` - bf16/fp16 operands, fp32 accumulation on the 5th-generation
+  tensor cores.  Persistent, warp-specialised CTAs of 192 threads: warp 0
+  issues TMA tile loads (128x64 of A, 64x256 of B, 128-byte swizzle) into a
+  4-stage mbarrier ring, warp 1 allocates 512 TMEM columns and issues
+  ``tcgen05.mma.cta_group::1.kind::f16`` 128x256x16 instructions into one of
+  two TMEM accumulators, warps 2-5 drain the other accumulator with
+  ``tcgen05.ld``, run the IR's epilogue in registers and store C - so the
+  epilogue of tile t overlaps the main loop of tile t+1.  Every wait is
+  bounded (a timeout raises a status bit instead of hanging).  Needs K and,
+  for a [K, N] B, N to be multiples of 8 (16-byte TMA strides).
+* ``simt`` - everything else (f32 operands, ragged strides): shared-memory
+  tiles and CUDA-core FMAs, each output accumulated in k order exactly as the
+  reference's loop does, so f32 results match the reference PTX bit for bit.
+"""
+
+from __future__ import annotations
+
+import re
+from dataclasses import dataclass
+
+from .. import ir
+from ..cgen import DEVICE_PRELUDE, Emitter, ctype, f32_lit, store_from
+from ..errors import UnsupportedIR
+from .common import KernelSource, LaunchPlan, ParamSpec, SM_COUNT, TmapSpec, launch_record_source
+
+BM, BN, BK, STAGES = 128, 256, 64, 4
+TC_THREADS = 192
+SIMT_BM, SIMT_BN, SIMT_BK, SIMT_THREADS = 64, 64, 16, 256
+GROUP_M = 16
+TMAP_DTYPE = {"bf16": 9, "f16": 6}
+SWIZZLE_128B = 3
+L2_256B = 3
 
 
-def match(kop, shapes, dtypes):
-    return None
+@dataclass
+class GemmPlan:
+    i: str
+    j: str
+    k: str
+    M: int
+    N: int
+    K: int
+    a: ir.Load
+    b: ir.Load
+    b_nk: bool            # B stored [N, K] (K-major) instead of [K, N]
+    acc: str
+    seed: float
+    epilogue: tuple
+    out: ir.Write | None
+    ab_dtype: str
 
 
-def generate(*a, **k):
-    raise NotImplementedError
+def _var_names(index) -> list[str] | None:
+    out = []
+    for ix in index:
+        if not isinstance(ix, ir.Var):
+            return None
+        out.append(ix.name)
+    return out
+
+
+def match(kop: ir.KernelOp, shapes: dict, dtypes: dict) -> GemmPlan | None:
+    body = ir.body_stmts(kop.body)
+    if len(body) != 1 or not isinstance(body[0], ir.Tile):
+        return None
+    tile = body[0]
+    if len(tile.axes) != 2:
+        return None
+    (i, M), (j, N) = [(a.name, a.size) for a in tile.axes]
+    stmts = list(ir.body_stmts(tile.body))
+    loops = [s for s in stmts if isinstance(s, ir.Loop)]
+    if len(loops) != 1 or any(isinstance(s, ir.StridedLoop) for s in stmts):
+        return None
+    loop = loops[0]
+    k, K = loop.axis.name, loop.axis.size
+    lb = list(ir.body_stmts(loop.body))
+    if len(lb) != 4 or not all(isinstance(s, ir.Load) for s in lb[:2]):
+        return None
+    l0, l1, mul, acc = lb
+    if not (isinstance(mul, ir.Assign) and ir.op_name(mul.op) == "multiply" and len(mul.args) == 2
+            and isinstance(acc, ir.Accum) and ir.op_name(acc.op) in ("add", "sum") and acc.value == mul.name
+            and acc.base in (None, acc.name) and set(mul.args) == {l0.names[0], l1.names[0]}
+            and len(l0.names) == 1 and len(l1.names) == 1):
+        return None
+    n0, n1 = _var_names(l0.index), _var_names(l1.index)
+    if n0 is None or n1 is None:
+        return None
+    if n0 == [i, k]:
+        a, b, nb = l0, l1, n1
+    elif n1 == [i, k]:
+        a, b, nb = l1, l0, n0
+    else:
+        return None
+    if nb == [k, j]:
+        b_nk = False
+    elif nb == [j, k]:
+        b_nk = True
+    else:
+        return None
+    if tuple(shapes.get(a.input, (M, K))) != (M, K):
+        return None
+    if tuple(shapes.get(b.input, ())) != ((N, K) if b_nk else (K, N)):
+        return None
+    li = stmts.index(loop)
+    seed = 0.0
+    for s in stmts[:li]:
+        if isinstance(s, ir.Init) and s.name == acc.name:
+            seed = float(s.identity)
+        elif not isinstance(s, (ir.Init, ir.Let)):
+            return None
+    epi = tuple(stmts[li + 1:])
+    for s in ir.walk(epi):
+        if isinstance(s, (ir.Loop, ir.StridedLoop, ir.Accum, ir.Smem, ir.Sync, ir.WarpShuffle, ir.TreeHalve)):
+            return None
+        if isinstance(s, ir.Write) and s.atomic:
+            return None
+    writes = [s for s in ir.walk(epi) if isinstance(s, ir.Write)]
+    if not writes:
+        return None
+    out = None
+    if (len(writes) == 1 and writes[0] in epi and _var_names(writes[0].index) == [i, j]
+            and len(writes[0].values) == 1 and tuple(shapes.get(writes[0].output, (M, N))) == (M, N)):
+        out = writes[0]
+    adt = ir.canon_dtype(a.dtype or dtypes.get(a.input))
+    bdt = ir.canon_dtype(b.dtype or dtypes.get(b.input))
+    if adt != bdt or adt not in ("f32", "bf16", "f16"):
+        raise UnsupportedIR(f"GEMM operands {adt} x {bdt} (need matching f32, bf16 or f16)")
+    return GemmPlan(i, j, k, M, N, K, a, b, b_nk, acc.name, seed, epi, out, adt)
+
+
+def _c(name: str) -> str:
+    return re.sub(r"[^A-Za-z0-9_]", "_", name)
+
+
+def _tc_ok(plan: GemmPlan, dtypes) -> tuple[bool, list[str]]:
+    why = []
+    if plan.ab_dtype not in ("bf16", "f16"):
+        why.append(f"{plan.ab_dtype} operands run on CUDA cores (tcgen05 kind::f16 needs bf16/f16)")
+    if plan.K % 8:
+        why.append(f"K={plan.K} is not a multiple of 8 (16-byte TMA row stride)")
+    if not plan.b_nk and plan.N % 8:
+        why.append(f"N={plan.N} is not a multiple of 8 (16-byte TMA row stride of B)")
+    if plan.out is None:
+        why.append("epilogue does not write exactly one C[i, j]")
+    else:
+        odt = ir.canon_dtype(plan.out.value_dtype or dtypes.get(plan.out.output))
+        if odt not in ("bf16", "f16", "f32"):
+            why.append(f"output type {odt}")
+    if plan.seed != 0.0:
+        why.append("non-zero accumulator seed")
+    return (not why), why
+
+
+def generate(kop: ir.KernelOp, plan: GemmPlan, shapes: dict, dtypes: dict, args: list[str],
+             scalars: dict[str, str], written: set[str]) -> KernelSource:
+    params: list[ParamSpec] = []
+    ptrs: dict[str, str] = {}
+    sig: list[str] = []
+    for name in args:
+        if name in scalars:
+            sig.append(f"{ctype(scalars[name])} p_{_c(name)}")
+            params.append(ParamSpec(name, "scalar", scalars[name]))
+            continue
+        dt = ir.canon_dtype(dtypes.get(name))
+        const = "" if name in written else "const "
+        sig.append(f"{const}{ctype(dt)}* __restrict__ p_{_c(name)}")
+        ptrs[name] = f"p_{_c(name)}"
+        params.append(ParamSpec(name, "ptr", dt))
+    scalar_env = {n: (("f32", f"p_{_c(n)}") if scalars[n] == "f32" else ("int", f"(long long)p_{_c(n)}"))
+                  for n in scalars}
+    ok, why = _tc_ok(plan, dtypes)
+    if ok:
+        return _gen_tcgen05(kop, plan, shapes, dtypes, args, ptrs, sig, params, scalar_env)
+    return _gen_simt(kop, plan, shapes, dtypes, args, ptrs, sig, params, scalar_env, why)
+
+
+# ---------------------------------------------------------------------------- epilogue
+
+
+def _epilogue_code(plan: GemmPlan, shapes, dtypes, ptrs, scalar_env, acc_code: str, i_code: str,
+                   j_code: str, ind: str, out_var: str | None) -> list[str]:
+    """The IR's post-loop statements for one output, with the accumulator
+    bound to ``acc_code``.  With ``out_var`` the C write is captured into that
+    variable (converted to C's element type) instead of stored."""
+
+    def write_hook(s, k, kind, code):
+        dt = ir.canon_dtype(s.value_dtype or dtypes.get(s.output))
+        if out_var is not None and s is plan.out:
+            return f"{out_var} = {store_from(kind, code, dt)};"
+        return em._default_write(s, k, kind, code)
+
+    em = Emitter(shapes, dtypes, ptrs, write_hook=write_hook, indent=ind)
+    em.env.update(scalar_env)
+    em.bind_const(plan.i, "int", i_code)
+    em.bind_const(plan.j, "int", j_code)
+    em.assign(plan.acc, "f32", acc_code)
+    em.run(plan.epilogue)
+    return em.lines
+
+
+# ---------------------------------------------------------------------------- tcgen05
+
+
+def _gen_tcgen05(kop, plan: GemmPlan, shapes, dtypes, args, ptrs, sig, params, scalar_env) -> KernelSource:
+    M, N, K = plan.M, plan.N, plan.K
+    mb, nb, kb = -(-M // BM), -(-N // BN), -(-K // BK)
+    tiles = mb * nb
+    odt = ir.canon_dtype(plan.out.value_dtype or dtypes.get(plan.out.output))
+    ocls = ctype(odt)
+    fmt = 1 if plan.ab_dtype == "bf16" else 0
+    a_idx = args.index(plan.a.input)
+    b_idx = args.index(plan.b.input)
+    esz = 2
+    tm_a = TmapSpec(a_idx, TMAP_DTYPE[plan.ab_dtype], [K, M], [K * esz], [BK, BM], SWIZZLE_128B, L2_256B)
+    if plan.b_nk:
+        tm_b = TmapSpec(b_idx, TMAP_DTYPE[plan.ab_dtype], [K, N], [K * esz], [BK, BN], SWIZZLE_128B, L2_256B)
+    else:
+        tm_b = TmapSpec(b_idx, TMAP_DTYPE[plan.ab_dtype], [N, K], [N * esz], [64, BK], SWIZZLE_128B, L2_256B)
+    a_stage = BM * BK * esz
+    b_stage = BN * BK * esz
+    smem = 1024 + STAGES * (a_stage + b_stage) + 256
+    sig = list(sig) + ["const __grid_constant__ CUtensorMap tm_a", "const __grid_constant__ CUtensorMap tm_b"]
+    out_ptr = ptrs[plan.out.output]
+    vec_store = (N % 8 == 0) if odt in ("bf16", "f16") else (N % 4 == 0)
+    epi_full = _epilogue_code(plan, shapes, dtypes, ptrs, scalar_env, "__uint_as_float(r[jj])", "row",
+                              "(col0 + jj)", " " * 24, "ov[jj]")
+    epi_any = _epilogue_code(plan, shapes, dtypes, ptrs, scalar_env, "__uint_as_float(r[jj])", "row",
+                             "(col0 + jj)", " " * 28, "ov1")
+    if odt in ("bf16", "f16"):
+        pack = ("                    uint4 *dst = reinterpret_cast<uint4 *>(" + out_ptr + " + row * (long long)N + col0);\n"
+                "                    #pragma unroll\n"
+                "                    for (int v = 0; v < 4; ++v) {\n"
+                "                        uint4 w;\n"
+                "                        memcpy(&w, &ov[v * 8], 16);\n"
+                "                        dst[v] = w;\n"
+                "                    }\n")
+    else:
+        pack = ("                    float4 *dst = reinterpret_cast<float4 *>(" + out_ptr + " + row * (long long)N + col0);\n"
+                "                    #pragma unroll\n"
+                "                    for (int v = 0; v < 8; ++v) dst[v] = make_float4(ov[4*v], ov[4*v+1], ov[4*v+2], ov[4*v+3]);\n")
+    src = f"""{DEVICE_PRELUDE}
+#include <string.h>
+#include "emmy_sm100.cuh"
+
+namespace {{
+constexpr long long M = {M}LL, N = {N}LL, K = {K}LL;
+constexpr int BM = {BM}, BN = {BN}, BK = {BK}, STAGES = {STAGES};
+constexpr int MB = {mb}, NB = {nb}, KB = {kb}, TILES = {tiles}, GROUP_M = {GROUP_M};
+constexpr uint32_t A_STAGE = {a_stage}u, B_STAGE = {b_stage}u;
+constexpr uint32_t SMEM_BYTES = {smem}u;
+constexpr uint32_t IDESC = emmy::idesc_f16({fmt}u, {0 if plan.b_nk else 1}u, BM, BN);
+constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s per wait: orders of magnitude above any legal wait
+
+__device__ __forceinline__ void tile_coords(int t, int &mb, int &nb) {{
+    const int per_group = GROUP_M * NB;
+    const int g = t / per_group;
+    const int r = t - g * per_group;
+    const int first = g * GROUP_M;
+    const int rows = (MB - first) < GROUP_M ? (MB - first) : GROUP_M;
+    mb = first + r % rows;
+    nb = r / rows;
+}}
+}}  // namespace
+
+extern "C" __global__ void __launch_bounds__({TC_THREADS}, 1) {kop.name}({", ".join(sig)}) {{
+    uint32_t dyn_smem;
+    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn_smem));
+    if (blockDim.x != {TC_THREADS} || blockDim.y != 1 || blockDim.z != 1 || dyn_smem < SMEM_BYTES) {{
+        if (threadIdx.x == 0 && threadIdx.y == 0 && threadIdx.z == 0) atomicOr(&emmy_status, EMMY_STATUS_BAD_LAUNCH);
+        return;
+    }}
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + STAGES * A_STAGE;
+    uint64_t *full = reinterpret_cast<uint64_t *>(sB + STAGES * B_STAGE);
+    uint64_t *empty = full + STAGES;
+    uint64_t *tfull = empty + STAGES;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *drain = tempty + 2;
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile uint32_t *abort_flag = tmem_holder + 1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {{
+        for (int s = 0; s < STAGES; ++s) {{ emmy::mbar_init(&full[s], 1); emmy::mbar_init(&empty[s], 1); }}
+        for (int a = 0; a < 2; ++a) {{ emmy::mbar_init(&tfull[a], 1); emmy::mbar_init(&tempty[a], 4); }}
+        emmy::mbar_init(drain, 1);
+        *abort_flag = 0u;
+        emmy::fence_barrier_init();
+    }}
+    if (warp == 1) {{
+        emmy::tmem_alloc(tmem_holder, 512);
+        emmy::tmem_relinquish();
+    }}
+    if (warp == 0 && lane == 0) {{
+        emmy::tma_prefetch(&tm_a);
+        emmy::tma_prefetch(&tm_b);
+    }}
+    emmy::tc_fence_before();
+    __syncthreads();
+    emmy::tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    if (warp == 0) {{
+        if (lane == 0) {{
+            // ---------------- TMA producer
+            uint32_t stage = 0, phase = 0;
+            uint32_t issued = 0u, parity_bits = 0u;  // per stage: load in flight, its phase parity
+            bool ok = true;
+            for (int t = blockIdx.x; t < TILES && ok; t += gridDim.x) {{
+                int tm, tn;
+                tile_coords(t, tm, tn);
+                for (int k = 0; k < KB; ++k) {{
+                    if (!emmy::mbar_wait(&empty[stage], phase ^ 1u, abort_flag, EMMY_STATUS_TIMEOUT_PRODUCER, WAIT_NS)) {{ ok = false; break; }}
+                    emmy::mbar_arrive_expect_tx(&full[stage], A_STAGE + B_STAGE);
+                    emmy::tma_load_2d(sA + stage * A_STAGE, &tm_a, &full[stage], k * BK, tm * BM);
+{_b_loads(plan.b_nk)}
+                    issued |= 1u << stage;
+                    parity_bits = (parity_bits & ~(1u << stage)) | (phase << stage);
+                    if (++stage == STAGES) {{ stage = 0; phase ^= 1u; }}
+                }}
+            }}
+            if (!ok) {{
+                // drain this CTA's own loads still in flight before teardown (bounded)
+                volatile uint32_t never = 0u;
+                for (int s = 0; s < STAGES; ++s)
+                    if (issued & (1u << s)) emmy::mbar_wait(&full[s], (parity_bits >> s) & 1u, &never, 0u, 20000000ull);
+            }}
+        }}
+        __syncwarp();
+    }} else if (warp == 1) {{
+        if (lane == 0) {{
+            // ---------------- MMA issuer
+            uint32_t stage = 0, phase = 0, it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < TILES && ok; t += gridDim.x, ++it) {{
+                const uint32_t acc = it & 1u, aphase = (it >> 1) & 1u;
+                if (!emmy::mbar_wait(&tempty[acc], aphase ^ 1u, abort_flag, EMMY_STATUS_TIMEOUT_MMA, WAIT_NS)) break;
+                emmy::tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (int k = 0; k < KB; ++k) {{
+                    if (!emmy::mbar_wait(&full[stage], phase, abort_flag, EMMY_STATUS_TIMEOUT_MMA, WAIT_NS)) {{ ok = false; break; }}
+                    emmy::tc_fence_after();
+                    const uint32_t a_base = emmy::smem_u32(sA + stage * A_STAGE);
+                    const uint32_t b_base = emmy::smem_u32(sB + stage * B_STAGE);
+                    #pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk) {{
+                        const uint64_t ad = emmy::smem_desc_sw128(a_base + kk * 32, 16, 1024);
+{_b_desc(plan.b_nk)}
+                        emmy::umma_f16(d_tmem, ad, bd, IDESC, (k | kk) != 0 ? 1u : 0u);
+                    }}
+                    emmy::umma_commit(&empty[stage]);
+                    if (++stage == STAGES) {{ stage = 0; phase ^= 1u; }}
+                }}
+                if (!ok) break;
+                emmy::umma_commit(&tfull[acc]);
+            }}
+            // every MMA this thread issued has finished before TMEM is released (bounded)
+            emmy::umma_commit(drain);
+            volatile uint32_t never = 0u;
+            emmy::mbar_wait(drain, 0u, &never, 0u, 20000000ull);
+        }}
+        __syncwarp();
+    }} else {{
+        // ---------------- epilogue: TMEM -> registers -> IR epilogue -> C
+        const int q = warp & 3;
+        uint32_t it = 0;
+        for (int t = blockIdx.x; t < TILES; t += gridDim.x, ++it) {{
+            const uint32_t acc = it & 1u, aphase = (it >> 1) & 1u;
+            if (!emmy::mbar_wait(&tfull[acc], aphase, abort_flag, EMMY_STATUS_TIMEOUT_EPILOGUE, WAIT_NS)) break;
+            emmy::tc_fence_after();
+            int tm, tn;
+            tile_coords(t, tm, tn);
+            const long long row = (long long)tm * BM + q * 32 + lane;
+            #pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {{
+                uint32_t r[32];
+                emmy::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + c * 32, r);
+                emmy::tmem_ld_wait();
+                const long long col0 = (long long)tn * BN + c * 32;
+                if (row < M && col0 + 32 <= N && {'true' if vec_store else 'false'}) {{
+                    {ocls} ov[32];
+                    #pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) {{
+{chr(10).join(epi_full)}
+                    }}
+{pack}                }} else if (row < M) {{
+                    #pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) {{
+                        if (col0 + jj < N) {{
+                            {ocls} ov1;
+{chr(10).join(epi_any)}
+                            {out_ptr}[row * N + col0 + jj] = ov1;
+                        }}
+                    }}
+                }}
+            }}
+            emmy::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) emmy::mbar_arrive(&tempty[acc]);
+        }}
+    }}
+    emmy::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {{
+        emmy::tc_fence_after();
+        emmy::tmem_dealloc(tmem_base, 512);
+    }}
+}}
+"""
+    grid = max(1, min(tiles, SM_COUNT))
+    launch = LaunchPlan(grid=(grid, 1, 1), block=(TC_THREADS, 1, 1), smem=smem)
+    src += launch_record_source("gemm", launch, params, [tm_a, tm_b])
+    notes = {"kernel": "tcgen05", "tile": [BM, BN, BK], "stages": STAGES, "tiles": tiles,
+             "b_layout": "NK" if plan.b_nk else "KN", "vector_store": vec_store}
+    return KernelSource(entry=kop.name, source=src, launch=launch, params=params, family="gemm",
+                        notes=notes, tmaps=[tm_a, tm_b])
+
+
+def _b_loads(b_nk: bool) -> str:
+    ind = " " * 20
+    if b_nk:
+        return f"{ind}emmy::tma_load_2d(sB + stage * B_STAGE, &tm_b, &full[stage], k * BK, tn * BN);"
+    return "\n".join(
+        f"{ind}emmy::tma_load_2d(sB + stage * B_STAGE + {j * 8192}u, &tm_b, &full[stage], tn * BN + {64 * j}, k * BK);"
+        for j in range(BN // 64))
+
+
+def _b_desc(b_nk: bool) -> str:
+    ind = " " * 24
+    if b_nk:
+        return f"{ind}const uint64_t bd = emmy::smem_desc_sw128(b_base + kk * 32, 16, 1024);"
+    # MN-major: 64-column blocks 8 KB apart (LBO), 8-row K groups 1 KB apart (SBO); 16 K rows = 2 KB
+    return f"{ind}const uint64_t bd = emmy::smem_desc_sw128(b_base + kk * 2048, 8192, 1024);"
+
+
+# ---------------------------------------------------------------------------- SIMT
+
+
+def _gen_simt(kop, plan: GemmPlan, shapes, dtypes, args, ptrs, sig, params, scalar_env, why) -> KernelSource:
+    M, N, K = plan.M, plan.N, plan.K
+    mb, nb = -(-M // SIMT_BM), -(-N // SIMT_BN)
+    tiles = mb * nb
+    adt = plan.ab_dtype
+    a_ptr, b_ptr = ptrs[plan.a.input], ptrs[plan.b.input]
+    conv = {"f32": "{x}", "bf16": "__bfloat162float({x})", "f16": "__half2float({x})"}[adt]
+    b_elem = (f"{b_ptr}[(long long)gn * K + gk]" if plan.b_nk else f"{b_ptr}[(long long)gk * N + gn]")
+    epi = _epilogue_code(plan, shapes, dtypes, ptrs, scalar_env, "acc[ii][jj]", "gi", "gj", " " * 16, None)
+    seed = f32_lit(plan.seed)
+    src = f"""{DEVICE_PRELUDE}
+#include "emmy_launch_record.h"
+extern "C" __device__ unsigned int emmy_status;
+
+extern "C" __global__ void __launch_bounds__({SIMT_THREADS}) {kop.name}({", ".join(sig)}) {{
+    constexpr long long M = {M}LL, N = {N}LL, K = {K}LL;
+    constexpr int TBM = {SIMT_BM}, TBN = {SIMT_BN}, TBK = {SIMT_BK}, MB = {mb}, NB = {nb};
+    if (blockDim.x != {SIMT_THREADS} || blockDim.y != 1 || blockDim.z != 1) {{
+        if (threadIdx.x == 0 && threadIdx.y == 0 && threadIdx.z == 0) atomicOr(&emmy_status, EMMY_STATUS_BAD_LAUNCH);
+        return;
+    }}
+    __shared__ float sa[TBK][TBM + 1];
+    __shared__ float sb[TBK][TBN + 1];
+    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+    for (int t = blockIdx.x; t < MB * NB; t += gridDim.x) {{
+        const long long m0 = (long long)(t / NB) * TBM, n0 = (long long)(t % NB) * TBN;
+        float acc[4][4];
+        #pragma unroll
+        for (int a = 0; a < 4; ++a)
+            #pragma unroll
+            for (int b = 0; b < 4; ++b) acc[a][b] = {seed};
+        for (long long k0 = 0; k0 < K; k0 += TBK) {{
+            for (int e = threadIdx.x; e < TBK * TBM; e += blockDim.x) {{
+                const int kk = e % TBK, mm = e / TBK;
+                const long long gm = m0 + mm, gk = k0 + kk;
+                sa[kk][mm] = (gm < M && gk < K) ? {conv.format(x=f"{a_ptr}[gm * K + gk]")} : 0.0f;
+            }}
+            for (int e = threadIdx.x; e < TBK * TBN; e += blockDim.x) {{
+                const int kk = e / TBN, nn = e % TBN;
+                const long long gn = n0 + nn, gk = k0 + kk;
+                sb[kk][nn] = (gn < N && gk < K) ? {conv.format(x=b_elem)} : 0.0f;
+            }}
+            __syncthreads();
+            const int kmax = (K - k0) < TBK ? (int)(K - k0) : TBK;
+            for (int kk = 0; kk < kmax; ++kk) {{
+                float av[4], bv[4];
+                #pragma unroll
+                for (int a = 0; a < 4; ++a) av[a] = sa[kk][ty * 4 + a];
+                #pragma unroll
+                for (int b = 0; b < 4; ++b) bv[b] = sb[kk][tx * 4 + b];
+                #pragma unroll
+                for (int a = 0; a < 4; ++a)
+                    #pragma unroll
+                    for (int b = 0; b < 4; ++b) acc[a][b] = __fmaf_rn(av[a], bv[b], acc[a][b]);
+            }}
+            __syncthreads();
+        }}
+        #pragma unroll
+        for (int ii = 0; ii < 4; ++ii) {{
+            #pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {{
+                const long long gi = m0 + ty * 4 + ii, gj = n0 + tx * 4 + jj;
+                if (gi < M && gj < N) {{
+{chr(10).join(epi)}
+                }}
+            }}
+        }}
+    }}
+}}
+"""
+    grid = max(1, min(tiles, SM_COUNT * 8))
+    launch = LaunchPlan(grid=(grid, 1, 1), block=(SIMT_THREADS, 1, 1), smem=0)
+    src += launch_record_source("gemm", launch, params)
+    notes = {"kernel": "simt", "tile": [SIMT_BM, SIMT_BN, SIMT_BK], "tiles": tiles, "why_not_tcgen05": why}
+    return KernelSource(entry=kop.name, source=src, launch=launch, params=params, family="gemm", notes=notes)

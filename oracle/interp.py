@@ -799,3 +799,19 @@ def ulp_distance(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     d = np.abs(ia - ib)
     both_nan = np.isnan(a) & np.isnan(b)
     return np.where(both_nan, 0, d)
+
+
+def within(got, ref, crit: dict) -> tuple[bool, str]:
+    """Compare against an oracle criterion: {"ulp": n} (max f32 ulp distance)
+    or {"rtol": r, "atol": a} (|got - ref| <= a + r |ref|, NaN == NaN)."""
+    got = np.asarray(got, F32).reshape(-1)
+    ref = np.asarray(ref, F32).reshape(-1)
+    if "ulp" in crit:
+        d = int(ulp_distance(got, ref).max()) if got.size else 0
+        return d <= crit["ulp"], f"max {d} ulp (bound {crit['ulp']})"
+    with np.errstate(invalid="ignore"):
+        err = np.abs(got.astype(np.float64) - ref.astype(np.float64))
+        bound = crit.get("atol", 0.0) + crit.get("rtol", 0.0) * np.abs(ref.astype(np.float64))
+        bad = ~((err <= bound) | (np.isnan(got) & np.isnan(ref)))
+    worst = float(np.nanmax(err - bound)) if got.size else 0.0
+    return (not bad.any()), f"{int(bad.sum())} of {got.size} outside, worst excess {worst:.3g}"

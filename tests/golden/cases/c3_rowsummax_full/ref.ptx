@@ -34,6 +34,8 @@
         shr.u32         %r9, %r3, 5;
         shr.u32         %r10, %r6, 7;
         and.b32         %r11, %r6, 127;
+        mov.f32         %f1, 0f00000000;
+        mov.f32         %f2, 0fF149F2CA;
         mov.s32         %r12, %r11;
         .pragma "nounroll";
 SLOOP_1:
@@ -42,62 +44,60 @@ SLOOP_1:
         shl.b32         %r13, %r10, 16;
         add.s32         %r14, %r13, %r12;
         mad.wide.s32    %rd4, %r14, 4, %rd1;
-        ld.global.nc.f32   %f1, [%rd4];
-        mov.f32         %f2, 0f00000000;
-        add.f32         %f2, %f2, %f1;
-        mov.f32         %f3, 0fF149F2CA;
-        max.f32         %f3, %f3, %f1;
+        ld.global.nc.f32   %f3, [%rd4];
+        add.f32         %f1, %f1, %f3;
+        max.f32         %f2, %f2, %f3;
         add.s32         %r12, %r12, 128;
         bra             SLOOP_1;
 SLEND_2:
         activemask.b32  %r15;
-        mov.b32         %r16, %f2;
+        mov.b32         %r16, %f1;
         shfl.sync.bfly.b32 %r16, %r16, 16, 31, %r15;
         mov.b32         %f4, %r16;
-        mov.b32         %r17, %f3;
+        mov.b32         %r17, %f2;
         shfl.sync.bfly.b32 %r17, %r17, 16, 31, %r15;
         mov.b32         %f5, %r17;
-        add.f32         %f2, %f2, %f4;
-        max.f32         %f3, %f3, %f5;
-        mov.b32         %r18, %f2;
+        add.f32         %f1, %f1, %f4;
+        max.f32         %f2, %f2, %f5;
+        mov.b32         %r18, %f1;
         shfl.sync.bfly.b32 %r18, %r18, 8, 31, %r15;
         mov.b32         %f6, %r18;
-        mov.b32         %r19, %f3;
+        mov.b32         %r19, %f2;
         shfl.sync.bfly.b32 %r19, %r19, 8, 31, %r15;
         mov.b32         %f7, %r19;
-        add.f32         %f2, %f2, %f6;
-        max.f32         %f3, %f3, %f7;
-        mov.b32         %r20, %f2;
+        add.f32         %f1, %f1, %f6;
+        max.f32         %f2, %f2, %f7;
+        mov.b32         %r20, %f1;
         shfl.sync.bfly.b32 %r20, %r20, 4, 31, %r15;
         mov.b32         %f8, %r20;
-        mov.b32         %r21, %f3;
+        mov.b32         %r21, %f2;
         shfl.sync.bfly.b32 %r21, %r21, 4, 31, %r15;
         mov.b32         %f9, %r21;
-        add.f32         %f2, %f2, %f8;
-        max.f32         %f3, %f3, %f9;
-        mov.b32         %r22, %f2;
+        add.f32         %f1, %f1, %f8;
+        max.f32         %f2, %f2, %f9;
+        mov.b32         %r22, %f1;
         shfl.sync.bfly.b32 %r22, %r22, 2, 31, %r15;
         mov.b32         %f10, %r22;
-        mov.b32         %r23, %f3;
+        mov.b32         %r23, %f2;
         shfl.sync.bfly.b32 %r23, %r23, 2, 31, %r15;
         mov.b32         %f11, %r23;
-        add.f32         %f2, %f2, %f10;
-        max.f32         %f3, %f3, %f11;
-        mov.b32         %r24, %f2;
+        add.f32         %f1, %f1, %f10;
+        max.f32         %f2, %f2, %f11;
+        mov.b32         %r24, %f1;
         shfl.sync.bfly.b32 %r24, %r24, 1, 31, %r15;
         mov.b32         %f12, %r24;
-        mov.b32         %r25, %f3;
+        mov.b32         %r25, %f2;
         shfl.sync.bfly.b32 %r25, %r25, 1, 31, %r15;
         mov.b32         %f13, %r25;
-        add.f32         %f2, %f2, %f12;
-        max.f32         %f3, %f3, %f13;
+        add.f32         %f1, %f1, %f12;
+        max.f32         %f2, %f2, %f13;
         setp.eq.s32    %p2, %r8, 0;
         not.pred        %p3, %p2;
         @%p3 bra      CEND_3;
         mad.lo.s32      %r26, %r9, 4, %r1;
-        st.shared.f32   [%r26], %f2;
+        st.shared.f32   [%r26], %f1;
         mad.lo.s32      %r27, %r9, 4, %r2;
-        st.shared.f32   [%r27], %f3;
+        st.shared.f32   [%r27], %f2;
 CEND_3:
         bar.sync        0;
         setp.lt.s32     %p4, %r9, 2;

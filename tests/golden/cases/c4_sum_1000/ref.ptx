@@ -27,44 +27,44 @@
         mov.u32         %r6, %nctaid.x;
         and.b32         %r7, %r2, 31;
         shr.u32         %r8, %r2, 5;
+        mov.f32         %f1, 0f00000000;
         mov.s32         %r9, %r5;
         .pragma "nounroll";
 SLOOP_1:
         setp.ge.s32     %p1, %r9, 1000;
         @%p1 bra        SLEND_2;
         mad.wide.s32    %rd3, %r9, 4, %rd1;
-        ld.global.nc.f32   %f1, [%rd3];
-        mov.f32         %f2, 0f00000000;
-        add.f32         %f2, %f2, %f1;
+        ld.global.nc.f32   %f2, [%rd3];
+        add.f32         %f1, %f1, %f2;
         add.s32         %r9, %r9, 128;
         bra             SLOOP_1;
 SLEND_2:
         activemask.b32  %r10;
-        mov.b32         %r11, %f2;
+        mov.b32         %r11, %f1;
         shfl.sync.bfly.b32 %r11, %r11, 16, 31, %r10;
         mov.b32         %f3, %r11;
-        add.f32         %f2, %f2, %f3;
-        mov.b32         %r12, %f2;
+        add.f32         %f1, %f1, %f3;
+        mov.b32         %r12, %f1;
         shfl.sync.bfly.b32 %r12, %r12, 8, 31, %r10;
         mov.b32         %f4, %r12;
-        add.f32         %f2, %f2, %f4;
-        mov.b32         %r13, %f2;
+        add.f32         %f1, %f1, %f4;
+        mov.b32         %r13, %f1;
         shfl.sync.bfly.b32 %r13, %r13, 4, 31, %r10;
         mov.b32         %f5, %r13;
-        add.f32         %f2, %f2, %f5;
-        mov.b32         %r14, %f2;
+        add.f32         %f1, %f1, %f5;
+        mov.b32         %r14, %f1;
         shfl.sync.bfly.b32 %r14, %r14, 2, 31, %r10;
         mov.b32         %f6, %r14;
-        add.f32         %f2, %f2, %f6;
-        mov.b32         %r15, %f2;
+        add.f32         %f1, %f1, %f6;
+        mov.b32         %r15, %f1;
         shfl.sync.bfly.b32 %r15, %r15, 1, 31, %r10;
         mov.b32         %f7, %r15;
-        add.f32         %f2, %f2, %f7;
+        add.f32         %f1, %f1, %f7;
         setp.eq.s32    %p2, %r7, 0;
         not.pred        %p3, %p2;
         @%p3 bra      CEND_3;
         mad.lo.s32      %r16, %r8, 4, %r1;
-        st.shared.f32   [%r16], %f2;
+        st.shared.f32   [%r16], %f1;
 CEND_3:
         bar.sync        0;
         setp.lt.s32     %p4, %r8, 2;

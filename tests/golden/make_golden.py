@@ -154,6 +154,12 @@ def _meta_kernel(node: str, entry: str, arg_order: list[str], grid, block, args:
             "smem_bytes": 0, "zero_outputs": zero_outputs or [], "args": args, "final": True}
 
 
+# The reference builds exp/tanh/sigmoid/silu/log/rsqrt/pow from ex2/lg2/rsqrt.approx,
+# whose exact bits are not published; the oracle uses correctly rounded libm
+# instead, so for those IRs oracle == reference only up to the approximation
+# error (amplified by cancellation, e.g. 1 + tanh(w) for w << 0).
+APPROX_OPS = ("exp", "exp2", "tanh", "sigmoid", "silu", "log", "log2", "rsqrt", "pow")
+APPROX_ORACLE = {"rtol": 4e-6, "atol": 2e-6}
 UNIF = lambda lo, hi: {"kind": "uniform", "low": lo, "high": hi}  # noqa: E731
 NORM = lambda std=1.0: {"kind": "normal", "mean": 0.0, "std": std}  # noqa: E731
 
@@ -224,7 +230,7 @@ def gelu_case(cid: str, rows: int, cols: int, *, config: str | None = None) -> C
         _arg("t", [cols], init=UNIF(-0.1, 0.1), seed=2),
         _arg("y", [rows, cols], output=True)])
     return Case(cid, entry, graph, kern, family="pointwise", config=config,
-                check={"kind": "ulp", "ulp": 1, "oracle_ulp": 8})
+                check={"kind": "ulp", "ulp": 1, "oracle": APPROX_ORACLE})
 
 
 # ------------------------------------------------------------------ config 3 / 4
@@ -243,7 +249,10 @@ def _reduce_body(red_axis: Axis, start: str, index, accs: list[tuple[str, str]],
     final = tuple(Write(output=o, index=idx, values=(a,), value_dtype=F32)
                   for (a, _), (o, idx) in zip(accs, outs))
     return (
-        StridedLoop(axis=red_axis, start=Var(start), step=Literal(BT, "int"), body=loads + accums),
+        # seed=True: accumulators start at their identity before the loop (compile.py:1868,
+        # seed_accums 1769-1783); without it the reference seeds inside the loop body.
+        StridedLoop(axis=red_axis, start=Var(start), step=Literal(BT, "int"), body=loads + accums,
+                    seed=True),
         WarpShuffle(state=tuple(a for a, _ in accs), state_b=tuple(f"{a}__o" for a, _ in accs),
                     combine_states=combine, length=32, dtype=F32),
         *smems,
@@ -441,8 +450,10 @@ def unary_case(cid: str, op: str, n: int, *, prep_abs: float | None = None, extr
     grid, block = _launch(n)
     kern = _meta_kernel("out", entry, ["x", "out"], grid, block, [
         _arg("x", [n], init=NORM(), seed=0), _arg("out", [n], output=True)])
+    approx = op in APPROX_OPS
     return Case(cid, entry, graph, kern, family="pointwise",
-                check={"kind": "ulp", "ulp": 0, "oracle_ulp": 8}, tags=("catalog",))
+                check={"kind": "ulp", "ulp": 0, "oracle": APPROX_ORACLE if approx else {"ulp": 0}},
+                tags=("catalog",))
 
 
 def binary_case(cid: str, op: str, n: int) -> Case:
@@ -525,7 +536,7 @@ def chain_case(cid: str, n: int, which: str) -> Case:
     kern = _meta_kernel("out", entry, ins + ["out"], grid, block, args)
     approx = which in ("silu_sigmoid", "exp_log_sqrt")
     return Case(cid, entry, graph, kern, family="pointwise",
-                check={"kind": "ulp", "ulp": 0, "oracle_ulp": 16 if approx else 0},
+                check={"kind": "ulp", "ulp": 0, "oracle": APPROX_ORACLE if approx else {"ulp": 0}},
                 tags=("catalog",))
 
 
