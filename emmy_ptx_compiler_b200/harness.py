@@ -125,3 +125,61 @@ class ForeignModule:
         stream = torch.cuda.current_stream(self.device).cuda_stream
         g, b = self.spec.kernel["grid"], self.spec.kernel["block"]
         self.module.launch([bufs[n] for n in self.spec.arg_order], stream=stream, grid=g, block=b)
+
+
+def _seeded_device_inputs(spec: CaseSpec, device: int, seed: int = 0) -> dict:
+    """Device tensors with the fixture's shapes and input distributions."""
+    torch = _torch()
+    g = torch.Generator(device=f"cuda:{device}")
+    g.manual_seed(seed)
+    bufs = {}
+    for name in spec.arg_order:
+        a = spec.args[name]
+        shape = tuple(a.get("shape") or ()) or (1,)
+        tdt = getattr(torch, TORCH_DTYPES.get(a.get("dtype", "f32"), "float32"))
+        if a.get("output"):
+            bufs[name] = torch.zeros(shape, dtype=tdt, device=f"cuda:{device}")
+            continue
+        init = a.get("init") or {"kind": "normal", "mean": 0.0, "std": 1.0}
+        t = torch.empty(shape, dtype=torch.float32, device=f"cuda:{device}")
+        if "data" in a:
+            t.copy_(torch.tensor(a["data"], dtype=torch.float32).reshape(shape))
+        elif init["kind"] == "uniform":
+            t.uniform_(init["low"], init["high"], generator=g)
+        else:
+            t.normal_(init.get("mean", 0.0), init.get("std", 1.0), generator=g)
+        bufs[name] = t.to(tdt)
+    return bufs
+
+
+def main(argv=None) -> int:
+    """``python -m emmy_ptx_compiler_b200.harness CASE_DIR [--iters N]``: compile
+    a fixture, launch it N times on seeded device inputs, print the mean
+    device time per launch (used for profiler captures of one kernel)."""
+    import argparse
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case_dir")
+    ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--device", type=int, default=0)
+    ns = ap.parse_args(argv)
+    torch = _torch()
+    case = DeviceCase(ns.case_dir, ns.device)
+    bufs = _seeded_device_inputs(case.spec, ns.device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    case.launch(bufs)
+    torch.cuda.synchronize(ns.device)
+    e0.record()
+    for _ in range(ns.iters):
+        case.launch(bufs)
+    e1.record()
+    torch.cuda.synchronize(ns.device)
+    st = case.module.status()
+    print(json.dumps({"case": case.spec.meta.get("id"), "family": case.module.family,
+                      "ms_per_launch": e0.elapsed_time(e1) / ns.iters, "status": st,
+                      "launch": case.bundle["launch"]}))
+    case.module.close()
+    return 1 if st else 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

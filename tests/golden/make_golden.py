@@ -629,6 +629,7 @@ def all_cases() -> list[Case]:
     cases.append(add_case("c1_add_1000", 1000))
     # config 2
     cases.append(gelu_case("c2_gelu_full", 16384, 16384, config="c2"))
+    cases.append(gelu_case("c2_gelu_prof_4096x16384", 4096, 16384))  # > L2, for profiler captures
     cases.append(gelu_case("c2_gelu_256x4096", 256, 4096))
     cases.append(gelu_case("c2_gelu_64x1000", 64, 1000))
     cases.append(gelu_case("c2_gelu_3x7", 3, 7))
