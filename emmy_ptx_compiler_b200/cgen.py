@@ -15,6 +15,11 @@ PTX computes for the same statement:
   ``add`` Assign that consumes it (compile.py:1285-1303), each only when the
   product is not read again later in the same statement list
   (compile.py:1415-1428);
+* the contraction the reference's PTX gets from ptxas at load time: the
+  reference emits plain ``mul.f32``/``add.f32``/``sub.f32`` (no rounding
+  modifier, so the assembler may fuse them); a plain product whose only use
+  is a plain add/sub (or an Accum add) is computed as one FMA here too
+  (observed on B200 against the reference PTX, see :meth:`Emitter.plain_product`);
 * f32 literal rounding (``f32_hex``, compile.py:205-207), accumulator seeds
   (``identity_of``, compile.py:327-338), ordered float compares
   (``setp.<cmp>.f32``) and truncating float->int casts (``cvt.rzi``);
@@ -178,6 +183,28 @@ def uses_name(stmt, name: str) -> bool:
     return False
 
 
+def _operand_reads(s) -> list[str]:
+    """IR names a statement reads as instruction operands (one entry per read)."""
+    out: list[str] = []
+    if isinstance(s, ir.Assign):
+        out += [a for a in s.args if isinstance(a, str)]
+    elif isinstance(s, ir.Accum):
+        out += [x for x in (s.value, s.base) if isinstance(x, str)]
+    elif isinstance(s, ir.Write):
+        out += [v for v in s.values if isinstance(v, str)]
+        for ix in s.index:
+            out += sorted(ix.var_names()) if isinstance(ix, ir.Expr) else []
+    elif isinstance(s, ir.Select):
+        for br in s.branches:
+            if isinstance(br.value, str):
+                out.append(br.value)
+            if isinstance(br.select, ir.Expr):
+                out += sorted(br.select.var_names())
+    elif isinstance(s, (ir.Load, ir.Let, ir.Cond)):
+        out += sorted(s.reads())
+    return out
+
+
 # ------------------------------------------------------------------ the emitter
 
 
@@ -203,6 +230,9 @@ class Emitter:
         self.write_hook = write_hook or self._default_write
         self.tmp = 0
         self.declared: dict[str, str] = {}
+        # plain products (name -> (a, b) factor codes) and per-name read counts
+        self.products: dict[str, tuple[str, str]] = {}
+        self.uses: dict[str, int] = {}
 
     # -------------------------------------------------------------- small utils
     def emit(self, line: str) -> None:
@@ -226,6 +256,7 @@ class Emitter:
         return self.declared[key]
 
     def assign(self, name: str, kind: str, code: str) -> str:
+        self.products.pop(name, None)
         var = self.declare(name, kind)
         self.emit(f"{var} = {code};")
         self.env[name] = (kind, var)
@@ -450,8 +481,16 @@ class Emitter:
         raise UnsupportedIR(f"unsupported assign op {op!r}")
 
     # -------------------------------------------------------------- statements
+    def count_uses(self, body) -> None:
+        for t in ir.walk(body):
+            if isinstance(t, ir.Stmt):
+                for n in _operand_reads(t):
+                    self.uses[n] = self.uses.get(n, 0) + 1
+
     def run(self, body) -> None:
         """Statement list with the reference's FMA lookahead (compile.py:1096-1131)."""
+        if not self.uses:
+            self.count_uses(body)
         sl = list(ir.body_stmts(body))
         i = 0
         while i < len(sl):
@@ -532,7 +571,12 @@ class Emitter:
                 self.assign(s.name, "f32", f32_lit(identity_of(s.op)))
             acc = self.as_f32(s.name)
             left = self.as_f32(s.base) if s.base else acc
-            self.assign(s.name, "f32", combine_code(ir.op_name(s.op), left, self.as_f32(s.value)))
+            op = ir.op_name(s.op)
+            prod = self.plain_product(s.value) if op in ("add", "sum") or op not in F32_BINARY else None
+            if prod is not None:
+                self.assign(s.name, "f32", f"__fmaf_rn({prod[0]}, {prod[1]}, {left})")
+            else:
+                self.assign(s.name, "f32", combine_code(op, left, self.as_f32(s.value)))
         elif isinstance(s, ir.Cond):
             p = self.pred_of(s.cond)
             # declare every name assigned inside either branch before the branch
@@ -575,6 +619,8 @@ class Emitter:
                     self.ind + "    ")
         c.declared = self.declared
         c.tmp = self.tmp + 1000
+        c.uses = self.uses
+        c.products = self.products
         return c
 
     @staticmethod
@@ -622,7 +668,46 @@ class Emitter:
             p = self.as_pred(args[0])
             self.assign(s.name, "f32", f"({p} ? {self.as_f32(args[1])} : {self.as_f32(args[2])})")
             return
-        self.assign(s.name, "f32", self.f32_op(op, [self.as_f32(a) for a in args]))
+        if op in ("add", "sum", "subtract", "sub") and len(args) == 2:
+            pa, pb = self.plain_product(args[0]), self.plain_product(args[1])
+            a, b = self.as_f32(args[0]), self.as_f32(args[1])
+            sub = op in ("subtract", "sub")
+            if pa is not None:
+                self.assign(s.name, "f32", f"__fmaf_rn({pa[0]}, {pa[1]}, {'-(' + b + ')' if sub else b})")
+                return
+            if pb is not None:
+                first = f"-({pb[0]})" if sub else pb[0]
+                self.assign(s.name, "f32", f"__fmaf_rn({first}, {pb[1]}, {a})")
+                return
+        fargs = [self.as_f32(a) for a in args]
+        factors = None
+        if op in ("multiply", "mul") and len(fargs) == 2:
+            factors = (fargs[0], fargs[1])
+        elif op == "square" and fargs:
+            factors = (fargs[0], fargs[0])
+        elif op in ("log", "log_fast") and fargs:
+            lg = self.fresh("lg2")
+            self.emit(f"const float {lg} = emmy_lg2_approx({fargs[0]});")
+            factors = (lg, LN2_F32)
+        elif op == "silu" and fargs:
+            sg = self.fresh("sig")
+            self.emit(f"const float {sg} = emmy_sigmoid_ref({fargs[0]});")
+            factors = (fargs[0], sg)
+        if factors is not None:
+            self.assign(s.name, "f32", f"__fmul_rn({factors[0]}, {factors[1]})")
+            self.products[s.name] = factors
+            return
+        self.assign(s.name, "f32", self.f32_op(op, fargs))
+
+    def plain_product(self, name):
+        """Factors of ``name`` if the reference computes it with a plain
+        ``mul.f32`` whose only use is the instruction being emitted now - the
+        pattern the assembler fuses into an FMA."""
+        if not isinstance(name, str) or name not in self.products or self.uses.get(name, 0) != 1:
+            return None
+        if self.env.get(name, ("", ""))[1] != self.declared.get(f"{name}|f32"):
+            return None
+        return self.products[name]
 
 
 DEVICE_PRELUDE = r"""

@@ -62,7 +62,7 @@ def lib():
             getattr(L, n).argtypes = [vp, vp, C.c_size_t]
         L.ora_gemm_seqfma_f32.argtypes = [vp, vp, vp, i64, i64, i64, i32]
         L.ora_strided_reduce_f32.argtypes = [vp, vp, i64, i64, i32, i32, f32, vp]
-        L.ora_loop_reduce_f32.argtypes = [vp, i64, i64, i32, f32, i32, vp]
+        L.ora_loop_reduce_f32.argtypes = [vp, vp, i64, i64, i32, f32, vp]
         L.ora_row_sum_f64.argtypes = [vp, i64, i64, vp]
         del fp
         _LIB = L
@@ -269,6 +269,9 @@ class Cells:
         self.dtypes = dtypes
         self.env: dict[str, tuple[str, np.ndarray]] = {}
         self.mask: np.ndarray | None = None
+        # plain mul.f32 results the assembler may fuse into a following add/sub
+        self.products: dict[str, tuple] = {}
+        self.uses: dict[str, int] = {}
 
     # values -----------------------------------------------------------------
     def f32(self, name):
@@ -287,6 +290,7 @@ class Cells:
         return ordered_cmp("!=", self.f32(name), F32(0))
 
     def bind(self, name: str, kind: str, val) -> None:
+        self.products.pop(name, None)
         val = np.asarray(val)
         if self.mask is not None and name in self.env:
             ok, old = self.env[name]
@@ -416,7 +420,38 @@ class Cells:
         return tuple(indices[:-1]) + (BinaryExpr("+", indices[-1], Literal(k, "int")),)
 
     # statements -------------------------------------------------------------
+    def count_uses(self, body) -> None:
+        def walk(b):
+            for t in b:
+                yield t
+                for child in t.nested():
+                    yield from walk(child)
+        for t in walk(body):
+            names: list = []
+            if isinstance(t, Assign):
+                names = [a for a in t.args if isinstance(a, str)]
+            elif isinstance(t, Accum):
+                names = [x for x in (t.value, t.base) if isinstance(x, str)]
+            elif isinstance(t, Write):
+                names = [v for v in t.values if isinstance(v, str)] + sorted(
+                    set().union(*[ix.vars() for ix in t.index]) if t.index else set())
+            elif isinstance(t, Select):
+                names = sorted(t.deps())
+            elif isinstance(t, (Load, Let, Cond)):
+                names = sorted(t.deps())
+            for n in names:
+                self.uses[n] = self.uses.get(n, 0) + 1
+
+    def product(self, name):
+        """Factors of a plain product whose only use is the current instruction:
+        the reference's mul.f32 + add/sub.f32 pair, which ptxas contracts."""
+        if isinstance(name, str) and name in self.products and self.uses.get(name, 0) == 1:
+            return self.products[name]
+        return None
+
     def run(self, body) -> None:
+        if not self.uses:
+            self.count_uses(body)
         sl = list(body)
         i = 0
         while i < len(sl):
@@ -514,14 +549,41 @@ class Cells:
             elif op == "where" and len(s.args) == 3:
                 self.bind(s.name, "f32", np.where(self.pred(s.args[0]), self.f32(s.args[1]),
                                                   self.f32(s.args[2])).astype(F32))
+            elif op in ("add", "sum", "subtract", "sub") and len(s.args) == 2 and (
+                    self.product(s.args[0]) is not None or self.product(s.args[1]) is not None):
+                sub = op in ("subtract", "sub")
+                pa, pb = self.product(s.args[0]), self.product(s.args[1])
+                if pa is not None:
+                    c = self.f32(s.args[1])
+                    v = c_fma(pa[0], pa[1], np.negative(c) if sub else c)
+                else:
+                    v = c_fma(np.negative(pb[0]) if sub else pb[0], pb[1], self.f32(s.args[0]))
+                self.bind(s.name, "f32", np.broadcast_to(v, (self.n,)))
             else:
-                self.bind(s.name, "f32", np.broadcast_to(f32_op(op, [self.f32(a) for a in s.args]),
-                                                         (self.n,)))
+                fargs = [self.f32(a) for a in s.args]
+                v = np.broadcast_to(f32_op(op, fargs), (self.n,))
+                factors = None
+                if op in ("multiply", "mul") and len(fargs) == 2:
+                    factors = (fargs[0], fargs[1])
+                elif op == "square":
+                    factors = (fargs[0], fargs[0])
+                elif op in ("log", "log_fast"):
+                    factors = (lg2(fargs[0]), LN2)
+                elif op == "silu":
+                    e = ex2(np.multiply(np.negative(fargs[0]), LOG2E, dtype=F32))
+                    factors = (fargs[0], np.divide(F32(1), np.add(F32(1), e, dtype=F32), dtype=F32))
+                self.bind(s.name, "f32", v)
+                if factors is not None:
+                    self.products[s.name] = factors
         elif isinstance(s, Accum):
             if s.name not in self.env:
                 self.bind(s.name, "f32", np.full(self.n, F32(identity_of(s.op))))
             left = self.f32(s.base) if s.base else self.f32(s.name)
-            self.bind(s.name, "f32", combine(opname(s.op), left, self.f32(s.value)))
+            pv = self.product(s.value) if opname(s.op) in ("add", "sum") else None
+            if pv is not None:
+                self.bind(s.name, "f32", c_fma(pv[0], pv[1], left))
+            else:
+                self.bind(s.name, "f32", combine(opname(s.op), left, self.f32(s.value)))
         elif isinstance(s, Cond):
             p = np.broadcast_to(self._top(*self.expr(s.cond)), (self.n,))
             outer = self.mask
@@ -656,27 +718,22 @@ def _eval_loop_reduce(tile, stmts, axes, loop, bufs, shapes, dtypes):
     accs = [s for s in body if isinstance(s, Accum)]
     assert len(accs) == 1, "oracle: one accumulator in Loop reductions"
     acc = accs[0]
-    j = body.index(acc)
-    prev = body[j - 1] if j else None
-    square = False
-    if (isinstance(prev, Assign) and opname(prev.op) == "multiply" and acc.value == prev.name
-            and opname(acc.op) in ("add", "sum") and not any(uses_name(t, prev.name) for t in body[j + 1:])):
-        m.run(body[:j - 1])
-        a, b = m.f32(prev.args[0]), m.f32(prev.args[1])
-        if not np.array_equal(a, b):
-            raise NotImplementedError("oracle: fma Loop reduce of two different operands")
-        vals = np.ascontiguousarray(a, F32)
-        square = True
-    else:
-        m.run(body[:j])
-        vals = np.ascontiguousarray(np.broadcast_to(m.f32(acc.value), (n,)), F32)
+    m.count_uses(body)
+    m.run([t for t in body if t is not acc])
+    pv = m.product(acc.value) if opname(acc.op) in ("add", "sum") else None
     seed = identity_of(acc.op)
     for s in stmts[:stmts.index(loop)]:
         if isinstance(s, Init) and s.name == acc.name:
             seed = float(s.identity)
     out = np.empty(rows, F32)
-    op = {"add": 0, "sum": 0, "maximum": 1, "max": 1, "minimum": 2, "min": 2, "multiply": 3}[opname(acc.op)]
-    lib().ora_loop_reduce_f32(_p(vals), rows, K, op, F32(seed), int(square), _p(out))
+    if pv is not None:
+        xs = np.ascontiguousarray(np.broadcast_to(pv[0], (n,)), F32)
+        ys = np.ascontiguousarray(np.broadcast_to(pv[1], (n,)), F32)
+        lib().ora_loop_reduce_f32(_p(xs), _p(ys), rows, K, 4, F32(seed), _p(out))
+    else:
+        vals = np.ascontiguousarray(np.broadcast_to(m.f32(acc.value), (n,)), F32)
+        op = {"add": 0, "sum": 0, "maximum": 1, "max": 1, "minimum": 2, "min": 2, "multiply": 3}[opname(acc.op)]
+        lib().ora_loop_reduce_f32(_p(vals), None, rows, K, op, F32(seed), _p(out))
     pm = Cells(rows, bufs, shapes, dtypes)
     for k, v in _cells_for(axes, rows).items():
         pm.env[k] = ("int", v)
@@ -697,26 +754,17 @@ def _eval_strided(tile, stmts, axes, loop, bufs, shapes, dtypes):
     m = Cells(n, bufs, shapes, dtypes)
     for k, v in _cells_for(row_axes + [(kname, K)], n).items():
         m.env[k] = ("int", v)
-    # evaluate element values; an Accum directly preceded by its multiply is an fma accumulation
-    done = set()
-    i = 0
+    # element values; an Accum of a single-use product accumulates with fma
+    # (the reference's multiply/Accum contraction, or ptxas fusing its mul/add pair)
+    m.count_uses(body)
+    m.run([t for t in body if not isinstance(t, Accum)])
     pending: list = []
-    while i < len(body):
-        s = body[i]
-        nxt = body[i + 1] if i + 1 < len(body) else None
-        if (isinstance(s, Assign) and isinstance(nxt, Accum) and opname(s.op) == "multiply"
-                and opname(nxt.op) in ("add", "sum") and nxt.value == s.name and len(s.args) == 2
-                and not any(uses_name(t, s.name) for t in body[i + 2:])):
-            pending.append((nxt, m.f32(s.args[0]), m.f32(s.args[1])))
-            done.add(id(nxt))
-            i += 2
-            continue
-        if isinstance(s, Accum):
-            pending.append((s, np.broadcast_to(m.f32(s.value), (n,)), None))
-            i += 1
-            continue
-        m.stmt(s)
-        i += 1
+    for acc in accs:
+        pv = m.product(acc.value) if opname(acc.op) in ("add", "sum") else None
+        if pv is not None:
+            pending.append((acc, pv[0], pv[1]))
+        else:
+            pending.append((acc, np.broadcast_to(m.f32(acc.value), (n,)), None))
     opcode = {"add": 0, "sum": 0, "maximum": 1, "amax": 1, "max": 1, "minimum": 2, "amin": 2, "min": 2,
               "multiply": 3}
     for acc, x, y in pending:

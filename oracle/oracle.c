@@ -58,7 +58,6 @@ void ora_rsqrt_f32(const float *x, float *y, size_t n) {
  * stored [N, K]. */
 void ora_gemm_seqfma_f32(const float *A, const float *B, float *C, int64_t M, int64_t N, int64_t K,
                          int b_nk) {
-#pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < M; ++i) {
         const float *a = A + i * K;
         for (int64_t j = 0; j < N; ++j) {
@@ -96,7 +95,6 @@ static float combine(int op, float a, float b) {
 void ora_strided_reduce_f32(const float *x, const float *y, int64_t rows, int64_t cols, int bt, int op,
                             float ident, float *out) {
     const int nw = bt / 32;
-#pragma omp parallel for schedule(static)
     for (int64_t r = 0; r < rows; ++r) {
         float acc[1024];
         float smem[32];
@@ -124,16 +122,16 @@ void ora_strided_reduce_f32(const float *x, const float *y, int64_t rows, int64_
 }
 
 /* Sequential f32 accumulation of one row per thread (Loop schedule,
- * compile.py:1813-1864 with Accum 2201-2211); square != 0 accumulates
- * fma(v, v, acc) as the multiply/Accum contraction does (1263-1283). */
-void ora_loop_reduce_f32(const float *x, int64_t rows, int64_t cols, int op, float seed, int square,
+ * compile.py:1813-1864 with Accum 2201-2211); op 4 accumulates
+ * fma(x, y, acc), the multiply/Accum contraction (1263-1283). */
+void ora_loop_reduce_f32(const float *x, const float *y, int64_t rows, int64_t cols, int op, float seed,
                          float *out) {
-#pragma omp parallel for schedule(static)
     for (int64_t r = 0; r < rows; ++r) {
         float acc = seed;
         const float *row = x + r * cols;
+        const float *yr = y ? y + r * cols : 0;
         for (int64_t k = 0; k < cols; ++k)
-            acc = square ? fmaf(row[k], row[k], acc) : combine(op, acc, row[k]);
+            acc = (op == 4) ? fmaf(row[k], yr[k], acc) : combine(op, acc, row[k]);
         out[r] = acc;
     }
 }
@@ -141,7 +139,6 @@ void ora_loop_reduce_f32(const float *x, int64_t rows, int64_t cols, int op, flo
 /* f64 row sums: the exact-ish reference the fixtures' expected values use
  * (tools/make_proxy_set.py:256, 335). */
 void ora_row_sum_f64(const float *x, int64_t rows, int64_t cols, double *out) {
-#pragma omp parallel for schedule(static)
     for (int64_t r = 0; r < rows; ++r) {
         double s = 0.0;
         const float *row = x + r * cols;

@@ -351,6 +351,27 @@ def rowsum_loop_case(cid: str, rows: int, cols: int) -> Case:
                                                                      "atol": 1e-5})
 
 
+def rowsum_loop_nonadjacent_case(cid: str, rows: int, cols: int) -> Case:
+    """Loop reduction whose product and Accum are separated by a Let (no
+    explicit fma.rn; the plain mul/add pair is left to the assembler)."""
+    c = rowsum_loop_case(cid, rows, cols)
+    entry = "k_row_sumsq_gap"
+    body = Tile(axes=(Axis("r", Dim(rows)),), body=(
+        Init("acc", 0.0, dtype=F32),
+        Loop(axis=Axis("c", Dim(cols)), body=(
+            Load(names=("v",), input="x", index=(Var("r"), Var("c")), dtype=F32),
+            Assign("sq", EW("multiply"), ("v", "v"), F32),
+            Let("z", Literal(0.0, "float"), F32),
+            Accum("acc", "sq", EW("add"), F32, axes=("c",)),
+        )),
+        Write(output="ss", index=(Var("r"),), values=("acc",), value_dtype=F32),
+    ))
+    c.graph["nodes"]["ss"] = _kernel(entry, body, ["x"], [("ss", [rows], "f32")])
+    c.entry = entry
+    c.kernel["entry"] = entry
+    return c
+
+
 def atomic_sum_case(cid: str, n: int) -> Case:
     """make_world_set.py:247-266: every cell red.add's into sum_1[0]."""
     entry = "k_atomic_sum"
@@ -522,6 +543,25 @@ def chain_case(cid: str, n: int, which: str) -> Case:
                  Assign("q", EW("sqrt"), ("p",), F32), Assign("rq", EW("rsqrt"), ("p",), F32),
                  Assign("ex", EW("exp"), ("l",), F32), Assign("m", EW("multiply"), ("q", "rq"), F32),
                  Assign("d", EW("divide"), ("ex", "m"), F32), Assign("r", EW("add"), ("d", "l"), F32))
+    elif which == "contract_square_add":
+        # plain mul.f32 (square) whose only use is a plain add.f32
+        stmts = (x, Assign("q", EW("square"), ("in0",), F32), Assign("r", EW("add"), ("q", "in0"), F32))
+    elif which == "contract_nonadjacent":
+        # multiply and add separated by a Let: no explicit fma.rn, plain mul/add pair
+        stmts = (x, Let("c", Literal(1.5, "float"), F32), Assign("p", EW("multiply"), ("in0", "c"), F32),
+                 Let("d", Literal(0.25, "float"), F32), Assign("r", EW("add"), ("p", "d"), F32))
+    elif which == "contract_sub":
+        stmts = (x, Let("c", Literal(1.5, "float"), F32), Assign("p", EW("multiply"), ("in0", "c"), F32),
+                 Let("d", Literal(0.25, "float"), F32), Assign("r", EW("subtract"), ("d", "p"), F32))
+    elif which == "contract_multiuse":
+        # the product feeds two adds: not a single-use pair
+        stmts = (x, Let("c", Literal(1.5, "float"), F32), Assign("p", EW("multiply"), ("in0", "c"), F32),
+                 Assign("r1", EW("add"), ("p", "in0"), F32), Assign("r2", EW("subtract"), ("p", "c"), F32),
+                 Assign("r", EW("multiply"), ("r1", "r2"), F32))
+    elif which == "contract_log_add":
+        stmts = (x, Assign("ab", EW("abs"), ("in0",), F32), Let("e", Literal(1e-3, "float"), F32),
+                 Assign("p", EW("add"), ("ab", "e"), F32), Assign("l", EW("log"), ("p",), F32),
+                 Assign("r", EW("add"), ("l", "in0"), F32))
     else:
         raise ValueError(which)
     entry = f"k_{which}"
@@ -534,7 +574,7 @@ def chain_case(cid: str, n: int, which: str) -> Case:
     grid, block = _launch(n)
     args = [_arg(i, [n], seed=k) for k, i in enumerate(ins)] + [_arg("out", [n], output=True)]
     kern = _meta_kernel("out", entry, ins + ["out"], grid, block, args)
-    approx = which in ("silu_sigmoid", "exp_log_sqrt")
+    approx = which in ("silu_sigmoid", "exp_log_sqrt", "contract_log_add")
     return Case(cid, entry, graph, kern, family="pointwise",
                 check={"kind": "ulp", "ulp": 0, "oracle": APPROX_ORACLE if approx else {"ulp": 0}},
                 tags=("catalog",))
@@ -650,6 +690,7 @@ def all_cases() -> list[Case]:
     cases.append(mean_case("r_mean_777", 777))
     cases.append(fullmax_case("r_max_1024", 1024))
     cases.append(rowsum_loop_case("r_rowsumsq_loop_33x250", 33, 250))
+    cases.append(rowsum_loop_nonadjacent_case("r_rowsumsq_gap_17x300", 17, 300))
     cases.append(atomic_sum_case("r_atomic_sum_512", 512))
     # config 5
     cases.append(gemm_case("c5_gemm_full", 16384, 8192, 16384, config="c5", with_ref=False))
@@ -672,7 +713,9 @@ def all_cases() -> list[Case]:
         cases.append(unary_case(f"p_{op}_{n}", op, n, prep_abs=pa))
     for which, n in (("relu_mul", 300), ("scale_shift", 1536), ("leaky", 180), ("clamp", 240),
                      ("where", 384), ("select", 256), ("cond_else", 300), ("square_scale", 512),
-                     ("silu_sigmoid", 4100), ("exp_log_sqrt", 2051)):
+                     ("silu_sigmoid", 4100), ("exp_log_sqrt", 2051), ("contract_square_add", 1000),
+                     ("contract_nonadjacent", 1000), ("contract_sub", 1000), ("contract_multiuse", 1000),
+                     ("contract_log_add", 1000)):
         cases.append(chain_case(f"p_{which}_{n}", n, which))
     cases.append(add2d_case("p_add2d_7x13", 7, 13))
     cases.append(add2d_case("p_add2d_32x64", 32, 64))
