@@ -694,6 +694,7 @@ def all_cases() -> list[Case]:
     cases.append(atomic_sum_case("r_atomic_sum_512", 512))
     # config 5
     cases.append(gemm_case("c5_gemm_full", 16384, 8192, 16384, config="c5", with_ref=False))
+    cases.append(gemm_case("c5_gemm_prof_8192x8192x8192", 8192, 8192, 8192, with_ref=False))  # profiler size
     cases.append(gemm_case("c5_gemm_128x64x256", 128, 64, 256))
     cases.append(gemm_case("c5_gemm_256x512x512", 256, 512, 512))
     cases.append(gemm_case("c5_gemm_384x1024x768", 384, 1024, 768))
