@@ -17,9 +17,10 @@ PTX computes for the same statement:
   (compile.py:1415-1428);
 * the contraction the reference's PTX gets from ptxas at load time: the
   reference emits plain ``mul.f32``/``add.f32``/``sub.f32`` (no rounding
-  modifier, so the assembler may fuse them); a plain product whose only use
-  is a plain add/sub (or an Accum add) is computed as one FMA here too
-  (observed on B200 against the reference PTX, see :meth:`Emitter.plain_product`);
+  modifier, so the assembler may fuse them); every plain add/sub (or Accum
+  add) that consumes a plain product is computed as one FMA here too, however
+  many other uses the product has (observed on B200 against the reference
+  PTX, see :meth:`Emitter.plain_product`);
 * f32 literal rounding (``f32_hex``, compile.py:205-207), accumulator seeds
   (``identity_of``, compile.py:327-338), ordered float compares
   (``setp.<cmp>.f32``) and truncating float->int casts (``cvt.rzi``);
@@ -701,9 +702,10 @@ class Emitter:
 
     def plain_product(self, name):
         """Factors of ``name`` if the reference computes it with a plain
-        ``mul.f32`` whose only use is the instruction being emitted now - the
-        pattern the assembler fuses into an FMA."""
-        if not isinstance(name, str) or name not in self.products or self.uses.get(name, 0) != 1:
+        ``mul.f32``: the assembler fuses such a product into each plain
+        add/sub that consumes it (the multiply is repeated per consumer when
+        it has several), so the consumer is computed as one FMA."""
+        if not isinstance(name, str) or name not in self.products:
             return None
         if self.env.get(name, ("", ""))[1] != self.declared.get(f"{name}|f32"):
             return None

@@ -558,6 +558,18 @@ def chain_case(cid: str, n: int, which: str) -> Case:
         stmts = (x, Let("c", Literal(1.5, "float"), F32), Assign("p", EW("multiply"), ("in0", "c"), F32),
                  Assign("r1", EW("add"), ("p", "in0"), F32), Assign("r2", EW("subtract"), ("p", "c"), F32),
                  Assign("r", EW("multiply"), ("r1", "r2"), F32))
+    elif which == "contract_two_products":
+        # an add of two plain products: the assembler can fuse only one of them
+        stmts = (x, Let("c", Literal(1.5, "float"), F32), Let("d", Literal(-0.75, "float"), F32),
+                 Assign("p1", EW("multiply"), ("in0", "c"), F32), Assign("sq", EW("square"), ("in0",), F32),
+                 Assign("p2", EW("multiply"), ("sq", "d"), F32), Assign("r", EW("add"), ("p1", "p2"), F32))
+    elif which == "contract_cond":
+        # product defined before a Cond, consumed by adds inside both branches
+        stmts = (x, Let("c", Literal(1.5, "float"), F32), Assign("p", EW("multiply"), ("in0", "c"), F32),
+                 Init("r", 0.0, dtype=F32),
+                 Cond(BinaryExpr(">", Var("a0"), Literal(n // 2, "int")),
+                      body=(Assign("r", EW("add"), ("p", "in0"), F32),),
+                      else_body=(Assign("r", EW("subtract"), ("p", "c"), F32),)))
     elif which == "contract_log_add":
         stmts = (x, Assign("ab", EW("abs"), ("in0",), F32), Let("e", Literal(1e-3, "float"), F32),
                  Assign("p", EW("add"), ("ab", "e"), F32), Assign("l", EW("log"), ("p",), F32),
@@ -716,7 +728,7 @@ def all_cases() -> list[Case]:
                      ("where", 384), ("select", 256), ("cond_else", 300), ("square_scale", 512),
                      ("silu_sigmoid", 4100), ("exp_log_sqrt", 2051), ("contract_square_add", 1000),
                      ("contract_nonadjacent", 1000), ("contract_sub", 1000), ("contract_multiuse", 1000),
-                     ("contract_log_add", 1000)):
+                     ("contract_log_add", 1000), ("contract_two_products", 1000), ("contract_cond", 1000)):
         cases.append(chain_case(f"p_{which}_{n}", n, which))
     cases.append(add2d_case("p_add2d_7x13", 7, 13))
     cases.append(add2d_case("p_add2d_32x64", 32, 64))
