@@ -292,6 +292,11 @@ int launch_locked(emmy_module *m, const uint64_t *args, int nargs, const uint32_
 
 }  // namespace
 
+// Lets other translation units of the library report through emmy_last_error.
+extern "C" __attribute__((visibility("hidden"))) int emmy_record_error(int code, const char *msg) {
+    return fail(code, "%s", msg);
+}
+
 extern "C" {
 
 const char *emmy_version(void) { return "emmy_b200 1.0 (sm_100a)"; }

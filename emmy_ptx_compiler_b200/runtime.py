@@ -53,6 +53,7 @@ def _declare(lib) -> None:
         "emmy_host_free": ([vp], i32),
         "emmy_run_host": ([vp, P(vp), P(sz), P(C.c_uint8), i32, u64], i32),
         "emmy_time_launch": ([vp, P(u64), i32, i32, u64, P(C.c_float)], i32),
+        "emmy_sum_f32_noalloc": ([i32, u64, u64, u64, u64], i32),
         "emmy_comm_unique_id": ([P(C.c_uint8)], i32),
         "emmy_comm_init": ([i32, i32, i32, P(C.c_uint8), i32, P(vp)], i32),
         "emmy_allreduce_f32": ([vp, u64, u64, sz, u64, i32], i32),
@@ -69,7 +70,7 @@ def _declare(lib) -> None:
 EXPORTED = ("emmy_version", "emmy_last_error", "emmy_init", "emmy_device_count", "emmy_load",
             "emmy_unload", "emmy_module_info", "emmy_launch", "emmy_module_status", "emmy_sync",
             "emmy_alloc", "emmy_free", "emmy_memcpy_htod", "emmy_memcpy_dtoh", "emmy_memset_d8",
-            "emmy_host_alloc", "emmy_host_free", "emmy_run_host", "emmy_time_launch",
+            "emmy_host_alloc", "emmy_host_free", "emmy_run_host", "emmy_time_launch", "emmy_sum_f32_noalloc",
             "emmy_comm_unique_id", "emmy_comm_init", "emmy_allreduce_f32", "emmy_allgather_f32",
             "emmy_comm_destroy", "emmy_comm_abort")
 
@@ -183,6 +184,14 @@ class Module:
         sizes = (C.c_size_t * n)(*nbytes)
         rl = (C.c_uint8 * n)(*roles)
         _check(lib().emmy_run_host(self._h, ptrs, sizes, rl, n, C.c_uint64(stream)))
+
+
+def sum_f32_noalloc(x, n: int, out, device: int = 0, stream: int = 0) -> None:
+    """``out[0] = sum(x[:n])`` through emmy_sum_f32_noalloc: no device memory is
+    allocated; cross-block partials live in the library's fixed scratch array
+    (calls overlapping on one GPU race on it)."""
+    init(device)
+    _check(lib().emmy_sum_f32_noalloc(device, arg_word(x), n, arg_word(out), stream))
 
 
 def sync(device: int = 0, stream: int = 0, timeout_ms: int = 0) -> None:

@@ -111,6 +111,21 @@ int emmy_run_host(emmy_module_t m, void *const *host_ptrs, const size_t *bytes,
 int emmy_time_launch(emmy_module_t m, const uint64_t *args, int nargs, int iters, uint64_t stream,
                      float *ms_total);
 
+/* Full-array f32 sum that allocates nothing.  No counterpart in the
+ * reference.  For callers that may not call cudaMalloc (fixed memory budgets,
+ * pre-sized pools, runtimes that own every allocation): the cross-block
+ * scratch is one fixed __device__ array inside this library, of
+ * EMMY_NOALLOC_SCRATCH_BYTES per GPU that loads the library, held until the
+ * process exits.  Computes *out = sum(x[0..n)) on `stream` (asynchronous),
+ * n <= EMMY_NOALLOC_MAX_ELEMENTS, else EMMY_ERR_INVALID.  All calls on a
+ * device share the array: calls that overlap on the GPU race.  The first call
+ * on each device resolves the array's address (cudaGetSymbolAddress); make it
+ * before any stream capture. */
+#define EMMY_NOALLOC_MAX_CHUNKS 4096
+#define EMMY_NOALLOC_SCRATCH_BYTES (EMMY_NOALLOC_MAX_CHUNKS * 4 + 256)
+#define EMMY_NOALLOC_MAX_ELEMENTS (1ull << 36)
+int emmy_sum_f32_noalloc(int dev, const float *x, uint64_t n, float *out, uint64_t stream);
+
 /* NCCL over NVLink/NVSwitch for the one collective of the path: combining
  * per-GPU partials of a full-array reduction.  No reference counterpart
  * (the reference is single-GPU). */
