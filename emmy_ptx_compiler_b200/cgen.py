@@ -17,10 +17,11 @@ PTX computes for the same statement:
   (compile.py:1415-1428);
 * the contraction the reference's PTX gets from ptxas at load time: the
   reference emits plain ``mul.f32``/``add.f32``/``sub.f32`` (no rounding
-  modifier, so the assembler may fuse them); every plain add/sub (or Accum
-  add) that consumes a plain product is computed as one FMA here too, however
-  many other uses the product has (observed on B200 against the reference
-  PTX, see :meth:`Emitter.plain_product`);
+  modifier, so the assembler may fuse them).  A plain product all of whose
+  uses are plain add/sub (or Accum add) operands is fused into each of them,
+  in any branch; when both operands of one add qualify, the later-defined
+  product is the one fused (observed on B200 against the reference PTX, see
+  :meth:`Emitter.plain_product`);
 * f32 literal rounding (``f32_hex``, compile.py:205-207), accumulator seeds
   (``identity_of``, compile.py:327-338), ordered float compares
   (``setp.<cmp>.f32``) and truncating float->int casts (``cvt.rzi``);
@@ -184,6 +185,42 @@ def uses_name(stmt, name: str) -> bool:
     return False
 
 
+PRODUCT_OPS = ("multiply", "mul", "square", "log", "log_fast", "silu")
+
+
+def fusable_products(body) -> set[str]:
+    """Names defined once by a plain-product Assign (``mul.f32`` in the
+    reference's PTX) whose every read is an operand of a plain add/sub Assign
+    or the value of an add Accum: the products the assembler folds into FMAs."""
+    defs: dict[str, int] = {}
+    for t in ir.walk(body):
+        for name in _defined_names(t):
+            defs[name] = defs.get(name, 0) + 1
+    cands = {t.name for t in ir.walk(body)
+             if isinstance(t, ir.Assign) and ir.op_name(t.op) in PRODUCT_OPS and defs.get(t.name) == 1}
+    bad: set[str] = set()
+    for t in ir.walk(body):
+        if not isinstance(t, ir.Stmt):
+            continue
+        fusing = set()
+        if isinstance(t, ir.Assign) and ir.op_name(t.op) in ("add", "sum", "subtract", "sub") and len(t.args) == 2:
+            fusing = {a for a in t.args if isinstance(a, str)}
+        elif isinstance(t, ir.Accum) and ir.op_name(t.op) in ("add", "sum") and t.base in (None, t.name):
+            fusing = {t.value} if isinstance(t.value, str) else set()
+        for n in _operand_reads(t):
+            if n in cands and n not in fusing:
+                bad.add(n)
+    return cands - bad
+
+
+def _defined_names(t) -> list[str]:
+    if isinstance(t, ir.Load):
+        return list(t.names)
+    if isinstance(t, (ir.Assign, ir.Let, ir.Init, ir.Select)):
+        return [t.name]
+    return []
+
+
 def _operand_reads(s) -> list[str]:
     """IR names a statement reads as instruction operands (one entry per read)."""
     out: list[str] = []
@@ -231,9 +268,11 @@ class Emitter:
         self.write_hook = write_hook or self._default_write
         self.tmp = 0
         self.declared: dict[str, str] = {}
-        # plain products (name -> (a, b) factor codes) and per-name read counts
-        self.products: dict[str, tuple[str, str]] = {}
-        self.uses: dict[str, int] = {}
+        # plain products (name -> (a, b) factor codes, definition order) and the
+        # names whose every use is a plain add/sub operand
+        self.products: dict[str, tuple[str, str, int]] = {}
+        self.fusable: set[str] | None = None
+        self.order = 0
 
     # -------------------------------------------------------------- small utils
     def emit(self, line: str) -> None:
@@ -482,16 +521,10 @@ class Emitter:
         raise UnsupportedIR(f"unsupported assign op {op!r}")
 
     # -------------------------------------------------------------- statements
-    def count_uses(self, body) -> None:
-        for t in ir.walk(body):
-            if isinstance(t, ir.Stmt):
-                for n in _operand_reads(t):
-                    self.uses[n] = self.uses.get(n, 0) + 1
-
     def run(self, body) -> None:
         """Statement list with the reference's FMA lookahead (compile.py:1096-1131)."""
-        if not self.uses:
-            self.count_uses(body)
+        if self.fusable is None:
+            self.fusable = fusable_products(body)
         sl = list(ir.body_stmts(body))
         i = 0
         while i < len(sl):
@@ -620,7 +653,7 @@ class Emitter:
                     self.ind + "    ")
         c.declared = self.declared
         c.tmp = self.tmp + 1000
-        c.uses = self.uses
+        c.fusable = self.fusable
         c.products = self.products
         return c
 
@@ -671,6 +704,12 @@ class Emitter:
             return
         if op in ("add", "sum", "subtract", "sub") and len(args) == 2:
             pa, pb = self.plain_product(args[0]), self.plain_product(args[1])
+            if pa is not None and pb is not None:
+                # the assembler fuses one: the product defined last
+                if pa[2] > pb[2]:
+                    pb = None
+                else:
+                    pa = None
             a, b = self.as_f32(args[0]), self.as_f32(args[1])
             sub = op in ("subtract", "sub")
             if pa is not None:
@@ -696,7 +735,8 @@ class Emitter:
             factors = (fargs[0], sg)
         if factors is not None:
             self.assign(s.name, "f32", f"__fmul_rn({factors[0]}, {factors[1]})")
-            self.products[s.name] = factors
+            self.order += 1
+            self.products[s.name] = (factors[0], factors[1], self.order)
             return
         self.assign(s.name, "f32", self.f32_op(op, fargs))
 
@@ -706,6 +746,8 @@ class Emitter:
         add/sub that consumes it (the multiply is repeated per consumer when
         it has several), so the consumer is computed as one FMA."""
         if not isinstance(name, str) or name not in self.products:
+            return None
+        if self.fusable is not None and name not in self.fusable:
             return None
         if self.env.get(name, ("", ""))[1] != self.declared.get(f"{name}|f32"):
             return None

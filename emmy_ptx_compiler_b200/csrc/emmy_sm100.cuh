@@ -108,6 +108,15 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
         : "memory");
 }
 
+// 1-D bulk copy global -> this CTA's shared memory, completion on `bar`.
+// Both addresses 16-byte aligned, `bytes` a multiple of 16.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 
 __device__ __forceinline__ void tmem_alloc(uint32_t *holder, uint32_t ncols) {

@@ -31,6 +31,12 @@ from .common import KernelSource, LaunchPlan, ParamSpec, SM_COUNT, launch_record
 BLOCK = 256
 UNROLL = 2
 VEC = 4
+# bulk-copy pipeline: 8 consumer warps + 1 producer warp, 4096-cell tiles, up to 4 stages
+BULK_MIN_CELLS = 1 << 20
+BULK_CONSUMERS = 256
+BULK_TILE = BULK_CONSUMERS * VEC * 4
+BULK_SMEM_TARGET = 96 * 1024
+BULK_CTAS_PER_SM = 2
 _CELL_STMTS = (ir.Load, ir.Write, ir.Let, ir.Init, ir.Assign, ir.Accum, ir.Cond, ir.Select)
 
 
@@ -151,11 +157,25 @@ def _decode_axes(em: Emitter, axes, cell: str, prefix: str) -> None:
         em.bind_const(name, "int", var)
 
 
+def _streamed_loads(plan: PointwisePlan) -> list[ir.Load]:
+    """Loads that read every tile cell once (index = all tile axes in order)."""
+    return [s for s in ir.walk(plan.tile.body)
+            if isinstance(s, ir.Load) and not _const_index(s.index) and _streamed(s, plan)]
+
+
 def generate(kop: ir.KernelOp, plan: PointwisePlan, shapes: dict, dtypes: dict, args: list[str],
-             scalars: dict[str, str], written: set[str]) -> KernelSource:
+             scalars: dict[str, str], written: set[str], *, variant: str = "auto",
+             unroll: int = UNROLL) -> KernelSource:
+    """``variant``: "auto"/"vector" (register vectors), or "bulk" (shared-memory
+    ring fed by bulk async copies)."""
     vec_ok, why = vector_eligible(plan, shapes, dtypes)
     plan.vector = vec_ok
     plan.reasons = why
+    streamed = _streamed_loads(plan) if vec_ok else []
+    # measured on B200 (C2, 2^28 cells): register vectors 5.60 TB/s vs bulk pipeline 4.71 TB/s,
+    # so "auto" keeps register vectors; the bulk pipeline stays selectable
+    if streamed and variant == "bulk":
+        return _generate_bulk(kop, plan, shapes, dtypes, args, scalars, written, streamed)
     params: list[ParamSpec] = []
     ptrs: dict[str, str] = {}
     sig: list[str] = []
@@ -191,8 +211,9 @@ def generate(kop: ir.KernelOp, plan: PointwisePlan, shapes: dict, dtypes: dict, 
         w("    if (aligned) {")
         w(f"        constexpr long long NVEC = NCELL / {VEC};")
         w("        long long v = gtid;")
-        w(f"        for (; v + gstride < NVEC; v += {UNROLL} * gstride) {{")
-        lines.extend(_vector_trip(plan, shapes, dtypes, ptrs, scalar_env, ["v", "v + gstride"],
+        w(f"        for (; v + {unroll - 1} * gstride < NVEC; v += {unroll} * gstride) {{")
+        lines.extend(_vector_trip(plan, shapes, dtypes, ptrs, scalar_env,
+                                  ["v"] + [f"v + {u} * gstride" for u in range(1, unroll)],
                                   "            "))
         w("        }")
         w("        if (v < NVEC) {")
@@ -209,7 +230,7 @@ def generate(kop: ir.KernelOp, plan: PointwisePlan, shapes: dict, dtypes: dict, 
     w("    }")
     w("}")
     nvec = ncell // VEC if vec_ok else ncell
-    per_block = BLOCK * (UNROLL if vec_ok else 1)
+    per_block = BLOCK * (unroll if vec_ok else 1)
     grid = max(1, min((nvec + per_block - 1) // per_block, SM_COUNT * 8))
     launch = LaunchPlan(grid=(grid, 1, 1), block=(BLOCK, 1, 1), smem=0)
     lines.append(launch_record_source("pointwise", launch, params))
@@ -224,9 +245,12 @@ def _c(name: str) -> str:
 
 
 def _vector_trip(plan: PointwisePlan, shapes, dtypes, ptrs, scalar_env, vexprs: list[str],
-                 ind: str) -> list[str]:
+                 ind: str, smem_src: dict[int, str] | None = None) -> list[str]:
     """One trip: load U vectors of every input, run the cell body per lane,
-    store U vectors of every output."""
+    store U vectors of every output.  ``smem_src`` maps a load's position to a
+    shared-memory element pointer expression (indexed by the vector's offset
+    within the current tile, ``lo<u>``) for loads staged by bulk copies."""
+    smem_src = smem_src or {}
     axes = plan.axes
     out: list[str] = []
     loads = [s for s in ir.walk(plan.tile.body) if isinstance(s, ir.Load)]
@@ -252,6 +276,10 @@ def _vector_trip(plan: PointwisePlan, shapes, dtypes, ptrs, scalar_env, vexprs: 
                     _const_flat(s, shapes)
                 out.append(f"{ind}const {ctype(dt)} {var} = {ptr}[{off}];")
                 fetched[(li, u)] = (var, False, dt)
+                continue
+            if li in smem_src:
+                out.append(f"{ind}const auto {var} = emmy_lds{VEC}_{dt}({smem_src[li]} + lo{u});")
+                fetched[(li, u)] = (var, True, dt)
                 continue
             pos = _axis_aligned(s.index, axes)
             bstrides = _axis_strides([axes[p] for p in pos])
@@ -322,6 +350,22 @@ def _streamed(s: ir.Load, plan: PointwisePlan) -> bool:
 
 _VEC_HELPERS = r"""
 template <class T, int N> struct EmmyVec { T v[N]; };
+static __device__ __forceinline__ EmmyVec<float, 4> emmy_lds4_f32(const float* p) {
+    const float4 t = *reinterpret_cast<const float4*>(p);
+    return EmmyVec<float, 4>{{t.x, t.y, t.z, t.w}};
+}
+static __device__ __forceinline__ EmmyVec<__nv_bfloat16, 4> emmy_lds4_bf16(const __nv_bfloat16* p) {
+    EmmyVec<__nv_bfloat16, 4> r;
+    const uint2 t = *reinterpret_cast<const uint2*>(p);
+    memcpy(&r, &t, 8);
+    return r;
+}
+static __device__ __forceinline__ EmmyVec<__half, 4> emmy_lds4_f16(const __half* p) {
+    EmmyVec<__half, 4> r;
+    const uint2 t = *reinterpret_cast<const uint2*>(p);
+    memcpy(&r, &t, 8);
+    return r;
+}
 static __device__ __forceinline__ EmmyVec<float, 4> emmy_ld4_f32(const float* p, bool stream) {
     float4 t = stream ? __ldcs(reinterpret_cast<const float4*>(p))
                       : __ldg(reinterpret_cast<const float4*>(p));
@@ -354,3 +398,150 @@ static __device__ __forceinline__ void emmy_st4_f16(__half* p, __half a, __half 
     __stcs(reinterpret_cast<uint2*>(p), t);
 }
 """
+
+
+def _generate_bulk(kop, plan: PointwisePlan, shapes, dtypes, args, scalars, written,
+                   streamed: list[ir.Load]) -> KernelSource:
+    """Large vectorisable tiles: a producer warp streams each full-tile input
+    through a shared-memory ring with 1-D bulk async copies (``cp.async.bulk``,
+    completion on an mbarrier), so tens of KB per SM are in flight without
+    costing registers; 8 consumer warps run the cell body from shared memory
+    and store 128-bit vectors straight to global memory.  Misaligned pointers
+    fall back to the register-vector loop."""
+    from ..cgen import DEVICE_PRELUDE as _P  # noqa: F401  (same prelude as the other paths)
+    params: list[ParamSpec] = []
+    ptrs: dict[str, str] = {}
+    sig: list[str] = []
+    for name in args:
+        if name in scalars:
+            dt = scalars[name]
+            sig.append(f"{ctype(dt)} p_{_c(name)}")
+            params.append(ParamSpec(name, "scalar", dt))
+            continue
+        dt = ir.canon_dtype(dtypes.get(name))
+        cty = ctype(dt)
+        sig.append(f"{cty}* __restrict__ p_{_c(name)}" if name in written
+                   else f"const {cty}* __restrict__ p_{_c(name)}")
+        ptrs[name] = f"p_{_c(name)}"
+        params.append(ParamSpec(name, "ptr", dt))
+    scalar_env = {name: (("f32", f"p_{_c(name)}") if scalars[name] == "f32" else
+                         ("int", f"(long long)p_{_c(name)}")) for name in scalars}
+    loads = [s for s in ir.walk(plan.tile.body) if isinstance(s, ir.Load)]
+    inputs = []          # unique streamed buffers, in first-use order
+    for s in streamed:
+        if s.input not in inputs:
+            inputs.append(s.input)
+    esz = {n: ir.ELEM_BYTES[ir.canon_dtype(dtypes.get(n))] for n in inputs}
+    offs, off = {}, 0
+    for n in inputs:
+        offs[n] = off
+        off += -(-BULK_TILE * esz[n] // 128) * 128
+    stage_bytes = off
+    stages = max(2, min(4, BULK_SMEM_TARGET // stage_bytes))
+    smem = stages * stage_bytes + 2 * stages * 8 + 16
+    ncell = plan.ncells
+    tiles = -(-ncell // BULK_TILE)
+    smem_src = {}
+    for li, s in enumerate(loads):
+        if s in streamed:
+            dt = ir.canon_dtype(s.dtype or dtypes.get(s.input))
+            smem_src[li] = (f"reinterpret_cast<const {ctype(dt)}*>(stage_base + {offs[s.input]}u)")
+    L: list[str] = []
+    w = L.append
+    w(DEVICE_PRELUDE)
+    w(_VEC_HELPERS)
+    w('#include "emmy_sm100.cuh"')
+    nthreads = BULK_CONSUMERS + 32
+    w(f'extern "C" __global__ void __launch_bounds__({nthreads}, {BULK_CTAS_PER_SM}) {kop.name}(' + ", ".join(sig) + ") {")
+    w(f"    constexpr long long NCELL = {ncell}LL, NVEC = NCELL / {VEC}, TILES = {tiles}LL;")
+    w(f"    constexpr int TILE = {BULK_TILE}, STAGES = {stages}, CONS = {BULK_CONSUMERS};")
+    w(f"    constexpr uint32_t STAGE_BYTES = {stage_bytes}u, SMEM_BYTES = {smem}u;")
+    w("    constexpr uint64_t WAIT_NS = 2000000000ull;")
+    align_terms = [f"(uintptr_t){p}" for p in ptrs.values()]
+    w("    uint32_t dyn_smem;")
+    w('    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn_smem));')
+    w("    const bool aligned = ((" + (" | ".join(align_terms) or "0") + ") & 15u) == 0;")
+    w(f"    if (blockDim.x != {nthreads} || blockDim.y != 1 || blockDim.z != 1 || dyn_smem < SMEM_BYTES || !aligned) {{")
+    w("        // any other launch or misaligned buffers: register-vector / scalar grid-stride loops")
+    w("        const long long gstride = (long long)gridDim.x * blockDim.x * blockDim.y * blockDim.z;")
+    w("        const long long gtid = (long long)blockIdx.x * blockDim.x * blockDim.y * blockDim.z"
+      " + (threadIdx.z * blockDim.y + threadIdx.y) * blockDim.x + threadIdx.x;")
+    w("        if (aligned) {")
+    w("            for (long long v = gtid; v < NVEC; v += gstride) {")
+    L.extend(_vector_trip(plan, shapes, dtypes, ptrs, scalar_env, ["v"], "                "))
+    w("            }")
+    w("            return;")
+    w("        }")
+    w("        for (long long cell = gtid; cell < NCELL; cell += gstride) {")
+    em = Emitter(shapes, dtypes, ptrs, indent="            ")
+    em.env.update(scalar_env)
+    _decode_axes(em, plan.axes, "cell", "ax")
+    em.run(plan.tile.body)
+    L.extend(em.lines)
+    w("        }")
+    w("        return;")
+    w("    }")
+    w("    extern __shared__ __align__(128) uint8_t smem[];")
+    w("    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);")
+    w("    uint64_t *empty = full + STAGES;")
+    w("    volatile uint32_t *abort_flag = reinterpret_cast<volatile uint32_t *>(empty + STAGES);")
+    w("    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;")
+    w("    if (threadIdx.x == 0) {")
+    w("        for (int s = 0; s < STAGES; ++s) { emmy::mbar_init(&full[s], 1); emmy::mbar_init(&empty[s], CONS / 32); }")
+    w("        *abort_flag = 0u;")
+    w("        emmy::fence_barrier_init();")
+    w("    }")
+    w("    __syncthreads();")
+    w("    if (warp == CONS / 32) {")
+    w("        if (lane == 0) {")
+    w("            // producer: bulk-copy each tile of every streamed input into the ring")
+    w("            uint32_t issued = 0u, parity_bits = 0u;")
+    w("            bool ok = true;")
+    w("            int j = 0;")
+    w("            for (long long t = blockIdx.x; t < TILES; t += gridDim.x, ++j) {")
+    w("                const int s = j % STAGES;")
+    w("                const uint32_t ph = (uint32_t)(j / STAGES) & 1u;")
+    w("                if (!emmy::mbar_wait(&empty[s], ph ^ 1u, abort_flag, EMMY_STATUS_TIMEOUT_PRODUCER, WAIT_NS)) { ok = false; break; }")
+    w("                const long long base = t * TILE;")
+    w("                const uint32_t cnt = (uint32_t)((NCELL - base) < TILE ? (NCELL - base) : TILE);")
+    total = " + ".join(f"cnt * {esz[n]}u" for n in inputs)
+    w(f"                emmy::mbar_arrive_expect_tx(&full[s], {total});")
+    for n in inputs:
+        w(f"                emmy::bulk_load(smem + s * STAGE_BYTES + {offs[n]}u, {ptrs[n]} + base, cnt * {esz[n]}u, &full[s]);")
+    w("                issued |= 1u << s;")
+    w("                parity_bits = (parity_bits & ~(1u << s)) | (ph << s);")
+    w("            }")
+    w("            if (!ok) {")
+    w("                volatile uint32_t never = 0u;")
+    w("                for (int s = 0; s < STAGES; ++s)")
+    w("                    if (issued & (1u << s)) emmy::mbar_wait(&full[s], (parity_bits >> s) & 1u, &never, 0u, 20000000ull);")
+    w("            }")
+    w("        }")
+    w("        __syncwarp();")
+    w("    } else {")
+    w("        // consumers: 4 vectors of 4 cells per thread per tile, straight from shared memory")
+    w("        int j = 0;")
+    w("        for (long long t = blockIdx.x; t < TILES; t += gridDim.x, ++j) {")
+    w("            const int s = j % STAGES;")
+    w("            const uint32_t ph = (uint32_t)(j / STAGES) & 1u;")
+    w("            if (!emmy::mbar_wait(&full[s], ph, abort_flag, EMMY_STATUS_TIMEOUT_EPILOGUE, WAIT_NS)) break;")
+    w("            const uint8_t *stage_base = smem + s * STAGE_BYTES;")
+    w("            const long long vb = t * (TILE / 4);")
+    for u in range(4):
+        w(f"            if (vb + {u} * CONS + tid < NVEC) {{")
+        w(f"                const int lo0 = ({u} * CONS + tid) * 4;")
+        L.extend(_vector_trip(plan, shapes, dtypes, ptrs, scalar_env, [f"vb + {u} * CONS + tid"],
+                              "                ", smem_src))
+        w("            }")
+    w("            __syncwarp();")
+    w("            if (lane == 0) emmy::mbar_arrive(&empty[s]);")
+    w("        }")
+    w("    }")
+    w("}")
+    grid = max(1, min(tiles, SM_COUNT * BULK_CTAS_PER_SM))
+    launch = LaunchPlan(grid=(grid, 1, 1), block=(nthreads, 1, 1), smem=smem)
+    L.append(launch_record_source("pointwise", launch, params))
+    return KernelSource(entry=kop.name, source="\n".join(L), launch=launch, params=params,
+                        family="pointwise",
+                        notes={"vector": True, "bulk": True, "stages": stages, "tile": BULK_TILE,
+                               "scalar_reasons": [], "ncells": ncell})

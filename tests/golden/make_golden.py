@@ -563,6 +563,11 @@ def chain_case(cid: str, n: int, which: str) -> Case:
         stmts = (x, Let("c", Literal(1.5, "float"), F32), Let("d", Literal(-0.75, "float"), F32),
                  Assign("p1", EW("multiply"), ("in0", "c"), F32), Assign("sq", EW("square"), ("in0",), F32),
                  Assign("p2", EW("multiply"), ("sq", "d"), F32), Assign("r", EW("add"), ("p1", "p2"), F32))
+    elif which == "contract_two_products_swapped":
+        # same products, the later-defined one is now the add's first operand
+        stmts = (x, Let("c", Literal(1.5, "float"), F32), Let("d", Literal(-0.75, "float"), F32),
+                 Assign("p1", EW("multiply"), ("in0", "c"), F32), Assign("sq", EW("square"), ("in0",), F32),
+                 Assign("p2", EW("multiply"), ("sq", "d"), F32), Assign("r", EW("add"), ("p2", "p1"), F32))
     elif which == "contract_cond":
         # product defined before a Cond, consumed by adds inside both branches
         stmts = (x, Let("c", Literal(1.5, "float"), F32), Assign("p", EW("multiply"), ("in0", "c"), F32),
@@ -728,7 +733,8 @@ def all_cases() -> list[Case]:
                      ("where", 384), ("select", 256), ("cond_else", 300), ("square_scale", 512),
                      ("silu_sigmoid", 4100), ("exp_log_sqrt", 2051), ("contract_square_add", 1000),
                      ("contract_nonadjacent", 1000), ("contract_sub", 1000), ("contract_multiuse", 1000),
-                     ("contract_log_add", 1000), ("contract_two_products", 1000), ("contract_cond", 1000)):
+                     ("contract_log_add", 1000), ("contract_two_products", 1000), ("contract_cond", 1000),
+                     ("contract_two_products_swapped", 1000)):
         cases.append(chain_case(f"p_{which}_{n}", n, which))
     cases.append(add2d_case("p_add2d_7x13", 7, 13))
     cases.append(add2d_case("p_add2d_32x64", 32, 64))
