@@ -159,6 +159,30 @@ def make_inputs(cfg: str, spec, rank: int, device: str):
     return out
 
 
+# ---------------------------------------------------------------------------- distributed glue
+
+
+def max_over_ranks(value: float, world: int, device) -> float:
+    """The slowest rank's time (every rank must call this, in the same order)."""
+    if world <= 1:
+        return float(value)
+    import torch
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def combine_step(cfg: str, bufs: dict, world: int):
+    """The path's one exchange: a full-array sum over N GPUs adds the per-GPU
+    partial sums (NCCL all-reduce of one float, enqueued on the current
+    stream).  Every other config shards with no collective."""
+    if cfg != "c4" or world <= 1:
+        return lambda: None
+    import torch
+    out = bufs["sum_1"]
+    return lambda: torch.distributed.all_reduce(out, op=torch.distributed.ReduceOp.SUM)
+
+
 # ---------------------------------------------------------------------------- our arm
 
 
@@ -181,8 +205,11 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
         if world > 1:
             torch.distributed.barrier()
 
+    combine = combine_step(args.config, bufs, world)
+
     for _ in range(args.warmup):
         mod.launch(order, stream=stream)
+        combine()
     torch.cuda.synchronize(local)
     st = mod.status()
     if st:
@@ -194,14 +221,11 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
         e0.record()
         for _ in range(args.steps):
             mod.launch(order, stream=stream)
+            combine()
         e1.record()
         torch.cuda.synchronize(local)
     barrier()
-    ms = e0.elapsed_time(e1)
-    ms_t = torch.tensor([ms], device=device)
-    if world > 1:
-        torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
-    ms_max = float(ms_t.item())
+    ms_max = max_over_ranks(e0.elapsed_time(e1), world, device)
     per_launch_ms = ms_max / args.steps
     value = units * world * args.steps / (ms_max / 1e3) / (1e9 if unit == "GB/s" else 1e12)
     achieved = units / (per_launch_ms / 1e3) / (1e9 if unit == "GB/s" else 1e12)
@@ -231,11 +255,7 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
         mod.run_host(ptrs, nbytes, roles, stream=stream)
-    e2e_s = time.perf_counter() - t0
-    e2e_t = torch.tensor([e2e_s], device=device)
-    if world > 1:
-        torch.distributed.all_reduce(e2e_t, op=torch.distributed.ReduceOp.MAX)
-    e2e_s = float(e2e_t.item())
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world, device)
     h2d = sum(b for b, r in zip(nbytes, roles) if r == runtime.EMMY_ROLE_IN)
     d2h = sum(b for b, r in zip(nbytes, roles) if r == runtime.EMMY_ROLE_OUT)
     e2e_value = units * world * e2e_steps / e2e_s / (1e9 if unit == "GB/s" else 1e12)
@@ -268,6 +288,10 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     }
     if ref_ptx is not None:
         line["reference_ptx_gpu"] = ref_ptx
+    if args.config == "c4" and world > 1:
+        line["config"]["parallelism"] = (f"{world} ranks, each its own 2^31-element shard; the per-rank "
+                                         "sums are combined by an NCCL all-reduce inside every step")
+        line["gpu_launches"] = args.steps
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.config, seconds=args.cpu_seconds)
     return line
