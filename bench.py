@@ -392,7 +392,7 @@ def run_reference(args, rank: int) -> dict | None:
             list(ex.map(lambda _: fn(), range(threads)))
         el = time.perf_counter() - t0
     value = units_task * threads * args.steps / el / 1e9
-    return {"metric": METRIC, "value": round(value, 3), "unit": unit, "n_gpus": 0, "steps": args.steps,
+    return {"metric": METRIC, "value": round(value, 3), "unit": unit, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
             "config": {"workload": workload, "case": case_id},
@@ -402,6 +402,20 @@ def run_reference(args, rank: int) -> dict | None:
 
 
 def main() -> int:
+    # stdout carries exactly one JSON line: native libraries (NCCL prints its
+    # version banner on fd 1) are pointed at stderr, the line goes to a copy
+    # of the original stdout
+    sys.stdout.flush()
+    json_fd = os.dup(1)
+    os.dup2(2, 1)
+    out = os.fdopen(json_fd, "w")
+    try:
+        return _main(out)
+    finally:
+        out.flush()
+
+
+def _main(out) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -419,7 +433,7 @@ def main() -> int:
     if args.impl == "reference":
         line = run_reference(args, rank)
         if line is not None:
-            print(json.dumps(line), flush=True)
+            print(json.dumps(line), file=out, flush=True)
         return 0
     if world > 1:
         import datetime
@@ -434,7 +448,7 @@ def main() -> int:
             import torch
             torch.distributed.destroy_process_group()
     if line is not None:
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line), file=out, flush=True)
     return 0
 
 

@@ -5,10 +5,8 @@ ranks that wait on each other never share one GPU)."""
 
 from __future__ import annotations
 
-import os
 import sys
 
-import numpy as np
 import pytest
 
 from conftest import CASES, REPO
@@ -65,4 +63,3 @@ def test_sharded_sum_with_nccl_combine():
         assert abs(part - ref) <= 1e-5 * abs(ref) + 1e-3
         assert abs(total - want) <= 1e-5 * abs(want) + 2e-3
     assert res[0][3] == res[1][3], "every rank sees the same combined sum"
-    del os, np
