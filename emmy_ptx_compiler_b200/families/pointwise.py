@@ -31,6 +31,9 @@ from .common import KernelSource, LaunchPlan, ParamSpec, SM_COUNT, launch_record
 BLOCK = 256
 UNROLL = 2
 VEC = 4
+PREFETCH = 0      # trips ahead to prefetch full-tile inputs into L2 (0 = off)
+MIN_BLOCKS = 0    # __launch_bounds__ minimum blocks per SM (0 = compiler's choice)
+ORDER = "grid"    # "grid": grid-stride vectors; "blocked": each CTA streams one contiguous chunk
 # bulk-copy pipeline: 8 consumer warps + 1 producer warp, 4096-cell tiles, up to 4 stages
 BULK_MIN_CELLS = 1 << 20
 BULK_CONSUMERS = 256
@@ -165,7 +168,8 @@ def _streamed_loads(plan: PointwisePlan) -> list[ir.Load]:
 
 def generate(kop: ir.KernelOp, plan: PointwisePlan, shapes: dict, dtypes: dict, args: list[str],
              scalars: dict[str, str], written: set[str], *, variant: str = "auto",
-             unroll: int = UNROLL) -> KernelSource:
+             unroll: int = UNROLL, prefetch: int = PREFETCH, min_blocks: int = MIN_BLOCKS,
+             order: str = ORDER, hoist_broadcast: bool = True) -> KernelSource:
     """``variant``: "auto"/"vector" (register vectors), or "bulk" (shared-memory
     ring fed by bulk async copies)."""
     vec_ok, why = vector_eligible(plan, shapes, dtypes)
@@ -199,7 +203,8 @@ def generate(kop: ir.KernelOp, plan: PointwisePlan, shapes: dict, dtypes: dict, 
     w = lines.append
     w(DEVICE_PRELUDE)
     w(_VEC_HELPERS)
-    w(f'extern "C" __global__ void __launch_bounds__({BLOCK}) {kop.name}(' + ", ".join(sig) + ") {")
+    lb = f"{BLOCK}, {min_blocks}" if min_blocks else f"{BLOCK}"
+    w(f'extern "C" __global__ void __launch_bounds__({lb}) {kop.name}(' + ", ".join(sig) + ") {")
     w(f"    constexpr long long NCELL = {ncell}LL;")
     w("    const long long gstride = (long long)gridDim.x * blockDim.x;")
     w("    const long long gtid = (long long)blockIdx.x * blockDim.x + threadIdx.x;")
@@ -210,8 +215,69 @@ def generate(kop: ir.KernelOp, plan: PointwisePlan, shapes: dict, dtypes: dict, 
         w("    const bool aligned = ((" + (" | ".join(align_terms) if align_terms else "0") + ") & 15u) == 0;")
         w("    if (aligned) {")
         w(f"        constexpr long long NVEC = NCELL / {VEC};")
+        if order == "blocked":
+            # CTA b owns vectors [b*per, (b+1)*per); a trip covers unroll*blockDim consecutive vectors
+            w("        const long long per = (NVEC + gridDim.x - 1) / gridDim.x;")
+            w("        const long long vbeg = (long long)blockIdx.x * per;")
+            w("        const long long vend = (vbeg + per < NVEC) ? (vbeg + per) : NVEC;")
+            w("        const long long bstride = blockDim.x;")
+            w("        long long v = vbeg + threadIdx.x;")
+            w(f"        for (; v + {unroll - 1} * bstride < vend; v += {unroll} * bstride) {{")
+            lines.extend(_vector_trip(plan, shapes, dtypes, ptrs, scalar_env,
+                                      ["v"] + [f"v + {u} * bstride" for u in range(1, unroll)],
+                                      "            "))
+            w("        }")
+            w("        for (; v < vend; v += bstride) {")
+            lines.extend(_vector_trip(plan, shapes, dtypes, ptrs, scalar_env, ["v"], "            "))
+            w("        }")
+            w("        return;")
+            w("    }")
+            return _finish_vector(kop, plan, lines, ncell, unroll, vec_ok, params, why, em_path=True,
+                                  shapes=shapes, dtypes=dtypes, ptrs=ptrs, scalar_env=scalar_env)
         w("        long long v = gtid;")
+        hoist = _hoistable(plan) if hoist_broadcast else {}
+        if hoist:
+            period = max(p for _, p in hoist.values())
+            # a thread's broadcast operands are the same on every trip when the grid
+            # stride is a whole number of their periods: load them once
+            w(f"        if ((gstride * {VEC}) % {period}LL == 0 && v < NVEC) {{")
+            names = {}
+            w("            const long long hc = v * %dLL;" % VEC)
+            strides = _axis_strides(axes)
+            for i, ((name, ext), st) in enumerate(zip(axes, strides)):
+                q = "hc" if st == 1 else f"(hc / {st}LL)"
+                expr = q if i == 0 else f"({q} % {ext}LL)"
+                w(f"            const long long h_ax{i} = {expr};")
+            loads_all = [t for t in ir.walk(plan.tile.body) if isinstance(t, ir.Load)]
+            for li, (ld, _) in hoist.items():
+                dt = ir.canon_dtype(ld.dtype or dtypes.get(ld.input))
+                pos = _axis_aligned(ld.index, axes)
+                bstr = _axis_strides([axes[p_] for p_ in pos])
+                off = " + ".join(f"h_ax{p_} * {bs}LL" for p_, bs in zip(pos, bstr))
+                var = f"hl{li}"
+                if _contiguous(ld, plan):
+                    w(f"            const auto {var} = emmy_ld{VEC}_{dt}({ptrs[ld.input]} + ({off}), false);")
+                else:
+                    w(f"            const {ctype(dt)} {var} = {ptrs[ld.input]}[{off}];")
+                names[li] = var
+            del loads_all
+            w(f"            for (; v + {unroll - 1} * gstride < NVEC; v += {unroll} * gstride) {{")
+            lines.extend(_vector_trip(plan, shapes, dtypes, ptrs, scalar_env,
+                                      ["v"] + [f"v + {u} * gstride" for u in range(1, unroll)],
+                                      "                ", hoisted=names))
+            w("            }")
+            w("            if (v < NVEC) {")
+            lines.extend(_vector_trip(plan, shapes, dtypes, ptrs, scalar_env, ["v"], "                ",
+                                      hoisted=names))
+            w("            }")
+            w("            return;")
+            w("        }")
         w(f"        for (; v + {unroll - 1} * gstride < NVEC; v += {unroll} * gstride) {{")
+        if prefetch:
+            for s_ in _streamed_loads(plan):
+                for u in range(unroll):
+                    w(f"            {{ const long long pv = v + {prefetch * unroll + u} * gstride;")
+                    w(f"              if (pv < NVEC) emmy_prefetch_l2({ptrs[s_.input]} + pv * {VEC}); }}")
         lines.extend(_vector_trip(plan, shapes, dtypes, ptrs, scalar_env,
                                   ["v"] + [f"v + {u} * gstride" for u in range(1, unroll)],
                                   "            "))
@@ -221,10 +287,18 @@ def generate(kop: ir.KernelOp, plan: PointwisePlan, shapes: dict, dtypes: dict, 
         w("        }")
         w("        return;")
         w("    }")
+    return _finish_vector(kop, plan, lines, ncell, unroll, vec_ok, params, why, em_path=True,
+                          shapes=shapes, dtypes=dtypes, ptrs=ptrs, scalar_env=scalar_env)
+
+
+def _finish_vector(kop, plan, lines, ncell, unroll, vec_ok, params, why, *, em_path, shapes, dtypes, ptrs,
+                   scalar_env) -> KernelSource:
+    """The scalar grid-stride loop (any launch, any alignment) and the launch record."""
+    w = lines.append
     w("    for (long long cell = gtid; cell < NCELL; cell += gstride) {")
     em = Emitter(shapes, dtypes, ptrs, indent="        ")
     em.env.update(scalar_env)
-    _decode_axes(em, axes, "cell", "ax")
+    _decode_axes(em, plan.axes, "cell", "ax")
     em.run(plan.tile.body)
     lines.extend(em.lines)
     w("    }")
@@ -245,12 +319,14 @@ def _c(name: str) -> str:
 
 
 def _vector_trip(plan: PointwisePlan, shapes, dtypes, ptrs, scalar_env, vexprs: list[str],
-                 ind: str, smem_src: dict[int, str] | None = None) -> list[str]:
+                 ind: str, smem_src: dict[int, str] | None = None,
+                 hoisted: dict[int, str] | None = None) -> list[str]:
     """One trip: load U vectors of every input, run the cell body per lane,
     store U vectors of every output.  ``smem_src`` maps a load's position to a
     shared-memory element pointer expression (indexed by the vector's offset
     within the current tile, ``lo<u>``) for loads staged by bulk copies."""
     smem_src = smem_src or {}
+    hoisted = hoisted or {}
     axes = plan.axes
     out: list[str] = []
     loads = [s for s in ir.walk(plan.tile.body) if isinstance(s, ir.Load)]
@@ -280,6 +356,9 @@ def _vector_trip(plan: PointwisePlan, shapes, dtypes, ptrs, scalar_env, vexprs: 
             if li in smem_src:
                 out.append(f"{ind}const auto {var} = emmy_lds{VEC}_{dt}({smem_src[li]} + lo{u});")
                 fetched[(li, u)] = (var, True, dt)
+                continue
+            if li in hoisted:
+                fetched[(li, u)] = (hoisted[li], _contiguous(s, plan), dt)
                 continue
             pos = _axis_aligned(s.index, axes)
             bstrides = _axis_strides([axes[p] for p in pos])
@@ -331,6 +410,31 @@ def _vector_trip(plan: PointwisePlan, shapes, dtypes, ptrs, scalar_env, vexprs: 
     return out
 
 
+def _contiguous(s: ir.Load, plan: PointwisePlan) -> bool:
+    pos = _axis_aligned(s.index, plan.axes)
+    return bool(pos) and pos[-1] == len(plan.axes) - 1
+
+
+def _hoistable(plan: PointwisePlan) -> dict[int, tuple[ir.Load, int]]:
+    """Broadcast loads indexed by a proper suffix of the tile axes: their value
+    for cell c depends only on c mod P (P = product of those axes' extents).
+    Maps load position -> (load, P)."""
+    out = {}
+    loads = [t for t in ir.walk(plan.tile.body) if isinstance(t, ir.Load)]
+    n = len(plan.axes)
+    for li, ld in enumerate(loads):
+        if _const_index(ld.index) or _streamed(ld, plan):
+            continue
+        pos = _axis_aligned(ld.index, plan.axes)
+        if not pos or pos != list(range(pos[0], n)):
+            continue
+        period = 1
+        for p_ in pos:
+            period *= plan.axes[p_][1]
+        out[li] = (ld, period)
+    return out
+
+
 def _const_flat(s: ir.Load, shapes) -> str:
     shape = shapes.get(s.input)
     vals = [int(ix.value) for ix in s.index]
@@ -350,6 +454,9 @@ def _streamed(s: ir.Load, plan: PointwisePlan) -> bool:
 
 _VEC_HELPERS = r"""
 template <class T, int N> struct EmmyVec { T v[N]; };
+static __device__ __forceinline__ void emmy_prefetch_l2(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" :: "l"(p));
+}
 static __device__ __forceinline__ EmmyVec<float, 4> emmy_lds4_f32(const float* p) {
     const float4 t = *reinterpret_cast<const float4*>(p);
     return EmmyVec<float, 4>{{t.x, t.y, t.z, t.w}};
