@@ -49,9 +49,14 @@ def _scalars(meta: dict | None, dtypes: dict) -> dict[str, str]:
     return out
 
 
-def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: dict | None) -> Lowered:
-    """Classify ``kop`` into a family and generate its specialised source."""
+def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: dict | None,
+          options: dict | None = None) -> Lowered:
+    """Classify ``kop`` into a family and generate its specialised source.
+
+    ``options`` selects among equivalent schedules (results do not depend on
+    it): ``{"gemm_variant": "auto" | "pair" | "single"}``."""
     meta = meta or {}
+    options = options or {}
     written = {s.output for s in ir.walk(kop.body) if isinstance(s, ir.Write)}
     scalars = _scalars(meta, dtypes)
     for name in args:
@@ -59,7 +64,8 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
             raise UnsupportedIR(f"parameter {name!r} has no shape or dtype")
     plan = gemm.match(kop, shapes, dtypes)
     if plan is not None:
-        ks = gemm.generate(kop, plan, shapes, dtypes, args, scalars, written)
+        ks = gemm.generate(kop, plan, shapes, dtypes, args, scalars, written,
+                           variant=options.get("gemm_variant", "auto"))
         return Lowered(ks, args, shapes, dtypes, meta)
     plan = reduction.match(kop, shapes, dtypes)
     if plan is not None:
@@ -79,17 +85,18 @@ class Compiler:
     constructor the reference's tests use (compile.py:410-411, 823)."""
 
     def __init__(self, kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str],
-                 meta: dict | None = None):
+                 meta: dict | None = None, options: dict | None = None):
         self.kop = kop
         self.shapes = {k: tuple(int(x) for x in v) for k, v in shapes.items()}
         self.dtypes = dict(dtypes)
         self.args = list(args)
         self.meta = meta or {}
+        self.options = dict(options or {})
         self.lowered: Lowered | None = None
 
     def lower(self) -> Lowered:
         if self.lowered is None:
-            self.lowered = lower(self.kop, self.shapes, self.dtypes, self.args, self.meta)
+            self.lowered = lower(self.kop, self.shapes, self.dtypes, self.args, self.meta, self.options)
         return self.lowered
 
     def run(self) -> str:
@@ -102,10 +109,10 @@ class Compiler:
 
 
 def _bundle_from(kop: ir.KernelOp, raw: dict | None, meta_k: dict | None, path: Path | None,
-                 want_cubin: bool = False) -> dict:
+                 want_cubin: bool = False, options: dict | None = None) -> dict:
     args = frontend.arg_order_for(kop, meta_k)
     shapes, dtypes = frontend.load_shapes(raw, kop, meta_k)
-    comp = Compiler(kop, shapes, dtypes, args, meta_k)
+    comp = Compiler(kop, shapes, dtypes, args, meta_k, options)
     low = comp.lower()
     ks = low.kernel
     ptx = comp.run()
@@ -142,12 +149,12 @@ def _bundle_from(kop: ir.KernelOp, raw: dict | None, meta_k: dict | None, path: 
     return out
 
 
-def compile_bundle(path, want_cubin: bool = False) -> dict:
+def compile_bundle(path, want_cubin: bool = False, options: dict | None = None) -> dict:
     path = Path(path)
     raw = json.loads(path.read_text(encoding="utf-8"))
     info = frontend.load_graph(raw)
     meta_k = frontend.load_meta_kernel(path, info.kop.name)
-    return _bundle_from(info.kop, raw, meta_k, path, want_cubin)
+    return _bundle_from(info.kop, raw, meta_k, path, want_cubin, options)
 
 
 def compile_ir(path) -> str:

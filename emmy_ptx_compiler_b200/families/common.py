@@ -80,7 +80,7 @@ def launch_record_source(family: str, launch: LaunchPlan, params: list[ParamSpec
         "\n#include \"emmy_launch_record.h\"\n"
         "extern \"C\" __device__ unsigned int emmy_status = 0u;\n"
         "extern \"C\" __device__ const EmmyLaunchRecord emmy_launch_record = {\n"
-        f"    EMMY_LR_MAGIC, EMMY_LR_VERSION, {FAMILY_ID[family]}u, 0u,\n"
+        f"    EMMY_LR_MAGIC, EMMY_LR_VERSION, {FAMILY_ID[family]}u, {int(launch.cluster[0])}u,\n"
         f"    {{{g[0]}u, {g[1]}u, {g[2]}u}}, {{{b[0]}u, {b[1]}u, {b[2]}u}}, {launch.smem}u, {len(params)}u,\n"
         "    {" + ", ".join(f"{k}u" for k in kinds) + "},\n"
         f"    {len(tmaps)}u, 0u,\n"

@@ -35,6 +35,7 @@ from ..errors import UnsupportedIR
 from .common import KernelSource, LaunchPlan, ParamSpec, SM_COUNT, TmapSpec, launch_record_source
 
 BM, BN, BK, STAGES = 128, 256, 64, 4
+PAIR_BM, PAIR_STAGES = 256, 6   # CTA-pair tile: 256 x 256, 128 rows and 128 B-columns per CTA
 TC_THREADS = 192
 SIMT_BM, SIMT_BN, SIMT_BK, SIMT_THREADS = 64, 64, 16, 256
 GROUP_M = 16
@@ -163,7 +164,9 @@ def _tc_ok(plan: GemmPlan, dtypes) -> tuple[bool, list[str]]:
 
 
 def generate(kop: ir.KernelOp, plan: GemmPlan, shapes: dict, dtypes: dict, args: list[str],
-             scalars: dict[str, str], written: set[str]) -> KernelSource:
+             scalars: dict[str, str], written: set[str], *, variant: str = "auto") -> KernelSource:
+    """``variant``: "auto" (CTA-pair kernel when M >= 256 and N >= 256, else
+    single-CTA), "pair", "single"; non-TMA-able shapes and f32 go to SIMT."""
     params: list[ParamSpec] = []
     ptrs: dict[str, str] = {}
     sig: list[str] = []
@@ -181,6 +184,8 @@ def generate(kop: ir.KernelOp, plan: GemmPlan, shapes: dict, dtypes: dict, args:
                   for n in scalars}
     ok, why = _tc_ok(plan, dtypes)
     if ok:
+        if variant == "pair" or (variant == "auto" and plan.M >= PAIR_BM and plan.N >= BN):
+            return _gen_tcgen05_pair(kop, plan, shapes, dtypes, args, ptrs, sig, params, scalar_env)
         return _gen_tcgen05(kop, plan, shapes, dtypes, args, ptrs, sig, params, scalar_env)
     return _gen_simt(kop, plan, shapes, dtypes, args, ptrs, sig, params, scalar_env, why)
 
@@ -524,3 +529,258 @@ extern "C" __global__ void __launch_bounds__({SIMT_THREADS}) {kop.name}({", ".jo
     src += launch_record_source("gemm", launch, params)
     notes = {"kernel": "simt", "tile": [SIMT_BM, SIMT_BN, SIMT_BK], "tiles": tiles, "why_not_tcgen05": why}
     return KernelSource(entry=kop.name, source=src, launch=launch, params=params, family="gemm", notes=notes)
+
+
+# ---------------------------------------------------------------------------- tcgen05, CTA pair
+
+
+def _gen_tcgen05_pair(kop, plan: GemmPlan, shapes, dtypes, args, ptrs, sig, params, scalar_env) -> KernelSource:
+    """256x256 tiles on a cluster of two CTAs (``cta_group::2``): each CTA loads
+    its 128 rows of A and its 128 columns of B per stage (32 KB instead of the
+    single-CTA kernel's 48 KB for half the FLOPs), the leader issues
+    ``tcgen05.mma.cta_group::2`` 256x256x16 over both CTAs' shared memory into
+    both CTAs' tensor memory, and each CTA's epilogue drains its own 128 rows.
+    6 pipeline stages fit in shared memory."""
+    M, N, K = plan.M, plan.N, plan.K
+    mb, nb, kb = -(-M // PAIR_BM), -(-N // BN), -(-K // BK)
+    tiles = mb * nb
+    odt = ir.canon_dtype(plan.out.value_dtype or dtypes.get(plan.out.output))
+    ocls = ctype(odt)
+    fmt = 1 if plan.ab_dtype == "bf16" else 0
+    a_idx, b_idx = args.index(plan.a.input), args.index(plan.b.input)
+    esz = 2
+    cbm, cbn = PAIR_BM // 2, BN // 2
+    tm_a = TmapSpec(a_idx, TMAP_DTYPE[plan.ab_dtype], [K, M], [K * esz], [BK, cbm], SWIZZLE_128B, L2_256B)
+    if plan.b_nk:
+        tm_b = TmapSpec(b_idx, TMAP_DTYPE[plan.ab_dtype], [K, N], [K * esz], [BK, cbn], SWIZZLE_128B, L2_256B)
+    else:
+        tm_b = TmapSpec(b_idx, TMAP_DTYPE[plan.ab_dtype], [N, K], [N * esz], [64, BK], SWIZZLE_128B, L2_256B)
+    a_stage = cbm * BK * esz
+    b_stage = cbn * BK * esz
+    smem = 1024 + PAIR_STAGES * (a_stage + b_stage) + 256
+    sig = list(sig) + ["const __grid_constant__ CUtensorMap tm_a", "const __grid_constant__ CUtensorMap tm_b"]
+    out_ptr = ptrs[plan.out.output]
+    vec_store = (N % 8 == 0) if odt in ("bf16", "f16") else (N % 4 == 0)
+    epi_full = _epilogue_code(plan, shapes, dtypes, ptrs, scalar_env, "__uint_as_float(r[jj])", "row",
+                              "(col0 + jj)", " " * 24, "ov[jj]")
+    epi_any = _epilogue_code(plan, shapes, dtypes, ptrs, scalar_env, "__uint_as_float(r[jj])", "row",
+                             "(col0 + jj)", " " * 28, "ov1")
+    if odt in ("bf16", "f16"):
+        pack = ("                    uint4 *dst = reinterpret_cast<uint4 *>(" + out_ptr + " + row * (long long)N + col0);\n"
+                "                    #pragma unroll\n"
+                "                    for (int v = 0; v < 4; ++v) {\n"
+                "                        uint4 w;\n"
+                "                        memcpy(&w, &ov[v * 8], 16);\n"
+                "                        dst[v] = w;\n"
+                "                    }\n")
+    else:
+        pack = ("                    float4 *dst = reinterpret_cast<float4 *>(" + out_ptr + " + row * (long long)N + col0);\n"
+                "                    #pragma unroll\n"
+                "                    for (int v = 0; v < 8; ++v) dst[v] = make_float4(ov[4*v], ov[4*v+1], ov[4*v+2], ov[4*v+3]);\n")
+    if plan.b_nk:
+        b_loads = ("                    emmy::tma_load_2d_pair(sB + stage * B_STAGE, &tm_b, fbar, k * BK, "
+                   "tn * BN + (int)rank * CBN);")
+        b_desc = "                        const uint64_t bd = emmy::smem_desc_sw128(b_base + kk * 32, 16, 1024);"
+    else:
+        b_loads = "\n".join(
+            f"                    emmy::tma_load_2d_pair(sB + stage * B_STAGE + {j * 8192}u, &tm_b, fbar, "
+            f"tn * BN + (int)rank * CBN + {64 * j}, k * BK);" for j in range(cbn // 64))
+        b_desc = "                        const uint64_t bd = emmy::smem_desc_sw128(b_base + kk * 2048, 8192, 1024);"
+    src = f"""{DEVICE_PRELUDE}
+#include <string.h>
+#include "emmy_sm100.cuh"
+
+namespace {{
+constexpr long long M = {M}LL, N = {N}LL, K = {K}LL;
+constexpr int BM = {PAIR_BM}, CBM = {cbm}, BN = {BN}, CBN = {cbn}, BK = {BK}, STAGES = {PAIR_STAGES};
+constexpr int MB = {mb}, NB = {nb}, KB = {kb}, TILES = {tiles}, GROUP_M = {GROUP_M};
+constexpr uint32_t A_STAGE = {a_stage}u, B_STAGE = {b_stage}u;
+constexpr uint32_t SMEM_BYTES = {smem}u;
+constexpr uint32_t IDESC = emmy::idesc_f16({fmt}u, {0 if plan.b_nk else 1}u, BM, BN);
+constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s per wait: orders of magnitude above any legal wait
+
+__device__ __forceinline__ void tile_coords(int t, int &mb, int &nb) {{
+    const int per_group = GROUP_M * NB;
+    const int g = t / per_group;
+    const int r = t - g * per_group;
+    const int first = g * GROUP_M;
+    const int rows = (MB - first) < GROUP_M ? (MB - first) : GROUP_M;
+    mb = first + r % rows;
+    nb = r / rows;
+}}
+}}  // namespace
+
+extern "C" __global__ void __launch_bounds__({TC_THREADS}, 1) {kop.name}({", ".join(sig)}) {{
+    uint32_t dyn_smem;
+    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn_smem));
+    if (blockDim.x != {TC_THREADS} || blockDim.y != 1 || blockDim.z != 1 || dyn_smem < SMEM_BYTES ||
+        emmy::cluster_nctarank() != 2u || (gridDim.x & 1u)) {{
+        if (threadIdx.x == 0 && threadIdx.y == 0 && threadIdx.z == 0) atomicOr(&emmy_status, EMMY_STATUS_BAD_LAUNCH);
+        return;
+    }}
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + STAGES * A_STAGE;
+    uint64_t *full = reinterpret_cast<uint64_t *>(sB + STAGES * B_STAGE);
+    uint64_t *empty = full + STAGES;
+    uint64_t *tfull = empty + STAGES;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *drain = tempty + 2;
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile uint32_t *abort_flag = tmem_holder + 1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = emmy::cluster_ctarank();
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {{
+        for (int s = 0; s < STAGES; ++s) {{ emmy::mbar_init(&full[s], 1); emmy::mbar_init(&empty[s], 1); }}
+        for (int a = 0; a < 2; ++a) {{ emmy::mbar_init(&tfull[a], 1); emmy::mbar_init(&tempty[a], 8); }}
+        emmy::mbar_init(drain, 1);
+        *abort_flag = 0u;
+        emmy::fence_barrier_init();
+    }}
+    if (warp == 1) {{
+        emmy::tmem_alloc_pair(tmem_holder, 512);
+        emmy::tmem_relinquish_pair();
+    }}
+    if (warp == 0 && lane == 0) {{
+        emmy::tma_prefetch(&tm_a);
+        emmy::tma_prefetch(&tm_b);
+    }}
+    emmy::tc_fence_before();
+    __syncthreads();
+    emmy::cluster_sync();  // the peer signals the leader's barriers only after both are initialised
+    emmy::tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    if (warp == 0) {{
+        if (lane == 0) {{
+            // ---------------- TMA producer (both CTAs; completion counted on the leader's barrier)
+            uint32_t stage = 0, phase = 0;
+            uint32_t issued = 0u, parity_bits = 0u;
+            bool ok = true;
+            for (int t = pair; t < TILES && ok; t += npairs) {{
+                int tm, tn;
+                tile_coords(t, tm, tn);
+                for (int k = 0; k < KB; ++k) {{
+                    if (!emmy::mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, EMMY_STATUS_TIMEOUT_PRODUCER, WAIT_NS)) {{ ok = false; break; }}
+                    if (rank == 0) emmy::mbar_arrive_expect_tx(&full[stage], 2u * (A_STAGE + B_STAGE));
+                    const uint32_t fbar = emmy::mapa(&full[stage], 0);
+                    emmy::tma_load_2d_pair(sA + stage * A_STAGE, &tm_a, fbar, k * BK, tm * BM + (int)rank * CBM);
+{b_loads}
+                    if (rank == 0) {{
+                        issued |= 1u << stage;
+                        parity_bits = (parity_bits & ~(1u << stage)) | (phase << stage);
+                    }}
+                    if (++stage == STAGES) {{ stage = 0; phase ^= 1u; }}
+                }}
+            }}
+            if (!ok && rank == 0) {{
+                volatile uint32_t never = 0u;
+                for (int s = 0; s < STAGES; ++s)
+                    if (issued & (1u << s)) emmy::mbar_wait_cluster(&full[s], (parity_bits >> s) & 1u, &never, 0u, 20000000ull);
+            }}
+        }}
+        __syncwarp();
+    }} else if (warp == 1) {{
+        if (lane == 0) {{
+            if (rank == 0) {{
+                // ---------------- MMA issuer (leader CTA only)
+                uint32_t stage = 0, phase = 0, it = 0;
+                bool ok = true;
+                const uint32_t peer_empty0 = emmy::mapa(&empty[0], 1);
+                for (int t = pair; t < TILES && ok; t += npairs, ++it) {{
+                    const uint32_t acc = it & 1u, aphase = (it >> 1) & 1u;
+                    if (!emmy::mbar_wait_cluster(&tempty[acc], aphase ^ 1u, abort_flag, EMMY_STATUS_TIMEOUT_MMA, WAIT_NS)) break;
+                    emmy::tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + acc * BN;
+                    for (int k = 0; k < KB; ++k) {{
+                        if (!emmy::mbar_wait_cluster(&full[stage], phase, abort_flag, EMMY_STATUS_TIMEOUT_MMA, WAIT_NS)) {{ ok = false; break; }}
+                        emmy::tc_fence_after();
+                        const uint32_t a_base = emmy::smem_u32(sA + stage * A_STAGE);
+                        const uint32_t b_base = emmy::smem_u32(sB + stage * B_STAGE);
+                        #pragma unroll
+                        for (int kk = 0; kk < BK / 16; ++kk) {{
+                            const uint64_t ad = emmy::smem_desc_sw128(a_base + kk * 32, 16, 1024);
+{b_desc}
+                            emmy::umma_f16_pair(d_tmem, ad, bd, IDESC, (k | kk) != 0 ? 1u : 0u);
+                        }}
+                        emmy::umma_commit_pair(emmy::smem_u32(&empty[stage]));
+                        emmy::umma_commit_pair(peer_empty0 + stage * 8u);
+                        if (++stage == STAGES) {{ stage = 0; phase ^= 1u; }}
+                    }}
+                    if (!ok) break;
+                    emmy::umma_commit_pair(emmy::smem_u32(&tfull[acc]));
+                    emmy::umma_commit_pair(emmy::mapa(&tfull[acc], 1));
+                }}
+                // arrives on both CTAs once every pair MMA has finished
+                emmy::umma_commit_pair(emmy::smem_u32(drain));
+                emmy::umma_commit_pair(emmy::mapa(drain, 1));
+            }}
+        }}
+        __syncwarp();
+    }} else {{
+        // ---------------- epilogue (both CTAs): own 128 rows of the 256x256 tile
+        const int q = warp & 3;
+        const uint32_t leader_tempty0 = emmy::mapa(&tempty[0], 0);
+        uint32_t it = 0;
+        for (int t = pair; t < TILES; t += npairs, ++it) {{
+            const uint32_t acc = it & 1u, aphase = (it >> 1) & 1u;
+            if (!emmy::mbar_wait_cluster(&tfull[acc], aphase, abort_flag, EMMY_STATUS_TIMEOUT_EPILOGUE, WAIT_NS)) break;
+            emmy::tc_fence_after();
+            int tm, tn;
+            tile_coords(t, tm, tn);
+            const long long row = (long long)tm * BM + (int)rank * CBM + q * 32 + lane;
+            #pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {{
+                uint32_t r[32];
+                emmy::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + c * 32, r);
+                emmy::tmem_ld_wait();
+                const long long col0 = (long long)tn * BN + c * 32;
+                if (row < M && col0 + 32 <= N && {'true' if vec_store else 'false'}) {{
+                    {ocls} ov[32];
+                    #pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) {{
+{chr(10).join(epi_full)}
+                    }}
+{pack}                }} else if (row < M) {{
+                    #pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) {{
+                        if (col0 + jj < N) {{
+                            {ocls} ov1;
+{chr(10).join(epi_any)}
+                            {out_ptr}[row * N + col0 + jj] = ov1;
+                        }}
+                    }}
+                }}
+            }}
+            emmy::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) emmy::mbar_arrive_cluster(leader_tempty0 + acc * 8u);
+        }}
+    }}
+    emmy::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {{
+        // the last MMA, and the leader's last commit into this CTA, have landed (bounded)
+        if (lane == 0) {{
+            volatile uint32_t never = 0u;
+            emmy::mbar_wait_cluster(drain, 0u, &never, 0u, WAIT_NS);
+        }}
+        __syncwarp();
+    }}
+    emmy::cluster_sync();  // no CTA leaves while its peer may still signal or read it
+    if (warp == 1) {{
+        emmy::tc_fence_after();
+        emmy::tmem_dealloc_pair(tmem_base, 512);
+    }}
+}}
+"""
+    grid = max(2, min(tiles * 2, SM_COUNT) // 2 * 2)
+    launch = LaunchPlan(grid=(grid, 1, 1), block=(TC_THREADS, 1, 1), smem=smem, cluster=(2, 1, 1))
+    src += launch_record_source("gemm", launch, params, [tm_a, tm_b])
+    notes = {"kernel": "tcgen05_pair", "tile": [PAIR_BM, BN, BK], "stages": PAIR_STAGES, "tiles": tiles,
+             "b_layout": "NK" if plan.b_nk else "KN", "vector_store": vec_store, "cluster": 2}
+    return KernelSource(entry=kop.name, source=src, launch=launch, params=params, family="gemm",
+                        notes=notes, tmaps=[tm_a, tm_b])

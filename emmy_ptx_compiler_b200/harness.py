@@ -71,10 +71,10 @@ def from_device(t) -> np.ndarray:
 class DeviceCase:
     """A fixture compiled by our backend and loaded on ``device``."""
 
-    def __init__(self, case_dir, device: int = 0):
+    def __init__(self, case_dir, device: int = 0, options: dict | None = None):
         self.spec = load_case(case_dir)
         self.device = device
-        self.bundle = compiler.compile_bundle(self.spec.ir_path, want_cubin=True)
+        self.bundle = compiler.compile_bundle(self.spec.ir_path, want_cubin=True, options=options)
         self.module = runtime.Module(self.bundle["cubin"], self.spec.entry, device)
 
     def buffers(self, inputs: dict[str, np.ndarray]) -> dict:

@@ -716,6 +716,9 @@ def all_cases() -> list[Case]:
     cases.append(gemm_case("c5_gemm_256x512x512", 256, 512, 512))
     cases.append(gemm_case("c5_gemm_384x1024x768", 384, 1024, 768))
     cases.append(gemm_case("c5_gemm_200x136x300", 200, 136, 300))
+    # ragged CTA-pair tiles: last M tile holds 8 rows (its second CTA reads only
+    # out-of-bounds rows), last N tile 136 of 256 columns, 5 k-blocks
+    cases.append(gemm_case("c5_gemm_520x320x392", 520, 320, 392))
     cases.append(gemm_case("m_matmul_f32_17x33x19", 17, 33, 19, dtype=F32, epilogue=False))
     cases.append(gemm_case("m_matmul_f32_64x64x64", 64, 64, 64, dtype=F32, epilogue=False))
     cases.append(gemm_case("m_matmul_f32_bias_96x160x80", 96, 160, 80, dtype=F32))
