@@ -273,6 +273,9 @@ class Emitter:
         self.products: dict[str, tuple[str, str, int]] = {}
         self.fusable: set[str] | None = None
         self.order = 0
+        # C type of f32 values: "float", or "EmmyF2" when every value is a pair
+        # of adjacent cells computed with packed f32x2 instructions
+        self.ftype = "float"
 
     # -------------------------------------------------------------- small utils
     def emit(self, line: str) -> None:
@@ -290,7 +293,7 @@ class Emitter:
         key = f"{name}|{kind}"
         if key not in self.declared:
             var = cname(name) + ("" if kind == "f32" else "_" + kind)
-            cty = {"f32": "float", "int": "long long", "pred": "bool"}[kind]
+            cty = {"f32": self.ftype, "int": "long long", "pred": "bool"}[kind]
             self.emit(f"{cty} {var};")
             self.declared[key] = var
         return self.declared[key]
@@ -655,6 +658,7 @@ class Emitter:
         c.tmp = self.tmp + 1000
         c.fusable = self.fusable
         c.products = self.products
+        c.ftype = self.ftype
         return c
 
     @staticmethod
@@ -727,11 +731,11 @@ class Emitter:
             factors = (fargs[0], fargs[0])
         elif op in ("log", "log_fast") and fargs:
             lg = self.fresh("lg2")
-            self.emit(f"const float {lg} = emmy_lg2_approx({fargs[0]});")
+            self.emit(f"const {self.ftype} {lg} = emmy_lg2_approx({fargs[0]});")
             factors = (lg, LN2_F32)
         elif op == "silu" and fargs:
             sg = self.fresh("sig")
-            self.emit(f"const float {sg} = emmy_sigmoid_ref({fargs[0]});")
+            self.emit(f"const {self.ftype} {sg} = emmy_sigmoid_ref({fargs[0]});")
             factors = (fargs[0], sg)
         if factors is not None:
             self.assign(s.name, "f32", f"__fmul_rn({factors[0]}, {factors[1]})")
@@ -772,8 +776,11 @@ static __device__ __forceinline__ float emmy_rsqrt_approx(float x) {
     float y; asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x)); return y;
 }
 // tanh(x) = (2^(2x*log2e) - 1) / (2^(2x*log2e) + 1), compile.py:2142-2157.
+// The reference rounds (x*2)*log2e; x*(2*log2e) (0x4038AA3B) is the same
+// correctly rounded real product: doubling is exact, and where x*2 overflows
+// both forms give +-inf.
 static __device__ __forceinline__ float emmy_tanh_ref(float x) {
-    float e = emmy_ex2_approx(__fmul_rn(__fmul_rn(x, 2.0f), __uint_as_float(0x3FB8AA3Bu)));
+    float e = emmy_ex2_approx(__fmul_rn(x, __uint_as_float(0x4038AA3Bu)));
     return __fdiv_rn(__fsub_rn(e, 1.0f), __fadd_rn(e, 1.0f));
 }
 // sigmoid(x) = rcp(1 + 2^(-x*log2e)), compile.py:2158-2169.
@@ -789,6 +796,56 @@ static __device__ __forceinline__ float emmy_silu_ref(float x) {
 static __device__ __forceinline__ float emmy_leaky(float x, float slope) {
     float s = __fmul_rn(x, slope); return x > 0.0f ? x : s;
 }
+
+// Two adjacent cells in one value: add/sub/mul/fma go to the packed f32x2
+// instructions (each lane rounded exactly as the scalar .rn instruction), the
+// rest lane by lane.  a - b is computed as fma(b, -1, a): b*-1 is exact, so
+// the single rounding of a - b is the same.  A float operand is broadcast.
+struct EmmyF2 {
+    float2 v;
+    EmmyF2() = default;
+    __device__ __forceinline__ EmmyF2(float s) : v(make_float2(s, s)) {}
+    __device__ __forceinline__ EmmyF2(float2 p) : v(p) {}
+};
+#define EMMY_F2_LANES(f) make_float2(f(a.v.x), f(a.v.y))
+static __device__ __forceinline__ EmmyF2 operator-(EmmyF2 a) { return make_float2(-a.v.x, -a.v.y); }
+static __device__ __forceinline__ EmmyF2 __fadd_rn(EmmyF2 a, EmmyF2 b) { return __fadd2_rn(a.v, b.v); }
+static __device__ __forceinline__ EmmyF2 __fmul_rn(EmmyF2 a, EmmyF2 b) { return __fmul2_rn(a.v, b.v); }
+static __device__ __forceinline__ EmmyF2 __fmaf_rn(EmmyF2 a, EmmyF2 b, EmmyF2 c) {
+    return __ffma2_rn(a.v, b.v, c.v);
+}
+static __device__ __forceinline__ EmmyF2 __fsub_rn(EmmyF2 a, EmmyF2 b) {
+    return __ffma2_rn(b.v, make_float2(-1.0f, -1.0f), a.v);
+}
+static __device__ __forceinline__ EmmyF2 __fdiv_rn(EmmyF2 a, EmmyF2 b) {
+    return make_float2(__fdiv_rn(a.v.x, b.v.x), __fdiv_rn(a.v.y, b.v.y));
+}
+static __device__ __forceinline__ EmmyF2 fmaxf(EmmyF2 a, EmmyF2 b) {
+    return make_float2(fmaxf(a.v.x, b.v.x), fmaxf(a.v.y, b.v.y));
+}
+static __device__ __forceinline__ EmmyF2 fminf(EmmyF2 a, EmmyF2 b) {
+    return make_float2(fminf(a.v.x, b.v.x), fminf(a.v.y, b.v.y));
+}
+static __device__ __forceinline__ EmmyF2 __frcp_rn(EmmyF2 a) { return EMMY_F2_LANES(__frcp_rn); }
+static __device__ __forceinline__ EmmyF2 __fsqrt_rn(EmmyF2 a) { return EMMY_F2_LANES(__fsqrt_rn); }
+static __device__ __forceinline__ EmmyF2 fabsf(EmmyF2 a) { return EMMY_F2_LANES(fabsf); }
+static __device__ __forceinline__ EmmyF2 emmy_ex2_approx(EmmyF2 a) { return EMMY_F2_LANES(emmy_ex2_approx); }
+static __device__ __forceinline__ EmmyF2 emmy_lg2_approx(EmmyF2 a) { return EMMY_F2_LANES(emmy_lg2_approx); }
+static __device__ __forceinline__ EmmyF2 emmy_rsqrt_approx(EmmyF2 a) { return EMMY_F2_LANES(emmy_rsqrt_approx); }
+static __device__ __forceinline__ EmmyF2 emmy_tanh_ref(EmmyF2 x) {
+    const EmmyF2 e = emmy_ex2_approx(__fmul_rn(x, __uint_as_float(0x4038AA3Bu)));
+    return __fdiv_rn(__fsub_rn(e, 1.0f), __fadd_rn(e, 1.0f));
+}
+static __device__ __forceinline__ EmmyF2 emmy_sigmoid_ref(EmmyF2 x) {
+    const EmmyF2 e = emmy_ex2_approx(__fmul_rn(x, -__uint_as_float(0x3FB8AA3Bu)));
+    return __frcp_rn(__fadd_rn(1.0f, e));
+}
+static __device__ __forceinline__ EmmyF2 emmy_silu_ref(EmmyF2 x) { return __fmul_rn(x, emmy_sigmoid_ref(x)); }
+static __device__ __forceinline__ EmmyF2 emmy_leaky(EmmyF2 x, EmmyF2 slope) {
+    return make_float2(emmy_leaky(x.v.x, slope.v.x), emmy_leaky(x.v.y, slope.v.y));
+}
+#undef EMMY_F2_LANES
 """
 
 assert f32_bits(1.0 / math.log(2.0)) == 0x3FB8AA3B
+assert f32_bits(2.0 / math.log(2.0)) == 0x4038AA3B

@@ -54,7 +54,8 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
     """Classify ``kop`` into a family and generate its specialised source.
 
     ``options`` selects among equivalent schedules (results do not depend on
-    it): ``{"gemm_variant": "auto" | "pair" | "single"}``."""
+    it): ``{"gemm_variant": "auto" | "pair" | "single",
+    "pointwise_pair": "auto" | True | False}``."""
     meta = meta or {}
     options = options or {}
     written = {s.output for s in ir.walk(kop.body) if isinstance(s, ir.Write)}
@@ -73,7 +74,8 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
         return Lowered(ks, args, shapes, dtypes, meta)
     plan = pointwise.match(kop)
     if plan is not None:
-        ks = pointwise.generate(kop, plan, shapes, dtypes, args, scalars, written)
+        ks = pointwise.generate(kop, plan, shapes, dtypes, args, scalars, written,
+                                pair=options.get("pointwise_pair", "auto"))
         return Lowered(ks, args, shapes, dtypes, meta)
     kinds = sorted({type(s).__name__ for s in ir.walk(kop.body)})
     raise UnsupportedIR(f"KernelOp {kop.name!r} is not a pointwise, reduction or GEMM kernel "

@@ -50,6 +50,8 @@ struct Driver {
     EMMY_DRV(cuInit)
     EMMY_DRV(cuDeviceGetCount)
     EMMY_DRV(cuDeviceGet)
+    EMMY_DRV(cuDeviceGetAttribute)
+    EMMY_DRV(cuOccupancyMaxActiveBlocksPerMultiprocessor)
     EMMY_DRV(cuDevicePrimaryCtxRetain)
     EMMY_DRV(cuCtxSetCurrent)
     EMMY_DRV(cuCtxSynchronize)
@@ -112,6 +114,8 @@ int load_driver() {
     EMMY_GET(cuInit, true)
     EMMY_GET(cuDeviceGetCount, true)
     EMMY_GET(cuDeviceGet, true)
+    EMMY_GET(cuDeviceGetAttribute, true)
+    EMMY_GET(cuOccupancyMaxActiveBlocksPerMultiprocessor, true)
     EMMY_GET(cuDevicePrimaryCtxRetain, true)
     EMMY_GET(cuCtxSetCurrent, true)
     EMMY_GET(cuCtxSynchronize, true)
@@ -406,6 +410,28 @@ int emmy_load(int dev, const void *image, size_t len, const char *entry, emmy_mo
                 delete m;
                 return cu_fail(r, "cuFuncSetAttribute(max dynamic smem)");
             }
+        }
+        if (m->rec.flags & EMMY_LR_FILL_GRID) {
+            // grid = waves x (resident CTAs per SM for this build) x SMs, in whole quanta
+            CUdevice d = 0;
+            int nsm = 0, occ = 0;
+            const int threads = static_cast<int>(m->rec.block[0] * m->rec.block[1] * m->rec.block[2]);
+            r = g_drv.cuDeviceGet(&d, dev);
+            if (r == CUDA_SUCCESS) r = g_drv.cuDeviceGetAttribute(&nsm, CU_DEVICE_ATTRIBUTE_MULTIPROCESSOR_COUNT, d);
+            if (r == CUDA_SUCCESS)
+                r = g_drv.cuOccupancyMaxActiveBlocksPerMultiprocessor(&occ, m->fn, threads, m->rec.dyn_smem);
+            if (r != CUDA_SUCCESS) {
+                g_drv.cuModuleUnload(m->mod);
+                delete m;
+                return cu_fail(r, "sizing the grid from occupancy");
+            }
+            const uint64_t waves = m->rec.grid[0] ? m->rec.grid[0] : 1u;
+            const uint64_t q = m->rec.grid_quantum ? m->rec.grid_quantum : 1u;
+            uint64_t g = waves * static_cast<uint64_t>(occ > 0 ? occ : 1) * static_cast<uint64_t>(nsm > 0 ? nsm : 1);
+            g = g / q * q;
+            if (g == 0) g = q;
+            if (g > 0x7FFFFFFFu) g = 0x7FFFFFFFu / q * q;
+            m->rec.grid[0] = static_cast<uint32_t>(g);
         }
     }
     *out = m;

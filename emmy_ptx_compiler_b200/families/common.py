@@ -17,6 +17,12 @@ class LaunchPlan:
     block: tuple[int, int, int]
     smem: int = 0
     cluster: tuple[int, int, int] = (1, 1, 1)
+    # fill_waves > 0: the loader sets grid[0] = fill_waves x resident CTAs per SM
+    # x SMs (a multiple of grid_quantum); grid[0] here is the fallback estimate
+    fill_waves: int = 0
+    grid_quantum: int = 1
+
+FLAG_FILL_GRID = 0x100
 
 
 @dataclass
@@ -76,14 +82,18 @@ def launch_record_source(family: str, launch: LaunchPlan, params: list[ParamSpec
         tm_src.append("{0u, 0u, 0u, 0u, {0ull, 0ull, 0ull, 0ull, 0ull}, {0ull, 0ull, 0ull, 0ull}, "
                       "{0u, 0u, 0u, 0u, 0u}, 0u, {0u, 0u, 0u}}")
     g, b = launch.grid, launch.block
+    flags = int(launch.cluster[0])
+    if launch.fill_waves:
+        flags |= FLAG_FILL_GRID
+        g = (launch.fill_waves, g[1], g[2])
     return (
         "\n#include \"emmy_launch_record.h\"\n"
         "extern \"C\" __device__ unsigned int emmy_status = 0u;\n"
         "extern \"C\" __device__ const EmmyLaunchRecord emmy_launch_record = {\n"
-        f"    EMMY_LR_MAGIC, EMMY_LR_VERSION, {FAMILY_ID[family]}u, {int(launch.cluster[0])}u,\n"
+        f"    EMMY_LR_MAGIC, EMMY_LR_VERSION, {FAMILY_ID[family]}u, {flags}u,\n"
         f"    {{{g[0]}u, {g[1]}u, {g[2]}u}}, {{{b[0]}u, {b[1]}u, {b[2]}u}}, {launch.smem}u, {len(params)}u,\n"
         "    {" + ", ".join(f"{k}u" for k in kinds) + "},\n"
-        f"    {len(tmaps)}u, 0u,\n"
+        f"    {len(tmaps)}u, {max(1, int(launch.grid_quantum))}u,\n"
         "    {" + ",\n     ".join(tm_src) + "}\n"
         "};\n"
     )

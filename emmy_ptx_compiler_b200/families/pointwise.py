@@ -21,6 +21,9 @@ non-axis indices) takes the scalar grid-stride path with the same cell code.
 
 from __future__ import annotations
 
+import functools
+import math
+
 from dataclasses import dataclass, field
 
 from .. import ir
@@ -51,6 +54,7 @@ class PointwisePlan:
     ncells: int
     vector: bool
     reasons: list[str] = field(default_factory=list)
+    pair: bool = False  # f32x2 lane pairs in the register-vector path
 
 
 def _is_cell_body(body) -> bool:
@@ -169,9 +173,11 @@ def _streamed_loads(plan: PointwisePlan) -> list[ir.Load]:
 def generate(kop: ir.KernelOp, plan: PointwisePlan, shapes: dict, dtypes: dict, args: list[str],
              scalars: dict[str, str], written: set[str], *, variant: str = "auto",
              unroll: int = UNROLL, prefetch: int = PREFETCH, min_blocks: int = MIN_BLOCKS,
-             order: str = ORDER, hoist_broadcast: bool = True) -> KernelSource:
+             order: str = ORDER, hoist_broadcast: bool = True, pair="auto") -> KernelSource:
     """``variant``: "auto"/"vector" (register vectors), or "bulk" (shared-memory
-    ring fed by bulk async copies)."""
+    ring fed by bulk async copies).  ``pair``: compute the cell body on two
+    adjacent cells at once with packed f32x2 add/mul/fma ("auto": whenever the
+    body is pure f32 arithmetic, see ``pairable``)."""
     vec_ok, why = vector_eligible(plan, shapes, dtypes)
     plan.vector = vec_ok
     plan.reasons = why
@@ -199,6 +205,9 @@ def generate(kop: ir.KernelOp, plan: PointwisePlan, shapes: dict, dtypes: dict, 
         params.append(ParamSpec(name, "ptr", dt))
     ncell = plan.ncells
     axes = plan.axes
+    use_pair = vec_ok and (pair is True or (pair == "auto" and pairable(plan, dtypes)))
+    plan.pair = use_pair
+    vtrip = functools.partial(_vector_trip, pair=use_pair)
     lines: list[str] = []
     w = lines.append
     w(DEVICE_PRELUDE)
@@ -212,9 +221,11 @@ def generate(kop: ir.KernelOp, plan: PointwisePlan, shapes: dict, dtypes: dict, 
                          ("int", f"(long long)p_{_c(name)}")) for name in scalars}
     if vec_ok:
         align_terms = [f"(uintptr_t)p_{_c(n)}" for n in ptrs]
-        w("    const bool aligned = ((" + (" | ".join(align_terms) if align_terms else "0") + ") & 15u) == 0;")
+        idx32 = order != "blocked" and ncell < (1 << 31)
+        w("    const bool aligned = ((" + (" | ".join(align_terms) if align_terms else "0") + ") & 15u) == 0"
+          + (" && gstride <= (1LL << 27);" if idx32 else ";"))
         w("    if (aligned) {")
-        w(f"        constexpr long long NVEC = NCELL / {VEC};")
+        w(f"        constexpr {'unsigned' if idx32 else 'long long'} NVEC = NCELL / {VEC};")
         if order == "blocked":
             # CTA b owns vectors [b*per, (b+1)*per); a trip covers unroll*blockDim consecutive vectors
             w("        const long long per = (NVEC + gridDim.x - 1) / gridDim.x;")
@@ -223,76 +234,82 @@ def generate(kop: ir.KernelOp, plan: PointwisePlan, shapes: dict, dtypes: dict, 
             w("        const long long bstride = blockDim.x;")
             w("        long long v = vbeg + threadIdx.x;")
             w(f"        for (; v + {unroll - 1} * bstride < vend; v += {unroll} * bstride) {{")
-            lines.extend(_vector_trip(plan, shapes, dtypes, ptrs, scalar_env,
+            lines.extend(vtrip(plan, shapes, dtypes, ptrs, scalar_env,
                                       ["v"] + [f"v + {u} * bstride" for u in range(1, unroll)],
                                       "            "))
             w("        }")
             w("        for (; v < vend; v += bstride) {")
-            lines.extend(_vector_trip(plan, shapes, dtypes, ptrs, scalar_env, ["v"], "            "))
+            lines.extend(vtrip(plan, shapes, dtypes, ptrs, scalar_env, ["v"], "            "))
             w("        }")
             w("        return;")
             w("    }")
             return _finish_vector(kop, plan, lines, ncell, unroll, vec_ok, params, why, em_path=True,
                                   shapes=shapes, dtypes=dtypes, ptrs=ptrs, scalar_env=scalar_env)
-        w("        long long v = gtid;")
+        quantum = 1  # grid multiple that keeps hoisted broadcast operands valid
+        # vector offsets in 32 bits when they stay below 2^32: c < NCELL + 4*unroll*gstride
+        ity, isuf = ("unsigned", "u") if idx32 else ("long long", "LL")
+        w(f"        {ity} v = ({ity})gtid;")
+        w(f"        const {ity} vgs = ({ity})gstride;")
         hoist = _hoistable(plan) if hoist_broadcast else {}
         if hoist:
             period = max(p for _, p in hoist.values())
+            if period % VEC == 0:
+                q = (period // VEC) // math.gcd(period // VEC, BLOCK)
+                quantum = q if q <= SM_COUNT else 1
             # a thread's broadcast operands are the same on every trip when the grid
             # stride is a whole number of their periods: load them once
             w(f"        if ((gstride * {VEC}) % {period}LL == 0 && v < NVEC) {{")
             names = {}
-            w("            const long long hc = v * %dLL;" % VEC)
+            w(f"            const {ity} hc = v * {VEC}{isuf};")
             strides = _axis_strides(axes)
             for i, ((name, ext), st) in enumerate(zip(axes, strides)):
-                q = "hc" if st == 1 else f"(hc / {st}LL)"
-                expr = q if i == 0 else f"({q} % {ext}LL)"
-                w(f"            const long long h_ax{i} = {expr};")
-            loads_all = [t for t in ir.walk(plan.tile.body) if isinstance(t, ir.Load)]
+                q = "hc" if st == 1 else f"(hc / {st}{isuf})"
+                expr = q if i == 0 else f"({q} % {ext}{isuf})"
+                w(f"            const {ity} h_ax{i} = {expr};")
             for li, (ld, _) in hoist.items():
                 dt = ir.canon_dtype(ld.dtype or dtypes.get(ld.input))
                 pos = _axis_aligned(ld.index, axes)
                 bstr = _axis_strides([axes[p_] for p_ in pos])
-                off = " + ".join(f"h_ax{p_} * {bs}LL" for p_, bs in zip(pos, bstr))
+                off = " + ".join(f"h_ax{p_} * {bs}{isuf}" for p_, bs in zip(pos, bstr))
                 var = f"hl{li}"
                 if _contiguous(ld, plan):
                     w(f"            const auto {var} = emmy_ld{VEC}_{dt}({ptrs[ld.input]} + ({off}), false);")
                 else:
                     w(f"            const {ctype(dt)} {var} = {ptrs[ld.input]}[{off}];")
                 names[li] = var
-            del loads_all
-            w(f"            for (; v + {unroll - 1} * gstride < NVEC; v += {unroll} * gstride) {{")
-            lines.extend(_vector_trip(plan, shapes, dtypes, ptrs, scalar_env,
-                                      ["v"] + [f"v + {u} * gstride" for u in range(1, unroll)],
-                                      "                ", hoisted=names))
+            w(f"            for (; v + {unroll - 1} * vgs < NVEC; v += {unroll} * vgs) {{")
+            lines.extend(vtrip(plan, shapes, dtypes, ptrs, scalar_env,
+                               ["v"] + [f"v + {u} * vgs" for u in range(1, unroll)],
+                               "                ", hoisted=names, ix=(ity, isuf)))
             w("            }")
-            w("            if (v < NVEC) {")
-            lines.extend(_vector_trip(plan, shapes, dtypes, ptrs, scalar_env, ["v"], "                ",
-                                      hoisted=names))
+            w("            for (; v < NVEC; v += vgs) {")
+            lines.extend(vtrip(plan, shapes, dtypes, ptrs, scalar_env, ["v"], "                ",
+                               hoisted=names, ix=(ity, isuf)))
             w("            }")
             w("            return;")
             w("        }")
-        w(f"        for (; v + {unroll - 1} * gstride < NVEC; v += {unroll} * gstride) {{")
+        w(f"        for (; v + {unroll - 1} * vgs < NVEC; v += {unroll} * vgs) {{")
         if prefetch:
             for s_ in _streamed_loads(plan):
                 for u in range(unroll):
-                    w(f"            {{ const long long pv = v + {prefetch * unroll + u} * gstride;")
+                    w(f"            {{ const {ity} pv = v + {prefetch * unroll + u} * vgs;")
                     w(f"              if (pv < NVEC) emmy_prefetch_l2({ptrs[s_.input]} + pv * {VEC}); }}")
-        lines.extend(_vector_trip(plan, shapes, dtypes, ptrs, scalar_env,
-                                  ["v"] + [f"v + {u} * gstride" for u in range(1, unroll)],
-                                  "            "))
+        lines.extend(vtrip(plan, shapes, dtypes, ptrs, scalar_env,
+                           ["v"] + [f"v + {u} * vgs" for u in range(1, unroll)],
+                           "            ", ix=(ity, isuf)))
         w("        }")
-        w("        if (v < NVEC) {")
-        lines.extend(_vector_trip(plan, shapes, dtypes, ptrs, scalar_env, ["v"], "            "))
+        w("        for (; v < NVEC; v += vgs) {")
+        lines.extend(vtrip(plan, shapes, dtypes, ptrs, scalar_env, ["v"], "            ", ix=(ity, isuf)))
         w("        }")
         w("        return;")
         w("    }")
     return _finish_vector(kop, plan, lines, ncell, unroll, vec_ok, params, why, em_path=True,
-                          shapes=shapes, dtypes=dtypes, ptrs=ptrs, scalar_env=scalar_env)
+                          shapes=shapes, dtypes=dtypes, ptrs=ptrs, scalar_env=scalar_env,
+                          grid_quantum=quantum if vec_ok else 1)
 
 
 def _finish_vector(kop, plan, lines, ncell, unroll, vec_ok, params, why, *, em_path, shapes, dtypes, ptrs,
-                   scalar_env) -> KernelSource:
+                   scalar_env, grid_quantum: int = 1) -> KernelSource:
     """The scalar grid-stride loop (any launch, any alignment) and the launch record."""
     w = lines.append
     w("    for (long long cell = gtid; cell < NCELL; cell += gstride) {")
@@ -305,12 +322,20 @@ def _finish_vector(kop, plan, lines, ncell, unroll, vec_ok, params, why, *, em_p
     w("}")
     nvec = ncell // VEC if vec_ok else ncell
     per_block = BLOCK * (unroll if vec_ok else 1)
-    grid = max(1, min((nvec + per_block - 1) // per_block, SM_COUNT * 8))
+    want = (nvec + per_block - 1) // per_block
+    grid = max(1, min(want, SM_COUNT * 8))
     launch = LaunchPlan(grid=(grid, 1, 1), block=(BLOCK, 1, 1), smem=0)
+    if want >= SM_COUNT * 8:
+        # enough work to fill the device: one wave of exactly the CTAs that fit,
+        # counted by the loader for this build's registers (a partial second wave
+        # of a fixed grid leaves SMs idle in a bandwidth-bound loop)
+        launch.fill_waves = 1
+        launch.grid_quantum = grid_quantum
     lines.append(launch_record_source("pointwise", launch, params))
     return KernelSource(entry=kop.name, source="\n".join(lines), launch=launch, params=params,
                         family="pointwise",
-                        notes={"vector": vec_ok, "scalar_reasons": why, "ncells": ncell})
+                        notes={"vector": vec_ok, "scalar_reasons": why, "ncells": ncell,
+                               "pair": plan.pair})
 
 
 def _c(name: str) -> str:
@@ -320,7 +345,8 @@ def _c(name: str) -> str:
 
 def _vector_trip(plan: PointwisePlan, shapes, dtypes, ptrs, scalar_env, vexprs: list[str],
                  ind: str, smem_src: dict[int, str] | None = None,
-                 hoisted: dict[int, str] | None = None) -> list[str]:
+                 hoisted: dict[int, str] | None = None, pair: bool = False,
+                 ix: tuple[str, str] = ("long long", "LL")) -> list[str]:
     """One trip: load U vectors of every input, run the cell body per lane,
     store U vectors of every output.  ``smem_src`` maps a load's position to a
     shared-memory element pointer expression (indexed by the vector's offset
@@ -332,14 +358,15 @@ def _vector_trip(plan: PointwisePlan, shapes, dtypes, ptrs, scalar_env, vexprs: 
     loads = [s for s in ir.walk(plan.tile.body) if isinstance(s, ir.Load)]
     writes = [s for s in ir.walk(plan.tile.body) if isinstance(s, ir.Write)]
     strides = _axis_strides(axes)
+    ity, isuf = ix
     for u, vx in enumerate(vexprs):
-        out.append(f"{ind}const long long c{u} = ({vx}) * {VEC}LL;")
+        out.append(f"{ind}const {ity} c{u} = ({vx}) * {VEC}{isuf};")
         for i, ((name, ext), st) in enumerate(zip(axes, strides)):
-            q = f"c{u}" if st == 1 else f"(c{u} / {st}LL)"
-            expr = q if i == 0 else f"({q} % {ext}LL)"
+            q = f"c{u}" if st == 1 else f"(c{u} / {st}{isuf})"
+            expr = q if i == 0 else f"({q} % {ext}{isuf})"
             if ext == 1:
-                expr = "0LL"
-            out.append(f"{ind}const long long u{u}_ax{i} = {expr};")
+                expr = f"0{isuf}"
+            out.append(f"{ind}const {ity} u{u}_ax{i} = {expr};")
     # fetch every load for every trip vector before any compute
     fetched: dict[tuple[int, int], tuple[str, bool, str]] = {}
     for li, s in enumerate(loads):
@@ -362,7 +389,9 @@ def _vector_trip(plan: PointwisePlan, shapes, dtypes, ptrs, scalar_env, vexprs: 
                 continue
             pos = _axis_aligned(s.index, axes)
             bstrides = _axis_strides([axes[p] for p in pos])
-            off = " + ".join(f"u{u}_ax{p} * {bs}LL" for p, bs in zip(pos, bstrides)) or "0LL"
+            off = " + ".join(f"u{u}_ax{p} * {bs}{isuf}" for p, bs in zip(pos, bstrides)) or f"0{isuf}"
+            if pos == list(range(len(axes))):
+                off = f"c{u}"  # the whole tile, row-major: the cell offset itself
             contiguous = bool(pos) and pos[-1] == len(axes) - 1
             if contiguous:
                 out.append(f"{ind}const auto {var} = emmy_ld{VEC}_{dt}({ptr} + ({off}), "
@@ -378,7 +407,9 @@ def _vector_trip(plan: PointwisePlan, shapes, dtypes, ptrs, scalar_env, vexprs: 
             outs[(wi, u)] = [f"st{wi}_{u}_{lane}" for lane in range(VEC)]
             for lane in range(VEC):
                 out.append(f"{ind}{ctype(dt)} st{wi}_{u}_{lane};")
-    for u in range(len(vexprs)):
+    if pair:
+        out.extend(_pair_lanes(plan, shapes, dtypes, ptrs, scalar_env, vexprs, ind, fetched, loads, writes))
+    for u in range(len(vexprs) if not pair else 0):
         for lane in range(VEC):
             load_idx = {id(s): li for li, s in enumerate(loads)}
             write_idx = {id(s): wi for wi, s in enumerate(writes)}
@@ -408,6 +439,80 @@ def _vector_trip(plan: PointwisePlan, shapes, dtypes, ptrs, scalar_env, vexprs: 
             vals = ", ".join(outs[(wi, u)])
             out.append(f"{ind}emmy_st{VEC}_{dt}({ptrs[s.output]} + c{u}, {vals});")
     return out
+
+
+def _pair_lanes(plan, shapes, dtypes, ptrs, scalar_env, vexprs, ind, fetched, loads, writes) -> list[str]:
+    """The cell body once per pair of adjacent lanes (0,1), (2,3) of each trip
+    vector, every f32 value an ``EmmyF2``."""
+    out: list[str] = []
+    load_idx = {id(s): li for li, s in enumerate(loads)}
+    write_idx = {id(s): wi for wi, s in enumerate(writes)}
+    for u in range(len(vexprs)):
+        for l0 in range(0, VEC, 2):
+            l1 = l0 + 1
+
+            def load_hook(s, k, u=u, l0=l0, l1=l1):
+                var, is_vec, dt = fetched[(load_idx[id(s)], u)]
+                if not is_vec:
+                    return "f32", f"EmmyF2({load_to_kind(var, dt)[1]})"
+                a = load_to_kind(f"{var}.v[{l0}]", dt)[1]
+                b = load_to_kind(f"{var}.v[{l1}]", dt)[1]
+                return "f32", f"EmmyF2(make_float2({a}, {b}))"
+
+            def write_hook(s, k, kind, code, u=u, l0=l0, l1=l1):
+                dt = ir.canon_dtype(s.value_dtype or dtypes.get(s.output))
+                wi = write_idx[id(s)]
+                return (f"{{ const EmmyF2 w_ = {code}; st{wi}_{u}_{l0} = {store_from('f32', 'w_.v.x', dt)}; "
+                        f"st{wi}_{u}_{l1} = {store_from('f32', 'w_.v.y', dt)}; }}")
+
+            em = Emitter(shapes, dtypes, ptrs, load_hook=load_hook, write_hook=write_hook,
+                         indent=ind + "    ")
+            em.ftype = "EmmyF2"
+            em.env.update(scalar_env)
+            em.run(plan.tile.body)
+            out.append(f"{ind}{{")
+            out.extend(em.lines)
+            out.append(f"{ind}}}")
+    return out
+
+
+PAIR_OPS = {"add", "sum", "subtract", "sub", "multiply", "mul", "divide", "true_divide", "div",
+            "maximum", "amax", "max", "minimum", "amin", "min", "exp2", "exp", "exp_fast", "sqrt",
+            "rsqrt", "reciprocal", "recip", "square", "clamp", "clip", "relu", "leaky_relu", "neg",
+            "negative", "abs", "absolute", "copy", "log", "log_fast", "log2", "lg2", "tanh",
+            "sigmoid", "silu", "pow"}
+
+
+def pairable(plan: PointwisePlan, dtypes: dict) -> bool:
+    """True when the cell body is straight-line f32 arithmetic that reads no
+    axis value: loads, float literals, ops of ``PAIR_OPS`` and plain writes.
+    Such a body computes two adjacent cells independently in the two lanes
+    of an ``EmmyF2`` with the same per-lane rounding."""
+    axis_names = {a for a, _ in plan.axes}
+    for s in ir.walk(plan.tile.body):
+        if isinstance(s, ir.Load):
+            if ir.canon_dtype(s.dtype or dtypes.get(s.input)) not in ("f32", "bf16", "f16"):
+                return False
+        elif isinstance(s, ir.Write):
+            if s.atomic or ir.canon_dtype(s.value_dtype or dtypes.get(s.output)) not in ("f32", "bf16", "f16"):
+                return False
+            if any(not isinstance(v, str) for v in s.values):
+                return False
+        elif isinstance(s, ir.Let):
+            if not (isinstance(s.value, ir.Literal) and isinstance(s.value.value, float)):
+                return False
+        elif isinstance(s, ir.Assign):
+            if ir.op_name(s.op) not in PAIR_OPS:
+                return False
+            if s.dtype is not None and ir.canon_dtype(s.dtype) != "f32":
+                return False
+            if any(isinstance(a, str) and a in axis_names for a in s.args):
+                return False
+            if any(not isinstance(a, str) for a in s.args):
+                return False
+        else:
+            return False
+    return True
 
 
 def _contiguous(s: ir.Load, plan: PointwisePlan) -> bool:

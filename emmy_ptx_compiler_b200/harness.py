@@ -176,7 +176,8 @@ def main(argv=None) -> int:
     st = case.module.status()
     print(json.dumps({"case": case.spec.meta.get("id"), "family": case.module.family,
                       "ms_per_launch": e0.elapsed_time(e1) / ns.iters, "status": st,
-                      "launch": case.bundle["launch"]}))
+                      "launch": {"grid": list(case.module.grid), "block": list(case.module.block),
+                                 "smem": case.module.smem}}))
     case.module.close()
     return 1 if st else 0
 

@@ -45,6 +45,13 @@ enum EmmyParamKind { EMMY_PARAM_PTR = 0, EMMY_PARAM_F32 = 1, EMMY_PARAM_I32 = 2 
 #define EMMY_STATUS_TMEM_ALLOC 0x10u      /* tensor-memory allocation did not fit */
 #define EMMY_STATUS_TIMEOUT_REDUCE 0x20u  /* cross-block combine waited too long */
 
+/* flags: bits 0-7 cluster size (0/1 = no cluster); EMMY_LR_FILL_GRID asks the
+ * loader to size grid[0] from the kernel's occupancy on the device it is
+ * loaded on: grid[0] = waves x resident CTAs per SM x SM count, rounded down
+ * to a multiple of grid_quantum.  In the record as emitted, grid[0] holds the
+ * number of waves; emmy_module_info reports the resolved grid. */
+#define EMMY_LR_FILL_GRID 0x100u
+
 typedef struct EmmyTmapSpec {
     uint32_t src_param; /* index into arg_order of the global buffer */
     uint32_t dtype;     /* CUtensorMapDataType */
@@ -68,7 +75,7 @@ typedef struct EmmyLaunchRecord {
     uint32_t nparams;
     uint32_t param_kind[EMMY_LR_MAX_PARAMS];
     uint32_t ntmaps;
-    uint32_t reserved;
+    uint32_t grid_quantum; /* with EMMY_LR_FILL_GRID: grid[0] is a multiple of this (0 = 1) */
     EmmyTmapSpec tmaps[EMMY_LR_MAX_TMAPS];
 } EmmyLaunchRecord;
 
