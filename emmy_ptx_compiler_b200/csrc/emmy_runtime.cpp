@@ -73,6 +73,9 @@ struct Driver {
     EMMY_DRV(cuMemcpyDtoHAsync)
     EMMY_DRV(cuMemsetD8Async)
     EMMY_DRV(cuStreamQuery)
+    EMMY_DRV(cuStreamCreate)
+    EMMY_DRV(cuStreamDestroy)
+    EMMY_DRV(cuStreamWaitEvent)
     EMMY_DRV(cuStreamSynchronize)
     EMMY_DRV(cuEventCreate)
     EMMY_DRV(cuEventRecord)
@@ -137,6 +140,9 @@ int load_driver() {
     EMMY_GET(cuMemcpyDtoHAsync, true)
     EMMY_GET(cuMemsetD8Async, true)
     EMMY_GET(cuStreamQuery, true)
+    EMMY_GET(cuStreamCreate, true)
+    EMMY_GET(cuStreamDestroy, true)
+    EMMY_GET(cuStreamWaitEvent, true)
     EMMY_GET(cuStreamSynchronize, true)
     EMMY_GET(cuEventCreate, true)
     EMMY_GET(cuEventRecord, true)
@@ -189,6 +195,10 @@ struct emmy_module {
     // emmy_run_host device buffers
     std::vector<CUdeviceptr> dbuf;
     std::vector<size_t> dbuf_bytes;
+    // emmy_run_host chunk pipeline: copy-in and copy-out streams, one event pair per chunk
+    CUstream h2d = nullptr, d2h = nullptr;
+    std::vector<CUevent> ev_in, ev_out;
+    CUevent ev_whole = nullptr, ev_start = nullptr;
 };
 
 namespace {
@@ -226,8 +236,10 @@ int encode_tmaps(emmy_module *m, const uint64_t *args, int nargs) {
     return EMMY_OK;
 }
 
+bool has_range(const emmy_module *m) { return m->has_rec && (m->rec.flags & EMMY_LR_RANGE); }
+
 int launch_locked(emmy_module *m, const uint64_t *args, int nargs, const uint32_t *grid,
-                  const uint32_t *block, uint64_t stream) {
+                  const uint32_t *block, uint64_t stream, uint64_t rbegin = 0, uint64_t rend = ~0ull) {
     int rc = set_device(m->dev);
     if (rc) return rc;
     uint32_t g[3], b[3], smem = 0;
@@ -250,7 +262,18 @@ int launch_locked(emmy_module *m, const uint64_t *args, int nargs, const uint32_
         return fail(EMMY_ERR_INVALID, "entry takes %u parameters, got %d", m->rec.nparams, nargs);
     if ((rc = encode_tmaps(m, args, nargs))) return rc;
     const size_t ntm = m->has_rec ? m->rec.ntmaps : 0;
-    std::vector<void *> kp(static_cast<size_t>(nargs) + ntm);
+    const bool ranged = has_range(m);
+    uint64_t range[2] = {rbegin, rend == ~0ull && ranged ? m->rec.range_total : rend};
+    if (ranged) {
+        const uint64_t al = m->rec.range_align ? m->rec.range_align : 1;
+        if (range[0] > range[1] || range[1] > m->rec.range_total || range[0] % al ||
+            (range[1] % al && range[1] != m->rec.range_total))
+            return fail(EMMY_ERR_INVALID, "unit range [%llu, %llu) is not within [0, %llu) in steps of %llu",
+                        (unsigned long long)range[0], (unsigned long long)range[1],
+                        (unsigned long long)m->rec.range_total, (unsigned long long)al);
+        if (range[0] == range[1]) return EMMY_OK;
+    }
+    std::vector<void *> kp(static_cast<size_t>(nargs) + ntm + (ranged ? 2 : 0));
     std::vector<uint32_t> narrow(static_cast<size_t>(nargs));
     for (int i = 0; i < nargs; ++i) {
         size_t sz = 8;
@@ -266,6 +289,10 @@ int launch_locked(emmy_module *m, const uint64_t *args, int nargs, const uint32_
         }
     }
     for (size_t i = 0; i < ntm; ++i) kp[static_cast<size_t>(nargs) + i] = &m->tmaps[i];
+    if (ranged) {
+        kp[static_cast<size_t>(nargs) + ntm] = &range[0];
+        kp[static_cast<size_t>(nargs) + ntm + 1] = &range[1];
+    }
     const bool cluster = m->has_rec && (m->rec.flags & 0xFFu) > 1u;
     if (cluster) {
         if (!g_drv.cuLaunchKernelEx) return fail(EMMY_ERR_NO_DRIVER, "driver lacks cuLaunchKernelEx");
@@ -395,7 +422,7 @@ int emmy_load(int dev, const void *image, size_t len, const char *entry, emmy_mo
         }
     }
     if (m->has_rec) {
-        const size_t want = m->rec.nparams + m->rec.ntmaps;
+        const size_t want = m->rec.nparams + m->rec.ntmaps + ((m->rec.flags & EMMY_LR_RANGE) ? 2 : 0);
         if (!m->param_size.empty() && m->param_size.size() != want) {
             g_drv.cuModuleUnload(m->mod);
             delete m;
@@ -445,6 +472,12 @@ int emmy_unload(emmy_module_t m) {
     if (rc) return rc;
     for (CUdeviceptr p : m->dbuf)
         if (p) g_drv.cuMemFree(p);
+    for (CUevent e : m->ev_in) g_drv.cuEventDestroy(e);
+    for (CUevent e : m->ev_out) g_drv.cuEventDestroy(e);
+    if (m->ev_whole) g_drv.cuEventDestroy(m->ev_whole);
+    if (m->ev_start) g_drv.cuEventDestroy(m->ev_start);
+    if (m->h2d) g_drv.cuStreamDestroy(m->h2d);
+    if (m->d2h) g_drv.cuStreamDestroy(m->d2h);
     CUresult r = g_drv.cuModuleUnload(m->mod);
     delete m;
     if (r != CUDA_SUCCESS) return cu_fail(r, "cuModuleUnload");
@@ -570,6 +603,41 @@ int emmy_host_free(void *ptr) {
     return EMMY_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+bool is_in(uint8_t r) { return r == EMMY_ROLE_IN || r == EMMY_ROLE_INOUT; }
+bool is_out(uint8_t r) { return r == EMMY_ROLE_OUT || r == EMMY_ROLE_INOUT || r == EMMY_ROLE_OUT_ZEROED; }
+
+// Bytes [lo, hi) of parameter i's unit range, clipped to the caller's buffer.
+void unit_bytes(const emmy_module *m, int i, uint64_t b, uint64_t e, size_t have, size_t *lo, size_t *hi) {
+    const uint64_t per = m->rec.range_bytes[i];
+    *lo = static_cast<size_t>(std::min<uint64_t>(b * per, have));
+    *hi = static_cast<size_t>(std::min<uint64_t>(e * per, have));
+}
+
+int ensure_pipeline(emmy_module *m, size_t nchunks) {
+    if (!m->h2d) CU(g_drv.cuStreamCreate(&m->h2d, CU_STREAM_NON_BLOCKING), "cuStreamCreate");
+    if (!m->d2h) CU(g_drv.cuStreamCreate(&m->d2h, CU_STREAM_NON_BLOCKING), "cuStreamCreate");
+    if (!m->ev_whole) CU(g_drv.cuEventCreate(&m->ev_whole, CU_EVENT_DISABLE_TIMING), "cuEventCreate");
+    if (!m->ev_start) CU(g_drv.cuEventCreate(&m->ev_start, CU_EVENT_DISABLE_TIMING), "cuEventCreate");
+    while (m->ev_in.size() < nchunks) {
+        CUevent a, b;
+        CU(g_drv.cuEventCreate(&a, CU_EVENT_DISABLE_TIMING), "cuEventCreate");
+        CU(g_drv.cuEventCreate(&b, CU_EVENT_DISABLE_TIMING), "cuEventCreate");
+        m->ev_in.push_back(a);
+        m->ev_out.push_back(b);
+    }
+    return EMMY_OK;
+}
+
+constexpr uint64_t kChunkBytes = 32ull << 20;  // streamed bytes per pipeline chunk (in + out)
+
+}  // namespace
+
+extern "C" {
+
 int emmy_run_host(emmy_module_t m, void *const *host_ptrs, const size_t *bytes, const uint8_t *roles,
                   int nargs, uint64_t stream) {
     if (!m || (nargs > 0 && (!host_ptrs || !bytes || !roles)))
@@ -583,6 +651,7 @@ int emmy_run_host(emmy_module_t m, void *const *host_ptrs, const size_t *bytes, 
         m->dbuf_bytes.resize(nargs, 0);
     }
     std::vector<uint64_t> args(nargs);
+    uint64_t streamed = 0;
     for (int i = 0; i < nargs; ++i) {
         if (roles[i] == EMMY_ROLE_SCALAR) {
             uint32_t v = 0;
@@ -598,17 +667,97 @@ int emmy_run_host(emmy_module_t m, void *const *host_ptrs, const size_t *bytes, 
             m->dbuf_bytes[i] = bytes[i];
         }
         args[i] = m->dbuf[i];
-        if (roles[i] == EMMY_ROLE_IN || roles[i] == EMMY_ROLE_INOUT)
-            CU(g_drv.cuMemcpyHtoDAsync(m->dbuf[i], host_ptrs[i], bytes[i], s), "cuMemcpyHtoDAsync");
-        else if (roles[i] == EMMY_ROLE_OUT_ZEROED)
+        if (has_range(m) && i < EMMY_LR_MAX_PARAMS && m->rec.range_bytes[i]) streamed += bytes[i];
+    }
+    const uint64_t total = has_range(m) ? m->rec.range_total : 0;
+    const uint64_t align = has_range(m) && m->rec.range_align ? m->rec.range_align : 1;
+    if (total < 2 * align || streamed < 2 * kChunkBytes) {
+        // one launch: copy in, launch, copy out, all on `stream`
+        for (int i = 0; i < nargs; ++i) {
+            if (roles[i] == EMMY_ROLE_SCALAR) continue;
+            if (is_in(roles[i]))
+                CU(g_drv.cuMemcpyHtoDAsync(m->dbuf[i], host_ptrs[i], bytes[i], s), "cuMemcpyHtoDAsync");
+            else if (roles[i] == EMMY_ROLE_OUT_ZEROED)
+                CU(g_drv.cuMemsetD8Async(m->dbuf[i], 0, bytes[i], s), "cuMemsetD8Async");
+        }
+        if ((rc = launch_locked(m, args.data(), nargs, nullptr, nullptr, stream))) return rc;
+        for (int i = 0; i < nargs; ++i)
+            if (roles[i] != EMMY_ROLE_SCALAR && is_out(roles[i]))
+                CU(g_drv.cuMemcpyDtoHAsync(host_ptrs[i], m->dbuf[i], bytes[i], s), "cuMemcpyDtoHAsync");
+        CU(g_drv.cuStreamSynchronize(s), "cuStreamSynchronize");
+        return EMMY_OK;
+    }
+    // Chunk pipeline: unit ranges [b, e) flow through copy-in (h2d stream), the
+    // kernel (`stream`) and copy-out (d2h stream), so chunk k's copy-in, chunk
+    // k-1's kernel and chunk k-2's copy-out overlap, and both host-link
+    // directions are busy at once.
+    uint64_t nchunks = std::max<uint64_t>(2, std::min<uint64_t>(64, streamed / kChunkBytes));
+    uint64_t per = (total + nchunks - 1) / nchunks;
+    per = (per + align - 1) / align * align;
+    nchunks = (total + per - 1) / per;
+    if ((rc = ensure_pipeline(m, nchunks))) return rc;
+    CU(g_drv.cuEventRecord(m->ev_start, s), "cuEventRecord");
+    CU(g_drv.cuStreamWaitEvent(m->h2d, m->ev_start, 0), "cuStreamWaitEvent");
+    CU(g_drv.cuStreamWaitEvent(m->d2h, m->ev_start, 0), "cuStreamWaitEvent");
+    for (int i = 0; i < nargs; ++i) {
+        if (roles[i] == EMMY_ROLE_SCALAR) continue;
+        if (is_in(roles[i]) && !m->rec.range_bytes[i])
+            CU(g_drv.cuMemcpyHtoDAsync(m->dbuf[i], host_ptrs[i], bytes[i], m->h2d), "cuMemcpyHtoDAsync");
+        if (roles[i] == EMMY_ROLE_OUT_ZEROED)
             CU(g_drv.cuMemsetD8Async(m->dbuf[i], 0, bytes[i], s), "cuMemsetD8Async");
     }
-    if ((rc = launch_locked(m, args.data(), nargs, nullptr, nullptr, stream))) return rc;
-    for (int i = 0; i < nargs; ++i) {
-        if (roles[i] == EMMY_ROLE_OUT || roles[i] == EMMY_ROLE_INOUT || roles[i] == EMMY_ROLE_OUT_ZEROED)
-            CU(g_drv.cuMemcpyDtoHAsync(host_ptrs[i], m->dbuf[i], bytes[i], s), "cuMemcpyDtoHAsync");
+    CU(g_drv.cuEventRecord(m->ev_whole, m->h2d), "cuEventRecord");
+    CU(g_drv.cuStreamWaitEvent(s, m->ev_whole, 0), "cuStreamWaitEvent");
+    for (uint64_t k = 0; k < nchunks; ++k) {
+        const uint64_t b = k * per, e = std::min(total, b + per);
+        for (int i = 0; i < nargs; ++i) {
+            if (roles[i] == EMMY_ROLE_SCALAR || !is_in(roles[i]) || !m->rec.range_bytes[i]) continue;
+            size_t lo, hi;
+            unit_bytes(m, i, b, e, bytes[i], &lo, &hi);
+            if (hi > lo)
+                CU(g_drv.cuMemcpyHtoDAsync(m->dbuf[i] + lo, static_cast<const char *>(host_ptrs[i]) + lo, hi - lo,
+                                           m->h2d),
+                   "cuMemcpyHtoDAsync");
+        }
+        CU(g_drv.cuEventRecord(m->ev_in[k], m->h2d), "cuEventRecord");
+        CU(g_drv.cuStreamWaitEvent(s, m->ev_in[k], 0), "cuStreamWaitEvent");
+        if ((rc = launch_locked(m, args.data(), nargs, nullptr, nullptr, stream, b, e))) return rc;
+        CU(g_drv.cuEventRecord(m->ev_out[k], s), "cuEventRecord");
+        CU(g_drv.cuStreamWaitEvent(m->d2h, m->ev_out[k], 0), "cuStreamWaitEvent");
+        for (int i = 0; i < nargs; ++i) {
+            if (roles[i] == EMMY_ROLE_SCALAR || !is_out(roles[i]) || !m->rec.range_bytes[i]) continue;
+            size_t lo, hi;
+            unit_bytes(m, i, b, e, bytes[i], &lo, &hi);
+            if (hi > lo)
+                CU(g_drv.cuMemcpyDtoHAsync(static_cast<char *>(host_ptrs[i]) + lo, m->dbuf[i] + lo, hi - lo, m->d2h),
+                   "cuMemcpyDtoHAsync");
+        }
     }
+    // outputs written whole by every launch leave after the last one (d2h already waits on it)
+    for (int i = 0; i < nargs; ++i)
+        if (roles[i] != EMMY_ROLE_SCALAR && is_out(roles[i]) && !m->rec.range_bytes[i])
+            CU(g_drv.cuMemcpyDtoHAsync(host_ptrs[i], m->dbuf[i], bytes[i], m->d2h), "cuMemcpyDtoHAsync");
+    CU(g_drv.cuStreamSynchronize(m->d2h), "cuStreamSynchronize");
     CU(g_drv.cuStreamSynchronize(s), "cuStreamSynchronize");
+    CU(g_drv.cuStreamSynchronize(m->h2d), "cuStreamSynchronize");
+    return EMMY_OK;
+}
+
+int emmy_launch_range(emmy_module_t m, const uint64_t *args, int nargs, uint64_t begin, uint64_t end,
+                      uint64_t stream) {
+    if (!m || (nargs > 0 && !args)) return fail(EMMY_ERR_INVALID, "emmy_launch_range: NULL argument");
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!has_range(m)) return fail(EMMY_ERR_INVALID, "module takes no unit range (launch record has no EMMY_LR_RANGE)");
+    return launch_locked(m, args, nargs, nullptr, nullptr, stream, begin, end);
+}
+
+int emmy_module_range(emmy_module_t m, uint64_t *total, uint32_t *align, uint64_t *bytes_per_unit, int nargs) {
+    if (!m) return fail(EMMY_ERR_INVALID, "module is NULL");
+    const bool r = has_range(m);
+    if (total) *total = r ? m->rec.range_total : 0;
+    if (align) *align = r ? (m->rec.range_align ? m->rec.range_align : 1) : 0;
+    for (int i = 0; bytes_per_unit && i < nargs && i < EMMY_LR_MAX_PARAMS; ++i)
+        bytes_per_unit[i] = r ? m->rec.range_bytes[i] : 0;
     return EMMY_OK;
 }
 

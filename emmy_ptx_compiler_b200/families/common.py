@@ -21,8 +21,13 @@ class LaunchPlan:
     # x SMs (a multiple of grid_quantum); grid[0] here is the fallback estimate
     fill_waves: int = 0
     grid_quantum: int = 1
+    # unit ranges: the kernel takes (range_begin, range_end) after the tensor maps
+    range_total: int = 0          # 0 = no range parameters
+    range_align: int = 1
+    range_bytes: list[int] = field(default_factory=list)  # per arg_order parameter
 
 FLAG_FILL_GRID = 0x100
+FLAG_RANGE = 0x200
 
 
 @dataclass
@@ -83,6 +88,9 @@ def launch_record_source(family: str, launch: LaunchPlan, params: list[ParamSpec
                       "{0u, 0u, 0u, 0u, 0u}, 0u, {0u, 0u, 0u}}")
     g, b = launch.grid, launch.block
     flags = int(launch.cluster[0])
+    if launch.range_total:
+        flags |= FLAG_RANGE
+    rbytes = list(launch.range_bytes) + [0] * (32 - len(launch.range_bytes))
     if launch.fill_waves:
         flags |= FLAG_FILL_GRID
         g = (launch.fill_waves, g[1], g[2])
@@ -94,6 +102,8 @@ def launch_record_source(family: str, launch: LaunchPlan, params: list[ParamSpec
         f"    {{{g[0]}u, {g[1]}u, {g[2]}u}}, {{{b[0]}u, {b[1]}u, {b[2]}u}}, {launch.smem}u, {len(params)}u,\n"
         "    {" + ", ".join(f"{k}u" for k in kinds) + "},\n"
         f"    {len(tmaps)}u, {max(1, int(launch.grid_quantum))}u,\n"
-        "    {" + ",\n     ".join(tm_src) + "}\n"
+        "    {" + ",\n     ".join(tm_src) + "},\n"
+        f"    {int(launch.range_total)}ull, {max(1, int(launch.range_align))}u, 0u,\n"
+        "    {" + ", ".join(f"{int(x)}ull" for x in rbytes) + "}\n"
         "};\n"
     )

@@ -144,6 +144,40 @@ def _c(name: str) -> str:
     return re.sub(r"[^A-Za-z0-9_]", "_", name)
 
 
+def range_bytes(plan: GemmPlan, args: list[str], shapes: dict, dtypes: dict, scalars: dict) -> list[int] | None:
+    """Bytes per output row of each parameter for row-range launches: A's row
+    (K elements) and C's row (N elements); everything else is read whole.
+    None when the epilogue writes anything but C[i, j] of an [M, N] buffer."""
+    if plan.out is None:
+        return None
+    for s in ir.walk(plan.epilogue):
+        if isinstance(s, ir.Write) and s is not plan.out:
+            return None
+    out = []
+    for name in args:
+        if name in scalars:
+            out.append(0)
+        elif name == plan.a.input and tuple(shapes.get(name, ())) == (plan.M, plan.K) and name != plan.out.output:
+            out.append(plan.K * ir.ELEM_BYTES.get(ir.canon_dtype(dtypes.get(name)), 4))
+        elif name == plan.out.output and tuple(shapes.get(name, ())) == (plan.M, plan.N):
+            out.append(plan.N * ir.ELEM_BYTES.get(ir.canon_dtype(dtypes.get(name)), 4))
+        else:
+            out.append(0)
+    return out
+
+
+RANGE_SIG = ["unsigned long long emmy_rb", "unsigned long long emmy_re"]
+
+
+def _row_range(tile_rows: int, mb_total: int) -> str:
+    """Kernel prologue: this launch's rows [RB, RE) as row-tiles [MB0, MB0 + MBN)."""
+    return (f"    const long long RB = (long long)(emmy_rb < (unsigned long long)M ? emmy_rb : M);\n"
+            f"    const long long RE = (long long)(emmy_re < (unsigned long long)M ? emmy_re : M);\n"
+            f"    const int MB0 = (int)(RB / {tile_rows});\n"
+            f"    const int MBN = RE > RB ? (int)((RE + {tile_rows} - 1) / {tile_rows}) - MB0 : 0;\n"
+            f"    const int TILES = MBN * NB;\n")
+
+
 def _tc_ok(plan: GemmPlan, dtypes) -> tuple[bool, list[str]]:
     why = []
     if plan.ab_dtype not in ("bf16", "f16"):
@@ -182,12 +216,18 @@ def generate(kop: ir.KernelOp, plan: GemmPlan, shapes: dict, dtypes: dict, args:
         params.append(ParamSpec(name, "ptr", dt))
     scalar_env = {n: (("f32", f"p_{_c(n)}") if scalars[n] == "f32" else ("int", f"(long long)p_{_c(n)}"))
                   for n in scalars}
+    # every GEMM module takes a row range after its tensor maps (rows it cannot
+    # stream are then marked 0 bytes per row: read or written whole)
+    rbytes = range_bytes(plan, args, shapes, dtypes, scalars) or [0] * len(args)
     ok, why = _tc_ok(plan, dtypes)
     if ok:
         if variant == "pair" or (variant == "auto" and plan.M >= PAIR_BM and plan.N >= BN):
-            return _gen_tcgen05_pair(kop, plan, shapes, dtypes, args, ptrs, sig, params, scalar_env)
-        return _gen_tcgen05(kop, plan, shapes, dtypes, args, ptrs, sig, params, scalar_env)
-    return _gen_simt(kop, plan, shapes, dtypes, args, ptrs, sig, params, scalar_env, why)
+            ks = _gen_tcgen05_pair(kop, plan, shapes, dtypes, args, ptrs, sig, params, scalar_env, rbytes)
+        else:
+            ks = _gen_tcgen05(kop, plan, shapes, dtypes, args, ptrs, sig, params, scalar_env, rbytes)
+    else:
+        ks = _gen_simt(kop, plan, shapes, dtypes, args, ptrs, sig, params, scalar_env, why, rbytes)
+    return ks
 
 
 # ---------------------------------------------------------------------------- epilogue
@@ -217,7 +257,8 @@ def _epilogue_code(plan: GemmPlan, shapes, dtypes, ptrs, scalar_env, acc_code: s
 # ---------------------------------------------------------------------------- tcgen05
 
 
-def _gen_tcgen05(kop, plan: GemmPlan, shapes, dtypes, args, ptrs, sig, params, scalar_env) -> KernelSource:
+def _gen_tcgen05(kop, plan: GemmPlan, shapes, dtypes, args, ptrs, sig, params, scalar_env,
+                 rbytes) -> KernelSource:
     M, N, K = plan.M, plan.N, plan.K
     mb, nb, kb = -(-M // BM), -(-N // BN), -(-K // BK)
     tiles = mb * nb
@@ -235,7 +276,7 @@ def _gen_tcgen05(kop, plan: GemmPlan, shapes, dtypes, args, ptrs, sig, params, s
     a_stage = BM * BK * esz
     b_stage = BN * BK * esz
     smem = 1024 + STAGES * (a_stage + b_stage) + 256
-    sig = list(sig) + ["const __grid_constant__ CUtensorMap tm_a", "const __grid_constant__ CUtensorMap tm_b"]
+    sig = list(sig) + ["const __grid_constant__ CUtensorMap tm_a", "const __grid_constant__ CUtensorMap tm_b"] + RANGE_SIG
     out_ptr = ptrs[plan.out.output]
     vec_store = (N % 8 == 0) if odt in ("bf16", "f16") else (N % 4 == 0)
     epi_full = _epilogue_code(plan, shapes, dtypes, ptrs, scalar_env, "__uint_as_float(r[jj])", "row",
@@ -261,25 +302,26 @@ def _gen_tcgen05(kop, plan: GemmPlan, shapes, dtypes, args, ptrs, sig, params, s
 namespace {{
 constexpr long long M = {M}LL, N = {N}LL, K = {K}LL;
 constexpr int BM = {BM}, BN = {BN}, BK = {BK}, STAGES = {STAGES};
-constexpr int MB = {mb}, NB = {nb}, KB = {kb}, TILES = {tiles}, GROUP_M = {GROUP_M};
+constexpr int NB = {nb}, KB = {kb}, GROUP_M = {GROUP_M};
 constexpr uint32_t A_STAGE = {a_stage}u, B_STAGE = {b_stage}u;
 constexpr uint32_t SMEM_BYTES = {smem}u;
 constexpr uint32_t IDESC = emmy::idesc_f16({fmt}u, {0 if plan.b_nk else 1}u, BM, BN);
 constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s per wait: orders of magnitude above any legal wait
 
-__device__ __forceinline__ void tile_coords(int t, int &mb, int &nb) {{
+// tile t of a launch over row-tiles [mb0, mb0 + mbn): GROUP_M row-tiles share each column sweep
+__device__ __forceinline__ void tile_coords(int t, int mb0, int mbn, int &mb, int &nb) {{
     const int per_group = GROUP_M * NB;
     const int g = t / per_group;
     const int r = t - g * per_group;
     const int first = g * GROUP_M;
-    const int rows = (MB - first) < GROUP_M ? (MB - first) : GROUP_M;
-    mb = first + r % rows;
+    const int rows = (mbn - first) < GROUP_M ? (mbn - first) : GROUP_M;
+    mb = mb0 + first + r % rows;
     nb = r / rows;
 }}
 }}  // namespace
 
 extern "C" __global__ void __launch_bounds__({TC_THREADS}, 1) {kop.name}({", ".join(sig)}) {{
-    uint32_t dyn_smem;
+{_row_range(BM, mb)}    uint32_t dyn_smem;
     asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn_smem));
     if (blockDim.x != {TC_THREADS} || blockDim.y != 1 || blockDim.z != 1 || dyn_smem < SMEM_BYTES) {{
         if (threadIdx.x == 0 && threadIdx.y == 0 && threadIdx.z == 0) atomicOr(&emmy_status, EMMY_STATUS_BAD_LAUNCH);
@@ -326,7 +368,7 @@ extern "C" __global__ void __launch_bounds__({TC_THREADS}, 1) {kop.name}({", ".j
             bool ok = true;
             for (int t = blockIdx.x; t < TILES && ok; t += gridDim.x) {{
                 int tm, tn;
-                tile_coords(t, tm, tn);
+                tile_coords(t, MB0, MBN, tm, tn);
                 for (int k = 0; k < KB; ++k) {{
                     if (!emmy::mbar_wait(&empty[stage], phase ^ 1u, abort_flag, EMMY_STATUS_TIMEOUT_PRODUCER, WAIT_NS)) {{ ok = false; break; }}
                     emmy::mbar_arrive_expect_tx(&full[stage], A_STAGE + B_STAGE);
@@ -387,7 +429,7 @@ extern "C" __global__ void __launch_bounds__({TC_THREADS}, 1) {kop.name}({", ".j
             if (!emmy::mbar_wait(&tfull[acc], aphase, abort_flag, EMMY_STATUS_TIMEOUT_EPILOGUE, WAIT_NS)) break;
             emmy::tc_fence_after();
             int tm, tn;
-            tile_coords(t, tm, tn);
+            tile_coords(t, MB0, MBN, tm, tn);
             const long long row = (long long)tm * BM + q * 32 + lane;
             #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {{
@@ -426,7 +468,8 @@ extern "C" __global__ void __launch_bounds__({TC_THREADS}, 1) {kop.name}({", ".j
 }}
 """
     grid = max(1, min(tiles, SM_COUNT))
-    launch = LaunchPlan(grid=(grid, 1, 1), block=(TC_THREADS, 1, 1), smem=smem)
+    launch = LaunchPlan(grid=(grid, 1, 1), block=(TC_THREADS, 1, 1), smem=smem,
+                        range_total=M, range_align=BM, range_bytes=rbytes)
     src += launch_record_source("gemm", launch, params, [tm_a, tm_b])
     notes = {"kernel": "tcgen05", "tile": [BM, BN, BK], "stages": STAGES, "tiles": tiles,
              "b_layout": "NK" if plan.b_nk else "KN", "vector_store": vec_store}
@@ -454,7 +497,8 @@ def _b_desc(b_nk: bool) -> str:
 # ---------------------------------------------------------------------------- SIMT
 
 
-def _gen_simt(kop, plan: GemmPlan, shapes, dtypes, args, ptrs, sig, params, scalar_env, why) -> KernelSource:
+def _gen_simt(kop, plan: GemmPlan, shapes, dtypes, args, ptrs, sig, params, scalar_env, why,
+              rbytes) -> KernelSource:
     M, N, K = plan.M, plan.N, plan.K
     mb, nb = -(-M // SIMT_BM), -(-N // SIMT_BN)
     tiles = mb * nb
@@ -468,9 +512,10 @@ def _gen_simt(kop, plan: GemmPlan, shapes, dtypes, args, ptrs, sig, params, scal
 #include "emmy_launch_record.h"
 extern "C" __device__ unsigned int emmy_status;
 
-extern "C" __global__ void __launch_bounds__({SIMT_THREADS}) {kop.name}({", ".join(sig)}) {{
+extern "C" __global__ void __launch_bounds__({SIMT_THREADS}) {kop.name}({", ".join(sig + RANGE_SIG)}) {{
     constexpr long long M = {M}LL, N = {N}LL, K = {K}LL;
-    constexpr int TBM = {SIMT_BM}, TBN = {SIMT_BN}, TBK = {SIMT_BK}, MB = {mb}, NB = {nb};
+    constexpr int TBM = {SIMT_BM}, TBN = {SIMT_BN}, TBK = {SIMT_BK}, NB = {nb};
+{_row_range(SIMT_BM, mb)}
     if (blockDim.x != {SIMT_THREADS} || blockDim.y != 1 || blockDim.z != 1) {{
         if (threadIdx.x == 0 && threadIdx.y == 0 && threadIdx.z == 0) atomicOr(&emmy_status, EMMY_STATUS_BAD_LAUNCH);
         return;
@@ -478,8 +523,8 @@ extern "C" __global__ void __launch_bounds__({SIMT_THREADS}) {kop.name}({", ".jo
     __shared__ float sa[TBK][TBM + 1];
     __shared__ float sb[TBK][TBN + 1];
     const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
-    for (int t = blockIdx.x; t < MB * NB; t += gridDim.x) {{
-        const long long m0 = (long long)(t / NB) * TBM, n0 = (long long)(t % NB) * TBN;
+    for (int t = blockIdx.x; t < TILES; t += gridDim.x) {{
+        const long long m0 = (long long)(MB0 + t / NB) * TBM, n0 = (long long)(t % NB) * TBN;
         float acc[4][4];
         #pragma unroll
         for (int a = 0; a < 4; ++a)
@@ -525,7 +570,8 @@ extern "C" __global__ void __launch_bounds__({SIMT_THREADS}) {kop.name}({", ".jo
 }}
 """
     grid = max(1, min(tiles, SM_COUNT * 8))
-    launch = LaunchPlan(grid=(grid, 1, 1), block=(SIMT_THREADS, 1, 1), smem=0)
+    launch = LaunchPlan(grid=(grid, 1, 1), block=(SIMT_THREADS, 1, 1), smem=0,
+                        range_total=M, range_align=SIMT_BM, range_bytes=rbytes)
     src += launch_record_source("gemm", launch, params)
     notes = {"kernel": "simt", "tile": [SIMT_BM, SIMT_BN, SIMT_BK], "tiles": tiles, "why_not_tcgen05": why}
     return KernelSource(entry=kop.name, source=src, launch=launch, params=params, family="gemm", notes=notes)
@@ -534,7 +580,8 @@ extern "C" __global__ void __launch_bounds__({SIMT_THREADS}) {kop.name}({", ".jo
 # ---------------------------------------------------------------------------- tcgen05, CTA pair
 
 
-def _gen_tcgen05_pair(kop, plan: GemmPlan, shapes, dtypes, args, ptrs, sig, params, scalar_env) -> KernelSource:
+def _gen_tcgen05_pair(kop, plan: GemmPlan, shapes, dtypes, args, ptrs, sig, params, scalar_env,
+                      rbytes) -> KernelSource:
     """256x256 tiles on a cluster of two CTAs (``cta_group::2``): each CTA loads
     its 128 rows of A and its 128 columns of B per stage (32 KB instead of the
     single-CTA kernel's 48 KB for half the FLOPs), the leader issues
@@ -558,7 +605,7 @@ def _gen_tcgen05_pair(kop, plan: GemmPlan, shapes, dtypes, args, ptrs, sig, para
     a_stage = cbm * BK * esz
     b_stage = cbn * BK * esz
     smem = 1024 + PAIR_STAGES * (a_stage + b_stage) + 256
-    sig = list(sig) + ["const __grid_constant__ CUtensorMap tm_a", "const __grid_constant__ CUtensorMap tm_b"]
+    sig = list(sig) + ["const __grid_constant__ CUtensorMap tm_a", "const __grid_constant__ CUtensorMap tm_b"] + RANGE_SIG
     out_ptr = ptrs[plan.out.output]
     vec_store = (N % 8 == 0) if odt in ("bf16", "f16") else (N % 4 == 0)
     epi_full = _epilogue_code(plan, shapes, dtypes, ptrs, scalar_env, "__uint_as_float(r[jj])", "row",
@@ -593,25 +640,26 @@ def _gen_tcgen05_pair(kop, plan: GemmPlan, shapes, dtypes, args, ptrs, sig, para
 namespace {{
 constexpr long long M = {M}LL, N = {N}LL, K = {K}LL;
 constexpr int BM = {PAIR_BM}, CBM = {cbm}, BN = {BN}, CBN = {cbn}, BK = {BK}, STAGES = {PAIR_STAGES};
-constexpr int MB = {mb}, NB = {nb}, KB = {kb}, TILES = {tiles}, GROUP_M = {GROUP_M};
+constexpr int NB = {nb}, KB = {kb}, GROUP_M = {GROUP_M};
 constexpr uint32_t A_STAGE = {a_stage}u, B_STAGE = {b_stage}u;
 constexpr uint32_t SMEM_BYTES = {smem}u;
 constexpr uint32_t IDESC = emmy::idesc_f16({fmt}u, {0 if plan.b_nk else 1}u, BM, BN);
 constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s per wait: orders of magnitude above any legal wait
 
-__device__ __forceinline__ void tile_coords(int t, int &mb, int &nb) {{
+// tile t of a launch over row-tiles [mb0, mb0 + mbn): GROUP_M row-tiles share each column sweep
+__device__ __forceinline__ void tile_coords(int t, int mb0, int mbn, int &mb, int &nb) {{
     const int per_group = GROUP_M * NB;
     const int g = t / per_group;
     const int r = t - g * per_group;
     const int first = g * GROUP_M;
-    const int rows = (MB - first) < GROUP_M ? (MB - first) : GROUP_M;
-    mb = first + r % rows;
+    const int rows = (mbn - first) < GROUP_M ? (mbn - first) : GROUP_M;
+    mb = mb0 + first + r % rows;
     nb = r / rows;
 }}
 }}  // namespace
 
 extern "C" __global__ void __launch_bounds__({TC_THREADS}, 1) {kop.name}({", ".join(sig)}) {{
-    uint32_t dyn_smem;
+{_row_range(PAIR_BM, mb)}    uint32_t dyn_smem;
     asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn_smem));
     if (blockDim.x != {TC_THREADS} || blockDim.y != 1 || blockDim.z != 1 || dyn_smem < SMEM_BYTES ||
         emmy::cluster_nctarank() != 2u || (gridDim.x & 1u)) {{
@@ -662,7 +710,7 @@ extern "C" __global__ void __launch_bounds__({TC_THREADS}, 1) {kop.name}({", ".j
             bool ok = true;
             for (int t = pair; t < TILES && ok; t += npairs) {{
                 int tm, tn;
-                tile_coords(t, tm, tn);
+                tile_coords(t, MB0, MBN, tm, tn);
                 for (int k = 0; k < KB; ++k) {{
                     if (!emmy::mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, EMMY_STATUS_TIMEOUT_PRODUCER, WAIT_NS)) {{ ok = false; break; }}
                     if (rank == 0) emmy::mbar_arrive_expect_tx(&full[stage], 2u * (A_STAGE + B_STAGE));
@@ -730,7 +778,7 @@ extern "C" __global__ void __launch_bounds__({TC_THREADS}, 1) {kop.name}({", ".j
             if (!emmy::mbar_wait_cluster(&tfull[acc], aphase, abort_flag, EMMY_STATUS_TIMEOUT_EPILOGUE, WAIT_NS)) break;
             emmy::tc_fence_after();
             int tm, tn;
-            tile_coords(t, tm, tn);
+            tile_coords(t, MB0, MBN, tm, tn);
             const long long row = (long long)tm * BM + (int)rank * CBM + q * 32 + lane;
             #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {{
@@ -778,7 +826,8 @@ extern "C" __global__ void __launch_bounds__({TC_THREADS}, 1) {kop.name}({", ".j
 }}
 """
     grid = max(2, min(tiles * 2, SM_COUNT) // 2 * 2)
-    launch = LaunchPlan(grid=(grid, 1, 1), block=(TC_THREADS, 1, 1), smem=smem, cluster=(2, 1, 1))
+    launch = LaunchPlan(grid=(grid, 1, 1), block=(TC_THREADS, 1, 1), smem=smem, cluster=(2, 1, 1),
+                        range_total=M, range_align=PAIR_BM, range_bytes=rbytes)
     src += launch_record_source("gemm", launch, params, [tm_a, tm_b])
     notes = {"kernel": "tcgen05_pair", "tile": [PAIR_BM, BN, BK], "stages": PAIR_STAGES, "tiles": tiles,
              "b_layout": "NK" if plan.b_nk else "KN", "vector_store": vec_store, "cluster": 2}

@@ -27,6 +27,7 @@ import math
 from dataclasses import dataclass, field
 
 from .. import ir
+from ..ir import ELEM_BYTES
 from ..cgen import DEVICE_PRELUDE, Emitter, ctype, load_to_kind, store_from
 from ..errors import UnsupportedIR
 from .common import KernelSource, LaunchPlan, ParamSpec, SM_COUNT, launch_record_source
@@ -205,6 +206,9 @@ def generate(kop: ir.KernelOp, plan: PointwisePlan, shapes: dict, dtypes: dict, 
         params.append(ParamSpec(name, "ptr", dt))
     ncell = plan.ncells
     axes = plan.axes
+    rbytes = range_bytes(plan, args, scalars, dtypes, shapes)
+    if rbytes is not None:
+        sig += ["unsigned long long emmy_rb", "unsigned long long emmy_re"]
     use_pair = vec_ok and (pair is True or (pair == "auto" and pairable(plan, dtypes)))
     plan.pair = use_pair
     vtrip = functools.partial(_vector_trip, pair=use_pair)
@@ -215,6 +219,12 @@ def generate(kop: ir.KernelOp, plan: PointwisePlan, shapes: dict, dtypes: dict, 
     lb = f"{BLOCK}, {min_blocks}" if min_blocks else f"{BLOCK}"
     w(f'extern "C" __global__ void __launch_bounds__({lb}) {kop.name}(' + ", ".join(sig) + ") {")
     w(f"    constexpr long long NCELL = {ncell}LL;")
+    if rbytes is not None:
+        # this launch's cells: [RB, RE)
+        w("    const long long RB = (long long)(emmy_rb < (unsigned long long)NCELL ? emmy_rb : NCELL);")
+        w("    const long long RE = (long long)(emmy_re < (unsigned long long)NCELL ? emmy_re : NCELL);")
+    else:
+        w("    constexpr long long RB = 0, RE = NCELL;")
     w("    const long long gstride = (long long)gridDim.x * blockDim.x;")
     w("    const long long gtid = (long long)blockIdx.x * blockDim.x + threadIdx.x;")
     scalar_env = {name: (("f32", f"p_{_c(name)}") if scalars[name] == "f32" else
@@ -223,13 +233,16 @@ def generate(kop: ir.KernelOp, plan: PointwisePlan, shapes: dict, dtypes: dict, 
         align_terms = [f"(uintptr_t)p_{_c(n)}" for n in ptrs]
         idx32 = order != "blocked" and ncell < (1 << 31)
         w("    const bool aligned = ((" + (" | ".join(align_terms) if align_terms else "0") + ") & 15u) == 0"
+          + f" && RB % {VEC} == 0 && RE % {VEC} == 0"
           + (" && gstride <= (1LL << 27);" if idx32 else ";"))
         w("    if (aligned) {")
-        w(f"        constexpr {'unsigned' if idx32 else 'long long'} NVEC = NCELL / {VEC};")
+        ity0 = 'unsigned' if idx32 else 'long long'
+        w(f"        const {ity0} NVEC = ({ity0})(RE / {VEC});  // one past this launch's last vector")
+        w(f"        const {ity0} VB0 = ({ity0})(RB / {VEC});")
         if order == "blocked":
             # CTA b owns vectors [b*per, (b+1)*per); a trip covers unroll*blockDim consecutive vectors
-            w("        const long long per = (NVEC + gridDim.x - 1) / gridDim.x;")
-            w("        const long long vbeg = (long long)blockIdx.x * per;")
+            w("        const long long per = ((long long)NVEC - VB0 + gridDim.x - 1) / gridDim.x;")
+            w("        const long long vbeg = VB0 + (long long)blockIdx.x * per;")
             w("        const long long vend = (vbeg + per < NVEC) ? (vbeg + per) : NVEC;")
             w("        const long long bstride = blockDim.x;")
             w("        long long v = vbeg + threadIdx.x;")
@@ -244,11 +257,12 @@ def generate(kop: ir.KernelOp, plan: PointwisePlan, shapes: dict, dtypes: dict, 
             w("        return;")
             w("    }")
             return _finish_vector(kop, plan, lines, ncell, unroll, vec_ok, params, why, em_path=True,
-                                  shapes=shapes, dtypes=dtypes, ptrs=ptrs, scalar_env=scalar_env)
+                                  shapes=shapes, dtypes=dtypes, ptrs=ptrs, scalar_env=scalar_env,
+                                  rbytes=rbytes)
         quantum = 1  # grid multiple that keeps hoisted broadcast operands valid
         # vector offsets in 32 bits when they stay below 2^32: c < NCELL + 4*unroll*gstride
         ity, isuf = ("unsigned", "u") if idx32 else ("long long", "LL")
-        w(f"        {ity} v = ({ity})gtid;")
+        w(f"        {ity} v = VB0 + ({ity})gtid;")
         w(f"        const {ity} vgs = ({ity})gstride;")
         hoist = _hoistable(plan) if hoist_broadcast else {}
         if hoist:
@@ -305,14 +319,14 @@ def generate(kop: ir.KernelOp, plan: PointwisePlan, shapes: dict, dtypes: dict, 
         w("    }")
     return _finish_vector(kop, plan, lines, ncell, unroll, vec_ok, params, why, em_path=True,
                           shapes=shapes, dtypes=dtypes, ptrs=ptrs, scalar_env=scalar_env,
-                          grid_quantum=quantum if vec_ok else 1)
+                          grid_quantum=quantum if vec_ok else 1, rbytes=rbytes)
 
 
 def _finish_vector(kop, plan, lines, ncell, unroll, vec_ok, params, why, *, em_path, shapes, dtypes, ptrs,
-                   scalar_env, grid_quantum: int = 1) -> KernelSource:
+                   scalar_env, grid_quantum: int = 1, rbytes: list[int] | None = None) -> KernelSource:
     """The scalar grid-stride loop (any launch, any alignment) and the launch record."""
     w = lines.append
-    w("    for (long long cell = gtid; cell < NCELL; cell += gstride) {")
+    w("    for (long long cell = RB + gtid; cell < RE; cell += gstride) {")
     em = Emitter(shapes, dtypes, ptrs, indent="        ")
     em.env.update(scalar_env)
     _decode_axes(em, plan.axes, "cell", "ax")
@@ -325,6 +339,10 @@ def _finish_vector(kop, plan, lines, ncell, unroll, vec_ok, params, why, *, em_p
     want = (nvec + per_block - 1) // per_block
     grid = max(1, min(want, SM_COUNT * 8))
     launch = LaunchPlan(grid=(grid, 1, 1), block=(BLOCK, 1, 1), smem=0)
+    if rbytes is not None:
+        launch.range_total = ncell
+        launch.range_align = RANGE_ALIGN
+        launch.range_bytes = rbytes
     if want >= SM_COUNT * 8:
         # enough work to fill the device: one wave of exactly the CTAs that fit,
         # counted by the loader for this build's registers (a partial second wave
@@ -473,6 +491,39 @@ def _pair_lanes(plan, shapes, dtypes, ptrs, scalar_env, vexprs, ind, fetched, lo
             out.append(f"{ind}{{")
             out.extend(em.lines)
             out.append(f"{ind}}}")
+    return out
+
+
+RANGE_ALIGN = 4096  # cells: range ends keep vectors, hoisting periods up to 16 KB and pages whole
+
+
+def range_bytes(plan: PointwisePlan, args: list[str], scalars: dict, dtypes: dict,
+                shapes: dict) -> list[int] | None:
+    """Bytes per cell of each parameter for ranged launches (cell c of a
+    whole-tile buffer is element c), 0 for parameters read whole; None when
+    some output is written other than element-per-cell, so a range of cells
+    would write bytes outside its range."""
+    axes = plan.axes
+    full: dict[str, bool] = {}
+    written: set[str] = set()
+    for s in ir.walk(plan.tile.body):
+        if isinstance(s, (ir.Load, ir.Write)):
+            buf = s.input if isinstance(s, ir.Load) else s.output
+            pos = _axis_aligned(s.index, axes)
+            shape = [int(d) for d in shapes.get(buf, ())]
+            ok = (pos == list(range(len(axes))) and shape == [ext for _, ext in axes]
+                  and (isinstance(s, ir.Load) or len(s.values) == 1))
+            full[buf] = full.get(buf, True) and ok
+            if isinstance(s, ir.Write):
+                written.add(buf)
+                if not ok or s.atomic:
+                    return None
+    out = []
+    for name in args:
+        if name in scalars or name not in full or not full[name]:
+            out.append(0)
+            continue
+        out.append(ELEM_BYTES.get(ir.canon_dtype(dtypes.get(name)), 4))
     return out
 
 

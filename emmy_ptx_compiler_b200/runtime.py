@@ -53,6 +53,8 @@ def _declare(lib) -> None:
         "emmy_host_free": ([vp], i32),
         "emmy_run_host": ([vp, P(vp), P(sz), P(C.c_uint8), i32, u64], i32),
         "emmy_time_launch": ([vp, P(u64), i32, i32, u64, P(C.c_float)], i32),
+        "emmy_launch_range": ([vp, P(u64), i32, u64, u64, u64], i32),
+        "emmy_module_range": ([vp, P(u64), P(u32), P(u64), i32], i32),
         "emmy_sum_f32_noalloc": ([i32, u64, u64, u64, u64], i32),
         "emmy_comm_unique_id": ([P(C.c_uint8)], i32),
         "emmy_comm_init": ([i32, i32, i32, P(C.c_uint8), i32, P(vp)], i32),
@@ -70,7 +72,8 @@ def _declare(lib) -> None:
 EXPORTED = ("emmy_version", "emmy_last_error", "emmy_init", "emmy_device_count", "emmy_load",
             "emmy_unload", "emmy_module_info", "emmy_launch", "emmy_module_status", "emmy_sync",
             "emmy_alloc", "emmy_free", "emmy_memcpy_htod", "emmy_memcpy_dtoh", "emmy_memset_d8",
-            "emmy_host_alloc", "emmy_host_free", "emmy_run_host", "emmy_time_launch", "emmy_sum_f32_noalloc",
+            "emmy_host_alloc", "emmy_host_free", "emmy_run_host", "emmy_time_launch", "emmy_launch_range",
+            "emmy_module_range", "emmy_sum_f32_noalloc",
             "emmy_comm_unique_id", "emmy_comm_init", "emmy_allreduce_f32", "emmy_allgather_f32",
             "emmy_comm_destroy", "emmy_comm_abort")
 
@@ -165,6 +168,19 @@ class Module:
         g = (C.c_uint32 * 3)(*(list(grid) + [1, 1])[:3]) if grid is not None else None
         b = (C.c_uint32 * 3)(*(list(block) + [1, 1])[:3]) if block is not None else None
         _check(lib().emmy_launch(self._h, words, len(args), g, b, C.c_uint64(stream)))
+
+    def launch_range(self, args, begin: int, end: int, stream: int = 0) -> None:
+        """Launch over units [begin, end) (cells / output rows) only."""
+        words = self._words(args)
+        _check(lib().emmy_launch_range(self._h, words, len(args), C.c_uint64(begin), C.c_uint64(end),
+                                       C.c_uint64(stream)))
+
+    def unit_range(self) -> tuple[int, int, list[int]]:
+        """(total units, alignment, bytes per unit of each parameter); total 0 = no ranges."""
+        tot, al = C.c_uint64(0), C.c_uint32(0)
+        per = (C.c_uint64 * 32)()
+        _check(lib().emmy_module_range(self._h, C.byref(tot), C.byref(al), per, 32))
+        return tot.value, al.value, list(per)[: self.nparams]
 
     def status(self) -> int:
         st = C.c_uint32(0)

@@ -106,6 +106,19 @@ int emmy_host_free(void *ptr);
 int emmy_run_host(emmy_module_t m, void *const *host_ptrs, const size_t *bytes,
                   const uint8_t *roles, int nargs, uint64_t stream);
 
+/* Launch over units [begin, end) only (no counterpart in the reference):
+ * modules whose launch record carries EMMY_LR_RANGE (pointwise: cells, GEMM:
+ * output rows) read and write only those units' bytes of the streamed
+ * parameters, so a caller can overlap copies of one range with the kernel
+ * on another.  begin and end are multiples of the module's alignment (end may
+ * be the total); emmy_module_range reports total, alignment and the bytes per
+ * unit of each parameter (0 = read whole).  emmy_run_host uses this to pipeline
+ * large problems in chunks over a copy-in stream, `stream` and a copy-out
+ * stream. */
+int emmy_launch_range(emmy_module_t m, const uint64_t *args, int nargs, uint64_t begin, uint64_t end,
+                      uint64_t stream);
+int emmy_module_range(emmy_module_t m, uint64_t *total, uint32_t *align, uint64_t *bytes_per_unit, int nargs);
+
 /* Launch `iters` times back to back on `stream` between two CUDA events and
  * return the elapsed milliseconds (device time). */
 int emmy_time_launch(emmy_module_t m, const uint64_t *args, int nargs, int iters, uint64_t stream,

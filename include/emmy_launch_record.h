@@ -29,7 +29,7 @@
 #include <stdint.h>
 
 #define EMMY_LR_MAGIC 0x31594D45u /* "EMY1" little-endian */
-#define EMMY_LR_VERSION 1u
+#define EMMY_LR_VERSION 2u
 #define EMMY_LR_MAX_PARAMS 32
 #define EMMY_LR_MAX_TMAPS 4
 
@@ -51,6 +51,16 @@ enum EmmyParamKind { EMMY_PARAM_PTR = 0, EMMY_PARAM_F32 = 1, EMMY_PARAM_I32 = 2 
  * to a multiple of grid_quantum.  In the record as emitted, grid[0] holds the
  * number of waves; emmy_module_info reports the resolved grid. */
 #define EMMY_LR_FILL_GRID 0x100u
+/* EMMY_LR_RANGE: the kernel takes two more parameters after the tensor maps,
+ * uint64 range_begin and range_end, and does the work of units
+ * [range_begin, range_end) only (pointwise: cells; GEMM: rows of the output).
+ * A launch over the whole problem passes 0 and range_total.  Unit u of a
+ * parameter with range_bytes[i] > 0 is bytes [u * range_bytes[i],
+ * (u + 1) * range_bytes[i]) of that buffer, and a launch over a range reads
+ * and writes no other bytes of it; parameters with range_bytes[i] == 0 are
+ * read whole by every launch.  Range ends are multiples of range_align, or
+ * range_total. */
+#define EMMY_LR_RANGE 0x200u
 
 typedef struct EmmyTmapSpec {
     uint32_t src_param; /* index into arg_order of the global buffer */
@@ -77,6 +87,11 @@ typedef struct EmmyLaunchRecord {
     uint32_t ntmaps;
     uint32_t grid_quantum; /* with EMMY_LR_FILL_GRID: grid[0] is a multiple of this (0 = 1) */
     EmmyTmapSpec tmaps[EMMY_LR_MAX_TMAPS];
+    /* version 2: unit ranges (EMMY_LR_RANGE) */
+    uint64_t range_total;
+    uint32_t range_align;
+    uint32_t range_reserved;
+    uint64_t range_bytes[EMMY_LR_MAX_PARAMS];
 } EmmyLaunchRecord;
 
 #endif
