@@ -39,6 +39,10 @@ PAIR_BM, PAIR_STAGES = 256, 6   # CTA-pair tile: 256 x 256, 128 rows and 128 B-c
 TC_THREADS = 192
 SIMT_BM, SIMT_BN, SIMT_BK, SIMT_THREADS = 64, 64, 16, 256
 GROUP_M = 16
+# CTA-pair kernel schedule knobs (results do not depend on them): row-tiles per
+# column sweep, C stores ("wb" write-back, "cs" streaming), L2 policies of the
+# A and B tile loads (None, "evict_last", "evict_first")
+PAIR_TUNE = {"group_m": 16, "c_store": "wb", "a_policy": None, "b_policy": None}
 TMAP_DTYPE = {"bf16": 9, "f16": 6}
 SWIZZLE_128B = 3
 L2_256B = 3
@@ -198,7 +202,8 @@ def _tc_ok(plan: GemmPlan, dtypes) -> tuple[bool, list[str]]:
 
 
 def generate(kop: ir.KernelOp, plan: GemmPlan, shapes: dict, dtypes: dict, args: list[str],
-             scalars: dict[str, str], written: set[str], *, variant: str = "auto") -> KernelSource:
+             scalars: dict[str, str], written: set[str], *, variant: str = "auto",
+             tune: dict | None = None) -> KernelSource:
     """``variant``: "auto" (CTA-pair kernel when M >= 256 and N >= 256, else
     single-CTA), "pair", "single"; non-TMA-able shapes and f32 go to SIMT."""
     params: list[ParamSpec] = []
@@ -222,7 +227,7 @@ def generate(kop: ir.KernelOp, plan: GemmPlan, shapes: dict, dtypes: dict, args:
     ok, why = _tc_ok(plan, dtypes)
     if ok:
         if variant == "pair" or (variant == "auto" and plan.M >= PAIR_BM and plan.N >= BN):
-            ks = _gen_tcgen05_pair(kop, plan, shapes, dtypes, args, ptrs, sig, params, scalar_env, rbytes)
+            ks = _gen_tcgen05_pair(kop, plan, shapes, dtypes, args, ptrs, sig, params, scalar_env, rbytes, tune)
         else:
             ks = _gen_tcgen05(kop, plan, shapes, dtypes, args, ptrs, sig, params, scalar_env, rbytes)
     else:
@@ -581,13 +586,14 @@ extern "C" __global__ void __launch_bounds__({SIMT_THREADS}) {kop.name}({", ".jo
 
 
 def _gen_tcgen05_pair(kop, plan: GemmPlan, shapes, dtypes, args, ptrs, sig, params, scalar_env,
-                      rbytes) -> KernelSource:
+                      rbytes, tune: dict | None = None) -> KernelSource:
     """256x256 tiles on a cluster of two CTAs (``cta_group::2``): each CTA loads
     its 128 rows of A and its 128 columns of B per stage (32 KB instead of the
     single-CTA kernel's 48 KB for half the FLOPs), the leader issues
     ``tcgen05.mma.cta_group::2`` 256x256x16 over both CTAs' shared memory into
     both CTAs' tensor memory, and each CTA's epilogue drains its own 128 rows.
     6 pipeline stages fit in shared memory."""
+    tn_ = {**PAIR_TUNE, **(tune or {})}
     M, N, K = plan.M, plan.N, plan.K
     mb, nb, kb = -(-M // PAIR_BM), -(-N // BN), -(-K // BK)
     tiles = mb * nb
@@ -618,20 +624,32 @@ def _gen_tcgen05_pair(kop, plan: GemmPlan, shapes, dtypes, args, ptrs, sig, para
                 "                    for (int v = 0; v < 4; ++v) {\n"
                 "                        uint4 w;\n"
                 "                        memcpy(&w, &ov[v * 8], 16);\n"
-                "                        dst[v] = w;\n"
+                "                        " + ("__stcs(&dst[v], w);" if tn_["c_store"] == "cs" else "dst[v] = w;") + "\n"
                 "                    }\n")
     else:
         pack = ("                    float4 *dst = reinterpret_cast<float4 *>(" + out_ptr + " + row * (long long)N + col0);\n"
                 "                    #pragma unroll\n"
                 "                    for (int v = 0; v < 8; ++v) dst[v] = make_float4(ov[4*v], ov[4*v+1], ov[4*v+2], ov[4*v+3]);\n")
+    bpol = "pol_b" if tn_["b_policy"] else None
+    apol = "pol_a" if tn_["a_policy"] else None
+
+    def _ld(call_args: str, pol) -> str:
+        return (f"emmy::tma_load_2d_pair({call_args});" if pol is None
+                else f"emmy::tma_load_2d_pair_hint({call_args}, {pol});")
+
+    policies = "".join(
+        f"            const uint64_t {var} = emmy::l2_policy_{tn_[key].replace('evict_', 'evict_')}();\n"
+        for var, key in (("pol_a", "a_policy"), ("pol_b", "b_policy")) if tn_[key])
+    a_load = "                    " + _ld("sA + stage * A_STAGE, &tm_a, fbar, k * BK, tm * BM + (int)rank * CBM", apol)
     if plan.b_nk:
-        b_loads = ("                    emmy::tma_load_2d_pair(sB + stage * B_STAGE, &tm_b, fbar, k * BK, "
-                   "tn * BN + (int)rank * CBN);")
+        b_loads = "                    " + _ld("sB + stage * B_STAGE, &tm_b, fbar, k * BK, tn * BN + (int)rank * CBN",
+                                               bpol)
         b_desc = "                        const uint64_t bd = emmy::smem_desc_sw128(b_base + kk * 32, 16, 1024);"
     else:
         b_loads = "\n".join(
-            f"                    emmy::tma_load_2d_pair(sB + stage * B_STAGE + {j * 8192}u, &tm_b, fbar, "
-            f"tn * BN + (int)rank * CBN + {64 * j}, k * BK);" for j in range(cbn // 64))
+            "                    " + _ld(f"sB + stage * B_STAGE + {j * 8192}u, &tm_b, fbar, "
+                                          f"tn * BN + (int)rank * CBN + {64 * j}, k * BK", bpol)
+            for j in range(cbn // 64))
         b_desc = "                        const uint64_t bd = emmy::smem_desc_sw128(b_base + kk * 2048, 8192, 1024);"
     src = f"""{DEVICE_PRELUDE}
 #include <string.h>
@@ -640,7 +658,7 @@ def _gen_tcgen05_pair(kop, plan: GemmPlan, shapes, dtypes, args, ptrs, sig, para
 namespace {{
 constexpr long long M = {M}LL, N = {N}LL, K = {K}LL;
 constexpr int BM = {PAIR_BM}, CBM = {cbm}, BN = {BN}, CBN = {cbn}, BK = {BK}, STAGES = {PAIR_STAGES};
-constexpr int NB = {nb}, KB = {kb}, GROUP_M = {GROUP_M};
+constexpr int NB = {nb}, KB = {kb}, GROUP_M = {tn_['group_m']};
 constexpr uint32_t A_STAGE = {a_stage}u, B_STAGE = {b_stage}u;
 constexpr uint32_t SMEM_BYTES = {smem}u;
 constexpr uint32_t IDESC = emmy::idesc_f16({fmt}u, {0 if plan.b_nk else 1}u, BM, BN);
@@ -705,7 +723,7 @@ extern "C" __global__ void __launch_bounds__({TC_THREADS}, 1) {kop.name}({", ".j
     if (warp == 0) {{
         if (lane == 0) {{
             // ---------------- TMA producer (both CTAs; completion counted on the leader's barrier)
-            uint32_t stage = 0, phase = 0;
+{policies}            uint32_t stage = 0, phase = 0;
             uint32_t issued = 0u, parity_bits = 0u;
             bool ok = true;
             for (int t = pair; t < TILES && ok; t += npairs) {{
@@ -715,7 +733,7 @@ extern "C" __global__ void __launch_bounds__({TC_THREADS}, 1) {kop.name}({", ".j
                     if (!emmy::mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, EMMY_STATUS_TIMEOUT_PRODUCER, WAIT_NS)) {{ ok = false; break; }}
                     if (rank == 0) emmy::mbar_arrive_expect_tx(&full[stage], 2u * (A_STAGE + B_STAGE));
                     const uint32_t fbar = emmy::mapa(&full[stage], 0);
-                    emmy::tma_load_2d_pair(sA + stage * A_STAGE, &tm_a, fbar, k * BK, tm * BM + (int)rank * CBM);
+{a_load}
 {b_loads}
                     if (rank == 0) {{
                         issued |= 1u << stage;
