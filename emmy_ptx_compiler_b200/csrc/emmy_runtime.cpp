@@ -751,6 +751,48 @@ int emmy_launch_range(emmy_module_t m, const uint64_t *args, int nargs, uint64_t
     return launch_locked(m, args, nargs, nullptr, nullptr, stream, begin, end);
 }
 
+int emmy_shard_range(emmy_module_t m, int ndev, int d, uint64_t *begin, uint64_t *end) {
+    if (!m || ndev <= 0 || d < 0 || d >= ndev || !begin || !end)
+        return fail(EMMY_ERR_INVALID, "emmy_shard_range: bad argument");
+    if (!has_range(m)) return fail(EMMY_ERR_INVALID, "module takes no unit range (launch record has no EMMY_LR_RANGE)");
+    const uint64_t total = m->rec.range_total, al = m->rec.range_align ? m->rec.range_align : 1;
+    const uint64_t units = (total + al - 1) / al;  // aligned blocks, spread as evenly as possible
+    const uint64_t lo = units * static_cast<uint64_t>(d) / static_cast<uint64_t>(ndev);
+    const uint64_t hi = units * static_cast<uint64_t>(d + 1) / static_cast<uint64_t>(ndev);
+    *begin = std::min(total, lo * al);
+    *end = std::min(total, hi * al);
+    return EMMY_OK;
+}
+
+int emmy_launch_sharded(const emmy_module_t *mods, int ndev, const uint64_t *const *args, int nargs,
+                        const uint64_t *streams) {
+    if (!mods || ndev <= 0 || !args) return fail(EMMY_ERR_INVALID, "emmy_launch_sharded: NULL argument");
+    std::lock_guard<std::mutex> lk(g_mu);
+    for (int d = 0; d < ndev; ++d) {
+        emmy_module *m = mods[d];
+        if (!m || (nargs > 0 && !args[d])) return fail(EMMY_ERR_INVALID, "emmy_launch_sharded: NULL module or args");
+        if (!has_range(m))
+            return fail(EMMY_ERR_INVALID, "module takes no unit range (launch record has no EMMY_LR_RANGE)");
+        if (m->rec.range_total != mods[0]->rec.range_total || m->rec.nparams != mods[0]->rec.nparams)
+            return fail(EMMY_ERR_INVALID, "emmy_launch_sharded: modules of different kernels");
+    }
+    for (int d = 0; d < ndev; ++d) {
+        emmy_module *m = mods[d];
+        const uint64_t total = m->rec.range_total, al = m->rec.range_align ? m->rec.range_align : 1;
+        const uint64_t units = (total + al - 1) / al;
+        const uint64_t b = std::min(total, units * d / ndev * al), e = std::min(total, units * (d + 1) / ndev * al);
+        if (b == e) continue;
+        // a streamed parameter holds only this device's units: rebase it so that
+        // unit u sits at base + u * bytes_per_unit (modular 64-bit arithmetic)
+        std::vector<uint64_t> w(args[d], args[d] + nargs);
+        for (int i = 0; i < nargs && i < EMMY_LR_MAX_PARAMS; ++i)
+            if (m->rec.range_bytes[i] && m->rec.param_kind[i] == EMMY_PARAM_PTR) w[i] -= b * m->rec.range_bytes[i];
+        int rc = launch_locked(m, w.data(), nargs, nullptr, nullptr, streams ? streams[d] : 0, b, e);
+        if (rc) return rc;
+    }
+    return EMMY_OK;
+}
+
 int emmy_module_range(emmy_module_t m, uint64_t *total, uint32_t *align, uint64_t *bytes_per_unit, int nargs) {
     if (!m) return fail(EMMY_ERR_INVALID, "module is NULL");
     const bool r = has_range(m);

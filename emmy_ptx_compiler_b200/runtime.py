@@ -55,6 +55,8 @@ def _declare(lib) -> None:
         "emmy_time_launch": ([vp, P(u64), i32, i32, u64, P(C.c_float)], i32),
         "emmy_launch_range": ([vp, P(u64), i32, u64, u64, u64], i32),
         "emmy_module_range": ([vp, P(u64), P(u32), P(u64), i32], i32),
+        "emmy_shard_range": ([vp, i32, i32, P(u64), P(u64)], i32),
+        "emmy_launch_sharded": ([P(vp), i32, P(P(u64)), i32, P(u64)], i32),
         "emmy_sum_f32_noalloc": ([i32, u64, u64, u64, u64], i32),
         "emmy_comm_unique_id": ([P(C.c_uint8)], i32),
         "emmy_comm_init": ([i32, i32, i32, P(C.c_uint8), i32, P(vp)], i32),
@@ -73,7 +75,7 @@ EXPORTED = ("emmy_version", "emmy_last_error", "emmy_init", "emmy_device_count",
             "emmy_unload", "emmy_module_info", "emmy_launch", "emmy_module_status", "emmy_sync",
             "emmy_alloc", "emmy_free", "emmy_memcpy_htod", "emmy_memcpy_dtoh", "emmy_memset_d8",
             "emmy_host_alloc", "emmy_host_free", "emmy_run_host", "emmy_time_launch", "emmy_launch_range",
-            "emmy_module_range", "emmy_sum_f32_noalloc",
+            "emmy_module_range", "emmy_shard_range", "emmy_launch_sharded", "emmy_sum_f32_noalloc",
             "emmy_comm_unique_id", "emmy_comm_init", "emmy_allreduce_f32", "emmy_allgather_f32",
             "emmy_comm_destroy", "emmy_comm_abort")
 
@@ -200,6 +202,24 @@ class Module:
         sizes = (C.c_size_t * n)(*nbytes)
         rl = (C.c_uint8 * n)(*roles)
         _check(lib().emmy_run_host(self._h, ptrs, sizes, rl, n, C.c_uint64(stream)))
+
+
+def shard_range(module: "Module", ndev: int, d: int) -> tuple[int, int]:
+    """Units [begin, end) that device ``d`` of ``ndev`` processes in a sharded launch."""
+    b, e = C.c_uint64(0), C.c_uint64(0)
+    _check(lib().emmy_shard_range(module._h, ndev, d, C.byref(b), C.byref(e)))
+    return b.value, e.value
+
+
+def launch_sharded(modules: list["Module"], args_per_device: list[list], streams: list[int] | None = None) -> None:
+    """One launch split by unit range over the devices of ``modules`` (one
+    module per device); streamed parameters are each device's shard."""
+    n = len(modules)
+    mods = (C.c_void_p * n)(*[m._h.value for m in modules])
+    words = [(C.c_uint64 * max(1, len(a)))(*[arg_word(x) for x in a]) for a in args_per_device]
+    arr = (C.POINTER(C.c_uint64) * n)(*[C.cast(w, C.POINTER(C.c_uint64)) for w in words])
+    st = (C.c_uint64 * n)(*(streams or [0] * n))
+    _check(lib().emmy_launch_sharded(mods, n, arr, len(args_per_device[0]), st))
 
 
 def sum_f32_noalloc(x, n: int, out, device: int = 0, stream: int = 0) -> None:

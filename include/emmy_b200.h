@@ -119,6 +119,18 @@ int emmy_launch_range(emmy_module_t m, const uint64_t *args, int nargs, uint64_t
                       uint64_t stream);
 int emmy_module_range(emmy_module_t m, uint64_t *total, uint32_t *align, uint64_t *bytes_per_unit, int nargs);
 
+/* One launch split over `ndev` GPUs by unit range: the row / M split of the
+ * boundary's sharded launch.  mods[d] is the kernel's module loaded on device d
+ * (emmy_load(d, ...)); args[d] are that device's `nargs` parameter words.  A
+ * streamed parameter (bytes per unit > 0) points at device d's shard, which
+ * holds exactly its units [begin, end) from emmy_shard_range; every other
+ * parameter is complete on each device.  Device d gets units
+ * [floor(d*U/ndev), floor((d+1)*U/ndev)) of the U aligned blocks.  Launches are
+ * asynchronous on streams[d] (NULL: each device's default stream). */
+int emmy_shard_range(emmy_module_t m, int ndev, int d, uint64_t *begin, uint64_t *end);
+int emmy_launch_sharded(const emmy_module_t *mods, int ndev, const uint64_t *const *args, int nargs,
+                        const uint64_t *streams);
+
 /* Launch `iters` times back to back on `stream` between two CUDA events and
  * return the elapsed milliseconds (device time). */
 int emmy_time_launch(emmy_module_t m, const uint64_t *args, int nargs, int iters, uint64_t stream,
