@@ -58,6 +58,14 @@ CONFIGS = {
            "BASELINE configs[3]: sum of f32 [2^31]"),
     "c5": ("c5_gemm_full", "TFLOP/s", "tensor", 2 * 16384 * 16384 * 8192,
            "BASELINE configs[4]: relu(A@B + bias), A bf16 [16384, 8192], B bf16 [8192, 16384]"),
+    # fused row reduction + pointwise (the next row of the scope table, not a BASELINE config):
+    # algorithmic bytes = one read of x, one write of y (+ the weight vector)
+    "f_rmsnorm": ("f_rmsnorm_bench_16384x8192", "GB/s", "hbm", 2 * 16384 * 8192 * 4 + 8192 * 4,
+                  "row-fused rmsnorm: y = x * rsqrt(mean(x^2) + 1e-6) * w, x f32 [16384, 8192]"),
+    "f_softmax": ("f_softmax_bench_16384x8192", "GB/s", "hbm", 2 * 16384 * 8192 * 4,
+                  "row-fused softmax over rows of x f32 [16384, 8192]"),
+    "f_l2norm": ("f_l2norm_bench_16384x8192", "GB/s", "hbm", 2 * 16384 * 8192 * 4,
+                 "row-fused l2norm: y = x * rsqrt(sum(x^2) + 1e-12), x f32 [16384, 8192]"),
 }
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
@@ -272,7 +280,7 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     e2e_value = units * world * e2e_steps / e2e_s / (1e9 if unit == "GB/s" else 1e12)
 
     ref_ptx = None
-    if rank == 0 and world == 1 and args.config == "c2" and not args.no_ref_ptx:
+    if rank == 0 and world == 1 and (args.config == "c2" or args.config.startswith("f_")) and not args.no_ref_ptx:
         ref_ptx = time_reference_ptx(spec, bufs, local, units, unit)
 
     mod.close()

@@ -27,7 +27,7 @@ from pathlib import Path
 
 from . import frontend, ir, toolchain
 from .errors import ToolchainError, UnsupportedIR
-from .families import gemm, pointwise, reduction
+from .families import gemm, pointwise, reduction, rownorm
 from .families.common import KernelSource
 
 
@@ -71,6 +71,10 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
     plan = reduction.match(kop, shapes, dtypes)
     if plan is not None:
         ks = reduction.generate(kop, plan, shapes, dtypes, args, scalars, written)
+        return Lowered(ks, args, shapes, dtypes, meta)
+    plan = rownorm.match(kop, shapes, dtypes)
+    if plan is not None:
+        ks = rownorm.generate(kop, plan, shapes, dtypes, args, scalars, written)
         return Lowered(ks, args, shapes, dtypes, meta)
     plan = pointwise.match(kop)
     if plan is not None:

@@ -33,7 +33,12 @@
 #define EMMY_LR_MAX_PARAMS 32
 #define EMMY_LR_MAX_TMAPS 4
 
-enum EmmyFamily { EMMY_FAMILY_POINTWISE = 1, EMMY_FAMILY_REDUCTION = 2, EMMY_FAMILY_GEMM = 3 };
+enum EmmyFamily {
+    EMMY_FAMILY_POINTWISE = 1,
+    EMMY_FAMILY_REDUCTION = 2,
+    EMMY_FAMILY_GEMM = 3,
+    EMMY_FAMILY_ROWFUSED = 4 /* row reductions + pointwise pass in one kernel */
+};
 
 enum EmmyParamKind { EMMY_PARAM_PTR = 0, EMMY_PARAM_F32 = 1, EMMY_PARAM_I32 = 2 };
 

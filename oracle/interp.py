@@ -683,7 +683,9 @@ def evaluate(kop, shapes: dict, dtypes: dict, inputs: dict[str, np.ndarray],
     axes = _axes(tile)
     strided = [s for s in stmts if isinstance(s, StridedLoop)]
     loops = [s for s in stmts if isinstance(s, Loop)]
-    if strided:
+    if len(strided) > 1 or (strided and not any(isinstance(t, Accum) for t in ir_walk(strided[0].body))):
+        _eval_phases(tile, stmts, axes, bufs, shapes, dtypes)
+    elif strided:
         _eval_strided(tile, stmts, axes, strided[0], bufs, shapes, dtypes)
     elif loops and _is_matmul(loops[0]):
         _eval_matmul(tile, stmts, axes, loops[0], bufs, shapes, dtypes)
@@ -823,6 +825,81 @@ def _eval_strided(tile, stmts, axes, loop, bufs, shapes, dtypes):
     for name, v in results.items():
         pm.env[name] = ("f32", v)
     pm.run(post)
+
+
+def ir_walk(body):
+    for t in body:
+        yield t
+        for child in t.nested():
+            yield from ir_walk(child)
+
+
+def _eval_phases(tile, stmts, axes, bufs, shapes, dtypes):
+    """Block-per-row kernels with several strided passes over the row (fused
+    reduction + pointwise: rmsnorm, softmax, l2norm).  Each reduction pass is
+    the strided warp/tree schedule in the reference's exact order (as in
+    ``_eval_strided``) and leaves its result in every thread; statements
+    between passes are per-row scalars; a pass without Accum is pointwise over
+    the row's elements and writes the output."""
+    co, bt = axes[-1]
+    row_axes = axes[:-1]
+    rows = int(np.prod([e for _, e in row_axes])) if row_axes else 1
+    smem = {t.name for t in stmts if isinstance(t, Smem)}
+    pm = Cells(rows, bufs, shapes, dtypes)
+    pm.count_uses(stmts)
+    for k, v in _cells_for(row_axes, rows).items():
+        pm.env[k] = ("int", v)
+    opcode = {"add": 0, "sum": 0, "maximum": 1, "amax": 1, "max": 1, "minimum": 2, "amin": 2, "min": 2,
+              "multiply": 3}
+    row_stmts: list = []
+
+    def flush():
+        if row_stmts:
+            pm.run(list(row_stmts))
+            row_stmts.clear()
+
+    for s in stmts:
+        if isinstance(s, (WarpShuffle, TreeHalve, Smem, Sync)):
+            continue
+        if isinstance(s, Cond):
+            inner = list(s.body) + list(s.else_body)
+            if inner and all(isinstance(t, Write) and t.output in smem for t in inner):
+                continue
+            c = s.cond
+            if isinstance(c, BinaryExpr) and c.op == "==" and isinstance(c.left, Var) and c.left.name == co:
+                row_stmts.extend(s.body)
+                continue
+        if not isinstance(s, StridedLoop):
+            row_stmts.append(s)
+            continue
+        flush()
+        K = int(s.axis.extent.value) if s.end is None else int(s.end.value)
+        n = rows * K
+        m = Cells(n, bufs, shapes, dtypes)
+        m.count_uses(stmts)
+        for k, v in _cells_for(row_axes + [(s.axis.name, K)], n).items():
+            m.env[k] = ("int", v)
+        row_of = np.arange(n, dtype=np.int64) // K
+        for name, (kind, v) in pm.env.items():
+            if name not in m.env:
+                v = np.asarray(v)
+                m.env[name] = (kind, v[row_of] if v.ndim == 1 and v.shape[0] == rows else v)
+        body = list(s.body)
+        accs = [t for t in body if isinstance(t, Accum)]
+        m.run([t for t in body if not isinstance(t, Accum)])
+        for acc in accs:
+            pv = m.product(acc.value) if opname(acc.op) in ("add", "sum") else None
+            out = np.empty(rows, F32)
+            if pv is not None:
+                xs = np.ascontiguousarray(np.broadcast_to(pv[0], (n,)), F32)
+                ys = np.ascontiguousarray(np.broadcast_to(pv[1], (n,)), F32)
+                lib().ora_strided_reduce_f32(_p(xs), _p(ys), rows, K, bt, 4, F32(0.0), _p(out))
+            else:
+                xs = np.ascontiguousarray(np.broadcast_to(m.f32(acc.value), (n,)), F32)
+                lib().ora_strided_reduce_f32(_p(xs), None, rows, K, bt, opcode[opname(acc.op)],
+                                             F32(identity_of(acc.op)), _p(out))
+            pm.bind(acc.name, "f32", out)
+    flush()
 
 
 def make_inputs(mk: dict, shapes: dict, dtypes: dict) -> dict[str, np.ndarray]:

@@ -36,7 +36,7 @@ def case_index() -> list[dict]:
 def small_cases(family: str | None = None) -> list[str]:
     out = []
     for c in case_index():
-        if c["id"].endswith("_full") or "2p28" in c["id"] or "_prof_" in c["id"]:
+        if c["id"].endswith("_full") or "2p28" in c["id"] or "_prof_" in c["id"] or "_bench_" in c["id"]:
             continue
         if family and c["family"] != family:
             continue

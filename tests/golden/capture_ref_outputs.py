@@ -42,7 +42,7 @@ def main() -> int:
     done = {}
     for rec in index:
         cid = rec["id"]
-        if cid.endswith("_full") or "2p28" in cid or "_prof_" in cid:
+        if cid.endswith("_full") or "2p28" in cid or "_prof_" in cid or "_bench_" in cid:
             continue
         d = HERE / "cases" / cid
         ref_dir = d if (d / "ref.ptx").is_file() else (d / "ref_f32" if (d / "ref_f32" / "ref.ptx").is_file() else None)

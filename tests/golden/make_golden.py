@@ -266,6 +266,86 @@ def _reduce_body(red_axis: Axis, start: str, index, accs: list[tuple[str, str]],
     )
 
 
+def _tree_phase(red_axis: Axis, start: str, body: tuple, acc: str, op: str) -> tuple:
+    """One reduction phase of the strided warp/tree schedule whose result every
+    thread of the block holds afterwards (TreeHalve re-reads the root slot,
+    compile.py:2271-2277)."""
+    comb = (Assign(acc, EW(op), (acc, f"{acc}__o"), None),)
+    return (
+        StridedLoop(axis=red_axis, start=Var(start), step=Literal(BT, "int"), body=body, seed=True),
+        WarpShuffle(state=(acc,), state_b=(f"{acc}__o",), combine_states=comb, length=32, dtype=F32),
+        Smem(f"{acc}_smem", (BT // 32,), "float", 0),
+        Cond(BinaryExpr("==", Var("lane"), Literal(0, "int")),
+             body=(Write(output=f"{acc}_smem", index=(Var("warp"),), values=(acc,), value_dtype=F32),)),
+        Sync(),
+        TreeHalve(bufs=(f"{acc}_smem",), state=(acc,), state_b=(f"{acc}__o",), combine_states=comb,
+                  length=BT // 32, tid_var="warp", dtype=F32),
+    )
+
+
+def rownorm_case(cid: str, rows: int, cols: int, kind: str, *, config: str | None = None) -> Case:
+    """Fused row reduction + pointwise epilogue, the rmsnorm / softmax / l2norm
+    class (the reference's f01-f03): one block per row runs one or two
+    reduction phases on the warp/tree schedule, then a strided pass that
+    rereads the row and writes the normalised values."""
+    ax = Axis("a1", Dim(cols))
+    idx = (Var("a0"), Var("a1"))
+    ld = lambda nm: Load(names=(nm,), input="x", index=idx, dtype=F32)  # noqa: E731
+    ins = ["x"]
+    if kind == "rmsnorm":
+        entry = "k_rmsnorm"
+        ins = ["x", "w"]
+        phases = _tree_phase(ax, "a1_co", (ld("in0"), Assign("sq", EW("multiply"), ("in0", "in0"), F32),
+                                           Accum("acc0", "sq", EW("add"), F32, axes=("a1",))), "acc0", "add")
+        mid = (Let("inv_n", Literal(1.0 / cols, "float"), F32),
+               Assign("ms", EW("multiply"), ("acc0", "inv_n"), F32),
+               Let("eps", Literal(1e-6, "float"), F32),
+               Assign("mse", EW("add"), ("ms", "eps"), F32),
+               Assign("r", EW("rsqrt"), ("mse",), F32))
+        tail = (ld("in1"), Load(names=("wv",), input="w", index=(Var("a1"),), dtype=F32),
+                Assign("xr", EW("multiply"), ("in1", "r"), F32),
+                Assign("yv", EW("multiply"), ("xr", "wv"), F32))
+    elif kind == "softmax":
+        entry = "k_softmax"
+        phases = _tree_phase(ax, "a1_co", (ld("in0"), Accum("acc0", "in0", EW("maximum"), F32, axes=("a1",))),
+                             "acc0", "maximum")
+        phases += _tree_phase(ax, "a1_co", (ld("in1"), Assign("d1", EW("subtract"), ("in1", "acc0"), F32),
+                                            Assign("e1", EW("exp"), ("d1",), F32),
+                                            Accum("acc1", "e1", EW("add"), F32, axes=("a1",))), "acc1", "add")
+        mid = ()
+        tail = (ld("in2"), Assign("d2", EW("subtract"), ("in2", "acc0"), F32),
+                Assign("e2", EW("exp"), ("d2",), F32),
+                Assign("yv", EW("divide"), ("e2", "acc1"), F32))
+    elif kind == "l2norm":
+        entry = "k_l2norm"
+        phases = _tree_phase(ax, "a1_co", (ld("in0"), Assign("sq", EW("multiply"), ("in0", "in0"), F32),
+                                           Accum("acc0", "sq", EW("add"), F32, axes=("a1",))), "acc0", "add")
+        mid = (Let("eps", Literal(1e-12, "float"), F32),
+               Assign("se", EW("add"), ("acc0", "eps"), F32),
+               Assign("r", EW("rsqrt"), ("se",), F32))
+        tail = (ld("in1"), Assign("yv", EW("multiply"), ("in1", "r"), F32))
+    else:
+        raise ValueError(kind)
+    final = StridedLoop(axis=ax, start=Var("a1_co"), step=Literal(BT, "int"),
+                        body=tail + (Write(output="y", index=idx, values=("yv",), value_dtype=F32),))
+    body = Tile(axes=(Axis("a0", Dim(rows)), Axis("a1_co", Dim(BT))), body=phases + mid + (final,),
+                block_threads=BT)
+    nodes = {"x": _input("x", [rows, cols])}
+    if "w" in ins:
+        nodes["w"] = _input("w", [cols])
+    nodes["y"] = _kernel(entry, body, ins, [("y", [rows, cols], "f32")])
+    graph = {"inputs": ins, "outputs": ["y"], "nodes": nodes}
+    args = [_arg("x", [rows, cols], init=NORM(), seed=0)]
+    if "w" in ins:
+        args.append(_arg("w", [cols], init=UNIF(0.5, 1.5), seed=1))
+    args.append(_arg("y", [rows, cols], output=True))
+    kern = _meta_kernel("y", entry, ins + ["y"], [rows, 1, 1], [BT, 1, 1], args)
+    # every kind uses an approximate instruction (rsqrt.approx, ex2.approx): the
+    # oracle's libm stand-ins pin it within APPROX_ORACLE, not bit for bit
+    check = {"kind": "rtol", "rtol": 1e-5, "atol": 1e-6, "oracle": APPROX_ORACLE}
+    return Case(cid, entry, graph, kern, family="rownorm", config=config, check=check)
+
+
 def rowsummax_case(cid: str, rows: int, cols: int, *, config: str | None = None) -> Case:
     """row sum and row max of x[rows, cols] in one pass."""
     entry = "k_row_sum_max_reduce"
@@ -739,6 +819,12 @@ def all_cases() -> list[Case]:
                      ("contract_log_add", 1000), ("contract_two_products", 1000), ("contract_cond", 1000),
                      ("contract_two_products_swapped", 1000)):
         cases.append(chain_case(f"p_{which}_{n}", n, which))
+    # fused row reduction + pointwise epilogue (rmsnorm / softmax / l2norm)
+    for kind in ("rmsnorm", "softmax", "l2norm"):
+        cases.append(rownorm_case(f"f_{kind}_64x1000", 64, 1000, kind))
+        cases.append(rownorm_case(f"f_{kind}_7x4096", 7, 4096, kind))
+        cases.append(rownorm_case(f"f_{kind}_33x130", 33, 130, kind))
+        cases.append(rownorm_case(f"f_{kind}_bench_16384x8192", 16384, 8192, kind, config=f"f_{kind}"))
     cases.append(add2d_case("p_add2d_7x13", 7, 13))
     cases.append(add2d_case("p_add2d_32x64", 32, 64))
     cases.append(vec4_case("p_vec4_1024", 1024))
