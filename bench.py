@@ -66,7 +66,13 @@ CONFIGS = {
                   "row-fused softmax over rows of x f32 [16384, 8192]"),
     "f_l2norm": ("f_l2norm_bench_16384x8192", "GB/s", "hbm", 2 * 16384 * 8192 * 4,
                  "row-fused l2norm: y = x * rsqrt(sum(x^2) + 1e-12), x f32 [16384, 8192]"),
+    # naive-attention IR, f32 on CUDA cores (exact reference arithmetic): algorithmic FLOP =
+    # q.k^T and p.v once each, 2 * 2 * seq^2 * dim
+    "a_attn": ("a_attn_bench_2048x64", "TFLOP/s", "fp32", 4 * 2048 * 2048 * 64,
+               "naive attention softmax(q k^T / sqrt(64)) v, q,k,v f32 [2048, 64]"),
 }
+# nominal FP32 CUDA-core peak: 148 SMs x 128 lanes x 2 FLOP x 1.965 GHz
+FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -253,6 +259,9 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     achieved = units / (per_launch_ms / 1e3) / (1e9 if unit == "GB/s" else 1e12)
     pk, pk_kind = peaks()
     peak = pk["hbm_gbs"] if bound == "hbm" else pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+    if bound == "fp32":
+        peak, pk_kind = round(FP32_NOMINAL_TFLOPS, 1), "nominal"
+    peak_key = {"hbm": "hbm_gbs", "tensor": "bf16_tflops", "fp32": "fp32 CUDA cores"}[bound]
     traffic = DRAM_TRAFFIC.get(case_id)
 
     # e2e: the C-ABI host-buffer call, copies in the timed region
@@ -280,7 +289,8 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     e2e_value = units * world * e2e_steps / e2e_s / (1e9 if unit == "GB/s" else 1e12)
 
     ref_ptx = None
-    if rank == 0 and world == 1 and (args.config == "c2" or args.config.startswith("f_")) and not args.no_ref_ptx:
+    if rank == 0 and world == 1 and (args.config == "c2" or args.config[:2] in ("f_", "a_")) \
+            and not args.no_ref_ptx:
         ref_ptx = time_reference_ptx(spec, bufs, local, units, unit)
 
     mod.close()
@@ -297,7 +307,7 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
                    "launch": launch},
         "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": peak,
                      "unit": unit, "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "peak_source": f"{pk_kind} ({'hbm_gbs' if bound == 'hbm' else 'bf16_tflops'})",
+                     "peak_source": f"{pk_kind} ({peak_key})",
                      "units_per_launch": units},
         "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,

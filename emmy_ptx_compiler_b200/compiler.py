@@ -27,7 +27,7 @@ from pathlib import Path
 
 from . import frontend, ir, toolchain
 from .errors import ToolchainError, UnsupportedIR
-from .families import gemm, pointwise, reduction, rownorm
+from .families import attention, gemm, pointwise, reduction, rownorm
 from .families.common import KernelSource
 
 
@@ -63,6 +63,10 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
     for name in args:
         if name not in scalars and name not in shapes and name not in dtypes:
             raise UnsupportedIR(f"parameter {name!r} has no shape or dtype")
+    plan = attention.match(kop, shapes, dtypes)
+    if plan is not None:
+        ks = attention.generate(kop, plan, shapes, dtypes, args, scalars, written)
+        return Lowered(ks, args, shapes, dtypes, meta)
     plan = gemm.match(kop, shapes, dtypes)
     if plan is not None:
         ks = gemm.generate(kop, plan, shapes, dtypes, args, scalars, written,

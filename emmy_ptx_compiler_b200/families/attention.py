@@ -1,0 +1,531 @@
+"""Attention family: ``out[i, j] = sum_k w(i, k) * v[k, j]`` where ``w`` comes
+from per-key passes over the scores ``s(i, k) = sum_d q[i, d] * kt[d, k]``.
+
+Recognises the naive attention IR (tools/make_proxy_set.py:416-474; lowered
+by the reference with compile.py:1813-1864 for every ``Loop``): a Tile over
+``(i, j)`` with one thread per output cell, whose body is a sequence of key
+loops.  Each key loop recomputes the dot product ``s(i, k)`` with an inner
+``Loop`` over ``d`` and then runs a few per-key statements, accumulating
+either a per-row value (the row max, the softmax denominator) or the output
+cell (the weighted sum of ``v[k, j]``).  Per-row statements (``Init``,
+``Let``, ``Assign``, e.g. the reciprocal of the denominator) sit between the
+loops, and a final ``Write out[i, j]``.
+
+The reference recomputes every score ``3 x |j|`` times (once per pass and per
+output column).  Here a CTA owns ``BQ`` query rows and walks the keys in
+tiles of ``BK``:
+
+* all threads compute the tile's ``BQ x BK`` dot products once, sequentially
+  over ``d`` with ``fma.rn`` as the reference does, from shared-memory tiles
+  of ``q`` and ``kt``; the per-key statements that do not depend on ``j``
+  run right there, once per (row, key);
+* row accumulations (max, sum) then run in key order by one thread per row,
+  so every sum is added in the reference's order;
+* the statements that depend on ``j`` (the ``v[k, j]`` product) run in key
+  order in the threads that own the output cells, reading ``v`` from a
+  shared-memory tile.
+
+Every value is computed with the reference's op table in the reference's
+order, FMA contraction included, so results match the reference's PTX to
+rounding of its approximate instructions.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+from .. import ir
+from ..cgen import DEVICE_PRELUDE, Emitter, combine_code, ctype, f32_lit, fusable_products, identity_of
+from ..errors import UnsupportedIR
+from .common import KernelSource, LaunchPlan, ParamSpec, SM_COUNT, launch_record_source
+
+THREADS = 256
+BK = 64
+SCORE_CACHE_BYTES = 96 * 1024  # scores of a CTA's rows kept in shared memory across passes
+_COMBINE = {"add": "add", "sum": "add", "maximum": "maximum", "amax": "maximum", "max": "maximum",
+            "minimum": "minimum", "amin": "minimum", "min": "minimum"}
+
+
+@dataclass
+class KeyLoop:
+    loop: ir.Loop
+    dot_acc: str            # accumulator of the inner dot product
+    dot_init: float
+    post: list              # statements after the dot loop
+    indep: list             # post statements that do not depend on j
+    dep: list               # post statements that depend on j (run by the output owners)
+    row_accs: list          # (name, combine op): Accums of j-independent values into per-row state
+    stash: list             # j-independent names read by dep statements
+
+
+@dataclass
+class AttnPlan:
+    i: str
+    j: str
+    SQ: int
+    DV: int
+    SK: int
+    D: int
+    q: str
+    kmat: str
+    k_dk: bool              # keys stored [D, SK] (kt) rather than [SK, D]
+    v: str | None
+    steps: list             # KeyLoop | ("row", stmt)
+    out: ir.Write
+    out_name: str
+    cell_accs: list         # names accumulated per output cell
+    notes: dict = field(default_factory=dict)
+
+
+def _names(index) -> list[str] | None:
+    out = []
+    for ix in index:
+        if not isinstance(ix, ir.Var):
+            return None
+        out.append(ix.name)
+    return out
+
+
+def _defs(t) -> list[str]:
+    if isinstance(t, ir.Load):
+        return list(t.names)
+    if isinstance(t, (ir.Assign, ir.Let, ir.Init, ir.Accum, ir.Select)):
+        return [t.name]
+    return []
+
+
+def match(kop: ir.KernelOp, shapes: dict, dtypes: dict) -> AttnPlan | None:
+    body = ir.body_stmts(kop.body)
+    if len(body) != 1 or not isinstance(body[0], ir.Tile):
+        return None
+    tile = body[0]
+    if len(tile.axes) != 2:
+        return None
+    (i, SQ), (j, DV) = [(a.name, a.size) for a in tile.axes]
+    stmts = list(ir.body_stmts(tile.body))
+    loops = [s for s in stmts if isinstance(s, ir.Loop)]
+    if len(loops) < 2 or not all(any(isinstance(t, ir.Loop) for t in lp.body) for lp in loops):
+        return None
+    q = kmat = v = None
+    k_dk = None
+    SK = D = None
+    steps: list = []
+    jdep: set[str] = {j}
+    cell_accs: list[str] = []
+    for s in stmts:
+        if isinstance(s, ir.Loop):
+            kname = s.axis.name
+            ext = s.axis.size
+            if SK is None:
+                SK = ext
+            elif SK != ext:
+                return None
+            lb = list(s.body)
+            inner = [t for t in lb if isinstance(t, ir.Loop)]
+            if len(inner) != 1:
+                return None
+            dl = inner[0]
+            pos = lb.index(dl)
+            pre = lb[:pos]
+            if len(pre) != 1 or not isinstance(pre[0], ir.Init):
+                return None
+            dot_acc = pre[0].name
+            dname = dl.axis.name
+            if D is None:
+                D = dl.axis.size
+            elif D != dl.axis.size:
+                return None
+            dbody = list(dl.body)
+            loads = [t for t in dbody if isinstance(t, ir.Load)]
+            accs = [t for t in dbody if isinstance(t, ir.Accum)]
+            mults = [t for t in dbody if isinstance(t, ir.Assign)]
+            if len(loads) != 2 or len(accs) != 1 or len(dbody) != 4 or len(mults) != 1:
+                return None
+            mul, acc = mults[0], accs[0]
+            if ir.op_name(mul.op) not in ("multiply", "mul") or ir.op_name(acc.op) not in ("add", "sum"):
+                return None
+            if acc.name != dot_acc or acc.value != mul.name or acc.base not in (None, acc.name):
+                return None
+            if dbody.index(mul) + 1 != dbody.index(acc):
+                return None                      # the reference fuses this pair into fma.rn
+            lq = lk = None
+            for ld in loads:
+                nm = _names(ld.index)
+                if nm == [i, dname]:
+                    lq = ld
+                elif nm in ([dname, kname], [kname, dname]):
+                    lk = ld
+            if lq is None or lk is None or sorted(mul.args) != sorted([lq.names[0], lk.names[0]]):
+                return None
+            kd = _names(lk.index) == [dname, kname]
+            if q is None:
+                q, kmat, k_dk = lq.input, lk.input, kd
+            elif (q, kmat, k_dk) != (lq.input, lk.input, kd):
+                return None
+            post = lb[pos + 1:]
+            indep, dep, row_accs = [], [], []
+            local_dep: set[str] = set()
+            for t in post:
+                if not isinstance(t, (ir.Let, ir.Assign, ir.Accum, ir.Load)):
+                    return None
+                reads = set(t.reads())
+                if isinstance(t, ir.Load):
+                    nm = _names(t.index)
+                    if nm == [kname, j]:
+                        if v is None:
+                            v = t.input
+                        elif v != t.input:
+                            return None
+                        local_dep |= set(t.names)
+                        dep.append(t)
+                        continue
+                    if nm not in ([kname], [i], [i, kname]) and t.index:
+                        return None
+                if isinstance(t, ir.Accum):
+                    if t.base not in (None, t.name):
+                        return None
+                    if (reads - {t.name}) & (local_dep | jdep) or t.name in cell_accs:
+                        if ir.op_name(t.op) not in ("add", "sum"):
+                            return None
+                        if t.name not in cell_accs:
+                            cell_accs.append(t.name)
+                        dep.append(t)
+                        jdep.add(t.name)
+                        continue
+                    op = _COMBINE.get(ir.op_name(t.op))
+                    if op is None:
+                        return None
+                    row_accs.append((t.name, op))
+                    continue
+                if reads & (local_dep | jdep):
+                    local_dep |= set(_defs(t))
+                    dep.append(t)
+                else:
+                    indep.append(t)
+            if any(isinstance(t, ir.Accum) for t in indep):
+                return None
+            own = {a for a, _ in row_accs}
+            if any(set(t.reads()) & own for t in indep + [t for t in dep if not isinstance(t, ir.Accum)]):
+                return None                      # reads a row value while it is still accumulating
+            dep_reads = set()
+            for t in dep:
+                dep_reads |= set(t.reads())
+            stash = [n for n in dict.fromkeys(n for t in indep for n in _defs(t)) if n in dep_reads]
+            if dot_acc in dep_reads:
+                stash.append(dot_acc)
+            steps.append(KeyLoop(s, dot_acc, float(pre[0].identity), post, indep, dep, row_accs, stash))
+            continue
+        if isinstance(s, ir.Write):
+            continue
+        if not isinstance(s, (ir.Init, ir.Let, ir.Assign)):
+            return None
+        if set(s.reads()) & jdep:
+            return None
+        steps.append(("row", s))
+    writes = [s for s in stmts if isinstance(s, ir.Write)]
+    if len(writes) != 1 or stmts[-1] is not writes[0]:
+        return None
+    w = writes[0]
+    if _names(w.index) != [i, j] or len(w.values) != 1 or w.atomic:
+        return None
+    if tuple(shapes.get(w.output, ())) != (SQ, DV):
+        return None
+    if tuple(shapes.get(q, ())) != (SQ, D):
+        return None
+    if tuple(shapes.get(kmat, ())) != ((D, SK) if k_dk else (SK, D)):
+        return None
+    if v is not None and tuple(shapes.get(v, ())) != (SK, DV):
+        return None
+    for nm in (q, kmat, v, w.output):
+        if nm is not None and ir.canon_dtype(dtypes.get(nm)) != "f32":
+            raise UnsupportedIR(f"attention on {dtypes.get(nm)} tensor {nm!r} (f32 only)")
+    if D > 256 or DV > 256:
+        raise UnsupportedIR(f"attention head sizes {D}/{DV} above 256")
+    return AttnPlan(i, j, SQ, DV, SK, D, q, kmat, k_dk, v, steps, w, w.output, cell_accs)
+
+
+def _c(name: str) -> str:
+    import re
+    return re.sub(r"[^A-Za-z0-9_]", "_", name)
+
+
+def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args: list[str],
+             scalars: dict[str, str], written: set[str]) -> KernelSource:
+    params: list[ParamSpec] = []
+    ptrs: dict[str, str] = {}
+    sig: list[str] = []
+    for name in args:
+        if name in scalars:
+            sig.append(f"{ctype(scalars[name])} p_{_c(name)}")
+            params.append(ParamSpec(name, "scalar", scalars[name]))
+            continue
+        dt = ir.canon_dtype(dtypes.get(name))
+        const = "" if name in written else "const "
+        sig.append(f"{const}{ctype(dt)}* __restrict__ p_{_c(name)}")
+        ptrs[name] = f"p_{_c(name)}"
+        params.append(ParamSpec(name, "ptr", dt))
+    sig += ["unsigned long long emmy_rb", "unsigned long long emmy_re"]
+    scalar_env = {n: (("f32", f"p_{_c(n)}") if scalars[n] == "f32" else ("int", f"(long long)p_{_c(n)}"))
+                  for n in scalars}
+    SQ, DV, SK, D = plan.SQ, plan.DV, plan.SK, plan.D
+    BQ = 16 if -(-SQ // 16) >= 2 * SM_COUNT else (8 if -(-SQ // 8) >= SM_COUNT else 4)
+    T = THREADS
+    fus = fusable_products(kop.body)
+    # per-row names: top-level statements and row accumulators (kept in shared memory per row)
+    row_names: list[str] = []
+    for st in plan.steps:
+        if isinstance(st, KeyLoop):
+            for a, _ in st.row_accs:
+                if a not in row_names:
+                    row_names.append(a)
+        else:
+            for n in _defs(st[1]):
+                if n not in row_names and n not in plan.cell_accs:
+                    row_names.append(n)
+    nstash = max([len(st.stash) for st in plan.steps if isinstance(st, KeyLoop)] + [0])
+    nfac = max([len(st.row_accs) for st in plan.steps if isinstance(st, KeyLoop)] + [0])
+    # shared memory layout (floats)
+    q_stride = D + 1
+    s_stride = BK + 1
+    off = {}
+    cur = 0
+
+    def alloc(name, n):
+        nonlocal cur
+        off[name] = cur
+        cur += n
+
+    alloc("qs", BQ * q_stride)
+    alloc("ks", D * BK)
+    alloc("vs", BK * DV if plan.v else 1)
+    alloc("rowv", max(1, len(row_names)) * BQ)
+    alloc("acca", max(1, nfac) * BQ * s_stride)   # accumulate operand (or first factor) per (row, key)
+    alloc("accb", max(1, nfac) * BQ * s_stride)   # second factor when the accumulate is an fma
+    alloc("stash", max(1, nstash) * BQ * s_stride)
+    # every key loop computes the same dot products: keep the first pass's scores for the rest
+    keyloops = [st for st in plan.steps if isinstance(st, KeyLoop)]
+    cache = len(keyloops) > 1 and len({st.dot_init for st in keyloops}) == 1 and BQ * (SK + 1) * 4 <= SCORE_CACHE_BYTES
+    if cache:
+        alloc("scache", BQ * (SK + 1))
+    smem_bytes = cur * 4
+    lines: list[str] = []
+    w = lines.append
+    w(DEVICE_PRELUDE)
+    w('#include "emmy_launch_record.h"')
+    w('extern "C" __device__ unsigned int emmy_status;')
+    w(f'extern "C" __global__ void __launch_bounds__({T}) {kop.name}(' + ", ".join(sig) + ") {")
+    w(f"    constexpr int SQ = {SQ}, DV = {DV}, SK = {SK}, D = {D}, BQ = {BQ}, BK = {BK};")
+    w(f"    constexpr int QS = {q_stride}, SS = {s_stride};")
+    w("    extern __shared__ __align__(16) float sm[];")
+    for name, o in off.items():
+        w(f"    float *const {name} = sm + {o};")
+    w(f"    uint32_t dyn_smem;")
+    w('    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn_smem));')
+    w(f"    if (blockDim.x != {T} || blockDim.y != 1 || blockDim.z != 1 || dyn_smem < {smem_bytes}u) {{")
+    w("        if (threadIdx.x == 0 && threadIdx.y == 0 && threadIdx.z == 0) atomicOr(&emmy_status, EMMY_STATUS_BAD_LAUNCH);")
+    w("        return;")
+    w("    }")
+    w("    const int tid = threadIdx.x;")
+    w("    const long long RB = (long long)(emmy_rb < (unsigned long long)SQ ? emmy_rb : SQ);")
+    w("    const long long RE = (long long)(emmy_re < (unsigned long long)SQ ? emmy_re : SQ);")
+    w("    for (long long q0 = RB + (long long)blockIdx.x * BQ; q0 < RE; q0 += (long long)gridDim.x * BQ) {")
+    w("        const int nq = (RE - q0) < BQ ? (int)(RE - q0) : BQ;")
+    w(f"        for (int e = tid; e < BQ * D; e += {T}) {{")
+    w("            const int r = e / D, d = e - r * D;")
+    w(f"            qs[r * QS + d] = r < nq ? {ptrs[plan.q]}[(q0 + r) * D + d] : 0.0f;")
+    w("        }")
+    # output cell accumulators: thread owns cells o = tid + u*T of the BQ x DV block
+    nown = -(-(BQ * DV) // T)
+    for a in plan.cell_accs:
+        w(f"        float cacc_{_c(a)}[{nown}];")
+    row_slot = {n: k for k, n in enumerate(row_names)}
+
+    def row_ref(n: str, r: str) -> str:
+        return f"rowv[{row_slot[n]} * BQ + {r}]"
+
+    ind = "        "
+    for st in plan.steps:
+        if not isinstance(st, KeyLoop):
+            s = st[1]
+            # per-row statement: thread r < BQ computes it for row r
+            if isinstance(s, ir.Init) and s.name in plan.cell_accs:
+                for u in range(nown):
+                    w(f"{ind}cacc_{_c(s.name)}[{u}] = {f32_lit(float(s.identity))};")
+                continue
+            w(f"{ind}__syncthreads();")
+            w(f"{ind}if (tid < BQ) {{")
+            em = Emitter(shapes, dtypes, ptrs, indent=ind + "    ")
+            em.fusable = fus
+            em.env.update(scalar_env)
+            em.bind_const(plan.i, "int", "(q0 + tid)")
+            for n in row_names:
+                if n in row_slot and _row_defined(plan, n, st):
+                    em.env[n] = ("f32", row_ref(n, "tid"))
+            em.run((s,))
+            w("\n".join(em.lines))
+            for n in _defs(s):
+                if n in row_slot:
+                    w(f"{ind}    {row_ref(n, 'tid')} = {em.as_f32(n)};")
+            w(f"{ind}}}")
+            continue
+        w(f"{ind}__syncthreads();")
+        # row accumulators start from their Init (held in rowv by the row statements)
+        w(f"{ind}for (int k0 = 0; k0 < SK; k0 += BK) {{")
+        i2 = ind + "    "
+        w(f"{i2}const int nk = (SK - k0) < BK ? (SK - k0) : BK;")
+        w(f"{i2}__syncthreads();")
+        reuse = cache and st is not keyloops[0]
+        if reuse:
+            pass
+        elif plan.k_dk:
+            w(f"{i2}for (int e = tid; e < D * BK; e += {T}) {{")
+            w(f"{i2}    const int d = e / BK, kk = e - d * BK;")
+            w(f"{i2}    ks[d * BK + kk] = kk < nk ? {ptrs[plan.kmat]}[(long long)d * SK + k0 + kk] : 0.0f;")
+            w(f"{i2}}}")
+        else:
+            w(f"{i2}for (int e = tid; e < D * BK; e += {T}) {{")
+            w(f"{i2}    const int kk = e / D, d = e - kk * D;")
+            w(f"{i2}    ks[d * BK + kk] = kk < nk ? {ptrs[plan.kmat]}[(long long)(k0 + kk) * D + d] : 0.0f;")
+            w(f"{i2}}}")
+        if st.dep and plan.v:
+            w(f"{i2}for (int e = tid; e < BK * DV; e += {T}) {{")
+            w(f"{i2}    const int kk = e / DV, jj = e - kk * DV;")
+            w(f"{i2}    vs[kk * DV + jj] = kk < nk ? {ptrs[plan.v]}[(long long)(k0 + kk) * DV + jj] : 0.0f;")
+            w(f"{i2}}}")
+        w(f"{i2}__syncthreads();")
+        # scores and j-independent statements, once per (row, key)
+        w(f"{i2}for (int p = tid; p < BQ * BK; p += {T}) {{")
+        i3 = i2 + "    "
+        w(f"{i3}const int r = p / BK, kk = p - r * BK;")
+        w(f"{i3}if (r < nq && kk < nk) {{")
+        i4 = i3 + "    "
+        if reuse:
+            w(f"{i4}float sc = scache[r * (SK + 1) + k0 + kk];")
+        else:
+            w(f"{i4}float sc = {f32_lit(st.dot_init)};")
+            w(f"{i4}#pragma unroll 8")
+            w(f"{i4}for (int d = 0; d < D; ++d) sc = __fmaf_rn(qs[r * QS + d], ks[d * BK + kk], sc);")
+            if cache:
+                w(f"{i4}scache[r * (SK + 1) + k0 + kk] = sc;")
+        em = Emitter(shapes, dtypes, ptrs, indent=i4)
+        em.fusable = fus
+        em.env.update(scalar_env)
+        em.bind_const(plan.i, "int", "(q0 + r)")
+        em.bind_const(st.loop.axis.name, "int", "(k0 + kk)")
+        em.env[st.dot_acc] = ("f32", "sc")
+        em.declared[f"{st.dot_acc}|f32"] = "sc"
+        for n in row_names:
+            em.env.setdefault(n, ("f32", row_ref(n, "r")))
+        em.run(tuple(st.indep))
+        w("\n".join(em.lines))
+        # stash the accumulate operands and the values the j-dependent statements read
+        acc_ops = []
+        for fi, (a, op) in enumerate(st.row_accs):
+            accum = next(t for t in st.post if isinstance(t, ir.Accum) and t.name == a)
+            prod = em.plain_product(accum.value) if op == "add" else None
+            if prod is not None:
+                w(f"{i4}acca[({fi} * BQ + r) * SS + kk] = {prod[0]};")
+                w(f"{i4}accb[({fi} * BQ + r) * SS + kk] = {prod[1]};")
+                acc_ops.append((a, op, True))
+            else:
+                w(f"{i4}acca[({fi} * BQ + r) * SS + kk] = {em.as_f32(accum.value)};")
+                acc_ops.append((a, op, False))
+        stash_codes = {}
+        for si, n in enumerate(st.stash):
+            w(f"{i4}stash[({si} * BQ + r) * SS + kk] = {em.as_f32(n)};")
+            stash_codes[n] = si
+        w(f"{i3}}}")
+        w(f"{i2}}}")
+        w(f"{i2}__syncthreads();")
+        # row accumulations in key order, one thread per row
+        if acc_ops:
+            w(f"{i2}if (tid < nq) {{")
+            for fi, (a, op, is_fma) in enumerate(acc_ops):
+                ref = row_ref(a, "tid")
+                w(f"{i2}    float ra = {ref};")
+                w(f"{i2}    for (int kk = 0; kk < nk; ++kk)")
+                if is_fma:
+                    w(f"{i2}        ra = __fmaf_rn(acca[({fi} * BQ + tid) * SS + kk], accb[({fi} * BQ + tid) * SS + kk], ra);")
+                else:
+                    w(f"{i2}        ra = {combine_code(op, 'ra', f'acca[({fi} * BQ + tid) * SS + kk]')};")
+                w(f"{i2}    {ref} = ra;")
+            w(f"{i2}}}")
+        # j-dependent statements in key order, in the threads that own the output cells
+        if st.dep:
+            w(f"{i2}#pragma unroll")
+            w(f"{i2}for (int u = 0; u < {nown}; ++u) {{")
+            w(f"{i2}    const int o = tid + u * {T};")
+            w(f"{i2}    const int r = o / DV, jj = o - r * DV;")
+            w(f"{i2}    if (r < nq) {{")
+            i5 = i2 + "        "
+            w(f"{i5}for (int kk = 0; kk < nk; ++kk) {{")
+            em2 = Emitter(shapes, dtypes, ptrs, indent=i5 + "    ",
+                          load_hook=lambda s_, k_, kk="kk": ("f32", f"vs[{kk} * DV + jj]"))
+            em2.fusable = fus
+            em2.env.update(scalar_env)
+            em2.bind_const(plan.i, "int", "(q0 + r)")
+            em2.bind_const(plan.j, "int", "jj")
+            em2.bind_const(st.loop.axis.name, "int", "(k0 + kk)")
+            for n in row_names:
+                em2.env.setdefault(n, ("f32", row_ref(n, "r")))
+            for n, si in stash_codes.items():
+                em2.env[n] = ("f32", f"stash[({si} * BQ + r) * SS + kk]")
+            for a in plan.cell_accs:
+                em2.env[a] = ("f32", f"cacc_{_c(a)}[u]")
+                em2.declared[f"{a}|f32"] = f"cacc_{_c(a)}[u]"
+            em2.run(tuple(st.dep))
+            w("\n".join(em2.lines))
+            w(f"{i5}}}")
+            w(f"{i2}    }}")
+            w(f"{i2}}}")
+        w(f"{ind}}}")
+    # the output
+    w(f"{ind}#pragma unroll")
+    w(f"{ind}for (int u = 0; u < {nown}; ++u) {{")
+    w(f"{ind}    const int o = tid + u * {T};")
+    w(f"{ind}    const int r = o / DV, jj = o - r * DV;")
+    w(f"{ind}    if (r < nq) {{")
+    val = plan.out.values[0]
+    if val in plan.cell_accs:
+        code = f"cacc_{_c(val)}[u]"
+    elif val in row_slot:
+        code = row_ref(val, "r")
+    else:
+        raise UnsupportedIR(f"attention output {val!r} is neither a cell nor a row value")
+    w(f"{ind}        {ptrs[plan.out_name]}[(q0 + r) * DV + jj] = {code};")
+    w(f"{ind}    }}")
+    w(f"{ind}}}")
+    w(f"{ind}__syncthreads();")
+    w("    }")
+    w("}")
+    blocks = -(-SQ // BQ)
+    grid = max(1, min(blocks, SM_COUNT * 8))
+    rb = []
+    for name in args:
+        if name in (plan.q,):
+            rb.append(D * 4)
+        elif name == plan.out_name:
+            rb.append(DV * 4)
+        else:
+            rb.append(0)
+    launch = LaunchPlan(grid=(grid, 1, 1), block=(T, 1, 1), smem=smem_bytes, range_total=SQ, range_align=BQ,
+                        range_bytes=rb)
+    lines.append(launch_record_source("attention", launch, params))
+    notes = {"kernel": "attention_rows", "rows_per_cta": BQ, "key_tile": BK, "threads": T, "score_cache": cache,
+             "passes":
+             sum(isinstance(s, KeyLoop) for s in plan.steps), "smem": smem_bytes}
+    return KernelSource(entry=kop.name, source="\n".join(lines), launch=launch, params=params,
+                        family="attention", notes=notes)
+
+
+def _row_defined(plan: AttnPlan, name: str, upto) -> bool:
+    """Whether ``name`` already holds a value in shared memory before step ``upto``."""
+    for st in plan.steps:
+        if st is upto:
+            return False
+        if isinstance(st, KeyLoop):
+            if name in [a for a, _ in st.row_accs]:
+                return True
+        elif name in _defs(st[1]):
+            return True
+    return False

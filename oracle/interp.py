@@ -617,6 +617,11 @@ class Cells:
                 self.mask = ~p if outer is None else (outer & ~p)
                 self.run(s.else_body)
             self.mask = outer
+        elif isinstance(s, Loop):
+            # sequential trips, every cell at once (the reference's per-thread loop order)
+            for it in range(int(s.axis.extent.value)):
+                self.env[s.axis.name] = ("int", np.int64(it))
+                self.run(s.body)
         elif isinstance(s, Select):
             out = np.zeros(self.n, F32)
             taken = np.zeros(self.n, bool)
@@ -687,6 +692,13 @@ def evaluate(kop, shapes: dict, dtypes: dict, inputs: dict[str, np.ndarray],
         _eval_phases(tile, stmts, axes, bufs, shapes, dtypes)
     elif strided:
         _eval_strided(tile, stmts, axes, strided[0], bufs, shapes, dtypes)
+    elif loops and (len(loops) > 1 or any(isinstance(t, Loop) for t in ir_walk(loops[0].body))):
+        # nested or several loops per cell (the naive attention IR): general sequential evaluation
+        n = int(np.prod([e for _, e in axes])) if axes else 1
+        m = Cells(n, bufs, shapes, dtypes)
+        for k, v in _cells_for(axes, n).items():
+            m.env[k] = ("int", v)
+        m.run(stmts)
     elif loops and _is_matmul(loops[0]):
         _eval_matmul(tile, stmts, axes, loops[0], bufs, shapes, dtypes)
     elif loops:

@@ -346,6 +346,63 @@ def rownorm_case(cid: str, rows: int, cols: int, kind: str, *, config: str | Non
     return Case(cid, entry, graph, kern, family="rownorm", config=config, check=check)
 
 
+def attention_case(cid: str, seq: int, dim: int, *, config: str | None = None, k_rows: bool = False) -> Case:
+    """Naive attention, one thread per output cell (i, j) recomputing the
+    scores three times: for the row max, for the softmax denominator, and
+    for the weighted sum of V (the reference generator's a-class IR shape,
+    tools/make_proxy_set.py:416-474).  q [seq, dim], kt = K^T [dim, seq],
+    v [seq, dim], scale 1/sqrt(dim)."""
+    entry = "k_attn_naive"
+    scale = 1.0 / math.sqrt(dim)
+
+    def scores(k: str, d: str, tag: str) -> tuple:
+        return (
+            Init(f"sc{tag}", 0.0, dtype=F32),
+            Loop(axis=Axis(d, Dim(dim)), body=(
+                Load(names=(f"q{tag}",), input="q", index=(Var("i"), Var(d)), dtype=F32),
+                Load(names=(f"kt{tag}",), input="kt", index=((Var(k), Var(d)) if k_rows else (Var(d), Var(k))),
+                     dtype=F32),
+                Assign(f"p{tag}", EW("multiply"), (f"q{tag}", f"kt{tag}"), F32),
+                Accum(f"sc{tag}", f"p{tag}", EW("add"), F32, axes=(d,)),
+            )),
+            Let(f"inv{tag}", Literal(scale, "float"), F32),
+            Assign(f"sc{tag}", EW("multiply"), (f"sc{tag}", f"inv{tag}"), F32),
+        )
+
+    body = Tile(axes=(Axis("i", Dim(seq)), Axis("j", Dim(dim))), body=(
+        Init("m", -1e30, dtype=F32),
+        Loop(axis=Axis("k0", Dim(seq)), body=scores("k0", "d0", "0") + (
+            Accum("m", "sc0", EW("maximum"), F32, axes=("k0",)),)),
+        Init("den", 0.0, dtype=F32),
+        Loop(axis=Axis("k1", Dim(seq)), body=scores("k1", "d1", "1") + (
+            Assign("dl1", EW("subtract"), ("sc1", "m"), F32),
+            Assign("ex1", EW("exp"), ("dl1",), F32),
+            Accum("den", "ex1", EW("add"), F32, axes=("k1",)),)),
+        Assign("invd", EW("reciprocal"), ("den",), F32),
+        Init("acc", 0.0, dtype=F32),
+        Loop(axis=Axis("k2", Dim(seq)), body=scores("k2", "d2", "2") + (
+            Assign("dl2", EW("subtract"), ("sc2", "m"), F32),
+            Assign("ex2", EW("exp"), ("dl2",), F32),
+            Assign("wt", EW("multiply"), ("ex2", "invd"), F32),
+            Load(names=("vv",), input="v", index=(Var("k2"), Var("j")), dtype=F32),
+            Assign("wv", EW("multiply"), ("wt", "vv"), F32),
+            Accum("acc", "wv", EW("add"), F32, axes=("k2",)),)),
+        Write(output="attn", index=(Var("i"), Var("j")), values=("acc",), value_dtype=F32),
+    ))
+    ins = ["q", "kt", "v"]
+    graph = {"inputs": ins, "outputs": ["attn"], "nodes": {
+        "q": _input("q", [seq, dim]), "kt": _input("kt", [seq, dim] if k_rows else [dim, seq]),
+        "v": _input("v", [seq, dim]),
+        "attn": _kernel(entry, body, ins, [("attn", [seq, dim], "f32")])}}
+    grid, block = _launch(seq * dim)
+    kern = _meta_kernel("attn", entry, ins + ["attn"], grid, block, [
+        _arg("q", [seq, dim], init=NORM(), seed=0),
+        _arg("kt", [seq, dim] if k_rows else [dim, seq], init=NORM(), seed=1),
+        _arg("v", [seq, dim], init=NORM(), seed=2), _arg("attn", [seq, dim], output=True)])
+    return Case(cid, entry, graph, kern, family="attention", config=config,
+                check={"kind": "rtol", "rtol": 1e-4, "atol": 1e-5, "oracle": APPROX_ORACLE})
+
+
 def rowsummax_case(cid: str, rows: int, cols: int, *, config: str | None = None) -> Case:
     """row sum and row max of x[rows, cols] in one pass."""
     entry = "k_row_sum_max_reduce"
@@ -825,6 +882,12 @@ def all_cases() -> list[Case]:
         cases.append(rownorm_case(f"f_{kind}_7x4096", 7, 4096, kind))
         cases.append(rownorm_case(f"f_{kind}_33x130", 33, 130, kind))
         cases.append(rownorm_case(f"f_{kind}_bench_16384x8192", 16384, 8192, kind, config=f"f_{kind}"))
+    # naive attention (one thread per output cell, scores recomputed per pass)
+    cases.append(attention_case("a_attn_64x32", 64, 32))
+    cases.append(attention_case("a_attn_100x48", 100, 48))
+    cases.append(attention_case("a_attn_256x64", 256, 64))
+    cases.append(attention_case("a_attn_krows_80x40", 80, 40, k_rows=True))  # keys stored [seq, dim]
+    cases.append(attention_case("a_attn_bench_2048x64", 2048, 64, config="a_attn"))
     cases.append(add2d_case("p_add2d_7x13", 7, 13))
     cases.append(add2d_case("p_add2d_32x64", 32, 64))
     cases.append(vec4_case("p_vec4_1024", 1024))
