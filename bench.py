@@ -91,70 +91,89 @@ def peaks() -> tuple[dict, str]:
 
 
 class ClockSampler:
-    """SM clock and clock-event (throttle) reasons sampled every ~2 ms through
-    NVML while the timed region runs (read-only queries)."""
+    """SM clocks and clock-event (throttle) reasons of the job's GPUs, sampled
+    through NVML (read-only queries) while the timed region runs.
+
+    One sampler per job, on rank 0, polls every GPU of the node the job uses
+    (devices 0..world-1 of this process's view) every ~3 ms.  NVML is opened
+    before the timed region; ``start``/``stop`` only run the polling thread,
+    so the timed region pays no NVML set-up.  With one poller per rank,
+    eight ranks' NVML calls slowed the host's launch loop enough to stretch
+    steps that end in a collective."""
 
     REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
                "sw_power_cap": 0x4}
+    INTERVAL_S = 0.003
 
-    def __init__(self, device: int):
-        self.device = device
+    def __init__(self, devices: list[int], active: bool = True):
         self.samples: list[tuple[float, int]] = []
         self.max_mhz = None
         self._stop = threading.Event()
         self._thread = None
         self._nvml = None
-
-    def __enter__(self):
+        self._handles = []
+        if not active:
+            return
         try:
             import pynvml
             pynvml.nvmlInit()
             self._nvml = pynvml
-            h = pynvml.nvmlDeviceGetHandleByIndex(self._physical_index())
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self._handles = [pynvml.nvmlDeviceGetHandleByIndex(self._physical_index(d)) for d in devices]
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handles[0], pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nvml = None
 
-            def run():
-                while not self._stop.is_set():
+    @staticmethod
+    def _physical_index(device: int) -> int:
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if vis:
+            try:
+                return int(vis.split(",")[device])
+            except (ValueError, IndexError):
+                pass
+        return device
+
+    def start(self) -> None:
+        if self._nvml is None:
+            return
+        pynvml = self._nvml
+
+        def run():
+            while not self._stop.is_set():
+                for h in self._handles:
                     try:
                         sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
                         rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
                         self.samples.append((sm, rs))
                     except pynvml.NVMLError:
                         pass
-                    self._stop.wait(0.002)
-            self._thread = threading.Thread(target=run, daemon=True)
-            self._thread.start()
-        except Exception:
-            self._nvml = None
-        return self
+                self._stop.wait(self.INTERVAL_S)
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
 
-    def _physical_index(self) -> int:
-        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-        if vis:
-            try:
-                return int(vis.split(",")[self.device])
-            except (ValueError, IndexError):
-                pass
-        return self.device
-
-    def __exit__(self, *exc):
+    def stop(self) -> None:
         self._stop.set()
         if self._thread is not None:
             self._thread.join(timeout=2)
+
+    def close(self) -> None:
+        self.stop()
         if self._nvml is not None:
             try:
                 self._nvml.nvmlShutdown()
             except Exception:
                 pass
+            self._nvml = None
 
     def summary(self) -> dict:
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
-                    "source": "nvml unavailable"}
+                    "source": "nvml unavailable" if self._nvml is None and not self._handles else "nvml, no sample"}
         reasons = sorted(name for name, bit in self.REASONS.items()
                          if any(rs & bit for _, rs in self.samples))
         return {"sm_mhz": statistics.median(sm for sm, _ in self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": reasons, "samples": len(self.samples), "source": "nvml, 2 ms polling"}
+                "reasons": reasons, "samples": len(self.samples), "gpus": len(self._handles),
+                "source": f"nvml from rank 0, every {self.INTERVAL_S * 1e3:.0f} ms, all GPUs of the job"}
 
 
 # ---------------------------------------------------------------------------- inputs
@@ -242,17 +261,21 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     st = mod.status()
     if st:
         raise RuntimeError(f"kernel status 0x{st:x} during warm-up")
+    clocks = ClockSampler(list(range(min(world, torch.cuda.device_count()))) if world > 1 else [local],
+                          active=(rank == 0))
     barrier()
     torch.cuda.synchronize(local)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        e0.record()
-        for _ in range(args.steps):
-            mod.launch(order, stream=stream)
-            combine()
-        e1.record()
-        torch.cuda.synchronize(local)
+    clocks.start()
+    e0.record()
+    for _ in range(args.steps):
+        mod.launch(order, stream=stream)
+        combine()
+    e1.record()
+    torch.cuda.synchronize(local)
+    clocks.stop()
     barrier()
+    clocks.close()
     ms_max = max_over_ranks(e0.elapsed_time(e1), world, device)
     per_launch_ms = ms_max / args.steps
     value = units * world * args.steps / (ms_max / 1e3) / (1e9 if unit == "GB/s" else 1e12)
