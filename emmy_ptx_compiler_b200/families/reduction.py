@@ -200,12 +200,18 @@ def _match_atomic(stmts, axes, atomics) -> ReductionPlan | None:
     if len(atomics) != 1 or atomics[0].index or len(atomics[0].values) != 1:
         return None
     w = atomics[0]
-    elem = tuple(s for s in stmts if s is not w)
+    # ZeroPrologue (compile.py:2890-2913): the kernel itself zero-fills `words`
+    # 32-bit words of a buffer before accumulating into it
+    zps = [s for s in stmts if isinstance(s, ir.ZeroPrologue)]
+    elem = tuple(s for s in stmts if s is not w and not isinstance(s, ir.ZeroPrologue))
     if w not in stmts or not _only(elem, (ir.Load, ir.Let, ir.Assign, ir.Select)):
         return None
     acc = "__atomic_total"
     elem = elem + (ir.Accum(acc, w.values[0], ir.ElementwiseImpl("add"), None),)
-    return ReductionPlan("atomic", [], axes, elem, [(acc, "add")], {}, (), (), atomic_write=w)
+    plan = ReductionPlan("atomic", [], axes, elem, [(acc, "add")], {}, (), (), atomic_write=w)
+    plan.notes["zero_prologue"] = [(z.dst, int(lit_int(z.words) if not isinstance(z.words, int) else z.words))
+                                   for z in zps]
+    return plan
 
 
 def _seeds(pre, accs, strict: bool) -> dict[str, float]:
@@ -528,6 +534,10 @@ def _epilogue(plan, shapes, dtypes, ptrs, scalar_env, totals: dict[str, str], in
         em.assign(a, "f32", total)
     if plan.kind == "atomic":
         w = plan.atomic_write
+        # the zero fill comes first: no block writes these buffers before the final combine
+        for dst, words in plan.notes.get("zero_prologue", []):
+            if dst in ptrs and words > 0:
+                em.emit(f"for (int zw = 0; zw < {words}; ++zw) reinterpret_cast<unsigned *>({ptrs[dst]})[zw] = 0u;")
         em.stmt(ir.Write(w.output, (), (plan.accs[0][0],), w.value_dtype, False))
     else:
         em.run(plan.post_body)

@@ -42,7 +42,7 @@ sys.path.insert(0, str(HERE / "emmy_shim"))
 
 from emmy._core import (  # noqa: E402
     Accum, Assign, BinaryExpr, Builtin, CastExpr, Cond, FlatIndex, FuncCallExpr, Graph, Init, KernelOp,
-    Let, Literal, Load, Loop, Select, Smem, StridedLoop, Sync, TernaryExpr, Tile, TreeHalve, Var,
+    Let, Literal, Load, Loop, Select, Smem, StridedLoop, Sync, TernaryExpr, Tile, TreeHalve, Var, ZeroPrologue,
     WarpShuffle, Write,
 )
 
@@ -617,6 +617,9 @@ class Cells:
                 self.mask = ~p if outer is None else (outer & ~p)
                 self.run(s.else_body)
             self.mask = outer
+        elif isinstance(s, ZeroPrologue):
+            # the kernel's own zero fill of `words` 32-bit words (compile.py:2890-2913)
+            self.bufs[s.dst].view(np.uint32)[:int(s.words)] = 0
         elif isinstance(s, Loop):
             # sequential trips, every cell at once (the reference's per-thread loop order)
             for it in range(int(s.axis.extent.value)):

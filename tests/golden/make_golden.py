@@ -56,7 +56,9 @@ from emmy.compiler.ir.expr import BinaryExpr, Literal, Var  # noqa: E402
 from emmy.compiler.ir.kernel.ir import (  # noqa: E402
     Axis, DataType, Smem, Sync, Tile, TreeHalve, WarpShuffle,
 )
-from emmy.compiler.ir.stmt import Accum, Assign, Cond, Init, Let, Load, Loop, StridedLoop, Write  # noqa: E402
+from emmy.compiler.ir.stmt import (  # noqa: E402
+    Accum, Assign, Cond, Init, Let, Load, Loop, StridedLoop, Write, ZeroPrologue,
+)
 from emmy.compiler.ir.stmt.leaves import Select, SelectBranch  # noqa: E402
 
 F32 = DataType("f32", np.dtype("float32"), 4)
@@ -509,10 +511,13 @@ def rowsum_loop_nonadjacent_case(cid: str, rows: int, cols: int) -> Case:
     return c
 
 
-def atomic_sum_case(cid: str, n: int) -> Case:
-    """make_world_set.py:247-266: every cell red.add's into sum_1[0]."""
+def atomic_sum_case(cid: str, n: int, *, zero_prologue: bool = False) -> Case:
+    """make_world_set.py:247-266: every cell red.add's into sum_1[0].  With
+    ``zero_prologue`` the kernel zeroes sum_1 itself (ZeroPrologue,
+    compile.py:2890-2913) instead of the runner's zero_outputs."""
     entry = "k_atomic_sum"
     body = Tile(axes=(Axis("a0", Dim(n)),), body=(
+        *((ZeroPrologue("sum_1", 1),) if zero_prologue else ()),
         Load(names=("in0",), input="x", index=(Var("a0"),), dtype=F32),
         Write(output="sum_1", index=(), values=("in0",), value_dtype=F32, atomic=True),
     ))
@@ -521,7 +526,7 @@ def atomic_sum_case(cid: str, n: int) -> Case:
     grid, block = _launch(n)
     kern = _meta_kernel("sum_1", entry, ["x", "sum_1"], grid, block, [
         _arg("x", [n], init=NORM(), seed=0), _arg("sum_1", [1], output=True)],
-        zero_outputs=["sum_1"])
+        zero_outputs=[] if zero_prologue else ["sum_1"])
     return Case(cid, entry, graph, kern, family="reduction", check={"kind": "rtol", "rtol": 1e-5,
                                                                      "atol": 1e-4})
 
@@ -846,6 +851,8 @@ def all_cases() -> list[Case]:
     cases.append(rowsum_loop_case("r_rowsumsq_loop_33x250", 33, 250))
     cases.append(rowsum_loop_nonadjacent_case("r_rowsumsq_gap_17x300", 17, 300))
     cases.append(atomic_sum_case("r_atomic_sum_512", 512))
+    # one block: the reference's in-kernel zero fill races with other blocks' adds otherwise
+    cases.append(atomic_sum_case("r_atomic_zp_sum_128", 128, zero_prologue=True))
     # config 5
     cases.append(gemm_case("c5_gemm_full", 16384, 8192, 16384, config="c5", with_ref=False))
     cases.append(gemm_case("c5_gemm_prof_8192x8192x8192", 8192, 8192, 8192, with_ref=False))  # profiler size
