@@ -36,8 +36,9 @@ BLOCK = 256
 UNROLL = 2
 VEC = 4
 PREFETCH = 0      # trips ahead to prefetch full-tile inputs into L2 (0 = off)
-MIN_BLOCKS = 0    # __launch_bounds__ minimum blocks per SM (0 = compiler's choice)
+MIN_BLOCKS = 4    # __launch_bounds__ minimum blocks per SM (0 = compiler's choice)
 ORDER = "grid"    # "grid": grid-stride vectors; "blocked": each CTA streams one contiguous chunk
+PIPELINE = True   # load the next trip's streamed vectors before computing the current trip
 # bulk-copy pipeline: 8 consumer warps + 1 producer warp, 4096-cell tiles, up to 4 stages
 BULK_MIN_CELLS = 1 << 20
 BULK_CONSUMERS = 256
@@ -174,7 +175,8 @@ def _streamed_loads(plan: PointwisePlan) -> list[ir.Load]:
 def generate(kop: ir.KernelOp, plan: PointwisePlan, shapes: dict, dtypes: dict, args: list[str],
              scalars: dict[str, str], written: set[str], *, variant: str = "auto",
              unroll: int = UNROLL, prefetch: int = PREFETCH, min_blocks: int = MIN_BLOCKS,
-             order: str = ORDER, hoist_broadcast: bool = True, pair="auto") -> KernelSource:
+             order: str = ORDER, hoist_broadcast: bool = True, pair="auto",
+             pipeline: bool = PIPELINE) -> KernelSource:
     """``variant``: "auto"/"vector" (register vectors), or "bulk" (shared-memory
     ring fed by bulk async copies).  ``pair``: compute the cell body on two
     adjacent cells at once with packed f32x2 add/mul/fma ("auto": whenever the
@@ -291,17 +293,32 @@ def generate(kop: ir.KernelOp, plan: PointwisePlan, shapes: dict, dtypes: dict, 
                 else:
                     w(f"            const {ctype(dt)} {var} = {ptrs[ld.input]}[{off}];")
                 names[li] = var
-            w(f"            for (; v + {unroll - 1} * vgs < NVEC; v += {unroll} * vgs) {{")
-            lines.extend(vtrip(plan, shapes, dtypes, ptrs, scalar_env,
-                               ["v"] + [f"v + {u} * vgs" for u in range(1, unroll)],
-                               "                ", hoisted=names, ix=(ity, isuf)))
-            w("            }")
+            if pipeline:
+                lines.extend(_pipelined_loop(plan, dtypes, ptrs, vtrip, shapes, scalar_env, unroll, ity, isuf,
+                                             "            ", names))
+            else:
+                w(f"            for (; v + {unroll - 1} * vgs < NVEC; v += {unroll} * vgs) {{")
+                lines.extend(vtrip(plan, shapes, dtypes, ptrs, scalar_env,
+                                   ["v"] + [f"v + {u} * vgs" for u in range(1, unroll)],
+                                   "                ", hoisted=names, ix=(ity, isuf)))
+                w("            }")
             w("            for (; v < NVEC; v += vgs) {")
             lines.extend(vtrip(plan, shapes, dtypes, ptrs, scalar_env, ["v"], "                ",
                                hoisted=names, ix=(ity, isuf)))
             w("            }")
             w("            return;")
             w("        }")
+        if pipeline and not prefetch:
+            lines.extend(_pipelined_loop(plan, dtypes, ptrs, vtrip, shapes, scalar_env, unroll, ity, isuf,
+                                         "        ", {}))
+            w("        for (; v < NVEC; v += vgs) {")
+            lines.extend(vtrip(plan, shapes, dtypes, ptrs, scalar_env, ["v"], "            ", ix=(ity, isuf)))
+            w("        }")
+            w("        return;")
+            w("    }")
+            return _finish_vector(kop, plan, lines, ncell, unroll, vec_ok, params, why, em_path=True,
+                                  shapes=shapes, dtypes=dtypes, ptrs=ptrs, scalar_env=scalar_env,
+                                  grid_quantum=quantum if vec_ok else 1, rbytes=rbytes)
         w(f"        for (; v + {unroll - 1} * vgs < NVEC; v += {unroll} * vgs) {{")
         if prefetch:
             for s_ in _streamed_loads(plan):
@@ -320,6 +337,47 @@ def generate(kop: ir.KernelOp, plan: PointwisePlan, shapes: dict, dtypes: dict, 
     return _finish_vector(kop, plan, lines, ncell, unroll, vec_ok, params, why, em_path=True,
                           shapes=shapes, dtypes=dtypes, ptrs=ptrs, scalar_env=scalar_env,
                           grid_quantum=quantum if vec_ok else 1, rbytes=rbytes)
+
+
+def _pipelined_loop(plan, dtypes, ptrs, vtrip, shapes, scalar_env, unroll, ity, isuf, ind, hoisted) -> list[str]:
+    """The main grid-stride loop with the streamed whole-tile loads of trip
+    t+1 issued before trip t computes (register double buffer)."""
+    loads = [s for s in ir.walk(plan.tile.body) if isinstance(s, ir.Load)]
+    full = [li for li, s in enumerate(loads)
+            if li not in hoisted and not _const_index(s.index)
+            and _axis_aligned(s.index, plan.axes) == list(range(len(plan.axes)))]
+    out = []
+    o = out.append
+
+    def ld(li, vexpr):
+        s_ = loads[li]
+        dt = ir.canon_dtype(s_.dtype or dtypes.get(s_.input))
+        return f"emmy_ld{VEC}_{dt}({ptrs[s_.input]} + ({vexpr}) * {VEC}{isuf}, true)"
+
+    for li in full:
+        dt = ir.canon_dtype(loads[li].dtype or dtypes.get(loads[li].input))
+        for u in range(unroll):
+            o(f"{ind}EmmyVec<{ctype(dt)}, {VEC}> nx{li}_{u};")
+    o(f"{ind}if (v + {unroll - 1} * vgs < NVEC) {{")
+    for li in full:
+        for u in range(unroll):
+            o(f"{ind}    nx{li}_{u} = {ld(li, f'v + {u} * vgs')};")
+    o(f"{ind}}}")
+    o(f"{ind}for (; v + {unroll - 1} * vgs < NVEC; v += {unroll} * vgs) {{")
+    pre = {}
+    for li in full:
+        for u in range(unroll):
+            o(f"{ind}    const auto cu{li}_{u} = nx{li}_{u};")
+            pre[(li, u)] = f"cu{li}_{u}"
+    o(f"{ind}    if (v + {2 * unroll - 1} * vgs < NVEC) {{")
+    for li in full:
+        for u in range(unroll):
+            o(f"{ind}        nx{li}_{u} = {ld(li, f'v + {unroll + u} * vgs')};")
+    o(f"{ind}    }}")
+    out.extend(vtrip(plan, shapes, dtypes, ptrs, scalar_env, ["v"] + [f"v + {u} * vgs" for u in range(1, unroll)],
+                     ind + "    ", hoisted=hoisted, ix=(ity, isuf), preloaded=pre))
+    o(f"{ind}}}")
+    return out
 
 
 def _finish_vector(kop, plan, lines, ncell, unroll, vec_ok, params, why, *, em_path, shapes, dtypes, ptrs,
@@ -364,13 +422,15 @@ def _c(name: str) -> str:
 def _vector_trip(plan: PointwisePlan, shapes, dtypes, ptrs, scalar_env, vexprs: list[str],
                  ind: str, smem_src: dict[int, str] | None = None,
                  hoisted: dict[int, str] | None = None, pair: bool = False,
-                 ix: tuple[str, str] = ("long long", "LL")) -> list[str]:
+                 ix: tuple[str, str] = ("long long", "LL"),
+                 preloaded: dict[tuple[int, int], str] | None = None) -> list[str]:
     """One trip: load U vectors of every input, run the cell body per lane,
     store U vectors of every output.  ``smem_src`` maps a load's position to a
     shared-memory element pointer expression (indexed by the vector's offset
     within the current tile, ``lo<u>``) for loads staged by bulk copies."""
     smem_src = smem_src or {}
     hoisted = hoisted or {}
+    preloaded = preloaded or {}
     axes = plan.axes
     out: list[str] = []
     loads = [s for s in ir.walk(plan.tile.body) if isinstance(s, ir.Load)]
@@ -404,6 +464,9 @@ def _vector_trip(plan: PointwisePlan, shapes, dtypes, ptrs, scalar_env, vexprs: 
                 continue
             if li in hoisted:
                 fetched[(li, u)] = (hoisted[li], _contiguous(s, plan), dt)
+                continue
+            if (li, u) in preloaded:
+                fetched[(li, u)] = (preloaded[(li, u)], True, dt)
                 continue
             pos = _axis_aligned(s.index, axes)
             bstrides = _axis_strides([axes[p] for p in pos])
