@@ -251,7 +251,7 @@ def range_bytes(plan: RowPlan, args: list[str], scalars: dict, dtypes: dict, sha
 
 
 def generate(kop: ir.KernelOp, plan: RowPlan, shapes: dict, dtypes: dict, args: list[str],
-             scalars: dict[str, str], written: set[str]) -> KernelSource:
+             scalars: dict[str, str], written: set[str], *, bulk_prefetch: bool = False) -> KernelSource:
     params: list[ParamSpec] = []
     ptrs: dict[str, str] = {}
     sig: list[str] = []
@@ -283,8 +283,7 @@ def generate(kop: ir.KernelOp, plan: RowPlan, shapes: dict, dtypes: dict, args: 
     w = lines.append
     w(DEVICE_PRELUDE)
     w(_VEC_HELPERS)
-    w('#include "emmy_launch_record.h"')
-    w('extern "C" __device__ unsigned int emmy_status;')
+    w('#include "emmy_sm100.cuh"')
     w(f'extern "C" __global__ void __launch_bounds__({T}) {kop.name}(' + ", ".join(sig) + ") {")
     w(f"    constexpr long long NROWS = {plan.rows}LL, K = {K}LL;")
     w(f"    __shared__ float red_smem[{max(1, nred)}][{NW}];")
@@ -295,10 +294,43 @@ def generate(kop: ir.KernelOp, plan: RowPlan, shapes: dict, dtypes: dict, args: 
     w("    const long long RB = (long long)(emmy_rb < (unsigned long long)NROWS ? emmy_rb : NROWS);")
     w("    const long long RE = (long long)(emmy_re < (unsigned long long)NROWS ? emmy_re : NROWS);")
     w("    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;")
+    nvec4 = -(-K // 4)
+    cached4 = -(-nvec4 // T) * 4 * max(1, len(plan.streamed)) <= CACHE_FLOATS
+    stage = _stage_bytes(plan, dtypes)
+    bulk = bulk_prefetch and vec and cached4 and bool(plan.streamed) and stage <= STAGE_BYTES_MAX
+    dyn = 0
+    if bulk:
+        # dynamic shared memory: one stage per streamed tensor, then the mbarrier and flags
+        offs = {}
+        cur = 0
+        for n in plan.streamed:
+            offs[n] = cur
+            cur += K * ir.ELEM_BYTES[ir.canon_dtype(dtypes.get(n))]
+        bar_off = (cur + 15) // 16 * 16
+        dyn = bar_off + 16
+        w("    extern __shared__ __align__(16) unsigned char rn_smem[];")
+        for n in plan.streamed:
+            dt = ir.canon_dtype(dtypes.get(n))
+            w(f"    {ctype(dt)} *const stage_{_c(n)} = reinterpret_cast<{ctype(dt)} *>(rn_smem + {offs[n]});")
+        w(f"    uint64_t *const rn_bar = reinterpret_cast<uint64_t *>(rn_smem + {bar_off});")
+        w(f"    volatile uint32_t *const rn_abort = reinterpret_cast<volatile uint32_t *>(rn_smem + {bar_off + 8});")
+        w("    uint32_t rn_dyn;")
+        w('    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(rn_dyn));')
     if vec:
         terms = [f"(uintptr_t){ptrs[n]}" for n in plan.streamed + plan.vectors + plan.outputs]
         w("    const bool aligned = ((" + " | ".join(terms) + ") & 15u) == 0;")
-        w("    if (aligned) {")
+        if bulk:
+            w(f"    if (aligned && rn_dyn >= {dyn}u) {{")
+            w("        if (tid == 0) {")
+            w("            emmy::mbar_init(rn_bar, 1);")
+            w("            *rn_abort = 0u;")
+            w("            emmy::fence_barrier_init();")
+            w("        }")
+            w("        __syncthreads();")
+            lines.extend(_row_loop(plan, shapes, dtypes, ptrs, scalar_env, fus, 4, T, "        ", bulk=True))
+            w("    } else if (aligned) {")
+        else:
+            w("    if (aligned) {")
         lines.extend(_row_loop(plan, shapes, dtypes, ptrs, scalar_env, fus, 4, T, "        "))
         w("    } else {")
         lines.extend(_row_loop(plan, shapes, dtypes, ptrs, scalar_env, fus, 1, T, "        "))
@@ -307,7 +339,7 @@ def generate(kop: ir.KernelOp, plan: RowPlan, shapes: dict, dtypes: dict, args: 
         lines.extend(_row_loop(plan, shapes, dtypes, ptrs, scalar_env, fus, 1, T, "    "))
     w("}")
     grid = max(1, min(plan.rows, SM_COUNT * 8))
-    launch = LaunchPlan(grid=(grid, 1, 1), block=(T, 1, 1), smem=0, range_total=plan.rows, range_align=1,
+    launch = LaunchPlan(grid=(grid, 1, 1), block=(T, 1, 1), smem=dyn, range_total=plan.rows, range_align=1,
                         range_bytes=range_bytes(plan, args, scalars, dtypes, shapes))
     if plan.rows >= SM_COUNT * 8:
         launch.fill_waves = 1
@@ -316,20 +348,42 @@ def generate(kop: ir.KernelOp, plan: RowPlan, shapes: dict, dtypes: dict, args: 
     ept = -(-nvec // T)
     notes = {"kernel": "row_fused", "threads": T, "vector": vec, "passes": sum(isinstance(p, Pass) for p in plan.steps),
              "reductions": nred, "elems_per_thread": ept * (4 if vec else 1),
-             "cached": ept * (4 if vec else 1) * max(1, len(plan.streamed)) <= CACHE_FLOATS}
+             "cached": ept * (4 if vec else 1) * max(1, len(plan.streamed)) <= CACHE_FLOATS,
+             "bulk_prefetch": bool(bulk)}
     return KernelSource(entry=kop.name, source="\n".join(lines), launch=launch, params=params, family="rownorm",
                         notes=notes)
 
 
-def _row_loop(plan: RowPlan, shapes, dtypes, ptrs, scalar_env, fus, VW: int, T: int, ind: str) -> list[str]:
+STAGE_BYTES_MAX = 96 * 1024   # shared-memory stage for the next row (bulk prefetch)
+
+
+def _stage_bytes(plan: RowPlan, dtypes) -> int:
+    return sum(plan.K * ir.ELEM_BYTES[ir.canon_dtype(dtypes.get(n))] for n in plan.streamed)
+
+
+def _row_loop(plan: RowPlan, shapes, dtypes, ptrs, scalar_env, fus, VW: int, T: int, ind: str,
+              bulk: bool = False) -> list[str]:
     """The persistent loop over this CTA's rows, every pass inside it, for
-    vector width VW (4: float4 per access, 1: scalar)."""
+    vector width VW (4: float4 per access, 1: scalar).  With ``bulk`` the next
+    row of every streamed tensor is brought into shared memory by one bulk
+    async copy (completion on an mbarrier) while the CTA works on the current
+    row from registers."""
     K = plan.K
     nunits = -(-K // VW)
     EPT = -(-nunits // T)
     cached = EPT * VW * max(1, len(plan.streamed)) <= CACHE_FLOATS
+    bulk = bulk and cached and VW == 4
     out: list[str] = []
     o = out.append
+    if bulk:
+        o(f"{ind}uint32_t rn_phase = 0u;")
+        o(f"{ind}if (tid == 0 && RB + (long long)blockIdx.x < RE) {{")
+        o(f"{ind}    emmy::mbar_arrive_expect_tx(rn_bar, {_stage_bytes(plan, dtypes)}u);")
+        for n in plan.streamed:
+            dt = ir.canon_dtype(dtypes.get(n))
+            o(f"{ind}    emmy::bulk_load(stage_{_c(n)}, {ptrs[n]} + (RB + (long long)blockIdx.x) * K, "
+              f"{K * ir.ELEM_BYTES[dt]}u, rn_bar);")
+        o(f"{ind}}}")
     o(f"{ind}for (long long row = RB + blockIdx.x; row < RE; row += gridDim.x) {{")
     i2 = ind + "    "
     # row axes decoded from the flat row index
@@ -352,6 +406,12 @@ def _row_loop(plan: RowPlan, shapes, dtypes, ptrs, scalar_env, fus, VW: int, T: 
     for n in plan.outputs:
         dt = ir.canon_dtype(dtypes.get(n))
         o(f"{i2}{ctype(dt)} *rq_{_c(n)} = {ptrs[n]} + row * K;")
+    if bulk:
+        # this row has landed in shared memory (bounded wait; every thread leaves together)
+        o(f"{i2}const bool rn_ok = emmy::mbar_wait(rn_bar, rn_phase, rn_abort, EMMY_STATUS_TIMEOUT_PRODUCER, "
+          f"2000000000ull);")
+        o(f"{i2}if (__syncthreads_or(!rn_ok)) break;")
+        o(f"{i2}rn_phase ^= 1u;")
     if cached:
         for n in plan.streamed:
             dt = ir.canon_dtype(dtypes.get(n))
@@ -362,11 +422,23 @@ def _row_loop(plan: RowPlan, shapes, dtypes, ptrs, scalar_env, fus, VW: int, T: 
             o(f"{i2}#pragma unroll")
             o(f"{i2}for (int e = 0; e < {EPT}; ++e) {{")
             o(f"{i2}    const long long u = tid + (long long)e * {T};")
-            if VW == 4:
+            if bulk:
+                o(f"{i2}    if (u < {nunits}) cx_{_c(n)}[e] = emmy_lds4_{dt}(stage_{_c(n)} + u * 4);")
+            elif VW == 4:
                 o(f"{i2}    if (u < {nunits}) cx_{_c(n)}[e] = emmy_ld4_{dt}(rp_{_c(n)} + u * 4, true);")
             else:
                 o(f"{i2}    if (u < {nunits}) cx_{_c(n)}[e] = rp_{_c(n)}[u];")
             o(f"{i2}}}")
+    if bulk:
+        # every thread holds its part of the row: refill the stage with the next row
+        o(f"{i2}__syncthreads();")
+        o(f"{i2}if (tid == 0 && row + gridDim.x < RE) {{")
+        o(f"{i2}    emmy::mbar_arrive_expect_tx(rn_bar, {_stage_bytes(plan, dtypes)}u);")
+        for n in plan.streamed:
+            dt = ir.canon_dtype(dtypes.get(n))
+            o(f"{i2}    emmy::bulk_load(stage_{_c(n)}, {ptrs[n]} + (row + gridDim.x) * K, "
+              f"{K * ir.ELEM_BYTES[dt]}u, rn_bar);")
+        o(f"{i2}}}")
     declared_row: dict[str, str] = {}
     slot = 0
     row_em_lines: list[str] = []
