@@ -394,13 +394,41 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
             w(f"{i2}}}")
         w(f"{i2}__syncthreads();")
         # scores and j-independent statements, once per (row, key)
-        w(f"{i2}for (int p = tid; p < BQ * BK; p += {T}) {{")
+        blocked = not reuse and T % BK == 0 and (BQ * BK) % T == 0
         i3 = i2 + "    "
-        w(f"{i3}const int r = p / BK, kk = p - r * BK;")
+        if blocked:
+            # a thread's pairs share one key: each k element read from shared memory
+            # feeds NP rows' fma chains (each still sequential over d)
+            NP = BQ * BK // T
+            RS = T // BK
+            w(f"{i2}{{")
+            w(f"{i3}const int kk = tid % BK;")
+            w(f"{i3}float scv[{NP}];")
+            w(f"{i3}#pragma unroll")
+            w(f"{i3}for (int u = 0; u < {NP}; ++u) scv[u] = {f32_lit(st.dot_init)};")
+            w(f"{i3}if (kk < nk) {{")
+            w(f"{i3}    #pragma unroll 4")
+            w(f"{i3}    for (int d = 0; d < D; ++d) {{")
+            w(f"{i3}        const float kv = ks[d * BK + kk];")
+            w(f"{i3}        #pragma unroll")
+            w(f"{i3}        for (int u = 0; u < {NP}; ++u)")
+            w(f"{i3}            scv[u] = __fmaf_rn(qs[(tid / BK + u * {RS}) * QS + d], kv, scv[u]);")
+            w(f"{i3}    }}")
+            w(f"{i3}}}")
+            w(f"{i3}#pragma unroll")
+            w(f"{i3}for (int u = 0; u < {NP}; ++u) {{")
+            w(f"{i3}const int r = tid / BK + u * {RS};")
+        else:
+            w(f"{i2}for (int p = tid; p < BQ * BK; p += {T}) {{")
+            w(f"{i3}const int r = p / BK, kk = p - r * BK;")
         w(f"{i3}if (r < nq && kk < nk) {{")
         i4 = i3 + "    "
         if reuse:
             w(f"{i4}float sc = scache[r * (SK + 1) + k0 + kk];")
+        elif blocked:
+            w(f"{i4}float sc = scv[u];")
+            if cache:
+                w(f"{i4}scache[r * (SK + 1) + k0 + kk] = sc;")
         else:
             w(f"{i4}float sc = {f32_lit(st.dot_init)};")
             w(f"{i4}#pragma unroll 8")
@@ -436,6 +464,8 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
             stash_codes[n] = si
         w(f"{i3}}}")
         w(f"{i2}}}")
+        if blocked:
+            w(f"{i2}}}")
         w(f"{i2}__syncthreads();")
         # row accumulations in key order, one thread per row
         if acc_ops:
@@ -451,7 +481,21 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
                 w(f"{i2}    {ref} = ra;")
             w(f"{i2}}}")
         # j-dependent statements in key order, in the threads that own the output cells
-        if st.dep:
+        shared_j = st.dep and T % DV == 0
+        if shared_j:
+            # every owned cell of a thread has the same column: one v read per key feeds them all
+            w(f"{i2}{{")
+            w(f"{i2}const int jj = tid % DV;")
+            w(f"{i2}for (int kk = 0; kk < nk; ++kk) {{")
+            w(f"{i2}    const float vcur = vs[kk * DV + jj];")
+            w(f"{i2}    #pragma unroll")
+            w(f"{i2}    for (int u = 0; u < {nown}; ++u) {{")
+            w(f"{i2}        const int r = (tid + u * {T}) / DV;")
+            w(f"{i2}        if (r < nq) {{")
+            i5 = i2 + "        "
+            em2 = Emitter(shapes, dtypes, ptrs, indent=i5 + "    ",
+                          load_hook=lambda s_, k_: ("f32", "vcur"))
+        elif st.dep:
             w(f"{i2}#pragma unroll")
             w(f"{i2}for (int u = 0; u < {nown}; ++u) {{")
             w(f"{i2}    const int o = tid + u * {T};")
@@ -461,6 +505,7 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
             w(f"{i5}for (int kk = 0; kk < nk; ++kk) {{")
             em2 = Emitter(shapes, dtypes, ptrs, indent=i5 + "    ",
                           load_hook=lambda s_, k_, kk="kk": ("f32", f"vs[{kk} * DV + jj]"))
+        if st.dep:
             em2.fusable = fus
             em2.env.update(scalar_env)
             em2.bind_const(plan.i, "int", "(q0 + r)")
@@ -475,9 +520,15 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
                 em2.declared[f"{a}|f32"] = f"cacc_{_c(a)}[u]"
             em2.run(tuple(st.dep))
             w("\n".join(em2.lines))
-            w(f"{i5}}}")
-            w(f"{i2}    }}")
-            w(f"{i2}}}")
+            if shared_j:
+                w(f"{i2}        }}")
+                w(f"{i2}    }}")
+                w(f"{i2}}}")
+                w(f"{i2}}}")
+            else:
+                w(f"{i5}}}")
+                w(f"{i2}    }}")
+                w(f"{i2}}}")
         w(f"{ind}}}")
     # the output
     w(f"{ind}#pragma unroll")
