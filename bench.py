@@ -253,10 +253,19 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
             torch.distributed.barrier()
 
     combine = combine_step(args.config, bufs, world)
+    step = lambda: (mod.launch(order, stream=stream), combine())  # noqa: E731
+    xchg = None
+    if args.config == "c4" and world > 1 and args.combine == "fused":
+        # one kernel per GPU: shard sum fused with the combine over NVLink peer memory
+        xchg = runtime.Exchange(local, world, rank)
+        handles = [None] * world
+        torch.distributed.all_gather_object(handles, xchg.handle)
+        xchg.connect(handles)
+        x_in, total, n_in = bufs["x"], bufs["sum_1"], bufs["x"].numel()
+        step = lambda: xchg.sum_allreduce(x_in, n_in, total, timeout_ms=10000, stream=stream)  # noqa: E731
 
     for _ in range(args.warmup):
-        mod.launch(order, stream=stream)
-        combine()
+        step()
     torch.cuda.synchronize(local)
     st = mod.status()
     if st:
@@ -269,13 +278,17 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     clocks.start()
     e0.record()
     for _ in range(args.steps):
-        mod.launch(order, stream=stream)
-        combine()
+        step()
     e1.record()
     torch.cuda.synchronize(local)
     clocks.stop()
     barrier()
     clocks.close()
+    if xchg is not None:
+        xst = xchg.status()
+        xchg.close()
+        if xst:
+            raise RuntimeError(f"fused sum + combine status 0x{xst:x} (a peer did not arrive in time)")
     ms_max = max_over_ranks(e0.elapsed_time(e1), world, device)
     per_launch_ms = ms_max / args.steps
     value = units * world * args.steps / (ms_max / 1e3) / (1e9 if unit == "GB/s" else 1e12)
@@ -341,8 +354,12 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     if ref_ptx is not None:
         line["reference_ptx_gpu"] = ref_ptx
     if args.config == "c4" and world > 1:
-        line["config"]["parallelism"] = (f"{world} ranks, each its own 2^31-element shard; the per-rank "
-                                         "sums are combined by an NCCL all-reduce inside every step")
+        line["config"]["parallelism"] = (
+            f"{world} ranks, each its own 2^31-element shard; every step is one kernel per GPU that sums "
+            "the shard and combines the per-GPU totals over NVLink peer memory (emmy_sum_f32_allreduce)"
+            if args.combine == "fused" else
+            f"{world} ranks, each its own 2^31-element shard; the per-rank sums are combined by an NCCL "
+            "all-reduce inside every step")
         line["gpu_launches"] = args.steps
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.config, seconds=args.cpu_seconds)
@@ -477,6 +494,9 @@ def _main(out) -> int:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-ptx", action="store_true")
+    ap.add_argument("--combine", choices=["fused", "nccl"], default="nccl",
+                    help="c4 at N>1: our reduction kernel + NCCL all-reduce (measured faster), or the fused "
+                         "sum + NVLink peer combine kernel")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))

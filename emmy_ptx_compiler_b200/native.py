@@ -18,7 +18,7 @@ REPO = PKG.parent
 LIB_DIR = PKG / "lib"
 RUNTIME_SO = LIB_DIR / "libemmy_b200.so"
 SOURCES = [PKG / "csrc" / "emmy_runtime.cpp"]
-CUDA_SOURCES = [PKG / "csrc" / "emmy_noalloc.cu"]
+CUDA_SOURCES = [PKG / "csrc" / "emmy_noalloc.cu", PKG / "csrc" / "emmy_xchg.cu"]
 HEADERS = [REPO / "include" / "emmy_b200.h", REPO / "include" / "emmy_launch_record.h"]
 CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 CUDA_INC = CUDA_HOME / "include"

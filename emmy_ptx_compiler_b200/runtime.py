@@ -58,6 +58,11 @@ def _declare(lib) -> None:
         "emmy_shard_range": ([vp, i32, i32, P(u64), P(u64)], i32),
         "emmy_launch_sharded": ([P(vp), i32, P(P(u64)), i32, P(u64)], i32),
         "emmy_sum_f32_noalloc": ([i32, u64, u64, u64, u64], i32),
+        "emmy_xchg_create": ([i32, i32, i32, P(vp), P(C.c_uint8)], i32),
+        "emmy_xchg_connect": ([vp, P(C.c_uint8)], i32),
+        "emmy_sum_f32_allreduce": ([vp, u64, u64, u64, i32, u64], i32),
+        "emmy_xchg_status": ([vp, P(u32)], i32),
+        "emmy_xchg_destroy": ([vp], i32),
         "emmy_comm_unique_id": ([P(C.c_uint8)], i32),
         "emmy_comm_init": ([i32, i32, i32, P(C.c_uint8), i32, P(vp)], i32),
         "emmy_allreduce_f32": ([vp, u64, u64, sz, u64, i32], i32),
@@ -76,6 +81,8 @@ EXPORTED = ("emmy_version", "emmy_last_error", "emmy_init", "emmy_device_count",
             "emmy_alloc", "emmy_free", "emmy_memcpy_htod", "emmy_memcpy_dtoh", "emmy_memset_d8",
             "emmy_host_alloc", "emmy_host_free", "emmy_run_host", "emmy_time_launch", "emmy_launch_range",
             "emmy_module_range", "emmy_shard_range", "emmy_launch_sharded", "emmy_sum_f32_noalloc",
+            "emmy_xchg_create", "emmy_xchg_connect", "emmy_sum_f32_allreduce", "emmy_xchg_status",
+            "emmy_xchg_destroy",
             "emmy_comm_unique_id", "emmy_comm_init", "emmy_allreduce_f32", "emmy_allgather_f32",
             "emmy_comm_destroy", "emmy_comm_abort")
 
@@ -220,6 +227,42 @@ def launch_sharded(modules: list["Module"], args_per_device: list[list], streams
     arr = (C.POINTER(C.c_uint64) * n)(*[C.cast(w, C.POINTER(C.c_uint64)) for w in words])
     st = (C.c_uint64 * n)(*(streams or [0] * n))
     _check(lib().emmy_launch_sharded(mods, n, arr, len(args_per_device[0]), st))
+
+
+class Exchange:
+    """This GPU's end of the fused sum + cross-GPU combine (emmy_xchg_*):
+    ``Exchange(dev, nranks, rank)``, pass every rank's ``handle`` (in rank
+    order) to ``connect``, then ``sum_allreduce``."""
+
+    HANDLE_BYTES = 64
+
+    def __init__(self, device: int, nranks: int, rank: int):
+        init(device)
+        self.device = device
+        h = C.c_void_p()
+        buf = (C.c_uint8 * self.HANDLE_BYTES)()
+        _check(lib().emmy_xchg_create(device, nranks, rank, C.byref(h), buf))
+        self._h = h
+        self.handle = bytes(buf)
+
+    def connect(self, handles: list[bytes]) -> None:
+        blob = b"".join(handles)
+        arr = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        _check(lib().emmy_xchg_connect(self._h, arr))
+
+    def sum_allreduce(self, x, n: int, out, timeout_ms: int = 1000, stream: int = 0) -> None:
+        _check(lib().emmy_sum_f32_allreduce(self._h, C.c_uint64(arg_word(x)), C.c_uint64(n),
+                                            C.c_uint64(arg_word(out)), timeout_ms, C.c_uint64(stream)))
+
+    def status(self) -> int:
+        st = C.c_uint32(0)
+        _check(lib().emmy_xchg_status(self._h, C.byref(st)))
+        return st.value
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _check(lib().emmy_xchg_destroy(self._h))
+            self._h = None
 
 
 def sum_f32_noalloc(x, n: int, out, device: int = 0, stream: int = 0) -> None:

@@ -151,6 +151,33 @@ int emmy_time_launch(emmy_module_t m, const uint64_t *args, int nargs, int iters
 #define EMMY_NOALLOC_MAX_ELEMENTS (1ull << 36)
 int emmy_sum_f32_noalloc(int dev, const float *x, uint64_t n, float *out, uint64_t stream);
 
+/* The C4 step on N GPUs as ONE kernel per GPU (no counterpart in the
+ * reference, which has no multi-GPU path): the full-array sum of this GPU's
+ * shard fused with the cross-GPU combine over NVLink peer memory.
+ *
+ *   emmy_xchg_create   allocates this GPU's 256-byte exchange buffer and
+ *                      returns its CUDA IPC handle (EMMY_XCHG_HANDLE_BYTES);
+ *   emmy_xchg_connect  maps every rank's buffer, given all ranks' handles in
+ *                      rank order (exchanged by the caller, e.g. through
+ *                      torch.distributed);
+ *   emmy_sum_f32_allreduce  *out = sum over ranks of sum(data[0..n)), the same
+ *                      bits on every rank (partials added in rank order).
+ *                      Asynchronous on `stream`; every rank must make the same
+ *                      sequence of calls.  A rank whose peers do not arrive
+ *                      within timeout_ms (<= 0: 1000) writes NaN and sets bit 0
+ *                      of the status word;
+ *   emmy_xchg_status   reads and clears that word.
+ * At most EMMY_XCHG_MAX_RANKS ranks, one GPU each. */
+#define EMMY_XCHG_MAX_RANKS 8
+#define EMMY_XCHG_HANDLE_BYTES 64
+typedef struct emmy_xchg *emmy_xchg_t;
+int emmy_xchg_create(int dev, int nranks, int rank, emmy_xchg_t *out, uint8_t handle[EMMY_XCHG_HANDLE_BYTES]);
+int emmy_xchg_connect(emmy_xchg_t x, const uint8_t *handles);
+int emmy_sum_f32_allreduce(emmy_xchg_t x, const float *data, uint64_t n, float *out, int timeout_ms,
+                           uint64_t stream);
+int emmy_xchg_status(emmy_xchg_t x, uint32_t *status);
+int emmy_xchg_destroy(emmy_xchg_t x);
+
 /* NCCL over NVLink/NVSwitch for the one collective of the path: combining
  * per-GPU partials of a full-array reduction.  No reference counterpart
  * (the reference is single-GPU). */
