@@ -21,10 +21,8 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time

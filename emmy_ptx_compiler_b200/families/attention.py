@@ -35,7 +35,7 @@ from __future__ import annotations
 from dataclasses import dataclass, field
 
 from .. import ir
-from ..cgen import DEVICE_PRELUDE, Emitter, combine_code, ctype, f32_lit, fusable_products, identity_of
+from ..cgen import DEVICE_PRELUDE, Emitter, combine_code, ctype, f32_lit, fusable_products
 from ..errors import UnsupportedIR
 from .common import KernelSource, LaunchPlan, ParamSpec, SM_COUNT, launch_record_source
 

@@ -29,7 +29,6 @@ from dataclasses import dataclass, field
 from .. import ir
 from ..ir import ELEM_BYTES
 from ..cgen import DEVICE_PRELUDE, Emitter, ctype, load_to_kind, store_from
-from ..errors import UnsupportedIR
 from .common import KernelSource, LaunchPlan, ParamSpec, SM_COUNT, launch_record_source
 
 BLOCK = 256

@@ -33,8 +33,8 @@ from __future__ import annotations
 from dataclasses import dataclass, field
 
 from .. import ir
-from ..cgen import (DEVICE_PRELUDE, Emitter, cname, combine_code, ctype, f32_lit, fusable_products, identity_of,
-                    lit_int, load_to_kind, store_from)
+from ..cgen import (DEVICE_PRELUDE, Emitter, combine_code, ctype, f32_lit, fusable_products, identity_of, lit_int,
+                    load_to_kind, store_from)
 from ..errors import UnsupportedIR
 from .common import KernelSource, LaunchPlan, ParamSpec, SM_COUNT, launch_record_source
 from .pointwise import _VEC_HELPERS
@@ -441,7 +441,6 @@ def _row_loop(plan: RowPlan, shapes, dtypes, ptrs, scalar_env, fus, VW: int, T: 
         o(f"{i2}}}")
     declared_row: dict[str, str] = {}
     slot = 0
-    row_em_lines: list[str] = []
     for step in plan.steps:
         if isinstance(step, Pass):
             # per-thread accumulators
@@ -557,7 +556,6 @@ def _row_loop(plan: RowPlan, shapes, dtypes, ptrs, scalar_env, fus, VW: int, T: 
             out.extend(em.lines)
             row_env.update({k: v for k, v in em.env.items()})
             declared_row.update(em.declared)
-    del row_em_lines
     o(f"{i2}__syncthreads();  // shared partials are reused by the next row")
     o(f"{ind}}}")
     return out
