@@ -16,6 +16,7 @@
 #include <chrono>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -632,7 +633,19 @@ int ensure_pipeline(emmy_module *m, size_t nchunks) {
     return EMMY_OK;
 }
 
-constexpr uint64_t kChunkBytes = 32ull << 20;  // streamed bytes per pipeline chunk (in + out)
+constexpr uint64_t kChunkBytesDefault = 64ull << 20;  // streamed bytes per pipeline chunk (in + out)
+constexpr uint64_t kMaxPipelineChunks = 256;
+
+// EMMY_PIPELINE_CHUNK_BYTES overrides the chunk size (bytes of streamed copies per chunk,
+// at least 1 MiB) for callers that tune the copy pipeline to their host link.
+uint64_t pipeline_chunk_bytes() {
+    const char *v = std::getenv("EMMY_PIPELINE_CHUNK_BYTES");
+    if (v && *v) {
+        const unsigned long long b = std::strtoull(v, nullptr, 10);
+        if (b >= (1ull << 20)) return b;
+    }
+    return kChunkBytesDefault;
+}
 
 }  // namespace
 
@@ -671,7 +684,8 @@ int emmy_run_host(emmy_module_t m, void *const *host_ptrs, const size_t *bytes, 
     }
     const uint64_t total = has_range(m) ? m->rec.range_total : 0;
     const uint64_t align = has_range(m) && m->rec.range_align ? m->rec.range_align : 1;
-    if (total < 2 * align || streamed < 2 * kChunkBytes) {
+    const uint64_t chunk_bytes = pipeline_chunk_bytes();
+    if (total < 2 * align || streamed < 2 * chunk_bytes) {
         // one launch: copy in, launch, copy out, all on `stream`
         for (int i = 0; i < nargs; ++i) {
             if (roles[i] == EMMY_ROLE_SCALAR) continue;
@@ -691,7 +705,7 @@ int emmy_run_host(emmy_module_t m, void *const *host_ptrs, const size_t *bytes, 
     // kernel (`stream`) and copy-out (d2h stream), so chunk k's copy-in, chunk
     // k-1's kernel and chunk k-2's copy-out overlap, and both host-link
     // directions are busy at once.
-    uint64_t nchunks = std::max<uint64_t>(2, std::min<uint64_t>(64, streamed / kChunkBytes));
+    uint64_t nchunks = std::max<uint64_t>(2, std::min<uint64_t>(kMaxPipelineChunks, streamed / chunk_bytes));
     uint64_t per = (total + nchunks - 1) / nchunks;
     per = (per + align - 1) / align * align;
     nchunks = (total + per - 1) / per;

@@ -251,7 +251,8 @@ def range_bytes(plan: RowPlan, args: list[str], scalars: dict, dtypes: dict, sha
 
 
 def generate(kop: ir.KernelOp, plan: RowPlan, shapes: dict, dtypes: dict, args: list[str],
-             scalars: dict[str, str], written: set[str], *, bulk_prefetch: bool = False) -> KernelSource:
+             scalars: dict[str, str], written: set[str], *, bulk_prefetch: bool = False,
+             reuse_values: bool = True) -> KernelSource:
     params: list[ParamSpec] = []
     ptrs: dict[str, str] = {}
     sig: list[str] = []
@@ -327,16 +328,20 @@ def generate(kop: ir.KernelOp, plan: RowPlan, shapes: dict, dtypes: dict, args: 
             w("            emmy::fence_barrier_init();")
             w("        }")
             w("        __syncthreads();")
-            lines.extend(_row_loop(plan, shapes, dtypes, ptrs, scalar_env, fus, 4, T, "        ", bulk=True))
+            lines.extend(_row_loop(plan, shapes, dtypes, ptrs, scalar_env, fus, 4, T, "        ", bulk=True,
+                                   reuse_values=reuse_values))
             w("    } else if (aligned) {")
         else:
             w("    if (aligned) {")
-        lines.extend(_row_loop(plan, shapes, dtypes, ptrs, scalar_env, fus, 4, T, "        "))
+        lines.extend(_row_loop(plan, shapes, dtypes, ptrs, scalar_env, fus, 4, T, "        ",
+                               reuse_values=reuse_values))
         w("    } else {")
-        lines.extend(_row_loop(plan, shapes, dtypes, ptrs, scalar_env, fus, 1, T, "        "))
+        lines.extend(_row_loop(plan, shapes, dtypes, ptrs, scalar_env, fus, 1, T, "        ",
+                               reuse_values=reuse_values))
         w("    }")
     else:
-        lines.extend(_row_loop(plan, shapes, dtypes, ptrs, scalar_env, fus, 1, T, "    "))
+        lines.extend(_row_loop(plan, shapes, dtypes, ptrs, scalar_env, fus, 1, T, "    ",
+                               reuse_values=reuse_values))
     w("}")
     grid = max(1, min(plan.rows, SM_COUNT * 8))
     launch = LaunchPlan(grid=(grid, 1, 1), block=(T, 1, 1), smem=dyn, range_total=plan.rows, range_align=1,
@@ -355,6 +360,96 @@ def generate(kop: ir.KernelOp, plan: RowPlan, shapes: dict, dtypes: dict, args: 
 
 
 STAGE_BYTES_MAX = 96 * 1024   # shared-memory stage for the next row (bulk prefetch)
+KEEP_MAX = 2                  # element values carried in registers from one pass to a later one
+_NO_REUSE_OPS = {"multiply", "mul", "square", "log", "log_fast", "silu", "where"}
+
+
+def reuse_plan(plan: RowPlan, scalars: dict) -> tuple[dict, dict]:
+    """Element values a later pass recomputes exactly as an earlier pass did
+    (softmax's exp(x - max) in the sum pass and again in the output pass).
+
+    Every element value gets a structural key: the streamed tensor it loads,
+    the per-row values and literals it reads, and the op tree above them.
+    Subtrees with products are left out, since whether the assembler
+    contracts a product into an add depends on how each name is used.  A
+    later Assign whose key matches an earlier pass's value reads that value
+    from registers instead of recomputing it; the arithmetic and its order
+    are the same, so the bits are.
+
+    Returns ({(pass index, name): slot} for the values to keep,
+             {(pass index, name): slot} for the Assigns that reuse them)."""
+    row_defs: dict[str, int] = {}
+    for st in plan.steps:
+        if not isinstance(st, Pass):
+            body = st[1] if isinstance(st[1], tuple) else (st[1],)
+            for t in ir.walk(body):
+                for n in _defines(t):
+                    row_defs[n] = row_defs.get(n, 0) + 1
+        else:
+            for a, _ in st.accs:
+                row_defs[a] = row_defs.get(a, 0) + 1
+    avail: dict = {}
+    keep: dict = {}
+    reuse: dict = {}
+    passes = [st for st in plan.steps if isinstance(st, Pass)]
+    for pi, ps in enumerate(passes):
+        keys: dict[str, tuple] = {}
+        stmts = list(ir.body_stmts(ps.loop.body))
+        counts: dict[str, int] = {}
+        for t in stmts:
+            for n in _defines(t):
+                counts[n] = counts.get(n, 0) + 1
+
+        def key_of(x):
+            if not isinstance(x, str):
+                return ("num", float(x))
+            if x in keys:
+                return keys[x]
+            if x in row_defs:
+                return ("row", x) if row_defs[x] == 1 else None
+            if x in scalars:
+                return ("scalar", x)
+            return None
+
+        for t in stmts:
+            if isinstance(t, ir.Load) and t.input in plan.streamed and len(t.names) == 1 \
+                    and counts.get(t.names[0]) == 1:
+                keys[t.names[0]] = ("load", t.input)
+            elif isinstance(t, ir.Let) and isinstance(t.value, ir.Literal) and counts.get(t.name) == 1:
+                keys[t.name] = ("lit", float(t.value.value))
+            elif isinstance(t, ir.Assign) and counts.get(t.name) == 1:
+                op = ir.op_name(t.op)
+                ks = [key_of(x) for x in t.args]
+                if op in _NO_REUSE_OPS or any(k_ is None for k_ in ks):
+                    continue
+                k = ("op", op, ir.canon_dtype(t.dtype) if t.dtype is not None else "f32", tuple(ks))
+                keys[t.name] = k
+                if k in avail and avail[k][0] < pi:
+                    src = avail[k]
+                    if src not in keep:
+                        if len(keep) >= KEEP_MAX:
+                            continue
+                        keep[src] = len(keep)
+                    reuse[(pi, t.name)] = keep[src]
+                elif k not in avail and k[1] not in ("copy", "neg", "negative", "abs", "absolute"):
+                    avail[k] = (pi, t.name)
+    # a reused value that only feeds other reused values is dead in its pass: drop it
+    for pi, ps in enumerate(passes):
+        stmts = list(ir.body_stmts(ps.loop.body))
+        live_reads: set[str] = set()
+        for t in stmts:
+            if isinstance(t, ir.Assign) and (pi, t.name) in reuse:
+                continue
+            live_reads |= set(t.reads())
+        for t in stmts:
+            if isinstance(t, ir.Assign) and (pi, t.name) in reuse and t.name not in live_reads:
+                del reuse[(pi, t.name)]
+    used = sorted(set(reuse.values()))
+    renum = {old: new for new, old in enumerate(used)}
+    keep = {src: renum[sl] for src, sl in keep.items() if sl in renum}
+    reuse = {k: renum[sl] for k, sl in reuse.items()}
+    return keep, reuse
+
 
 
 def _stage_bytes(plan: RowPlan, dtypes) -> int:
@@ -362,7 +457,7 @@ def _stage_bytes(plan: RowPlan, dtypes) -> int:
 
 
 def _row_loop(plan: RowPlan, shapes, dtypes, ptrs, scalar_env, fus, VW: int, T: int, ind: str,
-              bulk: bool = False) -> list[str]:
+              bulk: bool = False, reuse_values: bool = True) -> list[str]:
     """The persistent loop over this CTA's rows, every pass inside it, for
     vector width VW (4: float4 per access, 1: scalar).  With ``bulk`` the next
     row of every streamed tensor is brought into shared memory by one bulk
@@ -441,8 +536,27 @@ def _row_loop(plan: RowPlan, shapes, dtypes, ptrs, scalar_env, fus, VW: int, T: 
         o(f"{i2}}}")
     declared_row: dict[str, str] = {}
     slot = 0
+    keep, reuse = reuse_plan(plan, scalar_env) if cached and reuse_values else ({}, {})
+    for k_slot in sorted(set(keep.values())):
+        if VW == 4:
+            o(f"{i2}EmmyVec<float, 4> kp{k_slot}[{EPT}];")
+        else:
+            o(f"{i2}float kp{k_slot}[{EPT}];")
+    pass_index = -1
     for step in plan.steps:
         if isinstance(step, Pass):
+            pass_index += 1
+            body = []
+            for t in ir.body_stmts(step.loop.body):
+                if isinstance(t, ir.Assign) and (pass_index, t.name) in reuse:
+                    body.append(ir.Load(names=(t.name,), input=f"__kp{reuse[(pass_index, t.name)]}", index=(),
+                                        dtype=ir.DataType("f32", "float32", 4)))
+                    continue
+                body.append(t)
+                if isinstance(t, ir.Assign) and (pass_index, t.name) in keep:
+                    body.append(ir.Write(output=f"__kp{keep[(pass_index, t.name)]}", index=(), values=(t.name,),
+                                         value_dtype=ir.DataType("f32", "float32", 4)))
+            pass_body = tuple(body)
             # per-thread accumulators
             acc_vars = {}
             for a, op in step.accs:
@@ -484,6 +598,8 @@ def _row_loop(plan: RowPlan, shapes, dtypes, ptrs, scalar_env, fus, VW: int, T: 
                     o(f"{body_ind}{ctype(dt)} st{wi}_{ln} = {store_from('f32', '0.0f', dt)};")
             for ln in range(VW):
                 def load_hook(s, k, ln=ln):
+                    if s.input.startswith("__kp"):  # a value an earlier pass computed
+                        return "f32", (f"kp{s.input[4:]}[e].v[{ln}]" if VW == 4 else f"kp{s.input[4:]}[e]")
                     dt = ir.canon_dtype(s.dtype or dtypes.get(s.input))
                     if s.input in plan.streamed:
                         src = f"cx_{_c(s.input)}[e]" if cached else f"sx_{_c(s.input)}"
@@ -494,6 +610,9 @@ def _row_loop(plan: RowPlan, shapes, dtypes, ptrs, scalar_env, fus, VW: int, T: 
                     return load_to_kind(f"{src}.v[{ln}]" if VW == 4 else src, dt)
 
                 def write_hook(s, k, kind, code, ln=ln):
+                    if s.output.startswith("__kp"):  # kept for a later pass
+                        return (f"kp{s.output[4:]}[e].v[{ln}] = {code};" if VW == 4
+                                else f"kp{s.output[4:]}[e] = {code};")
                     dt = ir.canon_dtype(s.value_dtype or dtypes.get(s.output))
                     return f"st{writes.index(s)}_{ln} = {store_from(kind, code, dt)};"
 
@@ -507,7 +626,7 @@ def _row_loop(plan: RowPlan, shapes, dtypes, ptrs, scalar_env, fus, VW: int, T: 
                 for key, var in declared_row.items():
                     em.declared[key] = var
                 em.bind_const(step.loop.axis.name, "int", f"(u * {VW}LL + {ln})" if VW == 4 else "u")
-                em.run(step.loop.body)
+                em.run(pass_body)
                 o(f"{body_ind}{{")
                 out.extend(em.lines)
                 o(f"{body_ind}}}")
