@@ -285,15 +285,17 @@ def _tree_phase(red_axis: Axis, start: str, body: tuple, acc: str, op: str) -> t
     )
 
 
-def rownorm_case(cid: str, rows: int, cols: int, kind: str, *, config: str | None = None) -> Case:
+def rownorm_case(cid: str, rows: int, cols: int, kind: str, *, config: str | None = None,
+                 dtype: DataType = F32) -> Case:
     """Fused row reduction + pointwise epilogue, the rmsnorm / softmax / l2norm
     class (the reference's f01-f03): one block per row runs one or two
     reduction phases on the warp/tree schedule, then a strided pass that
     rereads the row and writes the normalised values."""
     ax = Axis("a1", Dim(cols))
     idx = (Var("a0"), Var("a1"))
-    ld = lambda nm: Load(names=(nm,), input="x", index=idx, dtype=F32)  # noqa: E731
+    ld = lambda nm: Load(names=(nm,), input="x", index=idx, dtype=dtype)  # noqa: E731
     ins = ["x"]
+    dn = _dt(dtype)
     if kind == "rmsnorm":
         entry = "k_rmsnorm"
         ins = ["x", "w"]
@@ -304,7 +306,7 @@ def rownorm_case(cid: str, rows: int, cols: int, kind: str, *, config: str | Non
                Let("eps", Literal(1e-6, "float"), F32),
                Assign("mse", EW("add"), ("ms", "eps"), F32),
                Assign("r", EW("rsqrt"), ("mse",), F32))
-        tail = (ld("in1"), Load(names=("wv",), input="w", index=(Var("a1"),), dtype=F32),
+        tail = (ld("in1"), Load(names=("wv",), input="w", index=(Var("a1"),), dtype=dtype),
                 Assign("xr", EW("multiply"), ("in1", "r"), F32),
                 Assign("yv", EW("multiply"), ("xr", "wv"), F32))
     elif kind == "softmax":
@@ -329,23 +331,28 @@ def rownorm_case(cid: str, rows: int, cols: int, kind: str, *, config: str | Non
     else:
         raise ValueError(kind)
     final = StridedLoop(axis=ax, start=Var("a1_co"), step=Literal(BT, "int"),
-                        body=tail + (Write(output="y", index=idx, values=("yv",), value_dtype=F32),))
+                        body=tail + (Write(output="y", index=idx, values=("yv",), value_dtype=dtype),))
     body = Tile(axes=(Axis("a0", Dim(rows)), Axis("a1_co", Dim(BT))), body=phases + mid + (final,),
                 block_threads=BT)
-    nodes = {"x": _input("x", [rows, cols])}
+    nodes = {"x": _input("x", [rows, cols], dn)}
     if "w" in ins:
-        nodes["w"] = _input("w", [cols])
-    nodes["y"] = _kernel(entry, body, ins, [("y", [rows, cols], "f32")])
+        nodes["w"] = _input("w", [cols], dn)
+    nodes["y"] = _kernel(entry, body, ins, [("y", [rows, cols], dn)])
     graph = {"inputs": ins, "outputs": ["y"], "nodes": nodes}
-    args = [_arg("x", [rows, cols], init=NORM(), seed=0)]
+    args = [_arg("x", [rows, cols], dn, init=NORM(), seed=0)]
     if "w" in ins:
-        args.append(_arg("w", [cols], init=UNIF(0.5, 1.5), seed=1))
-    args.append(_arg("y", [rows, cols], output=True))
+        args.append(_arg("w", [cols], dn, init=UNIF(0.5, 1.5), seed=1))
+    args.append(_arg("y", [rows, cols], dn, output=True))
     kern = _meta_kernel("y", entry, ins + ["y"], [rows, 1, 1], [BT, 1, 1], args)
     # every kind uses an approximate instruction (rsqrt.approx, ex2.approx): the
     # oracle's libm stand-ins pin it within APPROX_ORACLE, not bit for bit
     check = {"kind": "rtol", "rtol": 1e-5, "atol": 1e-6, "oracle": APPROX_ORACLE}
-    return Case(cid, entry, graph, kern, family="rownorm", config=config, check=check)
+    if dtype.name != "f32":
+        # the reference cannot lower bf16 loads (ptxas rejects its ld.global.nc.bf16 form);
+        # ours and the oracle round the same f32 result to bf16, up to one bf16 ulp apart
+        check = {"kind": "rtol", "rtol": 8e-3, "atol": 1e-3}
+    return Case(cid, entry, graph, kern, family="rownorm", config=config, check=check,
+                ref=dtype.name == "f32")
 
 
 def attention_case(cid: str, seq: int, dim: int, *, config: str | None = None, k_rows: bool = False) -> Case:
@@ -889,6 +896,8 @@ def all_cases() -> list[Case]:
         cases.append(rownorm_case(f"f_{kind}_7x4096", 7, 4096, kind))
         cases.append(rownorm_case(f"f_{kind}_33x130", 33, 130, kind))
         cases.append(rownorm_case(f"f_{kind}_bench_16384x8192", 16384, 8192, kind, config=f"f_{kind}"))
+    cases.append(rownorm_case("f_rmsnorm_bf16_64x1000", 64, 1000, "rmsnorm", dtype=BF16))
+    cases.append(rownorm_case("f_softmax_bf16_33x4096", 33, 4096, "softmax", dtype=BF16))
     # naive attention (one thread per output cell, scores recomputed per pass)
     cases.append(attention_case("a_attn_64x32", 64, 32))
     cases.append(attention_case("a_attn_100x48", 100, 48))
