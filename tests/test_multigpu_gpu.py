@@ -65,7 +65,8 @@ def test_sharded_sum_with_nccl_combine():
     assert res[0][3] == res[1][3], "every rank sees the same combined sum"
 
 
-@pytest.mark.parametrize("cid", ["c2_gelu_256x4096", "c5_gemm_384x1024x768", "c5_gemm_200x136x300"])
+@pytest.mark.parametrize("cid", ["c2_gelu_256x4096", "c5_gemm_384x1024x768", "c5_gemm_200x136x300",
+                                 "f_softmax_64x1000", "a_attn_100x48"])
 def test_sharded_launch_matches_one_gpu(cid):
     """emmy_launch_sharded over 2 GPUs from one process: each device holds only
     its shard of the streamed parameters (rows of x / y, rows of A / C) and a

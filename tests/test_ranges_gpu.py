@@ -44,6 +44,8 @@ def _ranges(total: int, align: int, pieces: list[int]) -> list[tuple[int, int]]:
     ("c5_gemm_384x1024x768", [1]),
     ("c5_gemm_128x64x256", [1]),
     ("c5_gemm_200x136x300", [1, 2]),      # SIMT tiles of 64 rows
+    ("f_softmax_64x1000", [3, 10]),       # row-fused: units are rows
+    ("a_attn_100x48", [2, 5]),            # attention: blocks of 4 query rows
 ])
 def test_ranges_compose_to_whole(cid, pieces, cuda_device):
     import torch
