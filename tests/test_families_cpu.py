@@ -1,0 +1,97 @@
+"""Host-side checks of the family planners and the launch record (CPU only)."""
+
+from __future__ import annotations
+
+import json
+import subprocess
+
+import pytest
+
+from conftest import CASES, REPO
+
+
+def _plan_inputs(cid: str):
+    from emmy_ptx_compiler_b200 import frontend
+    ir_path = next((CASES / cid).glob("*.ir.json"))
+    raw = json.loads(ir_path.read_text())
+    info = frontend.load_graph(raw)
+    mk = frontend.load_meta_kernel(ir_path, info.kop.name)
+    shapes, dtypes = frontend.load_shapes(raw, info.kop, mk)
+    return info.kop, shapes, dtypes, frontend.arg_order_for(info.kop, mk)
+
+
+def test_launch_record_initialiser_matches_the_struct(tmp_path):
+    """The Python-emitted aggregate initialiser fills the C struct field by
+    field: compile it on the host against the header and read it back."""
+    from emmy_ptx_compiler_b200.families.common import LaunchPlan, ParamSpec, TmapSpec, launch_record_source
+    lp = LaunchPlan((7, 2, 1), (192, 1, 1), smem=197888, cluster=(2, 1, 1), fill_waves=3, grid_quantum=16,
+                    range_total=12345, range_align=256, range_bytes=[8, 0, 4])
+    params = [ParamSpec("a", "ptr", "bf16"), ParamSpec("s", "scalar", "f32"), ParamSpec("c", "ptr", "f32")]
+    tm = TmapSpec(0, 9, [64, 128], [128], [64, 32], 3, 3)
+    rec = launch_record_source("gemm", lp, params, [tm])
+    prog = tmp_path / "rec.cpp"
+    prog.write_text(
+        "#define __device__\n#include <cstdio>\n#include <cstddef>\n" + rec + """
+int main() {
+    const EmmyLaunchRecord &r = emmy_launch_record;
+    std::printf("%u %u %u %u %u %u %u %u %u %llu %u %llu %llu %llu %u %u\\n", r.family, r.flags, r.grid[0], r.grid[1],
+                r.block[0], r.dyn_smem, r.nparams, r.param_kind[1], r.ntmaps,
+                (unsigned long long)r.range_total, r.range_align, (unsigned long long)r.range_bytes[0],
+                (unsigned long long)r.range_bytes[2], (unsigned long long)r.tmaps[0].dims[1], r.tmaps[0].box[1],
+                r.grid_quantum);
+    return 0;
+}
+""")
+    exe = tmp_path / "rec"
+    cc = subprocess.run(["g++", "-std=c++17", f"-I{REPO / 'include'}", str(prog), "-o", str(exe)],
+                        capture_output=True, text=True)
+    assert cc.returncode == 0, cc.stderr[-2000:]
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()
+    # family 3 (gemm); flags = cluster 2 | FILL_GRID | RANGE; grid[0] carries the waves
+    assert out == ["3", str(2 | 0x100 | 0x200), "3", "2", "192", "197888", "3", "1", "1",
+                   "12345", "256", "8", "4", "128", "32", "16"]
+
+
+def test_softmax_reuses_its_exp_across_passes():
+    from emmy_ptx_compiler_b200.families import rownorm
+    kop, shapes, dtypes, args = _plan_inputs("f_softmax_64x1000")
+    plan = rownorm.match(kop, shapes, dtypes)
+    keep, reuse = rownorm.reuse_plan(plan, {})
+    assert keep == {(1, "e1"): 0}
+    assert reuse == {(2, "e2"): 0}
+
+
+def test_rmsnorm_has_nothing_to_reuse():
+    """Its later pass multiplies (products are never reused: contraction
+    depends on how each product is used)."""
+    from emmy_ptx_compiler_b200.families import rownorm
+    kop, shapes, dtypes, args = _plan_inputs("f_rmsnorm_64x1000")
+    plan = rownorm.match(kop, shapes, dtypes)
+    assert rownorm.reuse_plan(plan, {}) == ({}, {})
+
+
+def test_row_fused_plan_streams_and_ranges():
+    from emmy_ptx_compiler_b200.families import rownorm
+    kop, shapes, dtypes, args = _plan_inputs("f_rmsnorm_64x1000")
+    plan = rownorm.match(kop, shapes, dtypes)
+    assert plan.streamed == ["x"] and plan.vectors == ["w"] and plan.outputs == ["y"]
+    assert rownorm.range_bytes(plan, args, {}, dtypes, shapes) == [4000, 0, 4000]
+
+
+def test_attention_plan_splits_row_and_cell_work():
+    from emmy_ptx_compiler_b200.families import attention
+    kop, shapes, dtypes, args = _plan_inputs("a_attn_64x32")
+    plan = attention.match(kop, shapes, dtypes)
+    loops = [s for s in plan.steps if isinstance(s, attention.KeyLoop)]
+    assert len(loops) == 3 and plan.k_dk and plan.v == "v" and plan.cell_accs == ["acc"]
+    assert [a for a, _ in loops[0].row_accs] == ["m"] and [a for a, _ in loops[1].row_accs] == ["den"]
+    assert loops[2].stash == ["wt"] and not loops[2].row_accs
+
+
+@pytest.mark.parametrize("cid,family", [("c3_rowsummax_64x5000", "reduction"), ("c2_gelu_64x1000", "pointwise"),
+                                        ("c5_gemm_128x64x256", "gemm")])
+def test_new_families_do_not_claim_other_kernels(cid, family):
+    from emmy_ptx_compiler_b200.families import attention, rownorm
+    kop, shapes, dtypes, args = _plan_inputs(cid)
+    assert attention.match(kop, shapes, dtypes) is None
+    assert rownorm.match(kop, shapes, dtypes) is None
