@@ -395,39 +395,84 @@ def time_reference_ptx(spec, bufs, local: int, units: int, unit: str) -> dict:
 # ---------------------------------------------------------------------------- CPU arms
 
 
+# bounded CPU samples of each workload for the oracle arms: (rows per task, text)
+CPU_SAMPLES = {
+    "c2": (16, "rows of the GELU chain over 16384 columns"),
+    "c3": (4, "rows of 65536 reduced (sum and max) in the reference's strided schedule order"),
+    "c4": (1, "a 2^20+3-element full sum in the reference's strided schedule order"),
+    "c5": (1, "rows of A (1 x 8192) times B (8192 x 16384), sequential fma over k, plus bias and ReLU"),
+}
+
+
+def _scaled(kop, axes):
+    """``kop`` with its Tile's axes replaced (extents of a bounded sample)."""
+    import copy
+    from emmy._core import Axis, Dim
+    tile = copy.copy(list(kop.body)[0])
+    tile.axes = tuple(Axis(n, Dim(e)) for n, e in axes)
+    k2 = copy.copy(kop)
+    k2.body = (tile,)
+    return k2
+
+
 def _oracle_sample(cfg: str, rows: int):
-    """(callable, algorithmic units it processes) for a bounded CPU sample."""
+    """(callable, algorithmic units it processes) for a bounded CPU sample of
+    the config's workload, evaluated by the oracle (oracle/interp.py)."""
     import numpy as np
     sys.path.insert(0, str(REPO / "oracle"))
     import interp
     case_id, unit, bound, units, _ = CONFIGS[cfg]
-    kop, meta, mk, shapes, dtypes = interp.load_case(CASES / case_id)
     rng = np.random.default_rng(0)
     if cfg == "c2":
+        kop, meta, mk, shapes, dtypes = interp.load_case(CASES / case_id)
         cols = 16384
         shp = dict(shapes, x=(rows, cols), y=(rows, cols))
         ins = {"x": rng.standard_normal((rows, cols), dtype=np.float32),
                "s": rng.uniform(0.5, 1.5, cols).astype(np.float32),
                "t": rng.uniform(-0.1, 0.1, cols).astype(np.float32)}
-        body = list(kop.body)[0]
-        import copy
-        tile = copy.copy(body)
-        from emmy._core import Axis, Dim
-        tile.axes = (Axis("a0", Dim(rows)), Axis("a1", Dim(cols)))
-        kop2 = copy.copy(kop)
-        kop2.body = (tile,)
-        fn = lambda: interp.evaluate(kop2, shp, dtypes, ins, {"y": (rows, cols)})  # noqa: E731
+        k2 = _scaled(kop, [("a0", rows), ("a1", cols)])
+        fn = lambda: interp.evaluate(k2, shp, dtypes, ins, {"y": (rows, cols)})  # noqa: E731
         return fn, rows * cols * 8 + 2 * cols * 4
+    if cfg == "c3":
+        kop, meta, mk, shapes, dtypes = interp.load_case(CASES / case_id)
+        cols = 65536
+        axes = [(a.name, int(a.extent.value)) for a in list(kop.body)[0].axes]
+        shp = dict(shapes, x=(rows, cols), sum_1=(rows,), max_1=(rows,))
+        ins = {"x": rng.standard_normal((rows, cols), dtype=np.float32)}
+        k2 = _scaled(kop, [(axes[0][0], rows)] + axes[1:])
+        fn = lambda: interp.evaluate(k2, shp, dtypes, ins, {"sum_1": (rows,), "max_1": (rows,)})  # noqa: E731
+        return fn, rows * cols * 4 + 2 * rows * 4
+    if cfg == "c4":
+        kop, meta, mk, shapes, dtypes = interp.load_case(CASES / "c4_sum_1048579")
+        n = int(shapes["x"][0])
+        ins = {"x": rng.uniform(-1, 1, n).astype(np.float32)}
+        fn = lambda: interp.evaluate(kop, shapes, dtypes, ins, {"sum_1": ()})  # noqa: E731
+        return fn, n * 4 + 4
+    if cfg == "c5":
+        kop, meta, mk, shapes, dtypes = interp.load_case(CASES / case_id)
+        K, N = 8192, 16384
+        shp = dict(shapes, A=(rows, K), C=(rows, N))
+        ins = {"A": interp.bf16_round(rng.normal(0, 0.02, (rows, K)).astype(np.float32)),
+               "B": interp.bf16_round(rng.normal(0, 0.02, (K, N)).astype(np.float32)),
+               "bias": rng.normal(0, 0.02, N).astype(np.float32)}
+        k2 = _scaled(kop, [("i", rows), ("j", N)])
+        fn = lambda: interp.evaluate(k2, shp, dtypes, ins, {"C": (rows, N)})  # noqa: E731
+        return fn, 2 * rows * N * K
     raise ValueError(f"no CPU sample defined for {cfg}")
 
 
+def _units_scale(unit: str) -> float:
+    return 1e9 if unit == "GB/s" else 1e12
+
+
 def cpu_baseline(cfg: str, seconds: float = 10.0) -> dict:
-    """The oracle port on the host cores: rows split over a thread pool
+    """The oracle port on the host cores: samples split over a thread pool
     (numpy and the oracle's C loops release the GIL)."""
-    if cfg != "c2":
+    if cfg not in CPU_SAMPLES:
         return {"unavailable": f"CPU baseline for {cfg} not wired"}
+    unit = CONFIGS[cfg][1]
     threads = len(os.sched_getaffinity(0))
-    rows_per_task = 16
+    rows_per_task, what = CPU_SAMPLES[cfg]
     fn, units = _oracle_sample(cfg, rows_per_task)
     fn()  # warm
     done_units = 0
@@ -437,19 +482,19 @@ def cpu_baseline(cfg: str, seconds: float = 10.0) -> dict:
             list(ex.map(lambda _: fn(), range(threads)))
             done_units += units * threads
     el = time.perf_counter() - t0
-    return {"value": round(done_units / el / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"oracle/interp.py GELU chain, {threads} threads x {rows_per_task} rows of 16384 "
-                      f"per round, {el:.1f} s of rounds"}
+    return {"value": round(done_units / el / _units_scale(unit), 4), "unit": unit, "cores": threads, "kind": "port",
+            "sample": f"oracle/interp.py, {threads} threads x {rows_per_task} {what} per round, "
+                      f"{el:.1f} s of rounds"}
 
 
 def run_reference(args, rank: int) -> dict | None:
     if rank != 0:
         return None
     case_id, unit, bound, units, workload = CONFIGS[args.config]
-    if args.config != "c2":
+    if args.config not in CPU_SAMPLES:
         return {"impl": "reference", "unavailable": f"reference CPU arm not wired for {args.config}"}
     threads = len(os.sched_getaffinity(0))
-    rows_per_task = 16
+    rows_per_task, what = CPU_SAMPLES[args.config]
     fn, units_task = _oracle_sample(args.config, rows_per_task)
     with ThreadPoolExecutor(max_workers=threads) as ex:
         for _ in range(args.warmup):
@@ -458,14 +503,15 @@ def run_reference(args, rank: int) -> dict | None:
         for _ in range(args.steps):
             list(ex.map(lambda _: fn(), range(threads)))
         el = time.perf_counter() - t0
-    value = units_task * threads * args.steps / el / 1e9
-    return {"metric": METRIC, "value": round(value, 3), "unit": unit, "n_gpus": args.gpus, "steps": args.steps,
+    value = units_task * threads * args.steps / el / _units_scale(unit)
+    return {"metric": METRIC, "value": round(value, 4), "unit": unit, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32" if args.config != "c5" else "bf16",
+            "data": "synthetic", "impl": "reference",
             "config": {"workload": workload, "case": case_id},
-            "cpu_baseline": {"value": round(value, 3), "unit": unit, "cores": threads, "kind": "port",
-                             "sample": f"{threads} threads x {rows_per_task} rows of 16384 per step"},
-            "e2e": {"value": round(value, 3), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": threads, "kind": "port",
+                             "sample": f"{threads} threads x {rows_per_task} {what} per step"},
+            "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def main() -> int:
