@@ -647,6 +647,68 @@ uint64_t pipeline_chunk_bytes() {
     return kChunkBytesDefault;
 }
 
+// The chunk pipeline of emmy_run_host (caller holds g_mu, device is current).
+int run_pipeline(emmy_module *m, void *const *host_ptrs, const size_t *bytes, const uint8_t *roles, int nargs,
+                 uint64_t stream, std::vector<uint64_t> &args, uint64_t total, uint64_t align, uint64_t streamed,
+                 uint64_t chunk_bytes) {
+    CUstream s = reinterpret_cast<CUstream>(stream);
+    int rc = EMMY_OK;
+    // Unit ranges [b, e) flow through copy-in (h2d stream), the
+    // kernel (`stream`) and copy-out (d2h stream), so chunk k's copy-in, chunk
+    // k-1's kernel and chunk k-2's copy-out overlap, and both host-link
+    // directions are busy at once.
+    uint64_t nchunks = std::max<uint64_t>(2, std::min<uint64_t>(kMaxPipelineChunks, streamed / chunk_bytes));
+    uint64_t per = (total + nchunks - 1) / nchunks;
+    per = (per + align - 1) / align * align;
+    nchunks = (total + per - 1) / per;
+    if ((rc = ensure_pipeline(m, nchunks))) return rc;
+    CU(g_drv.cuEventRecord(m->ev_start, s), "cuEventRecord");
+    CU(g_drv.cuStreamWaitEvent(m->h2d, m->ev_start, 0), "cuStreamWaitEvent");
+    CU(g_drv.cuStreamWaitEvent(m->d2h, m->ev_start, 0), "cuStreamWaitEvent");
+    for (int i = 0; i < nargs; ++i) {
+        if (roles[i] == EMMY_ROLE_SCALAR) continue;
+        if (is_in(roles[i]) && !m->rec.range_bytes[i])
+            CU(g_drv.cuMemcpyHtoDAsync(m->dbuf[i], host_ptrs[i], bytes[i], m->h2d), "cuMemcpyHtoDAsync");
+        if (roles[i] == EMMY_ROLE_OUT_ZEROED)
+            CU(g_drv.cuMemsetD8Async(m->dbuf[i], 0, bytes[i], s), "cuMemsetD8Async");
+    }
+    CU(g_drv.cuEventRecord(m->ev_whole, m->h2d), "cuEventRecord");
+    CU(g_drv.cuStreamWaitEvent(s, m->ev_whole, 0), "cuStreamWaitEvent");
+    for (uint64_t k = 0; k < nchunks; ++k) {
+        const uint64_t b = k * per, e = std::min(total, b + per);
+        for (int i = 0; i < nargs; ++i) {
+            if (roles[i] == EMMY_ROLE_SCALAR || !is_in(roles[i]) || !m->rec.range_bytes[i]) continue;
+            size_t lo, hi;
+            unit_bytes(m, i, b, e, bytes[i], &lo, &hi);
+            if (hi > lo)
+                CU(g_drv.cuMemcpyHtoDAsync(m->dbuf[i] + lo, static_cast<const char *>(host_ptrs[i]) + lo, hi - lo,
+                                           m->h2d),
+                   "cuMemcpyHtoDAsync");
+        }
+        CU(g_drv.cuEventRecord(m->ev_in[k], m->h2d), "cuEventRecord");
+        CU(g_drv.cuStreamWaitEvent(s, m->ev_in[k], 0), "cuStreamWaitEvent");
+        if ((rc = launch_locked(m, args.data(), nargs, nullptr, nullptr, stream, b, e))) return rc;
+        CU(g_drv.cuEventRecord(m->ev_out[k], s), "cuEventRecord");
+        CU(g_drv.cuStreamWaitEvent(m->d2h, m->ev_out[k], 0), "cuStreamWaitEvent");
+        for (int i = 0; i < nargs; ++i) {
+            if (roles[i] == EMMY_ROLE_SCALAR || !is_out(roles[i]) || !m->rec.range_bytes[i]) continue;
+            size_t lo, hi;
+            unit_bytes(m, i, b, e, bytes[i], &lo, &hi);
+            if (hi > lo)
+                CU(g_drv.cuMemcpyDtoHAsync(static_cast<char *>(host_ptrs[i]) + lo, m->dbuf[i] + lo, hi - lo, m->d2h),
+                   "cuMemcpyDtoHAsync");
+        }
+    }
+    // outputs written whole by every launch leave after the last one (d2h already waits on it)
+    for (int i = 0; i < nargs; ++i)
+        if (roles[i] != EMMY_ROLE_SCALAR && is_out(roles[i]) && !m->rec.range_bytes[i])
+            CU(g_drv.cuMemcpyDtoHAsync(host_ptrs[i], m->dbuf[i], bytes[i], m->d2h), "cuMemcpyDtoHAsync");
+    CU(g_drv.cuStreamSynchronize(m->d2h), "cuStreamSynchronize");
+    CU(g_drv.cuStreamSynchronize(s), "cuStreamSynchronize");
+    CU(g_drv.cuStreamSynchronize(m->h2d), "cuStreamSynchronize");
+    return EMMY_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -701,60 +763,14 @@ int emmy_run_host(emmy_module_t m, void *const *host_ptrs, const size_t *bytes, 
         CU(g_drv.cuStreamSynchronize(s), "cuStreamSynchronize");
         return EMMY_OK;
     }
-    // Chunk pipeline: unit ranges [b, e) flow through copy-in (h2d stream), the
-    // kernel (`stream`) and copy-out (d2h stream), so chunk k's copy-in, chunk
-    // k-1's kernel and chunk k-2's copy-out overlap, and both host-link
-    // directions are busy at once.
-    uint64_t nchunks = std::max<uint64_t>(2, std::min<uint64_t>(kMaxPipelineChunks, streamed / chunk_bytes));
-    uint64_t per = (total + nchunks - 1) / nchunks;
-    per = (per + align - 1) / align * align;
-    nchunks = (total + per - 1) / per;
-    if ((rc = ensure_pipeline(m, nchunks))) return rc;
-    CU(g_drv.cuEventRecord(m->ev_start, s), "cuEventRecord");
-    CU(g_drv.cuStreamWaitEvent(m->h2d, m->ev_start, 0), "cuStreamWaitEvent");
-    CU(g_drv.cuStreamWaitEvent(m->d2h, m->ev_start, 0), "cuStreamWaitEvent");
-    for (int i = 0; i < nargs; ++i) {
-        if (roles[i] == EMMY_ROLE_SCALAR) continue;
-        if (is_in(roles[i]) && !m->rec.range_bytes[i])
-            CU(g_drv.cuMemcpyHtoDAsync(m->dbuf[i], host_ptrs[i], bytes[i], m->h2d), "cuMemcpyHtoDAsync");
-        if (roles[i] == EMMY_ROLE_OUT_ZEROED)
-            CU(g_drv.cuMemsetD8Async(m->dbuf[i], 0, bytes[i], s), "cuMemsetD8Async");
+    rc = run_pipeline(m, host_ptrs, bytes, roles, nargs, stream, args, total, align, streamed, chunk_bytes);
+    if (rc) {
+        // leave no copy or kernel of this call in flight on the module's buffers (best effort)
+        g_drv.cuStreamSynchronize(m->h2d);
+        g_drv.cuStreamSynchronize(s);
+        g_drv.cuStreamSynchronize(m->d2h);
     }
-    CU(g_drv.cuEventRecord(m->ev_whole, m->h2d), "cuEventRecord");
-    CU(g_drv.cuStreamWaitEvent(s, m->ev_whole, 0), "cuStreamWaitEvent");
-    for (uint64_t k = 0; k < nchunks; ++k) {
-        const uint64_t b = k * per, e = std::min(total, b + per);
-        for (int i = 0; i < nargs; ++i) {
-            if (roles[i] == EMMY_ROLE_SCALAR || !is_in(roles[i]) || !m->rec.range_bytes[i]) continue;
-            size_t lo, hi;
-            unit_bytes(m, i, b, e, bytes[i], &lo, &hi);
-            if (hi > lo)
-                CU(g_drv.cuMemcpyHtoDAsync(m->dbuf[i] + lo, static_cast<const char *>(host_ptrs[i]) + lo, hi - lo,
-                                           m->h2d),
-                   "cuMemcpyHtoDAsync");
-        }
-        CU(g_drv.cuEventRecord(m->ev_in[k], m->h2d), "cuEventRecord");
-        CU(g_drv.cuStreamWaitEvent(s, m->ev_in[k], 0), "cuStreamWaitEvent");
-        if ((rc = launch_locked(m, args.data(), nargs, nullptr, nullptr, stream, b, e))) return rc;
-        CU(g_drv.cuEventRecord(m->ev_out[k], s), "cuEventRecord");
-        CU(g_drv.cuStreamWaitEvent(m->d2h, m->ev_out[k], 0), "cuStreamWaitEvent");
-        for (int i = 0; i < nargs; ++i) {
-            if (roles[i] == EMMY_ROLE_SCALAR || !is_out(roles[i]) || !m->rec.range_bytes[i]) continue;
-            size_t lo, hi;
-            unit_bytes(m, i, b, e, bytes[i], &lo, &hi);
-            if (hi > lo)
-                CU(g_drv.cuMemcpyDtoHAsync(static_cast<char *>(host_ptrs[i]) + lo, m->dbuf[i] + lo, hi - lo, m->d2h),
-                   "cuMemcpyDtoHAsync");
-        }
-    }
-    // outputs written whole by every launch leave after the last one (d2h already waits on it)
-    for (int i = 0; i < nargs; ++i)
-        if (roles[i] != EMMY_ROLE_SCALAR && is_out(roles[i]) && !m->rec.range_bytes[i])
-            CU(g_drv.cuMemcpyDtoHAsync(host_ptrs[i], m->dbuf[i], bytes[i], m->d2h), "cuMemcpyDtoHAsync");
-    CU(g_drv.cuStreamSynchronize(m->d2h), "cuStreamSynchronize");
-    CU(g_drv.cuStreamSynchronize(s), "cuStreamSynchronize");
-    CU(g_drv.cuStreamSynchronize(m->h2d), "cuStreamSynchronize");
-    return EMMY_OK;
+    return rc;
 }
 
 int emmy_launch_range(emmy_module_t m, const uint64_t *args, int nargs, uint64_t begin, uint64_t end,
