@@ -920,7 +920,7 @@ def _eval_phases(tile, stmts, axes, bufs, shapes, dtypes):
 def make_inputs(mk: dict, shapes: dict, dtypes: dict) -> dict[str, np.ndarray]:
     """Inputs from a meta kernel record: ``data`` literal, else ``init`` recipe
     with ``seed`` (default: standard normal, the reference tools' scheme,
-    tools/make_proxy_set.py:62-67).  bf16 inputs are rounded to bf16 values."""
+    tools/make_proxy_set.py:62-67).  bf16 and f16 inputs are rounded to their type."""
     out = {}
     for a in mk.get("args") or []:
         if a.get("output"):
@@ -937,6 +937,8 @@ def make_inputs(mk: dict, shapes: dict, dtypes: dict) -> dict[str, np.ndarray]:
                 v = (rng.standard_normal(size=shape) * init.get("std", 1.0) + init.get("mean", 0.0)).astype(F32)
         if (a.get("dtype") or "f32") == "bf16":
             v = bf16_round(v).reshape(shape)
+        elif (a.get("dtype") or "f32") == "f16":
+            v = v.astype(np.float16).astype(F32)
         out[a["name"]] = v
     return out
 
