@@ -550,7 +550,7 @@ def atomic_sum_case(cid: str, n: int, *, zero_prologue: bool = False) -> Case:
 
 
 def gemm_case(cid: str, m: int, k: int, n: int, *, dtype: DataType = BF16, epilogue: bool = True,
-              config: str | None = None, with_ref: bool = True) -> Case:
+              config: str | None = None, with_ref: bool = True, b_nk: bool = False) -> Case:
     """C = relu(A@B + bias), the naive matmul IR
     (make_proxy_set.py:338-365) plus a bias/ReLU epilogue.  bf16 operands and
     output, fp32 accumulate."""
@@ -567,7 +567,8 @@ def gemm_case(cid: str, m: int, k: int, n: int, *, dtype: DataType = BF16, epilo
         Init("acc0", 0.0, dtype=F32),
         Loop(axis=Axis("kk", Dim(k)), body=(
             Load(names=("a",), input="A", index=(Var("i"), Var("kk")), dtype=dtype),
-            Load(names=("b",), input="B", index=(Var("kk"), Var("j")), dtype=dtype),
+            Load(names=("b",), input="B", index=((Var("j"), Var("kk")) if b_nk else (Var("kk"), Var("j"))),
+                 dtype=dtype),
             Assign("p", EW("multiply"), ("a", "b"), F32),
             Accum("acc0", "p", EW("add"), F32, axes=("kk",)),
         )),
@@ -575,7 +576,8 @@ def gemm_case(cid: str, m: int, k: int, n: int, *, dtype: DataType = BF16, epilo
         Write(output="C", index=(Var("i"), Var("j")), values=(res,), value_dtype=out_dt),
     ))
     ins = ["A", "B"] + (["bias"] if epilogue else [])
-    nodes = {"A": _input("A", [m, k], _dt(dtype)), "B": _input("B", [k, n], _dt(dtype))}
+    bshape = [n, k] if b_nk else [k, n]
+    nodes = {"A": _input("A", [m, k], _dt(dtype)), "B": _input("B", bshape, _dt(dtype))}
     if epilogue:
         nodes["bias"] = _input("bias", [n], "f32")
     nodes["C"] = _kernel(entry, body, ins, [("C", [m, n], _dt(out_dt))])
@@ -583,7 +585,7 @@ def gemm_case(cid: str, m: int, k: int, n: int, *, dtype: DataType = BF16, epilo
     grid, block = _launch(m * n)
     std = 0.02 if epilogue else 1.0
     args = [_arg("A", [m, k], _dt(dtype), init=NORM(std), seed=0),
-            _arg("B", [k, n], _dt(dtype), init=NORM(std), seed=1)]
+            _arg("B", bshape, _dt(dtype), init=NORM(std), seed=1)]
     if epilogue:
         args.append(_arg("bias", [n], "f32", init=NORM(std), seed=2))
     args.append(_arg("C", [m, n], _dt(out_dt), output=True))
@@ -593,7 +595,7 @@ def gemm_case(cid: str, m: int, k: int, n: int, *, dtype: DataType = BF16, epilo
     if dtype.name == "bf16":
         ref = False
         if with_ref:
-            ref_case = gemm_case("ref_f32", m, k, n, dtype=F32, epilogue=epilogue, with_ref=False)
+            ref_case = gemm_case("ref_f32", m, k, n, dtype=F32, epilogue=epilogue, with_ref=False, b_nk=b_nk)
             ref_case.check = {"kind": "oracle_route",
                               "note": "fp32 copies of the bf16 operands; output rounded to bf16 RNE"}
     check = {"kind": "rtol", "rtol": 1e-2, "atol": 1e-2}
@@ -880,6 +882,11 @@ def all_cases() -> list[Case]:
     # ragged CTA-pair tiles: last M tile holds 8 rows (its second CTA reads only
     # out-of-bounds rows), last N tile 136 of 256 columns, 5 k-blocks
     cases.append(gemm_case("c5_gemm_520x320x392", 520, 320, 392))
+    # K not a multiple of the 64-wide k-block (the last block is half out of bounds), N ragged
+    cases.append(gemm_case("c5_gemm_264x200x264", 264, 200, 264))
+    # B stored [N, K] (K-major B): both tcgen05 kernels and the single-CTA one
+    cases.append(gemm_case("c5_gemm_bnk_384x256x512", 384, 256, 512, b_nk=True))
+    cases.append(gemm_case("c5_gemm_bnk_128x128x256", 128, 128, 256, b_nk=True))
     cases.append(gemm_case("m_matmul_f32_17x33x19", 17, 33, 19, dtype=F32, epilogue=False))
     cases.append(gemm_case("m_matmul_f32_64x64x64", 64, 64, 64, dtype=F32, epilogue=False))
     cases.append(gemm_case("m_matmul_f32_bias_96x160x80", 96, 160, 80, dtype=F32))
