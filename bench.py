@@ -48,6 +48,9 @@ DRAM_TRAFFIC = {
 
 CONFIGS = {
     # name: (case dir, unit, bound, algorithmic units per launch, workload text)
+    # C1 is launch-latency bound: its line reports microseconds per launch (lower is better)
+    "c1": ("c1_add_64", "us", "latency", 3 * 64 * 4,
+           "BASELINE configs[0]: c = a + b, f32 [64], one 256-thread block (launch latency)"),
     "c2": ("c2_gelu_full", "GB/s", "hbm", 2 * (1 << 28) * 4 + 2 * 16384 * 4,
            "BASELINE configs[1]: y = GELU_tanh(x*s + t), x f32 [16384, 16384], s,t f32 [16384]"),
     "c3": ("c3_rowsummax_full", "GB/s", "hbm", (1 << 31) + 2 * 8192 * 4,
@@ -251,7 +254,8 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
             torch.distributed.barrier()
 
     combine = combine_step(args.config, bufs, world)
-    step = lambda: (mod.launch(order, stream=stream), combine())  # noqa: E731
+    go = mod.bind(order, stream=stream)  # argument words prepared once: one C-ABI call per launch
+    step = go if args.config != "c4" or world <= 1 else (lambda: (go(), combine()))
     xchg = None
     if args.config == "c4" and world > 1 and args.combine == "fused":
         # one kernel per GPU: shard sum fused with the combine over NVLink peer memory
@@ -289,13 +293,37 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
             raise RuntimeError(f"fused sum + combine status 0x{xst:x} (a peer did not arrive in time)")
     ms_max = max_over_ranks(e0.elapsed_time(e1), world, device)
     per_launch_ms = ms_max / args.steps
-    value = units * world * args.steps / (ms_max / 1e3) / (1e9 if unit == "GB/s" else 1e12)
-    achieved = units / (per_launch_ms / 1e3) / (1e9 if unit == "GB/s" else 1e12)
+    latency = unit == "us"
+    graph = None
+    if latency:
+        # the same launches recorded once as a CUDA graph and replayed: device
+        # time per launch without the host's per-launch submission cost
+        gs = torch.cuda.Stream(device=local)
+        torch.cuda.synchronize(local)
+        with runtime.Graph.record(local, gs.cuda_stream) as g:
+            for _ in range(args.steps):
+                mod.launch(order, stream=gs.cuda_stream)
+        for _ in range(args.warmup):
+            g.launch(gs.cuda_stream)
+        torch.cuda.synchronize(local)
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(gs)
+        g.launch(gs.cuda_stream)
+        g1.record(gs)
+        torch.cuda.synchronize(local)
+        graph = {"us_per_launch": round(g0.elapsed_time(g1) * 1e3 / args.steps, 3),
+                 "launches_per_graph": args.steps, "path": "emmy_graph_begin/end/launch (C ABI)"}
+        g.close()
+    if latency:
+        value = achieved = per_launch_ms * 1e3
+    else:
+        value = units * world * args.steps / (ms_max / 1e3) / (1e9 if unit == "GB/s" else 1e12)
+        achieved = units / (per_launch_ms / 1e3) / (1e9 if unit == "GB/s" else 1e12)
     pk, pk_kind = peaks()
     peak = pk["hbm_gbs"] if bound == "hbm" else pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
     if bound == "fp32":
         peak, pk_kind = round(FP32_NOMINAL_TFLOPS, 1), "nominal"
-    peak_key = {"hbm": "hbm_gbs", "tensor": "bf16_tflops", "fp32": "fp32 CUDA cores"}[bound]
+    peak_key = {"hbm": "hbm_gbs", "tensor": "bf16_tflops", "fp32": "fp32 CUDA cores", "latency": "none"}[bound]
     traffic = DRAM_TRAFFIC.get(case_id)
 
     # e2e: the C-ABI host-buffer call, copies in the timed region
@@ -320,10 +348,11 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     e2e_s = max_over_ranks(time.perf_counter() - t0, world, device)
     h2d = sum(b for b, r in zip(nbytes, roles) if r == runtime.EMMY_ROLE_IN)
     d2h = sum(b for b, r in zip(nbytes, roles) if r == runtime.EMMY_ROLE_OUT)
-    e2e_value = units * world * e2e_steps / e2e_s / (1e9 if unit == "GB/s" else 1e12)
+    e2e_value = (e2e_s / e2e_steps * 1e6 if latency
+                 else units * world * e2e_steps / e2e_s / (1e9 if unit == "GB/s" else 1e12))
 
     ref_ptx = None
-    if rank == 0 and world == 1 and (args.config == "c2" or args.config[:2] in ("f_", "a_")) \
+    if rank == 0 and world == 1 and (args.config in ("c1", "c2") or args.config[:2] in ("f_", "a_")) \
             and not args.no_ref_ptx:
         ref_ptx = time_reference_ptx(spec, bufs, local, units, unit)
 
@@ -332,17 +361,21 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
         return None
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": not latency,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32" if args.config != "c5" else "bf16",
         "data": "synthetic (seeded on device, BASELINE distributions)",
         "config": {"workload": workload, "case": case_id, "rows_per_rank": spec.args[spec.arg_order[0]]["shape"][0],
                    "parallelism": f"{world} ranks, each its own full-size shard; no collective",
-                   "l2": "inputs larger than L2 (126 MB), no flush needed",
+                   "l2": ("inputs larger than L2 (126 MB), no flush needed" if not latency
+                          else "768-byte inputs stay in L2: a latency measurement"),
                    "launch": launch},
-        "roofline": {"bound": bound, "achieved": round(achieved, 2), "peak": peak,
-                     "unit": unit, "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "peak_source": f"{pk_kind} ({peak_key})",
-                     "units_per_launch": units},
+        "roofline": ({"bound": bound, "achieved": round(achieved, 2), "peak": peak,
+                      "unit": unit, "frac": round(achieved / peak, 4), "traffic": traffic,
+                      "peak_source": f"{pk_kind} ({peak_key})",
+                      "units_per_launch": units} if not latency else
+                     {"bound": "latency", "achieved": round(achieved, 3), "peak": None, "unit": "us", "frac": None,
+                      "traffic": None, "units_per_launch": units,
+                      "note": "768 bytes per launch: bounded by launch latency, not by HBM or tensor cores"}),
         "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "path": "emmy_run_host (C ABI) on pinned host buffers"},
@@ -351,6 +384,8 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     }
     if ref_ptx is not None:
         line["reference_ptx_gpu"] = ref_ptx
+    if graph is not None:
+        line["graph_replay"] = graph
     if args.config == "c4" and world > 1:
         line["config"]["parallelism"] = (
             f"{world} ranks, each its own 2^31-element shard; every step is one kernel per GPU that sums "
@@ -380,7 +415,7 @@ def time_reference_ptx(spec, bufs, local: int, units: int, unit: str) -> dict:
         mod.launch(order, stream=stream, grid=g, block=b)
     torch.cuda.synchronize(local)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    n = 5
+    n = 200 if unit == "us" else 5
     e0.record()
     for _ in range(n):
         mod.launch(order, stream=stream, grid=g, block=b)
@@ -388,7 +423,8 @@ def time_reference_ptx(spec, bufs, local: int, units: int, unit: str) -> dict:
     torch.cuda.synchronize(local)
     ms = e0.elapsed_time(e1) / n
     mod.close()
-    return {"value": round(units / (ms / 1e3) / (1e9 if unit == "GB/s" else 1e12), 2), "unit": unit,
+    value = ms * 1e3 if unit == "us" else units / (ms / 1e3) / (1e9 if unit == "GB/s" else 1e12)
+    return {"value": round(value, 3), "unit": unit,
             "ms_per_launch": round(ms, 4), "launch": {"grid": g, "block": b}}
 
 
@@ -397,6 +433,7 @@ def time_reference_ptx(spec, bufs, local: int, units: int, unit: str) -> dict:
 
 # bounded CPU samples of each workload for the oracle arms: (rows per task, text)
 CPU_SAMPLES = {
+    "c1": (1, "calls of the 64-element add, one thread"),
     "c2": (16, "rows of the GELU chain over 16384 columns"),
     "c3": (4, "rows of 65536 reduced (sum and max) in the reference's strided schedule order"),
     "c4": (1, "a 2^20+3-element full sum in the reference's strided schedule order"),
@@ -423,6 +460,11 @@ def _oracle_sample(cfg: str, rows: int):
     import interp
     case_id, unit, bound, units, _ = CONFIGS[cfg]
     rng = np.random.default_rng(0)
+    if cfg == "c1":
+        kop, meta, mk, shapes, dtypes = interp.load_case(CASES / case_id)
+        ins = {n: rng.standard_normal(tuple(shapes[n])).astype(np.float32) for n in ("a", "b")}
+        fn = lambda: interp.evaluate(kop, shapes, dtypes, ins, {"c": tuple(shapes["c"])})  # noqa: E731
+        return fn, units
     if cfg == "c2":
         kop, meta, mk, shapes, dtypes = interp.load_case(CASES / case_id)
         cols = 16384
@@ -475,6 +517,14 @@ def cpu_baseline(cfg: str, seconds: float = 10.0) -> dict:
     rows_per_task, what = CPU_SAMPLES[cfg]
     fn, units = _oracle_sample(cfg, rows_per_task)
     fn()  # warm
+    if unit == "us":
+        calls, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < min(seconds, 2.0):
+            fn()
+            calls += 1
+        el = time.perf_counter() - t0
+        return {"value": round(el / calls * 1e6, 3), "unit": unit, "cores": 1, "kind": "port",
+                "sample": f"oracle/interp.py, {calls} {what}"}
     done_units = 0
     t0 = time.perf_counter()
     with ThreadPoolExecutor(max_workers=threads) as ex:
@@ -496,6 +546,22 @@ def run_reference(args, rank: int) -> dict | None:
     threads = len(os.sched_getaffinity(0))
     rows_per_task, what = CPU_SAMPLES[args.config]
     fn, units_task = _oracle_sample(args.config, rows_per_task)
+    if unit == "us":
+        # a latency config: one call at a time on one thread, microseconds per call
+        for _ in range(args.warmup):
+            fn()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            fn()
+        el = time.perf_counter() - t0
+        us = el / args.steps * 1e6
+        return {"metric": METRIC, "value": round(us, 3), "unit": unit, "n_gpus": args.gpus, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(us / 1e3, 4), "higher_is_better": False,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+                "config": {"workload": workload, "case": case_id},
+                "cpu_baseline": {"value": round(us, 3), "unit": unit, "cores": 1, "kind": "port",
+                                 "sample": f"{args.steps} {what}"},
+                "e2e": {"value": round(us, 3), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     with ThreadPoolExecutor(max_workers=threads) as ex:
         for _ in range(args.warmup):
             list(ex.map(lambda _: fn(), range(threads)))

@@ -85,6 +85,12 @@ struct Driver {
     EMMY_DRV(cuEventDestroy)
     EMMY_DRV(cuGetErrorString)
     EMMY_DRV(cuTensorMapEncodeTiled)
+    EMMY_DRV(cuStreamBeginCapture)
+    EMMY_DRV(cuStreamEndCapture)
+    EMMY_DRV(cuGraphInstantiateWithFlags)
+    EMMY_DRV(cuGraphLaunch)
+    EMMY_DRV(cuGraphExecDestroy)
+    EMMY_DRV(cuGraphDestroy)
 #undef EMMY_DRV
 };
 
@@ -152,6 +158,12 @@ int load_driver() {
     EMMY_GET(cuEventDestroy, true)
     EMMY_GET(cuGetErrorString, true)
     EMMY_GET(cuTensorMapEncodeTiled, false)
+    EMMY_GET(cuStreamBeginCapture, false)
+    EMMY_GET(cuStreamEndCapture, false)
+    EMMY_GET(cuGraphInstantiateWithFlags, false)
+    EMMY_GET(cuGraphLaunch, false)
+    EMMY_GET(cuGraphExecDestroy, false)
+    EMMY_GET(cuGraphDestroy, false)
 #undef EMMY_GET
     if (missing) return fail(EMMY_ERR_NO_DRIVER, "driver lacks:%s", which.c_str());
     g_drv.ok = true;
@@ -274,8 +286,11 @@ int launch_locked(emmy_module *m, const uint64_t *args, int nargs, const uint32_
                         (unsigned long long)m->rec.range_total, (unsigned long long)al);
         if (range[0] == range[1]) return EMMY_OK;
     }
-    std::vector<void *> kp(static_cast<size_t>(nargs) + ntm + (ranged ? 2 : 0));
-    std::vector<uint32_t> narrow(static_cast<size_t>(nargs));
+    // fixed-size parameter tables: a launch allocates nothing on the host
+    constexpr int kMaxArgs = 64;
+    if (nargs < 0 || nargs > kMaxArgs) return fail(EMMY_ERR_INVALID, "%d parameters (at most %d)", nargs, kMaxArgs);
+    void *kp[kMaxArgs + EMMY_LR_MAX_TMAPS + 2];
+    uint32_t narrow[kMaxArgs];
     for (int i = 0; i < nargs; ++i) {
         size_t sz = 8;
         if (m->has_rec) sz = m->rec.param_kind[i] == EMMY_PARAM_PTR ? 8 : 4;
@@ -313,10 +328,10 @@ int launch_locked(emmy_module *m, const uint64_t *args, int nargs, const uint32_
         cfg.hStream = reinterpret_cast<CUstream>(stream);
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        CU(g_drv.cuLaunchKernelEx(&cfg, m->fn, kp.data(), nullptr), "cuLaunchKernelEx");
+        CU(g_drv.cuLaunchKernelEx(&cfg, m->fn, kp, nullptr), "cuLaunchKernelEx");
     } else {
         CU(g_drv.cuLaunchKernel(m->fn, g[0], g[1], g[2], b[0], b[1], b[2], smem,
-                                reinterpret_cast<CUstream>(stream), kp.data(), nullptr),
+                                reinterpret_cast<CUstream>(stream), kp, nullptr),
            "cuLaunchKernel");
     }
     return EMMY_OK;
@@ -410,7 +425,15 @@ int emmy_load(int dev, const void *image, size_t len, const char *entry, emmy_mo
             delete m;
             return cu_fail(r, "reading emmy_launch_record");
         }
-        if (m->rec.magic == EMMY_LR_MAGIC && m->rec.version == EMMY_LR_VERSION) m->has_rec = true;
+        if (m->rec.magic == EMMY_LR_MAGIC && m->rec.version == EMMY_LR_VERSION) {
+            if (m->rec.nparams > EMMY_LR_MAX_PARAMS || m->rec.ntmaps > EMMY_LR_MAX_TMAPS) {
+                g_drv.cuModuleUnload(m->mod);
+                delete m;
+                return fail(EMMY_ERR_INVALID, "launch record lists %u parameters and %u tensor maps (at most %d, %d)",
+                            m->rec.nparams, m->rec.ntmaps, EMMY_LR_MAX_PARAMS, EMMY_LR_MAX_TMAPS);
+            }
+            m->has_rec = true;
+        }
     }
     size_t st_bytes = 0;
     if (g_drv.cuModuleGetGlobal(&m->status, &st_bytes, m->mod, "emmy_status") != CUDA_SUCCESS)
@@ -850,6 +873,76 @@ int emmy_time_launch(emmy_module_t m, const uint64_t *args, int nargs, int iters
     CU(g_drv.cuEventElapsedTime(ms_total, e0, e1), "cuEventElapsedTime");
     g_drv.cuEventDestroy(e0);
     g_drv.cuEventDestroy(e1);
+    return rc;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ graphs
+
+struct emmy_graph {
+    int dev = 0;
+    CUgraphExec exec = nullptr;
+};
+
+namespace {
+
+int graph_driver() {
+    if (!g_drv.cuStreamBeginCapture || !g_drv.cuStreamEndCapture || !g_drv.cuGraphInstantiateWithFlags ||
+        !g_drv.cuGraphLaunch || !g_drv.cuGraphExecDestroy || !g_drv.cuGraphDestroy)
+        return fail(EMMY_ERR_NO_DRIVER, "driver lacks the stream-capture / graph entry points");
+    return EMMY_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int emmy_graph_begin(int dev, uint64_t stream) {
+    if (stream == 0) return fail(EMMY_ERR_INVALID, "emmy_graph_begin: the legacy default stream cannot be recorded");
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = set_device(dev);
+    if (rc || (rc = graph_driver())) return rc;
+    // relaxed: other threads may keep using the driver while this stream records
+    CU(g_drv.cuStreamBeginCapture(reinterpret_cast<CUstream>(stream), CU_STREAM_CAPTURE_MODE_RELAXED),
+       "cuStreamBeginCapture");
+    return EMMY_OK;
+}
+
+int emmy_graph_end(int dev, uint64_t stream, emmy_graph_t *out) {
+    if (!out) return fail(EMMY_ERR_INVALID, "emmy_graph_end: out is NULL");
+    *out = nullptr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = set_device(dev);
+    if (rc || (rc = graph_driver())) return rc;
+    CUgraph graph = nullptr;
+    CU(g_drv.cuStreamEndCapture(reinterpret_cast<CUstream>(stream), &graph), "cuStreamEndCapture");
+    CUgraphExec exec = nullptr;
+    CUresult r = g_drv.cuGraphInstantiateWithFlags(&exec, graph, 0);
+    g_drv.cuGraphDestroy(graph);
+    if (r != CUDA_SUCCESS) return cu_fail(r, "cuGraphInstantiateWithFlags");
+    auto *g = new emmy_graph;
+    g->dev = dev;
+    g->exec = exec;
+    *out = g;
+    return EMMY_OK;
+}
+
+int emmy_graph_launch(emmy_graph_t g, uint64_t stream) {
+    if (!g || !g->exec) return fail(EMMY_ERR_INVALID, "emmy_graph_launch: no graph");
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = set_device(g->dev);
+    if (rc) return rc;
+    CU(g_drv.cuGraphLaunch(g->exec, reinterpret_cast<CUstream>(stream)), "cuGraphLaunch");
+    return EMMY_OK;
+}
+
+int emmy_graph_destroy(emmy_graph_t g) {
+    if (!g) return EMMY_OK;
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = set_device(g->dev);
+    if (rc == EMMY_OK && g->exec) g_drv.cuGraphExecDestroy(g->exec);
+    delete g;
     return rc;
 }
 

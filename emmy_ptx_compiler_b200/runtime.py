@@ -69,6 +69,10 @@ def _declare(lib) -> None:
         "emmy_allgather_f32": ([vp, u64, u64, sz, u64, i32], i32),
         "emmy_comm_destroy": ([vp], i32),
         "emmy_comm_abort": ([vp], i32),
+        "emmy_graph_begin": ([i32, u64], i32),
+        "emmy_graph_end": ([i32, u64, P(vp)], i32),
+        "emmy_graph_launch": ([vp, u64], i32),
+        "emmy_graph_destroy": ([vp], i32),
     }
     for name, (argtypes, restype) in sigs.items():
         fn = getattr(lib, name)
@@ -84,7 +88,8 @@ EXPORTED = ("emmy_version", "emmy_last_error", "emmy_init", "emmy_device_count",
             "emmy_xchg_create", "emmy_xchg_connect", "emmy_sum_f32_allreduce", "emmy_xchg_status",
             "emmy_xchg_destroy",
             "emmy_comm_unique_id", "emmy_comm_init", "emmy_allreduce_f32", "emmy_allgather_f32",
-            "emmy_comm_destroy", "emmy_comm_abort")
+            "emmy_comm_destroy", "emmy_comm_abort",
+            "emmy_graph_begin", "emmy_graph_end", "emmy_graph_launch", "emmy_graph_destroy")
 
 
 def library_path() -> Path:
@@ -178,6 +183,11 @@ class Module:
         b = (C.c_uint32 * 3)(*(list(block) + [1, 1])[:3]) if block is not None else None
         _check(lib().emmy_launch(self._h, words, len(args), g, b, C.c_uint64(stream)))
 
+    def bind(self, args, stream: int = 0) -> "BoundLaunch":
+        """A launcher with the argument words prepared once (the tensors must
+        stay alive and keep their storage): each call is one C-ABI launch."""
+        return BoundLaunch(self, self._words(args), len(args), stream)
+
     def launch_range(self, args, begin: int, end: int, stream: int = 0) -> None:
         """Launch over units [begin, end) (cells / output rows) only."""
         words = self._words(args)
@@ -209,6 +219,73 @@ class Module:
         sizes = (C.c_size_t * n)(*nbytes)
         rl = (C.c_uint8 * n)(*roles)
         _check(lib().emmy_run_host(self._h, ptrs, sizes, rl, n, C.c_uint64(stream)))
+
+
+class BoundLaunch:
+    """``Module.launch`` with fixed arguments and stream, for launch-rate-bound
+    loops: the call does no Python-side argument marshalling."""
+
+    def __init__(self, module: Module, words, nargs: int, stream: int):
+        self._module = module  # keeps the module loaded
+        self._fn = lib().emmy_launch
+        self._h = module._h
+        self._words = words
+        self._nargs = nargs
+        self._stream = C.c_uint64(stream)
+
+    def __call__(self) -> None:
+        rc = self._fn(self._h, self._words, self._nargs, None, None, self._stream)
+        if rc:
+            _check(rc)
+
+
+class Graph:
+    """A CUDA graph of the launches issued on one stream between
+    ``begin`` and ``end`` (``with Graph.record(dev, stream) as g: ...``);
+    ``launch`` replays them in order, with the recorded arguments."""
+
+    def __init__(self, device: int):
+        self.device = device
+        self._h = None
+
+    @classmethod
+    def record(cls, device: int, stream: int) -> "_Recording":
+        return _Recording(cls(device), stream)
+
+    def launch(self, stream: int) -> None:
+        if not self._h:
+            raise EmmyError(-1, "graph has not been recorded")
+        _check(lib().emmy_graph_launch(self._h, C.c_uint64(stream)))
+
+    def close(self) -> None:
+        if self._h:
+            h, self._h = self._h, None
+            _check(lib().emmy_graph_destroy(h))
+
+    def __del__(self):
+        try:
+            if self._h and _lib is not None:
+                _lib.emmy_graph_destroy(self._h)
+        except Exception:
+            pass
+
+
+class _Recording:
+    def __init__(self, graph: Graph, stream: int):
+        self.graph, self.stream = graph, stream
+
+    def __enter__(self) -> Graph:
+        _check(lib().emmy_graph_begin(self.graph.device, C.c_uint64(self.stream)))
+        return self.graph
+
+    def __exit__(self, exc_type, exc, tb) -> None:
+        h = C.c_void_p()
+        rc = lib().emmy_graph_end(self.graph.device, C.c_uint64(self.stream), C.byref(h))
+        if exc_type is None:
+            _check(rc)
+            self.graph._h = h
+        elif h:
+            lib().emmy_graph_destroy(h)
 
 
 def shard_range(module: "Module", ndev: int, d: int) -> tuple[int, int]:

@@ -136,6 +136,23 @@ int emmy_launch_sharded(const emmy_module_t *mods, int ndev, const uint64_t *con
 int emmy_time_launch(emmy_module_t m, const uint64_t *args, int nargs, int iters, uint64_t stream,
                      float *ms_total);
 
+/* CUDA graphs of launches.  No counterpart in the reference, which leaves
+ * launching to its caller.  emmy_graph_begin starts recording what is issued
+ * on `stream` of device `dev` (a stream the caller created: the legacy default
+ * stream 0 cannot be recorded); launches issued there are then recorded, not
+ * run.  emmy_graph_end stops recording and instantiates the graph.
+ * emmy_graph_launch replays every recorded launch, in order, with the argument
+ * values of the recording, on `stream` (asynchronous); the modules recorded
+ * must stay loaded while the graph exists.  emmy_graph_end always takes the
+ * stream out of recording, also when the recording was invalidated (it then
+ * returns the error and no graph).  emmy_run_host, emmy_sync and
+ * emmy_time_launch synchronise, so they cannot be recorded. */
+typedef struct emmy_graph *emmy_graph_t;
+int emmy_graph_begin(int dev, uint64_t stream);
+int emmy_graph_end(int dev, uint64_t stream, emmy_graph_t *out);
+int emmy_graph_launch(emmy_graph_t g, uint64_t stream);
+int emmy_graph_destroy(emmy_graph_t g);
+
 /* Full-array f32 sum that allocates nothing.  No counterpart in the
  * reference.  For callers that may not call cudaMalloc (fixed memory budgets,
  * pre-sized pools, runtimes that own every allocation): the cross-block
