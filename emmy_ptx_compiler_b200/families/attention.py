@@ -42,6 +42,9 @@ from .common import KernelSource, LaunchPlan, ParamSpec, SM_COUNT, launch_record
 THREADS = 256
 BK = 64
 SCORE_CACHE_BYTES = 96 * 1024  # scores of a CTA's rows kept in shared memory across passes
+ROWS_PER_CTA = 0               # 0: chosen from the number of query rows
+DOT_UNROLL = 16                # unroll of the q . k loop (groups of 4 d)
+PV_UNROLL = 16                 # unroll of the p . v loop (groups of 4 keys)
 _COMBINE = {"add": "add", "sum": "add", "maximum": "maximum", "amax": "maximum", "max": "maximum",
             "minimum": "minimum", "amin": "minimum", "min": "minimum"}
 
@@ -268,8 +271,9 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
     scalar_env = {n: (("f32", f"p_{_c(n)}") if scalars[n] == "f32" else ("int", f"(long long)p_{_c(n)}"))
                   for n in scalars}
     SQ, DV, SK, D = plan.SQ, plan.DV, plan.SK, plan.D
-    BQ = 16 if -(-SQ // 16) >= 2 * SM_COUNT else (8 if -(-SQ // 8) >= SM_COUNT else 4)
+    BQ = ROWS_PER_CTA or (16 if -(-SQ // 16) >= 2 * SM_COUNT else (8 if -(-SQ // 8) >= SM_COUNT else 4))
     T = THREADS
+    NW = T // 32
     fus = fusable_products(kop.body)
     # per-row names: top-level statements and row accumulators (kept in shared memory per row)
     row_names: list[str] = []
@@ -284,38 +288,60 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
                     row_names.append(n)
     nstash = max([len(st.stash) for st in plan.steps if isinstance(st, KeyLoop)] + [0])
     nfac = max([len(st.row_accs) for st in plan.steps if isinstance(st, KeyLoop)] + [0])
-    # shared memory layout (floats)
-    q_stride = D + 1
-    s_stride = BK + 1
+    keyloops = [st for st in plan.steps if isinstance(st, KeyLoop)]
+    # every key loop computes the same dot products: keep the first pass's scores for the rest
+    cache = len(keyloops) > 1 and len({st.dot_init for st in keyloops}) == 1 and BQ * (SK + 1) * 4 <= SCORE_CACHE_BYTES
+    # the tiles each pass streams through shared memory; passes run one after another,
+    # so one double-buffered region holds whatever the pass needs
+    need_k = {id(st): not (cache and st is not keyloops[0]) for st in keyloops}
+    need_v = {id(st): bool(st.dep and plan.v) for st in keyloops}
+    stage = max([(D * BK if need_k[id(st)] else 0) + (BK * DV if need_v[id(st)] else 0) for st in keyloops] + [4])
+    stage = -(-stage // 4) * 4
+    # 16-byte asynchronous copies when every tile row is whole 16-byte chunks
+    # (the kernel also checks the base pointers at run time)
+    async_k = plan.k_dk and SK % 4 == 0
+    async_v = plan.v is not None and DV % 4 == 0
+    q4 = D % 4 == 0
+    QS = D if q4 else D + 1     # warps read one q row at a time (broadcast): no padding needed
+    SS = BK + 4                 # per-(row, key) operands: float4 rows, rows 4 banks apart
     off = {}
     cur = 0
 
     def alloc(name, n):
         nonlocal cur
         off[name] = cur
-        cur += n
+        cur += -(-n // 4) * 4
 
-    alloc("qs", BQ * q_stride)
-    alloc("ks", D * BK)
-    alloc("vs", BK * DV if plan.v else 1)
+    alloc("qs", BQ * QS)
+    alloc("kv", 2 * stage)
     alloc("rowv", max(1, len(row_names)) * BQ)
-    alloc("acca", max(1, nfac) * BQ * s_stride)   # accumulate operand (or first factor) per (row, key)
-    alloc("accb", max(1, nfac) * BQ * s_stride)   # second factor when the accumulate is an fma
-    alloc("stash", max(1, nstash) * BQ * s_stride)
-    # every key loop computes the same dot products: keep the first pass's scores for the rest
-    keyloops = [st for st in plan.steps if isinstance(st, KeyLoop)]
-    cache = len(keyloops) > 1 and len({st.dot_init for st in keyloops}) == 1 and BQ * (SK + 1) * 4 <= SCORE_CACHE_BYTES
+    alloc("acca", max(1, nfac) * BQ * SS)   # accumulate operand (or first factor) per (row, key)
+    alloc("accb", max(1, nfac) * BQ * SS)   # second factor when the accumulate is an fma
+    alloc("stash", max(1, nstash) * BQ * SS)
+    np_map = BQ * BK // T if (T % BK == 0 and (BQ * BK) % T == 0) else 1
+    alloc("pred", max(1, nfac) * NW * max(1, np_map))   # per-warp partials of max / min rows
     if cache:
         alloc("scache", BQ * (SK + 1))
     smem_bytes = cur * 4
+    # CTAs per SM that shared memory allows (1 KiB of it is reserved per CTA), for the register cap
+    min_blocks = max(1, min(4, 2048 // T, (228 * 1024) // (smem_bytes + 1024)))
     lines: list[str] = []
     w = lines.append
     w(DEVICE_PRELUDE)
     w('#include "emmy_launch_record.h"')
     w('extern "C" __device__ unsigned int emmy_status;')
-    w(f'extern "C" __global__ void __launch_bounds__({T}) {kop.name}(' + ", ".join(sig) + ") {")
+    w("__device__ __forceinline__ void emmy_cp16(float *dst, const float *src, unsigned bytes) {")
+    w("    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);")
+    w('    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" :: "r"(d), "l"(src), "r"(bytes) : "memory");')
+    w("}")
+    w('__device__ __forceinline__ void emmy_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }')
+    w("template <int N> __device__ __forceinline__ void emmy_cp_wait() {")
+    w('    asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory");')
+    w("}")
+    w(f'extern "C" __global__ void __launch_bounds__({T}, {min_blocks}) {kop.name}(' + ", ".join(sig) + ") {")
     w(f"    constexpr int SQ = {SQ}, DV = {DV}, SK = {SK}, D = {D}, BQ = {BQ}, BK = {BK};")
-    w(f"    constexpr int QS = {q_stride}, SS = {s_stride};")
+    w(f"    constexpr int QS = {QS}, SS = {SS}, STAGE = {stage};")
+    w(f"    constexpr int NT = (SK + BK - 1) / BK;")
     w("    extern __shared__ __align__(16) float sm[];")
     for name, o in off.items():
         w(f"    float *const {name} = sm + {o};")
@@ -326,10 +352,17 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
     w("        return;")
     w("    }")
     w("    const int tid = threadIdx.x;")
+    w("    const int lane = tid & 31, warp = tid >> 5;")
+    w("    (void)lane; (void)warp;")
+    kp, vp = ptrs[plan.kmat], (ptrs[plan.v] if plan.v else None)
+    w(f"    const bool k_async = {'true' if async_k else 'false'} && ((reinterpret_cast<uintptr_t>({kp}) & 15) == 0);")
+    if plan.v:
+        w(f"    const bool v_async = {'true' if async_v else 'false'} && ((reinterpret_cast<uintptr_t>({vp}) & 15) == 0);")
     w("    const long long RB = (long long)(emmy_rb < (unsigned long long)SQ ? emmy_rb : SQ);")
     w("    const long long RE = (long long)(emmy_re < (unsigned long long)SQ ? emmy_re : SQ);")
     w("    for (long long q0 = RB + (long long)blockIdx.x * BQ; q0 < RE; q0 += (long long)gridDim.x * BQ) {")
     w("        const int nq = (RE - q0) < BQ ? (int)(RE - q0) : BQ;")
+    w("        __syncthreads();")
     w(f"        for (int e = tid; e < BQ * D; e += {T}) {{")
     w("            const int r = e / D, d = e - r * D;")
     w(f"            qs[r * QS + d] = r < nq ? {ptrs[plan.q]}[(q0 + r) * D + d] : 0.0f;")
@@ -342,6 +375,51 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
 
     def row_ref(n: str, r: str) -> str:
         return f"rowv[{row_slot[n]} * BQ + {r}]"
+
+    def tile_load(ind: str, st: KeyLoop, t: str) -> None:
+        """Issue the copies of key tile ``t`` into stage ``t & 1`` (asynchronous
+        where allowed; plain loads and stores otherwise)."""
+        w(f"{ind}{{")
+        i1 = ind + "    "
+        w(f"{i1}const int tk0 = ({t}) * BK;")
+        w(f"{i1}const int tnk = (SK - tk0) < BK ? (SK - tk0) : BK;")
+        w(f"{i1}float *const kst = kv + (({t}) & 1) * STAGE;")
+        w(f"{i1}(void)tnk; (void)kst;")
+        if need_k[id(st)]:
+            if plan.k_dk:
+                if async_k:
+                    w(f"{i1}if (k_async) {{")
+                    w(f"{i1}    for (int e = tid; e < D * (BK / 4); e += {T}) {{")
+                    w(f"{i1}        const int d = e / (BK / 4), kk = (e - d * (BK / 4)) * 4;")
+                    w(f"{i1}        const bool in = kk < tnk;")
+                    w(f"{i1}        emmy_cp16(kst + d * BK + kk, {kp} + (in ? (long long)d * SK + tk0 + kk : 0), in ? 16u : 0u);")
+                    w(f"{i1}    }}")
+                    w(f"{i1}}} else")
+                w(f"{i1}for (int e = tid; e < D * BK; e += {T}) {{")
+                w(f"{i1}    const int d = e / BK, kk = e - d * BK;")
+                w(f"{i1}    kst[d * BK + kk] = kk < tnk ? {kp}[(long long)d * SK + tk0 + kk] : 0.0f;")
+                w(f"{i1}}}")
+            else:
+                w(f"{i1}for (int e = tid; e < D * BK; e += {T}) {{")
+                w(f"{i1}    const int kk = e / D, d = e - kk * D;")
+                w(f"{i1}    kst[d * BK + kk] = kk < tnk ? {kp}[(long long)(tk0 + kk) * D + d] : 0.0f;")
+                w(f"{i1}}}")
+        if need_v[id(st)]:
+            voff = D * BK if need_k[id(st)] else 0
+            w(f"{i1}float *const vst = kst + {voff};")
+            if async_v:
+                w(f"{i1}if (v_async) {{")
+                w(f"{i1}    for (int e = tid; e < BK * (DV / 4); e += {T}) {{")
+                w(f"{i1}        const int kk = e / (DV / 4), jj = (e - kk * (DV / 4)) * 4;")
+                w(f"{i1}        const bool in = kk < tnk;")
+                w(f"{i1}        emmy_cp16(vst + kk * DV + jj, {vp} + (in ? (long long)(tk0 + kk) * DV + jj : 0), in ? 16u : 0u);")
+                w(f"{i1}    }}")
+                w(f"{i1}}} else")
+            w(f"{i1}for (int e = tid; e < BK * DV; e += {T}) {{")
+            w(f"{i1}    const int kk = e / DV, jj = e - kk * DV;")
+            w(f"{i1}    vst[kk * DV + jj] = kk < tnk ? {vp}[(long long)(tk0 + kk) * DV + jj] : 0.0f;")
+            w(f"{i1}}}")
+        w(f"{ind}}}")
 
     ind = "        "
     for st in plan.steps:
@@ -368,53 +446,89 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
                     w(f"{ind}    {row_ref(n, 'tid')} = {em.as_f32(n)};")
             w(f"{ind}}}")
             continue
-        w(f"{ind}__syncthreads();")
-        # row accumulators start from their Init (held in rowv by the row statements)
-        w(f"{ind}for (int k0 = 0; k0 < SK; k0 += BK) {{")
-        i2 = ind + "    "
-        w(f"{i2}const int nk = (SK - k0) < BK ? (SK - k0) : BK;")
-        w(f"{i2}__syncthreads();")
         reuse = cache and st is not keyloops[0]
-        if reuse:
-            pass
-        elif plan.k_dk:
-            w(f"{i2}for (int e = tid; e < D * BK; e += {T}) {{")
-            w(f"{i2}    const int d = e / BK, kk = e - d * BK;")
-            w(f"{i2}    ks[d * BK + kk] = kk < nk ? {ptrs[plan.kmat]}[(long long)d * SK + k0 + kk] : 0.0f;")
+        loads = need_k[id(st)] or need_v[id(st)]
+        # (row, key) pairs: thread tid takes key kk = tid % BK of rows tid / BK + u * RS,
+        # the same rows on every tile (so it can keep per-row partials in registers)
+        mapped = T % BK == 0 and (BQ * BK) % T == 0 and BK % 32 == 0
+        NP = BQ * BK // T if mapped else 0
+        RS = T // BK if mapped else 0
+        acc_kinds = []                 # (fi, name, op, kind): kind "reg", "fma" or "smem"
+        for fi, (a, op) in enumerate(st.row_accs):
+            accum = next(t for t in st.post if isinstance(t, ir.Accum) and t.name == a)
+            if mapped and op in ("maximum", "minimum"):
+                acc_kinds.append((fi, a, op, "reg", accum))
+            else:
+                acc_kinds.append((fi, a, op, "fma" if op == "add" else "smem", accum))
+        reg_accs = [k for k in acc_kinds if k[3] == "reg"]
+        smem_accs = [k for k in acc_kinds if k[3] != "reg"]
+        phase2 = bool(smem_accs or st.dep)
+        # the previous pass's readers of the stage buffers and row values are done
+        w(f"{ind}__syncthreads();")
+        for ri, (fi, a, op, _, _) in enumerate(reg_accs):
+            # per-thread partial of a max / min: same value in any order of keys
+            w(f"{ind}float pm{ri}[{NP}];")
+            w(f"{ind}#pragma unroll")
+            w(f"{ind}for (int u = 0; u < {NP}; ++u) pm{ri}[u] = {row_ref(a, f'(tid / BK + u * {RS})')};")
+        if loads:
+            tile_load(ind, st, "0")
+            w(f"{ind}emmy_cp_commit();")
+        w(f"{ind}for (int t = 0; t < NT; ++t) {{")
+        i2 = ind + "    "
+        w(f"{i2}const int k0 = t * BK;")
+        w(f"{i2}const int nk = (SK - k0) < BK ? (SK - k0) : BK;")
+        if loads:
+            w(f"{i2}emmy_cp_wait<0>();")
+        if loads or phase2:
+            # tile t is visible to all; every thread is done with tile t - 1
+            w(f"{i2}__syncthreads();")
+        if loads:
+            # the next tile streams into the other stage while this one is used
+            w(f"{i2}if (t + 1 < NT) {{")
+            tile_load(i2 + "    ", st, "t + 1")
+            w(f"{i2}    emmy_cp_commit();")
             w(f"{i2}}}")
-        else:
-            w(f"{i2}for (int e = tid; e < D * BK; e += {T}) {{")
-            w(f"{i2}    const int kk = e / D, d = e - kk * D;")
-            w(f"{i2}    ks[d * BK + kk] = kk < nk ? {ptrs[plan.kmat]}[(long long)(k0 + kk) * D + d] : 0.0f;")
-            w(f"{i2}}}")
-        if st.dep and plan.v:
-            w(f"{i2}for (int e = tid; e < BK * DV; e += {T}) {{")
-            w(f"{i2}    const int kk = e / DV, jj = e - kk * DV;")
-            w(f"{i2}    vs[kk * DV + jj] = kk < nk ? {ptrs[plan.v]}[(long long)(k0 + kk) * DV + jj] : 0.0f;")
-            w(f"{i2}}}")
-        w(f"{i2}__syncthreads();")
+        w(f"{i2}const float *const ks = kv + (t & 1) * STAGE;")
+        w(f"{i2}const float *const vs = ks + {D * BK if need_k[id(st)] else 0};")
+        w(f"{i2}(void)ks; (void)vs;")
         # scores and j-independent statements, once per (row, key)
-        blocked = not reuse and T % BK == 0 and (BQ * BK) % T == 0
         i3 = i2 + "    "
-        if blocked:
-            # a thread's pairs share one key: each k element read from shared memory
-            # feeds NP rows' fma chains (each still sequential over d)
-            NP = BQ * BK // T
-            RS = T // BK
+        if mapped:
             w(f"{i2}{{")
             w(f"{i3}const int kk = tid % BK;")
-            w(f"{i3}float scv[{NP}];")
-            w(f"{i3}#pragma unroll")
-            w(f"{i3}for (int u = 0; u < {NP}; ++u) scv[u] = {f32_lit(st.dot_init)};")
-            w(f"{i3}if (kk < nk) {{")
-            w(f"{i3}    #pragma unroll 4")
-            w(f"{i3}    for (int d = 0; d < D; ++d) {{")
-            w(f"{i3}        const float kv = ks[d * BK + kk];")
-            w(f"{i3}        #pragma unroll")
-            w(f"{i3}        for (int u = 0; u < {NP}; ++u)")
-            w(f"{i3}            scv[u] = __fmaf_rn(qs[(tid / BK + u * {RS}) * QS + d], kv, scv[u]);")
-            w(f"{i3}    }}")
-            w(f"{i3}}}")
+            if not reuse:
+                # each k element read from shared memory feeds NP rows' fma chains
+                # (each still sequential over d)
+                w(f"{i3}float scv[{NP}];")
+                w(f"{i3}#pragma unroll")
+                w(f"{i3}for (int u = 0; u < {NP}; ++u) scv[u] = {f32_lit(st.dot_init)};")
+                w(f"{i3}if (kk < nk) {{")
+                if q4:
+                    w(f"{i3}    #pragma unroll {DOT_UNROLL}")
+                    w(f"{i3}    for (int d4 = 0; d4 < D; d4 += 4) {{")
+                    w(f"{i3}        float4 qv[{NP}];")
+                    w(f"{i3}        #pragma unroll")
+                    w(f"{i3}        for (int u = 0; u < {NP}; ++u)")
+                    w(f"{i3}            qv[u] = *reinterpret_cast<const float4 *>(qs + (tid / BK + u * {RS}) * QS + d4);")
+                    w(f"{i3}        const float k0v = ks[(d4 + 0) * BK + kk], k1v = ks[(d4 + 1) * BK + kk];")
+                    w(f"{i3}        const float k2v = ks[(d4 + 2) * BK + kk], k3v = ks[(d4 + 3) * BK + kk];")
+                    w(f"{i3}        #pragma unroll")
+                    w(f"{i3}        for (int u = 0; u < {NP}; ++u) {{")
+                    w(f"{i3}            scv[u] = __fmaf_rn(qv[u].x, k0v, scv[u]);")
+                    w(f"{i3}            scv[u] = __fmaf_rn(qv[u].y, k1v, scv[u]);")
+                    w(f"{i3}            scv[u] = __fmaf_rn(qv[u].z, k2v, scv[u]);")
+                    w(f"{i3}            scv[u] = __fmaf_rn(qv[u].w, k3v, scv[u]);")
+                    w(f"{i3}        }}")
+                    w(f"{i3}    }}")
+                else:
+                    w(f"{i3}    #pragma unroll 4")
+                    w(f"{i3}    for (int d = 0; d < D; ++d) {{")
+                    w(f"{i3}        const float kv_ = ks[d * BK + kk];")
+                    w(f"{i3}        #pragma unroll")
+                    w(f"{i3}        for (int u = 0; u < {NP}; ++u)")
+                    w(f"{i3}            scv[u] = __fmaf_rn(qs[(tid / BK + u * {RS}) * QS + d], kv_, scv[u]);")
+                    w(f"{i3}    }}")
+                w(f"{i3}}}")
             w(f"{i3}#pragma unroll")
             w(f"{i3}for (int u = 0; u < {NP}; ++u) {{")
             w(f"{i3}const int r = tid / BK + u * {RS};")
@@ -425,7 +539,7 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
         i4 = i3 + "    "
         if reuse:
             w(f"{i4}float sc = scache[r * (SK + 1) + k0 + kk];")
-        elif blocked:
+        elif mapped:
             w(f"{i4}float sc = scv[u];")
             if cache:
                 w(f"{i4}scache[r * (SK + 1) + k0 + kk] = sc;")
@@ -446,91 +560,90 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
             em.env.setdefault(n, ("f32", row_ref(n, "r")))
         em.run(tuple(st.indep))
         w("\n".join(em.lines))
-        # stash the accumulate operands and the values the j-dependent statements read
+        # fold the register partials; stash the accumulate operands and the values
+        # the j-dependent statements read
         acc_ops = []
-        for fi, (a, op) in enumerate(st.row_accs):
-            accum = next(t for t in st.post if isinstance(t, ir.Accum) and t.name == a)
+        for ri, (fi, a, op, kind, accum) in enumerate(reg_accs):
+            w(f"{i4}pm{ri}[u] = {combine_code(op, f'pm{ri}[u]', em.as_f32(accum.value))};")
+        for fi, a, op, kind, accum in smem_accs:
             prod = em.plain_product(accum.value) if op == "add" else None
             if prod is not None:
                 w(f"{i4}acca[({fi} * BQ + r) * SS + kk] = {prod[0]};")
                 w(f"{i4}accb[({fi} * BQ + r) * SS + kk] = {prod[1]};")
-                acc_ops.append((a, op, True))
+                acc_ops.append((fi, a, op, True))
             else:
                 w(f"{i4}acca[({fi} * BQ + r) * SS + kk] = {em.as_f32(accum.value)};")
-                acc_ops.append((a, op, False))
+                acc_ops.append((fi, a, op, False))
         stash_codes = {}
         for si, n in enumerate(st.stash):
             w(f"{i4}stash[({si} * BQ + r) * SS + kk] = {em.as_f32(n)};")
             stash_codes[n] = si
         w(f"{i3}}}")
         w(f"{i2}}}")
-        if blocked:
+        if mapped:
             w(f"{i2}}}")
-        w(f"{i2}__syncthreads();")
-        # row accumulations in key order, one thread per row
-        if acc_ops:
+        if phase2:
+            w(f"{i2}__syncthreads();")
+        # row accumulations kept in shared memory.  max / min give the same value in
+        # any order: one warp per row combines the tile in parallel.  Sums run in key
+        # order, one thread per row, so every sum is added in the reference's order.
+        # The statements that depend on j read no accumulator of this loop, so they
+        # run alongside.
+        for fi, a, op, is_fma in acc_ops:
+            acc_at = f"acca[({fi} * BQ + r) * SS + kk]"
+            if op in ("maximum", "minimum") and not is_fma:
+                w(f"{i2}for (int r = warp; r < nq; r += {NW}) {{")
+                w(f"{i2}    float x = {row_ref(a, 'r')};")
+                w(f"{i2}    for (int kk = lane; kk < nk; kk += 32) x = {combine_code(op, 'x', acc_at)};")
+                w(f"{i2}    #pragma unroll")
+                w(f"{i2}    for (int o = 16; o > 0; o >>= 1) x = {combine_code(op, 'x', '__shfl_xor_sync(0xffffffffu, x, o)')};")
+                w(f"{i2}    __syncwarp();")
+                w(f"{i2}    if (lane == 0) {row_ref(a, 'r')} = x;")
+                w(f"{i2}}}")
+                continue
             w(f"{i2}if (tid < nq) {{")
-            for fi, (a, op, is_fma) in enumerate(acc_ops):
-                ref = row_ref(a, "tid")
-                w(f"{i2}    float ra = {ref};")
-                w(f"{i2}    for (int kk = 0; kk < nk; ++kk)")
-                if is_fma:
-                    w(f"{i2}        ra = __fmaf_rn(acca[({fi} * BQ + tid) * SS + kk], accb[({fi} * BQ + tid) * SS + kk], ra);")
-                else:
-                    w(f"{i2}        ra = {combine_code(op, 'ra', f'acca[({fi} * BQ + tid) * SS + kk]')};")
-                w(f"{i2}    {ref} = ra;")
+            w(f"{i2}    const int r = tid;")
+            w(f"{i2}    float ra = {row_ref(a, 'r')};")
+            if is_fma:
+                step = f"ra = __fmaf_rn({acc_at}, accb[({fi} * BQ + r) * SS + kk], ra);"
+            else:
+                step = f"ra = {combine_code(op, 'ra', acc_at)};"
+            w(f"{i2}    if (nk == BK) {{")
+            w(f"{i2}        #pragma unroll 16")
+            w(f"{i2}        for (int kk = 0; kk < BK; ++kk) {step}")
+            w(f"{i2}    }} else {{")
+            w(f"{i2}        for (int kk = 0; kk < nk; ++kk) {step}")
+            w(f"{i2}    }}")
+            w(f"{i2}    {row_ref(a, 'r')} = ra;")
             w(f"{i2}}}")
         # j-dependent statements in key order, in the threads that own the output cells
-        shared_j = st.dep and T % DV == 0
-        if shared_j:
-            # every owned cell of a thread has the same column: one v read per key feeds them all
-            w(f"{i2}{{")
-            w(f"{i2}const int jj = tid % DV;")
-            w(f"{i2}for (int kk = 0; kk < nk; ++kk) {{")
-            w(f"{i2}    const float vcur = vs[kk * DV + jj];")
-            w(f"{i2}    #pragma unroll")
-            w(f"{i2}    for (int u = 0; u < {nown}; ++u) {{")
-            w(f"{i2}        const int r = (tid + u * {T}) / DV;")
-            w(f"{i2}        if (r < nq) {{")
-            i5 = i2 + "        "
-            em2 = Emitter(shapes, dtypes, ptrs, indent=i5 + "    ",
-                          load_hook=lambda s_, k_: ("f32", "vcur"))
-        elif st.dep:
-            w(f"{i2}#pragma unroll")
-            w(f"{i2}for (int u = 0; u < {nown}; ++u) {{")
-            w(f"{i2}    const int o = tid + u * {T};")
-            w(f"{i2}    const int r = o / DV, jj = o - r * DV;")
-            w(f"{i2}    if (r < nq) {{")
-            i5 = i2 + "        "
-            w(f"{i5}for (int kk = 0; kk < nk; ++kk) {{")
-            em2 = Emitter(shapes, dtypes, ptrs, indent=i5 + "    ",
-                          load_hook=lambda s_, k_, kk="kk": ("f32", f"vs[{kk} * DV + jj]"))
         if st.dep:
-            em2.fusable = fus
-            em2.env.update(scalar_env)
-            em2.bind_const(plan.i, "int", "(q0 + r)")
-            em2.bind_const(plan.j, "int", "jj")
-            em2.bind_const(st.loop.axis.name, "int", "(k0 + kk)")
-            for n in row_names:
-                em2.env.setdefault(n, ("f32", row_ref(n, "r")))
-            for n, si in stash_codes.items():
-                em2.env[n] = ("f32", f"stash[({si} * BQ + r) * SS + kk]")
-            for a in plan.cell_accs:
-                em2.env[a] = ("f32", f"cacc_{_c(a)}[u]")
-                em2.declared[f"{a}|f32"] = f"cacc_{_c(a)}[u]"
-            em2.run(tuple(st.dep))
-            w("\n".join(em2.lines))
-            if shared_j:
-                w(f"{i2}        }}")
-                w(f"{i2}    }}")
-                w(f"{i2}}}")
-                w(f"{i2}}}")
-            else:
-                w(f"{i5}}}")
-                w(f"{i2}    }}")
-                w(f"{i2}}}")
+            _emit_dep(w, i2, st, plan, shapes, dtypes, ptrs, fus, scalar_env, row_names, row_ref,
+                      stash_codes, nown, T)
         w(f"{ind}}}")
-    # the output
+        if reg_accs:
+            # combine the partials of each row: over the lanes of a warp, then over the
+            # BK / 32 warps that hold the row
+            for ri, (fi, a, op, kind, accum) in enumerate(reg_accs):
+                w(f"{ind}#pragma unroll")
+                w(f"{ind}for (int u = 0; u < {NP}; ++u) {{")
+                w(f"{ind}    float x = pm{ri}[u];")
+                w(f"{ind}    #pragma unroll")
+                w(f"{ind}    for (int o = 16; o > 0; o >>= 1) x = {combine_code(op, 'x', '__shfl_xor_sync(0xffffffffu, x, o)')};")
+                w(f"{ind}    if (lane == 0) pred[({ri} * {NW} + warp) * {NP} + u] = x;")
+                w(f"{ind}}}")
+            w(f"{ind}__syncthreads();")
+            w(f"{ind}if (tid < nq) {{")
+            w(f"{ind}    const int r = tid, u = r / {RS}, w0 = (r % {RS}) * (BK / 32);")
+            for ri, (fi, a, op, kind, accum) in enumerate(reg_accs):
+                w(f"{ind}    {{")
+                w(f"{ind}        float x = {row_ref(a, 'r')};")
+                w(f"{ind}        for (int wv = w0; wv < w0 + BK / 32; ++wv) x = {combine_code(op, 'x', f'pred[({ri} * {NW} + wv) * {NP} + u]')};")
+                w(f"{ind}        {row_ref(a, 'r')} = x;")
+                w(f"{ind}    }}")
+            w(f"{ind}}}")
+    # the output (row values may come from a row statement of another thread)
+    w(f"{ind}__syncthreads();")
     w(f"{ind}#pragma unroll")
     w(f"{ind}for (int u = 0; u < {nown}; ++u) {{")
     w(f"{ind}    const int o = tid + u * {T};")
@@ -546,7 +659,6 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
     w(f"{ind}        {ptrs[plan.out_name]}[(q0 + r) * DV + jj] = {code};")
     w(f"{ind}    }}")
     w(f"{ind}}}")
-    w(f"{ind}__syncthreads();")
     w("    }")
     w("}")
     blocks = -(-SQ // BQ)
@@ -563,10 +675,89 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
                         range_bytes=rb)
     lines.append(launch_record_source("attention", launch, params))
     notes = {"kernel": "attention_rows", "rows_per_cta": BQ, "key_tile": BK, "threads": T, "score_cache": cache,
-             "passes":
-             sum(isinstance(s, KeyLoop) for s in plan.steps), "smem": smem_bytes}
+             "passes": len(keyloops), "smem": smem_bytes, "async_k": async_k, "async_v": async_v,
+             "min_blocks": min_blocks}
     return KernelSource(entry=kop.name, source="\n".join(lines), launch=launch, params=params,
                         family="attention", notes=notes)
+
+
+def _emit_dep(w, i2, st, plan, shapes, dtypes, ptrs, fus, scalar_env, row_names, row_ref, stash_codes,
+              nown, T) -> None:
+    """The statements of a key loop that depend on ``j`` (the ``v[k, j]``
+    product and the cell accumulation), in key order per output cell."""
+    DV = plan.DV
+
+    def run(indent, load_code, stash_code):
+        em2 = Emitter(shapes, dtypes, ptrs, indent=indent, load_hook=lambda s_, k_: ("f32", load_code))
+        em2.fusable = fus
+        em2.env.update(scalar_env)
+        em2.bind_const(plan.i, "int", "(q0 + r)")
+        em2.bind_const(plan.j, "int", "jj")
+        em2.bind_const(st.loop.axis.name, "int", "(k0 + kk)")
+        for n in row_names:
+            em2.env.setdefault(n, ("f32", row_ref(n, "r")))
+        for n, si in stash_codes.items():
+            em2.env[n] = ("f32", stash_code(si))
+        for a in plan.cell_accs:
+            em2.env[a] = ("f32", f"cacc_{_c(a)}[u]")
+            em2.declared[f"{a}|f32"] = f"cacc_{_c(a)}[u]"
+        em2.run(tuple(st.dep))
+        w("\n".join(em2.lines))
+
+    ns = len(stash_codes)
+    if T % DV == 0:
+        # every owned cell of a thread has the same column: one v read per key feeds
+        # them all; full tiles read each row's stashed values four keys at a time
+        w(f"{i2}{{")
+        w(f"{i2}const int jj = tid % DV;")
+        if ns:
+            w(f"{i2}if (nk == BK) {{")
+            w(f"{i2}    #pragma unroll {PV_UNROLL}")
+            w(f"{i2}    for (int k4 = 0; k4 < BK; k4 += 4) {{")
+            w(f"{i2}        float wst[{ns}][{nown}][4];")
+            w(f"{i2}        #pragma unroll")
+            w(f"{i2}        for (int u = 0; u < {nown}; ++u) {{")
+            w(f"{i2}            const int r = (tid + u * {T}) / DV;")
+            for si in range(ns):
+                w(f"{i2}            const float4 t{si} = r < nq ? *reinterpret_cast<const float4 *>(stash + ({si} * BQ + r) * SS + k4) : make_float4(0.f, 0.f, 0.f, 0.f);")
+                w(f"{i2}            wst[{si}][u][0] = t{si}.x; wst[{si}][u][1] = t{si}.y; wst[{si}][u][2] = t{si}.z; wst[{si}][u][3] = t{si}.w;")
+            w(f"{i2}        }}")
+            w(f"{i2}        #pragma unroll")
+            w(f"{i2}        for (int c = 0; c < 4; ++c) {{")
+            w(f"{i2}            const int kk = k4 + c;")
+            w(f"{i2}            const float vcur = vs[kk * DV + jj];")
+            w(f"{i2}            #pragma unroll")
+            w(f"{i2}            for (int u = 0; u < {nown}; ++u) {{")
+            w(f"{i2}                const int r = (tid + u * {T}) / DV;")
+            w(f"{i2}                if (r < nq) {{")
+            run(i2 + "                    ", "vcur", lambda si: f"wst[{si}][u][c]")
+            w(f"{i2}                }}")
+            w(f"{i2}            }}")
+            w(f"{i2}        }}")
+            w(f"{i2}    }}")
+            w(f"{i2}}} else")
+        w(f"{i2}for (int kk = 0; kk < nk; ++kk) {{")
+        w(f"{i2}    const float vcur = vs[kk * DV + jj];")
+        w(f"{i2}    #pragma unroll")
+        w(f"{i2}    for (int u = 0; u < {nown}; ++u) {{")
+        w(f"{i2}        const int r = (tid + u * {T}) / DV;")
+        w(f"{i2}        if (r < nq) {{")
+        run(i2 + "            ", "vcur", lambda si: f"stash[({si} * BQ + r) * SS + kk]")
+        w(f"{i2}        }}")
+        w(f"{i2}    }}")
+        w(f"{i2}}}")
+        w(f"{i2}}}")
+        return
+    w(f"{i2}#pragma unroll")
+    w(f"{i2}for (int u = 0; u < {nown}; ++u) {{")
+    w(f"{i2}    const int o = tid + u * {T};")
+    w(f"{i2}    const int r = o / DV, jj = o - r * DV;")
+    w(f"{i2}    if (r < nq) {{")
+    w(f"{i2}        for (int kk = 0; kk < nk; ++kk) {{")
+    run(i2 + "            ", "vs[kk * DV + jj]", lambda si: f"stash[({si} * BQ + r) * SS + kk]")
+    w(f"{i2}        }}")
+    w(f"{i2}    }}")
+    w(f"{i2}}}")
 
 
 def _row_defined(plan: AttnPlan, name: str, upto) -> bool:

@@ -64,6 +64,8 @@ def lib():
         L.ora_strided_reduce_f32.argtypes = [vp, vp, i64, i64, i32, i32, f32, vp]
         L.ora_loop_reduce_f32.argtypes = [vp, vp, i64, i64, i32, f32, vp]
         L.ora_row_sum_f64.argtypes = [vp, i64, i64, vp]
+        L.ora_attn_naive_f32.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, f32]
+        L.ora_attn_naive_f32.restype = i32
         del fp
         _LIB = L
     return _LIB

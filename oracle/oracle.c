@@ -21,6 +21,7 @@
 #include <math.h>
 #include <stdint.h>
 #include <stddef.h>
+#include <stdlib.h>
 #include <string.h>
 
 #ifdef _OPENMP
@@ -145,6 +146,50 @@ void ora_row_sum_f64(const float *x, int64_t rows, int64_t cols, double *out) {
         for (int64_t k = 0; k < cols; ++k) s += (double)row[k];
         out[r] = s;
     }
+}
+
+/* The naive attention IR (tools/make_proxy_set.py:416-474) as the reference
+ * lowers it: every Loop runs in order (compile.py:1813-1864), multiply +
+ * Accum pairs contract to fma.rn (compile.py:1263-1283), exp is ex2.approx of
+ * x * log2(e) (compile.py:2099-2104), reciprocal is rcp.rn (compile.py:2106).
+ * For output cell (i, j) the reference recomputes, in each of three passes
+ * over the keys, s = (fma chain over d of q[i, d] * kt[d, k]) * scale:
+ *   pass 1: m = max(m, s), m seeded -1e30 (compile.py:332);
+ *   pass 2: den = den + exp(s - m), den seeded 0;
+ *   then invd = 1 / den;
+ *   pass 3: acc = fma(exp(s - m) * invd, v[k, j], acc), acc seeded 0.
+ * s and exp(s - m) do not depend on j, so they are computed once per (i, k)
+ * here; the values are the same.  kt is [d, sk] (the IR's layout); v is
+ * [sk, dv].  Returns 0, or -1 when scratch memory is not available. */
+int ora_attn_naive_f32(const float *q, const float *kt, const float *v, float *out, int64_t sq, int64_t sk,
+                       int64_t d, int64_t dv, float scale) {
+    const float L2E = 1.44269502162933349609375f; /* 0x3FB8AA3B: log2(e) rounded to f32 */
+    float *s = (float *)malloc((size_t)sk * 2 * sizeof(float));
+    if (!s) return -1;
+    float *ex = s + sk;
+    for (int64_t i = 0; i < sq; ++i) {
+        float m = -1e30f;
+        for (int64_t k = 0; k < sk; ++k) {
+            float acc = 0.0f;
+            for (int64_t t = 0; t < d; ++t) acc = fmaf(q[i * d + t], kt[t * sk + k], acc);
+            s[k] = acc * scale;
+            m = fmaxf(m, s[k]);
+        }
+        float den = 0.0f;
+        for (int64_t k = 0; k < sk; ++k) {
+            const float dl = s[k] - m;
+            ex[k] = ftz(exp2f(ftz(dl * L2E)));
+            den = den + ex[k];
+        }
+        const float invd = 1.0f / den;
+        for (int64_t j = 0; j < dv; ++j) {
+            float acc = 0.0f;
+            for (int64_t k = 0; k < sk; ++k) acc = fmaf(ex[k] * invd, v[k * dv + j], acc);
+            out[i * dv + j] = acc;
+        }
+    }
+    free(s);
+    return 0;
 }
 
 int ora_num_threads(void) {

@@ -127,3 +127,44 @@ def test_oracle_against_reference_ptx_golden_vectors(cid):
             np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-5)
         else:
             assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), f"{cid}.{name}"
+
+
+def _attn_scale(kop) -> float:
+    """The score scale of the naive attention IR: its first ``Let`` of a literal."""
+    stack = list(kop.body)
+    while stack:
+        s = stack.pop(0)
+        val = getattr(s, "value", None)
+        if type(s).__name__ == "Let" and hasattr(val, "value"):
+            return float(np.float32(val.value))
+        for attr in ("body",):
+            stack = list(getattr(s, attr, ()) or ()) + stack
+    raise AssertionError("no scale literal in the attention IR")
+
+
+@pytest.mark.parametrize("cid", ["a_attn_64x32", "a_attn_100x48", "a_attn_256x64", "a_attn_krows_80x40"])
+def test_attention_c_restatement(cid):
+    """``ora_attn_naive_f32`` (the C restatement used for the bench's CPU arm)
+    gives the Python oracle's values bit for bit, and matches the golden
+    vectors of the reference's PTX run on a B200 within the oracle bound."""
+    import interp
+    kop, meta, mk, shapes, dtypes = interp.load_case(CASES / cid)
+    out, inputs = interp.run_case(CASES / cid)
+    q = np.ascontiguousarray(inputs["q"], dtype=np.float32)
+    kname = "kt" if "kt" in inputs else next(n for n in inputs if n not in ("q", "v"))
+    kmat = np.ascontiguousarray(inputs[kname], dtype=np.float32)
+    v = np.ascontiguousarray(inputs["v"], dtype=np.float32)
+    sq, d = q.shape
+    sk, dv = v.shape
+    if kmat.shape == (sk, d):
+        kmat = np.ascontiguousarray(kmat.T)    # the restatement takes keys as [d, sk]
+    got = np.empty((sq, dv), dtype=np.float32)
+    rc = interp.lib().ora_attn_naive_f32(interp._p(q), interp._p(kmat), interp._p(v), interp._p(got),
+                                         sq, sk, d, dv, _attn_scale(kop))
+    assert rc == 0
+    oname = next(iter(out))
+    assert np.array_equal(got.reshape(-1).view(np.uint32), out[oname].reshape(-1).view(np.uint32))
+    if (GOLDEN_DIR / f"{cid}.npz").is_file():
+        ref = np.load(GOLDEN_DIR / f"{cid}.npz")[oname].reshape(-1)
+        ok, why = interp.within(got.reshape(-1), ref, {"rtol": 4e-6, "atol": 2e-6})
+        assert ok, why
