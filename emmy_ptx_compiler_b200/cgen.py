@@ -116,6 +116,7 @@ F32_BINARY = {"add": "__fadd_rn({a}, {b})", "sum": "__fadd_rn({a}, {b})",
               "div": "__fdiv_rn({a}, {b})",
               "maximum": "fmaxf({a}, {b})", "amax": "fmaxf({a}, {b})", "max": "fmaxf({a}, {b})",
               "minimum": "fminf({a}, {b})", "amin": "fminf({a}, {b})", "min": "fminf({a}, {b})"}
+DIVIDE_OPS = ("divide", "true_divide", "div")
 INT_BINARY = {"add": "({a} + {b})", "sum": "({a} + {b})", "subtract": "({a} - {b})",
               "sub": "({a} - {b})", "multiply": "({a} * {b})", "mul": "({a} * {b})",
               "maximum": "max({a}, {b})", "max": "max({a}, {b})", "minimum": "min({a}, {b})",
@@ -276,6 +277,8 @@ class Emitter:
         # C type of f32 values: "float", or "EmmyF2" when every value is a pair
         # of adjacent cells computed with packed f32x2 instructions
         self.ftype = "float"
+        # divisor code -> (reciprocal code, fast-path flag code) for divisors shared by many cells
+        self.row_divisors: dict[str, tuple[str, str]] = {}
 
     # -------------------------------------------------------------- small utils
     def emit(self, line: str) -> None:
@@ -480,6 +483,9 @@ class Emitter:
     def f32_op(self, op: str, args: list[str]) -> str:
         """One Assign op on already-f32 operands (compile.py:2087-2199)."""
         n = len(args)
+        if op in DIVIDE_OPS and n == 2 and args[1] in self.row_divisors:
+            r, ok = self.row_divisors[args[1]]
+            return f"emmy_div_by({args[0]}, {args[1]}, {r}, {ok})"
         if op in F32_BINARY and n == 2:
             return F32_BINARY[op].format(a=args[0], b=args[1])
         if op in CMP and n == 2:
@@ -762,6 +768,28 @@ DEVICE_PRELUDE = r"""
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
+
+// x / y rounded to nearest (div.rn.f32, compile.py:2093) when many x share one
+// divisor y whose reciprocal ry = RN(1 / y) (rcp.rn.f32) is computed once:
+// Markstein's correction (P. Markstein, "Computation of elementary functions on
+// the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990):
+// q0 = RN(x * ry) is within one ulp of x / y, the remainder r = x - q0 * y is
+// exact in one fma, and RN(q0 + r * ry) is the correctly rounded quotient.  The
+// fast path requires the operands, the quotient and the remainder to stay away
+// from underflow and overflow (y_ok: 2^-64 <= |y| <= 2^64; |x| >= 2^-64;
+// 2^-125 <= |q0| <= 2^126); everything else, zeros, infinities and NaNs
+// included, takes __fdiv_rn itself.
+static __device__ __forceinline__ bool emmy_div_ok(float y) {
+    const float ay = fabsf(y);
+    return ay >= 0x1p-64f && ay <= 0x1p+64f;
+}
+static __device__ __forceinline__ float emmy_div_by(float x, float y, float ry, bool y_ok) {
+    const float q0 = __fmul_rn(x, ry);
+    const float ax = fabsf(x), aq = fabsf(q0);
+    if (!(y_ok && ax >= 0x1p-64f && aq >= 0x1p-125f && aq <= 0x1p+126f)) return __fdiv_rn(x, y);
+    const float r = __fmaf_rn(-q0, y, x);
+    return __fmaf_rn(r, ry, q0);
+}
 
 // Approximate-math instructions the reference compiler builds exp/tanh/
 // sigmoid/silu/log/pow from (compile.py:2098-2195).  Issued as the same PTX

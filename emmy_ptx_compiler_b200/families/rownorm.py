@@ -33,8 +33,8 @@ from __future__ import annotations
 from dataclasses import dataclass, field
 
 from .. import ir
-from ..cgen import (DEVICE_PRELUDE, Emitter, combine_code, ctype, f32_lit, fusable_products, identity_of, lit_int,
-                    load_to_kind, store_from)
+from ..cgen import (DEVICE_PRELUDE, DIVIDE_OPS, Emitter, combine_code, ctype, f32_lit, fusable_products, identity_of,
+                    lit_int, load_to_kind, store_from)
 from ..errors import UnsupportedIR
 from .common import KernelSource, LaunchPlan, ParamSpec, SM_COUNT, launch_record_source
 from .pointwise import _VEC_HELPERS
@@ -490,6 +490,10 @@ def _row_loop(plan: RowPlan, shapes, dtypes, ptrs, scalar_env, fus, VW: int, T: 
         acc *= e
     strides.reverse()
     row_env = dict(scalar_env)
+    # reduction results that divide the row's cells (each is final once folded)
+    divisors = {t.args[1] for t in ir.walk(plan.tile.body) if isinstance(t, ir.Assign)
+                and ir.op_name(t.op) in DIVIDE_OPS and len(t.args) == 2 and isinstance(t.args[1], str)}
+    row_div: dict[str, tuple[str, str]] = {}
     for (name, e), st in zip(plan.row_axes, strides):
         var = f"ra_{_c(name)}"
         expr = f"({rem} / {st}LL) % {e}LL" if st > 1 else f"{rem} % {e}LL"
@@ -619,6 +623,7 @@ def _row_loop(plan: RowPlan, shapes, dtypes, ptrs, scalar_env, fus, VW: int, T: 
                 em = Emitter(shapes, dtypes, ptrs, load_hook=load_hook, write_hook=write_hook,
                              indent=body_ind + "    ")
                 em.fusable = fus
+                em.row_divisors = dict(row_div)
                 em.env.update(row_env)
                 for a, var in acc_vars.items():
                     em.env[a] = ("f32", var)
@@ -658,10 +663,16 @@ def _row_loop(plan: RowPlan, shapes, dtypes, ptrs, scalar_env, fus, VW: int, T: 
                 o(f"{i2}for (int w2 = 1; w2 < {T // 32}; ++w2) {var} = {combine_code(op, var, f'red_smem[{sl}][w2]')};")
                 row_env[a] = ("f32", var)
                 declared_row[f"{a}|f32"] = var
+                if a in divisors:
+                    # every cell of the row divides by this value: its reciprocal once per row
+                    o(f"{i2}const float rcp_{var} = __frcp_rn({var});")
+                    o(f"{i2}const bool dok_{var} = emmy_div_ok({var});")
+                    row_div[var] = (f"rcp_{var}", f"dok_{var}")
             continue
         kind, stmt = step
         em = Emitter(shapes, dtypes, ptrs, indent=i2 + ("    " if kind == "leader" else ""))
         em.fusable = fus
+        em.row_divisors = dict(row_div)
         em.env.update(row_env)
         for key, var in declared_row.items():
             em.declared[key] = var
