@@ -27,7 +27,7 @@ from pathlib import Path
 
 from . import frontend, ir, toolchain
 from .errors import ToolchainError, UnsupportedIR
-from .families import attention, gemm, pointwise, reduction, rownorm
+from .families import attention, gemm, pointwise, reduction, rownorm, schedule
 from .families.common import KernelSource
 
 
@@ -63,6 +63,13 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
     for name in args:
         if name not in scalars and name not in shapes and name not in dtypes:
             raise UnsupportedIR(f"parameter {name!r} has no shape or dtype")
+    if options.get("family") == "schedule":
+        plan = schedule.match(kop, shapes, dtypes)
+        if plan is None:
+            raise UnsupportedIR(f"KernelOp {kop.name!r} cannot be lowered as its own schedule "
+                                f"(unsupported nodes: {', '.join(schedule.unsupported_nodes(kop)) or 'layout'})")
+        ks = schedule.generate(kop, plan, shapes, dtypes, args, scalars, written, meta)
+        return Lowered(ks, args, shapes, dtypes, meta)
     plan = attention.match(kop, shapes, dtypes)
     if plan is not None:
         ks = attention.generate(kop, plan, shapes, dtypes, args, scalars, written)
@@ -85,9 +92,15 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
         ks = pointwise.generate(kop, plan, shapes, dtypes, args, scalars, written,
                                 pair=options.get("pointwise_pair", "auto"))
         return Lowered(ks, args, shapes, dtypes, meta)
+    # no recognised computation: keep the schedule the IR spells out
+    plan = schedule.match(kop, shapes, dtypes)
+    if plan is not None:
+        ks = schedule.generate(kop, plan, shapes, dtypes, args, scalars, written, meta)
+        return Lowered(ks, args, shapes, dtypes, meta)
+    bad = schedule.unsupported_nodes(kop)
     kinds = sorted({type(s).__name__ for s in ir.walk(kop.body)})
-    raise UnsupportedIR(f"KernelOp {kop.name!r} is not a pointwise, reduction or GEMM kernel "
-                        f"(nodes: {', '.join(kinds)})")
+    raise UnsupportedIR(f"KernelOp {kop.name!r} has nodes no sm_100a lowering supports "
+                        f"({', '.join(bad) or 'layout'}; nodes: {', '.join(kinds)})")
 
 
 class Compiler:

@@ -7,7 +7,7 @@ from dataclasses import dataclass, field
 
 SM_COUNT = 148  # B200: 2 dies x 74 SMs
 
-FAMILY_ID = {"pointwise": 1, "reduction": 2, "gemm": 3, "rownorm": 4, "attention": 5}
+FAMILY_ID = {"pointwise": 1, "reduction": 2, "gemm": 3, "rownorm": 4, "attention": 5, "schedule": 6}
 PARAM_KIND = {"ptr": 0, "f32": 1, "i32": 2}
 
 

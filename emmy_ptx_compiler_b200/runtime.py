@@ -17,7 +17,8 @@ from pathlib import Path
 from . import native
 
 EMMY_ROLE_IN, EMMY_ROLE_OUT, EMMY_ROLE_INOUT, EMMY_ROLE_OUT_ZEROED, EMMY_ROLE_SCALAR = 0, 1, 2, 3, 4
-FAMILY_NAMES = {0: "foreign", 1: "pointwise", 2: "reduction", 3: "gemm", 4: "rownorm", 5: "attention"}
+FAMILY_NAMES = {0: "foreign", 1: "pointwise", 2: "reduction", 3: "gemm", 4: "rownorm", 5: "attention",
+                6: "schedule"}
 
 _lock = threading.Lock()
 _lib = None

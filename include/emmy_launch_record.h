@@ -38,7 +38,8 @@ enum EmmyFamily {
     EMMY_FAMILY_REDUCTION = 2,
     EMMY_FAMILY_GEMM = 3,
     EMMY_FAMILY_ROWFUSED = 4, /* row reductions + pointwise pass in one kernel */
-    EMMY_FAMILY_ATTENTION = 5 /* per-key passes over q.k scores, weighted sum of v */
+    EMMY_FAMILY_ATTENTION = 5, /* per-key passes over q.k scores, weighted sum of v */
+    EMMY_FAMILY_SCHEDULE = 6   /* any other KernelOp, in the schedule its IR spells out */
 };
 
 enum EmmyParamKind { EMMY_PARAM_PTR = 0, EMMY_PARAM_F32 = 1, EMMY_PARAM_I32 = 2 };

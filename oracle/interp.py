@@ -43,7 +43,7 @@ sys.path.insert(0, str(HERE / "emmy_shim"))
 from emmy._core import (  # noqa: E402
     Accum, Assign, BinaryExpr, Builtin, CastExpr, Cond, FlatIndex, FuncCallExpr, Graph, Init, KernelOp,
     Let, Literal, Load, Loop, Select, Smem, StridedLoop, Sync, TernaryExpr, Tile, TreeHalve, Var, ZeroPrologue,
-    WarpShuffle, Write,
+    WarpShuffle, Write, CpAsyncCopy, CpAsyncCommit, CpAsyncWait,
 )
 
 _LIB = None
@@ -684,6 +684,8 @@ def evaluate(kop, shapes: dict, dtypes: dict, inputs: dict[str, np.ndarray],
     """Run ``kop`` on float32 ``inputs`` (bf16 inputs passed as their f32 values);
     returns float32 outputs (bf16/f16 outputs rounded as the store would)."""
     body = list(kop.body)
+    if any(isinstance(t, (CpAsyncCopy, CpAsyncCommit, CpAsyncWait)) for t in ir_walk(body)):
+        return _eval_simt(kop, shapes, dtypes, inputs, outputs)
     assert len(body) == 1 and isinstance(body[0], Tile), "oracle: one Tile per KernelOp"
     tile = body[0]
     stmts = list(tile.body)
@@ -714,6 +716,153 @@ def evaluate(kop, shapes: dict, dtypes: dict, inputs: dict[str, np.ndarray],
         for k, v in _cells_for(axes, n).items():
             m.env[k] = ("int", v)
         m.run(stmts)
+    return {k: bufs[k].reshape(outputs[k]) if outputs[k] else bufs[k][:1] for k in outputs}
+
+
+class Simt(Cells):
+    """One thread block of a block-cooperative schedule, its threads as the
+    vector lanes, run in lockstep (compile.py:1520-1629 thread model).
+
+    Between barriers a race-free schedule gives the same values whatever the
+    interleaving of its threads, so lockstep evaluation with the barriers as
+    no-ops reproduces it.  Shared buffers live in ``bufs`` under their names
+    for the duration of the block; ``cp.async`` copies complete at once."""
+
+    def expr(self, e):
+        if isinstance(e, Builtin):
+            if e.name in self.env:
+                return self.env[e.name]
+            raise KeyError(f"oracle: thread builtin {e.name}")
+        return super().expr(e)
+
+    def stmt(self, s) -> None:
+        if isinstance(s, (Smem, Sync, CpAsyncCommit, CpAsyncWait)):
+            return
+        if isinstance(s, StridedLoop):
+            # per-thread start (compile.py:1866-1914): each lane runs its own trips
+            start = np.broadcast_to(self._toi(*self.expr(s.start)), (self.n,)).astype(np.int64)
+            step = np.broadcast_to(self._toi(*self.expr(s.step)), (self.n,)).astype(np.int64)
+            end = (np.broadcast_to(self._toi(*self.expr(s.end)), (self.n,)) if s.end is not None
+                   else np.full(self.n, int(s.axis.extent.value), np.int64))
+            if s.seed:
+                for t in s.body:
+                    if isinstance(t, Accum) and t.name not in self.env:
+                        self.bind(t.name, "f32", np.full(self.n, F32(identity_of(t.op))))
+            outer = self.mask
+            i = start.copy()
+            while True:
+                live = i < end
+                if outer is not None:
+                    live = live & outer
+                if not live.any():
+                    break
+                self.mask = live
+                self.env[s.axis.name] = ("int", i.copy())
+                self.run(s.body)
+                i = i + step
+            self.mask = outer
+            return
+        if isinstance(s, Loop) and s.seed:
+            for t in s.body:
+                if isinstance(t, Accum) and t.name not in self.env:
+                    self.bind(t.name, "f32", np.full(self.n, F32(identity_of(t.op))))
+        if isinstance(s, WarpShuffle):
+            lanes = np.arange(self.n, dtype=np.int64)
+            step = int(s.length) // 2
+            while step > 0:
+                for st, sb in zip(s.state, s.state_b):
+                    v = np.broadcast_to(self.f32(st), (self.n,))
+                    self.env[sb] = ("f32", v[lanes ^ step].astype(F32))
+                for asn in s.combine_states:
+                    super().stmt(asn)
+                step >>= 1
+            return
+        if isinstance(s, TreeHalve):
+            tid = np.broadcast_to(self._toi(*self.expr(Var(s.tid_var))), (self.n,)).astype(np.int64)
+            step = int(s.length) // 2
+
+            def slot(extra):
+                if s.inner is not None:
+                    iv, scale = s.inner
+                    return (tid + extra) * int(scale) + self._toi(*self.expr(Var(iv) if isinstance(iv, str) else iv))
+                return tid + extra
+            outer = self.mask
+            while step > 0:
+                take = tid < step
+                if outer is not None:
+                    take = take & outer
+                self.mask = take
+                for buf, st, sb in zip(s.bufs, s.state, s.state_b):
+                    b = self.bufs[buf]
+                    self.bind(st, "f32", b[np.where(take, slot(0), 0)].astype(F32))
+                    self.bind(sb, "f32", b[np.where(take, slot(step), 0)].astype(F32))
+                for asn in s.combine_states:
+                    super().stmt(asn)
+                for buf, st in zip(s.bufs, s.state):
+                    b = self.bufs[buf]
+                    vals = np.broadcast_to(self.f32(st), (self.n,))
+                    b[slot(0)[take]] = vals[take]
+                self.mask = outer
+                step >>= 1
+            for buf, st in zip(s.bufs, s.state):
+                root = (self._toi(*self.expr(Var(s.inner[0]) if isinstance(s.inner[0], str) else s.inner[0]))
+                        if s.inner is not None else 0)
+                self.bind(st, "f32", np.broadcast_to(self.bufs[buf][root], (self.n,)).astype(F32))
+            return
+        if isinstance(s, CpAsyncCopy):
+            # cp.async.ca|cg of nbytes (compile.py:2288-2319): f32 elements, contiguous
+            dst, src = self.bufs[s.smem], self.bufs[s.src]
+            didx = np.broadcast_to(self.flat(s.smem, s.smem_index), (self.n,)).astype(np.int64)
+            if s.lane_index is not None:
+                cols = int(self.shapes[s.smem][-1])
+                didx = didx + (np.broadcast_to(self._toi(*self.expr(s.lane_index[0])), (self.n,)) * cols
+                               + np.broadcast_to(self._toi(*self.expr(s.lane_index[1])), (self.n,)))
+            sidx = np.broadcast_to(self.flat(s.src, s.src_index), (self.n,)).astype(np.int64)
+            sel = np.ones(self.n, bool) if self.mask is None else self.mask
+            for k in range(int(s.nbytes) // 4):
+                dst[didx[sel] + k] = src[sidx[sel] + k]
+            return
+        super().stmt(s)
+
+
+def _eval_simt(kop, shapes: dict, dtypes: dict, inputs: dict, outputs: dict, block: int | None = None):
+    """Block-by-block lockstep evaluation of a block-cooperative KernelOp."""
+    bufs = {k: np.ascontiguousarray(v, F32).reshape(-1).copy() for k, v in inputs.items()}
+    for name, shp in outputs.items():
+        bufs[name] = np.zeros(int(np.prod(shp)) if shp else 1, F32)
+    shapes = dict(shapes)
+    smem = {}
+    for t in ir_walk(list(kop.body)):
+        if isinstance(t, Smem):
+            smem[t.name] = tuple(int(x) for x in t.extents)
+            shapes[t.name] = smem[t.name]
+    for top in kop.body:
+        if isinstance(top, ZeroPrologue):
+            bufs[top.dst].view(np.uint32)[:int(top.words)] = 0
+            continue
+        if isinstance(top, Smem):
+            continue
+        tile = top
+        axes = _axes(tile)
+        n_cells = int(np.prod([e for _, e in axes])) if axes else 1
+        bt = int(tile.block_threads or block or 128)
+        nblocks = max(1, -(-n_cells // bt))
+        strides = row_major([e for _, e in axes])
+        for b in range(nblocks):
+            for name, shp in smem.items():
+                bufs[name] = np.zeros(int(np.prod(shp)), F32)
+            m = Simt(bt, bufs, shapes, dtypes)
+            tid = np.arange(bt, dtype=np.int64)
+            gid = b * bt + tid
+            m.env.update({"_tid": ("int", tid), "_gid": ("int", gid), "lane": ("int", tid & 31),
+                          "warp": ("int", tid >> 5), "threadIdx.x": ("int", tid),
+                          "blockIdx.x": ("int", np.full(bt, b, np.int64)), "blockDim.x": ("int", np.int64(bt))})
+            for i, ((name, e), st) in enumerate(zip(axes, strides)):
+                term = gid // st
+                m.env[name] = ("int", term if i == 0 else term % e)
+            if n_cells % bt:
+                m.mask = gid < n_cells
+            m.run(list(tile.body))
     return {k: bufs[k].reshape(outputs[k]) if outputs[k] else bufs[k][:1] for k in outputs}
 
 

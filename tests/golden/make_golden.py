@@ -54,7 +54,7 @@ from emmy.compiler.dim import Dim  # noqa: E402
 from emmy.compiler.ir.elementwise import ElementwiseImpl as EW  # noqa: E402
 from emmy.compiler.ir.expr import BinaryExpr, Literal, Var  # noqa: E402
 from emmy.compiler.ir.kernel.ir import (  # noqa: E402
-    Axis, DataType, Smem, Sync, Tile, TreeHalve, WarpShuffle,
+    Axis, CpAsyncCommit, CpAsyncCopy, CpAsyncWait, DataType, Smem, Sync, Tile, TreeHalve, WarpShuffle,
 )
 from emmy.compiler.ir.stmt import (  # noqa: E402
     Accum, Assign, Cond, Init, Let, Load, Loop, StridedLoop, Write, ZeroPrologue,
@@ -605,6 +605,58 @@ def gemm_case(cid: str, m: int, k: int, n: int, *, dtype: DataType = BF16, epilo
                 ref_case=ref_case)
 
 
+def cpasync_matmul_case(cid: str, m: int, k: int, n: int, *, wide: bool = False) -> Case:
+    """A shared-memory matmul schedule of the kind Emmy emits with cp.async
+    (lowered by compile.py:2288-2319, 1460-1465): one 16x16 output tile per
+    256-thread block (Tile axes bi, bj, ty, tx), A and B staged tile by tile
+    into shared memory by cp.async, then a sequential k loop over the staged
+    tiles.  4-byte copies by every thread, or with ``wide`` 16-byte copies by
+    the threads of the first four columns.  No reference generator writes this
+    schedule; the IR is ours, its PTX is the reference compiler's."""
+    ts = 16
+    entry = "k_matmul_cpasync"
+    lit = lambda v: Literal(v, "int")  # noqa: E731
+    at = lambda blk, thr: BinaryExpr("+", BinaryExpr("*", Var(blk), lit(ts)), thr)  # noqa: E731
+    row, col = at("bi", Var("ty")), at("bj", Var("tx"))
+    if wide:
+        tx4 = BinaryExpr("*", Var("tx"), lit(4))
+        copies = (Cond(BinaryExpr("<", Var("tx"), lit(4)), body=(
+            CpAsyncCopy("As", (Var("ty"), tx4), "A", (row, at("kt", tx4)), 16),
+            CpAsyncCopy("Bs", (Var("ty"), tx4), "B", (at("kt", Var("ty")), at("bj", tx4)), 16),
+        )),)
+    else:
+        copies = (CpAsyncCopy("As", (Var("ty"), Var("tx")), "A", (row, at("kt", Var("tx"))), 4),
+                  CpAsyncCopy("Bs", (Var("ty"), Var("tx")), "B", (at("kt", Var("ty")), col), 4))
+    body = Tile(axes=(Axis("bi", Dim(m // ts)), Axis("bj", Dim(n // ts)), Axis("ty", Dim(ts)),
+                      Axis("tx", Dim(ts))), body=(
+        Smem("As", (ts, ts), "float", 16),
+        Smem("Bs", (ts, ts), "float", 16),
+        Init("acc", 0.0, dtype=F32),
+        Loop(axis=Axis("kt", Dim(k // ts)), body=(
+            *copies,
+            CpAsyncCommit(),
+            CpAsyncWait(0),
+            Sync(),
+            Loop(axis=Axis("kk", Dim(ts)), body=(
+                Load(names=("a",), input="As", index=(Var("ty"), Var("kk")), dtype=F32),
+                Load(names=("b",), input="Bs", index=(Var("kk"), Var("tx")), dtype=F32),
+                Assign("p", EW("multiply"), ("a", "b"), F32),
+                Accum("acc", "p", EW("add"), F32, axes=("kk",)),
+            )),
+            Sync(),
+        )),
+        Write(output="C", index=(row, col), values=("acc",), value_dtype=F32),
+    ), block_threads=ts * ts)
+    graph = {"inputs": ["A", "B"], "outputs": ["C"], "nodes": {
+        "A": _input("A", [m, k]), "B": _input("B", [k, n]),
+        "C": _kernel(entry, body, ["A", "B"], [("C", [m, n], "f32")])}}
+    grid = [(m // ts) * (n // ts), 1, 1]
+    kern = _meta_kernel("C", entry, ["A", "B", "C"], grid, [ts * ts, 1, 1], [
+        _arg("A", [m, k], init=NORM(), seed=0), _arg("B", [k, n], init=NORM(), seed=1),
+        _arg("C", [m, n], output=True)])
+    return Case(cid, entry, graph, kern, family="schedule", check={"kind": "ulp", "ulp": 0})
+
+
 # ------------------------------------------------------------ reference op catalog
 
 
@@ -926,22 +978,33 @@ def all_cases() -> list[Case]:
     cases.append(vec4_case("p_vec4_1024", 1024))
     cases.append(const_scale_case("p_const_scale_777", 777))
     cases.append(launch3d_case("p_launch3d_64"))
+    # Emmy's cp.async shared-memory matmul schedule (the schedule family)
+    cases.append(cpasync_matmul_case("s_cpasync_matmul_64x48x80", 64, 48, 80))
+    cases.append(cpasync_matmul_case("s_cpasync16_matmul_32x64x48", 32, 64, 48, wide=True))
     return cases
 
 
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
+    ap.add_argument("--only", default="", help="comma-separated case ids to (re)write; default all")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference).resolve()))
     sys.dont_write_bytecode = True
     ref = importlib.import_module("compile")
     CASES.mkdir(parents=True, exist_ok=True)
+    only = {c for c in args.only.split(",") if c}
+    old = {}
+    if only and (CASES / "INDEX.json").is_file():
+        old = {r["id"]: r for r in json.loads((CASES / "INDEX.json").read_text())["cases"]}
     index = []
     for case in all_cases():
+        if only and case.cid not in only and case.cid in old:
+            index.append(old[case.cid])
+            continue
         index.append(case.write(CASES, ref.compile_bundle))
     (CASES / "INDEX.json").write_text(json.dumps({"cases": index}, indent=1) + "\n")
-    print(f"wrote {len(index)} cases under {CASES}", file=sys.stderr)
+    print(f"indexed {len(index)} cases under {CASES}", file=sys.stderr)
     return 0
 
 

@@ -95,3 +95,49 @@ def test_new_families_do_not_claim_other_kernels(cid, family):
     kop, shapes, dtypes, args = _plan_inputs(cid)
     assert attention.match(kop, shapes, dtypes) is None
     assert rownorm.match(kop, shapes, dtypes) is None
+
+
+# ------------------------------------------------------------------ schedule family
+
+
+@pytest.mark.parametrize("cid,wide", [("s_cpasync_matmul_64x48x80", False), ("s_cpasync16_matmul_32x64x48", True)])
+def test_cp_async_schedule_lowers_to_the_schedule_family(cid, wide):
+    """No fast family recognises a cp.async-staged matmul: it keeps its own
+    schedule, with the reference's thread model and copy widths."""
+    from emmy_ptx_compiler_b200 import compiler
+    kop, shapes, dtypes, args = _plan_inputs(cid)
+    meta = json.loads((CASES / cid / "meta.json").read_text())["kernels"][0]
+    low = compiler.lower(kop, shapes, dtypes, args, meta)
+    ks = low.kernel
+    assert ks.family == "schedule"
+    assert ks.launch.grid == tuple(meta["grid"]) and ks.launch.block == tuple(meta["block"])
+    src = ks.source
+    assert "cp.async.cg.shared.global" in src if wide else "cp.async.ca.shared.global" in src
+    assert "cp.async.commit_group" in src and "cp.async.wait_group 0" in src
+    assert "__syncthreads();" in src and "__shared__" in src
+
+
+@pytest.mark.parametrize("cid", ["c3_rowsummax_5x64", "r_mean_777", "r_atomic_zp_sum_128", "f_softmax_33x130",
+                                 "a_attn_64x32", "m_matmul_f32_17x33x19", "p_launch3d_64", "p_select_256"])
+def test_every_family_input_also_lowers_as_its_own_schedule(cid):
+    """The schedule family accepts what the fast families accept (the GPU test
+    compares its outputs with the reference PTX bit for bit)."""
+    from emmy_ptx_compiler_b200 import compiler
+    ir_path = next((CASES / cid).glob("*.ir.json"))
+    b = compiler.compile_bundle(ir_path, want_cubin=True, options={"family": "schedule"})
+    assert b["family"] == "schedule" and len(b["cubin"]) > 0
+
+
+def test_tensor_core_nodes_are_reported_not_lowered():
+    """sm_90 tensor-core nodes (here mma.sync fragments) have no sm_100a
+    lowering in any family: the compiler names them."""
+    from emmy_ptx_compiler_b200 import compiler, ir
+    from emmy_ptx_compiler_b200.errors import UnsupportedIR
+    f16 = ir.DataType("f16", None, 2)
+    body = (ir.Tile(axes=(ir.Axis("a0", 32),), body=(
+        ir.RegFragment("fa", "a", (16, 8, 16), f16, 4),
+        ir.MmaSyncPtx("fc", "fa", "fb", (16, 8, 16), "f16", "f32"),
+    )),)
+    kop = ir.KernelOp(name="k_mma", body=body)
+    with pytest.raises(UnsupportedIR, match="MmaSyncPtx"):
+        compiler.lower(kop, {"x": (32,)}, {"x": "f32"}, ["x"], {"grid": [1, 1, 1], "block": [32, 1, 1]})

@@ -48,17 +48,31 @@ def test_gelu_contracts_where_the_reference_does():
     del lane
 
 
-def test_unsupported_kernel_is_reported():
+def test_block_cooperative_kernel_keeps_its_schedule():
+    """A Tile with a barrier is no pointwise kernel: it lowers as its own schedule."""
     from emmy_ptx_compiler_b200 import ir
     from emmy_ptx_compiler_b200.compiler import Compiler
-    from emmy_ptx_compiler_b200.errors import UnsupportedIR
     body = ir.Tile(axes=(ir.Axis("a0", ir.Dim(32)),), body=(
         ir.Load(names=("v",), input="x", index=(ir.Var("a0"),)),
         ir.Sync(),
         ir.Write(output="y", index=(ir.Var("a0"),), values=("v",)),
     ))
+    kop = ir.KernelOp(name="k_sync", body=(body,))
+    low = Compiler(kop, {"x": (32,), "y": (32,)}, {"x": "f32", "y": "f32"}, ["x", "y"]).lower()
+    assert low.kernel.family == "schedule" and "__syncthreads();" in low.kernel.source
+
+
+def test_unsupported_kernel_is_reported():
+    from emmy_ptx_compiler_b200 import ir
+    from emmy_ptx_compiler_b200.compiler import Compiler
+    from emmy_ptx_compiler_b200.errors import UnsupportedIR
+    body = ir.Tile(axes=(ir.Axis("a0", ir.Dim(32)),), body=(
+        ir.TmaLoad("smem_a", (ir.Literal(0, "int"),), "tensormap", (ir.Literal(0, "int"),), "mbar0"),
+        ir.Load(names=("v",), input="x", index=(ir.Var("a0"),)),
+        ir.Write(output="y", index=(ir.Var("a0"),), values=("v",)),
+    ))
     kop = ir.KernelOp(name="k_bad", body=(body,))
-    with pytest.raises(UnsupportedIR):
+    with pytest.raises(UnsupportedIR, match="TmaLoad"):
         Compiler(kop, {"x": (32,), "y": (32,)}, {"x": "f32", "y": "f32"}, ["x", "y"]).lower()
 
 

@@ -168,3 +168,17 @@ def test_attention_c_restatement(cid):
         ref = np.load(GOLDEN_DIR / f"{cid}.npz")[oname].reshape(-1)
         ok, why = interp.within(got.reshape(-1), ref, {"rtol": 4e-6, "atol": 2e-6})
         assert ok, why
+
+
+@pytest.mark.parametrize("cid", ["s_cpasync_matmul_64x48x80", "s_cpasync16_matmul_32x64x48"])
+def test_simt_oracle_on_cp_async_matmul_equals_sequential_fma(cid):
+    """The oracle's lockstep SIMT evaluation of a cp.async-staged matmul
+    schedule gives the sequential-fma GEMM (ora_gemm_seqfma_f32) bit for bit:
+    the staging changes where operands come from, not the order of the k sum."""
+    import interp
+    out, ins = interp.run_case(CASES / cid)
+    A = np.ascontiguousarray(ins["A"], np.float32)
+    B = np.ascontiguousarray(ins["B"], np.float32)
+    C = np.empty(out["C"].shape, np.float32)
+    interp.lib().ora_gemm_seqfma_f32(interp._p(A), interp._p(B), interp._p(C), A.shape[0], B.shape[1], A.shape[1], 0)
+    assert np.array_equal(C.view(np.uint32), out["C"].view(np.uint32))
