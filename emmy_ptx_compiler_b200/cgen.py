@@ -189,19 +189,58 @@ def uses_name(stmt, name: str) -> bool:
 PRODUCT_OPS = ("multiply", "mul", "square", "log", "log_fast", "silu")
 
 
+def carry_slot(index) -> str:
+    """The carry slot of a Carry/Pre index: a single literal index names its
+    slot, anything else is the wildcard (compile.py:2860-2866)."""
+    if not index:
+        return "0"
+    first = lit_int(index[0]) if len(index) == 1 else None
+    if first is not None and all(lit_int(x) == 0 for x in index[1:]):
+        return str(first)
+    return "_"
+
+
+def carry_aliases(body) -> dict[str, str]:
+    """Names that are plain copies of another name through Carry / Pre: the
+    reference emits both as ``mov.f32`` (compile.py:2868-2888), resolved in
+    program order."""
+    alias: dict[str, str] = {}
+    carried: dict[tuple[str, str], str] = {}
+    for t in ir.walk(body):
+        if isinstance(t, ir.Carry) and isinstance(t.value, str):
+            carried[(t.name, carry_slot(t.index))] = t.value
+            alias[t.name] = t.value
+        elif isinstance(t, ir.Pre):
+            src = carried.get((t.carrier, carry_slot(t.index))) or carried.get((t.carrier, "_"))
+            if src is not None:
+                alias[t.name] = src
+    return alias
+
+
 def fusable_products(body) -> set[str]:
     """Names defined once by a plain-product Assign (``mul.f32`` in the
     reference's PTX) whose every read is an operand of a plain add/sub Assign
-    or the value of an add Accum: the products the assembler folds into FMAs."""
+    or the value of an add Accum: the products the assembler folds into FMAs.
+    Reads through Carry / Pre copies count as reads of the product (the
+    assembler sees through the moves); the copies' names are returned too."""
     defs: dict[str, int] = {}
     for t in ir.walk(body):
         for name in _defined_names(t):
             defs[name] = defs.get(name, 0) + 1
     cands = {t.name for t in ir.walk(body)
              if isinstance(t, ir.Assign) and ir.op_name(t.op) in PRODUCT_OPS and defs.get(t.name) == 1}
+    alias = carry_aliases(body)
+
+    def root(n: str) -> str:
+        for _ in range(len(alias) + 1):
+            if n not in alias:
+                break
+            n = alias[n]
+        return n
+
     bad: set[str] = set()
     for t in ir.walk(body):
-        if not isinstance(t, ir.Stmt):
+        if not isinstance(t, ir.Stmt) or isinstance(t, ir.Carry):
             continue
         fusing = set()
         if isinstance(t, ir.Assign) and ir.op_name(t.op) in ("add", "sum", "subtract", "sub") and len(t.args) == 2:
@@ -209,9 +248,11 @@ def fusable_products(body) -> set[str]:
         elif isinstance(t, ir.Accum) and ir.op_name(t.op) in ("add", "sum") and t.base in (None, t.name):
             fusing = {t.value} if isinstance(t.value, str) else set()
         for n in _operand_reads(t):
-            if n in cands and n not in fusing:
-                bad.add(n)
-    return cands - bad
+            r = root(n)
+            if r in cands and n not in fusing:
+                bad.add(r)
+    ok = cands - bad
+    return ok | {n for n in alias if root(n) in ok}
 
 
 def _defined_names(t) -> list[str]:

@@ -38,13 +38,13 @@ from __future__ import annotations
 from dataclasses import dataclass
 
 from .. import ir
-from ..cgen import DEVICE_PRELUDE, Emitter, ctype, f32_lit, fusable_products, identity_of, lit_int
+from ..cgen import DEVICE_PRELUDE, Emitter, carry_slot, ctype, f32_lit, fusable_products, identity_of, lit_int
 from ..errors import UnsupportedIR
 from .common import KernelSource, LaunchPlan, ParamSpec, launch_record_source
 
 SUPPORTED = (ir.Tile, ir.Smem, ir.Sync, ir.WarpShuffle, ir.TreeHalve, ir.Load, ir.Write, ir.Assign,
              ir.Accum, ir.Init, ir.Let, ir.Loop, ir.StridedLoop, ir.Cond, ir.Select, ir.ZeroPrologue,
-             ir.CpAsyncCopy, ir.CpAsyncCommit, ir.CpAsyncWait)
+             ir.CpAsyncCopy, ir.CpAsyncCommit, ir.CpAsyncWait, ir.Pre, ir.Carry)
 COLLECTIVE = (ir.Sync, ir.TreeHalve, ir.WarpShuffle, ir.CpAsyncCopy, ir.CpAsyncCommit, ir.CpAsyncWait)
 STATIC_SMEM_MAX = 48 * 1024
 _SMEM_BYTES = {"f32": 4, "float": 4, "float32": 4, "i32": 4, "u32": 4, "s32": 4, "int": 4, "u64": 8,
@@ -64,11 +64,7 @@ def unsupported_nodes(kop: ir.KernelOp) -> list[str]:
 
 def match(kop: ir.KernelOp, shapes: dict, dtypes: dict) -> SchedPlan | None:
     top = ir.body_stmts(kop.body)
-    if not any(isinstance(s, ir.Tile) for s in top):
-        return None
-    if any(not isinstance(s, (ir.Tile, ir.ZeroPrologue, ir.Smem)) for s in top):
-        return None
-    if unsupported_nodes(kop):
+    if not top or unsupported_nodes(kop):
         return None
     smem, seen = [], set()
     for s in ir.walk(kop.body):
@@ -95,6 +91,12 @@ class SchedEmitter(Emitter):
         self.smem = smem or set()
         self.active = active
         self.counter = [0]
+        # Pre / Carry (compile.py:2860-2888): (carrier, slot) -> C variable of the
+        # Carry emitted last, and each carrier's seed; resolved in emission order
+        self.carry_vals: dict[tuple[str, str], str] = {}
+        self.carry_seed: dict[str, float] = {}
+        self.carry_var: dict[int, str] = {}
+        self.carry_prod: dict[str, tuple] = {}
 
     def _child(self) -> "SchedEmitter":
         # a child with the default hooks binds its own (its environment holds the loop variables)
@@ -107,6 +109,10 @@ class SchedEmitter(Emitter):
         c.ftype = self.ftype
         c.row_divisors = self.row_divisors
         c.counter = self.counter
+        c.carry_vals = self.carry_vals
+        c.carry_seed = self.carry_seed
+        c.carry_var = self.carry_var
+        c.carry_prod = self.carry_prod
         c.env = dict(self.env)
         return c
 
@@ -167,10 +173,45 @@ class SchedEmitter(Emitter):
         if isinstance(s, ir.ZeroPrologue):
             self._zero_prologue(s)
             return
+        if isinstance(s, ir.Carry):
+            self.carry_seed[s.name] = float(s.seed)
+            var = self._carry_decl(s)
+            self.emit(f"{var} = {self.as_f32(s.value)};")
+            self.carry_vals[(s.name, carry_slot(s.index))] = var
+            self.env[s.name] = ("f32", var)
+            # a carried plain product stays foldable into the add/sub that reads it back
+            prod = self.products.get(s.value) if isinstance(s.value, str) else None
+            if prod is not None:
+                self.carry_prod[var] = prod
+            else:
+                self.carry_prod.pop(var, None)
+            return
+        if isinstance(s, ir.Pre):
+            key = (s.carrier, carry_slot(s.index))
+            src = self.carry_vals.get(key) or self.carry_vals.get((s.carrier, "_"))
+            self.assign(s.name, "f32", src if src is not None else f32_lit(self.carry_seed.get(s.carrier, 0.0)))
+            if src is not None and src in self.carry_prod:
+                self.products[s.name] = self.carry_prod[src]
+            return
         super().stmt(s)
+
+    def _carry_decl(self, s) -> str:
+        """One function-scope variable per Carry statement (declared before any
+        enclosing loop or branch, so later Pre statements can read it)."""
+        if id(s) not in self.carry_var:
+            self.carry_var[id(s)] = self.declare(f"__carry{len(self.carry_var)}_{s.name}", "f32")
+        return self.carry_var[id(s)]
+
+    def _defines(self, s) -> list[tuple[str, str]]:
+        if isinstance(s, (ir.Pre, ir.Carry)):
+            return [(s.name, "f32")]
+        return super()._defines(s)
 
     def _predeclare(self, body) -> None:
         for t in ir.walk(body):
+            if isinstance(t, ir.Carry):
+                self._carry_decl(t)
+                continue
             for nm, kind in self._defines(t):
                 self.declare(nm, kind)
             if isinstance(t, (ir.WarpShuffle, ir.TreeHalve)):
@@ -352,15 +393,27 @@ def generate(kop: ir.KernelOp, plan: SchedPlan, shapes: dict, dtypes: dict, args
     fus = fusable_products(kop.body)
     launch_block = _launch_threads(meta)
     first_n = None
+    # statements outside any Tile run in every thread (compile.py:1077-1095); one scope for the kernel
+    top_em = SchedEmitter(shapes, dtypes, ptrs, indent="    ", smem=smem_names)
+    top_em.fusable = fus
+    top_em.env.update(base_env)
+    top_em._predeclare(tuple(t for t in ir.body_stmts(kop.body) if not isinstance(t, ir.Tile)))
+    loose: list = []
+
+    def flush_loose() -> None:
+        if loose:
+            top_em.run(tuple(loose))
+            loose.clear()
+        lines.extend(top_em.lines)
+        top_em.lines = []
+
     for ti, top in enumerate(ir.body_stmts(kop.body)):
         if isinstance(top, ir.Smem):
             continue
-        if isinstance(top, ir.ZeroPrologue):
-            em = SchedEmitter(shapes, dtypes, ptrs, indent="    ", smem=smem_names)
-            em.env.update(base_env)
-            em.stmt(top)
-            lines.extend(em.lines)
+        if not isinstance(top, ir.Tile):
+            loose.append(top)
             continue
+        flush_loose()
         tile = top
         extents = [a.size for a in tile.axes]
         n = 1
@@ -385,9 +438,10 @@ def generate(kop: ir.KernelOp, plan: SchedPlan, shapes: dict, dtypes: dict, args
         elif guard:
             w(f"        if ({gid} < {n}LL) {{")
             ind = "            "
-        em = SchedEmitter(shapes, dtypes, ptrs, indent=ind, smem=smem_names, active=active)
-        em.fusable = fus
-        em.env.update(base_env)
+        em = top_em._child()
+        em.declared = dict(top_em.declared)    # the tile's own scope
+        em.ind = ind
+        em.active = active
         if aux:
             em.env["_gid"] = ("int", gid)
         _bind_axes(em, tile, extents, gid)
@@ -396,12 +450,13 @@ def generate(kop: ir.KernelOp, plan: SchedPlan, shapes: dict, dtypes: dict, args
         if guard and not collective:
             w("        }")
         w("    }")
+    flush_loose()
     w("}")
     grid = tuple(int(x) for x in (meta.get("grid") or [])) or None
     block = tuple(int(x) for x in (meta.get("block") or [])) or None
     if block is None:
-        first_tile = next(s for s in ir.body_stmts(kop.body) if isinstance(s, ir.Tile))
-        block = (int(first_tile.block_threads or 128), 1, 1)
+        first_tile = next((s for s in ir.body_stmts(kop.body) if isinstance(s, ir.Tile)), None)
+        block = (int(first_tile.block_threads or 128) if first_tile is not None else 1, 1, 1)
     block = (tuple(block) + (1, 1))[:3]
     if grid is None:
         nthr = block[0] * block[1] * block[2]

@@ -43,7 +43,7 @@ sys.path.insert(0, str(HERE / "emmy_shim"))
 from emmy._core import (  # noqa: E402
     Accum, Assign, BinaryExpr, Builtin, CastExpr, Cond, FlatIndex, FuncCallExpr, Graph, Init, KernelOp,
     Let, Literal, Load, Loop, Select, Smem, StridedLoop, Sync, TernaryExpr, Tile, TreeHalve, Var, ZeroPrologue,
-    WarpShuffle, Write, CpAsyncCopy, CpAsyncCommit, CpAsyncWait,
+    WarpShuffle, Write, CpAsyncCopy, CpAsyncCommit, CpAsyncWait, Pre, Carry,
 )
 
 _LIB = None
@@ -440,8 +440,28 @@ class Cells:
                 defs[n] = defs.get(n, 0) + 1
         cands = {t.name for t in walk(body) if isinstance(t, Assign)
                  and opname(t.op) in ("multiply", "mul", "square", "log", "log_fast", "silu") and defs.get(t.name) == 1}
+        # Carry / Pre are plain moves the assembler sees through (compile.py:2868-2888)
+        alias: dict = {}
+        carried: dict = {}
+        for t in walk(body):
+            if isinstance(t, Carry) and isinstance(t.value, str):
+                carried[(t.name, _slot_of(t.index))] = t.value
+                alias[t.name] = t.value
+            elif isinstance(t, Pre):
+                src = carried.get((t.carrier, _slot_of(t.index))) or carried.get((t.carrier, "_"))
+                if src is not None:
+                    alias[t.name] = src
+
+        def root(n):
+            for _ in range(len(alias) + 1):
+                if n not in alias:
+                    break
+                n = alias[n]
+            return n
         bad = set()
         for t in walk(body):
+            if isinstance(t, Carry):
+                continue
             fusing: set = set()
             if isinstance(t, Assign) and opname(t.op) in ("add", "sum", "subtract", "sub") and len(t.args) == 2:
                 fusing = {a for a in t.args if isinstance(a, str)}
@@ -458,9 +478,11 @@ class Cells:
             elif isinstance(t, (Select, Load, Let, Cond)):
                 reads = sorted(t.deps())
             for n in reads:
-                if n in cands and n not in fusing:
-                    bad.add(n)
-        self.fusable = cands - bad
+                r = root(n) if isinstance(n, str) else n
+                if r in cands and n not in fusing:
+                    bad.add(r)
+        ok = cands - bad
+        self.fusable = ok | {n for n in alias if root(n) in ok}
 
     def product(self, name):
         """Factors of a plain product ptxas folds into the current add/sub
@@ -680,12 +702,15 @@ def _cells_for(axes, n_total):
 
 
 def evaluate(kop, shapes: dict, dtypes: dict, inputs: dict[str, np.ndarray],
-             outputs: dict[str, tuple[int, ...]]) -> dict[str, np.ndarray]:
+             outputs: dict[str, tuple[int, ...]], launch: dict | None = None) -> dict[str, np.ndarray]:
     """Run ``kop`` on float32 ``inputs`` (bf16 inputs passed as their f32 values);
-    returns float32 outputs (bf16/f16 outputs rounded as the store would)."""
+    returns float32 outputs (bf16/f16 outputs rounded as the store would).
+    ``launch`` (meta ``grid``/``block``) sizes schedules whose threads do not
+    all come from one Tile."""
     body = list(kop.body)
-    if any(isinstance(t, (CpAsyncCopy, CpAsyncCommit, CpAsyncWait)) for t in ir_walk(body)):
-        return _eval_simt(kop, shapes, dtypes, inputs, outputs)
+    if (any(isinstance(t, (CpAsyncCopy, CpAsyncCommit, CpAsyncWait, Pre, Carry)) for t in ir_walk(body))
+            or not all(isinstance(t, Tile) for t in body)):
+        return _eval_simt(kop, shapes, dtypes, inputs, outputs, launch)
     assert len(body) == 1 and isinstance(body[0], Tile), "oracle: one Tile per KernelOp"
     tile = body[0]
     stmts = list(tile.body)
@@ -809,6 +834,19 @@ class Simt(Cells):
                         if s.inner is not None else 0)
                 self.bind(st, "f32", np.broadcast_to(self.bufs[buf][root], (self.n,)).astype(F32))
             return
+        if isinstance(s, Carry):
+            v = np.broadcast_to(self.f32(s.value), (self.n,)).astype(F32)
+            prod = self.products.get(s.value) if isinstance(s.value, str) else None
+            self.carry_store[id(s)] = (v, prod)
+            self.bind(s.name, "f32", v)
+            return
+        if isinstance(s, Pre):
+            src, seed = self.carry_src.get(id(s), (None, 0.0))
+            got = self.carry_store.get(src) if src is not None else None
+            self.bind(s.name, "f32", got[0] if got is not None else np.full(self.n, F32(seed)))
+            if got is not None and got[1] is not None:
+                self.products[s.name] = got[1]    # a carried product stays foldable
+            return
         if isinstance(s, CpAsyncCopy):
             # cp.async.ca|cg of nbytes (compile.py:2288-2319): f32 elements, contiguous
             dst, src = self.bufs[s.smem], self.bufs[s.src]
@@ -825,8 +863,42 @@ class Simt(Cells):
         super().stmt(s)
 
 
-def _eval_simt(kop, shapes: dict, dtypes: dict, inputs: dict, outputs: dict, block: int | None = None):
-    """Block-by-block lockstep evaluation of a block-cooperative KernelOp."""
+def _slot_of(index) -> str:
+    """Carry slot of an index: a single literal index names its slot, else the wildcard (compile.py:2860-2866)."""
+    if not index:
+        return "0"
+    if len(index) == 1 and isinstance(index[0], Literal) and isinstance(index[0].value, int):
+        return str(index[0].value)
+    return "_"
+
+
+def _carry_sources(body) -> dict[int, tuple[int | None, float]]:
+    """For every Pre, the Carry it reads and the seed it falls back to, as the
+    reference resolves them while it emits code (compile.py:2860-2888): in
+    program order, each loop body once, both branches of a Cond in turn."""
+    vals: dict[tuple[str, str], int] = {}
+    seeds: dict[str, float] = {}
+    out: dict[int, tuple[int | None, float]] = {}
+
+    def visit(stmts) -> None:
+        for t in stmts:
+            if isinstance(t, Carry):
+                seeds[t.name] = float(t.seed)
+                vals[(t.name, _slot_of(t.index))] = id(t)
+            elif isinstance(t, Pre):
+                key = (t.carrier, _slot_of(t.index))
+                src = vals.get(key, vals.get((t.carrier, "_")))
+                out[id(t)] = (src, seeds.get(t.carrier, 0.0))
+            for child in (t.nested() if hasattr(t, "nested") else ()):
+                visit(list(child))
+    visit(list(body))
+    return out
+
+
+def _eval_simt(kop, shapes: dict, dtypes: dict, inputs: dict, outputs: dict, launch: dict | None = None):
+    """Block-by-block lockstep evaluation of a block-cooperative KernelOp.
+    Statements outside any Tile run in every thread of the meta launch."""
+    launch = launch or {}
     bufs = {k: np.ascontiguousarray(v, F32).reshape(-1).copy() for k, v in inputs.items()}
     for name, shp in outputs.items():
         bufs[name] = np.zeros(int(np.prod(shp)) if shp else 1, F32)
@@ -836,33 +908,54 @@ def _eval_simt(kop, shapes: dict, dtypes: dict, inputs: dict, outputs: dict, blo
         if isinstance(t, Smem):
             smem[t.name] = tuple(int(x) for x in t.extents)
             shapes[t.name] = smem[t.name]
-    for top in kop.body:
-        if isinstance(top, ZeroPrologue):
-            bufs[top.dst].view(np.uint32)[:int(top.words)] = 0
-            continue
-        if isinstance(top, Smem):
-            continue
-        tile = top
-        axes = _axes(tile)
-        n_cells = int(np.prod([e for _, e in axes])) if axes else 1
-        bt = int(tile.block_threads or block or 128)
-        nblocks = max(1, -(-n_cells // bt))
-        strides = row_major([e for _, e in axes])
+    carry_src = _carry_sources(list(kop.body))
+    top = [t for t in kop.body if not isinstance(t, Smem)]
+    tiles = [t for t in top if isinstance(t, Tile)]
+    mblock = int(np.prod(launch.get("block") or [1])) if launch.get("block") else None
+    mgrid = int(np.prod(launch.get("grid") or [1])) if launch.get("grid") else None
+
+    def block_of(tile) -> int:
+        return int(tile.block_threads or mblock or 128)
+
+    if not tiles or any(not isinstance(t, Tile) for t in top):
+        # one pass over the meta launch, every statement in order in every thread
+        bt = mblock or (block_of(tiles[0]) if tiles else 1)
+        nblocks = mgrid or max(1, -(-int(np.prod([a for _, a in _axes(tiles[0])])) // bt)) if tiles else (mgrid or 1)
+        groups = [(bt, nblocks, top)]
+    else:
+        groups = []
+        for tile in tiles:
+            bt = block_of(tile)
+            n_cells = int(np.prod([e for _, e in _axes(tile)])) if tile.axes else 1
+            groups.append((bt, mgrid or max(1, -(-n_cells // bt)), [tile]))
+    for bt, nblocks, stmts in groups:
         for b in range(nblocks):
             for name, shp in smem.items():
                 bufs[name] = np.zeros(int(np.prod(shp)), F32)
             m = Simt(bt, bufs, shapes, dtypes)
+            m.carry_src, m.carry_store = carry_src, {}
             tid = np.arange(bt, dtype=np.int64)
             gid = b * bt + tid
             m.env.update({"_tid": ("int", tid), "_gid": ("int", gid), "lane": ("int", tid & 31),
                           "warp": ("int", tid >> 5), "threadIdx.x": ("int", tid),
                           "blockIdx.x": ("int", np.full(bt, b, np.int64)), "blockDim.x": ("int", np.int64(bt))})
-            for i, ((name, e), st) in enumerate(zip(axes, strides)):
-                term = gid // st
-                m.env[name] = ("int", term if i == 0 else term % e)
-            if n_cells % bt:
-                m.mask = gid < n_cells
-            m.run(list(tile.body))
+            for t in stmts:
+                if not isinstance(t, Tile):
+                    if isinstance(t, ZeroPrologue):
+                        if b == 0:
+                            bufs[t.dst].view(np.uint32)[:int(t.words)] = 0
+                        continue
+                    m.mask = None
+                    m.stmt(t)
+                    continue
+                axes = _axes(t)
+                n_cells = int(np.prod([e for _, e in axes])) if axes else 1
+                for i, ((name, e), st) in enumerate(zip(axes, row_major([e for _, e in axes]))):
+                    term = gid // st
+                    m.env[name] = ("int", term if i == 0 else term % e)
+                m.mask = (gid < n_cells) if (n_cells % bt or nblocks * bt != n_cells) else None
+                m.run(list(t.body))
+                m.mask = None
     return {k: bufs[k].reshape(outputs[k]) if outputs[k] else bufs[k][:1] for k in outputs}
 
 
@@ -1100,7 +1193,7 @@ def run_case(case_dir: Path, inputs: dict[str, np.ndarray] | None = None) -> tup
     if inputs is None:
         inputs = make_inputs(mk, shapes, dtypes)
     outs = {a["name"]: tuple(a["shape"]) for a in mk["args"] if a.get("output")}
-    res = evaluate(kop, shapes, dtypes, inputs, outs)
+    res = evaluate(kop, shapes, dtypes, inputs, outs, {"grid": mk.get("grid"), "block": mk.get("block")})
     return res, inputs
 
 

@@ -56,8 +56,9 @@ from emmy.compiler.ir.expr import BinaryExpr, Literal, Var  # noqa: E402
 from emmy.compiler.ir.kernel.ir import (  # noqa: E402
     Axis, CpAsyncCommit, CpAsyncCopy, CpAsyncWait, DataType, Smem, Sync, Tile, TreeHalve, WarpShuffle,
 )
+from emmy.compiler.ir.expr import FlatIndex  # noqa: E402
 from emmy.compiler.ir.stmt import (  # noqa: E402
-    Accum, Assign, Cond, Init, Let, Load, Loop, StridedLoop, Write, ZeroPrologue,
+    Accum, Assign, Carry, Cond, Init, Let, Load, Loop, Pre, StridedLoop, Write, ZeroPrologue,
 )
 from emmy.compiler.ir.stmt.leaves import Select, SelectBranch  # noqa: E402
 
@@ -657,6 +658,54 @@ def cpasync_matmul_case(cid: str, m: int, k: int, n: int, *, wide: bool = False)
     return Case(cid, entry, graph, kern, family="schedule", check={"kind": "ulp", "ulp": 0})
 
 
+def pre_carry_case(cid: str, n: int) -> Case:
+    """Values carried between statements by Carry and read back by Pre
+    (compile.py:2860-2888): two slots of one carrier, and a carrier with no
+    Carry that falls back to its seed (0)."""
+    entry = "k_pre_carry"
+    lit = lambda v: Literal(v, "int")  # noqa: E731
+    body = Tile(axes=(Axis("a0", Dim(n)),), body=(
+        Load(names=("v0",), input="x", index=(Var("a0"),), dtype=F32),
+        Carry("c", "v0", (lit(0),), 0.0, F32),
+        Assign("v1", EW("multiply"), ("v0", "v0"), F32),
+        Carry("c", "v1", (lit(1),), 0.0, F32),
+        Pre("p0", "c", (lit(0),)),
+        Pre("p1", "c", (lit(1),)),
+        Pre("p2", "d", (lit(0),)),
+        Assign("s", EW("subtract"), ("p1", "p0"), F32),
+        Assign("t", EW("add"), ("s", "p2"), F32),
+        Write(output="y", index=(Var("a0"),), values=("t",), value_dtype=F32),
+    ))
+    graph = {"inputs": ["x"], "outputs": ["y"], "nodes": {
+        "x": _input("x", [n]), "y": _kernel(entry, body, ["x"], [("y", [n], "f32")])}}
+    grid, block = _launch(n)
+    kern = _meta_kernel("y", entry, ["x", "y"], grid, block, [
+        _arg("x", [n], init=NORM(), seed=0), _arg("y", [n], output=True)])
+    return Case(cid, entry, graph, kern, family="schedule", check={"kind": "ulp", "ulp": 0})
+
+
+def loose_statements_case(cid: str) -> Case:
+    """Statements with no Tile around them, run by every thread of the launch:
+    the kernel zeroes its output (ZeroPrologue), then every thread writes
+    x[0] to out[0] through a FlatIndex Let, a Carry and a Pre (the node mix
+    of the reference's tests/test_extra_isa.py:66-84)."""
+    entry = "k_loose_nodes"
+    lit = lambda v: Literal(v, "int")  # noqa: E731
+    body = (
+        ZeroPrologue("out", 32),
+        Let("off", FlatIndex("x", (lit(0),)), "i32"),
+        Load(names=("in0",), input="x", index=(Var("off"),), dtype=F32),
+        Carry("st", "in0", (lit(0),), 0.0, F32),
+        Pre("old", "st", (lit(0),)),
+        Write(output="out", index=(lit(0),), values=("old",), value_dtype=F32),
+    )
+    graph = {"inputs": ["x"], "outputs": ["out"], "nodes": {
+        "x": _input("x", [32]), "out": _kernel(entry, body, ["x"], [("out", [32], "f32")])}}
+    kern = _meta_kernel("out", entry, ["x", "out"], [1, 1, 1], [32, 1, 1], [
+        _arg("x", [32], init=NORM(), seed=0), _arg("out", [32], output=True)])
+    return Case(cid, entry, graph, kern, family="schedule", check={"kind": "ulp", "ulp": 0})
+
+
 # ------------------------------------------------------------ reference op catalog
 
 
@@ -981,6 +1030,8 @@ def all_cases() -> list[Case]:
     # Emmy's cp.async shared-memory matmul schedule (the schedule family)
     cases.append(cpasync_matmul_case("s_cpasync_matmul_64x48x80", 64, 48, 80))
     cases.append(cpasync_matmul_case("s_cpasync16_matmul_32x64x48", 32, 64, 48, wide=True))
+    cases.append(pre_carry_case("s_pre_carry_500", 500))
+    cases.append(loose_statements_case("s_loose_nodes_32"))
     return cases
 
 
