@@ -308,6 +308,7 @@ class Emitter:
         self.ind = indent
         self.load_hook = load_hook or self._default_load
         self.write_hook = write_hook or self._default_write
+        self._hooks_given = (load_hook, write_hook)
         self.tmp = 0
         self.declared: dict[str, str] = {}
         # plain products (name -> (a, b) factor codes, definition order) and the
@@ -699,8 +700,9 @@ class Emitter:
             raise UnsupportedIR(f"unsupported stmt {type(s).__name__}")
 
     def _child(self) -> "Emitter":
-        c = Emitter(self.shapes, self.dtypes, self.ptrs, self.load_hook, self.write_hook,
-                    self.ind + "    ")
+        # custom hooks are shared; default ones are the child's own (its environment
+        # holds the names a branch defines)
+        c = Emitter(self.shapes, self.dtypes, self.ptrs, *self._hooks_given, self.ind + "    ")
         c.declared = self.declared
         c.tmp = self.tmp + 1000
         c.fusable = self.fusable

@@ -55,7 +55,9 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
 
     ``options`` selects among equivalent schedules (results do not depend on
     it): ``{"gemm_variant": "auto" | "pair" | "single",
-    "pointwise_pair": "auto" | True | False}``."""
+    "pointwise_pair": "auto" | True | False, "family": "schedule"}``; the
+    last skips the fast families.  A KernelOp no fast family takes (or one a
+    family recognises but cannot specialise) keeps its own schedule."""
     meta = meta or {}
     options = options or {}
     written = {s.output for s in ir.walk(kop.body) if isinstance(s, ir.Write)}
@@ -70,28 +72,31 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
                                 f"(unsupported nodes: {', '.join(schedule.unsupported_nodes(kop)) or 'layout'})")
         ks = schedule.generate(kop, plan, shapes, dtypes, args, scalars, written, meta)
         return Lowered(ks, args, shapes, dtypes, meta)
-    plan = attention.match(kop, shapes, dtypes)
-    if plan is not None:
-        ks = attention.generate(kop, plan, shapes, dtypes, args, scalars, written)
-        return Lowered(ks, args, shapes, dtypes, meta)
-    plan = gemm.match(kop, shapes, dtypes)
-    if plan is not None:
-        ks = gemm.generate(kop, plan, shapes, dtypes, args, scalars, written,
-                           variant=options.get("gemm_variant", "auto"))
-        return Lowered(ks, args, shapes, dtypes, meta)
-    plan = reduction.match(kop, shapes, dtypes)
-    if plan is not None:
-        ks = reduction.generate(kop, plan, shapes, dtypes, args, scalars, written)
-        return Lowered(ks, args, shapes, dtypes, meta)
-    plan = rownorm.match(kop, shapes, dtypes)
-    if plan is not None:
-        ks = rownorm.generate(kop, plan, shapes, dtypes, args, scalars, written)
-        return Lowered(ks, args, shapes, dtypes, meta)
-    plan = pointwise.match(kop)
-    if plan is not None:
-        ks = pointwise.generate(kop, plan, shapes, dtypes, args, scalars, written,
-                                pair=options.get("pointwise_pair", "auto"))
-        return Lowered(ks, args, shapes, dtypes, meta)
+    fast = (
+        ("attention", lambda: attention.match(kop, shapes, dtypes),
+         lambda pl: attention.generate(kop, pl, shapes, dtypes, args, scalars, written)),
+        ("gemm", lambda: gemm.match(kop, shapes, dtypes),
+         lambda pl: gemm.generate(kop, pl, shapes, dtypes, args, scalars, written,
+                                  variant=options.get("gemm_variant", "auto"))),
+        ("reduction", lambda: reduction.match(kop, shapes, dtypes),
+         lambda pl: reduction.generate(kop, pl, shapes, dtypes, args, scalars, written)),
+        ("rownorm", lambda: rownorm.match(kop, shapes, dtypes),
+         lambda pl: rownorm.generate(kop, pl, shapes, dtypes, args, scalars, written)),
+        ("pointwise", lambda: pointwise.match(kop),
+         lambda pl: pointwise.generate(kop, pl, shapes, dtypes, args, scalars, written,
+                                       pair=options.get("pointwise_pair", "auto"))),
+    )
+    rejected: list[str] = []
+    for fam, match, generate in fast:
+        try:
+            plan = match()
+            if plan is None:
+                continue
+            return Lowered(generate(plan), args, shapes, dtypes, meta)
+        except UnsupportedIR as exc:
+            # a family that recognised the shape but cannot specialise it (dtype,
+            # head size, memory access pattern ...): the schedule family takes it
+            rejected.append(f"{fam}: {exc}")
     # no recognised computation: keep the schedule the IR spells out
     plan = schedule.match(kop, shapes, dtypes)
     if plan is not None:
@@ -100,7 +105,8 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
     bad = schedule.unsupported_nodes(kop)
     kinds = sorted({type(s).__name__ for s in ir.walk(kop.body)})
     raise UnsupportedIR(f"KernelOp {kop.name!r} has nodes no sm_100a lowering supports "
-                        f"({', '.join(bad) or 'layout'}; nodes: {', '.join(kinds)})")
+                        f"({', '.join(bad) or 'layout'}; nodes: {', '.join(kinds)})"
+                        + (f"; {'; '.join(rejected)}" if rejected else ""))
 
 
 class Compiler:

@@ -658,6 +658,31 @@ def cpasync_matmul_case(cid: str, m: int, k: int, n: int, *, wide: bool = False)
     return Case(cid, entry, graph, kern, family="schedule", check={"kind": "ulp", "ulp": 0})
 
 
+def cond_load_case(cid: str, n: int) -> Case:
+    """A load inside a Cond whose index is a name the branch defines:
+    y[i] = x[i] + x[i + n/2] for the first half, x[i]^2 for the rest."""
+    entry = "k_cond_load"
+    half = n // 2
+    body = Tile(axes=(Axis("a0", Dim(n)),), body=(
+        Load(names=("v",), input="x", index=(Var("a0"),), dtype=F32),
+        Init("r", 0.0, dtype=F32),
+        Cond(BinaryExpr("<", Var("a0"), Literal(half, "int")), body=(
+            Let("k", BinaryExpr("+", Var("a0"), Literal(half, "int")), "i32"),
+            Load(names=("w",), input="x", index=(Var("k"),), dtype=F32),
+            Assign("r", EW("add"), ("v", "w"), F32),
+        ), else_body=(
+            Assign("r", EW("multiply"), ("v", "v"), F32),
+        )),
+        Write(output="y", index=(Var("a0"),), values=("r",), value_dtype=F32),
+    ))
+    graph = {"inputs": ["x"], "outputs": ["y"], "nodes": {
+        "x": _input("x", [n]), "y": _kernel(entry, body, ["x"], [("y", [n], "f32")])}}
+    grid, block = _launch(n)
+    kern = _meta_kernel("y", entry, ["x", "y"], grid, block, [
+        _arg("x", [n], init=NORM(), seed=0), _arg("y", [n], output=True)])
+    return Case(cid, entry, graph, kern, family="pointwise", check={"kind": "ulp", "ulp": 0})
+
+
 def pre_carry_case(cid: str, n: int) -> Case:
     """Values carried between statements by Carry and read back by Pre
     (compile.py:2860-2888): two slots of one carrier, and a carrier with no
@@ -1031,6 +1056,7 @@ def all_cases() -> list[Case]:
     cases.append(cpasync_matmul_case("s_cpasync_matmul_64x48x80", 64, 48, 80))
     cases.append(cpasync_matmul_case("s_cpasync16_matmul_32x64x48", 32, 64, 48, wide=True))
     cases.append(pre_carry_case("s_pre_carry_500", 500))
+    cases.append(cond_load_case("p_cond_load_300", 300))
     cases.append(loose_statements_case("s_loose_nodes_32"))
     return cases
 
