@@ -68,6 +68,7 @@ struct Driver {
     EMMY_DRV(cuMemFree)
     EMMY_DRV(cuMemAllocHost)
     EMMY_DRV(cuMemFreeHost)
+    EMMY_DRV(cuMemHostGetDevicePointer)
     EMMY_DRV(cuMemcpyHtoD)
     EMMY_DRV(cuMemcpyDtoH)
     EMMY_DRV(cuMemcpyHtoDAsync)
@@ -141,6 +142,7 @@ int load_driver() {
     EMMY_GET(cuMemFree, true)
     EMMY_GET(cuMemAllocHost, true)
     EMMY_GET(cuMemFreeHost, true)
+    EMMY_GET(cuMemHostGetDevicePointer, false)
     EMMY_GET(cuMemcpyHtoD, true)
     EMMY_GET(cuMemcpyDtoH, true)
     EMMY_GET(cuMemcpyHtoDAsync, true)
@@ -212,6 +214,10 @@ struct emmy_module {
     CUstream h2d = nullptr, d2h = nullptr;
     std::vector<CUevent> ev_in, ev_out;
     CUevent ev_whole = nullptr, ev_start = nullptr;
+    // emmy_run_host small-payload path: pinned host memory the kernel reads and writes directly
+    void *zc_host = nullptr;
+    CUdeviceptr zc_dev = 0;
+    size_t zc_bytes = 0;
 };
 
 namespace {
@@ -502,6 +508,7 @@ int emmy_unload(emmy_module_t m) {
     if (m->ev_start) g_drv.cuEventDestroy(m->ev_start);
     if (m->h2d) g_drv.cuStreamDestroy(m->h2d);
     if (m->d2h) g_drv.cuStreamDestroy(m->d2h);
+    if (m->zc_host) g_drv.cuMemFreeHost(m->zc_host);
     CUresult r = g_drv.cuModuleUnload(m->mod);
     delete m;
     if (r != CUDA_SUCCESS) return cu_fail(r, "cuModuleUnload");
@@ -736,6 +743,70 @@ int run_pipeline(emmy_module *m, void *const *host_ptrs, const size_t *bytes, co
 
 extern "C" {
 
+namespace {
+
+constexpr size_t kMappedMaxBytes = 64 * 1024;
+constexpr size_t kMappedAlign = 256;
+
+// Problems of at most 64 KiB in all go through pinned host memory that the
+// kernel reads and writes over PCIe itself: no copy engine round trips, which
+// dominate at these sizes.  Only for families whose kernels touch their
+// parameters with plain loads and stores (pointwise, row-fused): no atomics,
+// tensor maps or async copies on host memory.
+bool mapped_path_ok(const emmy_module *m, const size_t *bytes, const uint8_t *roles, int nargs) {
+    if (!m->has_rec || m->rec.ntmaps != 0 || !g_drv.cuMemHostGetDevicePointer) return false;
+    if (m->rec.family != EMMY_FAMILY_POINTWISE && m->rec.family != EMMY_FAMILY_ROWFUSED) return false;
+    size_t total = 0;
+    for (int i = 0; i < nargs; ++i) {
+        if (roles[i] == EMMY_ROLE_SCALAR) continue;
+        total = (total + kMappedAlign - 1) / kMappedAlign * kMappedAlign + bytes[i];
+        if (total > kMappedMaxBytes) return false;
+    }
+    return nargs <= 64;
+}
+
+int run_host_mapped(emmy_module *m, void *const *host_ptrs, const size_t *bytes, const uint8_t *roles, int nargs,
+                    uint64_t stream) {
+    if (!m->zc_host) {
+        CU(g_drv.cuMemAllocHost(&m->zc_host, kMappedMaxBytes), "cuMemAllocHost (run_host small path)");
+        CUresult r = g_drv.cuMemHostGetDevicePointer(&m->zc_dev, m->zc_host, 0);
+        if (r != CUDA_SUCCESS) {
+            g_drv.cuMemFreeHost(m->zc_host);
+            m->zc_host = nullptr;
+            return cu_fail(r, "cuMemHostGetDevicePointer");
+        }
+        m->zc_bytes = kMappedMaxBytes;
+    }
+    uint64_t args[64];
+    size_t offs[64];
+    size_t off = 0;
+    char *base = static_cast<char *>(m->zc_host);
+    for (int i = 0; i < nargs; ++i) {
+        if (roles[i] == EMMY_ROLE_SCALAR) {
+            uint32_t v = 0;
+            std::memcpy(&v, host_ptrs[i], 4);
+            args[i] = v;
+            continue;
+        }
+        off = (off + kMappedAlign - 1) / kMappedAlign * kMappedAlign;
+        offs[i] = off;
+        if (is_in(roles[i]))
+            std::memcpy(base + off, host_ptrs[i], bytes[i]);
+        else if (roles[i] == EMMY_ROLE_OUT_ZEROED)
+            std::memset(base + off, 0, bytes[i]);
+        args[i] = m->zc_dev + off;
+        off += bytes[i];
+    }
+    int rc = launch_locked(m, args, nargs, nullptr, nullptr, stream);
+    if (rc) return rc;
+    CU(g_drv.cuStreamSynchronize(reinterpret_cast<CUstream>(stream)), "cuStreamSynchronize");
+    for (int i = 0; i < nargs; ++i)
+        if (roles[i] != EMMY_ROLE_SCALAR && is_out(roles[i])) std::memcpy(host_ptrs[i], base + offs[i], bytes[i]);
+    return EMMY_OK;
+}
+
+}  // namespace
+
 int emmy_run_host(emmy_module_t m, void *const *host_ptrs, const size_t *bytes, const uint8_t *roles,
                   int nargs, uint64_t stream) {
     if (!m || (nargs > 0 && (!host_ptrs || !bytes || !roles)))
@@ -743,6 +814,7 @@ int emmy_run_host(emmy_module_t m, void *const *host_ptrs, const size_t *bytes, 
     std::lock_guard<std::mutex> lk(g_mu);
     int rc = set_device(m->dev);
     if (rc) return rc;
+    if (mapped_path_ok(m, bytes, roles, nargs)) return run_host_mapped(m, host_ptrs, bytes, roles, nargs, stream);
     CUstream s = reinterpret_cast<CUstream>(stream);
     if (static_cast<int>(m->dbuf.size()) < nargs) {
         m->dbuf.resize(nargs, 0);

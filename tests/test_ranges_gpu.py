@@ -122,3 +122,45 @@ def test_pipelined_host_path_matches_device_launch(cid, cuda_device):
                 f"{cid}.{n}: pipelined host path differs from the device launch"
     assert case.module.status() == 0
     case.module.close()
+
+
+@pytest.mark.parametrize("cid,pinned", [
+    ("c1_add_64", True),            # pointwise, 768 B: pinned host memory the kernel reads directly
+    ("c1_add_64", False),           # same path from pageable buffers
+    ("c2_gelu_3x7", True),
+    ("f_softmax_33x130", True),     # row-fused, 34 KB
+    ("c4_sum_1000", True),          # reduction: copy-engine path whatever the size
+    ("c2_gelu_64x1000", False),     # 512 KB: above the small-payload bound
+])
+def test_small_host_path_matches_device_launch(cid, pinned, cuda_device):
+    """``emmy_run_host`` on small problems returns exactly the outputs of a
+    device launch, for every path it picks (and again on a second call)."""
+    import torch
+    from emmy_ptx_compiler_b200 import runtime
+    from emmy_ptx_compiler_b200 import harness
+    case = harness.DeviceCase(CASES / cid, cuda_device)
+    bufs = _device_inputs(case, cuda_device)
+    case.launch(bufs)
+    torch.cuda.synchronize(cuda_device)
+    zeroed = set(case.spec.meta.get("kernels", [{}])[0].get("zero_outputs", []))
+    host, ptrs, nbytes, roles = {}, [], [], []
+    for n in case.spec.arg_order:
+        t = bufs[n]
+        h = torch.empty(t.shape, dtype=t.dtype, pin_memory=pinned)
+        if n in case.spec.outputs:
+            h.fill_(7)
+            roles.append(runtime.EMMY_ROLE_OUT_ZEROED if n in zeroed else runtime.EMMY_ROLE_OUT)
+        else:
+            h.copy_(t)
+            roles.append(runtime.EMMY_ROLE_IN)
+        host[n] = h
+        ptrs.append(h.data_ptr())
+        nbytes.append(h.numel() * h.element_size())
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    for _ in range(2):
+        case.module.run_host(ptrs, nbytes, roles, stream=stream)
+        for n in case.spec.outputs:
+            assert torch.equal(host[n].view(torch.uint8), bufs[n].cpu().view(torch.uint8)), \
+                f"{cid}.{n}: host path differs from the device launch"
+    assert case.module.status() == 0
+    case.module.close()
