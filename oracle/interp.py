@@ -708,8 +708,12 @@ def evaluate(kop, shapes: dict, dtypes: dict, inputs: dict[str, np.ndarray],
     ``launch`` (meta ``grid``/``block``) sizes schedules whose threads do not
     all come from one Tile."""
     body = list(kop.body)
-    if (any(isinstance(t, (CpAsyncCopy, CpAsyncCommit, CpAsyncWait, Pre, Carry)) for t in ir_walk(body))
-            or not all(isinstance(t, Tile) for t in body)):
+    nodes = list(ir_walk(body))
+    if (any(isinstance(t, (CpAsyncCopy, CpAsyncCommit, CpAsyncWait, Pre, Carry)) for t in nodes)
+            or not all(isinstance(t, Tile) for t in body)
+            or (any(isinstance(t, Smem) for t in nodes)
+                and not any(isinstance(t, (WarpShuffle, TreeHalve)) for t in nodes))
+            or any(getattr(t, "aux_threads", 0) or getattr(t, "raster_group", None) for t in body)):
         return _eval_simt(kop, shapes, dtypes, inputs, outputs, launch)
     assert len(body) == 1 and isinstance(body[0], Tile), "oracle: one Tile per KernelOp"
     tile = body[0]

@@ -658,6 +658,83 @@ def cpasync_matmul_case(cid: str, m: int, k: int, n: int, *, wide: bool = False)
     return Case(cid, entry, graph, kern, family="schedule", check={"kind": "ulp", "ulp": 0})
 
 
+def raster_matmul_case(cid: str, m: int, k: int, n: int, group: int) -> Case:
+    """The naive f32 matmul with a raster group on its Tile (compile.py:1563-1609):
+    threads walk the (i, j) cells in groups of ``group`` rows."""
+    entry = "k_matmul_raster"
+    body = Tile(axes=(Axis("i", Dim(m)), Axis("j", Dim(n))), body=(
+        Init("acc0", 0.0, dtype=F32),
+        Loop(axis=Axis("kk", Dim(k)), body=(
+            Load(names=("a",), input="A", index=(Var("i"), Var("kk")), dtype=F32),
+            Load(names=("b",), input="B", index=(Var("kk"), Var("j")), dtype=F32),
+            Assign("p", EW("multiply"), ("a", "b"), F32),
+            Accum("acc0", "p", EW("add"), F32, axes=("kk",)),
+        )),
+        Write(output="C", index=(Var("i"), Var("j")), values=("acc0",), value_dtype=F32),
+    ), raster_group=group, raster_axes=("i", "j"), raster_orient="m")
+    graph = {"inputs": ["A", "B"], "outputs": ["C"], "nodes": {
+        "A": _input("A", [m, k]), "B": _input("B", [k, n]),
+        "C": _kernel(entry, body, ["A", "B"], [("C", [m, n], "f32")])}}
+    grid, block = _launch(m * n)
+    kern = _meta_kernel("C", entry, ["A", "B", "C"], grid, block, [
+        _arg("A", [m, k], init=NORM(), seed=0), _arg("B", [k, n], init=NORM(), seed=1),
+        _arg("C", [m, n], output=True)])
+    return Case(cid, entry, graph, kern, family="gemm", check={"kind": "rtol", "rtol": 1e-5, "atol": 1e-5,
+                                                                "exact_outputs": ["C"]})
+
+
+def aux_threads_case(cid: str, n: int) -> Case:
+    """A pointwise add whose Tile has 32 auxiliary threads per 128-thread
+    block (compile.py:1528-1537).  The launch has 160 threads per block, as a
+    32 x 5 block: the reference takes ``.reqntid`` from a multi-dimensional
+    meta block, else from ``block_threads`` (compile.py:901-911).  The extra
+    threads repeat cells of their block."""
+    entry = "k_add_aux"
+    body = Tile(axes=(Axis("a0", Dim(n)),), body=(
+        Load(names=("u",), input="a", index=(Var("a0"),), dtype=F32),
+        Load(names=("v",), input="b", index=(Var("a0"),), dtype=F32),
+        Assign("w", EW("add"), ("u", "v"), F32),
+        Write(output="c", index=(Var("a0"),), values=("w",), value_dtype=F32),
+    ), block_threads=128, aux_threads=32)
+    graph = {"inputs": ["a", "b"], "outputs": ["c"], "nodes": {
+        "a": _input("a", [n]), "b": _input("b", [n]),
+        "c": _kernel(entry, body, ["a", "b"], [("c", [n], "f32")])}}
+    kern = _meta_kernel("c", entry, ["a", "b", "c"], [math.ceil(n / 128), 1, 1], [32, 5, 1], [
+        _arg("a", [n], init=NORM(), seed=0), _arg("b", [n], init=NORM(), seed=1), _arg("c", [n], output=True)])
+    return Case(cid, entry, graph, kern, family="schedule", check={"kind": "ulp", "ulp": 0})
+
+
+def big_smem_case(cid: str, blocks: int, per_block: int) -> Case:
+    """Each 256-thread block stages its slice of x in one shared buffer larger
+    than 48 KiB (dynamic shared memory), then writes the slice reversed.  The
+    reference's PTX for it is not produced: its runner-style launch here passes
+    no dynamic shared memory, which such a kernel needs."""
+    entry = "k_reverse_slices"
+    t = 256
+    lit = lambda v: Literal(v, "int")  # noqa: E731
+    gidx = lambda e: BinaryExpr("+", BinaryExpr("*", Var("blk"), lit(per_block)), e)  # noqa: E731
+    body = Tile(axes=(Axis("blk", Dim(blocks)), Axis("t", Dim(t))), body=(
+        Smem("buf", (per_block,), "float", 16),
+        StridedLoop(axis=Axis("e", Dim(per_block)), start=Var("t"), step=lit(t), body=(
+            Load(names=("v",), input="x", index=(gidx(Var("e")),), dtype=F32),
+            Write(output="buf", index=(Var("e"),), values=("v",), value_dtype=F32),
+        )),
+        Sync(),
+        StridedLoop(axis=Axis("e2", Dim(per_block)), start=Var("t"), step=lit(t), body=(
+            Load(names=("w",), input="buf",
+                 index=(BinaryExpr("-", lit(per_block - 1), Var("e2")),), dtype=F32),
+            Write(output="y", index=(gidx(Var("e2")),), values=("w",), value_dtype=F32),
+        )),
+    ), block_threads=t)
+    n = blocks * per_block
+    graph = {"inputs": ["x"], "outputs": ["y"], "nodes": {
+        "x": _input("x", [n]), "y": _kernel(entry, body, ["x"], [("y", [n], "f32")])}}
+    kern = _meta_kernel("y", entry, ["x", "y"], [blocks, 1, 1], [t, 1, 1], [
+        _arg("x", [n], init=NORM(), seed=0), _arg("y", [n], output=True)])
+    kern["smem_bytes"] = per_block * 4
+    return Case(cid, entry, graph, kern, family="schedule", check={"kind": "exact"}, ref=False)
+
+
 def cond_load_case(cid: str, n: int) -> Case:
     """A load inside a Cond whose index is a name the branch defines:
     y[i] = x[i] + x[i + n/2] for the first half, x[i]^2 for the rest."""
@@ -1057,6 +1134,9 @@ def all_cases() -> list[Case]:
     cases.append(cpasync_matmul_case("s_cpasync16_matmul_32x64x48", 32, 64, 48, wide=True))
     cases.append(pre_carry_case("s_pre_carry_500", 500))
     cases.append(cond_load_case("p_cond_load_300", 300))
+    cases.append(raster_matmul_case("s_raster_matmul_48x40x64", 48, 40, 64, 4))
+    cases.append(aux_threads_case("s_aux_add_1000", 1000))
+    cases.append(big_smem_case("s_bigsmem_reverse_6x16384", 6, 16384))
     cases.append(loose_statements_case("s_loose_nodes_32"))
     return cases
 
