@@ -27,7 +27,7 @@ from pathlib import Path
 
 from . import frontend, ir, toolchain
 from .errors import ToolchainError, UnsupportedIR
-from .families import attention, gemm, pointwise, reduction, rownorm, schedule
+from .families import attention, canon, gemm, pointwise, reduction, rownorm, schedule
 from .families.common import KernelSource
 
 
@@ -72,6 +72,18 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
                                 f"(unsupported nodes: {', '.join(schedule.unsupported_nodes(kop)) or 'layout'})")
         ks = schedule.generate(kop, plan, shapes, dtypes, args, scalars, written, meta)
         return Lowered(ks, args, shapes, dtypes, meta)
+    # a matmul staged through shared memory is still a matmul: prove it and lower the naive form
+    staged = canon.staged_matmul(kop, shapes, dtypes, meta)
+    if staged is not None:
+        try:
+            plan = gemm.match(staged, shapes, dtypes)
+            if plan is not None:
+                ks = gemm.generate(staged, plan, shapes, dtypes, args, scalars, written,
+                                   variant=options.get("gemm_variant", "auto"))
+                ks.notes["canonical_form"] = "staged matmul -> naive matmul"
+                return Lowered(ks, args, shapes, dtypes, meta)
+        except UnsupportedIR:
+            pass
     fast = (
         ("attention", lambda: attention.match(kop, shapes, dtypes),
          lambda pl: attention.generate(kop, pl, shapes, dtypes, args, scalars, written)),

@@ -655,7 +655,7 @@ def cpasync_matmul_case(cid: str, m: int, k: int, n: int, *, wide: bool = False)
     kern = _meta_kernel("C", entry, ["A", "B", "C"], grid, [ts * ts, 1, 1], [
         _arg("A", [m, k], init=NORM(), seed=0), _arg("B", [k, n], init=NORM(), seed=1),
         _arg("C", [m, n], output=True)])
-    return Case(cid, entry, graph, kern, family="schedule", check={"kind": "ulp", "ulp": 0})
+    return Case(cid, entry, graph, kern, family="gemm", check={"kind": "ulp", "ulp": 0})
 
 
 def raster_matmul_case(cid: str, m: int, k: int, n: int, group: int) -> Case:

@@ -102,12 +102,14 @@ def test_new_families_do_not_claim_other_kernels(cid, family):
 
 @pytest.mark.parametrize("cid,wide", [("s_cpasync_matmul_64x48x80", False), ("s_cpasync16_matmul_32x64x48", True)])
 def test_cp_async_schedule_lowers_to_the_schedule_family(cid, wide):
-    """No fast family recognises a cp.async-staged matmul: it keeps its own
-    schedule, with the reference's thread model and copy widths."""
+    """A cp.async-staged matmul is proven a matmul and lowered by the GEMM
+    family; forced to keep its own schedule, it keeps the reference's thread
+    model and copy widths."""
     from emmy_ptx_compiler_b200 import compiler
     kop, shapes, dtypes, args = _plan_inputs(cid)
     meta = json.loads((CASES / cid / "meta.json").read_text())["kernels"][0]
-    low = compiler.lower(kop, shapes, dtypes, args, meta)
+    assert compiler.lower(kop, shapes, dtypes, args, meta).kernel.family == "gemm"
+    low = compiler.lower(kop, shapes, dtypes, args, meta, {"family": "schedule"})
     ks = low.kernel
     assert ks.family == "schedule"
     assert ks.launch.grid == tuple(meta["grid"]) and ks.launch.block == tuple(meta["block"])
@@ -141,3 +143,74 @@ def test_tensor_core_nodes_are_reported_not_lowered():
     kop = ir.KernelOp(name="k_mma", body=body)
     with pytest.raises(UnsupportedIR, match="MmaSyncPtx"):
         compiler.lower(kop, {"x": (32,)}, {"x": "f32"}, ["x"], {"grid": [1, 1, 1], "block": [32, 1, 1]})
+
+
+def _staged_matmul_kop(m=64, k=48, n=80, *, b_src=None, second_sync=True, a_kt_shift=16, wide_cols=4):
+    """The cp.async-staged matmul of the s_cpasync fixtures, with knobs that break it."""
+    from emmy_ptx_compiler_b200 import ir
+    F32 = ir.DataType("f32", "float32", 4)
+    ts = 16
+    V, L = ir.Var, lambda v: ir.Literal(v, "int")  # noqa: E731
+    add, mul = (lambda a, b: ir.BinaryExpr("+", a, b)), (lambda a, b: ir.BinaryExpr("*", a, b))  # noqa: E731
+    row, col = add(mul(V("bi"), L(ts)), V("ty")), add(mul(V("bj"), L(ts)), V("tx"))
+    tx4 = mul(V("tx"), L(4))
+    a_src = (row, add(mul(V("kt"), L(a_kt_shift)), tx4))
+    b_src = b_src or (add(mul(V("kt"), L(ts)), V("ty")), add(mul(V("bj"), L(ts)), tx4))
+    copies = (ir.Cond(ir.BinaryExpr("<", V("tx"), L(wide_cols)), body=(
+        ir.CpAsyncCopy("As", (V("ty"), tx4), "A", a_src, 16),
+        ir.CpAsyncCopy("Bs", (V("ty"), tx4), "B", b_src, 16),
+    )),)
+    kt_body = (*copies, ir.CpAsyncCommit(), ir.CpAsyncWait(0), ir.Sync(),
+               ir.Loop(axis=ir.Axis("kk", ts), body=(
+                   ir.Load(names=("a",), input="As", index=(V("ty"), V("kk")), dtype=F32),
+                   ir.Load(names=("b",), input="Bs", index=(V("kk"), V("tx")), dtype=F32),
+                   ir.Assign("p", ir.ElementwiseImpl("multiply"), ("a", "b"), F32),
+                   ir.Accum("acc", "p", ir.ElementwiseImpl("add"), F32, axes=("kk",)))))
+    if second_sync:
+        kt_body += (ir.Sync(),)
+    tile = ir.Tile(axes=(ir.Axis("bi", m // ts), ir.Axis("bj", n // ts), ir.Axis("ty", ts), ir.Axis("tx", ts)),
+                   block_threads=ts * ts, body=(
+        ir.Smem("As", (ts, ts), "float", 16), ir.Smem("Bs", (ts, ts), "float", 16),
+        ir.Init("acc", 0.0, dtype=F32),
+        ir.Loop(axis=ir.Axis("kt", k // ts), body=kt_body),
+        ir.Write(output="C", index=(row, col), values=("acc",), value_dtype=F32)))
+    kop = ir.KernelOp(name="k_staged", body=(tile,))
+    shapes = {"A": (m, k), "B": (k, n), "C": (m, n)}
+    return kop, shapes, {"A": "f32", "B": "f32", "C": "f32"}
+
+
+def test_staged_matmul_is_proven_and_lowered_as_a_gemm():
+    from emmy_ptx_compiler_b200 import compiler
+    from emmy_ptx_compiler_b200.families import canon
+    kop, shapes, dtypes = _staged_matmul_kop()
+    meta = {"grid": [20, 1, 1], "block": [256, 1, 1]}
+    naive = canon.staged_matmul(kop, shapes, dtypes, meta)
+    assert naive is not None
+    low = compiler.lower(kop, shapes, dtypes, ["A", "B", "C"], meta)
+    assert low.kernel.family == "gemm" and low.kernel.notes.get("canonical_form")
+
+
+@pytest.mark.parametrize("knob", ["b_transposed", "no_second_sync", "wrong_k_shift", "missing_copies"])
+def test_near_miss_schedules_keep_their_own_schedule(knob):
+    """A staged matmul the proof cannot establish stays in the schedule family."""
+    from emmy_ptx_compiler_b200 import compiler, ir
+    from emmy_ptx_compiler_b200.families import canon
+    V, L = ir.Var, lambda v: ir.Literal(v, "int")  # noqa: E731
+    kw = {}
+    if knob == "b_transposed":
+        tx4 = ir.BinaryExpr("*", V("tx"), L(4))
+        kw["b_src"] = (ir.BinaryExpr("+", ir.BinaryExpr("*", V("bj"), L(16)), tx4),
+                       ir.BinaryExpr("+", ir.BinaryExpr("*", V("kt"), L(16)), V("ty")))
+    elif knob == "no_second_sync":
+        kw["second_sync"] = False
+    elif knob == "wrong_k_shift":
+        kw["a_kt_shift"] = 8
+    else:
+        kw["wide_cols"] = 3
+    # square operands for the transposed copy, so only the index proof can tell
+    kop, shapes, dtypes = _staged_matmul_kop(m=64, k=64, n=64, **kw) if knob == "b_transposed" \
+        else _staged_matmul_kop(**kw)
+    meta = {"grid": [20, 1, 1], "block": [256, 1, 1]}
+    assert canon.staged_matmul(kop, shapes, dtypes, meta) is None
+    low = compiler.lower(kop, shapes, dtypes, ["A", "B", "C"], meta)
+    assert low.kernel.family == "schedule"
