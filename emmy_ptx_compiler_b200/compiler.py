@@ -55,7 +55,8 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
 
     ``options`` selects among equivalent schedules (results do not depend on
     it): ``{"gemm_variant": "auto" | "pair" | "single",
-    "pointwise_pair": "auto" | True | False, "family": "schedule"}``; the
+    "pointwise_pair": "auto" | True | False, "attention_first_pass": "auto" | "tiled",
+    "family": "schedule"}``; the
     last skips the fast families.  A KernelOp no fast family takes (or one a
     family recognises but cannot specialise) keeps its own schedule."""
     meta = meta or {}
@@ -86,7 +87,8 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
             pass
     fast = (
         ("attention", lambda: attention.match(kop, shapes, dtypes),
-         lambda pl: attention.generate(kop, pl, shapes, dtypes, args, scalars, written)),
+         lambda pl: attention.generate(kop, pl, shapes, dtypes, args, scalars, written,
+                                       first_pass=options.get("attention_first_pass", "auto"))),
         ("gemm", lambda: gemm.match(kop, shapes, dtypes),
          lambda pl: gemm.generate(kop, pl, shapes, dtypes, args, scalars, written,
                                   variant=options.get("gemm_variant", "auto"))),

@@ -253,7 +253,8 @@ def _c(name: str) -> str:
 
 
 def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args: list[str],
-             scalars: dict[str, str], written: set[str]) -> KernelSource:
+             scalars: dict[str, str], written: set[str], first_pass: str = "auto") -> KernelSource:
+    """``first_pass``: "auto" (register-tiled when it applies) or "tiled"."""
     params: list[ParamSpec] = []
     ptrs: dict[str, str] = {}
     sig: list[str] = []
@@ -290,10 +291,17 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
     nfac = max([len(st.row_accs) for st in plan.steps if isinstance(st, KeyLoop)] + [0])
     keyloops = [st for st in plan.steps if isinstance(st, KeyLoop)]
     # every key loop computes the same dot products: keep the first pass's scores for the rest
-    cache = len(keyloops) > 1 and len({st.dot_init for st in keyloops}) == 1 and BQ * (SK + 1) * 4 <= SCORE_CACHE_BYTES
+    cache = len(keyloops) > 1 and len({st.dot_init for st in keyloops}) == 1 and BQ * (SK + 4) * 4 <= SCORE_CACHE_BYTES
+    # first pass as a register tile: every thread computes all BQ rows for four
+    # consecutive keys, reading k straight from L2 (when its values are all that
+    # pass keeps: scores for the cache and max / min partials)
+    first = keyloops[0] if keyloops else None
+    fast1 = (first_pass == "auto" and cache and first is not None and plan.k_dk and D % 4 == 0 and SK % (4 * T) == 0
+             and BQ % 4 == 0 and BQ <= 16 and not first.dep and not first.stash
+             and all(op in ("maximum", "minimum") for _, op in first.row_accs))
     # the tiles each pass streams through shared memory; passes run one after another,
     # so one double-buffered region holds whatever the pass needs
-    need_k = {id(st): not (cache and st is not keyloops[0]) for st in keyloops}
+    need_k = {id(st): not (cache and st is not keyloops[0]) and not (fast1 and st is first) for st in keyloops}
     need_v = {id(st): bool(st.dep and plan.v) for st in keyloops}
     stage = max([(D * BK if need_k[id(st)] else 0) + (BK * DV if need_v[id(st)] else 0) for st in keyloops] + [4])
     stage = -(-stage // 4) * 4
@@ -312,6 +320,7 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
         off[name] = cur
         cur += -(-n // 4) * 4
 
+    SCS = SK + 4                # score-cache row stride: float4-aligned rows, rows 4 banks apart
     alloc("qs", BQ * QS)
     alloc("kv", 2 * stage)
     alloc("rowv", max(1, len(row_names)) * BQ)
@@ -319,9 +328,9 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
     alloc("accb", max(1, nfac) * BQ * SS)   # second factor when the accumulate is an fma
     alloc("stash", max(1, nstash) * BQ * SS)
     np_map = BQ * BK // T if (T % BK == 0 and (BQ * BK) % T == 0) else 1
-    alloc("pred", max(1, nfac) * NW * max(1, np_map))   # per-warp partials of max / min rows
+    alloc("pred", max(1, nfac) * NW * max(1, np_map, BQ if fast1 else 1))   # per-warp partials of max / min rows
     if cache:
-        alloc("scache", BQ * (SK + 1))
+        alloc("scache", BQ * SCS)
     smem_bytes = cur * 4
     # CTAs per SM that shared memory allows (1 KiB of it is reserved per CTA), for the register cap
     min_blocks = max(1, min(4, 2048 // T, (228 * 1024) // (smem_bytes + 1024)))
@@ -340,7 +349,7 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
     w("}")
     w(f'extern "C" __global__ void __launch_bounds__({T}, {min_blocks}) {kop.name}(' + ", ".join(sig) + ") {")
     w(f"    constexpr int SQ = {SQ}, DV = {DV}, SK = {SK}, D = {D}, BQ = {BQ}, BK = {BK};")
-    w(f"    constexpr int QS = {QS}, SS = {SS}, STAGE = {stage};")
+    w(f"    constexpr int QS = {QS}, SS = {SS}, STAGE = {stage}, SCS = {SCS};")
     w(f"    constexpr int NT = (SK + BK - 1) / BK;")
     w("    extern __shared__ __align__(16) float sm[];")
     for name, o in off.items():
@@ -365,7 +374,10 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
     w("        __syncthreads();")
     w(f"        for (int e = tid; e < BQ * D; e += {T}) {{")
     w("            const int r = e / D, d = e - r * D;")
-    w(f"            qs[r * QS + d] = r < nq ? {ptrs[plan.q]}[(q0 + r) * D + d] : 0.0f;")
+    # the fast first pass reads q transposed ([d][row]: one row-quad per float4); no
+    # other pass reads q then (the scores are cached)
+    qdst = "qs[d * BQ + r]" if fast1 else "qs[r * QS + d]"
+    w(f"            {qdst} = r < nq ? {ptrs[plan.q]}[(q0 + r) * D + d] : 0.0f;")
     w("        }")
     # output cell accumulators: thread owns cells o = tid + u*T of the BQ x DV block
     nown = -(-(BQ * DV) // T)
@@ -445,6 +457,10 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
                 if n in row_slot:
                     w(f"{ind}    {row_ref(n, 'tid')} = {em.as_f32(n)};")
             w(f"{ind}}}")
+            continue
+        if fast1 and st is first:
+            _emit_fast_first_pass(w, ind, st, plan, shapes, dtypes, ptrs, fus, scalar_env, row_names, row_ref,
+                                  BQ, T, NW, SK, D)
             continue
         reuse = cache and st is not keyloops[0]
         loads = need_k[id(st)] or need_v[id(st)]
@@ -538,17 +554,17 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
         w(f"{i3}if (r < nq && kk < nk) {{")
         i4 = i3 + "    "
         if reuse:
-            w(f"{i4}float sc = scache[r * (SK + 1) + k0 + kk];")
+            w(f"{i4}float sc = scache[r * SCS + k0 + kk];")
         elif mapped:
             w(f"{i4}float sc = scv[u];")
             if cache:
-                w(f"{i4}scache[r * (SK + 1) + k0 + kk] = sc;")
+                w(f"{i4}scache[r * SCS + k0 + kk] = sc;")
         else:
             w(f"{i4}float sc = {f32_lit(st.dot_init)};")
             w(f"{i4}#pragma unroll 8")
             w(f"{i4}for (int d = 0; d < D; ++d) sc = __fmaf_rn(qs[r * QS + d], ks[d * BK + kk], sc);")
             if cache:
-                w(f"{i4}scache[r * (SK + 1) + k0 + kk] = sc;")
+                w(f"{i4}scache[r * SCS + k0 + kk] = sc;")
         em = Emitter(shapes, dtypes, ptrs, indent=i4)
         em.fusable = fus
         em.env.update(scalar_env)
@@ -675,10 +691,93 @@ def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args:
                         range_bytes=rb)
     lines.append(launch_record_source("attention", launch, params))
     notes = {"kernel": "attention_rows", "rows_per_cta": BQ, "key_tile": BK, "threads": T, "score_cache": cache,
+             "register_tiled_first_pass": fast1,
              "passes": len(keyloops), "smem": smem_bytes, "async_k": async_k, "async_v": async_v,
              "min_blocks": min_blocks}
     return KernelSource(entry=kop.name, source="\n".join(lines), launch=launch, params=params,
                         family="attention", notes=notes)
+
+
+def _emit_fast_first_pass(w, ind, st, plan, shapes, dtypes, ptrs, fus, scalar_env, row_names, row_ref,
+                          BQ, T, NW, SK, D) -> None:
+    """The first key loop as a register tile: thread t owns keys kb * 4T + 4t .. +3
+    of every key block kb and all BQ rows, 4 * BQ independent fma chains, each
+    still sequential over d as the reference computes it.  k is read from L2 one
+    float4 (four keys) per d; q comes transposed from shared memory, one
+    broadcast float4 per four rows.  Scores go to the cache; the row max / min
+    stays in registers and is combined across threads once."""
+    kp = ptrs[plan.kmat]
+    w(f"{ind}__syncthreads();")
+    for ri, (a, op) in enumerate(st.row_accs):
+        w(f"{ind}float fm{ri}[BQ];")
+        w(f"{ind}#pragma unroll")
+        w(f"{ind}for (int r = 0; r < BQ; ++r) fm{ri}[r] = {row_ref(a, 'r')};")
+    w(f"{ind}const bool k_vec = ((reinterpret_cast<uintptr_t>({kp}) & 15) == 0);")
+    w(f"{ind}for (int kb = 0; kb < SK / (4 * {T}); ++kb) {{")
+    i2 = ind + "    "
+    w(f"{i2}const int kbase = kb * (4 * {T}) + 4 * tid;")
+    w(f"{i2}const float *const kcol = {kp} + kbase;")
+    w(f"{i2}float sv[BQ][4];")
+    w(f"{i2}#pragma unroll")
+    w(f"{i2}for (int r = 0; r < BQ; ++r) {{ sv[r][0] = sv[r][1] = sv[r][2] = sv[r][3] = {f32_lit(st.dot_init)}; }}")
+    w(f"{i2}#pragma unroll 8")
+    w(f"{i2}for (int d = 0; d < D; ++d) {{")
+    w(f"{i2}    const float *const kd = kcol + (long long)d * SK;")
+    w(f"{i2}    const float4 kv4 = k_vec ? *reinterpret_cast<const float4 *>(kd) : make_float4(kd[0], kd[1], kd[2], kd[3]);")
+    w(f"{i2}    #pragma unroll")
+    w(f"{i2}    for (int r4 = 0; r4 < BQ; r4 += 4) {{")
+    w(f"{i2}        const float4 q4 = *reinterpret_cast<const float4 *>(qs + d * BQ + r4);")
+    for rr, qc in enumerate(("x", "y", "z", "w")):
+        for c, kc in enumerate(("x", "y", "z", "w")):
+            w(f"{i2}        sv[r4 + {rr}][{c}] = __fmaf_rn(q4.{qc}, kv4.{kc}, sv[r4 + {rr}][{c}]);")
+    w(f"{i2}    }}")
+    w(f"{i2}}}")
+    w(f"{i2}#pragma unroll")
+    w(f"{i2}for (int r = 0; r < BQ; ++r) {{")
+    w(f"{i2}    #pragma unroll")
+    w(f"{i2}    for (int c = 0; c < 4; ++c) {{")
+    w(f"{i2}        if (r < nq) {{")
+    i5 = i2 + "            "
+    w(f"{i5}const int kk = kbase + c;")
+    w(f"{i5}float sc = sv[r][c];")
+    w(f"{i5}scache[r * SCS + kk] = sc;")
+    em = Emitter(shapes, dtypes, ptrs, indent=i5)
+    em.fusable = fus
+    em.env.update(scalar_env)
+    em.bind_const(plan.i, "int", "(q0 + r)")
+    em.bind_const(st.loop.axis.name, "int", "(long long)kk")
+    em.env[st.dot_acc] = ("f32", "sc")
+    em.declared[f"{st.dot_acc}|f32"] = "sc"
+    for n in row_names:
+        em.env.setdefault(n, ("f32", row_ref(n, "r")))
+    em.run(tuple(st.indep))
+    w("\n".join(em.lines))
+    for ri, (a, op) in enumerate(st.row_accs):
+        accum = next(t for t in st.post if isinstance(t, ir.Accum) and t.name == a)
+        w(f"{i5}fm{ri}[r] = {combine_code(op, f'fm{ri}[r]', em.as_f32(accum.value))};")
+    w(f"{i2}        }}")
+    w(f"{i2}    }}")
+    w(f"{i2}}}")
+    w(f"{ind}}}")
+    # every thread holds a partial of every row: over the warp, then over the warps
+    for ri, (a, op) in enumerate(st.row_accs):
+        w(f"{ind}#pragma unroll")
+        w(f"{ind}for (int r = 0; r < BQ; ++r) {{")
+        w(f"{ind}    float x = fm{ri}[r];")
+        w(f"{ind}    #pragma unroll")
+        w(f"{ind}    for (int o = 16; o > 0; o >>= 1) x = {combine_code(op, 'x', '__shfl_xor_sync(0xffffffffu, x, o)')};")
+        w(f"{ind}    if (lane == 0) pred[({ri} * {NW} + warp) * BQ + r] = x;")
+        w(f"{ind}}}")
+    if st.row_accs:
+        w(f"{ind}__syncthreads();")
+        w(f"{ind}if (tid < nq) {{")
+        for ri, (a, op) in enumerate(st.row_accs):
+            w(f"{ind}    {{")
+            w(f"{ind}        float x = {row_ref(a, 'tid')};")
+            w(f"{ind}        for (int wv = 0; wv < {NW}; ++wv) x = {combine_code(op, 'x', f'pred[({ri} * {NW} + wv) * BQ + tid]')};")
+            w(f"{ind}        {row_ref(a, 'tid')} = x;")
+            w(f"{ind}    }}")
+        w(f"{ind}}}")
 
 
 def _emit_dep(w, i2, st, plan, shapes, dtypes, ptrs, fus, scalar_env, row_names, row_ref, stash_codes,

@@ -41,3 +41,39 @@ def test_unaligned_kv_matches_aligned(cid, cuda_device):
     assert case.module.status() == 0
     assert torch.equal(moved[out_name].view(torch.int32), aligned.view(torch.int32))
     case.module.close()
+
+
+def test_register_tiled_first_pass_matches_tiled_pass(cuda_device):
+    """At the bench shape (2048 keys) the first pass runs as a register tile
+    (every thread: all rows x four keys, k straight from L2).  Its output must
+    be the tiled pass's bit for bit (each score is still one fma chain in d
+    order), and both match the C restatement of the IR within the oracle bound."""
+    import sys
+    import numpy as np
+    import torch
+    from emmy_ptx_compiler_b200 import harness
+    from conftest import REPO
+    sys.path.insert(0, str(REPO / "oracle"))
+    import interp
+    cid = "a_attn_bench_2048x64"
+    fast = harness.DeviceCase(CASES / cid, cuda_device)
+    tiled = harness.DeviceCase(CASES / cid, cuda_device, options={"attention_first_pass": "tiled"})
+    assert fast.bundle["notes"]["register_tiled_first_pass"] and not tiled.bundle["notes"]["register_tiled_first_pass"]
+    bufs = harness._seeded_device_inputs(fast.spec, cuda_device, seed=9)
+    outs = {}
+    for name, case in (("fast", fast), ("tiled", tiled)):
+        b = dict(bufs)
+        b["attn"] = torch.full_like(bufs["attn"], float("nan"))
+        case.launch(b)
+        torch.cuda.synchronize(cuda_device)
+        assert case.module.status() == 0
+        outs[name] = b["attn"].cpu().numpy()
+        case.module.close()
+    assert np.array_equal(outs["fast"].view(np.uint32), outs["tiled"].view(np.uint32))
+    q, kt, v = (bufs[n].cpu().numpy() for n in ("q", "kt", "v"))
+    rows = 96                      # the C restatement on the first rows
+    ref = np.empty((rows, 64), np.float32)
+    assert interp.lib().ora_attn_naive_f32(interp._p(np.ascontiguousarray(q[:rows])), interp._p(kt), interp._p(v),
+                                           interp._p(ref), rows, 2048, 64, 64, float(np.float32(1 / 8))) == 0
+    ok, why = interp.within(outs["fast"][:rows], ref, {"rtol": 4e-6, "atol": 2e-6})
+    assert ok, why
