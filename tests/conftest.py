@@ -18,7 +18,8 @@ import pytest
 REPO = Path(__file__).resolve().parents[1]
 GOLDEN = REPO / "tests" / "golden"
 CASES = GOLDEN / "cases"
-REFERENCE = Path(os.environ.get("EMMY_REFERENCE", "/root/reference"))
+# the reference checkout (read-only), by default beside this repository; tests that need it skip without it
+REFERENCE = Path(os.environ.get("EMMY_REFERENCE", str(Path(__file__).resolve().parents[2] / "reference")))
 
 for p in (REPO, REPO / "oracle"):
     if str(p) not in sys.path:
