@@ -182,3 +182,30 @@ def test_simt_oracle_on_cp_async_matmul_equals_sequential_fma(cid):
     C = np.empty(out["C"].shape, np.float32)
     interp.lib().ora_gemm_seqfma_f32(interp._p(A), interp._p(B), interp._p(C), A.shape[0], B.shape[1], A.shape[1], 0)
     assert np.array_equal(C.view(np.uint32), out["C"].view(np.uint32))
+
+
+def _block_cooperative_cases():
+    out = []
+    for c in json.loads((CASES / "INDEX.json").read_text())["cases"]:
+        cid = c["id"]
+        if "_full" in cid or "2p28" in cid or "_prof_" in cid or "_bench_" in cid:
+            continue
+        text = next((CASES / cid).glob("*.ir.json")).read_text()
+        if "TreeHalve" in text or "WarpShuffle" in text:
+            out.append(cid)
+    return out
+
+
+@pytest.mark.parametrize("cid", _block_cooperative_cases())
+def test_lockstep_simt_evaluation_agrees_with_the_schedule_evaluators(cid):
+    """Two independent restatements of the reference's block-cooperative
+    semantics: the oracle's schedule-specific evaluators (strided accumulate,
+    butterfly, smem tree, in the reference's order) and its lockstep SIMT
+    evaluation of the same IR, thread block by thread block.  Bit-identical."""
+    import interp
+    kop, meta, mk, shapes, dtypes = interp.load_case(CASES / cid)
+    out, ins = interp.run_case(CASES / cid)
+    outs = {a["name"]: tuple(a["shape"]) for a in mk["args"] if a.get("output")}
+    simt = interp._eval_simt(kop, shapes, dtypes, ins, outs, {"grid": mk.get("grid"), "block": mk.get("block")})
+    for name in out:
+        assert np.array_equal(np.asarray(out[name]).view(np.uint32), np.asarray(simt[name]).view(np.uint32)), name
