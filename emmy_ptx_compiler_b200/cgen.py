@@ -139,10 +139,6 @@ def combine_code(op: str, a: str, b: str) -> str:
     return F32_BINARY.get(op, F32_BINARY["add"]).format(a=a, b=b)
 
 
-def is_product_op(op: str) -> bool:
-    return op in ("multiply", "mul")
-
-
 # ------------------------------------------------------------------ names
 
 

@@ -38,6 +38,7 @@ from .. import ir
 from ..cgen import DEVICE_PRELUDE, Emitter, combine_code, ctype, f32_lit, fusable_products
 from ..errors import UnsupportedIR
 from .common import KernelSource, LaunchPlan, ParamSpec, SM_COUNT, launch_record_source
+from .common import c_ident as _c
 
 THREADS = 256
 BK = 64
@@ -245,11 +246,6 @@ def match(kop: ir.KernelOp, shapes: dict, dtypes: dict) -> AttnPlan | None:
     if D > 256 or DV > 256:
         raise UnsupportedIR(f"attention head sizes {D}/{DV} above 256")
     return AttnPlan(i, j, SQ, DV, SK, D, q, kmat, k_dk, v, steps, w, w.output, cell_accs)
-
-
-def _c(name: str) -> str:
-    import re
-    return re.sub(r"[^A-Za-z0-9_]", "_", name)
 
 
 def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args: list[str],

@@ -107,3 +107,9 @@ def launch_record_source(family: str, launch: LaunchPlan, params: list[ParamSpec
         "    {" + ", ".join(f"{int(x)}ull" for x in rbytes) + "}\n"
         "};\n"
     )
+
+
+def c_ident(name: str) -> str:
+    """An IR name as a C identifier fragment (every other character becomes '_')."""
+    import re
+    return re.sub(r"[^A-Za-z0-9_]", "_", name)

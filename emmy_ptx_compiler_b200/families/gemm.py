@@ -33,6 +33,7 @@ from .. import ir
 from ..cgen import DEVICE_PRELUDE, Emitter, ctype, f32_lit, store_from
 from ..errors import UnsupportedIR
 from .common import KernelSource, LaunchPlan, ParamSpec, SM_COUNT, TmapSpec, launch_record_source
+from .common import c_ident as _c
 
 BM, BN, BK, STAGES = 128, 256, 64, 4
 PAIR_BM, PAIR_STAGES = 256, 6   # CTA-pair tile: 256 x 256, 128 rows and 128 B-columns per CTA
@@ -142,10 +143,6 @@ def match(kop: ir.KernelOp, shapes: dict, dtypes: dict) -> GemmPlan | None:
     if adt != bdt or adt not in ("f32", "bf16", "f16"):
         raise UnsupportedIR(f"GEMM operands {adt} x {bdt} (need matching f32, bf16 or f16)")
     return GemmPlan(i, j, k, M, N, K, a, b, b_nk, acc.name, seed, epi, out, adt)
-
-
-def _c(name: str) -> str:
-    return re.sub(r"[^A-Za-z0-9_]", "_", name)
 
 
 def range_bytes(plan: GemmPlan, args: list[str], shapes: dict, dtypes: dict, scalars: dict) -> list[int] | None:

@@ -30,6 +30,7 @@ from .. import ir
 from ..ir import ELEM_BYTES
 from ..cgen import DEVICE_PRELUDE, Emitter, ctype, load_to_kind, store_from
 from .common import KernelSource, LaunchPlan, ParamSpec, SM_COUNT, launch_record_source
+from .common import c_ident as _c
 
 BLOCK = 256
 UNROLL = 2
@@ -411,11 +412,6 @@ def _finish_vector(kop, plan, lines, ncell, unroll, vec_ok, params, why, *, em_p
                         family="pointwise",
                         notes={"vector": vec_ok, "scalar_reasons": why, "ncells": ncell,
                                "pair": plan.pair})
-
-
-def _c(name: str) -> str:
-    import re
-    return re.sub(r"[^A-Za-z0-9_]", "_", name)
 
 
 def _vector_trip(plan: PointwisePlan, shapes, dtypes, ptrs, scalar_env, vexprs: list[str],

@@ -36,6 +36,7 @@ from ..cgen import (DEVICE_PRELUDE, Emitter, combine_code, ctype, f32_lit, ident
                     lit_int)
 from ..errors import UnsupportedIR
 from .common import KernelSource, LaunchPlan, ParamSpec, SM_COUNT, launch_record_source
+from .common import c_ident as _c
 
 BLOCK = 256
 UNROLL = 4
@@ -227,10 +228,6 @@ def _seeds(pre, accs, strict: bool) -> dict[str, float]:
 
 
 # ---------------------------------------------------------------------------- codegen
-
-
-def _c(name: str) -> str:
-    return re.sub(r"[^A-Za-z0-9_]", "_", name)
 
 
 def _vector_layout(plan: ReductionPlan, shapes, dtypes) -> tuple[bool, list[str]]:

@@ -37,6 +37,7 @@ from ..cgen import (DEVICE_PRELUDE, DIVIDE_OPS, Emitter, combine_code, ctype, f3
                     lit_int, load_to_kind, store_from)
 from ..errors import UnsupportedIR
 from .common import KernelSource, LaunchPlan, ParamSpec, SM_COUNT, launch_record_source
+from .common import c_ident as _c
 from .pointwise import _VEC_HELPERS
 
 MAX_THREADS = 256
@@ -222,11 +223,6 @@ def match(kop: ir.KernelOp, shapes: dict, dtypes: dict) -> RowPlan | None:
         if ir.canon_dtype(dtypes.get(name)) not in ("f32", "bf16", "f16"):
             raise UnsupportedIR(f"row-fused kernel on {dtypes.get(name)} tensor {name!r}")
     return RowPlan(tile, row_axes, co, K, steps, streamed, vectors, outputs)
-
-
-def _c(name: str) -> str:
-    import re
-    return re.sub(r"[^A-Za-z0-9_]", "_", name)
 
 
 def range_bytes(plan: RowPlan, args: list[str], scalars: dict, dtypes: dict, shapes: dict) -> list[int]:
@@ -449,7 +445,6 @@ def reuse_plan(plan: RowPlan, scalars: dict) -> tuple[dict, dict]:
     keep = {src: renum[sl] for src, sl in keep.items() if sl in renum}
     reuse = {k: renum[sl] for k, sl in reuse.items()}
     return keep, reuse
-
 
 
 def _stage_bytes(plan: RowPlan, dtypes) -> int:

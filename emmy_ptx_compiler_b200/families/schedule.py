@@ -41,6 +41,7 @@ from .. import ir
 from ..cgen import DEVICE_PRELUDE, Emitter, carry_slot, ctype, f32_lit, fusable_products, identity_of, lit_int
 from ..errors import UnsupportedIR
 from .common import KernelSource, LaunchPlan, ParamSpec, launch_record_source
+from .common import c_ident as _c
 
 SUPPORTED = (ir.Tile, ir.Smem, ir.Sync, ir.WarpShuffle, ir.TreeHalve, ir.Load, ir.Write, ir.Assign,
              ir.Accum, ir.Init, ir.Let, ir.Loop, ir.StridedLoop, ir.Cond, ir.Select, ir.ZeroPrologue,
@@ -74,11 +75,6 @@ def match(kop: ir.KernelOp, shapes: dict, dtypes: dict) -> SchedPlan | None:
             seen.add(s.name)
             smem.append(s)
     return SchedPlan(smem, sum(isinstance(s, ir.Tile) for s in top))
-
-
-def _c(name: str) -> str:
-    import re
-    return re.sub(r"[^A-Za-z0-9_]", "_", name)
 
 
 class SchedEmitter(Emitter):
