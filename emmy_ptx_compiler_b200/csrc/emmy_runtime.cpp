@@ -214,6 +214,8 @@ struct emmy_module {
     CUstream h2d = nullptr, d2h = nullptr;
     std::vector<CUevent> ev_in, ev_out;
     CUevent ev_whole = nullptr, ev_start = nullptr;
+    // largest dynamic shared memory the function may take (48 KiB unless raised)
+    uint32_t dyn_attr = 48 * 1024;
     // emmy_run_host small-payload path: pinned host memory the kernel reads and writes directly
     void *zc_host = nullptr;
     CUdeviceptr zc_dev = 0;
@@ -258,7 +260,8 @@ int encode_tmaps(emmy_module *m, const uint64_t *args, int nargs) {
 bool has_range(const emmy_module *m) { return m->has_rec && (m->rec.flags & EMMY_LR_RANGE); }
 
 int launch_locked(emmy_module *m, const uint64_t *args, int nargs, const uint32_t *grid,
-                  const uint32_t *block, uint64_t stream, uint64_t rbegin = 0, uint64_t rend = ~0ull) {
+                  const uint32_t *block, uint64_t stream, uint64_t rbegin = 0, uint64_t rend = ~0ull,
+                  int64_t dyn_override = -1) {
     int rc = set_device(m->dev);
     if (rc) return rc;
     uint32_t g[3], b[3], smem = 0;
@@ -268,6 +271,15 @@ int launch_locked(emmy_module *m, const uint64_t *args, int nargs, const uint32_
             b[i] = block[i] ? block[i] : 1;
         }
         smem = m->has_rec ? m->rec.dyn_smem : 0;
+        if (dyn_override >= 0) {
+            smem = static_cast<uint32_t>(dyn_override);
+            if (smem > m->dyn_attr) {
+                CU(g_drv.cuFuncSetAttribute(m->fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
+                                            static_cast<int>(smem)),
+                   "cuFuncSetAttribute (dynamic shared memory)");
+                m->dyn_attr = smem;
+            }
+        }
     } else if (m->has_rec) {
         for (int i = 0; i < 3; ++i) {
             g[i] = m->rec.grid[i];
@@ -460,6 +472,7 @@ int emmy_load(int dev, const void *image, size_t len, const char *entry, emmy_mo
                         m->param_size.size(), want);
         }
         if (m->rec.dyn_smem > 48 * 1024) {
+            m->dyn_attr = m->rec.dyn_smem;
             r = g_drv.cuFuncSetAttribute(m->fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
                                          static_cast<int>(m->rec.dyn_smem));
             if (r != CUDA_SUCCESS) {
@@ -534,6 +547,14 @@ int emmy_launch(emmy_module_t m, const uint64_t *args, int nargs, const uint32_t
     if (!m || (nargs > 0 && !args)) return fail(EMMY_ERR_INVALID, "emmy_launch: NULL argument");
     std::lock_guard<std::mutex> lk(g_mu);
     return launch_locked(m, args, nargs, grid, block, stream);
+}
+
+int emmy_launch_ex(emmy_module_t m, const uint64_t *args, int nargs, const uint32_t *grid,
+                   const uint32_t *block, uint32_t dyn_smem, uint64_t stream) {
+    if (!m || (nargs > 0 && !args) || !grid || !block)
+        return fail(EMMY_ERR_INVALID, "emmy_launch_ex: NULL argument (grid and block are required)");
+    std::lock_guard<std::mutex> lk(g_mu);
+    return launch_locked(m, args, nargs, grid, block, stream, 0, ~0ull, static_cast<int64_t>(dyn_smem));
 }
 
 int emmy_module_status(emmy_module_t m, uint32_t *status) {

@@ -124,7 +124,9 @@ class ForeignModule:
         torch = _torch()
         stream = torch.cuda.current_stream(self.device).cuda_stream
         g, b = self.spec.kernel["grid"], self.spec.kernel["block"]
-        self.module.launch([bufs[n] for n in self.spec.arg_order], stream=stream, grid=g, block=b)
+        smem = int(self.spec.kernel.get("smem_bytes") or 0)
+        self.module.launch([bufs[n] for n in self.spec.arg_order], stream=stream, grid=g, block=b,
+                           smem=smem if smem else None)
 
 
 def _seeded_device_inputs(spec: CaseSpec, device: int, seed: int = 0) -> dict:

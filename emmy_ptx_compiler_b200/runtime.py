@@ -43,6 +43,7 @@ def _declare(lib) -> None:
         "emmy_unload": ([vp], i32),
         "emmy_module_info": ([vp, P(u32), P(u32), P(u32), P(u32), P(u32)], i32),
         "emmy_launch": ([vp, P(u64), i32, P(u32), P(u32), u64], i32),
+        "emmy_launch_ex": ([vp, P(u64), i32, P(u32), P(u32), u32, u64], i32),
         "emmy_module_status": ([vp, P(u32)], i32),
         "emmy_sync": ([i32, u64, i32], i32),
         "emmy_alloc": ([i32, sz, P(u64)], i32),
@@ -82,7 +83,7 @@ def _declare(lib) -> None:
 
 
 EXPORTED = ("emmy_version", "emmy_last_error", "emmy_init", "emmy_device_count", "emmy_load",
-            "emmy_unload", "emmy_module_info", "emmy_launch", "emmy_module_status", "emmy_sync",
+            "emmy_unload", "emmy_module_info", "emmy_launch", "emmy_launch_ex", "emmy_module_status", "emmy_sync",
             "emmy_alloc", "emmy_free", "emmy_memcpy_htod", "emmy_memcpy_dtoh", "emmy_memset_d8",
             "emmy_host_alloc", "emmy_host_free", "emmy_run_host", "emmy_time_launch", "emmy_launch_range",
             "emmy_module_range", "emmy_shard_range", "emmy_launch_sharded", "emmy_sum_f32_noalloc",
@@ -178,10 +179,15 @@ class Module:
     def _words(self, args) -> C.Array:
         return (C.c_uint64 * max(1, len(args)))(*[arg_word(a) for a in args])
 
-    def launch(self, args, stream: int = 0, grid=None, block=None) -> None:
+    def launch(self, args, stream: int = 0, grid=None, block=None, smem: int | None = None) -> None:
+        """``smem``: dynamic shared-memory bytes for an explicit ``grid``/``block``
+        launch (the meta.json ``smem_bytes``); None keeps the module's own."""
         words = self._words(args)
         g = (C.c_uint32 * 3)(*(list(grid) + [1, 1])[:3]) if grid is not None else None
         b = (C.c_uint32 * 3)(*(list(block) + [1, 1])[:3]) if block is not None else None
+        if smem is not None:
+            _check(lib().emmy_launch_ex(self._h, words, len(args), g, b, C.c_uint32(int(smem)), C.c_uint64(stream)))
+            return
         _check(lib().emmy_launch(self._h, words, len(args), g, b, C.c_uint64(stream)))
 
     def bind(self, args, stream: int = 0) -> "BoundLaunch":

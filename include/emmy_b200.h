@@ -75,6 +75,15 @@ int emmy_module_info(emmy_module_t m, uint32_t *family, uint32_t grid[3], uint32
 int emmy_launch(emmy_module_t m, const uint64_t *args, int nargs, const uint32_t *grid,
                 const uint32_t *block, uint64_t stream);
 
+/* The reference runner's whole meta.json launch (grid, block and smem_bytes:
+ * reference README.md:170-182, tools/make_proxy_set.py:75-86): emmy_launch
+ * with explicit geometry and `dyn_smem` bytes of dynamic shared memory, for
+ * modules that size `.extern .shared` at launch (the reference's PTX above 48
+ * KiB, compile.py:827-836).  The function's dynamic shared-memory limit is
+ * raised when `dyn_smem` needs it. */
+int emmy_launch_ex(emmy_module_t m, const uint64_t *args, int nargs, const uint32_t *grid,
+                   const uint32_t *block, uint32_t dyn_smem, uint64_t stream);
+
 /* Read and clear the module's device status word (EMMY_STATUS_* bits from
  * include/emmy_launch_record.h).  Synchronises the device first. */
 int emmy_module_status(emmy_module_t m, uint32_t *status);

@@ -706,9 +706,9 @@ def aux_threads_case(cid: str, n: int) -> Case:
 
 def big_smem_case(cid: str, blocks: int, per_block: int) -> Case:
     """Each 256-thread block stages its slice of x in one shared buffer larger
-    than 48 KiB (dynamic shared memory), then writes the slice reversed.  The
-    reference's PTX for it is not produced: its runner-style launch here passes
-    no dynamic shared memory, which such a kernel needs."""
+    than 48 KiB, then writes the slice reversed.  The reference makes such a
+    buffer ``.extern .shared`` sized by meta ``smem_bytes`` at launch
+    (compile.py:827-836), which the harness passes (emmy_launch_ex)."""
     entry = "k_reverse_slices"
     t = 256
     lit = lambda v: Literal(v, "int")  # noqa: E731
@@ -732,7 +732,7 @@ def big_smem_case(cid: str, blocks: int, per_block: int) -> Case:
     kern = _meta_kernel("y", entry, ["x", "y"], [blocks, 1, 1], [t, 1, 1], [
         _arg("x", [n], init=NORM(), seed=0), _arg("y", [n], output=True)])
     kern["smem_bytes"] = per_block * 4
-    return Case(cid, entry, graph, kern, family="schedule", check={"kind": "exact"}, ref=False)
+    return Case(cid, entry, graph, kern, family="schedule", check={"kind": "exact"})
 
 
 def cond_load_case(cid: str, n: int) -> Case:
