@@ -13,10 +13,11 @@ lowers.  It answers None, and the IR keeps its own schedule, unless every step
 of the proof holds:
 
 * the structure is one Tile; then ``Init acc``; then a k-tile loop holding
-  the copies (``CpAsyncCopy`` of f32, optionally under a Cond on thread
-  coordinates), ``cp.async.wait_group 0``, a barrier, an inner loop of two
-  shared-memory loads, a multiply and an add Accum, and a barrier; then an
-  epilogue and one ``Write C[r, c]``;
+  the copies, a barrier, an inner loop of two shared-memory loads, a multiply
+  and an add Accum, and a barrier; then an epilogue and one ``Write C[r, c]``.
+  The copies are ``CpAsyncCopy`` of f32 (optionally under a Cond on thread
+  coordinates) followed by ``cp.async.wait_group 0``, or plain copies: a
+  global ``Load`` whose value a shared ``Write`` stores unchanged;
 * every index expression is affine in the Tile axes and the two loop
   variables (``+``, ``-``, ``*`` by a literal).  The trailing Tile axes that
   make up one thread block index the threads; the leading ones index blocks;
@@ -132,20 +133,33 @@ def _staged_matmul(kop, shapes, dtypes, meta):
         return None
     if len(tail) != 1 or not (isinstance(tail[0], ir.Sync) and not tail[0].warp and not tail[0].barrier_id):
         return None
-    copies, waited = [], False
-    for s in head[:-1]:
+    copies, waited, asyncs = [], False, False
+    staged = list(head[:-1])
+    i = 0
+    while i < len(staged):
+        s = staged[i]
         if isinstance(s, ir.CpAsyncCopy) and not waited:
-            copies.append((s, None))
+            copies.append((_Copy.of_async(s), None))
+            asyncs = True
         elif (isinstance(s, ir.Cond) and not s.else_body and not waited
               and all(isinstance(t, ir.CpAsyncCopy) for t in s.body)):
-            copies += [(t, s.cond) for t in s.body]
+            copies += [(_Copy.of_async(t), s.cond) for t in s.body]
+            asyncs = True
         elif isinstance(s, ir.CpAsyncCommit) and not waited:
-            continue
+            pass
         elif isinstance(s, ir.CpAsyncWait) and int(s.group) == 0:
             waited = True
+        elif isinstance(s, ir.Load) and i + 1 < len(staged) and not waited:
+            # a plain copy: one element loaded from global memory, stored unchanged into shared memory
+            cp = _Copy.of_pair(s, staged[i + 1])
+            if cp is None:
+                return None
+            copies.append((cp, None))
+            i += 1
         else:
             return None
-    if not copies or not waited:
+        i += 1
+    if not copies or (asyncs and not waited):
         return None
     kb = list(ir.body_stmts(kk_loop.body))
     if len(kb) != 4 or not all(isinstance(s, ir.Load) for s in kb[:2]):
@@ -297,6 +311,28 @@ def _staged_matmul(kop, shapes, dtypes, meta):
         ir.Write(output=out.output, index=(ir.Var(ci), ir.Var(cj)), values=out.values, value_dtype=out.value_dtype),
     ))
     return ir.KernelOp(name=kop.name, body=(canon,), inputs=kop.inputs, outputs=kop.outputs)
+
+
+class _Copy:
+    """One staging copy: shared buffer and index, global source and index, bytes."""
+
+    def __init__(self, smem, smem_index, src, src_index, nbytes, lane_index=None):
+        self.smem, self.smem_index = smem, tuple(smem_index)
+        self.src, self.src_index = src, tuple(src_index)
+        self.nbytes, self.lane_index = int(nbytes), lane_index
+
+    @classmethod
+    def of_async(cls, s) -> "_Copy":
+        return cls(s.smem, s.smem_index, s.src, s.src_index, s.nbytes, s.lane_index)
+
+    @classmethod
+    def of_pair(cls, ld, wr) -> "_Copy | None":
+        if not (isinstance(wr, ir.Write) and not wr.atomic and len(ld.names) == 1 and len(wr.values) == 1
+                and wr.values[0] == ld.names[0]):
+            return None
+        if ir.canon_dtype(ld.dtype) not in (None, "f32") or ir.canon_dtype(wr.value_dtype) not in (None, "f32"):
+            return None
+        return cls(wr.output, wr.index, ld.input, ld.index, 4)
 
 
 def _size(shape) -> int:

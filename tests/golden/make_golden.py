@@ -760,6 +760,46 @@ def cond_load_case(cid: str, n: int) -> Case:
     return Case(cid, entry, graph, kern, family="pointwise", check={"kind": "ulp", "ulp": 0})
 
 
+def smem_matmul_case(cid: str, m: int, k: int, n: int) -> Case:
+    """The shared-memory matmul staged with plain copies: every thread of a
+    16x16 block loads one element of the A tile and one of the B tile from
+    global memory and stores it into shared memory, then a barrier, the k loop
+    over the staged tiles, and a barrier before the next tile."""
+    ts = 16
+    entry = "k_matmul_smem"
+    lit = lambda v: Literal(v, "int")  # noqa: E731
+    at = lambda blk, thr: BinaryExpr("+", BinaryExpr("*", Var(blk), lit(ts)), thr)  # noqa: E731
+    row, col = at("bi", Var("ty")), at("bj", Var("tx"))
+    body = Tile(axes=(Axis("bi", Dim(m // ts)), Axis("bj", Dim(n // ts)), Axis("ty", Dim(ts)),
+                      Axis("tx", Dim(ts))), body=(
+        Smem("As", (ts, ts), "float", 16),
+        Smem("Bs", (ts, ts), "float", 16),
+        Init("acc", 0.0, dtype=F32),
+        Loop(axis=Axis("kt", Dim(k // ts)), body=(
+            Load(names=("ga",), input="A", index=(row, at("kt", Var("tx"))), dtype=F32),
+            Write(output="As", index=(Var("ty"), Var("tx")), values=("ga",), value_dtype=F32),
+            Load(names=("gb",), input="B", index=(at("kt", Var("ty")), col), dtype=F32),
+            Write(output="Bs", index=(Var("ty"), Var("tx")), values=("gb",), value_dtype=F32),
+            Sync(),
+            Loop(axis=Axis("kk", Dim(ts)), body=(
+                Load(names=("a",), input="As", index=(Var("ty"), Var("kk")), dtype=F32),
+                Load(names=("b",), input="Bs", index=(Var("kk"), Var("tx")), dtype=F32),
+                Assign("p", EW("multiply"), ("a", "b"), F32),
+                Accum("acc", "p", EW("add"), F32, axes=("kk",)),
+            )),
+            Sync(),
+        )),
+        Write(output="C", index=(row, col), values=("acc",), value_dtype=F32),
+    ), block_threads=ts * ts)
+    graph = {"inputs": ["A", "B"], "outputs": ["C"], "nodes": {
+        "A": _input("A", [m, k]), "B": _input("B", [k, n]),
+        "C": _kernel(entry, body, ["A", "B"], [("C", [m, n], "f32")])}}
+    kern = _meta_kernel("C", entry, ["A", "B", "C"], [(m // ts) * (n // ts), 1, 1], [ts * ts, 1, 1], [
+        _arg("A", [m, k], init=NORM(), seed=0), _arg("B", [k, n], init=NORM(), seed=1),
+        _arg("C", [m, n], output=True)])
+    return Case(cid, entry, graph, kern, family="gemm", check={"kind": "ulp", "ulp": 0})
+
+
 def pre_carry_case(cid: str, n: int) -> Case:
     """Values carried between statements by Carry and read back by Pre
     (compile.py:2860-2888): two slots of one carrier, and a carrier with no
@@ -1133,6 +1173,7 @@ def all_cases() -> list[Case]:
     cases.append(cpasync_matmul_case("s_cpasync_matmul_64x48x80", 64, 48, 80))
     cases.append(cpasync_matmul_case("s_cpasync16_matmul_32x64x48", 32, 64, 48, wide=True))
     cases.append(pre_carry_case("s_pre_carry_500", 500))
+    cases.append(smem_matmul_case("s_smem_matmul_48x32x64", 48, 32, 64))
     cases.append(cond_load_case("p_cond_load_300", 300))
     cases.append(raster_matmul_case("s_raster_matmul_48x40x64", 48, 40, 64, 4))
     cases.append(aux_threads_case("s_aux_add_1000", 1000))

@@ -214,3 +214,41 @@ def test_near_miss_schedules_keep_their_own_schedule(knob):
     assert canon.staged_matmul(kop, shapes, dtypes, meta) is None
     low = compiler.lower(kop, shapes, dtypes, ["A", "B", "C"], meta)
     assert low.kernel.family == "schedule"
+
+
+def _plain_copy_kop(swap: bool):
+    """The s_smem_matmul fixture's schedule; ``swap`` stores each loaded element into the other buffer."""
+    from emmy_ptx_compiler_b200 import ir
+    F32 = ir.DataType("f32", "float32", 4)
+    ts, m, k, n = 16, 48, 32, 48
+    V, L = ir.Var, lambda v: ir.Literal(v, "int")  # noqa: E731
+    at = lambda blk, thr: ir.BinaryExpr("+", ir.BinaryExpr("*", V(blk), L(ts)), thr)  # noqa: E731
+    row, col = at("bi", V("ty")), at("bj", V("tx"))
+    sa, sb = ("Bs", "As") if swap else ("As", "Bs")
+    tile = ir.Tile(axes=(ir.Axis("bi", m // ts), ir.Axis("bj", n // ts), ir.Axis("ty", ts), ir.Axis("tx", ts)),
+                   block_threads=ts * ts, body=(
+        ir.Smem("As", (ts, ts), "float", 16), ir.Smem("Bs", (ts, ts), "float", 16),
+        ir.Init("acc", 0.0, dtype=F32),
+        ir.Loop(axis=ir.Axis("kt", k // ts), body=(
+            ir.Load(names=("ga",), input="A", index=(row, at("kt", V("tx"))), dtype=F32),
+            ir.Write(output=sa, index=(V("ty"), V("tx")), values=("ga",), value_dtype=F32),
+            ir.Load(names=("gb",), input="B", index=(at("kt", V("ty")), col), dtype=F32),
+            ir.Write(output=sb, index=(V("ty"), V("tx")), values=("gb",), value_dtype=F32),
+            ir.Sync(),
+            ir.Loop(axis=ir.Axis("kk", ts), body=(
+                ir.Load(names=("a",), input="As", index=(V("ty"), V("kk")), dtype=F32),
+                ir.Load(names=("b",), input="Bs", index=(V("kk"), V("tx")), dtype=F32),
+                ir.Assign("p", ir.ElementwiseImpl("multiply"), ("a", "b"), F32),
+                ir.Accum("acc", "p", ir.ElementwiseImpl("add"), F32, axes=("kk",)))),
+            ir.Sync())),
+        ir.Write(output="C", index=(row, col), values=("acc",), value_dtype=F32)))
+    return (ir.KernelOp(name="k_plain", body=(tile,)), {"A": (m, k), "B": (k, n), "C": (m, n)},
+            {"A": "f32", "B": "f32", "C": "f32"})
+
+
+@pytest.mark.parametrize("swap", [False, True])
+def test_plain_copy_staging_is_proven_only_when_right(swap):
+    from emmy_ptx_compiler_b200.families import canon
+    kop, shapes, dtypes = _plain_copy_kop(swap)
+    got = canon.staged_matmul(kop, shapes, dtypes, {"block": [256, 1, 1]})
+    assert (got is None) == swap

@@ -170,7 +170,8 @@ def test_attention_c_restatement(cid):
         assert ok, why
 
 
-@pytest.mark.parametrize("cid", ["s_cpasync_matmul_64x48x80", "s_cpasync16_matmul_32x64x48"])
+@pytest.mark.parametrize("cid", ["s_cpasync_matmul_64x48x80", "s_cpasync16_matmul_32x64x48",
+                                 "s_smem_matmul_48x32x64"])
 def test_simt_oracle_on_cp_async_matmul_equals_sequential_fma(cid):
     """The oracle's lockstep SIMT evaluation of a cp.async-staged matmul
     schedule gives the sequential-fma GEMM (ora_gemm_seqfma_f32) bit for bit:
