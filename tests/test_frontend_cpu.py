@@ -94,3 +94,20 @@ def test_cli_unsupported_exits_2(tmp_path):
     assert p.returncode == 2
     assert "unsupported" in p.stderr
     assert p.stdout == ""
+
+
+@pytest.mark.parametrize("cid,entry", [("s_cpasync_matmul_64x48x80", "k_matmul_cpasync"),
+                                       ("s_pre_carry_500", "k_pre_carry"),
+                                       ("s_loose_nodes_32", "k_loose_nodes")])
+def test_cli_compiles_scheduled_irs(cid, entry, tmp_path):
+    """The CLI contract for IRs the fast families do not take as written (a staged
+    matmul, Pre/Carry, statements outside a Tile): exit 0, PTX only on stdout,
+    one sm_100a entry of the KernelOp's name (checked by the assembler)."""
+    p = _cli(str(next((CASES / cid).glob("*.ir.json"))))
+    assert p.returncode == 0, p.stderr
+    f = tmp_path / "out.ptx"
+    f.write_text(p.stdout)
+    v = subprocess.run(["ptxas", "-arch=sm_100a", "-v", "-o", str(tmp_path / "o.cubin"), str(f)],
+                       capture_output=True, text=True)
+    assert v.returncode == 0, v.stderr
+    assert f"Compiling entry function '{entry}' for 'sm_100a'" in v.stderr
