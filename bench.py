@@ -474,6 +474,9 @@ CPU_SAMPLES = {
     "c3": (4, "rows of 65536 reduced (sum and max) in the reference's strided schedule order"),
     "c4": (1, "a 2^20+3-element full sum in the reference's strided schedule order"),
     "c5": (1, "rows of A (1 x 8192) times B (8192 x 16384), sequential fma over k, plus bias and ReLU"),
+    "f_rmsnorm": (16, "rows of 8192 through the row-fused IR in the reference's order (strided sums, tree)"),
+    "f_softmax": (16, "rows of 8192 through the row-fused IR in the reference's order (strided sums, tree)"),
+    "f_l2norm": (16, "rows of 8192 through the row-fused IR in the reference's order (strided sums, tree)"),
     "a_attn": (64, "query rows of the naive attention IR over all 2048 keys (oracle.c restatement: scores and "
                    "exponentials once per key, sequential fma order)"),
 }
@@ -538,6 +541,17 @@ def _oracle_sample(cfg: str, rows: int):
         k2 = _scaled(kop, [("i", rows), ("j", N)])
         fn = lambda: interp.evaluate(k2, shp, dtypes, ins, {"C": (rows, N)})  # noqa: E731
         return fn, 2 * rows * N * K
+    if cfg in ("f_rmsnorm", "f_softmax", "f_l2norm"):
+        kop, meta, mk, shapes, dtypes = interp.load_case(CASES / case_id)
+        cols = int(shapes["x"][1])
+        axes = [(a.name, int(a.extent.value)) for a in list(kop.body)[0].axes]
+        shp = dict(shapes, x=(rows, cols), y=(rows, cols))
+        ins = {"x": rng.standard_normal((rows, cols), dtype=np.float32)}
+        if "w" in shapes:
+            ins["w"] = rng.uniform(0.5, 1.5, cols).astype(np.float32)
+        k2 = _scaled(kop, [(axes[0][0], rows)] + axes[1:])
+        fn = lambda: interp.evaluate(k2, shp, dtypes, ins, {"y": (rows, cols)})  # noqa: E731
+        return fn, 2 * rows * cols * 4 + (cols * 4 if "w" in shapes else 0)
     if cfg == "a_attn":
         # the C restatement of the naive attention IR (oracle/oracle.c), pinned to
         # the Python oracle and the reference's golden vectors by the CPU tests

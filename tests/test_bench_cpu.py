@@ -22,7 +22,7 @@ def _run(*args, env_extra=None):
     return [ln for ln in p.stdout.splitlines() if ln.strip()]
 
 
-@pytest.mark.parametrize("config,higher", [("c2", True), ("c1", False), ("a_attn", True)])
+@pytest.mark.parametrize("config,higher", [("c2", True), ("c1", False), ("a_attn", True), ("f_softmax", True)])
 def test_reference_arm_line(config, higher):
     lines = _run("--impl", "reference", "--config", config, "--steps", "2", "--warmup", "1")
     assert len(lines) == 1
