@@ -47,3 +47,24 @@ def test_launch_record_layout_matches_header():
     assert "EMMY_LR_MAGIC" in src and "emmy_status" in src
     hdr = (REPO / "include" / "emmy_launch_record.h").read_text()
     assert "uint32_t param_kind[EMMY_LR_MAX_PARAMS];" in hdr
+
+
+def test_new_entry_points_reject_bad_arguments_without_a_gpu():
+    """emmy_launch_ex needs explicit geometry; graphs need a caller stream and a
+    graph; run_host and graph_end need their pointers.  All refuse with
+    EMMY_ERR_INVALID before any driver call."""
+    import torch
+    from emmy_ptx_compiler_b200 import runtime
+    lib = runtime.lib()
+    if torch.cuda.is_available():
+        return
+    u32x3 = (ctypes.c_uint32 * 3)(1, 1, 1)
+    assert lib.emmy_launch_ex(None, None, 0, u32x3, u32x3, 0, 0) == -3
+    assert lib.emmy_graph_begin(0, 0) == -3                 # the legacy default stream cannot be recorded
+    assert lib.emmy_graph_end(0, 1, None) == -3
+    assert lib.emmy_graph_launch(None, 1) == -3
+    assert lib.emmy_graph_destroy(None) == 0                # destroying nothing is fine
+    assert lib.emmy_run_host(None, None, None, None, 0, 0) == -3
+    buf = ctypes.create_string_buffer(256)
+    lib.emmy_last_error(buf, 256)
+    assert b"NULL" in buf.value
