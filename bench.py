@@ -2,16 +2,25 @@
 """Benchmark of the emmy B200 backend on BASELINE.json's configurations.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2|c3|c4|c5]
+                    [--config c1|c2|c3|c4|c5|f_*|a_attn] [--only]
 
 One JSON line on stdout (rank 0).  A "step" is one pass of the hot path over
 one batch: one launch of the KernelOp compiled from the config's IR, on
 inputs already resident in HBM (``value``), and the same call through the
 C ABI on pinned host buffers with the copies inside the timed region
 (``e2e``).  The default workload is BASELINE configs[1] (the metric's
-HBM-bound pointwise chain, y = GELU_tanh(x*s + t) on f32 [16384, 16384]).
-Under torchrun every rank runs its own full-size shard (weak scaling, no
-data-path collective) and the slowest rank's device time is reported.
+HBM-bound pointwise chain, y = GELU_tanh(x*s + t) on f32 [16384, 16384]);
+the same run then times configs[2..4] (C3 row sum+max, C4 full sum, C5
+GEMM) the same way and reports them under ``configs``, each with its own
+roofline, e2e, reference-PTX and CPU baselines.
+
+Under torchrun (N > 1) the BASELINE problem is split over the ranks
+(strong scaling): rows / N per rank for C2, C3 and C5 (B replicated), 2^31 / N
+elements for C4 with the per-rank partial sums combined by an NCCL
+all-reduce inside every step; each rank compiles the KernelOp for its own
+shard (emmy_ptx_compiler_b200.shard) and checks its own result.  A weak
+pass (every rank a full-size copy) is reported beside it under ``weak``.
+The slowest rank's device time is reported.
 
 ``--impl reference`` times the reference's CPU restatement (oracle/) on
 the host cores, for the same metric, on a bounded sample per step.
@@ -182,16 +191,16 @@ class ClockSampler:
 # ---------------------------------------------------------------------------- inputs
 
 
-def make_inputs(cfg: str, spec, rank: int, device: str):
-    """Seeded synthetic inputs with the config's shapes and distributions
-    (generated on the device; per-rank seeds for weak scaling)."""
+def make_inputs(spec, shapes: dict, rank: int, device: str, row0: dict | None = None):
+    """Seeded synthetic inputs with the config's distributions and the shapes
+    this rank holds (its shard under strong scaling, generated on the device)."""
     import torch
     g = torch.Generator(device=device)
     g.manual_seed(1234 + 7919 * rank)
     out = {}
     for name in spec.arg_order:
         a = spec.args[name]
-        shape = tuple(a["shape"]) or (1,)
+        shape = tuple(shapes.get(name, a["shape"])) or (1,)
         dt = {"f32": torch.float32, "bf16": torch.bfloat16}[a.get("dtype", "f32")]
         if a.get("output"):
             out[name] = torch.empty(shape, dtype=dt, device=device)
@@ -224,7 +233,7 @@ def combine_step(cfg: str, bufs: dict, world: int):
     """The path's one exchange: a full-array sum over N GPUs adds the per-GPU
     partial sums (NCCL all-reduce of one float, enqueued on the current
     stream).  Every other config shards with no collective."""
-    if cfg != "c4" or world <= 1:
+    if CONFIGS[cfg][2] != "hbm" or cfg != "c4" or world <= 1:
         return lambda: None
     import torch
     out = bufs["sum_1"]
@@ -234,234 +243,435 @@ def combine_step(cfg: str, bufs: dict, world: int):
 # ---------------------------------------------------------------------------- our arm
 
 
-def run_ours(args, rank: int, world: int, local: int) -> dict | None:
-    import torch
-    from emmy_ptx_compiler_b200 import compiler, harness, runtime
+class Job:
+    """One config compiled and resident on this rank: the whole problem
+    (N = 1, or weak scaling), or this rank's shard of it (strong scaling,
+    emmy_ptx_compiler_b200.shard)."""
 
-    device = f"cuda:{local}"
-    torch.cuda.set_device(local)
-    case_id, unit, bound, units, workload = CONFIGS[args.config]
-    spec = harness.load_case(CASES / case_id)
-    bundle = compiler.compile_bundle(spec.ir_path, want_cubin=True)
-    runtime.init(local)
-    mod = runtime.Module(bundle["cubin"], spec.entry, local)
-    # the geometry actually launched (pointwise grids are sized by the loader from occupancy)
-    launch = {"grid": list(mod.grid), "block": list(mod.block), "smem": mod.smem}
-    bufs = make_inputs(args.config, spec, rank, device)
-    order = [bufs[n] for n in spec.arg_order]
-    stream = torch.cuda.current_stream(local).cuda_stream
+    def __init__(self, cfg: str, rank: int, world: int, local: int, mode: str):
+        import torch
+        from emmy_ptx_compiler_b200 import compiler, frontend, harness, runtime, shard
+        self.cfg, self.rank, self.world, self.local, self.mode = cfg, rank, world, local, mode
+        self.device = f"cuda:{local}"
+        case_id, self.unit, self.bound, self.units, self.workload = CONFIGS[cfg]
+        self.case_id = case_id
+        self.spec = harness.load_case(CASES / case_id)
+        raw = json.loads(self.spec.ir_path.read_text())
+        info = frontend.load_graph(raw)
+        args = frontend.arg_order_for(info.kop, self.spec.kernel)
+        shapes, dtypes = frontend.load_shapes(raw, info.kop, self.spec.kernel)
+        self.shard = None
+        if mode == "strong" and world > 1:
+            self.shard = shard.shard_kernel(info.kop, shapes, world, rank)
+            comp = compiler.Compiler(self.shard.kop, self.shard.shapes, dtypes, args, self.spec.kernel)
+            self.shapes = self.shard.shapes
+        else:
+            comp = compiler.Compiler(info.kop, shapes, dtypes, args, self.spec.kernel)
+            self.shapes = shapes
+        self.notes = comp.lower().kernel.notes
+        runtime.init(local)
+        self.mod = runtime.Module(comp.cubin(), self.spec.entry, local)
+        self.launch = {"grid": list(self.mod.grid), "block": list(self.mod.block), "smem": self.mod.smem}
+        self.bufs = make_inputs(self.spec, self.shapes, rank, self.device)
+        self.order = [self.bufs[n] for n in self.spec.arg_order]
+        self.stream = torch.cuda.current_stream(local).cuda_stream
+        self.go = self.mod.bind(self.order, stream=self.stream)
+        self.partial = self.shard is not None and self.shard.mode == "partial"
+        self.step = self.go
+        if self.partial:
+            combine = combine_step(cfg, self.bufs, world)
+            self.step = lambda: (self.go(), combine())
+
+    def close(self):
+        self.mod.close()
+
+
+def _timed(job, steps: int, warmup: int, world: int, rank: int, clocks_active: bool):
+    """Device time of ``steps`` steps after ``warmup``: max over ranks, plus the clock record."""
+    import torch
+    local = job.local
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
 
-    combine = combine_step(args.config, bufs, world)
-    go = mod.bind(order, stream=stream)  # argument words prepared once: one C-ABI call per launch
-    step = go if args.config != "c4" or world <= 1 else (lambda: (go(), combine()))
-    xchg = None
-    if args.config == "c4" and world > 1 and args.combine == "fused":
-        # one kernel per GPU: shard sum fused with the combine over NVLink peer memory
-        xchg = runtime.Exchange(local, world, rank)
-        handles = [None] * world
-        torch.distributed.all_gather_object(handles, xchg.handle)
-        xchg.connect(handles)
-        x_in, total, n_in = bufs["x"], bufs["sum_1"], bufs["x"].numel()
-        step = lambda: xchg.sum_allreduce(x_in, n_in, total, timeout_ms=10000, stream=stream)  # noqa: E731
-
-    for _ in range(args.warmup):
-        step()
+    for _ in range(warmup):
+        job.step()
     torch.cuda.synchronize(local)
-    st = mod.status()
+    st = job.mod.status()
     if st:
-        raise RuntimeError(f"kernel status 0x{st:x} during warm-up")
+        raise RuntimeError(f"{job.cfg}: kernel status 0x{st:x} during warm-up")
     clocks = ClockSampler(list(range(min(world, torch.cuda.device_count()))) if world > 1 else [local],
-                          active=(rank == 0))
+                          active=clocks_active and rank == 0)
     # inputs smaller than L2 would stay cached across steps: each step then runs
     # after a write of a buffer larger than L2 and is timed by its own events
-    footprint = sum(t.numel() * t.element_size() for t in bufs.values())
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device) if footprint < L2_BYTES else None
+    footprint = sum(t.numel() * t.element_size() for t in job.bufs.values())
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=job.device) if footprint < L2_BYTES else None
     barrier()
     torch.cuda.synchronize(local)
     clocks.start()
     if flush is None:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(args.steps):
-            step()
+        for _ in range(steps):
+            job.step()
         e1.record()
         torch.cuda.synchronize(local)
         timed_ms = e0.elapsed_time(e1)
     else:
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in range(args.steps)]
+              for _ in range(steps)]
         for a, b in ev:
             flush.fill_(1)
             a.record()
-            step()
+            job.step()
             b.record()
         torch.cuda.synchronize(local)
         timed_ms = sum(a.elapsed_time(b) for a, b in ev)
     clocks.stop()
     barrier()
     clocks.close()
-    if xchg is not None:
-        xst = xchg.status()
-        xchg.close()
-        if xst:
-            raise RuntimeError(f"fused sum + combine status 0x{xst:x} (a peer did not arrive in time)")
-    ms_max = max_over_ranks(timed_ms, world, device)
-    per_launch_ms = ms_max / args.steps
-    latency = unit == "us"
-    graph = None
-    if latency:
-        # back to back: the rate at which the host can submit bound launches
-        torch.cuda.synchronize(local)
-        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        b0.record()
-        for _ in range(args.steps):
-            go()
-        b1.record()
-        torch.cuda.synchronize(local)
-        back_to_back_us = b0.elapsed_time(b1) * 1e3 / args.steps
-        # the same launches recorded once as a CUDA graph and replayed: device
-        # time per launch without the host's per-launch submission cost
-        gs = torch.cuda.Stream(device=local)
-        torch.cuda.synchronize(local)
-        with runtime.Graph.record(local, gs.cuda_stream) as g:
-            for _ in range(args.steps):
-                mod.launch(order, stream=gs.cuda_stream)
-        for _ in range(args.warmup):
-            g.launch(gs.cuda_stream)
-        torch.cuda.synchronize(local)
-        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        g0.record(gs)
-        g.launch(gs.cuda_stream)
-        g1.record(gs)
-        torch.cuda.synchronize(local)
-        graph = {"graph_replay_us_per_launch": round(g0.elapsed_time(g1) * 1e3 / args.steps, 3),
-                 "launches_per_graph": args.steps, "graph_path": "emmy_graph_begin/end/launch (C ABI)",
-                 "back_to_back_us_per_launch": round(back_to_back_us, 3),
-                 "note": "value: one launch timed alone after an L2 flush; the back-to-back and graph "
-                         "figures run with L2 warm"}
-        g.close()
-    if latency:
-        value = achieved = per_launch_ms * 1e3
-    else:
-        value = units * world * args.steps / (ms_max / 1e3) / (1e9 if unit == "GB/s" else 1e12)
-        achieved = units / (per_launch_ms / 1e3) / (1e9 if unit == "GB/s" else 1e12)
-    pk, pk_kind = peaks()
-    peak = pk["hbm_gbs"] if bound == "hbm" else pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
-    if bound == "fp32":
-        peak, pk_kind = round(FP32_NOMINAL_TFLOPS, 1), "nominal"
-    peak_key = {"hbm": "hbm_gbs", "tensor": "bf16_tflops", "fp32": "fp32 CUDA cores", "latency": "none"}[bound]
-    traffic = DRAM_TRAFFIC.get(case_id)
+    st = job.mod.status()
+    if st:
+        raise RuntimeError(f"{job.cfg}: kernel status 0x{st:x} in the timed region")
+    l2 = ("inputs larger than L2 (126 MB), no flush needed" if flush is None else
+          f"working set {footprint} B < L2: a {L2_FLUSH_BYTES >> 20} MiB buffer is written before every "
+          "timed step, and each step is timed by its own CUDA events")
+    return max_over_ranks(timed_ms, world, job.device), clocks.summary(), l2
 
-    # e2e: the C-ABI host-buffer call, copies in the timed region
-    host = {}
-    nbytes, roles, ptrs = [], [], []
-    for name in spec.arg_order:
-        t = bufs[name]
+
+def _e2e(job, steps: int, world: int) -> dict:
+    """The same metric through the C-ABI host-buffer call (emmy_run_host):
+    pinned host inputs copied in and outputs copied out inside the timed
+    region, every step."""
+    import torch
+    from emmy_ptx_compiler_b200 import runtime
+    nbytes, roles, ptrs, host = [], [], [], {}
+    for name in job.spec.arg_order:
+        t = job.bufs[name]
         h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
-        if not spec.args[name].get("output"):
+        out = job.spec.args[name].get("output")
+        if not out:
             h.copy_(t)
         host[name] = h
         ptrs.append(h.data_ptr())
         nbytes.append(h.numel() * h.element_size())
-        roles.append(runtime.EMMY_ROLE_OUT if spec.args[name].get("output") else runtime.EMMY_ROLE_IN)
-    e2e_steps = max(1, args.steps if latency else min(args.steps, 5))
-    mod.run_host(ptrs, nbytes, roles, stream=stream)  # warm the module's device buffers
-    barrier()
-    torch.cuda.synchronize(local)
+        roles.append(runtime.EMMY_ROLE_OUT if out else runtime.EMMY_ROLE_IN)
+    job.mod.run_host(ptrs, nbytes, roles, stream=job.stream)  # warm the module's device buffers
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(job.local)
     t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        mod.run_host(ptrs, nbytes, roles, stream=stream)
-    e2e_s = max_over_ranks(time.perf_counter() - t0, world, device)
+    for _ in range(steps):
+        job.mod.run_host(ptrs, nbytes, roles, stream=job.stream)
+        if job.partial:
+            # the per-GPU partials of the host call's output are combined on the host's behalf
+            host_out = host[job.spec.outputs[0]]
+            part = host_out.to(job.device)
+            torch.distributed.all_reduce(part, op=torch.distributed.ReduceOp.SUM)
+            host_out.copy_(part)
+    el = max_over_ranks(time.perf_counter() - t0, world, job.device)
     h2d = sum(b for b, r in zip(nbytes, roles) if r == runtime.EMMY_ROLE_IN)
     d2h = sum(b for b, r in zip(nbytes, roles) if r == runtime.EMMY_ROLE_OUT)
-    e2e_value = (e2e_s / e2e_steps * 1e6 if latency
-                 else units * world * e2e_steps / e2e_s / (1e9 if unit == "GB/s" else 1e12))
+    latency = job.unit == "us"
+    units = job.units * (world if job.mode == "weak" else 1)
+    value = el / steps * 1e6 if latency else units * steps / el / _units_scale(job.unit)
+    return {"value": round(value, 3), "unit": job.unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "steps": steps, "path": "emmy_run_host (C ABI) on pinned host buffers"
+            + (", per rank on its shard" if world > 1 else "")}
 
-    ref_ptx = None
-    if rank == 0 and world == 1 and (args.config in ("c1", "c2") or args.config[:2] in ("f_", "a_")) \
-            and not args.no_ref_ptx:
-        ref_ptx = time_reference_ptx(spec, bufs, local, units, unit)
 
-    mod.close()
+def _verify(job) -> dict:
+    """The job checks its own result (multi-GPU runs): sharded outputs bit-equal
+    to the whole-problem kernel on sampled rows (pointwise, GEMM: the same
+    module's unit-range launch on those rows), row maxima exact and row sums
+    within rtol 1e-5 of an f64 sum (row reductions), and the combined total
+    of a full-array sum within rtol 1e-5 of an f64 checksum over all GPUs."""
+    import torch
+    from emmy_ptx_compiler_b200 import compiler, runtime
+    cfg, sh = job.cfg, job.shard
+    if sh is None:
+        return {"checked": False}
+    torch.cuda.synchronize(job.local)
+    if cfg == "c4":
+        part = job.bufs["x"].double().sum().reshape(1)
+        torch.distributed.all_reduce(part, op=torch.distributed.ReduceOp.SUM)
+        got, want = float(job.bufs["sum_1"].double().item()), float(part.item())
+        ok = abs(got - want) <= 1e-5 * abs(want) + 0.05
+        return {"checked": True, "ok": bool(ok), "what": "combined total vs f64 checksum of all shards, rtol 1e-5",
+                "total": got, "f64": want}
+    if cfg == "c3":
+        x = job.bufs["x"]
+        mx_ok = bool(torch.equal(job.bufs["max_1"], x.max(dim=1).values))
+        ref = x.double().sum(dim=1)
+        err = (job.bufs["sum_1"].double() - ref).abs()
+        s_ok = bool((err <= 1e-5 * ref.abs() + 1e-3).all())
+        return {"checked": True, "ok": mx_ok and s_ok, "what": "row maxima exact; row sums vs f64 within rtol 1e-5",
+                "rows": int(x.shape[0])}
+    # pointwise / GEMM: the whole-problem module on two sampled rows of this shard, by unit ranges
+    bundle = compiler.compile_bundle(job.spec.ir_path, want_cubin=True)
+    full = runtime.Module(bundle["cubin"], job.spec.entry, job.local)
+    total, align, per_unit = full.unit_range()
+    rows_total = sh.extent
+    unit_per_row = total // rows_total
+    ok, rows = True, []
+    for r in sorted({0, sh.hi - sh.lo - 1}):
+        g = sh.lo + r
+        b, e = g * unit_per_row, (g + 1) * unit_per_row
+        if b % align or (e % align and e != total):
+            continue
+        words = []
+        tmp = {}
+        for name, t, pb in zip(job.spec.arg_order, job.order, per_unit):
+            if name in sh.buffers and pb:
+                if job.spec.args[name].get("output"):
+                    tmp[name] = torch.empty_like(t[r:r + 1])
+                    words.append(tmp[name].data_ptr() - b * pb)
+                else:
+                    words.append(t[r:r + 1].data_ptr() - b * pb)
+            else:
+                words.append(t.data_ptr())
+        full.launch_range(words, b, e, stream=job.stream)
+        torch.cuda.synchronize(job.local)
+        out = job.spec.outputs[0]
+        same = bool(torch.equal(tmp[out].view(-1).view(torch.int16 if tmp[out].dtype == torch.bfloat16
+                                                          else torch.int32),
+                                job.bufs[out][r:r + 1].view(-1).view(torch.int16 if tmp[out].dtype == torch.bfloat16
+                                                                      else torch.int32)))
+        ok = ok and same
+        rows.append(g)
+    full.close()
+    return {"checked": bool(rows), "ok": ok, "rows": rows,
+            "what": "shard output bit-equal to the whole-problem kernel (unit-range launch) on sampled rows"}
+
+
+def measure(cfg: str, args, rank: int, world: int, local: int, mode: str, *, extras: bool = True) -> dict:
+    """One config: device-timed value, roofline, e2e, and (rank 0, N = 1) the
+    reference-PTX and CPU baselines."""
+    job = Job(cfg, rank, world, local, mode)
+    try:
+        ms_max, clocks, l2 = _timed(job, args.steps, args.warmup, world, rank, clocks_active=True)
+        check = _verify(job) if world > 1 and mode == "strong" else None
+        latency = job.unit == "us"
+        per_launch_ms = ms_max / args.steps
+        scale = 1 if latency else _units_scale(job.unit)
+        job_units = job.units * (world if mode == "weak" else 1)
+        if latency:
+            value = achieved = per_launch_ms * 1e3
+        else:
+            value = job_units * args.steps / (ms_max / 1e3) / scale
+            # per GPU: the units one launch processes on the slowest rank
+            achieved = job_units / world / (per_launch_ms / 1e3) / scale
+        e2e_steps = max(1, args.steps if latency else min(args.steps, 5))
+        e2e = _e2e(job, e2e_steps, world) if extras else None
+        ref_ptx = cpu = None
+        if rank == 0 and world == 1 and extras:
+            if not args.no_ref_ptx:
+                ref_ptx = time_reference_ptx(cfg, job, job.local, job.units, job.unit)
+            if not args.no_cpu_baseline:
+                cpu = cpu_baseline(cfg, seconds=args.cpu_seconds if cfg == args.config else args.cpu_seconds / 2)
+        graph = latency_extras(job, args) if latency and extras else None
+    finally:
+        job.close()
+    pk, pk_kind = peaks()
+    bound = job.bound
+    peak = pk["hbm_gbs"] if bound == "hbm" else pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+    if bound == "fp32":
+        peak, pk_kind = round(FP32_NOMINAL_TFLOPS, 1), "nominal"
+    peak_key = {"hbm": "hbm_gbs", "tensor": "bf16_tflops (burst: one kernel timed alone)",
+                "fp32": "fp32 CUDA cores", "latency": "none"}[bound]
+    traffic = DRAM_TRAFFIC.get(job.case_id) if world == 1 else None
+    entry = {
+        "value": round(value, 2), "unit": job.unit, "ms_per_step": round(per_launch_ms, 4),
+        "workload": job.workload, "case": job.case_id, "launch": job.launch, "l2": l2,
+        "roofline": ({"bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": job.unit,
+                      "frac": round(achieved / peak, 4), "traffic": traffic,
+                      "peak_source": f"{pk_kind} ({peak_key})", "units_per_launch": job_units // world,
+                      "per": "GPU (slowest rank)"} if not latency else
+                     {"bound": "latency", "achieved": round(achieved, 3), "peak": None, "unit": "us", "frac": None,
+                      "traffic": None, "units_per_launch": job.units,
+                      "note": "768 bytes per launch: bounded by launch latency, not by HBM or tensor cores"}),
+        "clocks": clocks,
+        "gpu_launches": args.steps,
+    }
+    if bound == "tensor" and not latency:
+        entry["roofline"]["frac_of_sustained"] = round(achieved / pk.get("bf16_tflops_sustained",
+                                                                          FALLBACK_PEAKS["bf16_tflops_sustained"]), 4)
+    if e2e is not None:
+        entry["e2e"] = e2e
+    if ref_ptx is not None:
+        entry["reference_ptx_gpu"] = ref_ptx
+    if cpu is not None:
+        entry["cpu_baseline"] = cpu
+    if graph is not None:
+        entry["latency"] = graph
+    if check is not None:
+        entry["check"] = check
+    if world > 1:
+        sh = job.shard
+        entry["parallelism"] = (
+            f"strong scaling: the BASELINE problem split over {world} ranks, rows [lo, hi) of axis "
+            f"'{sh.axis}' ({sh.extent // world} of {sh.extent}) per rank"
+            + ("; the per-rank partial sums are combined by an NCCL all-reduce inside every step"
+               if sh.mode == "partial" else "; no collective") if mode == "strong" else
+            f"weak scaling: {world} ranks, each its own full-size copy of the problem; "
+            + ("per-rank sums combined by an NCCL all-reduce in every step" if cfg == "c4" else "no collective"))
+    return entry
+
+
+def latency_extras(job, args) -> dict:
+    """C1: back-to-back launch rate, and the same launches replayed as a CUDA graph."""
+    import torch
+    from emmy_ptx_compiler_b200 import runtime
+    local = job.local
+    torch.cuda.synchronize(local)
+    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    b0.record()
+    for _ in range(args.steps):
+        job.go()
+    b1.record()
+    torch.cuda.synchronize(local)
+    back_to_back_us = b0.elapsed_time(b1) * 1e3 / args.steps
+    gs = torch.cuda.Stream(device=local)
+    torch.cuda.synchronize(local)
+    with runtime.Graph.record(local, gs.cuda_stream) as g:
+        for _ in range(args.steps):
+            job.mod.launch(job.order, stream=gs.cuda_stream)
+    for _ in range(args.warmup):
+        g.launch(gs.cuda_stream)
+    torch.cuda.synchronize(local)
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(gs)
+    g.launch(gs.cuda_stream)
+    g1.record(gs)
+    torch.cuda.synchronize(local)
+    out = {"graph_replay_us_per_launch": round(g0.elapsed_time(g1) * 1e3 / args.steps, 3),
+           "launches_per_graph": args.steps, "graph_path": "emmy_graph_begin/end/launch (C ABI)",
+           "back_to_back_us_per_launch": round(back_to_back_us, 3),
+           "note": "value: one launch timed alone after an L2 flush; the back-to-back and graph "
+                   "figures run with L2 warm"}
+    g.close()
+    return out
+
+
+def run_ours(args, rank: int, world: int, local: int) -> dict | None:
+    import torch
+    torch.cuda.set_device(local)
+    mode = "strong" if world > 1 else "single"
+    main_cfg = args.config
+    entry = measure(main_cfg, args, rank, world, local, mode)
+    weak = None
+    if world > 1 and not args.only:
+        weak = measure(main_cfg, args, rank, world, local, "weak", extras=False)
+    others = {}
+    if main_cfg == "c2" and not args.only:
+        for cfg in ("c3", "c4", "c5"):
+            others[cfg] = measure(cfg, args, rank, world, local, mode)
+            if weak is not None and cfg in ("c4",):
+                others[cfg]["weak"] = {k: v for k, v in measure(cfg, args, rank, world, local, "weak",
+                                                                 extras=False).items()
+                                       if k in ("value", "unit", "ms_per_step", "parallelism")}
     if rank != 0:
         return None
+    latency = entry["unit"] == "us"
+    dtype = {"c5": "bf16"}.get(main_cfg, "f32")
     line = {
-        "metric": METRIC, "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": not latency,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32" if args.config != "c5" else "bf16",
+        "metric": METRIC, "value": entry["value"], "unit": entry["unit"], "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": entry["ms_per_step"], "higher_is_better": not latency,
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": dtype,
         "data": "synthetic (seeded on device, BASELINE distributions)",
-        "config": {"workload": workload, "case": case_id, "rows_per_rank": spec.args[spec.arg_order[0]]["shape"][0],
-                   "parallelism": f"{world} ranks, each its own full-size shard; no collective",
-                   "l2": ("inputs larger than L2 (126 MB), no flush needed" if flush is None else
-                          f"working set {footprint} B < L2: a {L2_FLUSH_BYTES >> 20} MiB buffer is written before "
-                          "every timed step, and each step is timed by its own CUDA events"),
-                   "launch": launch},
-        "roofline": ({"bound": bound, "achieved": round(achieved, 2), "peak": peak,
-                      "unit": unit, "frac": round(achieved / peak, 4), "traffic": traffic,
-                      "peak_source": f"{pk_kind} ({peak_key})",
-                      "units_per_launch": units} if not latency else
-                     {"bound": "latency", "achieved": round(achieved, 3), "peak": None, "unit": "us", "frac": None,
-                      "traffic": None, "units_per_launch": units,
-                      "note": "768 bytes per launch: bounded by launch latency, not by HBM or tensor cores"}),
-        "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-                "path": "emmy_run_host (C ABI) on pinned host buffers"},
-        "gpu_launches": args.steps,
-        "clocks": clocks.summary(),
+        "config": {"workload": entry["workload"], "case": entry["case"],
+                   "parallelism": entry.get("parallelism", "1 GPU"), "l2": entry["l2"], "launch": entry["launch"]},
+        "roofline": entry["roofline"],
+        "e2e": entry.get("e2e"),
+        "gpu_launches": entry["gpu_launches"],
+        "clocks": entry["clocks"],
     }
-    if ref_ptx is not None:
-        line["reference_ptx_gpu"] = ref_ptx
-    if graph is not None:
-        line["latency"] = graph
-    if args.config == "c4" and world > 1:
-        line["config"]["parallelism"] = (
-            f"{world} ranks, each its own 2^31-element shard; every step is one kernel per GPU that sums "
-            "the shard and combines the per-GPU totals over NVLink peer memory (emmy_sum_f32_allreduce)"
-            if args.combine == "fused" else
-            f"{world} ranks, each its own 2^31-element shard; the per-rank sums are combined by an NCCL "
-            "all-reduce inside every step")
-        line["gpu_launches"] = args.steps
-    if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args.config, seconds=args.cpu_seconds)
+    for k in ("reference_ptx_gpu", "cpu_baseline", "latency", "check"):
+        if k in entry:
+            line[k] = entry[k]
+    if weak is not None:
+        line["weak"] = {k: weak[k] for k in ("value", "unit", "ms_per_step", "parallelism", "clocks")}
+    if others:
+        line["configs"] = others
+        line["gpu_launches"] = args.steps * (1 + len(others))
+        line["configs_note"] = ("C3-C5 of BASELINE, each timed like the headline line (same steps, warm-up and "
+                                "timing rules) in the same process after it; gpu_launches counts every config's "
+                                "timed launches")
     return line
 
 
-def time_reference_ptx(spec, bufs, local: int, units: int, unit: str) -> dict:
-    """The reference compiler's own PTX for the same IR on the same B200
-    (JIT-loaded, meta.json launch), on the same device buffers."""
+def time_reference_ptx(cfg: str, job, local: int, units: int, unit: str) -> dict:
+    """The reference compiler's own PTX for the same work on the same B200
+    (JIT-loaded, meta.json launch), on the same device buffers.
+
+    * c4: the reference indexes in s32 and cannot address 2^31 elements in
+      one launch; its route is its 2^28-element IR launched 8 times over
+      consecutive chunks (one step = the 8 launches);
+    * c5: the reference cannot lower bf16 loads; its route is its f32 naive
+      matmul IR on f32 copies of A and B, over the whole problem."""
     import torch
-    from emmy_ptx_compiler_b200 import runtime
-    ref = spec.root / "ref.ptx"
-    if not ref.is_file():
-        return {"unavailable": "no reference PTX for this IR"}
-    mod = runtime.Module(ref.read_bytes(), spec.entry, local)
-    g, b = spec.kernel["grid"], spec.kernel["block"]
-    order = [bufs[n] for n in spec.arg_order]
+    from emmy_ptx_compiler_b200 import harness, runtime
+    spec = job.spec
     stream = torch.cuda.current_stream(local).cuda_stream
-    for _ in range(3):
-        mod.launch(order, stream=stream, grid=g, block=b)
+    plan = []   # (module, args, grid, block, work units of this launch)
+    mods = []
+    if cfg == "c4":
+        rdir = CASES / "c4_sum_chunk_2p28"
+        rs = harness.load_case(rdir)
+        m = runtime.Module((rdir / "ref.ptx").read_bytes(), rs.entry, local)
+        mods.append(m)
+        x, chunk = job.bufs["x"], rs.args["x"]["shape"][0]
+        parts = torch.zeros(x.numel() // chunk, dtype=torch.float32, device=job.device)
+        for c in range(x.numel() // chunk):
+            plan.append((m, [x[c * chunk:(c + 1) * chunk], parts[c:c + 1]], rs.kernel["grid"], rs.kernel["block"]))
+        route = f"{len(plan)} launches of the reference's {chunk}-element full-sum IR over consecutive chunks"
+        work = units
+    elif cfg == "c5":
+        rdir = CASES / "c5_gemm_full" / "ref_f32"
+        rs = harness.load_case(rdir)
+        m = runtime.Module((rdir / "ref.ptx").read_bytes(), rs.entry, local)
+        mods.append(m)
+        A, B = job.bufs["A"].float(), job.bufs["B"].float()
+        out = torch.zeros((A.shape[0], B.shape[1]), dtype=torch.float32, device=job.device)
+        plan.append((m, [A, B, job.bufs["bias"], out], rs.kernel["grid"], rs.kernel["block"]))
+        route = "the reference's f32 naive matmul IR on f32 copies of A and B (it cannot lower bf16 loads)"
+        work = units
+    else:
+        ref = spec.root / "ref.ptx"
+        if not ref.is_file():
+            return {"unavailable": "no reference PTX for this IR"}
+        m = runtime.Module(ref.read_bytes(), spec.entry, local)
+        mods.append(m)
+        plan.append((m, [job.bufs[n] for n in spec.arg_order], spec.kernel["grid"], spec.kernel["block"]))
+        route = "the reference compiler's PTX for the same IR, meta.json launch"
+        work = units
+
+    def one():
+        for m, a, g, b in plan:
+            m.launch(a, stream=stream, grid=g, block=b)
+
+    for _ in range(1 if cfg in ("c4", "c5") else 3):
+        one()
     torch.cuda.synchronize(local)
-    n = 50 if unit == "us" else 5
-    footprint = sum(t.numel() * t.element_size() for t in bufs.values())
-    flush = (torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=f"cuda:{local}")
+    n = 50 if unit == "us" else (2 if cfg in ("c4", "c5") else 5)
+    footprint = sum(t.numel() * t.element_size() for t in job.bufs.values())
+    flush = (torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=job.device)
              if footprint < L2_BYTES else None)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
     for e0, e1 in ev:    # same rule as our arm: an L2 flush before each launch of a small working set
         if flush is not None:
             flush.fill_(1)
         e0.record()
-        mod.launch(order, stream=stream, grid=g, block=b)
+        one()
         e1.record()
     torch.cuda.synchronize(local)
     ms = sum(e0.elapsed_time(e1) for e0, e1 in ev) / n
-    mod.close()
-    value = ms * 1e3 if unit == "us" else units / (ms / 1e3) / (1e9 if unit == "GB/s" else 1e12)
-    return {"value": round(value, 3), "unit": unit,
-            "ms_per_launch": round(ms, 4), "launch": {"grid": g, "block": b}}
+    for m in mods:
+        m.close()
+    value = ms * 1e3 if unit == "us" else work / (ms / 1e3) / _units_scale(unit)
+    return {"value": round(value, 3), "unit": unit, "ms_per_step": round(ms, 4), "route": route,
+            "launch": {"grid": plan[0][2], "block": plan[0][3]}, "launches_per_step": len(plan)}
 
 
 # ---------------------------------------------------------------------------- CPU arms
@@ -674,9 +884,8 @@ def _main(out) -> int:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-ptx", action="store_true")
-    ap.add_argument("--combine", choices=["fused", "nccl"], default="nccl",
-                    help="c4 at N>1: our reduction kernel + NCCL all-reduce (measured faster), or the fused "
-                         "sum + NVLink peer combine kernel")
+    ap.add_argument("--only", action="store_true",
+                    help="time only --config (no C3-C5 block after C2, no weak-scaling pass at N > 1)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -25,7 +25,10 @@
 //
 // Set-up: the first call on each device looks up the array's device address
 // with cudaGetSymbolAddress (with that device current) and caches it; do
-// that first call before any stream capture.  No call allocates: no
+// that first call before any stream capture.  The cached address belongs to
+// the device's primary context as it was then: after cudaDeviceReset (or any
+// other reset of that context) the entry point must not be called again on
+// that device in this process.  No call allocates: no
 // cudaMalloc, cudaFree or allocating library routine is used.
 
 #include <cuda_runtime.h>

@@ -913,6 +913,8 @@ int emmy_shard_range(emmy_module_t m, int ndev, int d, uint64_t *begin, uint64_t
 int emmy_launch_sharded(const emmy_module_t *mods, int ndev, const uint64_t *const *args, int nargs,
                         const uint64_t *streams) {
     if (!mods || ndev <= 0 || !args) return fail(EMMY_ERR_INVALID, "emmy_launch_sharded: NULL argument");
+    if (nargs < 0 || nargs > EMMY_LR_MAX_PARAMS)
+        return fail(EMMY_ERR_INVALID, "emmy_launch_sharded: %d parameters (at most %d)", nargs, EMMY_LR_MAX_PARAMS);
     std::lock_guard<std::mutex> lk(g_mu);
     for (int d = 0; d < ndev; ++d) {
         emmy_module *m = mods[d];
@@ -955,18 +957,24 @@ int emmy_time_launch(emmy_module_t m, const uint64_t *args, int nargs, int iters
     std::lock_guard<std::mutex> lk(g_mu);
     int rc = set_device(m->dev);
     if (rc) return rc;
-    CUevent e0, e1;
-    CU(g_drv.cuEventCreate(&e0, CU_EVENT_DEFAULT), "cuEventCreate");
-    CU(g_drv.cuEventCreate(&e1, CU_EVENT_DEFAULT), "cuEventCreate");
+    // both events are destroyed on every path, including a failed launch
+    struct Events {
+        CUevent e[2] = {nullptr, nullptr};
+        ~Events() {
+            for (CUevent ev : e)
+                if (ev) g_drv.cuEventDestroy(ev);
+        }
+    } ev;
+    CU(g_drv.cuEventCreate(&ev.e[0], CU_EVENT_DEFAULT), "cuEventCreate");
+    CU(g_drv.cuEventCreate(&ev.e[1], CU_EVENT_DEFAULT), "cuEventCreate");
     CUstream s = reinterpret_cast<CUstream>(stream);
-    CU(g_drv.cuEventRecord(e0, s), "cuEventRecord");
+    CU(g_drv.cuEventRecord(ev.e[0], s), "cuEventRecord");
     for (int i = 0; i < iters && rc == EMMY_OK; ++i) rc = launch_locked(m, args, nargs, nullptr, nullptr, stream);
-    CU(g_drv.cuEventRecord(e1, s), "cuEventRecord");
-    CU(g_drv.cuEventSynchronize(e1), "cuEventSynchronize");
-    CU(g_drv.cuEventElapsedTime(ms_total, e0, e1), "cuEventElapsedTime");
-    g_drv.cuEventDestroy(e0);
-    g_drv.cuEventDestroy(e1);
-    return rc;
+    CU(g_drv.cuEventRecord(ev.e[1], s), "cuEventRecord");
+    CU(g_drv.cuEventSynchronize(ev.e[1]), "cuEventSynchronize");
+    if (rc) return rc;  // a launch failed: its error, not a time
+    CU(g_drv.cuEventElapsedTime(ms_total, ev.e[0], ev.e[1]), "cuEventElapsedTime");
+    return EMMY_OK;
 }
 
 }  // extern "C"

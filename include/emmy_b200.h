@@ -171,7 +171,9 @@ int emmy_graph_destroy(emmy_graph_t g);
  * n <= EMMY_NOALLOC_MAX_ELEMENTS, else EMMY_ERR_INVALID.  All calls on a
  * device share the array: calls that overlap on the GPU race.  The first call
  * on each device resolves the array's address (cudaGetSymbolAddress); make it
- * before any stream capture. */
+ * before any stream capture.  The address is kept for the life of the
+ * process: after cudaDeviceReset (or any reset of the device's primary
+ * context) this entry point must not be called again on that device. */
 #define EMMY_NOALLOC_MAX_CHUNKS 4096
 #define EMMY_NOALLOC_SCRATCH_BYTES (EMMY_NOALLOC_MAX_CHUNKS * 4 + 256)
 #define EMMY_NOALLOC_MAX_ELEMENTS (1ull << 36)

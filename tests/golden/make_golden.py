@@ -1116,7 +1116,7 @@ def all_cases() -> list[Case]:
     # one block: the reference's in-kernel zero fill races with other blocks' adds otherwise
     cases.append(atomic_sum_case("r_atomic_zp_sum_128", 128, zero_prologue=True))
     # config 5
-    cases.append(gemm_case("c5_gemm_full", 16384, 8192, 16384, config="c5", with_ref=False))
+    cases.append(gemm_case("c5_gemm_full", 16384, 8192, 16384, config="c5"))
     cases.append(gemm_case("c5_gemm_prof_8192x8192x8192", 8192, 8192, 8192, with_ref=False))  # profiler size
     cases.append(gemm_case("c5_gemm_128x64x256", 128, 64, 256))
     cases.append(gemm_case("c5_gemm_256x512x512", 256, 512, 512))

@@ -68,3 +68,11 @@ def test_new_entry_points_reject_bad_arguments_without_a_gpu():
     buf = ctypes.create_string_buffer(256)
     lib.emmy_last_error(buf, 256)
     assert b"NULL" in buf.value
+    # a negative or oversized parameter count is refused before anything reads the tables
+    mods = (ctypes.c_void_p * 1)(ctypes.c_void_p(16))
+    words = (ctypes.c_uint64 * 1)(0)
+    rows = (ctypes.POINTER(ctypes.c_uint64) * 1)(words)
+    for bad in (-1, 65, 1 << 30):
+        assert lib.emmy_launch_sharded(mods, 1, rows, bad, None) == -3
+        lib.emmy_last_error(buf, 256)
+        assert b"parameters" in buf.value

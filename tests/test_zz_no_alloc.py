@@ -47,6 +47,37 @@ def test_noalloc_sum_matches_the_module_path(cid, cuda_device):
     case.module.close()
 
 
+@pytest.mark.parametrize("n,offset", [(0, 0), (1, 0), (1, 1), (1000, 1), ((1 << 20) + 3, 0),
+                                      ((1 << 20) + 3, 1), ((1 << 22) + 5, 3)])
+def test_noalloc_sum_against_an_f64_sum(n, offset, cuda_device):
+    """Tiny sizes (n = 0 writes 0, n = 1), and x starting 4 or 12 bytes past a
+    16-byte boundary, which takes the kernel's scalar path instead of its
+    float4 path; the expected value is an f64 sum on the host."""
+    import numpy as np
+    import torch
+    from emmy_ptx_compiler_b200 import runtime
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5 + n)
+    base = torch.empty(n + 4, dtype=torch.float32, device="cuda").uniform_(-1.0, 1.0, generator=g)
+    x = base[offset:offset + n]
+    assert (x.data_ptr() % 16 == 0) == (offset == 0)
+    want = float(x.cpu().numpy().astype(np.float64).sum())
+    outs = []
+    for _ in range(2):
+        out = torch.full((1,), float("nan"), dtype=torch.float32, device="cuda")
+        runtime.sum_f32_noalloc(x, n, out, device=cuda_device, stream=torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        outs.append(float(out.item()))
+    for got in outs:
+        assert abs(got - want) <= 1e-5 * abs(want) + 1e-4, (got, want)
+    if n == 0:
+        assert outs == [0.0, 0.0]
+    if n == 1:
+        assert outs[0] == float(x.item())
+    assert outs[0] == outs[1]
+
+
 def test_noalloc_rejects_sizes_beyond_its_scratch(cuda_device):
     import ctypes
     from emmy_ptx_compiler_b200 import runtime
