@@ -248,7 +248,7 @@ class Job:
     (N = 1, or weak scaling), or this rank's shard of it (strong scaling,
     emmy_ptx_compiler_b200.shard)."""
 
-    def __init__(self, cfg: str, rank: int, world: int, local: int, mode: str):
+    def __init__(self, cfg: str, rank: int, world: int, local: int, mode: str, combine: str = "fused"):
         import torch
         from emmy_ptx_compiler_b200 import compiler, frontend, harness, runtime, shard
         self.cfg, self.rank, self.world, self.local, self.mode = cfg, rank, world, local, mode
@@ -276,13 +276,38 @@ class Job:
         self.order = [self.bufs[n] for n in self.spec.arg_order]
         self.stream = torch.cuda.current_stream(local).cuda_stream
         self.go = self.mod.bind(self.order, stream=self.stream)
-        self.partial = self.shard is not None and self.shard.mode == "partial"
+        # a full-array reduction's per-GPU results are combined in every step
+        # (weak scaling too: every rank then sums its own full-size copy)
+        self.partial = ((self.shard is not None and self.shard.mode == "partial")
+                        or (mode == "weak" and world > 1 and cfg == "c4"))
+        if mode == "weak":
+            combine = "nccl"
         self.step = self.go
-        if self.partial:
-            combine = combine_step(cfg, self.bufs, world)
-            self.step = lambda: (self.go(), combine())
+        self.xchg = None
+        self.combine = None
+        if self.partial and combine == "fused" and self.notes.get("cross_gpu_entry"):
+            # one kernel per GPU: the shard's reduction ends with the exchange of the
+            # per-GPU results over NVLink peer memory (the module's <entry>__xchg)
+            self.xchg = runtime.Exchange(local, world, rank)
+            handles = [None] * world
+            torch.distributed.all_gather_object(handles, self.xchg.handle)
+            self.xchg.connect(handles)
+            self.step = self.xchg.bind(self.mod, self.order, timeout_ms=10000, stream=self.stream)
+            self.combine = "fused: the KernelOp's reduction ends with the cross-GPU exchange (one kernel per GPU)"
+        elif self.partial:
+            nccl = combine_step(cfg, self.bufs, world)
+            self.step = lambda: (self.go(), nccl())
+            self.combine = "the KernelOp's reduction, then an NCCL all-reduce of the per-GPU results"
 
     def close(self):
+        if self.xchg is not None:
+            import torch
+            torch.cuda.synchronize(self.local)
+            st = self.xchg.status()
+            torch.distributed.barrier()       # no peer stores into this GPU's buffer any more
+            self.xchg.close()
+            if st:
+                raise RuntimeError(f"{self.cfg}: cross-GPU exchange status 0x{st:x} (a peer did not arrive in time)")
         self.mod.close()
 
 
@@ -445,10 +470,11 @@ def _verify(job) -> dict:
             "what": "shard output bit-equal to the whole-problem kernel (unit-range launch) on sampled rows"}
 
 
-def measure(cfg: str, args, rank: int, world: int, local: int, mode: str, *, extras: bool = True) -> dict:
+def measure(cfg: str, args, rank: int, world: int, local: int, mode: str, *, extras: bool = True,
+            combine: str = "fused") -> dict:
     """One config: device-timed value, roofline, e2e, and (rank 0, N = 1) the
     reference-PTX and CPU baselines."""
-    job = Job(cfg, rank, world, local, mode)
+    job = Job(cfg, rank, world, local, mode, combine)
     try:
         ms_max, clocks, l2 = _timed(job, args.steps, args.warmup, world, rank, clocks_active=True)
         check = _verify(job) if world > 1 and mode == "strong" else None
@@ -512,7 +538,7 @@ def measure(cfg: str, args, rank: int, world: int, local: int, mode: str, *, ext
         entry["parallelism"] = (
             f"strong scaling: the BASELINE problem split over {world} ranks, rows [lo, hi) of axis "
             f"'{sh.axis}' ({sh.extent // world} of {sh.extent}) per rank"
-            + ("; the per-rank partial sums are combined by an NCCL all-reduce inside every step"
+            + (f"; per-rank results combined inside every step: {job.combine}"
                if sh.mode == "partial" else "; no collective") if mode == "strong" else
             f"weak scaling: {world} ranks, each its own full-size copy of the problem; "
             + ("per-rank sums combined by an NCCL all-reduce in every step" if cfg == "c4" else "no collective"))
@@ -567,7 +593,11 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     if main_cfg == "c2" and not args.only:
         for cfg in ("c3", "c4", "c5"):
             others[cfg] = measure(cfg, args, rank, world, local, mode)
-            if weak is not None and cfg in ("c4",):
+            if world > 1 and cfg == "c4":
+                # the same step with the combine as a separate NCCL all-reduce, and weak scaling
+                others[cfg]["combine_nccl"] = {k: v for k, v in measure(cfg, args, rank, world, local, mode,
+                                                                        extras=False, combine="nccl").items()
+                                               if k in ("value", "unit", "ms_per_step", "parallelism")}
                 others[cfg]["weak"] = {k: v for k, v in measure(cfg, args, rank, world, local, "weak",
                                                                  extras=False).items()
                                        if k in ("value", "unit", "ms_per_step", "parallelism")}

@@ -27,7 +27,7 @@ from pathlib import Path
 
 from . import frontend, ir, toolchain
 from .errors import ToolchainError, UnsupportedIR
-from .families import attention, canon, gemm, pointwise, reduction, rownorm, schedule
+from .families import attention, canon, dropin, gemm, pointwise, reduction, rownorm, schedule
 from .families.common import KernelSource
 
 
@@ -73,6 +73,7 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
                                 f"(unsupported nodes: {', '.join(schedule.unsupported_nodes(kop)) or 'layout'})")
         ks = schedule.generate(kop, plan, shapes, dtypes, args, scalars, written, meta)
         return Lowered(ks, args, shapes, dtypes, meta)
+    meta_threads = dropin._threads(meta.get("block")) if meta.get("block") else 0
     # a matmul staged through shared memory is still a matmul: prove it and lower the naive form
     staged = canon.staged_matmul(kop, shapes, dtypes, meta)
     if staged is not None:
@@ -80,7 +81,7 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
             plan = gemm.match(staged, shapes, dtypes)
             if plan is not None:
                 ks = gemm.generate(staged, plan, shapes, dtypes, args, scalars, written,
-                                   variant=options.get("gemm_variant", "auto"))
+                                   variant=options.get("gemm_variant", "auto"), meta_threads=meta_threads)
                 ks.notes["canonical_form"] = "staged matmul -> naive matmul"
                 return Lowered(ks, args, shapes, dtypes, meta)
         except UnsupportedIR:
@@ -91,7 +92,7 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
                                        first_pass=options.get("attention_first_pass", "auto"))),
         ("gemm", lambda: gemm.match(kop, shapes, dtypes),
          lambda pl: gemm.generate(kop, pl, shapes, dtypes, args, scalars, written,
-                                  variant=options.get("gemm_variant", "auto"))),
+                                  variant=options.get("gemm_variant", "auto"), meta_threads=meta_threads)),
         ("reduction", lambda: reduction.match(kop, shapes, dtypes),
          lambda pl: reduction.generate(kop, pl, shapes, dtypes, args, scalars, written)),
         ("rownorm", lambda: rownorm.match(kop, shapes, dtypes),
@@ -106,7 +107,8 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
             plan = match()
             if plan is None:
                 continue
-            return Lowered(generate(plan), args, shapes, dtypes, meta)
+            ks = dropin.attach(generate(plan), kop, shapes, dtypes, args, scalars, written, meta)
+            return Lowered(ks, args, shapes, dtypes, meta)
         except UnsupportedIR as exc:
             # a family that recognised the shape but cannot specialise it (dtype,
             # head size, memory access pattern ...): the schedule family takes it

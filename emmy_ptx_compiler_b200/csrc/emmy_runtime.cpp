@@ -200,6 +200,8 @@ struct emmy_module {
     int dev = 0;
     CUmodule mod = nullptr;
     CUfunction fn = nullptr;
+    CUfunction fn_dropin = nullptr;  // the arg_order-only entry when fn is its <entry>__emmy twin
+    CUfunction fn_xchg = nullptr;    // <entry>__xchg: the reduction with the cross-GPU combine
     EmmyLaunchRecord rec{};
     bool has_rec = false;
     CUdeviceptr status = 0;
@@ -357,6 +359,11 @@ int launch_locked(emmy_module *m, const uint64_t *args, int nargs, const uint32_
 
 }  // namespace
 
+// emmy_xchg.cu: the next combining call's kernel parameter (struct EmmyXchgArgs of
+// emmy_xchg_dev.cuh, kXchgArgsBytes bytes) for exchange group x on device dev.
+extern "C" int emmy_xchg_fill_args(emmy_xchg_t x, int dev, int timeout_ms, void *args, size_t bytes);
+constexpr size_t kXchgArgsBytes = 8 * 8 + 8 + 4 * 4 + 8;
+
 // Lets other translation units of the library report through emmy_last_error.
 extern "C" __attribute__((visibility("hidden"))) int emmy_record_error(int code, const char *msg) {
     return fail(code, "%s", msg);
@@ -432,6 +439,23 @@ int emmy_load(int dev, const void *image, size_t len, const char *entry, emmy_mo
         g_drv.cuModuleUnload(m->mod);
         delete m;
         return fail(EMMY_ERR_NOT_FOUND, "entry '%s' not found in module", entry);
+    }
+    {
+        // modules of our compiler whose fast kernel takes more than the arg_order
+        // parameters (a unit range, tensor maps) export it as <entry>__emmy beside
+        // the drop-in <entry>; the library launches the fast one
+        char native[512];
+        if (std::snprintf(native, sizeof native, "%s__emmy", entry) < static_cast<int>(sizeof native)) {
+            CUfunction fast = nullptr;
+            if (g_drv.cuModuleGetFunction(&fast, m->mod, native) == CUDA_SUCCESS && fast) {
+                m->fn_dropin = m->fn;
+                m->fn = fast;
+            }
+        }
+        if (std::snprintf(native, sizeof native, "%s__xchg", entry) < static_cast<int>(sizeof native)) {
+            CUfunction xf = nullptr;
+            if (g_drv.cuModuleGetFunction(&xf, m->mod, native) == CUDA_SUCCESS) m->fn_xchg = xf;
+        }
     }
     CUdeviceptr rec_ptr = 0;
     size_t rec_bytes = 0;
@@ -895,6 +919,36 @@ int emmy_launch_range(emmy_module_t m, const uint64_t *args, int nargs, uint64_t
     std::lock_guard<std::mutex> lk(g_mu);
     if (!has_range(m)) return fail(EMMY_ERR_INVALID, "module takes no unit range (launch record has no EMMY_LR_RANGE)");
     return launch_locked(m, args, nargs, nullptr, nullptr, stream, begin, end);
+}
+
+int emmy_launch_xchg(emmy_module_t m, const uint64_t *args, int nargs, emmy_xchg_t x, int timeout_ms,
+                     uint64_t stream) {
+    if (!m || !x || (nargs > 0 && !args)) return fail(EMMY_ERR_INVALID, "emmy_launch_xchg: NULL argument");
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!m->fn_xchg || !m->has_rec)
+        return fail(EMMY_ERR_INVALID, "module has no cross-GPU combine entry (only full-array reductions do)");
+    if (static_cast<uint32_t>(nargs) != m->rec.nparams || nargs > EMMY_LR_MAX_PARAMS)
+        return fail(EMMY_ERR_INVALID, "entry takes %u parameters, got %d", m->rec.nparams, nargs);
+    int rc = set_device(m->dev);
+    if (rc) return rc;
+    alignas(16) unsigned char xargs[kXchgArgsBytes];
+    if ((rc = emmy_xchg_fill_args(x, m->dev, timeout_ms, xargs, sizeof xargs))) return rc;
+    void *kp[EMMY_LR_MAX_PARAMS + 1];
+    uint32_t narrow[EMMY_LR_MAX_PARAMS];
+    for (int i = 0; i < nargs; ++i) {
+        if (m->rec.param_kind[i] == EMMY_PARAM_PTR) {
+            kp[i] = const_cast<uint64_t *>(&args[i]);
+        } else {
+            narrow[i] = static_cast<uint32_t>(args[i]);
+            kp[i] = &narrow[i];
+        }
+    }
+    kp[nargs] = xargs;
+    CU(g_drv.cuLaunchKernel(m->fn_xchg, m->rec.grid[0], m->rec.grid[1], m->rec.grid[2], m->rec.block[0],
+                            m->rec.block[1], m->rec.block[2], m->rec.dyn_smem, reinterpret_cast<CUstream>(stream),
+                            kp, nullptr),
+       "cuLaunchKernel (cross-GPU combine)");
+    return EMMY_OK;
 }
 
 int emmy_shard_range(emmy_module_t m, int ndev, int d, uint64_t *begin, uint64_t *end) {

@@ -1,32 +1,27 @@
-// Full-array f32 sum fused with its cross-GPU combine over NVLink peer memory.
+// Full-array f32 sum fused with its cross-GPU combine over NVLink peer memory,
+// and the exchange group that compiled modules use for the same combine.
 //
 // The C4 step on N GPUs is: every GPU sums its shard, then the N partial sums
 // are added so that every GPU holds the total.  emmy_sum_f32_allreduce does
 // both in ONE kernel per GPU:
 //
-//   1. CTAs sum fixed-size chunks of the shard (128-bit streaming loads, lane
-//      butterflies) and store per-chunk partials; the CTA that finishes the
-//      last chunk adds the partials in chunk order (the reduction family's
-//      last-block combine scheme);
-//   2. that CTA's thread 0 stores the GPU's total into slot[rank] of EVERY
-//      GPU's exchange buffer (plain stores to peer memory, mapped through
-//      CUDA IPC), fences at system scope, then publishes the call's epoch in
-//      flag[rank] of every buffer;
-//   3. it waits (bounded by a timeout) until every flag in its own buffer has
-//      reached the epoch, fences, and adds slot[0..N) in rank order.  Every
-//      GPU adds the same N values in the same order, so all GPUs get the same
-//      bits, independent of timing.
+//   1. CTAs sum fixed-size chunks of the shard (four 128-bit streaming loads
+//      in flight per thread, lane butterflies) and store per-chunk partials;
+//      the CTA that finishes the last chunk adds the partials in chunk order
+//      (the reduction family's last-block combine scheme);
+//   2. that CTA's thread 0 exchanges the GPU's total with every other GPU
+//      through their exchange buffers (emmy_xchg_dev.cuh: one 64-bit
+//      epoch+value store per peer, a bounded wait for every peer's word) and
+//      adds the N totals in rank order, so all GPUs get the same bits.
 //
-// Slots are double-buffered by epoch parity: a GPU can be at most one call
-// ahead of any other (it cannot finish call e+1 before every GPU has published
-// e+1, i.e. finished reading call e), so call e+1's stores never overwrite a
-// slot a slower GPU is still reading for call e.  Flags hold the latest epoch
-// and are compared with "has reached", so a peer already one call ahead does
-// not hide the epoch being waited for.
+// emmy_launch_xchg (emmy_runtime.cpp) runs the same exchange at the end of a
+// compiled full-array reduction KernelOp (its <entry>__xchg kernel); this
+// file owns the exchange buffers and hands their addresses over through
+// emmy_xchg_fill_args.
 //
-// A wait that runs out sets bit 0 of the exchange object's status word and
-// writes NaN to *out; the kernel then returns, so the context stays usable.
-// emmy_xchg_status reads and clears the word.
+// A wait that runs out marks the GPU's group as failed (no more publishing
+// until emmy_xchg_reset), sets bit 0 of the status word and writes NaN to the
+// outputs; the kernel then returns, so the context stays usable.
 
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -38,6 +33,7 @@
 #include <mutex>
 
 #include "emmy_b200.h"
+#include "emmy_xchg_dev.cuh"
 
 extern "C" int emmy_record_error(int code, const char *msg);  // emmy_runtime.cpp (not exported)
 
@@ -49,11 +45,8 @@ constexpr uint64_t kMinChunk = 1ull << 14;
 constexpr int kThreads = 256;
 constexpr int kSms = 148;
 constexpr int kBlocksPerSm = 8;
-// exchange buffer layout (bytes)
-constexpr size_t kSlotsOff = 0;      // float slots[2][kMaxRanks]
-constexpr size_t kFlagsOff = 64;     // uint32 flags[kMaxRanks]
-constexpr size_t kStatusOff = 128;   // uint32 status
-constexpr size_t kXchgBytes = 256;
+constexpr size_t kXchgBytes = EMMY_XCHG_BUFFER_BYTES;
+static_assert(EMMY_XCHG_MAX_RANKS_DEV == EMMY_XCHG_MAX_RANKS, "exchange rank limit");
 // scratch layout (bytes)
 constexpr size_t kCounterOff = (kMaxChunks * sizeof(float) + 255) / 256 * 256;
 constexpr size_t kScratchBytes = kCounterOff + 256;
@@ -69,12 +62,6 @@ int report(int code, const char *fmt, ...) {
     vsnprintf(msg, sizeof msg, fmt, ap);
     va_end(ap);
     return emmy_record_error(code, msg);
-}
-
-__device__ __forceinline__ uint64_t now_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -98,8 +85,7 @@ __device__ float block_sum(float v, float *s_warp) {
 
 __global__ void __launch_bounds__(kThreads) sum_allreduce_kernel(
     const float *__restrict__ x, uint64_t n, uint64_t chunk, uint32_t nchunks, float *__restrict__ out,
-    unsigned char *scratch, unsigned char *local, Peers peers, int nranks, int rank, uint32_t epoch,
-    uint64_t timeout_ns) {
+    unsigned char *scratch, EmmyXchgArgs xa) {
     __shared__ float s_warp[32];
     __shared__ int s_last;
     float *partials = reinterpret_cast<float *>(scratch);
@@ -108,22 +94,40 @@ __global__ void __launch_bounds__(kThreads) sum_allreduce_kernel(
     for (uint32_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
         const uint64_t k0 = static_cast<uint64_t>(c) * chunk;
         const uint64_t k1 = (k0 + chunk < n) ? (k0 + chunk) : n;
-        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+        float a[4][4] = {};
         uint64_t k;
         if (vec) {
             const uint64_t kv_end = k0 + (k1 - k0) / 4 * 4;
-            for (k = k0 + 4ull * threadIdx.x; k + 3 < kv_end; k += 4ull * blockDim.x) {
-                const float4 v = __ldcs(reinterpret_cast<const float4 *>(x + k));
-                a0 += v.x;
-                a1 += v.y;
-                a2 += v.z;
-                a3 += v.w;
+            const uint64_t step = 4ull * blockDim.x;
+            k = k0 + 4ull * threadIdx.x;
+            // four 16-byte loads in flight per thread
+            for (; k + 3 * step + 3 < kv_end; k += 4 * step) {
+                float4 v[4];
+                #pragma unroll
+                for (int u = 0; u < 4; ++u) v[u] = __ldcs(reinterpret_cast<const float4 *>(x + k + u * step));
+                #pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    a[u][0] += v[u].x;
+                    a[u][1] += v[u].y;
+                    a[u][2] += v[u].z;
+                    a[u][3] += v[u].w;
+                }
             }
-            for (k = kv_end + threadIdx.x; k < k1; k += blockDim.x) a0 += x[k];
+            for (; k + 3 < kv_end; k += step) {
+                const float4 v = __ldcs(reinterpret_cast<const float4 *>(x + k));
+                a[0][0] += v.x;
+                a[0][1] += v.y;
+                a[0][2] += v.z;
+                a[0][3] += v.w;
+            }
+            for (k = kv_end + threadIdx.x; k < k1; k += blockDim.x) a[0][0] += x[k];
         } else {
-            for (k = k0 + threadIdx.x; k < k1; k += blockDim.x) a0 += __ldcs(x + k);
+            for (k = k0 + threadIdx.x; k < k1; k += blockDim.x) a[0][0] += __ldcs(x + k);
         }
-        const float total = block_sum((a0 + a1) + (a2 + a3), s_warp);
+        float t = 0.0f;
+        #pragma unroll
+        for (int u = 0; u < 4; ++u) t += (a[u][0] + a[u][1]) + (a[u][2] + a[u][3]);
+        const float total = block_sum(t, s_warp);
         if (threadIdx.x == 0) {
             __stcg(&partials[c], total);
             __threadfence();
@@ -138,39 +142,13 @@ __global__ void __launch_bounds__(kThreads) sum_allreduce_kernel(
             f = block_sum(f, s_warp);
             if (threadIdx.x == 0) {
                 *arrivals = 0u;
-                // publish this GPU's total to every GPU, then the epoch
-                const int par = static_cast<int>(epoch & 1u);
-                for (int r = 0; r < nranks; ++r) {
-                    volatile float *slot = reinterpret_cast<volatile float *>(peers.buf[r] + kSlotsOff);
-                    slot[par * kMaxRanks + rank] = f;
-                }
-                __threadfence_system();
-                for (int r = 0; r < nranks; ++r) {
-                    volatile unsigned int *flag = reinterpret_cast<volatile unsigned int *>(peers.buf[r] + kFlagsOff);
-                    flag[rank] = epoch;
-                }
-                // wait for every GPU's total of this call (bounded)
-                volatile unsigned int *mine = reinterpret_cast<volatile unsigned int *>(local + kFlagsOff);
-                const uint64_t t0 = now_ns();
-                bool ok = true;
-                for (int r = 0; r < nranks && ok; ++r) {
-                    while (static_cast<int>(mine[r] - epoch) < 0) {
-                        if (now_ns() - t0 > timeout_ns) {
-                            ok = false;
-                            break;
-                        }
-                        __nanosleep(64);
-                    }
-                }
-                if (!ok) {
-                    atomicOr(reinterpret_cast<unsigned int *>(local + kStatusOff), 1u);
-                    *out = __int_as_float(0x7fffffff);
-                } else {
-                    __threadfence_system();
-                    volatile float *slot = reinterpret_cast<volatile float *>(local + kSlotsOff);
-                    float s = slot[par * kMaxRanks + 0];
-                    for (int r = 1; r < nranks; ++r) s = __fadd_rn(s, slot[par * kMaxRanks + r]);
+                float got[EMMY_XCHG_MAX_RANKS_DEV];
+                if (emmy_xchg_exchange(xa, &f, 1, got)) {
+                    float s = got[0];
+                    for (uint32_t r = 1; r < xa.nranks; ++r) s = __fadd_rn(s, got[r]);
                     *out = s;
+                } else {
+                    *out = __int_as_float(0x7fffffff);
                 }
             }
         }
@@ -203,6 +181,20 @@ struct DeviceGuard {
         if (ok) cudaSetDevice(prev);
     }
 };
+
+// Parameters of the next call: the group's buffers and a fresh epoch (0 is the
+// value of a word nobody wrote, so it is skipped).
+void next_args(emmy_xchg *x, int timeout_ms, EmmyXchgArgs *xa) {
+    std::memset(xa, 0, sizeof *xa);
+    for (int r = 0; r < x->nranks; ++r) xa->peer[r] = reinterpret_cast<unsigned long long>(x->peers.buf[r]);
+    xa->local = reinterpret_cast<unsigned long long>(x->local);
+    xa->rank = static_cast<unsigned>(x->rank);
+    xa->nranks = static_cast<unsigned>(x->nranks);
+    x->epoch += 1u;
+    if (x->epoch == 0u) x->epoch = 1u;
+    xa->epoch = x->epoch;
+    xa->timeout_ns = static_cast<unsigned long long>(timeout_ms) * 1000000ull;
+}
 
 }  // namespace
 
@@ -276,13 +268,36 @@ extern "C" int emmy_sum_f32_allreduce(emmy_xchg_t x, const float *data, uint64_t
         nchunks = (n + chunk - 1) / chunk;
     }
     const unsigned grid = static_cast<unsigned>(nchunks < target ? nchunks : target);
-    x->epoch += 1u;
-    if (x->epoch == 0u) x->epoch = 1u;  // 0 is the initial flag value
+    EmmyXchgArgs xa;
+    next_args(x, timeout_ms, &xa);
     sum_allreduce_kernel<<<grid, kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        data, n, chunk, static_cast<uint32_t>(nchunks), out, x->scratch, x->local, x->peers, x->nranks, x->rank,
-        x->epoch, static_cast<uint64_t>(timeout_ms) * 1000000ull);
+        data, n, chunk, static_cast<uint32_t>(nchunks), out, x->scratch, xa);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return report(EMMY_ERR_CUDA, "emmy_sum_f32_allreduce launch: %s", cudaGetErrorString(e));
+    return EMMY_OK;
+}
+
+// The next call's kernel parameter for a compiled module's <entry>__xchg kernel
+// (emmy_launch_xchg in emmy_runtime.cpp).  Not exported.
+extern "C" __attribute__((visibility("hidden"))) int emmy_xchg_fill_args(emmy_xchg_t x, int dev, int timeout_ms,
+                                                                          void *args, size_t bytes) {
+    if (!x || !args || bytes != sizeof(EmmyXchgArgs)) return report(EMMY_ERR_INVALID, "emmy_launch_xchg: bad exchange");
+    if (!x->connected) return report(EMMY_ERR_INVALID, "emmy_launch_xchg: emmy_xchg_connect first");
+    if (x->dev != dev)
+        return report(EMMY_ERR_INVALID, "emmy_launch_xchg: exchange is on device %d, module on %d", x->dev, dev);
+    next_args(x, timeout_ms <= 0 ? 1000 : timeout_ms, static_cast<EmmyXchgArgs *>(args));
+    return EMMY_OK;
+}
+
+extern "C" int emmy_xchg_reset(emmy_xchg_t x) {
+    if (!x) return report(EMMY_ERR_INVALID, "emmy_xchg_reset: NULL argument");
+    DeviceGuard g(x->dev);
+    if (!g.ok) return report(EMMY_ERR_CUDA, "emmy_xchg_reset: cannot make device %d current", x->dev);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemset(x->local, 0, kXchgBytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return report(EMMY_ERR_CUDA, "emmy_xchg_reset: %s", cudaGetErrorString(e));
+    x->epoch = 0;
     return EMMY_OK;
 }
 
@@ -291,8 +306,8 @@ extern "C" int emmy_xchg_status(emmy_xchg_t x, uint32_t *status) {
     DeviceGuard g(x->dev);
     if (!g.ok) return report(EMMY_ERR_CUDA, "emmy_xchg_status: cannot make device %d current", x->dev);
     uint32_t v = 0, zero = 0;
-    cudaError_t e = cudaMemcpy(&v, x->local + kStatusOff, 4, cudaMemcpyDeviceToHost);
-    if (e == cudaSuccess) e = cudaMemcpy(x->local + kStatusOff, &zero, 4, cudaMemcpyHostToDevice);
+    cudaError_t e = cudaMemcpy(&v, x->local + EMMY_XCHG_STATUS_OFF, 4, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(x->local + EMMY_XCHG_STATUS_OFF, &zero, 4, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return report(EMMY_ERR_CUDA, "emmy_xchg_status: %s", cudaGetErrorString(e));
     *status = v;
     return EMMY_OK;

@@ -294,14 +294,26 @@ def generate(kop: ir.KernelOp, plan: ReductionPlan, shapes: dict, dtypes: dict, 
     scalar_env = {n: (("f32", f"p_{_c(n)}") if scalars[n] == "f32" else ("int", f"(long long)p_{_c(n)}"))
                   for n in scalars}
     accs = plan.accs
+    # a full-array reduction can combine its result across GPUs at the end of
+    # the kernel (<name>__xchg, emmy_xchg_dev.cuh); the body then takes the
+    # exchange parameter, NULL in the single-GPU entry
+    xchg = (rows == 1 and plan.kind != "atomic" and 1 <= nacc <= XCHG_MAX_VALUES
+            and all(op in XCHG_OPS for _, op in accs))
     L: list[str] = []
     w = L.append
     w(DEVICE_PRELUDE)
     w(_RED_HELPERS)
+    if xchg:
+        w('#include "emmy_xchg_dev.cuh"')
     if ch > 1:
         w(f"__device__ float emmy_red_partials[{nacc * rows * ch}];")
         w(f"__device__ unsigned int emmy_red_arrivals[{rows}];")
-    w(f'extern "C" __global__ void __launch_bounds__(1024) {kop.name}(' + ", ".join(sig) + ") {")
+    body_fn = f"emmy_red_body_{_c(kop.name)}"
+    if xchg:
+        w(f"static __device__ __forceinline__ void {body_fn}(" + ", ".join(sig + ["const EmmyXchgArgs *emmy_xa"])
+          + ") {")
+    else:
+        w(f'extern "C" __global__ void __launch_bounds__(1024) {kop.name}(' + ", ".join(sig) + ") {")
     w(f"    constexpr long long ROWS = {rows}LL, KLEN = {klen}LL, CH = {ch}LL, CHUNK = {chunk}LL;")
     w("    constexpr int NACC = %d;" % nacc)
     w("    if ((blockDim.x & 31u) != 0u || blockDim.y != 1u || blockDim.z != 1u) {")
@@ -365,6 +377,8 @@ def generate(kop: ir.KernelOp, plan: ReductionPlan, shapes: dict, dtypes: dict, 
         w(f"            for (int off = 16; off > 0; off >>= 1) b_{_c(a)} = {combine_code(op, f'b_{_c(a)}', f'__shfl_xor_sync(0xffffffffu, b_{_c(a)}, off)')};")
     if ch == 1:
         w("            if (lane == 0) {")
+        if xchg:
+            L.extend(_xchg_combine(accs, "b_", "                "))
         L.extend(_epilogue(plan, shapes, dtypes, ptrs, scalar_env, {a: f"b_{_c(a)}" for a, _ in accs},
                            "                "))
         w("            }")
@@ -399,6 +413,8 @@ def generate(kop: ir.KernelOp, plan: ReductionPlan, shapes: dict, dtypes: dict, 
             w(f"                float f_{_c(a)} = lane < nwarps ? s_warp[{i}][lane] : {ident};")
             w(f"                for (int off = 16; off > 0; off >>= 1) f_{_c(a)} = {combine_code(op, f'f_{_c(a)}', f'__shfl_xor_sync(0xffffffffu, f_{_c(a)}, off)')};")
         w("                if (lane == 0) {")
+        if xchg:
+            L.extend(_xchg_combine(accs, "f_", "                    "))
         L.extend(_epilogue(plan, shapes, dtypes, ptrs, scalar_env, {a: f"f_{_c(a)}" for a, _ in accs},
                            "                    "))
         w("                    emmy_red_arrivals[row] = 0u;")
@@ -408,14 +424,49 @@ def generate(kop: ir.KernelOp, plan: ReductionPlan, shapes: dict, dtypes: dict, 
         w("        __syncthreads();")
     w("    }")
     w("}")
+    if xchg:
+        names = ", ".join(s_.split()[-1] for s_ in sig)
+        w(f'extern "C" __global__ void __launch_bounds__(1024) {kop.name}(' + ", ".join(sig) + ") {")
+        w(f"    {body_fn}({names}{', ' if names else ''}nullptr);")
+        w("}")
+        w(f'extern "C" __global__ void __launch_bounds__(1024) {kop.name}__xchg('
+          + ", ".join(sig + ["const __grid_constant__ EmmyXchgArgs emmy_xa"]) + ") {")
+        w(f"    {body_fn}({names}{', ' if names else ''}&emmy_xa);")
+        w("}")
     nvb = rows * ch
     grid = max(1, min(nvb, SM_COUNT * BLOCKS_PER_SM))
     launch = LaunchPlan(grid=(grid, 1, 1), block=(BLOCK, 1, 1), smem=0)
     L.append(launch_record_source("reduction", launch, params))
     notes = {"vector": vec_ok, "scalar_reasons": why, "rows": rows, "klen": klen, "chunks": ch,
-             "chunk_len": chunk, "schedule": plan.kind, "accumulators": [a for a, _ in accs]}
+             "chunk_len": chunk, "schedule": plan.kind, "accumulators": [a for a, _ in accs],
+             "cross_gpu_entry": f"{kop.name}__xchg" if xchg else None}
     return KernelSource(entry=kop.name, source="\n".join(L), launch=launch, params=params,
                         family="reduction", notes=notes)
+
+
+XCHG_MAX_VALUES = 4
+XCHG_OPS = ("add", "sum", "max", "maximum", "amax", "min", "minimum", "amin")
+
+
+def _xchg_combine(accs, prefix: str, ind: str) -> list[str]:
+    """In the thread holding the row's final values: with an exchange
+    parameter, replace each value by the combine of every GPU's value in rank
+    order (NaN when the exchange failed)."""
+    out = [f"{ind}if (emmy_xa) {{",
+           f"{ind}    float emmy_v[{len(accs)}] = {{{', '.join(prefix + _c(a) for a, _ in accs)}}};",
+           f"{ind}    float emmy_g[{len(accs)} * EMMY_XCHG_MAX_RANKS_DEV];",
+           f"{ind}    const bool emmy_ok = emmy_xchg_exchange(*emmy_xa, emmy_v, {len(accs)}, emmy_g);"]
+    for i, (a, op) in enumerate(accs):
+        v = prefix + _c(a)
+        out += [f"{ind}    if (emmy_ok) {{",
+                f"{ind}        {v} = emmy_g[{i} * emmy_xa->nranks];",
+                f"{ind}        for (unsigned r = 1; r < emmy_xa->nranks; ++r)"
+                f" {v} = {combine_code(op, v, f'emmy_g[{i} * emmy_xa->nranks + r]')};",
+                f"{ind}    }} else {{",
+                f"{ind}        {v} = __int_as_float(0x7fffffff);",
+                f"{ind}    }}"]
+    out.append(f"{ind}}}")
+    return out
 
 
 def _row_decode(plan: ReductionPlan, ind: str) -> list[str]:

@@ -319,7 +319,11 @@ def _launch_threads(meta: dict) -> int:
 
 
 def generate(kop: ir.KernelOp, plan: SchedPlan, shapes: dict, dtypes: dict, args: list[str],
-             scalars: dict[str, str], written: set[str], meta: dict | None = None) -> KernelSource:
+             scalars: dict[str, str], written: set[str], meta: dict | None = None,
+             device_fn: str | None = None) -> KernelSource:
+    """The KernelOp in its own schedule.  With ``device_fn`` the code is a
+    ``static __device__`` function of that name taking the same parameters
+    (no prelude, no launch record), for a module that already has them."""
     meta = meta or {}
     shapes = dict(shapes)
     dtypes = dict(dtypes)
@@ -361,9 +365,12 @@ def generate(kop: ir.KernelOp, plan: SchedPlan, shapes: dict, dtypes: dict, args
             decl.append(f"    {cty} *const s_{_c(sm.name)} = reinterpret_cast<{cty} *>(emmy_dsm + {off});")
         else:
             decl.append(f"    __shared__ __align__({align}) {cty} s_{_c(sm.name)}[{max(1, count)}];")
-    lines: list[str] = [DEVICE_PRELUDE]
+    lines: list[str] = [] if device_fn else [DEVICE_PRELUDE]
     w = lines.append
-    w(f'extern "C" __global__ void {kop.name}(' + ", ".join(sig) + ") {")
+    if device_fn:
+        w(f"static __device__ void {device_fn}(" + ", ".join(sig) + ") {")
+    else:
+        w(f'extern "C" __global__ void {kop.name}(' + ", ".join(sig) + ") {")
     if dyn:
         w("    extern __shared__ __align__(128) unsigned char emmy_dsm[];")
     lines.extend(decl)
@@ -459,7 +466,8 @@ def generate(kop: ir.KernelOp, plan: SchedPlan, shapes: dict, dtypes: dict, args
         grid = (max(1, -(-(first_n or 1) // nthr)), 1, 1)
     grid = (tuple(grid) + (1, 1))[:3]
     launch = LaunchPlan(grid=grid, block=block, smem=dyn)
-    lines.append(launch_record_source("schedule", launch, params))
+    if not device_fn:
+        lines.append(launch_record_source("schedule", launch, params))
     notes = {"kernel": "schedule", "tiles": plan.tiles, "smem_static": 0 if dyn else total, "smem_dynamic": dyn}
     return KernelSource(entry=kop.name, source="\n".join(lines), launch=launch, params=params,
                         family="schedule", notes=notes)

@@ -19,7 +19,8 @@ LIB_DIR = PKG / "lib"
 RUNTIME_SO = LIB_DIR / "libemmy_b200.so"
 SOURCES = [PKG / "csrc" / "emmy_runtime.cpp"]
 CUDA_SOURCES = [PKG / "csrc" / "emmy_noalloc.cu", PKG / "csrc" / "emmy_xchg.cu"]
-HEADERS = [REPO / "include" / "emmy_b200.h", REPO / "include" / "emmy_launch_record.h"]
+HEADERS = [REPO / "include" / "emmy_b200.h", REPO / "include" / "emmy_launch_record.h",
+           PKG / "csrc" / "emmy_xchg_dev.cuh"]
 CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 CUDA_INC = CUDA_HOME / "include"
 CUDA_LIB = CUDA_HOME / "lib64"

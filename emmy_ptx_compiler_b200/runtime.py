@@ -64,6 +64,8 @@ def _declare(lib) -> None:
         "emmy_xchg_connect": ([vp, P(C.c_uint8)], i32),
         "emmy_sum_f32_allreduce": ([vp, u64, u64, u64, i32, u64], i32),
         "emmy_xchg_status": ([vp, P(u32)], i32),
+        "emmy_xchg_reset": ([vp], i32),
+        "emmy_launch_xchg": ([vp, P(u64), i32, vp, i32, u64], i32),
         "emmy_xchg_destroy": ([vp], i32),
         "emmy_comm_unique_id": ([P(C.c_uint8)], i32),
         "emmy_comm_init": ([i32, i32, i32, P(C.c_uint8), i32, P(vp)], i32),
@@ -88,7 +90,7 @@ EXPORTED = ("emmy_version", "emmy_last_error", "emmy_init", "emmy_device_count",
             "emmy_host_alloc", "emmy_host_free", "emmy_run_host", "emmy_time_launch", "emmy_launch_range",
             "emmy_module_range", "emmy_shard_range", "emmy_launch_sharded", "emmy_sum_f32_noalloc",
             "emmy_xchg_create", "emmy_xchg_connect", "emmy_sum_f32_allreduce", "emmy_xchg_status",
-            "emmy_xchg_destroy",
+            "emmy_xchg_reset", "emmy_launch_xchg", "emmy_xchg_destroy",
             "emmy_comm_unique_id", "emmy_comm_init", "emmy_allreduce_f32", "emmy_allgather_f32",
             "emmy_comm_destroy", "emmy_comm_abort",
             "emmy_graph_begin", "emmy_graph_end", "emmy_graph_launch", "emmy_graph_destroy")
@@ -338,10 +340,32 @@ class Exchange:
         _check(lib().emmy_sum_f32_allreduce(self._h, C.c_uint64(arg_word(x)), C.c_uint64(n),
                                             C.c_uint64(arg_word(out)), timeout_ms, C.c_uint64(stream)))
 
+    def launch(self, module: "Module", args, timeout_ms: int = 1000, stream: int = 0) -> None:
+        """One launch of ``module``'s cross-GPU entry (a compiled full-array
+        reduction): this GPU's shard reduced, every GPU's result combined."""
+        words = module._words(args)
+        _check(lib().emmy_launch_xchg(module._h, words, len(args), self._h, timeout_ms, C.c_uint64(stream)))
+
+    def bind(self, module: "Module", args, timeout_ms: int = 1000, stream: int = 0):
+        """A no-argument callable for ``launch`` with the words prepared once."""
+        words = module._words(args)
+        n, h, mh, f = len(args), self._h, module._h, lib().emmy_launch_xchg
+        st = C.c_uint64(stream)
+
+        def go() -> None:
+            rc = f(mh, words, n, h, timeout_ms, st)
+            if rc:
+                _check(rc)
+        return go
+
     def status(self) -> int:
         st = C.c_uint32(0)
         _check(lib().emmy_xchg_status(self._h, C.byref(st)))
         return st.value
+
+    def reset(self) -> None:
+        """Clear the group after a failed call (every rank, nothing in flight)."""
+        _check(lib().emmy_xchg_reset(self._h))
 
     def close(self) -> None:
         if getattr(self, "_h", None):

@@ -183,18 +183,33 @@ int emmy_sum_f32_noalloc(int dev, const float *x, uint64_t n, float *out, uint64
  * reference, which has no multi-GPU path): the full-array sum of this GPU's
  * shard fused with the cross-GPU combine over NVLink peer memory.
  *
- *   emmy_xchg_create   allocates this GPU's 256-byte exchange buffer and
- *                      returns its CUDA IPC handle (EMMY_XCHG_HANDLE_BYTES);
+ *   emmy_xchg_create   allocates this GPU's exchange buffer and returns its
+ *                      CUDA IPC handle (EMMY_XCHG_HANDLE_BYTES);
  *   emmy_xchg_connect  maps every rank's buffer, given all ranks' handles in
  *                      rank order (exchanged by the caller, e.g. through
  *                      torch.distributed);
  *   emmy_sum_f32_allreduce  *out = sum over ranks of sum(data[0..n)), the same
  *                      bits on every rank (partials added in rank order).
  *                      Asynchronous on `stream`; every rank must make the same
- *                      sequence of calls.  A rank whose peers do not arrive
- *                      within timeout_ms (<= 0: 1000) writes NaN and sets bit 0
- *                      of the status word;
- *   emmy_xchg_status   reads and clears that word.
+ *                      sequence of calls (of this and of emmy_launch_xchg).
+ *                      A rank whose peers do not arrive within timeout_ms
+ *                      (<= 0: 1000) writes NaN and sets bit 0 of the status
+ *                      word, and the group is then FAILED on that rank: every
+ *                      later call returns NaN at once, without publishing,
+ *                      until emmy_xchg_reset;
+ *   emmy_launch_xchg   the same combine at the end of a compiled full-array
+ *                      reduction KernelOp: launches the module's
+ *                      <entry>__xchg kernel (this GPU's shard reduced, the
+ *                      per-GPU results exchanged and combined with the
+ *                      reduction's operator in rank order, the epilogue run
+ *                      on the combined value), same rules as above;
+ *   emmy_xchg_status   reads and clears the status word;
+ *   emmy_xchg_reset    clears the buffer (and the FAILED state) and restarts
+ *                      the call count: every rank must reset, with no call of
+ *                      the group in flight on any rank (e.g. after a barrier
+ *                      that follows a stream synchronisation);
+ *   emmy_xchg_destroy  requires every peer to have stopped calling (peers
+ *                      store into this GPU's buffer through their mapping).
  * At most EMMY_XCHG_MAX_RANKS ranks, one GPU each. */
 #define EMMY_XCHG_MAX_RANKS 8
 #define EMMY_XCHG_HANDLE_BYTES 64
@@ -203,7 +218,10 @@ int emmy_xchg_create(int dev, int nranks, int rank, emmy_xchg_t *out, uint8_t ha
 int emmy_xchg_connect(emmy_xchg_t x, const uint8_t *handles);
 int emmy_sum_f32_allreduce(emmy_xchg_t x, const float *data, uint64_t n, float *out, int timeout_ms,
                            uint64_t stream);
+int emmy_launch_xchg(emmy_module_t m, const uint64_t *args, int nargs, emmy_xchg_t x, int timeout_ms,
+                     uint64_t stream);
 int emmy_xchg_status(emmy_xchg_t x, uint32_t *status);
+int emmy_xchg_reset(emmy_xchg_t x);
 int emmy_xchg_destroy(emmy_xchg_t x);
 
 /* NCCL over NVLink/NVSwitch for the one collective of the path: combining
