@@ -76,13 +76,16 @@ CONFIGS = {
                   "row-fused softmax over rows of x f32 [16384, 8192]"),
     "f_l2norm": ("f_l2norm_bench_16384x8192", "GB/s", "hbm", 2 * 16384 * 8192 * 4,
                  "row-fused l2norm: y = x * rsqrt(sum(x^2) + 1e-12), x f32 [16384, 8192]"),
-    # naive-attention IR, f32 on CUDA cores (exact reference arithmetic): algorithmic FLOP =
-    # q.k^T and p.v once each, 2 * 2 * seq^2 * dim
-    "a_attn": ("a_attn_bench_2048x64", "TFLOP/s", "fp32", 4 * 2048 * 2048 * 64,
+    # naive-attention IR, f32 operands on the tensor cores (tf32 with a three-term split):
+    # algorithmic FLOP = q.k^T and p.v once each, 2 * 2 * seq^2 * dim
+    "a_attn": ("a_attn_bench_2048x64", "TFLOP/s", "tf32x3", 4 * 2048 * 2048 * 64,
                "naive attention softmax(q k^T / sqrt(64)) v, q,k,v f32 [2048, 64]"),
 }
 # nominal FP32 CUDA-core peak: 148 SMs x 128 lanes x 2 FLOP x 1.965 GHz
 FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
+# nominal dense tf32 tensor peak; every f32 product of the attention kernel takes three
+# tf32 MMAs (hi*hi + hi*lo + lo*hi), so its algorithmic ceiling is a third of it
+TF32_NOMINAL_TFLOPS = 1100.0
 L2_BYTES = 126 * 1024 * 1024
 L2_FLUSH_BYTES = 256 * 1024 * 1024
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -504,8 +507,11 @@ def measure(cfg: str, args, rank: int, world: int, local: int, mode: str, *, ext
     peak = pk["hbm_gbs"] if bound == "hbm" else pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
     if bound == "fp32":
         peak, pk_kind = round(FP32_NOMINAL_TFLOPS, 1), "nominal"
+    if bound == "tf32x3":
+        peak, pk_kind = round(TF32_NOMINAL_TFLOPS / 3, 1), "nominal"
     peak_key = {"hbm": "hbm_gbs", "tensor": "bf16_tflops (burst: one kernel timed alone)",
-                "fp32": "fp32 CUDA cores", "latency": "none"}[bound]
+                "fp32": "fp32 CUDA cores", "latency": "none",
+                "tf32x3": "dense tf32 tensor peak / 3 (three MMAs per f32 product)"}[bound]
     traffic = DRAM_TRAFFIC.get(job.case_id) if world == 1 else None
     entry = {
         "value": round(value, 2), "unit": job.unit, "ms_per_step": round(per_launch_ms, 4),

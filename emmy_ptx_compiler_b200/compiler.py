@@ -54,8 +54,10 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
     """Classify ``kop`` into a family and generate its specialised source.
 
     ``options`` selects among equivalent schedules (results do not depend on
-    it): ``{"gemm_variant": "auto" | "pair" | "single",
+    it): ``{"gemm_variant": "auto" | "pair" | "single", "gemm_tune": {...}
+    (families/gemm.py PAIR_TUNE),
     "pointwise_pair": "auto" | True | False, "attention_first_pass": "auto" | "tiled",
+    "attention_kernel": "auto" | "tc" | "exact",
     "family": "schedule"}``; the
     last skips the fast families.  A KernelOp no fast family takes (or one a
     family recognises but cannot specialise) keeps its own schedule."""
@@ -81,7 +83,8 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
             plan = gemm.match(staged, shapes, dtypes)
             if plan is not None:
                 ks = gemm.generate(staged, plan, shapes, dtypes, args, scalars, written,
-                                   variant=options.get("gemm_variant", "auto"), meta_threads=meta_threads)
+                                   variant=options.get("gemm_variant", "auto"), meta_threads=meta_threads,
+                                   tune=options.get("gemm_tune"))
                 ks.notes["canonical_form"] = "staged matmul -> naive matmul"
                 return Lowered(ks, args, shapes, dtypes, meta)
         except UnsupportedIR:
@@ -89,10 +92,12 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
     fast = (
         ("attention", lambda: attention.match(kop, shapes, dtypes),
          lambda pl: attention.generate(kop, pl, shapes, dtypes, args, scalars, written,
-                                       first_pass=options.get("attention_first_pass", "auto"))),
+                                       first_pass=options.get("attention_first_pass", "auto"),
+                                       kernel=options.get("attention_kernel", "auto"))),
         ("gemm", lambda: gemm.match(kop, shapes, dtypes),
          lambda pl: gemm.generate(kop, pl, shapes, dtypes, args, scalars, written,
-                                  variant=options.get("gemm_variant", "auto"), meta_threads=meta_threads)),
+                                  variant=options.get("gemm_variant", "auto"), meta_threads=meta_threads,
+                                  tune=options.get("gemm_tune"))),
         ("reduction", lambda: reduction.match(kop, shapes, dtypes),
          lambda pl: reduction.generate(kop, pl, shapes, dtypes, args, scalars, written)),
         ("rownorm", lambda: rownorm.match(kop, shapes, dtypes),

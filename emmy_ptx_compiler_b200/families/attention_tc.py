@@ -1,0 +1,500 @@
+"""Attention on the 5th-generation tensor cores: the naive attention IR
+(tools/make_proxy_set.py:416-490 shape) as one tcgen05 kernel.
+
+Both contractions of the IR run on ``tcgen05.mma.kind::tf32`` with a
+three-term split of every f32 operand (``x = hi + lo``, ``hi`` = x with its
+13 low mantissa bits cleared, ``lo = x - hi`` exactly; a product is taken as
+``hi*hi + hi*lo + lo*hi``), which keeps about 21 bits of each product and
+accumulates in f32 in tensor memory:
+
+* scores ``S = q kᵀ`` (M = 128 query rows x N = the CTA's keys, K = head
+  size) once per (row, key), kept in tensor memory for every pass of the IR;
+* the weighted sum ``O = P v`` (M = 128 rows x N = head size, K = keys), with
+  ``P`` the per-(row, key) weight the IR's last key loop computes.
+
+Everything between - the IR's per-key statements (scale, ``exp``, the
+weights), its per-row statements (reciprocal of the denominator) and its row
+accumulations (max, sum) - runs on CUDA cores with the reference's op table
+(cgen), one thread per query row reading its scores from tensor memory.
+
+A query tile of 128 rows is shared by a cluster of CL CTAs that split the
+keys: each CTA computes its keys' scores and partial row statistics, the
+cluster exchanges the partials through distributed shared memory after every
+key loop (combined in CTA order, so every CTA holds the same row values),
+each CTA multiplies its own keys' weights into a partial ``O``, and the
+partial outputs are added in CTA order, each CTA writing 128 / CL rows.
+
+Shared-memory operands use the 128-byte swizzled K-major layout (rows of 32
+f32 words, 16-byte chunk c of row r stored at chunk c ^ (r & 7)); all
+operands are read from this GPU's memory with ordinary loads.  Every
+mbarrier wait is bounded.  Results follow the reference's arithmetic except
+for the summation order and the tensor-core products, within rtol 1e-4.
+"""
+
+from __future__ import annotations
+
+from .. import ir
+from ..cgen import DEVICE_PRELUDE, Emitter, combine_code, ctype, f32_lit, fusable_products, identity_of
+from ..errors import UnsupportedIR
+from .common import KernelSource, LaunchPlan, ParamSpec, SM_COUNT, launch_record_source
+from .common import c_ident as _c
+
+T = 128                 # threads: one per query row of the tile
+SMEM_MAX = 220 * 1024   # dynamic shared memory budget per CTA
+TMEM_COLS_MAX = 512
+
+
+def _pad(x: int, m: int) -> int:
+    return -(-x // m) * m
+
+
+def _dep_pattern(st, plan) -> str | None:
+    """The weight name ``w`` when the key loop's j-dependent statements are
+    exactly ``vv = v[k, j]; p = w * vv; acc += p`` (a matrix product)."""
+    dep = list(st.dep)
+    if len(dep) != 3:
+        return None
+    ld, mul, acc = dep
+    if not (isinstance(ld, ir.Load) and isinstance(mul, ir.Assign) and isinstance(acc, ir.Accum)):
+        return None
+    if ld.input != plan.v or len(ld.names) != 1:
+        return None
+    if ir.op_name(mul.op) not in ("multiply", "mul") or len(mul.args) != 2 or ld.names[0] not in mul.args:
+        return None
+    if ir.op_name(acc.op) not in ("add", "sum") or acc.value != mul.name or acc.name not in plan.cell_accs:
+        return None
+    w = mul.args[0] if mul.args[1] == ld.names[0] else mul.args[1]
+    if w == ld.names[0] or w not in st.stash:
+        return None
+    return w
+
+
+def layout(plan, shapes: dict, dtypes: dict) -> tuple[dict | None, list[str]]:
+    """Tile sizes of the tensor-core kernel for ``plan``, or None with reasons."""
+    from .attention import KeyLoop
+    why: list[str] = []
+    SQ, SK, D, DV = plan.SQ, plan.SK, plan.D, plan.DV
+    keyloops = [s for s in plan.steps if isinstance(s, KeyLoop)]
+    if plan.v is None or not keyloops:
+        why.append("no weighted sum of v")
+        return None, why
+    last = keyloops[-1]
+    if any(s.dep for s in keyloops[:-1]):
+        why.append("j-dependent statements before the last key loop")
+    w = _dep_pattern(last, plan) if last.dep else None
+    if w is None:
+        why.append("last key loop is not acc += w(i, k) * v[k, j]")
+    if plan.steps[-1] is not last:
+        why.append("row statements after the last key loop")
+    if any(s.dot_init != 0.0 for s in keyloops):
+        why.append("dot product seeded with a non-zero value")
+    if len(plan.cell_accs) != 1 or plan.out.values[0] != plan.cell_accs[0]:
+        why.append("output is not the single cell accumulator")
+    # the cell accumulator starts at 0 (a row statement Init before the last loop)
+    for st in plan.steps:
+        if not isinstance(st, KeyLoop) and isinstance(st[1], ir.Init) and st[1].name in plan.cell_accs:
+            if float(st[1].identity) != 0.0:
+                why.append("cell accumulator seeded with a non-zero value")
+    for s in keyloops:
+        for a, op in s.row_accs:
+            if op not in ("add", "maximum", "minimum"):
+                why.append(f"row accumulation {op}")
+    if D % 4 or DV % 4:
+        why.append("head sizes not multiples of 4")
+    if SQ < 64 or SK < 32:
+        why.append("fewer than 64 query rows or 32 keys")
+    if why:
+        return None, why
+    DP, DVP = _pad(D, 32), _pad(DV, 16)
+    nq = -(-SQ // 128)
+    best = None
+    for CL in (1, 2, 4, 8):
+        KC = _pad(-(-SK // CL), 32)
+        if CL > 1 and (CL - 1) * KC >= SK:
+            continue                   # a CTA without keys
+        tcols = 32
+        while tcols < KC + DVP:
+            tcols *= 2
+        if KC > 256 or tcols > TMEM_COLS_MAX:
+            continue
+        r1 = max(2 * (DP // 32) * 128 * 128, 4 * 128 * 128, 128 * DVP * 4)
+        r2 = max(2 * (DP // 32) * KC * 128, 2 * (KC // 32) * DVP * 128)
+        nstat = sum(len(s.row_accs) for s in keyloops) * 128 * 4
+        smem = 1024 + r1 + r2 + nstat + 64
+        if smem > SMEM_MAX:
+            continue
+        cand = dict(CL=CL, KC=KC, DP=DP, DVP=DVP, TCOLS=tcols, R1=r1, R2=r2, NSTAT=nstat, SMEM=smem, nq=nq, W=w)
+        best = cand
+        if nq * CL >= SM_COUNT // 2:
+            break
+    if best is None:
+        why.append("no cluster split fits shared and tensor memory")
+    return best, why
+
+
+_TC_HELPERS = r"""
+#include <string.h>
+#include "emmy_sm100.cuh"
+namespace {
+__device__ __forceinline__ void emmy_umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ float4 emmy_ld4(const float *p, bool aligned) {
+    return aligned ? *reinterpret_cast<const float4 *>(p) : make_float4(p[0], p[1], p[2], p[3]);
+}
+__device__ __forceinline__ void emmy_fence_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ float emmy_dsmem_ld(uint32_t cluster_addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+    return v;
+}
+// x = hi + lo exactly; hi keeps the 10 explicit mantissa bits a tf32 operand holds
+__device__ __forceinline__ float emmy_tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
+// byte offset of word w (0..31) of row r in a 128-byte-swizzled K-major tile of 32-word rows
+__device__ __forceinline__ uint32_t emmy_sw128(uint32_t r, uint32_t w) {
+    return r * 128u + ((((w >> 2) ^ (r & 7u)) << 4) | ((w & 3u) << 2));
+}
+__device__ __forceinline__ void emmy_put_split(uint8_t *hi, uint8_t *lo, uint32_t off, float x) {
+    const float h = emmy_tf32_hi(x);
+    *reinterpret_cast<float *>(hi + off) = h;
+    *reinterpret_cast<float *>(lo + off) = x - h;
+}
+__device__ __forceinline__ void emmy_put_split4(uint8_t *hi, uint8_t *lo, uint32_t off, float4 x) {
+    const float4 h = make_float4(emmy_tf32_hi(x.x), emmy_tf32_hi(x.y), emmy_tf32_hi(x.z), emmy_tf32_hi(x.w));
+    *reinterpret_cast<float4 *>(hi + off) = h;
+    *reinterpret_cast<float4 *>(lo + off) = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
+}
+}  // namespace
+"""
+
+
+def generate_tc(kop: ir.KernelOp, plan, lay: dict, shapes: dict, dtypes: dict, args: list[str],
+                scalars: dict[str, str], written: set[str]) -> KernelSource:
+    from .attention import KeyLoop
+    params: list[ParamSpec] = []
+    ptrs: dict[str, str] = {}
+    sig: list[str] = []
+    for name in args:
+        if name in scalars:
+            sig.append(f"{ctype(scalars[name])} p_{_c(name)}")
+            params.append(ParamSpec(name, "scalar", scalars[name]))
+            continue
+        dt = ir.canon_dtype(dtypes.get(name))
+        const = "" if name in written else "const "
+        sig.append(f"{const}{ctype(dt)}* __restrict__ p_{_c(name)}")
+        ptrs[name] = f"p_{_c(name)}"
+        params.append(ParamSpec(name, "ptr", dt))
+    sig += ["unsigned long long emmy_rb", "unsigned long long emmy_re"]
+    scalar_env = {n: (("f32", f"p_{_c(n)}") if scalars[n] == "f32" else ("int", f"(long long)p_{_c(n)}"))
+                  for n in scalars}
+    SQ, SK, D, DV = plan.SQ, plan.SK, plan.D, plan.DV
+    CL, KC, DP, DVP = lay["CL"], lay["KC"], lay["DP"], lay["DVP"]
+    NKB, NCH = DP // 32, KC // 32
+    fus = fusable_products(kop.body)
+    keyloops = [s for s in plan.steps if isinstance(s, KeyLoop)]
+    last = keyloops[-1]
+    wname = lay["W"]
+    qp, kp, vp, op_ = ptrs[plan.q], ptrs[plan.kmat], ptrs[plan.v], ptrs[plan.out_name]
+    L: list[str] = []
+    w = L.append
+    w(DEVICE_PRELUDE)
+    w(_TC_HELPERS)
+    w(f"""namespace {{
+constexpr int SQ = {SQ}, SK = {SK}, D = {D}, DV = {DV}, DP = {DP}, DVP = {DVP};
+constexpr int CL = {CL}, KC = {KC}, NKB = {NKB}, NCH = {NCH}, TCOLS = {lay['TCOLS']};
+constexpr uint32_t R1 = {lay['R1']}u, R2 = {lay['R2']}u, NSTAT = {lay['NSTAT']}u, SMEM_BYTES = {lay['SMEM']}u;
+constexpr uint32_t IDESC_S = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(KC >> 3) << 17) | ((128u >> 4) << 24);
+constexpr uint32_t IDESC_O = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(DVP >> 3) << 17) | ((128u >> 4) << 24);
+constexpr uint64_t WAIT_NS = 2000000000ull;
+}}  // namespace
+""")
+    w('extern "C" __global__ void __launch_bounds__(128, 1) ' + kop.name + "(" + ", ".join(sig) + ") {")
+    w("    uint32_t dyn_smem;")
+    w('    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn_smem));')
+    w("    if (blockDim.x != 128 || blockDim.y != 1 || blockDim.z != 1 || dyn_smem < SMEM_BYTES ||")
+    w("        emmy::cluster_nctarank() != (uint32_t)CL || (gridDim.x % CL) != 0) {")
+    w("        if (threadIdx.x == 0 && threadIdx.y == 0 && threadIdx.z == 0) atomicOr(&emmy_status, EMMY_STATUS_BAD_LAUNCH);")
+    w("        return;")
+    w("    }")
+    w("    const long long RB = (long long)(emmy_rb < (unsigned long long)SQ ? emmy_rb : SQ);")
+    w("    const long long RE = (long long)(emmy_re < (unsigned long long)SQ ? emmy_re : SQ);")
+    w("    extern __shared__ __align__(1024) uint8_t smem_raw[];")
+    w("    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));")
+    w("    uint8_t *const r1 = smem;            // Q hi/lo, then P hi/lo x 2, then the partial O")
+    w("    uint8_t *const r2 = smem + R1;       // K hi/lo, then V hi/lo")
+    w("    float *const stats = reinterpret_cast<float *>(smem + R1 + R2);")
+    w("    uint64_t *const bars = reinterpret_cast<uint64_t *>(smem + R1 + R2 + NSTAT);  // s_done, o_done, pfree0, pfree1")
+    w("    uint32_t *const tmem_holder = reinterpret_cast<uint32_t *>(bars + 4);")
+    w("    volatile uint32_t *const abort_flag = tmem_holder + 1;")
+    w("    const int tid = threadIdx.x, warp = tid >> 5;")
+    w(f"    const bool q_al = (reinterpret_cast<uintptr_t>({qp}) & 15u) == 0;   // 16-byte loads, else four 4-byte ones")
+    w(f"    const bool k_al = (reinterpret_cast<uintptr_t>({kp}) & 15u) == 0;")
+    w(f"    const bool v_al = (reinterpret_cast<uintptr_t>({vp}) & 15u) == 0;")
+    w("    (void)q_al; (void)k_al; (void)v_al;")
+    w("    const uint32_t crank = emmy::cluster_ctarank();")
+    w("    const int kbeg = (int)crank * KC;")
+    w("    if (tid == 0) {")
+    w("        for (int b = 0; b < 4; ++b) emmy::mbar_init(&bars[b], 1);")
+    w("        *abort_flag = 0u;")
+    w("        emmy::fence_barrier_init();")
+    w("    }")
+    w("    if (warp == 0) { emmy::tmem_alloc(tmem_holder, TCOLS); emmy::tmem_relinquish(); }")
+    w("    emmy::tc_fence_before();")
+    w("    __syncthreads();")
+    w("    emmy::tc_fence_after();")
+    w("    const uint32_t tmem = *tmem_holder;")
+    w("    const uint32_t trow = (uint32_t)(warp * 32) << 16;")
+    w("    uint32_t ph_s = 0, ph_o = 0, pissued[2] = {0u, 0u}, pwaited[2] = {0u, 0u};")
+    w("    bool ok = true;")
+    w("    const int qt0 = (int)(RB / 128);")
+    w("    const int nqt = RE > RB ? (int)((RE + 127) / 128) - qt0 : 0;")
+    w("    for (int qt = qt0 + (int)(blockIdx.x / CL); qt < qt0 + nqt; qt += (int)(gridDim.x / CL)) {")
+    w("        const long long q0 = (long long)qt * 128;")
+    # ---- Q and K operands
+    w("        // Q tile (A of S): 128 rows x DP, hi and lo; rows past SQ and columns past D are 0")
+    w("        for (int e = tid; e < 128 * (DP / 4); e += 128) {")
+    w("            const int r = e / (DP / 4), c4 = e % (DP / 4);")
+    w("            const long long gr = q0 + r;")
+    w("            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);")
+    w(f"            if (gr < SQ && 4 * c4 < D) x = emmy_ld4({qp} + gr * D + 4 * c4, q_al);")
+    w("            const uint32_t off = (uint32_t)((4 * c4) / 32) * 16384u + emmy_sw128((uint32_t)r, (uint32_t)((4 * c4) % 32));")
+    w("            emmy_put_split4(r1, r1 + NKB * 16384u, off, x);")
+    w("        }")
+    w("        // this CTA's keys (B of S): KC rows (keys) x DP, hi and lo; keys past SK are 0")
+    if plan.k_dk:
+        w("        for (int e = tid; e < DP * (KC / 4); e += 128) {")
+        w("            const int d = e / (KC / 4), k4 = e % (KC / 4);")
+        w("            float xs[4] = {0.f, 0.f, 0.f, 0.f};")
+        w("            if (d < D) {")
+        w("                #pragma unroll")
+        w("                for (int u = 0; u < 4; ++u) {")
+        w("                    const int key = kbeg + 4 * k4 + u;")
+        w(f"                    if (key < SK) xs[u] = {kp}[(long long)d * SK + key];")
+        w("                }")
+        w("            }")
+        w("            #pragma unroll")
+        w("            for (int u = 0; u < 4; ++u) {")
+        w("                const uint32_t off = (uint32_t)(d / 32) * (KC * 128u) + emmy_sw128((uint32_t)(4 * k4 + u), (uint32_t)(d % 32));")
+        w("                emmy_put_split(r2, r2 + NKB * KC * 128u, off, xs[u]);")
+        w("            }")
+        w("        }")
+    else:
+        w("        for (int e = tid; e < KC * (DP / 4); e += 128) {")
+        w("            const int r = e / (DP / 4), c4 = e % (DP / 4);")
+        w("            const int key = kbeg + r;")
+        w("            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);")
+        w(f"            if (key < SK && 4 * c4 < D) x = emmy_ld4({kp} + (long long)key * D + 4 * c4, k_al);")
+        w("            const uint32_t off = (uint32_t)((4 * c4) / 32) * (KC * 128u) + emmy_sw128((uint32_t)r, (uint32_t)((4 * c4) % 32));")
+        w("            emmy_put_split4(r2, r2 + NKB * KC * 128u, off, x);")
+        w("        }")
+    w("        emmy_fence_async_smem();")
+    w("        emmy::tc_fence_before();")
+    w("        __syncthreads();")
+    w("        if (tid == 0) {")
+    w("            emmy::tc_fence_after();")
+    w("            const uint32_t qh = emmy::smem_u32(r1), ql = qh + NKB * 16384u;")
+    w("            const uint32_t kh = emmy::smem_u32(r2), kl = kh + NKB * KC * 128u;")
+    w("            #pragma unroll 1")
+    w("            for (int kb = 0; kb < NKB; ++kb) {")
+    w("                #pragma unroll")
+    w("                for (int kk = 0; kk < 4; ++kk) {")
+    w("                    const uint32_t ao = kb * 16384u + kk * 32u, bo = kb * (KC * 128u) + kk * 32u;")
+    w("                    const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;")
+    w("                    emmy_umma_tf32(tmem, emmy::smem_desc_sw128(qh + ao, 16, 1024), emmy::smem_desc_sw128(kh + bo, 16, 1024), IDESC_S, acc);")
+    w("                    emmy_umma_tf32(tmem, emmy::smem_desc_sw128(qh + ao, 16, 1024), emmy::smem_desc_sw128(kl + bo, 16, 1024), IDESC_S, 1u);")
+    w("                    emmy_umma_tf32(tmem, emmy::smem_desc_sw128(ql + ao, 16, 1024), emmy::smem_desc_sw128(kh + bo, 16, 1024), IDESC_S, 1u);")
+    w("                }")
+    w("            }")
+    w("            emmy::umma_commit(&bars[0]);")
+    w("        }")
+    w("        __syncwarp();")
+    w("        if (!emmy::mbar_wait(&bars[0], ph_s, abort_flag, EMMY_STATUS_TIMEOUT_MMA, WAIT_NS)) ok = false;")
+    w("        ph_s ^= 1u;")
+    w("        emmy::tc_fence_after();")
+    w("        // this CTA's v rows (B of O): DVP rows (columns of v) x KC keys in 32-key chunks, hi and lo")
+    w("        for (int e = tid; e < KC * (DVP / 4); e += 128) {")
+    w("            const int kl_ = e / (DVP / 4), j4 = e % (DVP / 4);")
+    w("            const int key = kbeg + kl_;")
+    w("            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);")
+    w(f"            if (key < SK && 4 * j4 < DV) x = emmy_ld4({vp} + (long long)key * DV + 4 * j4, v_al);")
+    w("            const float xs[4] = {x.x, x.y, x.z, x.w};")
+    w("            #pragma unroll")
+    w("            for (int u = 0; u < 4; ++u) {")
+    w("                const uint32_t off = (uint32_t)(kl_ / 32) * (DVP * 128u) + emmy_sw128((uint32_t)(4 * j4 + u), (uint32_t)(kl_ % 32));")
+    w("                emmy_put_split(r2, r2 + NCH * DVP * 128u, off, xs[u]);")
+    w("            }")
+    w("        }")
+    w("        emmy_fence_async_smem();")
+    w("        __syncthreads();")
+    # ---- the IR's passes
+    w("        const long long row = q0 + tid;")
+    rem = Emitter(shapes, dtypes, ptrs, indent="        ")
+    rem.fusable = fus
+    rem.env.update(scalar_env)
+    rem.bind_const(plan.i, "int", "row")
+    slot = 0
+    for st in plan.steps:
+        if not isinstance(st, KeyLoop):
+            s = st[1]
+            if isinstance(s, ir.Init) and s.name in plan.cell_accs:
+                continue
+            rem.run((s,))
+            continue
+        final = st is last
+        accs = []
+        for a, op in st.row_accs:
+            accum = next(t for t in st.post if isinstance(t, ir.Accum) and t.name == a)
+            accs.append((a, op, accum))
+            L.extend(rem.lines)
+            rem.lines = []
+            w(f"        float part_{_c(a)} = {f32_lit(identity_of(op))};")
+        L.extend(rem.lines)
+        rem.lines = []
+        w(f"        // key loop over {st.loop.axis.name}: scores from tensor memory, 32 keys at a time")
+        w("        #pragma unroll 1")
+        w("        for (int ch = 0; ch < NCH; ++ch) {")
+        w("            uint32_t sreg[32];")
+        w("            emmy::tmem_ld_32x32b_x32(tmem + trow + (uint32_t)(ch * 32), sreg);")
+        w("            emmy::tmem_ld_wait();")
+        if final:
+            w("            float pw[32];")
+        w("            #pragma unroll")
+        w("            for (int kk = 0; kk < 32; ++kk) {")
+        w("                const int key = kbeg + ch * 32 + kk;")
+        if final:
+            w("                pw[kk] = 0.0f;")
+        w("                if (key < SK) {")
+        kem = Emitter(shapes, dtypes, ptrs, indent="                    ")
+        kem.fusable = fus
+        kem.env.update(rem.env)
+        kem.declared = {}
+        kem.bind_const(plan.i, "int", "row")
+        kem.bind_const(st.loop.axis.name, "int", "(long long)key")
+        kem.env[st.dot_acc] = ("f32", "__uint_as_float(sreg[kk])")
+        kem.run(tuple(st.indep))
+        L.extend(kem.lines)
+        for a, op, accum in accs:
+            prod = kem.plain_product(accum.value) if op == "add" else None
+            if prod is not None:
+                w(f"                    part_{_c(a)} = __fmaf_rn({prod[0]}, {prod[1]}, part_{_c(a)});")
+            else:
+                w(f"                    part_{_c(a)} = {combine_code(op, f'part_{_c(a)}', kem.as_f32(accum.value))};")
+        if final:
+            w(f"                    pw[kk] = {kem.as_f32(wname)};")
+        w("                }")
+        w("            }")
+        if final:
+            w("            // P chunk (A of O): this thread's row of 32 weights, hi and lo, into buffer ch & 1")
+            w("            const int b = ch & 1;")
+            w("            if (pissued[b] > pwaited[b]) {")
+            w("                if (!emmy::mbar_wait(&bars[2 + b], pwaited[b] & 1u, abort_flag, EMMY_STATUS_TIMEOUT_MMA, WAIT_NS)) ok = false;")
+            w("                ++pwaited[b];")
+            w("            }")
+            w("            uint8_t *const ph = r1 + (uint32_t)b * 32768u, *const pl = ph + 16384u;")
+            w("            #pragma unroll")
+            w("            for (int c = 0; c < 8; ++c) {")
+            w("                const float4 x = make_float4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]);")
+            w("                emmy_put_split4(ph, pl, emmy_sw128((uint32_t)tid, (uint32_t)(4 * c)), x);")
+            w("            }")
+            w("            emmy_fence_async_smem();")
+            w("            emmy::tc_fence_before();")
+            w("            __syncthreads();")
+            w("            if (tid == 0) {")
+            w("                emmy::tc_fence_after();")
+            w("                const uint32_t pa = emmy::smem_u32(ph), pb = emmy::smem_u32(pl);")
+            w("                const uint32_t vh = emmy::smem_u32(r2) + (uint32_t)ch * (DVP * 128u);")
+            w("                const uint32_t vl = vh + NCH * DVP * 128u;")
+            w("                #pragma unroll")
+            w("                for (int kk = 0; kk < 4; ++kk) {")
+            w("                    const uint32_t acc = (ch | kk) != 0 ? 1u : 0u;")
+            w("                    emmy_umma_tf32(tmem + KC, emmy::smem_desc_sw128(pa + kk * 32u, 16, 1024), emmy::smem_desc_sw128(vh + kk * 32u, 16, 1024), IDESC_O, acc);")
+            w("                    emmy_umma_tf32(tmem + KC, emmy::smem_desc_sw128(pa + kk * 32u, 16, 1024), emmy::smem_desc_sw128(vl + kk * 32u, 16, 1024), IDESC_O, 1u);")
+            w("                    emmy_umma_tf32(tmem + KC, emmy::smem_desc_sw128(pb + kk * 32u, 16, 1024), emmy::smem_desc_sw128(vh + kk * 32u, 16, 1024), IDESC_O, 1u);")
+            w("                }")
+            w("                emmy::umma_commit(&bars[2 + b]);")
+            w("            }")
+            w("            __syncwarp();")
+            w("            ++pissued[b];")
+        w("        }")
+        if accs:
+            w("        // partial row values of this CTA's keys -> every CTA of the cluster, combined in CTA order")
+            for fi, (a, op, accum) in enumerate(accs):
+                w(f"        stats[{slot + fi} * 128 + tid] = part_{_c(a)};")
+            w("        emmy::cluster_sync();")
+            for fi, (a, op, accum) in enumerate(accs):
+                cur = rem.as_f32(a)
+                w(f"        {{ float tot = {cur};")
+                w("          #pragma unroll 1")
+                w("          for (int rr = 0; rr < CL; ++rr)")
+                w(f"              tot = {combine_code(op, 'tot', f'emmy_dsmem_ld(emmy::mapa(&stats[{slot + fi} * 128 + tid], (uint32_t)rr))')};")
+                L.extend(rem.lines)
+                rem.lines = []
+                var = rem.declare(a, "f32")
+                L.extend(rem.lines)
+                rem.lines = []
+                w(f"          {var} = tot; }}")
+                rem.env[a] = ("f32", var)
+            slot += len(accs)
+    L.extend(rem.lines)
+    rem.lines = []
+    w("        // the partial O of this CTA's keys")
+    w("        if (tid == 0) emmy::umma_commit(&bars[1]);")
+    w("        __syncwarp();")
+    w("        if (!emmy::mbar_wait(&bars[1], ph_o, abort_flag, EMMY_STATUS_TIMEOUT_MMA, WAIT_NS)) ok = false;")
+    w("        ph_o ^= 1u;")
+    w("        for (int b = 0; b < 2; ++b)")
+    w("            while (pwaited[b] < pissued[b]) {")
+    w("                if (!emmy::mbar_wait(&bars[2 + b], pwaited[b] & 1u, abort_flag, EMMY_STATUS_TIMEOUT_MMA, WAIT_NS)) ok = false;")
+    w("                ++pwaited[b];")
+    w("            }")
+    w("        emmy::tc_fence_after();")
+    w("        float *const opart = reinterpret_cast<float *>(r1);")
+    w("        #pragma unroll 1")
+    w("        for (int c = 0; c < DVP; c += 32) {")
+    w("            uint32_t oreg[32];")
+    w("            emmy::tmem_ld_32x32b_x32(tmem + trow + (uint32_t)(KC + c), oreg);")
+    w("            emmy::tmem_ld_wait();")
+    w("            #pragma unroll")
+    w("            for (int jj = 0; jj < 32; ++jj)")
+    w("                if (c + jj < DVP) opart[tid * DVP + c + jj] = __uint_as_float(oreg[jj]);")
+    w("        }")
+    w("        emmy::tc_fence_before();")
+    w("        emmy::cluster_sync();")
+    w("        // rows [crank * 128 / CL, (crank + 1) * 128 / CL): the CL partials added in CTA order")
+    w("        for (int e = tid; e < (128 / CL) * DV; e += 128) {")
+    w("            const int r = (int)crank * (128 / CL) + e / DV, jj = e % DV;")
+    w("            float tot = 0.0f;")
+    w("            #pragma unroll 1")
+    w("            for (int rr = 0; rr < CL; ++rr) tot += emmy_dsmem_ld(emmy::mapa(&opart[r * DVP + jj], (uint32_t)rr));")
+    w(f"            if (q0 + r < RE && q0 + r >= RB) {op_}[(q0 + r) * DV + jj] = tot;")
+    w("        }")
+    w("        emmy::cluster_sync();")
+    w("    }")
+    w("    if (!ok) atomicOr(&emmy_status, EMMY_STATUS_TIMEOUT_MMA);")
+    w("    emmy::tc_fence_before();")
+    w("    __syncthreads();")
+    w("    if (warp == 0) { emmy::tc_fence_after(); emmy::tmem_dealloc(tmem, TCOLS); }")
+    w("}")
+    grid = lay["nq"] * CL
+    rb = []
+    for name in args:
+        if name == plan.q:
+            rb.append(D * 4)
+        elif name == plan.out_name:
+            rb.append(DV * 4)
+        else:
+            rb.append(0)
+    launch = LaunchPlan(grid=(grid, 1, 1), block=(T, 1, 1), smem=lay["SMEM"], cluster=(CL, 1, 1),
+                        range_total=SQ, range_align=128, range_bytes=rb)
+    L.append(launch_record_source("attention", launch, params))
+    notes = {"kernel": "attention_tcgen05_tf32x3", "cluster": CL, "keys_per_cta": KC, "query_tile": 128,
+             "smem": lay["SMEM"], "tmem_cols": lay["TCOLS"], "weights": wname}
+    return KernelSource(entry=kop.name, source="\n".join(L), launch=launch, params=params,
+                        family="attention", notes=notes)

@@ -111,8 +111,12 @@ def attach(ks: KernelSource, kop: ir.KernelOp, shapes: dict, dtypes: dict, args:
             f'extern "C" __global__ void __launch_bounds__({threads}) {name}({", ".join(sig[:n])}) {{\n'
             "    uint32_t emmy_dyn;\n"
             '    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(emmy_dyn));\n'
+            + (f"    uint32_t emmy_ncl;\n"
+               '    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(emmy_ncl));\n'
+               if ks.launch.cluster[0] > 1 else "") +
             f"    if (blockDim.x == {own[0]} && blockDim.y == {own[1]} && blockDim.z == {own[2]}"
-            f" && emmy_dyn >= {ks.launch.smem}u) {{\n"
+            f" && emmy_dyn >= {ks.launch.smem}u"
+            + (f" && emmy_ncl == {ks.launch.cluster[0]}u" if ks.launch.cluster[0] > 1 else "") + ") {\n"
             f"        {whole}\n"
             "    } else {\n"
             f"        emmy_sched_{c_ident(name)}({', '.join(names[:n])});\n"

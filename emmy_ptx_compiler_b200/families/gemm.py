@@ -43,7 +43,11 @@ GROUP_M = 16
 # CTA-pair kernel schedule knobs (results do not depend on them): row-tiles per
 # column sweep, C stores ("wb" write-back, "cs" streaming), L2 policies of the
 # A and B tile loads (None, "evict_last", "evict_first")
-PAIR_TUNE = {"group_m": 16, "c_store": "wb", "a_policy": None, "b_policy": None}
+PAIR_TUNE = {"group_m": 16, "c_store": "wb", "a_policy": None, "b_policy": None,
+             # failure-detection tests only: a shorter limit for every bounded wait, and a
+             # producer that leaves out its first TMA load (CTA 1 of cluster 0, first tile),
+             # so that the leader's stage never fills and the bounded waits run out
+             "wait_ns": 2000000000, "skip_first_load": False}
 TMAP_DTYPE = {"bf16": 9, "f16": 6}
 SWIZZLE_128B = 3
 L2_256B = 3
@@ -762,6 +766,10 @@ def _gen_tcgen05_pair(kop, plan: GemmPlan, shapes, dtypes, args, ptrs, sig, para
         f"            const uint64_t {var} = emmy::l2_policy_{tn_[key].replace('evict_', 'evict_')}();\n"
         for var, key in (("pol_a", "a_policy"), ("pol_b", "b_policy")) if tn_[key])
     a_load = "                    " + _ld("sA + stage * A_STAGE, &tm_a, fbar, k * BK, tm * BM + (int)rank * CBM", apol)
+    skip_open = skip_close = ""
+    if tn_["skip_first_load"]:
+        skip_open = "                    if (!(rank == 1u && pair == 0 && t == pair && k == 0)) {\n"
+        skip_close = "\n                    }"
     if plan.b_nk:
         b_loads = "                    " + _ld("sB + stage * B_STAGE, &tm_b, fbar, k * BK, tn * BN + (int)rank * CBN",
                                                bpol)
@@ -783,7 +791,7 @@ constexpr int NB = {nb}, KB = {kb}, GROUP_M = {tn_['group_m']};
 constexpr uint32_t A_STAGE = {a_stage}u, B_STAGE = {b_stage}u;
 constexpr uint32_t SMEM_BYTES = {smem}u;
 constexpr uint32_t IDESC = emmy::idesc_f16({fmt}u, {0 if plan.b_nk else 1}u, BM, BN);
-constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s per wait: orders of magnitude above any legal wait
+constexpr uint64_t WAIT_NS = {int(tn_["wait_ns"])}ull;  // per wait (2 s by default: orders of magnitude above any legal wait)
 
 // tile t of a launch over row-tiles [mb0, mb0 + mbn): GROUP_M row-tiles share each column sweep
 __device__ __forceinline__ void tile_coords(int t, int mb0, int mbn, int &mb, int &nb) {{
@@ -854,8 +862,8 @@ extern "C" __global__ void __launch_bounds__({TC_THREADS}, 1) {kop.name}({", ".j
                     if (!emmy::mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, EMMY_STATUS_TIMEOUT_PRODUCER, WAIT_NS)) {{ ok = false; break; }}
                     if (rank == 0) emmy::mbar_arrive_expect_tx(&full[stage], 2u * (A_STAGE + B_STAGE));
                     const uint32_t fbar = emmy::mapa(&full[stage], 0);
-{a_load}
-{b_loads}
+{skip_open}{a_load}
+{b_loads}{skip_close}
                     if (rank == 0) {{
                         issued |= 1u << stage;
                         parity_bits = (parity_bits & ~(1u << stage)) | (phase << stage);

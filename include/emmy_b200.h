@@ -56,7 +56,23 @@ int emmy_device_count(int *count);
 /* Load a PTX (NUL-terminated text) or cubin image on device `dev` and resolve
  * `entry` (the reference's `.visible .entry <KernelOp.name>`,
  * compile.py:862).  Modules from our compiler also carry a launch record
- * (include/emmy_launch_record.h), read here. */
+ * (include/emmy_launch_record.h), read here.
+ *
+ * Entries of our modules: `<entry>` itself always takes exactly the meta.json
+ * arg_order parameters and is correct under the reference runner's launch
+ * (meta grid, block, smem_bytes).  When the fast kernel needs more - a unit
+ * range after the buffers, TMA tensor maps, a thread-block cluster - the
+ * module also exports it as `<entry>__emmy`, and this library launches that
+ * one (with the record's geometry and extras).  Full-array reductions also
+ * export `<entry>__xchg` (emmy_launch_xchg).
+ *
+ * Reduction modules whose blocks split a row keep their cross-block partials
+ * and per-row arrival counters in globals of the loaded module (created
+ * zeroed by the load; the block that completes a row resets its counter).
+ * Two launches of ONE loaded module that overlap on the GPU (two streams)
+ * race on them: serialise them, or load the module once per stream.  A launch
+ * that does not run to completion (its context is then lost) leaves the
+ * counters undefined: unload and load the module again before reusing it. */
 int emmy_load(int dev, const void *image, size_t len, const char *entry, emmy_module_t *out);
 
 int emmy_unload(emmy_module_t m);

@@ -1,9 +1,16 @@
 """Attention family launch paths (no reference counterpart).
 
-Key and value tiles are copied into shared memory with 16-byte asynchronous
-copies when the base pointers are 16-byte aligned, and with plain loads
-otherwise (every chunk address is the base plus a multiple of 16 bytes, so
-the base decides).  Both paths must give the same bytes.
+Two kernels lower the naive attention IR: the tensor-core kernel
+(families/attention_tc.py, tcgen05 kind::tf32 with a three-term split, the
+default) and the exact CUDA-core kernel (``attention_kernel: "exact"``, every
+score and weighted sum in the reference's sequential fma order).
+
+* Both read operands with 16-byte loads when the base pointers are 16-byte
+  aligned, and with 4-byte loads otherwise; both paths must give the same
+  bytes.
+* The tensor-core kernel must stay within the attention bar (rtol 1e-4,
+  atol 1e-5) of the exact kernel and of the CPU oracle, on every fixture and
+  at the bench shape, and repeat its bits from launch to launch.
 """
 
 from __future__ import annotations
@@ -15,11 +22,12 @@ from conftest import CASES
 pytestmark = pytest.mark.gpu
 
 
+@pytest.mark.parametrize("kernel", ["exact", "tc"])
 @pytest.mark.parametrize("cid", ["a_attn_64x32", "a_attn_256x64", "a_attn_100x48"])
-def test_unaligned_kv_matches_aligned(cid, cuda_device):
+def test_unaligned_kv_matches_aligned(cid, kernel, cuda_device):
     import torch
     from emmy_ptx_compiler_b200 import harness
-    case = harness.DeviceCase(CASES / cid, cuda_device)
+    case = harness.DeviceCase(CASES / cid, cuda_device, options={"attention_kernel": kernel})
     bufs = harness._seeded_device_inputs(case.spec, cuda_device, seed=5)
     case.launch(bufs)
     torch.cuda.synchronize(cuda_device)
@@ -56,8 +64,9 @@ def test_register_tiled_first_pass_matches_tiled_pass(cuda_device):
     sys.path.insert(0, str(REPO / "oracle"))
     import interp
     cid = "a_attn_bench_2048x64"
-    fast = harness.DeviceCase(CASES / cid, cuda_device)
-    tiled = harness.DeviceCase(CASES / cid, cuda_device, options={"attention_first_pass": "tiled"})
+    fast = harness.DeviceCase(CASES / cid, cuda_device, options={"attention_kernel": "exact"})
+    tiled = harness.DeviceCase(CASES / cid, cuda_device,
+                               options={"attention_kernel": "exact", "attention_first_pass": "tiled"})
     assert fast.bundle["notes"]["register_tiled_first_pass"] and not tiled.bundle["notes"]["register_tiled_first_pass"]
     bufs = harness._seeded_device_inputs(fast.spec, cuda_device, seed=9)
     outs = {}
@@ -77,3 +86,29 @@ def test_register_tiled_first_pass_matches_tiled_pass(cuda_device):
                                            interp._p(ref), rows, 2048, 64, 64, float(np.float32(1 / 8))) == 0
     ok, why = interp.within(outs["fast"][:rows], ref, {"rtol": 4e-6, "atol": 2e-6})
     assert ok, why
+
+
+@pytest.mark.parametrize("cid", ["a_attn_64x32", "a_attn_256x64", "a_attn_100x48", "a_attn_krows_80x40",
+                                 "a_attn_bench_2048x64"])
+def test_tensor_core_kernel_matches_the_exact_kernel(cid, cuda_device):
+    import torch
+    from emmy_ptx_compiler_b200 import harness
+    tc = harness.DeviceCase(CASES / cid, cuda_device, options={"attention_kernel": "tc"})
+    ex = harness.DeviceCase(CASES / cid, cuda_device, options={"attention_kernel": "exact"})
+    assert tc.bundle["notes"]["kernel"] == "attention_tcgen05_tf32x3"
+    bufs = harness._seeded_device_inputs(tc.spec, cuda_device, seed=13)
+    out = tc.spec.outputs[0]
+    got = {}
+    for name, case in (("tc", tc), ("tc_again", tc), ("exact", ex)):
+        b = dict(bufs)
+        b[out] = torch.full_like(bufs[out], float("nan"))
+        case.launch(b)
+        torch.cuda.synchronize(cuda_device)
+        assert case.module.status() == 0, name
+        got[name] = b[out]
+    assert torch.equal(got["tc"].view(torch.int32), got["tc_again"].view(torch.int32))
+    err = (got["tc"] - got["exact"]).abs()
+    bad = int((err > 1e-5 + 1e-4 * got["exact"].abs()).sum())
+    assert bad == 0, (cid, float(err.max()))
+    tc.module.close()
+    ex.module.close()
