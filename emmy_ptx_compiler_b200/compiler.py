@@ -182,7 +182,9 @@ def _bundle_from(kop: ir.KernelOp, raw: dict | None, meta_k: dict | None, path: 
         "smem_bytes": ks.launch.smem,
         "dynamic_smem": ks.launch.smem > 48 * 1024,
         "block": ks.launch.block[0] * ks.launch.block[1] * ks.launch.block[2],
-        "virt_regs": {},
+        # physical registers per entry from ptxas (the reference counted its virtual
+        # registers by type; nvcc's PTX is not read here, so ptxas -v gives the counts)
+        "virt_regs": _register_counts(ks),
         "stats": {"family": ks.family, **{k: v for k, v in ks.notes.items() if isinstance(v, (int, bool))}},
         "ops": mix,
         "ir_txt": ir_txt,
@@ -197,6 +199,16 @@ def _bundle_from(kop: ir.KernelOp, raw: dict | None, meta_k: dict | None, path: 
     if want_cubin:
         out["cubin"] = comp.cubin()
     return out
+
+
+def _register_counts(ks: KernelSource) -> dict:
+    try:
+        per = toolchain.register_usage(ks.source, ks.entry)
+    except ToolchainError as exc:
+        return {"unavailable": str(exc)[:200]}
+    entry = per.get(ks.entry, {})
+    return {"registers": entry.get("registers"), "spill_stores": entry.get("spill_stores", 0),
+            "spill_loads": entry.get("spill_loads", 0), "entries": per, "source": "ptxas -v, sm_100a"}
 
 
 def compile_bundle(path, want_cubin: bool = False, options: dict | None = None) -> dict:

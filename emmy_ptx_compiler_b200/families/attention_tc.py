@@ -152,7 +152,7 @@ __device__ __forceinline__ void emmy_fence_async_smem() {
 }
 __device__ __forceinline__ float emmy_dsmem_ld(uint32_t cluster_addr) {
     float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr));
     return v;
 }
 // x = hi + lo exactly; hi keeps the 10 explicit mantissa bits a tf32 operand holds
@@ -269,16 +269,22 @@ constexpr uint64_t WAIT_NS = 2000000000ull;
     w("        }")
     w("        // this CTA's keys (B of S): KC rows (keys) x DP, hi and lo; keys past SK are 0")
     if plan.k_dk:
+        # consecutive threads take consecutive d (one row of kt each, four keys per thread), so
+        # each store instruction of a warp writes 32 different words of the same key rows
         w("        for (int e = tid; e < DP * (KC / 4); e += 128) {")
-        w("            const int d = e / (KC / 4), k4 = e % (KC / 4);")
-        w("            float xs[4] = {0.f, 0.f, 0.f, 0.f};")
+        w("            const int d = e % DP, k4 = e / DP;")
+        w("            const int key0 = kbeg + 4 * k4;")
+        w("            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);")
         w("            if (d < D) {")
-        w("                #pragma unroll")
-        w("                for (int u = 0; u < 4; ++u) {")
-        w("                    const int key = kbeg + 4 * k4 + u;")
-        w(f"                    if (key < SK) xs[u] = {kp}[(long long)d * SK + key];")
+        w("                if (key0 + 3 < SK) {")
+        w(f"                    x = emmy_ld4({kp} + (long long)d * SK + key0, k_al && (SK % 4) == 0);")
+        w("                } else {")
+        w(f"                    if (key0 < SK) x.x = {kp}[(long long)d * SK + key0];")
+        w(f"                    if (key0 + 1 < SK) x.y = {kp}[(long long)d * SK + key0 + 1];")
+        w(f"                    if (key0 + 2 < SK) x.z = {kp}[(long long)d * SK + key0 + 2];")
         w("                }")
         w("            }")
+        w("            const float xs[4] = {x.x, x.y, x.z, x.w};")
         w("            #pragma unroll")
         w("            for (int u = 0; u < 4; ++u) {")
         w("                const uint32_t off = (uint32_t)(d / 32) * (KC * 128u) + emmy_sw128((uint32_t)(4 * k4 + u), (uint32_t)(d % 32));")
@@ -319,8 +325,9 @@ constexpr uint64_t WAIT_NS = 2000000000ull;
     w("        ph_s ^= 1u;")
     w("        emmy::tc_fence_after();")
     w("        // this CTA's v rows (B of O): DVP rows (columns of v) x KC keys in 32-key chunks, hi and lo")
+    w("        // consecutive threads take consecutive keys: a warp's stores cover 32 words of the same rows")
     w("        for (int e = tid; e < KC * (DVP / 4); e += 128) {")
-    w("            const int kl_ = e / (DVP / 4), j4 = e % (DVP / 4);")
+    w("            const int kl_ = e % KC, j4 = e / KC;")
     w("            const int key = kbeg + kl_;")
     w("            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);")
     w(f"            if (key < SK && 4 * j4 < DV) x = emmy_ld4({vp} + (long long)key * DV + 4 * j4, v_al);")
@@ -430,10 +437,12 @@ constexpr uint64_t WAIT_NS = 2000000000ull;
             w("        emmy::cluster_sync();")
             for fi, (a, op, accum) in enumerate(accs):
                 cur = rem.as_f32(a)
-                w(f"        {{ float tot = {cur};")
-                w("          #pragma unroll 1")
+                w(f"        {{ float tot = {cur}, got[CL];")
+                w("          #pragma unroll")
+                w(f"          for (int rr = 0; rr < CL; ++rr) got[rr] = emmy_dsmem_ld(emmy::mapa(&stats[{slot + fi} * 128 + tid], (uint32_t)rr));")
+                w("          #pragma unroll")
                 w("          for (int rr = 0; rr < CL; ++rr)")
-                w(f"              tot = {combine_code(op, 'tot', f'emmy_dsmem_ld(emmy::mapa(&stats[{slot + fi} * 128 + tid], (uint32_t)rr))')};")
+                w(f"              tot = {combine_code(op, 'tot', 'got[rr]')};")
                 L.extend(rem.lines)
                 rem.lines = []
                 var = rem.declare(a, "f32")
@@ -470,9 +479,11 @@ constexpr uint64_t WAIT_NS = 2000000000ull;
     w("        // rows [crank * 128 / CL, (crank + 1) * 128 / CL): the CL partials added in CTA order")
     w("        for (int e = tid; e < (128 / CL) * DV; e += 128) {")
     w("            const int r = (int)crank * (128 / CL) + e / DV, jj = e % DV;")
-    w("            float tot = 0.0f;")
-    w("            #pragma unroll 1")
-    w("            for (int rr = 0; rr < CL; ++rr) tot += emmy_dsmem_ld(emmy::mapa(&opart[r * DVP + jj], (uint32_t)rr));")
+    w("            float tot = 0.0f, got[CL];")
+    w("            #pragma unroll")
+    w("            for (int rr = 0; rr < CL; ++rr) got[rr] = emmy_dsmem_ld(emmy::mapa(&opart[r * DVP + jj], (uint32_t)rr));")
+    w("            #pragma unroll")
+    w("            for (int rr = 0; rr < CL; ++rr) tot += got[rr];")
     w(f"            if (q0 + r < RE && q0 + r >= RB) {op_}[(q0 + r) * DV + jj] = tot;")
     w("        }")
     w("        emmy::cluster_sync();")

@@ -10,7 +10,9 @@ distinct kernel.
 from __future__ import annotations
 
 import hashlib
+import json
 import os
+import re
 import shutil
 import subprocess
 import tempfile
@@ -92,3 +94,34 @@ def resource_usage(source: str, name: str = "kernel") -> str:
         if proc.returncode != 0:
             raise ToolchainError(proc.stderr[-4000:])
         return proc.stderr
+
+
+def register_usage(source: str, name: str = "kernel") -> dict:
+    """Registers, barriers and spill bytes per entry of ``source`` as
+    ``ptxas -v`` reports them for sm_100a, cached like the builds."""
+    key = _key(source, "ptxas-v", [])
+    path = cache_dir() / f"{name}-{key}.regs.json"
+    if path.is_file():
+        return json.loads(path.read_text())
+    out: dict[str, dict] = {}
+    cur = None
+    for line in resource_usage(source, name).splitlines():
+        m = re.search(r"Compiling entry function '([^']+)'", line)
+        if m:
+            cur = out.setdefault(m.group(1), {})
+            continue
+        if cur is None:
+            continue
+        m = re.search(r"Used (\d+) registers", line)
+        if m:
+            cur["registers"] = int(m.group(1))
+            b = re.search(r"used (\d+) barriers", line)
+            if b:
+                cur["barriers"] = int(b.group(1))
+        m = re.search(r"(\d+) bytes spill stores, (\d+) bytes spill loads", line)
+        if m:
+            cur["spill_stores"], cur["spill_loads"] = int(m.group(1)), int(m.group(2))
+    tmp = path.with_suffix(path.suffix + f".tmp{os.getpid()}")
+    tmp.write_text(json.dumps(out))
+    os.replace(tmp, path)
+    return out

@@ -91,3 +91,16 @@ def test_python_ir_api_matches_reference_constructor_style():
                  {"block": [128, 1, 1], "grid": [1, 1, 1]})
     assert c.lower().kernel.family == "pointwise"
     assert c.run().isascii()
+
+
+def test_bundle_reports_register_counts_per_entry():
+    """compile_bundle's ``virt_regs`` (compile.py:3194-3215 reports its virtual
+    registers) carries ptxas's per-entry register and spill counts for sm_100a:
+    the drop-in entry and, where there is one, the fast ``__emmy`` twin."""
+    from emmy_ptx_compiler_b200 import compiler
+    from conftest import CASES
+    b = compiler.compile_bundle(next((CASES / "c5_gemm_200x136x300").glob("*.ir.json")))
+    regs = b["virt_regs"]
+    assert regs["registers"] > 0 and regs["spill_stores"] == 0
+    assert set(regs["entries"]) == {b["entry"], b["entry"] + "__emmy"}
+    assert all(e["registers"] <= 255 for e in regs["entries"].values())
