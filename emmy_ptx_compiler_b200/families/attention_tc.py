@@ -39,7 +39,8 @@ from ..errors import UnsupportedIR
 from .common import KernelSource, LaunchPlan, ParamSpec, SM_COUNT, launch_record_source
 from .common import c_ident as _c
 
-T = 128                 # threads: one per query row of the tile
+T = 512                 # threads: 4 column groups x 128 query rows of the tile
+NG = T // 128           # column groups: warp w reads tensor-memory lanes 32 (w % 4).. and keys group w / 4
 SMEM_MAX = 220 * 1024   # dynamic shared memory budget per CTA
 TMEM_COLS_MAX = 512
 
@@ -103,6 +104,8 @@ def layout(plan, shapes: dict, dtypes: dict) -> tuple[dict | None, list[str]]:
         why.append("head sizes not multiples of 4")
     if SQ < 64 or SK < 32:
         why.append("fewer than 64 query rows or 32 keys")
+    if _pad(DV, 32) > 32 * NG:
+        why.append(f"head size {DV} above {32 * NG}")
     if why:
         return None, why
     DP, DVP = _pad(D, 32), _pad(DV, 16)
@@ -113,13 +116,14 @@ def layout(plan, shapes: dict, dtypes: dict) -> tuple[dict | None, list[str]]:
         if CL > 1 and (CL - 1) * KC >= SK:
             continue                   # a CTA without keys
         tcols = 32
-        while tcols < KC + DVP:
+        while tcols < KC + _pad(DVP, 32):
             tcols *= 2
         if KC > 256 or tcols > TMEM_COLS_MAX:
             continue
         r1 = max(2 * (DP // 32) * 128 * 128, 4 * 128 * 128, 128 * DVP * 4)
         r2 = max(2 * (DP // 32) * KC * 128, 2 * (KC // 32) * DVP * 128)
-        nstat = sum(len(s.row_accs) for s in keyloops) * 128 * 4
+        # per accumulator: the cluster exchange slot and the column groups' partials, 128 rows each
+        nstat = sum(len(s.row_accs) for s in keyloops) * 128 * 4 * (1 + NG)
         smem = 1024 + r1 + r2 + nstat + 64
         if smem > SMEM_MAX:
             continue
@@ -143,6 +147,12 @@ __device__ __forceinline__ void emmy_umma_tf32(uint32_t d_tmem, uint64_t a_desc,
         " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
+}
+// 32 lanes x 8 consecutive 32-bit columns: thread t of the warp gets lane (base + t)
+__device__ __forceinline__ void emmy_tmem_ld_x8(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
 }
 __device__ __forceinline__ float4 emmy_ld4(const float *p, bool aligned) {
     return aligned ? *reinterpret_cast<const float4 *>(p) : make_float4(p[0], p[1], p[2], p[3]);
@@ -201,6 +211,7 @@ def generate_tc(kop: ir.KernelOp, plan, lay: dict, shapes: dict, dtypes: dict, a
     keyloops = [s for s in plan.steps if isinstance(s, KeyLoop)]
     last = keyloops[-1]
     wname = lay["W"]
+    nacc = sum(len(st.row_accs) for st in keyloops)
     qp, kp, vp, op_ = ptrs[plan.q], ptrs[plan.kmat], ptrs[plan.v], ptrs[plan.out_name]
     L: list[str] = []
     w = L.append
@@ -209,16 +220,18 @@ def generate_tc(kop: ir.KernelOp, plan, lay: dict, shapes: dict, dtypes: dict, a
     w(f"""namespace {{
 constexpr int SQ = {SQ}, SK = {SK}, D = {D}, DV = {DV}, DP = {DP}, DVP = {DVP};
 constexpr int CL = {CL}, KC = {KC}, NKB = {NKB}, NCH = {NCH}, TCOLS = {lay['TCOLS']};
+constexpr int T = {T}, NG = {NG}, NACC = {max(1, nacc)};
 constexpr uint32_t R1 = {lay['R1']}u, R2 = {lay['R2']}u, NSTAT = {lay['NSTAT']}u, SMEM_BYTES = {lay['SMEM']}u;
 constexpr uint32_t IDESC_S = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(KC >> 3) << 17) | ((128u >> 4) << 24);
 constexpr uint32_t IDESC_O = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(DVP >> 3) << 17) | ((128u >> 4) << 24);
 constexpr uint64_t WAIT_NS = 2000000000ull;
+constexpr int UB = 4;   // float4 loads in flight per thread while operands are staged
 }}  // namespace
 """)
-    w('extern "C" __global__ void __launch_bounds__(128, 1) ' + kop.name + "(" + ", ".join(sig) + ") {")
+    w(f'extern "C" __global__ void __launch_bounds__({T}, 1) ' + kop.name + "(" + ", ".join(sig) + ") {")
     w("    uint32_t dyn_smem;")
     w('    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn_smem));')
-    w("    if (blockDim.x != 128 || blockDim.y != 1 || blockDim.z != 1 || dyn_smem < SMEM_BYTES ||")
+    w("    if (blockDim.x != T || blockDim.y != 1 || blockDim.z != 1 || dyn_smem < SMEM_BYTES ||")
     w("        emmy::cluster_nctarank() != (uint32_t)CL || (gridDim.x % CL) != 0) {")
     w("        if (threadIdx.x == 0 && threadIdx.y == 0 && threadIdx.z == 0) atomicOr(&emmy_status, EMMY_STATUS_BAD_LAUNCH);")
     w("        return;")
@@ -229,11 +242,14 @@ constexpr uint64_t WAIT_NS = 2000000000ull;
     w("    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));")
     w("    uint8_t *const r1 = smem;            // Q hi/lo, then P hi/lo x 2, then the partial O")
     w("    uint8_t *const r2 = smem + R1;       // K hi/lo, then V hi/lo")
-    w("    float *const stats = reinterpret_cast<float *>(smem + R1 + R2);")
+    w("    float *const stats = reinterpret_cast<float *>(smem + R1 + R2);      // [NACC][128]: cluster exchange")
+    w("    float *const gpart = stats + NACC * 128;                             // [NACC][NG][128]: column groups")
     w("    uint64_t *const bars = reinterpret_cast<uint64_t *>(smem + R1 + R2 + NSTAT);  // s_done, o_done, pfree0, pfree1")
     w("    uint32_t *const tmem_holder = reinterpret_cast<uint32_t *>(bars + 4);")
     w("    volatile uint32_t *const abort_flag = tmem_holder + 1;")
-    w("    const int tid = threadIdx.x, warp = tid >> 5;")
+    w("    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;")
+    w("    const int lq = warp & 3, grp = warp >> 2;        // tensor-memory lane quarter, key column group")
+    w("    const int rloc = lq * 32 + lane;                 // this thread's query row in the tile")
     w(f"    const bool q_al = (reinterpret_cast<uintptr_t>({qp}) & 15u) == 0;   // 16-byte loads, else four 4-byte ones")
     w(f"    const bool k_al = (reinterpret_cast<uintptr_t>({kp}) & 15u) == 0;")
     w(f"    const bool v_al = (reinterpret_cast<uintptr_t>({vp}) & 15u) == 0;")
@@ -250,56 +266,119 @@ constexpr uint64_t WAIT_NS = 2000000000ull;
     w("    __syncthreads();")
     w("    emmy::tc_fence_after();")
     w("    const uint32_t tmem = *tmem_holder;")
-    w("    const uint32_t trow = (uint32_t)(warp * 32) << 16;")
+    w("    const uint32_t trow = (uint32_t)(lq * 32) << 16;")
     w("    uint32_t ph_s = 0, ph_o = 0, pissued[2] = {0u, 0u}, pwaited[2] = {0u, 0u};")
     w("    bool ok = true;")
     w("    const int qt0 = (int)(RB / 128);")
     w("    const int nqt = RE > RB ? (int)((RE + 127) / 128) - qt0 : 0;")
     w("    for (int qt = qt0 + (int)(blockIdx.x / CL); qt < qt0 + nqt; qt += (int)(gridDim.x / CL)) {")
     w("        const long long q0 = (long long)qt * 128;")
-    # ---- Q and K operands
+
+    # each loop loads UB float4s per thread before it stores any, so a thread keeps UB loads
+    # in flight (a loop that consumes each load at once waits out the memory latency per element)
+    def batched(total: str, decode: list[str], load: list[str], store: list[str], ind: str = "        ") -> None:
+        w(f"{ind}for (int e0 = tid; e0 < {total}; e0 += T * UB) {{")
+        w(f"{ind}    float4 xb[UB];")
+        w(f"{ind}    #pragma unroll")
+        w(f"{ind}    for (int u = 0; u < UB; ++u) {{")
+        w(f"{ind}        const int e = e0 + u * T;")
+        w(f"{ind}        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);")
+        w(f"{ind}        if (e < {total}) {{")
+        for ln in decode + load:
+            w(f"{ind}            {ln}")
+        w(f"{ind}        }}")
+        w(f"{ind}        xb[u] = x;")
+        w(f"{ind}    }}")
+        w(f"{ind}    #pragma unroll")
+        w(f"{ind}    for (int u = 0; u < UB; ++u) {{")
+        w(f"{ind}        const int e = e0 + u * T;")
+        w(f"{ind}        if (e < {total}) {{")
+        w(f"{ind}            const float4 x = xb[u];")
+        for ln in decode + store:
+            w(f"{ind}            {ln}")
+        w(f"{ind}        }}")
+        w(f"{ind}    }}")
+        w(f"{ind}}}")
+
+    def staged(tag: str, total: int, decode: list[str], load: list[str], ind: str = "        ") -> bool:
+        """Loads of a whole operand into registers (at most 8 float4 per thread), stored later by
+        ``staged_store``: the loads of several operands are then all in flight together."""
+        n = -(-total // T)
+        if n > 8:
+            return False
+        w(f"{ind}float4 {tag}[{n}];")
+        w(f"{ind}#pragma unroll")
+        w(f"{ind}for (int u = 0; u < {n}; ++u) {{")
+        w(f"{ind}    const int e = tid + u * T;")
+        w(f"{ind}    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);")
+        w(f"{ind}    if (e < {total}) {{")
+        for ln in decode + load:
+            w(f"{ind}        {ln}")
+        w(f"{ind}    }}")
+        w(f"{ind}    {tag}[u] = x;")
+        w(f"{ind}}}")
+        return True
+
+    def staged_store(tag: str, total: int, decode: list[str], store: list[str], ind: str = "        ") -> None:
+        n = -(-total // T)
+        w(f"{ind}#pragma unroll")
+        w(f"{ind}for (int u = 0; u < {n}; ++u) {{")
+        w(f"{ind}    const int e = tid + u * T;")
+        w(f"{ind}    if (e < {total}) {{")
+        w(f"{ind}        const float4 x = {tag}[u];")
+        for ln in decode + store:
+            w(f"{ind}        {ln}")
+        w(f"{ind}    }}")
+        w(f"{ind}}}")
+
+    def operand(tag: str, total: int, decode, load, store, deferred: list) -> None:
+        """Stage an operand in registers if it fits (its stores are emitted by ``flush``), else
+        load and store it in batches right here."""
+        if staged(tag, total, decode, load):
+            deferred.append((tag, total, decode, store))
+        else:
+            batched(str(total), decode, load, store)
+
+    def flush(deferred: list) -> None:
+        for tag, total, decode, store in deferred:
+            staged_store(tag, total, decode, store)
+        deferred.clear()
+
+    pending: list = []
     w("        // Q tile (A of S): 128 rows x DP, hi and lo; rows past SQ and columns past D are 0")
-    w("        for (int e = tid; e < 128 * (DP / 4); e += 128) {")
-    w("            const int r = e / (DP / 4), c4 = e % (DP / 4);")
-    w("            const long long gr = q0 + r;")
-    w("            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);")
-    w(f"            if (gr < SQ && 4 * c4 < D) x = emmy_ld4({qp} + gr * D + 4 * c4, q_al);")
-    w("            const uint32_t off = (uint32_t)((4 * c4) / 32) * 16384u + emmy_sw128((uint32_t)r, (uint32_t)((4 * c4) % 32));")
-    w("            emmy_put_split4(r1, r1 + NKB * 16384u, off, x);")
-    w("        }")
+    operand("qreg", 128 * (DP // 4),
+            ["const int r = e / (DP / 4), c4 = e % (DP / 4);", "const long long gr = q0 + r;"],
+            [f"if (gr < SQ && 4 * c4 < D) x = emmy_ld4({qp} + gr * D + 4 * c4, q_al);"],
+            ["const uint32_t off = (uint32_t)((4 * c4) / 32) * 16384u + emmy_sw128((uint32_t)r, (uint32_t)((4 * c4) % 32));",
+             "emmy_put_split4(r1, r1 + NKB * 16384u, off, x);"], pending)
     w("        // this CTA's keys (B of S): KC rows (keys) x DP, hi and lo; keys past SK are 0")
     if plan.k_dk:
         # consecutive threads take consecutive d (one row of kt each, four keys per thread), so
         # each store instruction of a warp writes 32 different words of the same key rows
-        w("        for (int e = tid; e < DP * (KC / 4); e += 128) {")
-        w("            const int d = e % DP, k4 = e / DP;")
-        w("            const int key0 = kbeg + 4 * k4;")
-        w("            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);")
-        w("            if (d < D) {")
-        w("                if (key0 + 3 < SK) {")
-        w(f"                    x = emmy_ld4({kp} + (long long)d * SK + key0, k_al && (SK % 4) == 0);")
-        w("                } else {")
-        w(f"                    if (key0 < SK) x.x = {kp}[(long long)d * SK + key0];")
-        w(f"                    if (key0 + 1 < SK) x.y = {kp}[(long long)d * SK + key0 + 1];")
-        w(f"                    if (key0 + 2 < SK) x.z = {kp}[(long long)d * SK + key0 + 2];")
-        w("                }")
-        w("            }")
-        w("            const float xs[4] = {x.x, x.y, x.z, x.w};")
-        w("            #pragma unroll")
-        w("            for (int u = 0; u < 4; ++u) {")
-        w("                const uint32_t off = (uint32_t)(d / 32) * (KC * 128u) + emmy_sw128((uint32_t)(4 * k4 + u), (uint32_t)(d % 32));")
-        w("                emmy_put_split(r2, r2 + NKB * KC * 128u, off, xs[u]);")
-        w("            }")
-        w("        }")
+        operand("kreg", DP * (KC // 4),
+                ["const int d = e % DP, k4 = e / DP;", "const int key0 = kbeg + 4 * k4;"],
+                ["if (d < D) {",
+                 "    if (key0 + 3 < SK) {",
+                 f"        x = emmy_ld4({kp} + (long long)d * SK + key0, k_al && (SK % 4) == 0);",
+                 "    } else {",
+                 f"        if (key0 < SK) x.x = {kp}[(long long)d * SK + key0];",
+                 f"        if (key0 + 1 < SK) x.y = {kp}[(long long)d * SK + key0 + 1];",
+                 f"        if (key0 + 2 < SK) x.z = {kp}[(long long)d * SK + key0 + 2];",
+                 "    }",
+                 "}"],
+                ["const float xs[4] = {x.x, x.y, x.z, x.w};",
+                 "#pragma unroll",
+                 "for (int q = 0; q < 4; ++q) {",
+                 "    const uint32_t off = (uint32_t)(d / 32) * (KC * 128u) + emmy_sw128((uint32_t)(4 * k4 + q), (uint32_t)(d % 32));",
+                 "    emmy_put_split(r2, r2 + NKB * KC * 128u, off, xs[q]);",
+                 "}"], pending)
     else:
-        w("        for (int e = tid; e < KC * (DP / 4); e += 128) {")
-        w("            const int r = e / (DP / 4), c4 = e % (DP / 4);")
-        w("            const int key = kbeg + r;")
-        w("            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);")
-        w(f"            if (key < SK && 4 * c4 < D) x = emmy_ld4({kp} + (long long)key * D + 4 * c4, k_al);")
-        w("            const uint32_t off = (uint32_t)((4 * c4) / 32) * (KC * 128u) + emmy_sw128((uint32_t)r, (uint32_t)((4 * c4) % 32));")
-        w("            emmy_put_split4(r2, r2 + NKB * KC * 128u, off, x);")
-        w("        }")
+        operand("kreg", KC * (DP // 4),
+                ["const int r = e / (DP / 4), c4 = e % (DP / 4);", "const int key = kbeg + r;"],
+                [f"if (key < SK && 4 * c4 < D) x = emmy_ld4({kp} + (long long)key * D + 4 * c4, k_al);"],
+                ["const uint32_t off = (uint32_t)((4 * c4) / 32) * (KC * 128u) + emmy_sw128((uint32_t)r, (uint32_t)((4 * c4) % 32));",
+                 "emmy_put_split4(r2, r2 + NKB * KC * 128u, off, x);"], pending)
+    flush(pending)
     w("        emmy_fence_async_smem();")
     w("        emmy::tc_fence_before();")
     w("        __syncthreads();")
@@ -321,27 +400,29 @@ constexpr uint64_t WAIT_NS = 2000000000ull;
     w("            emmy::umma_commit(&bars[0]);")
     w("        }")
     w("        __syncwarp();")
+    w("        // this CTA's v rows (B of O): DVP rows (columns of v) x KC keys in 32-key chunks, hi and lo;")
+    w("        // consecutive threads take consecutive keys, so a warp's stores cover 32 words of the same rows.")
+    w("        // Loaded while the score MMAs run, stored over the K operand once they are done")
+    v_decode = ["const int kl_ = e % KC, j4 = e / KC;", "const int key = kbeg + kl_;"]
+    v_load = [f"if (key < SK && 4 * j4 < DV) x = emmy_ld4({vp} + (long long)key * DV + 4 * j4, v_al);"]
+    v_store = ["const float xs[4] = {x.x, x.y, x.z, x.w};",
+               "#pragma unroll",
+               "for (int q = 0; q < 4; ++q) {",
+               "    const uint32_t off = (uint32_t)(kl_ / 32) * (DVP * 128u) + emmy_sw128((uint32_t)(4 * j4 + q), (uint32_t)(kl_ % 32));",
+               "    emmy_put_split(r2, r2 + NCH * DVP * 128u, off, xs[q]);",
+               "}"]
+    v_early = staged("vreg", KC * (DVP // 4), v_decode, v_load)
     w("        if (!emmy::mbar_wait(&bars[0], ph_s, abort_flag, EMMY_STATUS_TIMEOUT_MMA, WAIT_NS)) ok = false;")
     w("        ph_s ^= 1u;")
     w("        emmy::tc_fence_after();")
-    w("        // this CTA's v rows (B of O): DVP rows (columns of v) x KC keys in 32-key chunks, hi and lo")
-    w("        // consecutive threads take consecutive keys: a warp's stores cover 32 words of the same rows")
-    w("        for (int e = tid; e < KC * (DVP / 4); e += 128) {")
-    w("            const int kl_ = e % KC, j4 = e / KC;")
-    w("            const int key = kbeg + kl_;")
-    w("            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);")
-    w(f"            if (key < SK && 4 * j4 < DV) x = emmy_ld4({vp} + (long long)key * DV + 4 * j4, v_al);")
-    w("            const float xs[4] = {x.x, x.y, x.z, x.w};")
-    w("            #pragma unroll")
-    w("            for (int u = 0; u < 4; ++u) {")
-    w("                const uint32_t off = (uint32_t)(kl_ / 32) * (DVP * 128u) + emmy_sw128((uint32_t)(4 * j4 + u), (uint32_t)(kl_ % 32));")
-    w("                emmy_put_split(r2, r2 + NCH * DVP * 128u, off, xs[u]);")
-    w("            }")
-    w("        }")
+    if v_early:
+        staged_store("vreg", KC * (DVP // 4), v_decode, v_store)
+    else:
+        batched(str(KC * (DVP // 4)), v_decode, v_load, v_store)
     w("        emmy_fence_async_smem();")
     w("        __syncthreads();")
-    # ---- the IR's passes
-    w("        const long long row = q0 + tid;")
+    # ---- the IR's passes: thread (rloc, grp) takes keys [8 grp, 8 grp + 8) of every 32-key chunk
+    w("        const long long row = q0 + rloc;")
     rem = Emitter(shapes, dtypes, ptrs, indent="        ")
     rem.fusable = fus
     rem.env.update(scalar_env)
@@ -349,32 +430,30 @@ constexpr uint64_t WAIT_NS = 2000000000ull;
     slot = 0
     for st in plan.steps:
         if not isinstance(st, KeyLoop):
-            s = st[1]
-            if isinstance(s, ir.Init) and s.name in plan.cell_accs:
+            s_ = st[1]
+            if isinstance(s_, ir.Init) and s_.name in plan.cell_accs:
                 continue
-            rem.run((s,))
+            rem.run((s_,))
             continue
         final = st is last
         accs = []
+        L.extend(rem.lines)
+        rem.lines = []
         for a, op in st.row_accs:
             accum = next(t for t in st.post if isinstance(t, ir.Accum) and t.name == a)
             accs.append((a, op, accum))
-            L.extend(rem.lines)
-            rem.lines = []
             w(f"        float part_{_c(a)} = {f32_lit(identity_of(op))};")
-        L.extend(rem.lines)
-        rem.lines = []
-        w(f"        // key loop over {st.loop.axis.name}: scores from tensor memory, 32 keys at a time")
+        w(f"        // key loop over {st.loop.axis.name}: scores from tensor memory, 8 keys of each 32-key chunk per thread")
         w("        #pragma unroll 1")
         w("        for (int ch = 0; ch < NCH; ++ch) {")
-        w("            uint32_t sreg[32];")
-        w("            emmy::tmem_ld_32x32b_x32(tmem + trow + (uint32_t)(ch * 32), sreg);")
+        w("            uint32_t sreg[8];")
+        w("            emmy_tmem_ld_x8(tmem + trow + (uint32_t)(ch * 32 + 8 * grp), sreg);")
         w("            emmy::tmem_ld_wait();")
         if final:
-            w("            float pw[32];")
+            w("            float pw[8];")
         w("            #pragma unroll")
-        w("            for (int kk = 0; kk < 32; ++kk) {")
-        w("                const int key = kbeg + ch * 32 + kk;")
+        w("            for (int kk = 0; kk < 8; ++kk) {")
+        w("                const int key = kbeg + ch * 32 + 8 * grp + kk;")
         if final:
             w("                pw[kk] = 0.0f;")
         w("                if (key < SK) {")
@@ -398,18 +477,15 @@ constexpr uint64_t WAIT_NS = 2000000000ull;
         w("                }")
         w("            }")
         if final:
-            w("            // P chunk (A of O): this thread's row of 32 weights, hi and lo, into buffer ch & 1")
+            w("            // P chunk (A of O): words [8 grp, 8 grp + 8) of this row, hi and lo, into buffer ch & 1")
             w("            const int b = ch & 1;")
             w("            if (pissued[b] > pwaited[b]) {")
             w("                if (!emmy::mbar_wait(&bars[2 + b], pwaited[b] & 1u, abort_flag, EMMY_STATUS_TIMEOUT_MMA, WAIT_NS)) ok = false;")
             w("                ++pwaited[b];")
             w("            }")
             w("            uint8_t *const ph = r1 + (uint32_t)b * 32768u, *const pl = ph + 16384u;")
-            w("            #pragma unroll")
-            w("            for (int c = 0; c < 8; ++c) {")
-            w("                const float4 x = make_float4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]);")
-            w("                emmy_put_split4(ph, pl, emmy_sw128((uint32_t)tid, (uint32_t)(4 * c)), x);")
-            w("            }")
+            w("            emmy_put_split4(ph, pl, emmy_sw128((uint32_t)rloc, (uint32_t)(8 * grp)), make_float4(pw[0], pw[1], pw[2], pw[3]));")
+            w("            emmy_put_split4(ph, pl, emmy_sw128((uint32_t)rloc, (uint32_t)(8 * grp + 4)), make_float4(pw[4], pw[5], pw[6], pw[7]));")
             w("            emmy_fence_async_smem();")
             w("            emmy::tc_fence_before();")
             w("            __syncthreads();")
@@ -431,15 +507,24 @@ constexpr uint64_t WAIT_NS = 2000000000ull;
             w("            ++pissued[b];")
         w("        }")
         if accs:
-            w("        // partial row values of this CTA's keys -> every CTA of the cluster, combined in CTA order")
+            w("        // row partials: the column groups in group order, then the cluster's CTAs in CTA order")
             for fi, (a, op, accum) in enumerate(accs):
-                w(f"        stats[{slot + fi} * 128 + tid] = part_{_c(a)};")
+                w(f"        gpart[({slot + fi} * NG + grp) * 128 + rloc] = part_{_c(a)};")
+            w("        __syncthreads();")
+            w("        if (grp == 0) {")
+            for fi, (a, op, accum) in enumerate(accs):
+                w(f"            float c = gpart[({slot + fi} * NG) * 128 + rloc];")
+                w("            #pragma unroll")
+                w("            for (int g = 1; g < NG; ++g)")
+                w(f"                c = {combine_code(op, 'c', f'gpart[({slot + fi} * NG + g) * 128 + rloc]')};")
+                w(f"            stats[{slot + fi} * 128 + rloc] = c;")
+            w("        }")
             w("        emmy::cluster_sync();")
             for fi, (a, op, accum) in enumerate(accs):
                 cur = rem.as_f32(a)
                 w(f"        {{ float tot = {cur}, got[CL];")
                 w("          #pragma unroll")
-                w(f"          for (int rr = 0; rr < CL; ++rr) got[rr] = emmy_dsmem_ld(emmy::mapa(&stats[{slot + fi} * 128 + tid], (uint32_t)rr));")
+                w(f"          for (int rr = 0; rr < CL; ++rr) got[rr] = emmy_dsmem_ld(emmy::mapa(&stats[{slot + fi} * 128 + rloc], (uint32_t)rr));")
                 w("          #pragma unroll")
                 w("          for (int rr = 0; rr < CL; ++rr)")
                 w(f"              tot = {combine_code(op, 'tot', 'got[rr]')};")
@@ -465,19 +550,20 @@ constexpr uint64_t WAIT_NS = 2000000000ull;
     w("            }")
     w("        emmy::tc_fence_after();")
     w("        float *const opart = reinterpret_cast<float *>(r1);")
-    w("        #pragma unroll 1")
-    w("        for (int c = 0; c < DVP; c += 32) {")
+    w("        if (grp * 32 < DVP) {")
     w("            uint32_t oreg[32];")
-    w("            emmy::tmem_ld_32x32b_x32(tmem + trow + (uint32_t)(KC + c), oreg);")
+    w("            emmy::tmem_ld_32x32b_x32(tmem + trow + (uint32_t)(KC + 32 * grp), oreg);")
     w("            emmy::tmem_ld_wait();")
     w("            #pragma unroll")
     w("            for (int jj = 0; jj < 32; ++jj)")
-    w("                if (c + jj < DVP) opart[tid * DVP + c + jj] = __uint_as_float(oreg[jj]);")
+    w("                if (32 * grp + jj < DVP) opart[rloc * DVP + 32 * grp + jj] = __uint_as_float(oreg[jj]);")
     w("        }")
+    if DVP > 32 * NG:
+        raise UnsupportedIR(f"head size {DV} above {32 * NG}")
     w("        emmy::tc_fence_before();")
     w("        emmy::cluster_sync();")
     w("        // rows [crank * 128 / CL, (crank + 1) * 128 / CL): the CL partials added in CTA order")
-    w("        for (int e = tid; e < (128 / CL) * DV; e += 128) {")
+    w("        for (int e = tid; e < (128 / CL) * DV; e += T) {")
     w("            const int r = (int)crank * (128 / CL) + e / DV, jj = e % DV;")
     w("            float tot = 0.0f, got[CL];")
     w("            #pragma unroll")
@@ -506,6 +592,6 @@ constexpr uint64_t WAIT_NS = 2000000000ull;
                         range_total=SQ, range_align=128, range_bytes=rb)
     L.append(launch_record_source("attention", launch, params))
     notes = {"kernel": "attention_tcgen05_tf32x3", "cluster": CL, "keys_per_cta": KC, "query_tile": 128,
-             "smem": lay["SMEM"], "tmem_cols": lay["TCOLS"], "weights": wname}
+             "threads": T, "smem": lay["SMEM"], "tmem_cols": lay["TCOLS"], "weights": wname}
     return KernelSource(entry=kop.name, source="\n".join(L), launch=launch, params=params,
                         family="attention", notes=notes)

@@ -43,7 +43,7 @@ GROUP_M = 16
 # CTA-pair kernel schedule knobs (results do not depend on them): row-tiles per
 # column sweep, C stores ("wb" write-back, "cs" streaming), L2 policies of the
 # A and B tile loads (None, "evict_last", "evict_first")
-PAIR_TUNE = {"group_m": 16, "c_store": "wb", "a_policy": None, "b_policy": None,
+PAIR_TUNE = {"group_m": 8, "c_store": "wb", "a_policy": None, "b_policy": None,
              # failure-detection tests only: a shorter limit for every bounded wait, and a
              # producer that leaves out its first TMA load (CTA 1 of cluster 0, first tile),
              # so that the leader's stage never fills and the bounded waits run out
