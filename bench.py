@@ -52,7 +52,7 @@ DRAM_TRAFFIC = {
     "c2_gelu_full": 1073930240 + 1024718592,
     "c3_rowsummax_full": 2147724544 + 3113472,
     "c4_sum_full": 8 * (1073763072 + 3136256),
-    "c5_gemm_full": 6476781312 + 532221952,
+    "c5_gemm_full": 5619480320 + 530271232,
 }
 
 CONFIGS = {

@@ -305,6 +305,7 @@ def generate(kop: ir.KernelOp, plan: ReductionPlan, shapes: dict, dtypes: dict, 
     w(_RED_HELPERS)
     if xchg:
         w('#include "emmy_xchg_dev.cuh"')
+        L.extend(_xchg_function(accs, _c(kop.name)))
     if ch > 1:
         w(f"__device__ float emmy_red_partials[{nacc * rows * ch}];")
         w(f"__device__ unsigned int emmy_red_arrivals[{rows}];")
@@ -378,7 +379,7 @@ def generate(kop: ir.KernelOp, plan: ReductionPlan, shapes: dict, dtypes: dict, 
     if ch == 1:
         w("            if (lane == 0) {")
         if xchg:
-            L.extend(_xchg_combine(accs, "b_", "                "))
+            L.extend(_xchg_combine(accs, "b_", "                ", _c(kop.name)))
         L.extend(_epilogue(plan, shapes, dtypes, ptrs, scalar_env, {a: f"b_{_c(a)}" for a, _ in accs},
                            "                "))
         w("            }")
@@ -414,7 +415,7 @@ def generate(kop: ir.KernelOp, plan: ReductionPlan, shapes: dict, dtypes: dict, 
             w(f"                for (int off = 16; off > 0; off >>= 1) f_{_c(a)} = {combine_code(op, f'f_{_c(a)}', f'__shfl_xor_sync(0xffffffffu, f_{_c(a)}, off)')};")
         w("                if (lane == 0) {")
         if xchg:
-            L.extend(_xchg_combine(accs, "f_", "                    "))
+            L.extend(_xchg_combine(accs, "f_", "                    ", _c(kop.name)))
         L.extend(_epilogue(plan, shapes, dtypes, ptrs, scalar_env, {a: f"f_{_c(a)}" for a, _ in accs},
                            "                    "))
         w("                    emmy_red_arrivals[row] = 0u;")
@@ -448,23 +449,39 @@ XCHG_MAX_VALUES = 4
 XCHG_OPS = ("add", "sum", "max", "maximum", "amax", "min", "minimum", "amin")
 
 
-def _xchg_combine(accs, prefix: str, ind: str) -> list[str]:
-    """In the thread holding the row's final values: with an exchange
-    parameter, replace each value by the combine of every GPU's value in rank
+def _xchg_function(accs, name: str) -> list[str]:
+    """A separate (not inlined) device function for the cross-GPU combine, so the
+    exchange's arrays do not weigh on the register allocation of the streaming
+    loop: every GPU's values exchanged, each accumulator's combined in rank
     order (NaN when the exchange failed)."""
-    out = [f"{ind}if (emmy_xa) {{",
-           f"{ind}    float emmy_v[{len(accs)}] = {{{', '.join(prefix + _c(a) for a, _ in accs)}}};",
-           f"{ind}    float emmy_g[{len(accs)} * EMMY_XCHG_MAX_RANKS_DEV];",
-           f"{ind}    const bool emmy_ok = emmy_xchg_exchange(*emmy_xa, emmy_v, {len(accs)}, emmy_g);"]
+    lanes = "xyzw"
+    out = [f"static __device__ __noinline__ float4 emmy_red_combine_{name}(const EmmyXchgArgs *xa, float4 in) {{",
+           f"    const float v[4] = {{in.x, in.y, in.z, in.w}};",
+           f"    float g[{len(accs)} * EMMY_XCHG_MAX_RANKS_DEV];",
+           "    float4 out = in;",
+           f"    if (!emmy_xchg_exchange(*xa, v, {len(accs)}, g)) {{",
+           "        const float nan = __int_as_float(0x7fffffff);",
+           "        return make_float4(nan, nan, nan, nan);",
+           "    }"]
     for i, (a, op) in enumerate(accs):
-        v = prefix + _c(a)
-        out += [f"{ind}    if (emmy_ok) {{",
-                f"{ind}        {v} = emmy_g[{i} * emmy_xa->nranks];",
-                f"{ind}        for (unsigned r = 1; r < emmy_xa->nranks; ++r)"
-                f" {v} = {combine_code(op, v, f'emmy_g[{i} * emmy_xa->nranks + r]')};",
-                f"{ind}    }} else {{",
-                f"{ind}        {v} = __int_as_float(0x7fffffff);",
-                f"{ind}    }}"]
+        out += ["    {",
+                f"        float c = g[{i} * xa->nranks];",
+                f"        for (unsigned r = 1; r < xa->nranks; ++r) c = {combine_code(op, 'c', f'g[{i} * xa->nranks + r]')};",
+                f"        out.{lanes[i]} = c;",
+                "    }"]
+    out += ["    return out;", "}"]
+    return out
+
+
+def _xchg_combine(accs, prefix: str, ind: str, name: str) -> list[str]:
+    """In the thread holding the row's final values: with an exchange
+    parameter, replace each value by the combine of every GPU's value."""
+    lanes = "xyzw"
+    vals = [prefix + _c(a) for a, _ in accs] + ["0.0f"] * (4 - len(accs))
+    out = [f"{ind}if (emmy_xa) {{",
+           f"{ind}    const float4 emmy_r = emmy_red_combine_{name}(emmy_xa, make_float4({', '.join(vals)}));"]
+    for i, (a, _) in enumerate(accs):
+        out.append(f"{ind}    {prefix}{_c(a)} = emmy_r.{lanes[i]};")
     out.append(f"{ind}}}")
     return out
 

@@ -155,17 +155,19 @@ def _seeded_device_inputs(spec: CaseSpec, device: int, seed: int = 0) -> dict:
 
 
 def main(argv=None) -> int:
-    """``python -m emmy_ptx_compiler_b200.harness CASE_DIR [--iters N]``: compile
-    a fixture, launch it N times on seeded device inputs, print the mean
-    device time per launch (used for profiler captures of one kernel)."""
+    """``python -m emmy_ptx_compiler_b200.harness CASE_DIR [--iters N] [--options JSON]``:
+    compile a fixture (with lowering options, e.g. a GEMM tuning), launch it once
+    and then N times on seeded device inputs, print the mean device time per
+    launch (used for profiler captures of one kernel)."""
     import argparse
     ap = argparse.ArgumentParser()
     ap.add_argument("case_dir")
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--device", type=int, default=0)
+    ap.add_argument("--options", default="{}", help="lowering options as JSON (compiler.lower)")
     ns = ap.parse_args(argv)
     torch = _torch()
-    case = DeviceCase(ns.case_dir, ns.device)
+    case = DeviceCase(ns.case_dir, ns.device, options=json.loads(ns.options))
     bufs = _seeded_device_inputs(case.spec, ns.device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     case.launch(bufs)
