@@ -305,6 +305,10 @@ int launch_locked(emmy_module *m, const uint64_t *args, int nargs, const uint32_
                         (unsigned long long)range[0], (unsigned long long)range[1],
                         (unsigned long long)m->rec.range_total, (unsigned long long)al);
         if (range[0] == range[1]) return EMMY_OK;
+        if (!(grid && block) && (m->rec.flags & EMMY_LR_GRID_UNITS)) {
+            const uint64_t units = range[1] - range[0];
+            if (units < g[0]) g[0] = static_cast<uint32_t>(units);
+        }
     }
     // fixed-size parameter tables: a launch allocates nothing on the host
     constexpr int kMaxArgs = 64;

@@ -25,9 +25,12 @@ class LaunchPlan:
     range_total: int = 0          # 0 = no range parameters
     range_align: int = 1
     range_bytes: list[int] = field(default_factory=list)  # per arg_order parameter
+    # grid_units: a launch over a unit range runs min(grid[0], units in the range) CTAs
+    grid_units: bool = False
 
 FLAG_FILL_GRID = 0x100
 FLAG_RANGE = 0x200
+FLAG_GRID_UNITS = 0x400
 
 
 @dataclass
@@ -90,6 +93,8 @@ def launch_record_source(family: str, launch: LaunchPlan, params: list[ParamSpec
     flags = int(launch.cluster[0])
     if launch.range_total:
         flags |= FLAG_RANGE
+        if launch.grid_units:
+            flags |= FLAG_GRID_UNITS
     rbytes = list(launch.range_bytes) + [0] * (32 - len(launch.range_bytes))
     if launch.fill_waves:
         flags |= FLAG_FILL_GRID

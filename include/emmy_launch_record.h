@@ -68,6 +68,10 @@ enum EmmyParamKind { EMMY_PARAM_PTR = 0, EMMY_PARAM_F32 = 1, EMMY_PARAM_I32 = 2 
  * read whole by every launch.  Range ends are multiples of range_align, or
  * range_total. */
 #define EMMY_LR_RANGE 0x200u
+/* EMMY_LR_GRID_UNITS (with EMMY_LR_RANGE): one CTA per unit of the launch's
+ * range, at most grid[0] CTAs (the kernel strides over any units beyond its
+ * grid).  A launch that passes its own grid keeps it. */
+#define EMMY_LR_GRID_UNITS 0x400u
 
 typedef struct EmmyTmapSpec {
     uint32_t src_param; /* index into arg_order of the global buffer */

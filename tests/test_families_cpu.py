@@ -252,3 +252,23 @@ def test_plain_copy_staging_is_proven_only_when_right(swap):
     kop, shapes, dtypes = _plain_copy_kop(swap)
     got = canon.staged_matmul(kop, shapes, dtypes, {"block": [256, 1, 1]})
     assert (got is None) == swap
+
+
+@pytest.mark.parametrize("cid, per_row", [("f_rmsnorm_bench_16384x8192", True), ("f_softmax_bench_16384x8192", True),
+                                          ("f_rmsnorm_64x1000", False), ("f_l2norm_7x4096", True)])
+def test_row_fused_grid_follows_the_row_range_for_wide_rows(cid, per_row):
+    """Rows of 16 KiB or more get one CTA each: the record asks for
+    EMMY_LR_GRID_UNITS with grid[0] = rows (a range launch then runs one CTA
+    per row of its range); shorter rows keep the occupancy-filled grid."""
+    from emmy_ptx_compiler_b200.families import rownorm
+    from emmy_ptx_compiler_b200.families.common import FLAG_GRID_UNITS, launch_record_source
+    kop, shapes, dtypes, args = _plan_inputs(cid)
+    plan = rownorm.match(kop, shapes, dtypes)
+    ks = rownorm.generate(kop, plan, shapes, dtypes, args, {}, set(plan.outputs))
+    assert ks.notes["cta_per_row"] is per_row
+    assert ks.launch.grid_units is per_row
+    rec = launch_record_source("rownorm", ks.launch, ks.params)
+    flags = int(rec.split("EMMY_LR_VERSION, 4u, ")[1].split("u")[0])
+    assert bool(flags & FLAG_GRID_UNITS) is per_row
+    if per_row:
+        assert ks.launch.grid[0] == plan.rows and not ks.launch.fill_waves

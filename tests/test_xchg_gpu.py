@@ -289,3 +289,31 @@ def test_compiled_reduction_combines_across_two_gpus():
         else:
             want = float(np.float32(np.float32(m0) + np.float32(m1)))
         assert o0 == o1 == want, (cid, o0, o1, want)
+
+
+@pytest.mark.parametrize("cid", ["c4_sum_1048579", "r_max_1024", "r_mean_777"])
+def test_compiled_reduction_exchange_entry_on_one_gpu(cid, cuda_device):
+    """A compiled full-array reduction's <entry>__xchg on a group of one GPU
+    (it exchanges with itself): the same bits as its plain entry, twice in a
+    row, and a clean status word."""
+    import torch
+    from conftest import CASES
+    from emmy_ptx_compiler_b200 import harness, runtime
+    case = harness.DeviceCase(CASES / cid, cuda_device)
+    assert case.bundle["notes"]["cross_gpu_entry"]
+    bufs = harness._seeded_device_inputs(case.spec, cuda_device, seed=21)
+    out = case.spec.outputs[0]
+    case.launch(bufs)
+    torch.cuda.synchronize(cuda_device)
+    want = bufs[out].clone()
+    ex = runtime.Exchange(cuda_device, 1, 0)
+    ex.connect([ex.handle])
+    for _ in range(2):
+        bufs[out].fill_(float("nan"))
+        ex.launch(case.module, [bufs[n] for n in case.spec.arg_order], timeout_ms=2000,
+                  stream=torch.cuda.current_stream(cuda_device).cuda_stream)
+        torch.cuda.synchronize(cuda_device)
+        assert torch.equal(bufs[out].view(torch.int32), want.view(torch.int32))
+    assert ex.status() == 0
+    ex.close()
+    case.module.close()
