@@ -49,6 +49,16 @@ def _scalars(meta: dict | None, dtypes: dict) -> dict[str, str]:
     return out
 
 
+def _pointwise_tune(tune: dict | None) -> dict:
+    """The pointwise generator's schedule knobs a caller may set (every value
+    gives the same results)."""
+    tune = dict(tune or {})
+    bad = set(tune) - {"unroll", "pipeline", "min_blocks"}
+    if bad:
+        raise ValueError(f"unknown pointwise_tune keys: {sorted(bad)}")
+    return tune
+
+
 def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: dict | None,
           options: dict | None = None) -> Lowered:
     """Classify ``kop`` into a family and generate its specialised source.
@@ -56,8 +66,9 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
     ``options`` selects among equivalent schedules (results do not depend on
     it): ``{"gemm_variant": "auto" | "pair" | "single", "gemm_tune": {...}
     (families/gemm.py PAIR_TUNE),
-    "pointwise_pair": "auto" | True | False, "attention_first_pass": "auto" | "tiled",
-    "attention_kernel": "auto" | "tc" | "exact",
+    "pointwise_pair": "auto" | True | False, "pointwise_tune": {"unroll", "pipeline",
+    "min_blocks"}, "attention_first_pass": "auto" | "tiled",
+    "attention_kernel": "auto" | "tc" | "exact", "attention_exchange": "auto" | "cluster" | "grid",
     "family": "schedule"}``; the
     last skips the fast families.  A KernelOp no fast family takes (or one a
     family recognises but cannot specialise) keeps its own schedule."""
@@ -93,7 +104,8 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
         ("attention", lambda: attention.match(kop, shapes, dtypes),
          lambda pl: attention.generate(kop, pl, shapes, dtypes, args, scalars, written,
                                        first_pass=options.get("attention_first_pass", "auto"),
-                                       kernel=options.get("attention_kernel", "auto"))),
+                                       kernel=options.get("attention_kernel", "auto"),
+                                       exchange=options.get("attention_exchange", "auto"))),
         ("gemm", lambda: gemm.match(kop, shapes, dtypes),
          lambda pl: gemm.generate(kop, pl, shapes, dtypes, args, scalars, written,
                                   variant=options.get("gemm_variant", "auto"), meta_threads=meta_threads,
@@ -104,7 +116,8 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
          lambda pl: rownorm.generate(kop, pl, shapes, dtypes, args, scalars, written)),
         ("pointwise", lambda: pointwise.match(kop),
          lambda pl: pointwise.generate(kop, pl, shapes, dtypes, args, scalars, written,
-                                       pair=options.get("pointwise_pair", "auto"))),
+                                       pair=options.get("pointwise_pair", "auto"),
+                                       **_pointwise_tune(options.get("pointwise_tune")))),
     )
     rejected: list[str] = []
     for fam, match, generate in fast:

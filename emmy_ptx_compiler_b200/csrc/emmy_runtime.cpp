@@ -334,13 +334,24 @@ int launch_locked(emmy_module *m, const uint64_t *args, int nargs, const uint32_
         kp[static_cast<size_t>(nargs) + ntm + 1] = &range[1];
     }
     const bool cluster = m->has_rec && (m->rec.flags & 0xFFu) > 1u;
-    if (cluster) {
+    const bool coop = m->has_rec && (m->rec.flags & EMMY_LR_COOPERATIVE);
+    if (cluster || coop) {
         if (!g_drv.cuLaunchKernelEx) return fail(EMMY_ERR_NO_DRIVER, "driver lacks cuLaunchKernelEx");
-        CUlaunchAttribute attr[1];
-        attr[0].id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
-        attr[0].value.clusterDim.x = m->rec.flags & 0xFFu;
-        attr[0].value.clusterDim.y = 1;
-        attr[0].value.clusterDim.z = 1;
+        CUlaunchAttribute attr[2];
+        unsigned nattr = 0;
+        if (cluster) {
+            attr[nattr].id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+            attr[nattr].value.clusterDim.x = m->rec.flags & 0xFFu;
+            attr[nattr].value.clusterDim.y = 1;
+            attr[nattr].value.clusterDim.z = 1;
+            ++nattr;
+        }
+        if (coop) {
+            // every CTA resident at once, or the launch fails (the CTAs wait on one another)
+            attr[nattr].id = CU_LAUNCH_ATTRIBUTE_COOPERATIVE;
+            attr[nattr].value.cooperative = 1;
+            ++nattr;
+        }
         CUlaunchConfig cfg{};
         cfg.gridDimX = g[0];
         cfg.gridDimY = g[1];
@@ -351,7 +362,7 @@ int launch_locked(emmy_module *m, const uint64_t *args, int nargs, const uint32_
         cfg.sharedMemBytes = smem;
         cfg.hStream = reinterpret_cast<CUstream>(stream);
         cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        cfg.numAttrs = nattr;
         CU(g_drv.cuLaunchKernelEx(&cfg, m->fn, kp, nullptr), "cuLaunchKernelEx");
     } else {
         CU(g_drv.cuLaunchKernel(m->fn, g[0], g[1], g[2], b[0], b[1], b[2], smem,

@@ -17,12 +17,15 @@ weights), its per-row statements (reciprocal of the denominator) and its row
 accumulations (max, sum) - runs on CUDA cores with the reference's op table
 (cgen), one thread per query row reading its scores from tensor memory.
 
-A query tile of 128 rows is shared by a cluster of CL CTAs that split the
-keys: each CTA computes its keys' scores and partial row statistics, the
-cluster exchanges the partials through distributed shared memory after every
-key loop (combined in CTA order, so every CTA holds the same row values),
-each CTA multiplies its own keys' weights into a partial ``O``, and the
-partial outputs are added in CTA order, each CTA writing 128 / CL rows.
+A query tile of 128 rows is shared by CL CTAs that split the keys: each CTA
+computes its keys' scores and partial row statistics, the CTAs exchange the
+partials after every key loop (combined in CTA order, so every CTA holds the
+same row values), each CTA multiplies its own keys' weights into a partial
+``O``, and the partial outputs are added in CTA order, each CTA writing
+128 / CL rows.  The exchange goes through distributed shared memory when the
+CL CTAs form a cluster, or through global memory with a counter barrier per
+tile when every CTA of the problem is resident at once under a cooperative
+launch (``layout``'s ``exchange``).
 
 Shared-memory operands use the 128-byte swizzled K-major layout (rows of 32
 f32 words, 16-byte chunk c of row r stored at chunk c ^ (r & 7)); all
@@ -43,6 +46,10 @@ T = 512                 # threads: 4 column groups x 128 query rows of the tile
 NG = T // 128           # column groups: warp w reads tensor-memory lanes 32 (w % 4).. and keys group w / 4
 SMEM_MAX = 220 * 1024   # dynamic shared memory budget per CTA
 TMEM_COLS_MAX = 512
+SM_SMEM_BYTES = 228 * 1024   # shared memory of one SM (each resident CTA also takes 1 KB)
+# clusters of CL CTAs (one CTA per SM) a B200 holds at once (ncu launch__cluster_max_active: 15
+# for clusters of 8); sizes not listed are taken to fit whenever their CTAs do
+CLUSTERS_RESIDENT = {8: 15}
 
 
 def _pad(x: int, m: int) -> int:
@@ -70,8 +77,20 @@ def _dep_pattern(st, plan) -> str | None:
     return w
 
 
-def layout(plan, shapes: dict, dtypes: dict) -> tuple[dict | None, list[str]]:
-    """Tile sizes of the tensor-core kernel for ``plan``, or None with reasons."""
+def layout(plan, shapes: dict, dtypes: dict, exchange: str = "auto") -> tuple[dict | None, list[str]]:
+    """Tile sizes of the tensor-core kernel for ``plan``, or None with reasons.
+
+    ``exchange``: how the CL CTAs of one query tile combine row values and
+    partial outputs.  "cluster": the CTAs form a thread-block cluster and read
+    one another's shared memory.  "grid": plain CTAs under a cooperative launch
+    (all resident at once) that exchange through global memory with a
+    counter barrier per tile.  A cluster of 8 CTAs of about 200 KB of shared
+    memory needs 8 free SMs of one GPC, so a B200 holds 15 such clusters at
+    once: 16 query tiles then run in two rounds, while 128 plain CTAs all fit
+    on its 148 SMs.  "auto" takes "grid" when every CTA fits on the SMs at
+    once and the clusters would not (``CLUSTERS_RESIDENT``), else "cluster":
+    where both fit, the cluster exchange is the faster (a_attn 256 x 64: 17
+    against 23 us; 2048 x 64: 58 against 40 us the other way)."""
     from .attention import KeyLoop
     why: list[str] = []
     SQ, SK, D, DV = plan.SQ, plan.SK, plan.D, plan.DV
@@ -133,6 +152,21 @@ def layout(plan, shapes: dict, dtypes: dict) -> tuple[dict | None, list[str]]:
             break
     if best is None:
         why.append("no cluster split fits shared and tensor memory")
+        return best, why
+    fits = best["CL"] > 1 and best["nq"] * best["CL"] <= SM_COUNT
+    if exchange == "grid" and not fits:
+        why.append(f"{best['nq'] * best['CL']} CTAs do not fit on the SMs at once (grid exchange)")
+        return None, why
+    if exchange not in ("auto", "grid", "cluster"):
+        raise ValueError(f"attention exchange {exchange!r}")
+    crowded = best["nq"] > CLUSTERS_RESIDENT.get(best["CL"], best["nq"])
+    best["XM"] = "grid" if exchange == "grid" or (exchange == "auto" and fits and crowded) else "cluster"
+    best["SMEM_LAUNCH"] = best["SMEM"]
+    if best["XM"] == "grid":
+        # CTAs of one tile wait on one another, and tcgen05.alloc waits for free columns: no SM
+        # may hold more of these CTAs than its tensor memory serves, so pad the shared memory
+        per_sm = TMEM_COLS_MAX // best["TCOLS"]
+        best["SMEM_LAUNCH"] = max(best["SMEM"], SM_SMEM_BYTES // (per_sm + 1) - 1024 + 1)
     return best, why
 
 
@@ -184,6 +218,53 @@ __device__ __forceinline__ void emmy_put_split4(uint8_t *hi, uint8_t *lo, uint32
 }  // namespace
 """
 
+# barrier of the CTAs of one query tile under a cooperative launch (every CTA resident)
+_GRID_HELPERS = r"""
+namespace {
+__device__ __forceinline__ unsigned emmy_ld_acquire_gpu(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Every thread of the CTA calls it.  sync[0] counts arrivals, sync[1] is the generation: the
+// last of the n CTAs to arrive clears the count and advances the generation, the others wait
+// (bounded) for it to advance.  false: the wait ran out, now or in an earlier call of this
+// launch (*failed is set then; later calls return at once).  The CTA's own tensor-core work
+// does not depend on the other CTAs, so its mbarrier waits go on as usual after a failure.
+__device__ __noinline__ bool emmy_group_sync(unsigned *sync, unsigned n, volatile uint32_t *failed,
+                                             uint64_t wait_ns) {
+    __shared__ int ok_s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int ok = *failed == 0u;
+        if (ok) {
+            const unsigned g0 = emmy_ld_acquire_gpu(sync + 1);
+            __threadfence();
+            if (atomicAdd(sync, 1u) == n - 1u) {
+                atomicExch(sync, 0u);
+                __threadfence();
+                atomicAdd(sync + 1, 1u);
+            } else {
+                const uint64_t t0 = emmy::globaltimer();
+                while (emmy_ld_acquire_gpu(sync + 1) == g0) {
+                    if (emmy::globaltimer() - t0 > wait_ns) {
+                        ok = 0;
+                        *failed = 1u;
+                        break;
+                    }
+                    __nanosleep(32);
+                }
+            }
+            __threadfence();
+        }
+        ok_s = ok;
+    }
+    __syncthreads();
+    return ok_s != 0;
+}
+}  // namespace
+"""
+
 
 def generate_tc(kop: ir.KernelOp, plan, lay: dict, shapes: dict, dtypes: dict, args: list[str],
                 scalars: dict[str, str], written: set[str]) -> KernelSource:
@@ -206,6 +287,8 @@ def generate_tc(kop: ir.KernelOp, plan, lay: dict, shapes: dict, dtypes: dict, a
                   for n in scalars}
     SQ, SK, D, DV = plan.SQ, plan.SK, plan.D, plan.DV
     CL, KC, DP, DVP = lay["CL"], lay["KC"], lay["DP"], lay["DVP"]
+    grid_x = lay.get("XM", "cluster") == "grid"
+    GMAX = lay["nq"] * CL
     NKB, NCH = DP // 32, KC // 32
     fus = fusable_products(kop.body)
     keyloops = [s for s in plan.steps if isinstance(s, KeyLoop)]
@@ -226,13 +309,27 @@ constexpr uint32_t IDESC_S = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(KC
 constexpr uint32_t IDESC_O = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(DVP >> 3) << 17) | ((128u >> 4) << 24);
 constexpr uint64_t WAIT_NS = 2000000000ull;
 constexpr int UB = 4;   // float4 loads in flight per thread while operands are staged
+constexpr int GMAX = {GMAX};  // CTAs of the whole problem (CL per query tile)
 }}  // namespace
+""")
+    if grid_x:
+        w(_GRID_HELPERS)
+        w("""namespace {
+// exchange through global memory: row values [CTA][NACC][128], partial outputs [CTA][DVP][128]
+// (column-major, so a warp's stores are contiguous), and one (count, generation) pair per tile
+__device__ __align__(16) float emmy_attn_stats[GMAX * NACC * 128];
+__device__ __align__(16) float emmy_attn_opart[(size_t)GMAX * DVP * 128];
+__device__ unsigned int emmy_attn_sync[2 * (GMAX / CL)];
+}  // namespace
 """)
     w(f'extern "C" __global__ void __launch_bounds__({T}, 1) ' + kop.name + "(" + ", ".join(sig) + ") {")
     w("    uint32_t dyn_smem;")
     w('    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn_smem));')
     w("    if (blockDim.x != T || blockDim.y != 1 || blockDim.z != 1 || dyn_smem < SMEM_BYTES ||")
-    w("        emmy::cluster_nctarank() != (uint32_t)CL || (gridDim.x % CL) != 0) {")
+    if grid_x:
+        w("        gridDim.x > (unsigned)GMAX || gridDim.y != 1 || gridDim.z != 1 || (gridDim.x % CL) != 0) {")
+    else:
+        w("        emmy::cluster_nctarank() != (uint32_t)CL || (gridDim.x % CL) != 0) {")
     w("        if (threadIdx.x == 0 && threadIdx.y == 0 && threadIdx.z == 0) atomicOr(&emmy_status, EMMY_STATUS_BAD_LAUNCH);")
     w("        return;")
     w("    }")
@@ -247,6 +344,8 @@ constexpr int UB = 4;   // float4 loads in flight per thread while operands are 
     w("    uint64_t *const bars = reinterpret_cast<uint64_t *>(smem + R1 + R2 + NSTAT);  // s_done, o_done, pfree0, pfree1")
     w("    uint32_t *const tmem_holder = reinterpret_cast<uint32_t *>(bars + 4);")
     w("    volatile uint32_t *const abort_flag = tmem_holder + 1;")
+    if grid_x:
+        w("    volatile uint32_t *const gfail = tmem_holder + 2;   // a wait for the tile's other CTAs ran out")
     w("    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;")
     w("    const int lq = warp & 3, grp = warp >> 2;        // tensor-memory lane quarter, key column group")
     w("    const int rloc = lq * 32 + lane;                 // this thread's query row in the tile")
@@ -254,11 +353,18 @@ constexpr int UB = 4;   // float4 loads in flight per thread while operands are 
     w(f"    const bool k_al = (reinterpret_cast<uintptr_t>({kp}) & 15u) == 0;")
     w(f"    const bool v_al = (reinterpret_cast<uintptr_t>({vp}) & 15u) == 0;")
     w("    (void)q_al; (void)k_al; (void)v_al;")
-    w("    const uint32_t crank = emmy::cluster_ctarank();")
+    if grid_x:
+        w("    const uint32_t crank = blockIdx.x % CL;           // this CTA's key chunk of its tile")
+        w("    const uint32_t gbase = blockIdx.x - crank;        // first CTA of its tile")
+        w("    unsigned *const gsync = emmy_attn_sync + 2 * (blockIdx.x / CL);")
+    else:
+        w("    const uint32_t crank = emmy::cluster_ctarank();")
     w("    const int kbeg = (int)crank * KC;")
     w("    if (tid == 0) {")
     w("        for (int b = 0; b < 4; ++b) emmy::mbar_init(&bars[b], 1);")
     w("        *abort_flag = 0u;")
+    if grid_x:
+        w("        *gfail = 0u;")
     w("        emmy::fence_barrier_init();")
     w("    }")
     w("    if (warp == 0) { emmy::tmem_alloc(tmem_holder, TCOLS); emmy::tmem_relinquish(); }")
@@ -269,6 +375,8 @@ constexpr int UB = 4;   // float4 loads in flight per thread while operands are 
     w("    const uint32_t trow = (uint32_t)(lq * 32) << 16;")
     w("    uint32_t ph_s = 0, ph_o = 0, pissued[2] = {0u, 0u}, pwaited[2] = {0u, 0u};")
     w("    bool ok = true;")
+    if grid_x:
+        w("    bool gok = true;   // every wait for the tile's other CTAs ended in time")
     w("    const int qt0 = (int)(RB / 128);")
     w("    const int nqt = RE > RB ? (int)((RE + 127) / 128) - qt0 : 0;")
     w("    for (int qt = qt0 + (int)(blockIdx.x / CL); qt < qt0 + nqt; qt += (int)(gridDim.x / CL)) {")
@@ -517,14 +625,23 @@ constexpr int UB = 4;   // float4 loads in flight per thread while operands are 
                 w("            #pragma unroll")
                 w("            for (int g = 1; g < NG; ++g)")
                 w(f"                c = {combine_code(op, 'c', f'gpart[({slot + fi} * NG + g) * 128 + rloc]')};")
-                w(f"            stats[{slot + fi} * 128 + rloc] = c;")
+                if grid_x:
+                    w(f"            emmy_attn_stats[((size_t)blockIdx.x * NACC + {slot + fi}) * 128 + rloc] = c;")
+                else:
+                    w(f"            stats[{slot + fi} * 128 + rloc] = c;")
             w("        }")
-            w("        emmy::cluster_sync();")
+            if grid_x:
+                w("        if (!emmy_group_sync(gsync, CL, gfail, WAIT_NS)) gok = false;")
+            else:
+                w("        emmy::cluster_sync();")
             for fi, (a, op, accum) in enumerate(accs):
                 cur = rem.as_f32(a)
                 w(f"        {{ float tot = {cur}, got[CL];")
                 w("          #pragma unroll")
-                w(f"          for (int rr = 0; rr < CL; ++rr) got[rr] = emmy_dsmem_ld(emmy::mapa(&stats[{slot + fi} * 128 + rloc], (uint32_t)rr));")
+                if grid_x:
+                    w(f"          for (int rr = 0; rr < CL; ++rr) got[rr] = __ldcg(&emmy_attn_stats[((size_t)(gbase + rr) * NACC + {slot + fi}) * 128 + rloc]);")
+                else:
+                    w(f"          for (int rr = 0; rr < CL; ++rr) got[rr] = emmy_dsmem_ld(emmy::mapa(&stats[{slot + fi} * 128 + rloc], (uint32_t)rr));")
                 w("          #pragma unroll")
                 w("          for (int rr = 0; rr < CL; ++rr)")
                 w(f"              tot = {combine_code(op, 'tot', 'got[rr]')};")
@@ -549,32 +666,55 @@ constexpr int UB = 4;   // float4 loads in flight per thread while operands are 
     w("                ++pwaited[b];")
     w("            }")
     w("        emmy::tc_fence_after();")
-    w("        float *const opart = reinterpret_cast<float *>(r1);")
+    if grid_x:
+        w("        float *const opart = emmy_attn_opart + (size_t)blockIdx.x * DVP * 128;")
+    else:
+        w("        float *const opart = reinterpret_cast<float *>(r1);")
     w("        if (grp * 32 < DVP) {")
     w("            uint32_t oreg[32];")
     w("            emmy::tmem_ld_32x32b_x32(tmem + trow + (uint32_t)(KC + 32 * grp), oreg);")
     w("            emmy::tmem_ld_wait();")
     w("            #pragma unroll")
     w("            for (int jj = 0; jj < 32; ++jj)")
-    w("                if (32 * grp + jj < DVP) opart[rloc * DVP + 32 * grp + jj] = __uint_as_float(oreg[jj]);")
+    if grid_x:
+        w("                if (32 * grp + jj < DVP) opart[(32 * grp + jj) * 128 + rloc] = __uint_as_float(oreg[jj]);")
+    else:
+        w("                if (32 * grp + jj < DVP) opart[rloc * DVP + 32 * grp + jj] = __uint_as_float(oreg[jj]);")
     w("        }")
     if DVP > 32 * NG:
         raise UnsupportedIR(f"head size {DV} above {32 * NG}")
     w("        emmy::tc_fence_before();")
-    w("        emmy::cluster_sync();")
+    if grid_x:
+        w("        if (!emmy_group_sync(gsync, CL, gfail, WAIT_NS)) gok = false;")
+    else:
+        w("        emmy::cluster_sync();")
     w("        // rows [crank * 128 / CL, (crank + 1) * 128 / CL): the CL partials added in CTA order")
     w("        for (int e = tid; e < (128 / CL) * DV; e += T) {")
-    w("            const int r = (int)crank * (128 / CL) + e / DV, jj = e % DV;")
+    if grid_x:
+        w("            const int r = (int)crank * (128 / CL) + e % (128 / CL), jj = e / (128 / CL);")
+    else:
+        w("            const int r = (int)crank * (128 / CL) + e / DV, jj = e % DV;")
     w("            float tot = 0.0f, got[CL];")
     w("            #pragma unroll")
-    w("            for (int rr = 0; rr < CL; ++rr) got[rr] = emmy_dsmem_ld(emmy::mapa(&opart[r * DVP + jj], (uint32_t)rr));")
+    if grid_x:
+        w("            for (int rr = 0; rr < CL; ++rr) got[rr] = __ldcg(&emmy_attn_opart[(size_t)(gbase + rr) * DVP * 128 + jj * 128 + r]);")
+    else:
+        w("            for (int rr = 0; rr < CL; ++rr) got[rr] = emmy_dsmem_ld(emmy::mapa(&opart[r * DVP + jj], (uint32_t)rr));")
     w("            #pragma unroll")
     w("            for (int rr = 0; rr < CL; ++rr) tot += got[rr];")
     w(f"            if (q0 + r < RE && q0 + r >= RB) {op_}[(q0 + r) * DV + jj] = tot;")
     w("        }")
-    w("        emmy::cluster_sync();")
+    if grid_x:
+        w("        // the next tile reuses the exchange slots: wait until every CTA of this one has read them")
+        w("        if (qt + (int)(gridDim.x / CL) < qt0 + nqt) {")
+        w("            if (!emmy_group_sync(gsync, CL, gfail, WAIT_NS)) gok = false;")
+        w("        }")
+    else:
+        w("        emmy::cluster_sync();")
     w("    }")
     w("    if (!ok) atomicOr(&emmy_status, EMMY_STATUS_TIMEOUT_MMA);")
+    if grid_x:
+        w("    if (!gok) atomicOr(&emmy_status, EMMY_STATUS_TIMEOUT_REDUCE);")
     w("    emmy::tc_fence_before();")
     w("    __syncthreads();")
     w("    if (warp == 0) { emmy::tc_fence_after(); emmy::tmem_dealloc(tmem, TCOLS); }")
@@ -588,10 +728,13 @@ constexpr int UB = 4;   // float4 loads in flight per thread while operands are 
             rb.append(DV * 4)
         else:
             rb.append(0)
-    launch = LaunchPlan(grid=(grid, 1, 1), block=(T, 1, 1), smem=lay["SMEM"], cluster=(CL, 1, 1),
+    launch = LaunchPlan(grid=(grid, 1, 1), block=(T, 1, 1), smem=lay.get("SMEM_LAUNCH", lay["SMEM"]),
+                        cluster=(1, 1, 1) if grid_x else (CL, 1, 1), cooperative=grid_x,
                         range_total=SQ, range_align=128, range_bytes=rb)
     L.append(launch_record_source("attention", launch, params))
-    notes = {"kernel": "attention_tcgen05_tf32x3", "cluster": CL, "keys_per_cta": KC, "query_tile": 128,
+    notes = {"kernel": "attention_tcgen05_tf32x3", "cluster": 1 if grid_x else CL,
+             "exchange": "grid" if grid_x else "cluster",
+             "ctas_per_tile": CL, "keys_per_cta": KC, "query_tile": 128,
              "threads": T, "smem": lay["SMEM"], "tmem_cols": lay["TCOLS"], "weights": wname}
     return KernelSource(entry=kop.name, source="\n".join(L), launch=launch, params=params,
                         family="attention", notes=notes)

@@ -27,10 +27,13 @@ class LaunchPlan:
     range_bytes: list[int] = field(default_factory=list)  # per arg_order parameter
     # grid_units: a launch over a unit range runs min(grid[0], units in the range) CTAs
     grid_units: bool = False
+    # cooperative: the loader launches every CTA at once (cooperative launch) or fails
+    cooperative: bool = False
 
 FLAG_FILL_GRID = 0x100
 FLAG_RANGE = 0x200
 FLAG_GRID_UNITS = 0x400
+FLAG_COOPERATIVE = 0x800
 
 
 @dataclass
@@ -95,6 +98,8 @@ def launch_record_source(family: str, launch: LaunchPlan, params: list[ParamSpec
         flags |= FLAG_RANGE
         if launch.grid_units:
             flags |= FLAG_GRID_UNITS
+    if launch.cooperative:
+        flags |= FLAG_COOPERATIVE
     rbytes = list(launch.range_bytes) + [0] * (32 - len(launch.range_bytes))
     if launch.fill_waves:
         flags |= FLAG_FILL_GRID

@@ -20,7 +20,9 @@ Such a module carries two entries:
     the drop-in always runs the fast body;
   - row-fused and attention kernels fall back to the IR's own schedule
     (the schedule family: the reference's thread model, compiled for
-    sm_100a), which is what meta.json's geometry was written for;
+    sm_100a), which is what meta.json's geometry was written for; a fast
+    kernel that needs a cooperative launch (CTAs that wait on one another)
+    is never run from the drop-in;
   - the GEMM's drop-in is a separate kernel (families/gemm.py).
 
 The PTX parameter names are nvcc's (``<entry>_param_<i>``), not the
@@ -99,11 +101,23 @@ def attach(ks: KernelSource, kop: ir.KernelOp, shapes: dict, dtypes: dict, args:
         except UnsupportedIR:
             fallback = None
     lines = [src, native]
+    cooperative = ks.launch.cooperative
+    if cooperative and fallback is None:
+        raise UnsupportedIR(f"{name}: a cooperative fast kernel needs the IR's own schedule as its drop-in")
     if fallback is None:
         lines.append(f'extern "C" __global__ void __launch_bounds__({threads}) {name}({", ".join(sig[:n])}) {{\n'
                      f"    {whole}\n}}\n")
         mode = "fast body under every launch" if ks.family == "pointwise" else \
             "fast body; other launches raise EMMY_STATUS_BAD_LAUNCH"
+    elif cooperative:
+        # the fast kernel's CTAs wait on one another, which only a cooperative launch makes safe,
+        # and a kernel cannot tell how it was launched: the drop-in always runs the IR's schedule
+        lines.append(fallback.source)
+        threads = max(threads, 1024 if not meta_threads else meta_threads)
+        lines.append(
+            f'extern "C" __global__ void __launch_bounds__({threads}) {name}({", ".join(sig[:n])}) {{\n'
+            f"    emmy_sched_{c_ident(name)}({', '.join(names[:n])});\n}}\n")
+        mode = "the IR's own schedule under every launch (the fast kernel needs a cooperative launch)"
     else:
         lines.append(fallback.source)
         threads = max(threads, 1024 if not meta_threads else meta_threads)

@@ -72,6 +72,10 @@ enum EmmyParamKind { EMMY_PARAM_PTR = 0, EMMY_PARAM_F32 = 1, EMMY_PARAM_I32 = 2 
  * range, at most grid[0] CTAs (the kernel strides over any units beyond its
  * grid).  A launch that passes its own grid keeps it. */
 #define EMMY_LR_GRID_UNITS 0x400u
+/* EMMY_LR_COOPERATIVE: launched as a cooperative grid (every CTA resident at
+ * once, or the launch fails): the kernel's CTAs wait on one another through
+ * global memory. */
+#define EMMY_LR_COOPERATIVE 0x800u
 
 typedef struct EmmyTmapSpec {
     uint32_t src_param; /* index into arg_order of the global buffer */

@@ -88,14 +88,16 @@ def test_register_tiled_first_pass_matches_tiled_pass(cuda_device):
     assert ok, why
 
 
+@pytest.mark.parametrize("exchange", ["grid", "cluster"])
 @pytest.mark.parametrize("cid", ["a_attn_64x32", "a_attn_256x64", "a_attn_100x48", "a_attn_krows_80x40",
                                  "a_attn_bench_2048x64"])
-def test_tensor_core_kernel_matches_the_exact_kernel(cid, cuda_device):
+def test_tensor_core_kernel_matches_the_exact_kernel(cid, exchange, cuda_device):
     import torch
     from emmy_ptx_compiler_b200 import harness
-    tc = harness.DeviceCase(CASES / cid, cuda_device, options={"attention_kernel": "tc"})
+    tc = harness.DeviceCase(CASES / cid, cuda_device, options={"attention_kernel": "tc", "attention_exchange": exchange})
     ex = harness.DeviceCase(CASES / cid, cuda_device, options={"attention_kernel": "exact"})
     assert tc.bundle["notes"]["kernel"] == "attention_tcgen05_tf32x3"
+    assert tc.bundle["notes"]["exchange"] == exchange
     bufs = harness._seeded_device_inputs(tc.spec, cuda_device, seed=13)
     out = tc.spec.outputs[0]
     got = {}
@@ -112,3 +114,81 @@ def test_tensor_core_kernel_matches_the_exact_kernel(cid, cuda_device):
     assert bad == 0, (cid, float(err.max()))
     tc.module.close()
     ex.module.close()
+
+
+@pytest.mark.parametrize("cid", ["a_attn_256x64", "a_attn_bench_2048x64", "a_attn_krows_80x40"])
+def test_grid_and_cluster_exchanges_give_the_same_bits(cid, cuda_device):
+    """The CTAs of a query tile combine their row values and partial outputs
+    in CTA order either way: through distributed shared memory (a cluster) or
+    through global memory under a cooperative launch.  The bits must agree,
+    launch after launch (the grid exchange's counters return to zero)."""
+    import torch
+    from emmy_ptx_compiler_b200 import harness
+    cases = {x: harness.DeviceCase(CASES / cid, cuda_device, options={"attention_kernel": "tc", "attention_exchange": x})
+             for x in ("grid", "cluster")}
+    bufs = harness._seeded_device_inputs(cases["grid"].spec, cuda_device, seed=17)
+    out = cases["grid"].spec.outputs[0]
+    got = {}
+    for name in ("grid", "cluster", "grid2", "grid3"):
+        case = cases[name.rstrip("23")]
+        b = dict(bufs)
+        b[out] = torch.full_like(bufs[out], float("nan"))
+        case.launch(b)
+        torch.cuda.synchronize(cuda_device)
+        assert case.module.status() == 0, name
+        got[name] = b[out].view(torch.int32)
+    for name in ("cluster", "grid2", "grid3"):
+        assert torch.equal(got["grid"], got[name]), name
+    for case in cases.values():
+        case.module.close()
+
+
+def test_grid_exchange_rejects_a_grid_beyond_its_exchange_slots(cuda_device):
+    """A launch with more CTAs than the module's exchange slots raises
+    EMMY_STATUS_BAD_LAUNCH before any CTA waits on another, and the next
+    launch under the launch record is correct."""
+    import torch
+    from emmy_ptx_compiler_b200 import harness
+    case = harness.DeviceCase(CASES / "a_attn_256x64", cuda_device, options={"attention_exchange": "grid"})
+    assert case.bundle["notes"]["exchange"] == "grid"
+    g = case.bundle["launch"]["grid"][0]
+    bufs = harness._seeded_device_inputs(case.spec, cuda_device, seed=3)
+    out = case.spec.outputs[0]
+    case.launch(bufs)
+    torch.cuda.synchronize(cuda_device)
+    want = bufs[out].clone()
+    bufs[out].fill_(float("nan"))
+    case.launch(bufs, grid=[g + case.bundle["notes"]["ctas_per_tile"], 1, 1], block=[512, 1, 1])
+    torch.cuda.synchronize(cuda_device)
+    assert case.module.status() == 0x8       # EMMY_STATUS_BAD_LAUNCH
+    assert bool(torch.isnan(bufs[out]).all())
+    case.launch(bufs)
+    torch.cuda.synchronize(cuda_device)
+    assert case.module.status() == 0
+    assert torch.equal(bufs[out].view(torch.int32), want.view(torch.int32))
+    case.module.close()
+
+
+def test_grid_exchange_range_launches_compose(cuda_device):
+    """Launches over the two query tiles separately give the whole launch's
+    bits; the CTAs of the tile outside a range wait for nothing."""
+    import torch
+    from emmy_ptx_compiler_b200 import harness
+    case = harness.DeviceCase(CASES / "a_attn_256x64", cuda_device, options={"attention_exchange": "grid"})
+    assert case.bundle["notes"]["exchange"] == "grid"
+    bufs = harness._seeded_device_inputs(case.spec, cuda_device, seed=23)
+    out = case.spec.outputs[0]
+    case.launch(bufs)
+    torch.cuda.synchronize(cuda_device)
+    whole = bufs[out].clone()
+    bufs[out].fill_(float("nan"))
+    order = [bufs[n] for n in case.spec.arg_order]
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    case.module.launch_range(order, 128, 256, stream=stream)
+    torch.cuda.synchronize(cuda_device)
+    assert bool(torch.isnan(bufs[out][:128]).all())
+    case.module.launch_range(order, 0, 128, stream=stream)
+    torch.cuda.synchronize(cuda_device)
+    assert case.module.status() == 0
+    assert torch.equal(bufs[out].view(torch.int32), whole.view(torch.int32))
+    case.module.close()

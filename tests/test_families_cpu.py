@@ -272,3 +272,50 @@ def test_row_fused_grid_follows_the_row_range_for_wide_rows(cid, per_row):
     assert bool(flags & FLAG_GRID_UNITS) is per_row
     if per_row:
         assert ks.launch.grid[0] == plan.rows and not ks.launch.fill_waves
+
+
+def test_attention_exchange_choice_and_launch_record():
+    """The bench shape (16 query tiles x 8 CTAs = 128 CTAs) fits on the SMs at
+    once, so "auto" takes the grid exchange: no cluster, a cooperative launch,
+    enough shared memory that no SM holds two of these CTAs (each takes all
+    512 tensor-memory columns), and a drop-in that never runs the fast body."""
+    from emmy_ptx_compiler_b200 import compiler
+    from emmy_ptx_compiler_b200.families import attention, attention_tc
+    from emmy_ptx_compiler_b200.families.common import FLAG_COOPERATIVE, launch_record_source
+    kop, shapes, dtypes, args = _plan_inputs("a_attn_bench_2048x64")
+    plan = attention.match(kop, shapes, dtypes)
+    lay, why = attention_tc.layout(plan, shapes, dtypes)
+    assert lay["XM"] == "grid" and lay["CL"] == 8 and lay["TCOLS"] == 512
+    assert lay["SMEM_LAUNCH"] > attention_tc.SM_SMEM_BYTES // 2 - 1024
+    cl, _ = attention_tc.layout(plan, shapes, dtypes, exchange="cluster")
+    assert cl["XM"] == "cluster"
+    ks = attention_tc.generate_tc(kop, plan, lay, shapes, dtypes, args, {}, {plan.out_name})
+    assert ks.launch.cooperative and ks.launch.cluster == (1, 1, 1)
+    rec = launch_record_source("attention", ks.launch, ks.params)
+    flags = int(rec.split("EMMY_LR_VERSION, 5u, ")[1].split("u")[0])
+    assert flags & FLAG_COOPERATIVE and (flags & 0xFF) == 1
+    b = compiler.compile_bundle(next((CASES / "a_attn_bench_2048x64").glob("*.ir.json")))
+    assert b["notes"]["exchange"] == "grid"
+    assert b["notes"]["entries"]["drop_in_path"].startswith("the IR's own schedule under every launch")
+
+
+def test_attention_small_problems_keep_the_cluster_exchange():
+    """Two query tiles: both exchanges fit, and the cluster's is the faster."""
+    from emmy_ptx_compiler_b200.families import attention, attention_tc
+    kop, shapes, dtypes, args = _plan_inputs("a_attn_256x64")
+    plan = attention.match(kop, shapes, dtypes)
+    lay, why = attention_tc.layout(plan, shapes, dtypes)
+    assert lay["XM"] == "cluster" and lay["nq"] == 2
+    lay, why = attention_tc.layout(plan, shapes, dtypes, exchange="grid")
+    assert lay["XM"] == "grid"
+
+
+def test_attention_grid_exchange_needs_every_cta_resident():
+    from emmy_ptx_compiler_b200.families import attention, attention_tc
+    kop, shapes, dtypes, args = _plan_inputs("a_attn_bench_2048x64")
+    plan = attention.match(kop, shapes, dtypes)
+    plan.SQ = 128 * 40               # 40 query tiles x 8 CTAs: more CTAs than SMs
+    lay, why = attention_tc.layout(plan, shapes, dtypes)
+    assert lay["XM"] == "cluster"
+    lay, why = attention_tc.layout(plan, shapes, dtypes, exchange="grid")
+    assert lay is None and "do not fit" in why[-1]

@@ -46,6 +46,7 @@ def _ranges(total: int, align: int, pieces: list[int]) -> list[tuple[int, int]]:
     ("c5_gemm_200x136x300", [1, 2]),      # SIMT tiles of 64 rows
     ("f_softmax_64x1000", [3, 10]),       # row-fused: units are rows
     ("a_attn_100x48", [2, 5]),            # attention: blocks of 4 query rows
+    ("a_attn_256x64", [1]),               # tensor-core attention, two query tiles
 ])
 def test_ranges_compose_to_whole(cid, pieces, cuda_device):
     import torch
