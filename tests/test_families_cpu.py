@@ -319,3 +319,17 @@ def test_attention_grid_exchange_needs_every_cta_resident():
     assert lay["XM"] == "cluster"
     lay, why = attention_tc.layout(plan, shapes, dtypes, exchange="grid")
     assert lay is None and "do not fit" in why[-1]
+
+
+def test_pointwise_tune_option_changes_the_schedule_only():
+    """``pointwise_tune`` sets the pointwise generator's unroll / pipelining /
+    occupancy knobs; unknown keys are rejected."""
+    from emmy_ptx_compiler_b200 import compiler
+    ir_path = next((CASES / "c2_gelu_64x1000").glob("*.ir.json"))
+    base = compiler.compile_bundle(ir_path)
+    tuned = compiler.compile_bundle(ir_path, options={"pointwise_tune": {"unroll": 4, "pipeline": False,
+                                                                         "min_blocks": 3}})
+    assert tuned["family"] == base["family"] == "pointwise"
+    assert "__launch_bounds__(256, 3)" in tuned["source"] and tuned["source"] != base["source"]
+    with pytest.raises(ValueError):
+        compiler.compile_bundle(ir_path, options={"pointwise_tune": {"unrol": 4}})
