@@ -143,7 +143,7 @@ def layout(plan, shapes: dict, dtypes: dict, exchange: str = "auto") -> tuple[di
         r2 = max(2 * (DP // 32) * KC * 128, 2 * (KC // 32) * DVP * 128)
         # per accumulator: the cluster exchange slot and the column groups' partials, 128 rows each
         nstat = sum(len(s.row_accs) for s in keyloops) * 128 * 4 * (1 + NG)
-        smem = 1024 + r1 + r2 + nstat + 64
+        smem = 1024 + r1 + r2 + nstat + 64      # 6 mbarriers, the tensor-memory address, 2 flags
         if smem > SMEM_MAX:
             continue
         cand = dict(CL=CL, KC=KC, DP=DP, DVP=DVP, TCOLS=tcols, R1=r1, R2=r2, NSTAT=nstat, SMEM=smem, nq=nq, W=w)
@@ -341,8 +341,9 @@ __device__ unsigned int emmy_attn_sync[2 * (GMAX / CL)];
     w("    uint8_t *const r2 = smem + R1;       // K hi/lo, then V hi/lo")
     w("    float *const stats = reinterpret_cast<float *>(smem + R1 + R2);      // [NACC][128]: cluster exchange")
     w("    float *const gpart = stats + NACC * 128;                             // [NACC][NG][128]: column groups")
-    w("    uint64_t *const bars = reinterpret_cast<uint64_t *>(smem + R1 + R2 + NSTAT);  // s_done, o_done, pfree0, pfree1")
-    w("    uint32_t *const tmem_holder = reinterpret_cast<uint32_t *>(bars + 4);")
+    w("    // s_done, o_done, pfree0, pfree1 (MMA commits); pfull0, pfull1 (one arrival per warp)")
+    w("    uint64_t *const bars = reinterpret_cast<uint64_t *>(smem + R1 + R2 + NSTAT);")
+    w("    uint32_t *const tmem_holder = reinterpret_cast<uint32_t *>(bars + 6);")
     w("    volatile uint32_t *const abort_flag = tmem_holder + 1;")
     if grid_x:
         w("    volatile uint32_t *const gfail = tmem_holder + 2;   // a wait for the tile's other CTAs ran out")
@@ -362,6 +363,7 @@ __device__ unsigned int emmy_attn_sync[2 * (GMAX / CL)];
     w("    const int kbeg = (int)crank * KC;")
     w("    if (tid == 0) {")
     w("        for (int b = 0; b < 4; ++b) emmy::mbar_init(&bars[b], 1);")
+    w("        for (int b = 4; b < 6; ++b) emmy::mbar_init(&bars[b], T / 32);")
     w("        *abort_flag = 0u;")
     if grid_x:
         w("        *gfail = 0u;")
@@ -594,10 +596,13 @@ __device__ unsigned int emmy_attn_sync[2 * (GMAX / CL)];
             w("            uint8_t *const ph = r1 + (uint32_t)b * 32768u, *const pl = ph + 16384u;")
             w("            emmy_put_split4(ph, pl, emmy_sw128((uint32_t)rloc, (uint32_t)(8 * grp)), make_float4(pw[0], pw[1], pw[2], pw[3]));")
             w("            emmy_put_split4(ph, pl, emmy_sw128((uint32_t)rloc, (uint32_t)(8 * grp + 4)), make_float4(pw[4], pw[5], pw[6], pw[7]));")
+            w("            // each warp reports its part of the chunk; only the issuing thread waits for all")
             w("            emmy_fence_async_smem();")
             w("            emmy::tc_fence_before();")
-            w("            __syncthreads();")
+            w("            __syncwarp();")
+            w("            if (lane == 0) emmy::mbar_arrive(&bars[4 + b]);")
             w("            if (tid == 0) {")
+            w("                if (!emmy::mbar_wait(&bars[4 + b], pissued[b] & 1u, abort_flag, EMMY_STATUS_TIMEOUT_MMA, WAIT_NS)) ok = false;")
             w("                emmy::tc_fence_after();")
             w("                const uint32_t pa = emmy::smem_u32(ph), pb = emmy::smem_u32(pl);")
             w("                const uint32_t vh = emmy::smem_u32(r2) + (uint32_t)ch * (DVP * 128u);")
