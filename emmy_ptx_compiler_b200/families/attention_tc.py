@@ -233,11 +233,9 @@ __device__ __forceinline__ unsigned emmy_ld_acquire_gpu(const unsigned *p) {
 // does not depend on the other CTAs, so its mbarrier waits go on as usual after a failure.
 __device__ __noinline__ bool emmy_group_sync(unsigned *sync, unsigned n, volatile uint32_t *failed,
                                              uint64_t wait_ns) {
-    __shared__ int ok_s;
     __syncthreads();
     if (threadIdx.x == 0) {
-        int ok = *failed == 0u;
-        if (ok) {
+        if (*failed == 0u) {
             const unsigned g0 = emmy_ld_acquire_gpu(sync + 1);
             __threadfence();
             if (atomicAdd(sync, 1u) == n - 1u) {
@@ -248,7 +246,6 @@ __device__ __noinline__ bool emmy_group_sync(unsigned *sync, unsigned n, volatil
                 const uint64_t t0 = emmy::globaltimer();
                 while (emmy_ld_acquire_gpu(sync + 1) == g0) {
                     if (emmy::globaltimer() - t0 > wait_ns) {
-                        ok = 0;
                         *failed = 1u;
                         break;
                     }
@@ -257,10 +254,9 @@ __device__ __noinline__ bool emmy_group_sync(unsigned *sync, unsigned n, volatil
             }
             __threadfence();
         }
-        ok_s = ok;
     }
     __syncthreads();
-    return ok_s != 0;
+    return *failed == 0u;
 }
 }  // namespace
 """
