@@ -69,6 +69,7 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
     "pointwise_pair": "auto" | True | False, "pointwise_tune": {"unroll", "pipeline",
     "min_blocks"}, "attention_first_pass": "auto" | "tiled",
     "attention_kernel": "auto" | "tc" | "exact", "attention_exchange": "auto" | "cluster" | "grid",
+    "attention_tune": {...} (families/attention_tc.py TC_TUNE),
     "family": "schedule"}``; the
     last skips the fast families.  A KernelOp no fast family takes (or one a
     family recognises but cannot specialise) keeps its own schedule."""
@@ -105,7 +106,8 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
          lambda pl: attention.generate(kop, pl, shapes, dtypes, args, scalars, written,
                                        first_pass=options.get("attention_first_pass", "auto"),
                                        kernel=options.get("attention_kernel", "auto"),
-                                       exchange=options.get("attention_exchange", "auto"))),
+                                       exchange=options.get("attention_exchange", "auto"),
+                                       tune=options.get("attention_tune"))),
         ("gemm", lambda: gemm.match(kop, shapes, dtypes),
          lambda pl: gemm.generate(kop, pl, shapes, dtypes, args, scalars, written,
                                   variant=options.get("gemm_variant", "auto"), meta_threads=meta_threads,

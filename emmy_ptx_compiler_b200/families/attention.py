@@ -250,18 +250,18 @@ def match(kop: ir.KernelOp, shapes: dict, dtypes: dict) -> AttnPlan | None:
 
 def generate(kop: ir.KernelOp, plan: AttnPlan, shapes: dict, dtypes: dict, args: list[str],
              scalars: dict[str, str], written: set[str], first_pass: str = "auto",
-             kernel: str = "auto", exchange: str = "auto") -> KernelSource:
+             kernel: str = "auto", exchange: str = "auto", tune: dict | None = None) -> KernelSource:
     """``kernel``: "auto" (the tensor-core kernel, families/attention_tc.py,
     when the IR has its shape; else the exact CUDA-core kernel below), "tc"
     or "exact".  ``first_pass`` (exact kernel): "auto" (register-tiled when
     it applies) or "tiled".  ``exchange`` (tensor-core kernel): how the CTAs
     that share a query tile combine their row values, see
-    ``attention_tc.layout``."""
+    ``attention_tc.layout``; ``tune``: ``attention_tc.TC_TUNE``."""
     if kernel in ("auto", "tc"):
         from . import attention_tc
         lay, why_tc = attention_tc.layout(plan, shapes, dtypes, exchange=exchange)
         if lay is not None:
-            return attention_tc.generate_tc(kop, plan, lay, shapes, dtypes, args, scalars, written)
+            return attention_tc.generate_tc(kop, plan, lay, shapes, dtypes, args, scalars, written, tune=tune)
         if kernel == "tc":
             raise UnsupportedIR("no tensor-core attention for this IR: " + "; ".join(why_tc))
     params: list[ParamSpec] = []

@@ -262,8 +262,13 @@ __device__ __noinline__ bool emmy_group_sync(unsigned *sync, unsigned n, volatil
 """
 
 
+# schedule knobs: every wait's limit, and a test-only switch under which CTA 1 leaves out its
+# first arrival at its tile's barrier (grid exchange), so that the other CTAs' waits run out
+TC_TUNE = {"wait_ns": 2_000_000_000, "skip_first_arrive": False}
+
+
 def generate_tc(kop: ir.KernelOp, plan, lay: dict, shapes: dict, dtypes: dict, args: list[str],
-                scalars: dict[str, str], written: set[str]) -> KernelSource:
+                scalars: dict[str, str], written: set[str], tune: dict | None = None) -> KernelSource:
     from .attention import KeyLoop
     params: list[ParamSpec] = []
     ptrs: dict[str, str] = {}
@@ -284,6 +289,11 @@ def generate_tc(kop: ir.KernelOp, plan, lay: dict, shapes: dict, dtypes: dict, a
     SQ, SK, D, DV = plan.SQ, plan.SK, plan.D, plan.DV
     CL, KC, DP, DVP = lay["CL"], lay["KC"], lay["DP"], lay["DVP"]
     grid_x = lay.get("XM", "cluster") == "grid"
+    tune = {**TC_TUNE, **(tune or {})}
+    if set(tune) - set(TC_TUNE):
+        raise ValueError(f"unknown attention_tune keys: {sorted(set(tune) - set(TC_TUNE))}")
+    if tune["skip_first_arrive"] and not grid_x:
+        raise ValueError("skip_first_arrive needs the grid exchange")
     GMAX = lay["nq"] * CL
     NKB, NCH = DP // 32, KC // 32
     fus = fusable_products(kop.body)
@@ -303,7 +313,7 @@ constexpr int T = {T}, NG = {NG}, NACC = {max(1, nacc)};
 constexpr uint32_t R1 = {lay['R1']}u, R2 = {lay['R2']}u, NSTAT = {lay['NSTAT']}u, SMEM_BYTES = {lay['SMEM']}u;
 constexpr uint32_t IDESC_S = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(KC >> 3) << 17) | ((128u >> 4) << 24);
 constexpr uint32_t IDESC_O = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(DVP >> 3) << 17) | ((128u >> 4) << 24);
-constexpr uint64_t WAIT_NS = 2000000000ull;
+constexpr uint64_t WAIT_NS = {int(tune["wait_ns"])}ull;
 constexpr int UB = 4;   // float4 loads in flight per thread while operands are staged
 constexpr int GMAX = {GMAX};  // CTAs of the whole problem (CL per query tile)
 }}  // namespace
@@ -631,7 +641,10 @@ __device__ unsigned int emmy_attn_sync[2 * (GMAX / CL)];
                 else:
                     w(f"            stats[{slot + fi} * 128 + rloc] = c;")
             w("        }")
-            if grid_x:
+            if grid_x and tune["skip_first_arrive"] and slot == 0:
+                w("        if (blockIdx.x == 1u && qt == qt0) __syncthreads();   // test build: no arrival")
+                w("        else if (!emmy_group_sync(gsync, CL, gfail, WAIT_NS)) gok = false;")
+            elif grid_x:
                 w("        if (!emmy_group_sync(gsync, CL, gfail, WAIT_NS)) gok = false;")
             else:
                 w("        emmy::cluster_sync();")
@@ -735,7 +748,7 @@ __device__ unsigned int emmy_attn_sync[2 * (GMAX / CL)];
     L.append(launch_record_source("attention", launch, params))
     notes = {"kernel": "attention_tcgen05_tf32x3", "cluster": 1 if grid_x else CL,
              "exchange": "grid" if grid_x else "cluster",
-             "ctas_per_tile": CL, "keys_per_cta": KC, "query_tile": 128,
+             "ctas_per_tile": CL, "keys_per_cta": KC, "query_tile": 128, "tune": tune,
              "threads": T, "smem": lay["SMEM"], "tmem_cols": lay["TCOLS"], "weights": wname}
     return KernelSource(entry=kop.name, source="\n".join(L), launch=launch, params=params,
                         family="attention", notes=notes)

@@ -192,3 +192,47 @@ def test_grid_exchange_range_launches_compose(cuda_device):
     assert case.module.status() == 0
     assert torch.equal(bufs[out].view(torch.int32), whole.view(torch.int32))
     case.module.close()
+
+
+def test_grid_exchange_wait_runs_out_and_the_next_launch_is_correct(cuda_device):
+    """Failure detection of the grid exchange without a GPU fault: a test-only
+    build in which CTA 1 leaves out its first arrival at its tile's barrier,
+    with every wait limited to 5 ms.  The other CTAs of the tile wait out
+    their limit, the launch ends by itself with EMMY_STATUS_TIMEOUT_REDUCE,
+    and a freshly loaded normal module (its barrier counters start at zero)
+    gives the cluster exchange's bits."""
+    import time
+
+    import torch
+    from emmy_ptx_compiler_b200 import harness
+    cid = "a_attn_bench_2048x64"
+    faulty = harness.DeviceCase(CASES / cid, cuda_device,
+                                options={"attention_exchange": "grid",
+                                         "attention_tune": {"skip_first_arrive": True, "wait_ns": 5_000_000}})
+    assert faulty.bundle["notes"]["exchange"] == "grid"
+    bufs = harness._seeded_device_inputs(faulty.spec, cuda_device, seed=29)
+    out = faulty.spec.outputs[0]
+    t0 = time.perf_counter()
+    faulty.launch(bufs)
+    torch.cuda.synchronize(cuda_device)
+    elapsed = time.perf_counter() - t0
+    st = faulty.module.status()
+    assert st & 0x20, f"status 0x{st:x}"          # EMMY_STATUS_TIMEOUT_REDUCE
+    assert elapsed < 5.0, elapsed
+    faulty.module.close()
+    ref = harness.DeviceCase(CASES / cid, cuda_device, options={"attention_exchange": "cluster"})
+    b = dict(bufs)
+    b[out] = torch.full_like(bufs[out], float("nan"))
+    ref.launch(b)
+    torch.cuda.synchronize(cuda_device)
+    assert ref.module.status() == 0
+    want = b[out].clone()
+    ref.module.close()
+    for _ in range(2):
+        normal = harness.DeviceCase(CASES / cid, cuda_device, options={"attention_exchange": "grid"})
+        b[out].fill_(float("nan"))
+        normal.launch(b)
+        torch.cuda.synchronize(cuda_device)
+        assert normal.module.status() == 0
+        assert torch.equal(b[out].view(torch.int32), want.view(torch.int32))
+        normal.module.close()
