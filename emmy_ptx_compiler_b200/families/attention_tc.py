@@ -83,8 +83,8 @@ def layout(plan, shapes: dict, dtypes: dict, exchange: str = "auto") -> tuple[di
     ``exchange``: how the CL CTAs of one query tile combine row values and
     partial outputs.  "cluster": the CTAs form a thread-block cluster and read
     one another's shared memory.  "grid": plain CTAs under a cooperative launch
-    (all resident at once) that exchange through global memory with a
-    counter barrier per tile.  A cluster of 8 CTAs of about 200 KB of shared
+    (all resident at once) that exchange through global memory behind an
+    arrival-counter barrier per tile.  A cluster of 8 CTAs of about 200 KB of shared
     memory needs 8 free SMs of one GPC, so a B200 holds 15 such clusters at
     once: 16 query tiles then run in two rounds, while 128 plain CTAs all fit
     on its 148 SMs.  "auto" takes "grid" when every CTA fits on the SMs at
@@ -226,31 +226,27 @@ __device__ __forceinline__ unsigned emmy_ld_acquire_gpu(const unsigned *p) {
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-// Every thread of the CTA calls it.  sync[0] counts arrivals, sync[1] is the generation: the
-// last of the n CTAs to arrive clears the count and advances the generation, the others wait
-// (bounded) for it to advance.  false: the wait ran out, now or in an earlier call of this
-// launch (*failed is set then; later calls return at once).  The CTA's own tensor-core work
-// does not depend on the other CTAs, so its mbarrier waits go on as usual after a failure.
-__device__ __noinline__ bool emmy_group_sync(unsigned *sync, unsigned n, volatile uint32_t *failed,
+// Every thread of the CTA calls it.  *count only ever grows: every CTA of the tile adds 1 per
+// barrier, so the n arrivals at one barrier return values in [i n, (i + 1) n) and the barrier is
+// passed once the count reaches (i + 1) n (n a power of two: the wrap at 2^32 keeps this).  A
+// launch leaves the count a multiple of n; one whose wait ran out may not, and the module must
+// be loaded again before its next launch.  false: the wait ran out, now or in an earlier call
+// of this launch (*failed is set then; later calls return at once).  The CTA's own
+// tensor-core work does not depend on the other CTAs, so its mbarrier waits go on as usual.
+__device__ __noinline__ bool emmy_group_sync(unsigned *count, unsigned n, volatile uint32_t *failed,
                                              uint64_t wait_ns) {
     __syncthreads();
     if (threadIdx.x == 0) {
         if (*failed == 0u) {
-            const unsigned g0 = emmy_ld_acquire_gpu(sync + 1);
             __threadfence();
-            if (atomicAdd(sync, 1u) == n - 1u) {
-                atomicExch(sync, 0u);
-                __threadfence();
-                atomicAdd(sync + 1, 1u);
-            } else {
-                const uint64_t t0 = emmy::globaltimer();
-                while (emmy_ld_acquire_gpu(sync + 1) == g0) {
-                    if (emmy::globaltimer() - t0 > wait_ns) {
-                        *failed = 1u;
-                        break;
-                    }
-                    __nanosleep(32);
+            const unsigned target = (atomicAdd(count, 1u) / n + 1u) * n;
+            const uint64_t t0 = emmy::globaltimer();
+            while ((int)(emmy_ld_acquire_gpu(count) - target) < 0) {
+                if (emmy::globaltimer() - t0 > wait_ns) {
+                    *failed = 1u;
+                    break;
                 }
+                __nanosleep(32);
             }
             __threadfence();
         }
@@ -322,10 +318,10 @@ constexpr int GMAX = {GMAX};  // CTAs of the whole problem (CL per query tile)
         w(_GRID_HELPERS)
         w("""namespace {
 // exchange through global memory: row values [CTA][NACC][128], partial outputs [CTA][DVP][128]
-// (column-major, so a warp's stores are contiguous), and one (count, generation) pair per tile
+// (column-major, so a warp's stores are contiguous), and one arrival counter per tile
 __device__ __align__(16) float emmy_attn_stats[GMAX * NACC * 128];
 __device__ __align__(16) float emmy_attn_opart[(size_t)GMAX * DVP * 128];
-__device__ unsigned int emmy_attn_sync[2 * (GMAX / CL)];
+__device__ unsigned int emmy_attn_sync[GMAX / CL];
 }  // namespace
 """)
     w(f'extern "C" __global__ void __launch_bounds__({T}, 1) ' + kop.name + "(" + ", ".join(sig) + ") {")
@@ -363,7 +359,7 @@ __device__ unsigned int emmy_attn_sync[2 * (GMAX / CL)];
     if grid_x:
         w("    const uint32_t crank = blockIdx.x % CL;           // this CTA's key chunk of its tile")
         w("    const uint32_t gbase = blockIdx.x - crank;        // first CTA of its tile")
-        w("    unsigned *const gsync = emmy_attn_sync + 2 * (blockIdx.x / CL);")
+        w("    unsigned *const gsync = emmy_attn_sync + blockIdx.x / CL;")
     else:
         w("    const uint32_t crank = emmy::cluster_ctarank();")
     w("    const int kbeg = (int)crank * KC;")

@@ -71,8 +71,8 @@ int emmy_device_count(int *count);
  * zeroed by the load; the block that completes a row resets its counter).
  * So do tensor-core attention modules launched as a cooperative grid
  * (EMMY_LR_COOPERATIVE in the record): the CTAs of a query tile exchange row
- * values and partial outputs there, behind a per-tile barrier whose counter
- * the last CTA to arrive resets.
+ * values and partial outputs there, behind a per-tile arrival counter that
+ * every completed launch leaves at a multiple of the tile's CTA count.
  * Two launches of ONE loaded module that overlap on the GPU (two streams)
  * race on them: serialise them, or load the module once per stream.  A launch
  * that does not run to completion (its context is then lost) leaves the
