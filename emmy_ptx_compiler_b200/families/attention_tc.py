@@ -465,10 +465,14 @@ __device__ unsigned int emmy_attn_sync[GMAX / CL];
              "emmy_put_split4(r1, r1 + NKB * 16384u, off, x);"], pending)
     w("        // this CTA's keys (B of S): KC rows (keys) x DP, hi and lo; keys past SK are 0")
     if plan.k_dk:
-        # consecutive threads take consecutive d (one row of kt each, four keys per thread), so
-        # each store instruction of a warp writes 32 different words of the same key rows
+        # a warp takes 16 rows of kt (d) x 8 keys: two lanes read the 32 contiguous bytes of one
+        # row (one sector per lane pair), and each lane stores its 4 keys as 4 words of 4 key
+        # rows; the 32 stores of an instruction fall in 32 different banks (rows 4k and 4k + 4
+        # differ in bit 2 of the swizzle)
         operand("kreg", DP * (KC // 4),
-                ["const int d = e % DP, k4 = e / DP;", "const int key0 = kbeg + 4 * k4;"],
+                ["const int grp_ = e >> 5, di = (e >> 1) & 15, kj = e & 1;",
+                 "const int d = 16 * (grp_ % (DP / 16)) + di, k4 = 2 * (grp_ / (DP / 16)) + kj;",
+                 "const int key0 = kbeg + 4 * k4;"],
                 ["if (d < D) {",
                  "    if (key0 + 3 < SK) {",
                  f"        x = emmy_ld4({kp} + (long long)d * SK + key0, k_al && (SK % 4) == 0);",
@@ -515,7 +519,11 @@ __device__ unsigned int emmy_attn_sync[GMAX / CL];
     w("        // this CTA's v rows (B of O): DVP rows (columns of v) x KC keys in 32-key chunks, hi and lo;")
     w("        // consecutive threads take consecutive keys, so a warp's stores cover 32 words of the same rows.")
     w("        // Loaded while the score MMAs run, stored over the K operand once they are done")
-    v_decode = ["const int kl_ = e % KC, j4 = e / KC;", "const int key = kbeg + kl_;"]
+    # a warp takes 16 keys x 8 columns of v: two lanes read 32 contiguous bytes of one key's row,
+    # and each lane stores its 4 columns as one word of 4 operand rows (32 banks, as for K)
+    v_decode = ["const int grp_ = e >> 5, ki = (e >> 1) & 15, jj = e & 1;",
+                "const int kl_ = 16 * (grp_ % (KC / 16)) + ki, j4 = 2 * (grp_ / (KC / 16)) + jj;",
+                "const int key = kbeg + kl_;"]
     v_load = [f"if (key < SK && 4 * j4 < DV) x = emmy_ld4({vp} + (long long)key * DV + 4 * j4, v_al);"]
     v_store = ["const float xs[4] = {x.x, x.y, x.z, x.w};",
                "#pragma unroll",
