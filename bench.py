@@ -53,6 +53,8 @@ DRAM_TRAFFIC = {
     "c3_rowsummax_full": 2147724544 + 3113472,
     "c4_sum_full": 8 * (1073763072 + 3136256),
     "c5_gemm_full": 5619480320 + 530271232,
+    # q, k, v read once from DRAM (1.5 MiB); the output stays in L2 within the launch
+    "a_attn_bench_2048x64": 1618944 + 256,
 }
 
 CONFIGS = {
