@@ -45,6 +45,7 @@ def _ranges(total: int, align: int, pieces: list[int]) -> list[tuple[int, int]]:
     ("c5_gemm_128x64x256", [1]),
     ("c5_gemm_200x136x300", [1, 2]),      # SIMT tiles of 64 rows
     ("f_softmax_64x1000", [3, 10]),       # row-fused: units are rows
+    ("f_rmsnorm_7x4096", [2, 3]),         # row-fused, 16 KiB rows: one CTA per row of the range
     ("a_attn_100x48", [2, 5]),            # attention: blocks of 4 query rows
     ("a_attn_256x64", [1]),               # tensor-core attention, two query tiles
 ])
