@@ -9,8 +9,30 @@ import pytest
 from conftest import CASES, case_index
 
 
+@pytest.fixture(scope="module")
+def assembled(tmp_path_factory):
+    """ptxas -arch=sm_100a on every fixture's printed module, run in parallel:
+    case id -> (return code, stderr)."""
+    import os
+    from concurrent.futures import ThreadPoolExecutor
+    from emmy_ptx_compiler_b200 import compiler
+    root = tmp_path_factory.mktemp("ptxas")
+
+    def one(rec):
+        b = compiler.compile_bundle(CASES / rec["ir"])
+        d = root / rec["id"]
+        d.mkdir()
+        (d / "m.ptx").write_text(b["ptx"])
+        v = subprocess.run(["ptxas", "-arch=sm_100a", "-v", "-o", str(d / "m.cubin"), str(d / "m.ptx")],
+                           capture_output=True, text=True)
+        return rec["id"], (v.returncode, v.stderr)
+
+    with ThreadPoolExecutor(max(1, min(16, os.cpu_count() or 1))) as ex:
+        return dict(ex.map(one, case_index()))
+
+
 @pytest.mark.parametrize("rec", case_index(), ids=lambda r: r["id"])
-def test_family_and_build(rec, tmp_path):
+def test_family_and_build(rec, assembled):
     from emmy_ptx_compiler_b200 import compiler
     b = compiler.compile_bundle(CASES / rec["ir"], want_cubin=True)
     assert b["family"] == rec["family"], (rec["id"], b["family"])
@@ -18,12 +40,9 @@ def test_family_and_build(rec, tmp_path):
     assert [p["name"] for p in b["params"]] == b["args"]
     assert b["cubin"][:4] == b"\x7fELF"
     # the printed module assembles for sm_100a and exports the KernelOp's entry
-    f = tmp_path / "m.ptx"
-    f.write_text(b["ptx"])
-    v = subprocess.run(["ptxas", "-arch=sm_100a", "-v", "-o", str(tmp_path / "m.cubin"), str(f)],
-                       capture_output=True, text=True)
-    assert v.returncode == 0, v.stderr[-2000:]
-    assert f"Compiling entry function '{rec['entry']}' for 'sm_100a'" in v.stderr
+    rc, err = assembled[rec["id"]]
+    assert rc == 0, err[-2000:]
+    assert f"Compiling entry function '{rec['entry']}' for 'sm_100a'" in err
 
 
 def test_headline_configs_take_the_fast_paths():
