@@ -209,6 +209,7 @@ struct emmy_module {
     // tensor-map cache: encoded for these source pointers
     std::vector<CUtensorMap> tmaps;
     std::vector<uint64_t> tmap_src;
+    std::vector<uint64_t> tmap_rows;
     // emmy_run_host device buffers
     std::vector<CUdeviceptr> dbuf;
     std::vector<size_t> dbuf_bytes;
@@ -226,19 +227,35 @@ struct emmy_module {
 
 namespace {
 
-int encode_tmaps(emmy_module *m, const uint64_t *args, int nargs) {
+bool has_range(const emmy_module *m);
+
+// The tensor maps of a launch over units [rb, re).  A map over a streamed parameter (one that
+// holds only its units' bytes in a sharded launch) starts at unit rb and spans re - rb units, so
+// the TMA unit is never given an address outside the caller's buffer; the kernels address such
+// maps relative to their first unit.
+int encode_tmaps(emmy_module *m, const uint64_t *args, int nargs, uint64_t rb, uint64_t re) {
     const uint32_t n = m->has_rec ? m->rec.ntmaps : 0;
     if (n == 0) return EMMY_OK;
     if (!g_drv.cuTensorMapEncodeTiled)
         return fail(EMMY_ERR_NO_DRIVER, "driver lacks cuTensorMapEncodeTiled (needed by the GEMM family)");
     m->tmaps.resize(n);
     m->tmap_src.resize(n, ~0ull);
+    m->tmap_rows.resize(n, ~0ull);
     for (uint32_t i = 0; i < n; ++i) {
         const EmmyTmapSpec &t = m->rec.tmaps[i];
-        if (t.src_param >= static_cast<uint32_t>(nargs))
+        if (t.src_param >= static_cast<uint32_t>(nargs) || t.rank < 1 || t.rank > 5)
             return fail(EMMY_ERR_INVALID, "tensor map %u reads parameter %u of %d", i, t.src_param, nargs);
-        const uint64_t base = args[t.src_param];
-        if (m->tmap_src[i] == base) continue;
+        uint64_t base = args[t.src_param];
+        uint64_t rows = t.dims[t.rank - 1];
+        const uint64_t unit_bytes = has_range(m) && t.src_param < EMMY_LR_MAX_PARAMS ? m->rec.range_bytes[t.src_param] : 0;
+        if (unit_bytes) {
+            if (rows != m->rec.range_total)
+                return fail(EMMY_ERR_INVALID, "tensor map %u: outer extent %llu is not the unit count %llu", i,
+                            (unsigned long long)rows, (unsigned long long)m->rec.range_total);
+            base += rb * unit_bytes;
+            rows = re - rb;
+        }
+        if (m->tmap_src[i] == base && m->tmap_rows[i] == rows) continue;
         if (base & 15ull) return fail(EMMY_ERR_INVALID, "TMA operand %u is not 16-byte aligned", t.src_param);
         cuuint64_t dims[5], strides[4];
         cuuint32_t box[5], estr[5];
@@ -247,6 +264,7 @@ int encode_tmaps(emmy_module *m, const uint64_t *args, int nargs) {
             box[d] = t.box[d];
             estr[d] = 1;
         }
+        dims[t.rank - 1] = rows;
         for (uint32_t d = 0; d + 1 < t.rank; ++d) strides[d] = t.strides[d];
         CUresult r = g_drv.cuTensorMapEncodeTiled(
             &m->tmaps[i], static_cast<CUtensorMapDataType>(t.dtype), t.rank,
@@ -255,6 +273,7 @@ int encode_tmaps(emmy_module *m, const uint64_t *args, int nargs) {
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) return cu_fail(r, "cuTensorMapEncodeTiled");
         m->tmap_src[i] = base;
+        m->tmap_rows[i] = rows;
     }
     return EMMY_OK;
 }
@@ -293,7 +312,6 @@ int launch_locked(emmy_module *m, const uint64_t *args, int nargs, const uint32_
     }
     if (m->has_rec && static_cast<uint32_t>(nargs) != m->rec.nparams)
         return fail(EMMY_ERR_INVALID, "entry takes %u parameters, got %d", m->rec.nparams, nargs);
-    if ((rc = encode_tmaps(m, args, nargs))) return rc;
     const size_t ntm = m->has_rec ? m->rec.ntmaps : 0;
     const bool ranged = has_range(m);
     uint64_t range[2] = {rbegin, rend == ~0ull && ranged ? m->rec.range_total : rend};
@@ -310,6 +328,7 @@ int launch_locked(emmy_module *m, const uint64_t *args, int nargs, const uint32_
             if (units < g[0]) g[0] = static_cast<uint32_t>(units);
         }
     }
+    if ((rc = encode_tmaps(m, args, nargs, ranged ? range[0] : 0, ranged ? range[1] : 0))) return rc;
     // fixed-size parameter tables: a launch allocates nothing on the host
     constexpr int kMaxArgs = 64;
     if (nargs < 0 || nargs > kMaxArgs) return fail(EMMY_ERR_INVALID, "%d parameters (at most %d)", nargs, kMaxArgs);

@@ -502,7 +502,7 @@ extern "C" __global__ void __launch_bounds__({TC_THREADS}, 1) {kop.name}({", ".j
                 for (int k = 0; k < KB; ++k) {{
                     if (!emmy::mbar_wait(&empty[stage], phase ^ 1u, abort_flag, EMMY_STATUS_TIMEOUT_PRODUCER, WAIT_NS)) {{ ok = false; break; }}
                     emmy::mbar_arrive_expect_tx(&full[stage], A_STAGE + B_STAGE);
-                    emmy::tma_load_2d(sA + stage * A_STAGE, &tm_a, &full[stage], k * BK, tm * BM);
+                    emmy::tma_load_2d(sA + stage * A_STAGE, &tm_a, &full[stage], k * BK, (tm - MB0) * BM);
 {_b_loads(plan.b_nk)}
                     issued |= 1u << stage;
                     parity_bits = (parity_bits & ~(1u << stage)) | (phase << stage);
@@ -765,7 +765,9 @@ def _gen_tcgen05_pair(kop, plan: GemmPlan, shapes, dtypes, args, ptrs, sig, para
     policies = "".join(
         f"            const uint64_t {var} = emmy::l2_policy_{tn_[key].replace('evict_', 'evict_')}();\n"
         for var, key in (("pol_a", "a_policy"), ("pol_b", "b_policy")) if tn_[key])
-    a_load = "                    " + _ld("sA + stage * A_STAGE, &tm_a, fbar, k * BK, tm * BM + (int)rank * CBM", apol)
+    # A's tensor map starts at this launch's first row (the loader encodes it per unit range)
+    a_load = "                    " + _ld("sA + stage * A_STAGE, &tm_a, fbar, k * BK, (tm - MB0) * BM + (int)rank * CBM",
+                                        apol)
     skip_open = skip_close = ""
     if tn_["skip_first_load"]:
         skip_open = "                    if (!(rank == 1u && pair == 0 && t == pair && k == 0)) {\n"

@@ -166,3 +166,46 @@ def test_small_host_path_matches_device_launch(cid, pinned, cuda_device):
                 f"{cid}.{n}: host path differs from the device launch"
     assert case.module.status() == 0
     case.module.close()
+
+
+@pytest.mark.parametrize("cid", ["c2_gelu_256x4096", "c5_gemm_384x1024x768", "c5_gemm_520x320x392",
+                                 "c5_gemm_bnk_384x256x512", "c5_gemm_200x136x300", "f_rmsnorm_7x4096",
+                                 "a_attn_100x48"])
+def test_sharded_launch_of_two_modules_on_one_device(cid, cuda_device):
+    """emmy_launch_sharded over two modules loaded on the same GPU: the second
+    shard's streamed buffers hold only its units, and the runtime rebases their
+    pointers by the shard's first unit.  The GEMM's tensor map over A must then
+    start at the shard's first row (it never points outside the buffer); the
+    gathered result is bit-identical to one whole launch."""
+    import torch
+    from emmy_ptx_compiler_b200 import harness, runtime
+    case = harness.DeviceCase(CASES / cid, cuda_device)
+    bufs = harness._seeded_device_inputs(case.spec, cuda_device, seed=3)
+    case.launch(bufs)
+    torch.cuda.synchronize(cuda_device)
+    want = {n: bufs[n].clone() for n in case.spec.outputs}
+    mods = [case.module, runtime.Module(case.bundle["cubin"], case.spec.entry, cuda_device)]
+    total, align, per_unit = case.module.unit_range()
+    args, outs = [], []
+    for d in range(2):
+        b, e = runtime.shard_range(mods[d], 2, d)
+        assert b < e
+        row, shard_out = [], {}
+        for k, n in enumerate(case.spec.arg_order):
+            full = bufs[n] if n not in case.spec.outputs else torch.zeros_like(bufs[n])
+            flat = full.reshape(-1)
+            t = flat[b * (per_unit[k] // full.element_size()):e * (per_unit[k] // full.element_size())].clone() \
+                if per_unit[k] else full.clone()
+            if n in case.spec.outputs:
+                shard_out[n] = t
+            row.append(t)
+        args.append(row)
+        outs.append(shard_out)
+    runtime.launch_sharded(mods, args)
+    torch.cuda.synchronize(cuda_device)
+    assert mods[0].status() == 0 and mods[1].status() == 0
+    for n in case.spec.outputs:
+        got = torch.cat([outs[d][n].reshape(-1) for d in range(2)])
+        assert torch.equal(got.view(torch.uint8), want[n].reshape(-1).view(torch.uint8)), f"{cid}.{n}"
+    mods[1].close()
+    case.module.close()
