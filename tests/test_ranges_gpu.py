@@ -170,7 +170,7 @@ def test_small_host_path_matches_device_launch(cid, pinned, cuda_device):
 
 @pytest.mark.parametrize("cid", ["c2_gelu_256x4096", "c5_gemm_384x1024x768", "c5_gemm_520x320x392",
                                  "c5_gemm_bnk_384x256x512", "c5_gemm_200x136x300", "f_rmsnorm_7x4096",
-                                 "a_attn_100x48"])
+                                 "a_attn_256x64"])
 def test_sharded_launch_of_two_modules_on_one_device(cid, cuda_device):
     """emmy_launch_sharded over two modules loaded on the same GPU: the second
     shard's streamed buffers hold only its units, and the runtime rebases their
@@ -187,9 +187,9 @@ def test_sharded_launch_of_two_modules_on_one_device(cid, cuda_device):
     mods = [case.module, runtime.Module(case.bundle["cubin"], case.spec.entry, cuda_device)]
     total, align, per_unit = case.module.unit_range()
     args, outs = [], []
+    assert runtime.shard_range(mods[1], 2, 1)[0] > 0, "the second shard starts past unit 0"
     for d in range(2):
-        b, e = runtime.shard_range(mods[d], 2, d)
-        assert b < e
+        b, e = runtime.shard_range(mods[d], 2, d)   # a shard may be empty (units of 128 rows)
         row, shard_out = [], {}
         for k, n in enumerate(case.spec.arg_order):
             full = bufs[n] if n not in case.spec.outputs else torch.zeros_like(bufs[n])
