@@ -66,7 +66,10 @@ enum EmmyParamKind { EMMY_PARAM_PTR = 0, EMMY_PARAM_F32 = 1, EMMY_PARAM_I32 = 2 
  * (u + 1) * range_bytes[i]) of that buffer, and a launch over a range reads
  * and writes no other bytes of it; parameters with range_bytes[i] == 0 are
  * read whole by every launch.  Range ends are multiples of range_align, or
- * range_total. */
+ * range_total.  A tensor map over a parameter with range_bytes[i] > 0 is
+ * encoded per launch: it starts at the launch's first unit and its outer
+ * extent is the launch's unit count (the kernel addresses it relative to
+ * range_begin). */
 #define EMMY_LR_RANGE 0x200u
 /* EMMY_LR_GRID_UNITS (with EMMY_LR_RANGE): one CTA per unit of the launch's
  * range, at most grid[0] CTAs (the kernel strides over any units beyond its
