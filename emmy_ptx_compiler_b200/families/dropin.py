@@ -103,8 +103,14 @@ def attach(ks: KernelSource, kop: ir.KernelOp, shapes: dict, dtypes: dict, args:
     lines = [src, native]
     cooperative = ks.launch.cooperative
     if cooperative and fallback is None:
-        raise UnsupportedIR(f"{name}: a cooperative fast kernel needs the IR's own schedule as its drop-in")
-    if fallback is None:
+        # no schedule to fall back on, and the fast body needs a cooperative launch: the
+        # drop-in only reports that it cannot run (the C ABI launches the fast entry)
+        lines.append(
+            f'extern "C" __global__ void {name}({", ".join(sig[:n])}) {{\n'
+            "    if (threadIdx.x == 0 && threadIdx.y == 0 && threadIdx.z == 0 && blockIdx.x == 0 &&\n"
+            "        blockIdx.y == 0 && blockIdx.z == 0) atomicOr(&emmy_status, EMMY_STATUS_BAD_LAUNCH);\n}\n")
+        mode = "reports EMMY_STATUS_BAD_LAUNCH (the fast kernel needs a cooperative launch; no schedule to run)"
+    elif fallback is None:
         lines.append(f'extern "C" __global__ void __launch_bounds__({threads}) {name}({", ".join(sig[:n])}) {{\n'
                      f"    {whole}\n}}\n")
         mode = "fast body under every launch" if ks.family == "pointwise" else \

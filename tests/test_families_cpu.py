@@ -333,3 +333,16 @@ def test_pointwise_tune_option_changes_the_schedule_only():
     assert "__launch_bounds__(256, 3)" in tuned["source"] and tuned["source"] != base["source"]
     with pytest.raises(ValueError):
         compiler.compile_bundle(ir_path, options={"pointwise_tune": {"unrol": 4}})
+
+
+def test_cooperative_attention_without_a_schedule_still_compiles(monkeypatch):
+    """When the IR's own schedule cannot be lowered, a cooperative attention
+    module's drop-in entry only reports EMMY_STATUS_BAD_LAUNCH (a kernel cannot
+    tell whether it was launched cooperatively); the fast entry is unchanged."""
+    from emmy_ptx_compiler_b200 import compiler
+    from emmy_ptx_compiler_b200.families import schedule
+    monkeypatch.setattr(schedule, "match", lambda *a, **k: None)
+    b = compiler.compile_bundle(next((CASES / "a_attn_bench_2048x64").glob("*.ir.json")), want_cubin=True)
+    assert b["family"] == "attention" and b["notes"]["exchange"] == "grid"
+    assert b["notes"]["entries"]["drop_in_path"].startswith("reports EMMY_STATUS_BAD_LAUNCH")
+    assert b["cubin"][:4] == b"\x7fELF"
