@@ -324,8 +324,9 @@ int launch_locked(emmy_module *m, const uint64_t *args, int nargs, const uint32_
                         (unsigned long long)m->rec.range_total, (unsigned long long)al);
         if (range[0] == range[1]) return EMMY_OK;
         if (!(grid && block) && (m->rec.flags & EMMY_LR_GRID_UNITS)) {
-            const uint64_t units = range[1] - range[0];
-            if (units < g[0]) g[0] = static_cast<uint32_t>(units);
+            const uint64_t per_cta = m->rec.grid_quantum ? m->rec.grid_quantum : 1;
+            const uint64_t need = (range[1] - range[0] + per_cta - 1) / per_cta;
+            if (need < g[0]) g[0] = static_cast<uint32_t>(need);
         }
     }
     if ((rc = encode_tmaps(m, args, nargs, ranged ? range[0] : 0, ranged ? range[1] : 0))) return rc;

@@ -25,7 +25,7 @@ class LaunchPlan:
     range_total: int = 0          # 0 = no range parameters
     range_align: int = 1
     range_bytes: list[int] = field(default_factory=list)  # per arg_order parameter
-    # grid_units: a launch over a unit range runs min(grid[0], units in the range) CTAs
+    # grid_units: a launch over a unit range runs min(grid[0], units in the range / grid_quantum) CTAs
     grid_units: bool = False
     # cooperative: the loader launches every CTA at once (cooperative launch) or fails
     cooperative: bool = False

@@ -15,10 +15,12 @@ fused kernels of tools/make_proxy_set.py:393-414): a Tile over
 * mapping passes ``StridedLoop(k, ...)`` without ``Accum`` that write
   ``out[row..., k]``.
 
-The reference rereads the row from global memory in every pass.  Here one
-CTA owns a row at a time: rows of at least ``ROW_PER_CTA_BYTES`` get one CTA
-each (the launch's grid follows its row range), shorter rows a persistent grid
-sized by the loader from occupancy.  The row is read once with 128-bit loads into registers when it
+The reference rereads the row from global memory in every pass.  Here rows
+of at least ``ROW_PER_CTA_BYTES`` get one CTA each, rows whose values fit one
+warp's registers get one warp each (``WR_ROWS`` rows per CTA, reductions
+within the warp), and the launch's grid follows its row range in both cases;
+other rows run on a persistent grid sized by the loader from occupancy, one
+CTA per row at a time.  The row is read once with 128-bit loads into registers when it
 fits (up to 64 floats per thread), every pass runs on those registers, each
 reduction is a ``__shfl_xor_sync`` butterfly plus one shared-memory stage
 that every thread combines in the same fixed warp order, and the output is
@@ -47,6 +49,9 @@ CACHE_FLOATS = 64          # per thread: rows whose streamed tensors fit stay in
 # SM start the next row's loads while the last row's stores drain (16384 x 8192 f32:
 # 0.159 ms against 0.178 ms for a persistent grid of 4 CTAs per SM)
 ROW_PER_CTA_BYTES = 16 * 1024
+# shorter rows whose streamed values fit one warp's registers run one row per warp, this many
+# rows per CTA: reductions are butterflies within the warp, and no CTA barrier is taken
+WR_ROWS = 8
 _SCHEDULE = (ir.WarpShuffle, ir.TreeHalve, ir.Smem, ir.Sync)
 _PASS_STMTS = (ir.Load, ir.Let, ir.Init, ir.Assign, ir.Accum, ir.Write, ir.Select, ir.Cond)
 _COMBINE = {"add": "add", "sum": "add", "maximum": "maximum", "amax": "maximum", "max": "maximum",
@@ -253,7 +258,10 @@ def range_bytes(plan: RowPlan, args: list[str], scalars: dict, dtypes: dict, sha
 
 def generate(kop: ir.KernelOp, plan: RowPlan, shapes: dict, dtypes: dict, args: list[str],
              scalars: dict[str, str], written: set[str], *, bulk_prefetch: bool = False,
-             reuse_values: bool = True) -> KernelSource:
+             reuse_values: bool = True, warp_rows: bool = True) -> KernelSource:
+    """``warp_rows``: rows short enough for one warp's registers run one row per
+    warp, ``WR_ROWS`` rows per CTA (reductions are warp butterflies, no CTA
+    barrier); longer rows run one row per CTA of up to ``MAX_THREADS``."""
     params: list[ParamSpec] = []
     ptrs: dict[str, str] = {}
     sig: list[str] = []
@@ -280,23 +288,34 @@ def generate(kop: ir.KernelOp, plan: RowPlan, shapes: dict, dtypes: dict, args: 
         return max(32, min(MAX_THREADS, -(-units // 32) * 32))
 
     T = threads_for(4 if vec else 1)
+    nvec4 = -(-K // 4)
+    row_bytes = K * max([ir.ELEM_BYTES[ir.canon_dtype(dtypes.get(n))] for n in plan.streamed] or [0])
+    wr = (warp_rows and vec and not bulk_prefetch and plan.rows >= WR_ROWS and row_bytes < ROW_PER_CTA_BYTES
+          and -(-nvec4 // 32) * 4 * max(1, len(plan.streamed)) <= CACHE_FLOATS)
+    if wr:
+        T = 32                     # threads per row; the CTA holds WR_ROWS rows
+    CT = T * WR_ROWS if wr else T  # threads per CTA
     NW = T // 32
     lines: list[str] = []
     w = lines.append
     w(DEVICE_PRELUDE)
     w(_VEC_HELPERS)
     w('#include "emmy_sm100.cuh"')
-    w(f'extern "C" __global__ void __launch_bounds__({T}) {kop.name}(' + ", ".join(sig) + ") {")
+    w(f'extern "C" __global__ void __launch_bounds__({CT}) {kop.name}(' + ", ".join(sig) + ") {")
     w(f"    constexpr long long NROWS = {plan.rows}LL, K = {K}LL;")
-    w(f"    __shared__ float red_smem[{max(1, nred)}][{NW}];")
-    w(f"    if (blockDim.x != {T} || blockDim.y != 1 || blockDim.z != 1) {{")
+    if not wr:
+        w(f"    __shared__ float red_smem[{max(1, nred)}][{NW}];")
+    w(f"    if (blockDim.x != {CT} || blockDim.y != 1 || blockDim.z != 1) {{")
     w("        if (threadIdx.x == 0 && threadIdx.y == 0 && threadIdx.z == 0) atomicOr(&emmy_status, EMMY_STATUS_BAD_LAUNCH);")
     w("        return;")
     w("    }")
     w("    const long long RB = (long long)(emmy_rb < (unsigned long long)NROWS ? emmy_rb : NROWS);")
     w("    const long long RE = (long long)(emmy_re < (unsigned long long)NROWS ? emmy_re : NROWS);")
-    w("    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;")
-    nvec4 = -(-K // 4)
+    if wr:
+        # one warp per row: tid is the lane, wrow the warp's row slot in the CTA
+        w("    const int tid = threadIdx.x & 31, lane = tid, wrow = threadIdx.x >> 5;")
+    else:
+        w("    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;")
     cached4 = -(-nvec4 // T) * 4 * max(1, len(plan.streamed)) <= CACHE_FLOATS
     stage = _stage_bytes(plan, dtypes)
     bulk = bulk_prefetch and vec and cached4 and bool(plan.streamed) and stage <= STAGE_BYTES_MAX
@@ -335,29 +354,38 @@ def generate(kop: ir.KernelOp, plan: RowPlan, shapes: dict, dtypes: dict, args: 
         else:
             w("    if (aligned) {")
         lines.extend(_row_loop(plan, shapes, dtypes, ptrs, scalar_env, fus, 4, T, "        ",
-                               reuse_values=reuse_values))
+                               reuse_values=reuse_values, wr=wr))
         w("    } else {")
         lines.extend(_row_loop(plan, shapes, dtypes, ptrs, scalar_env, fus, 1, T, "        ",
-                               reuse_values=reuse_values))
+                               reuse_values=reuse_values, wr=wr))
         w("    }")
     else:
         lines.extend(_row_loop(plan, shapes, dtypes, ptrs, scalar_env, fus, 1, T, "    ",
                                reuse_values=reuse_values))
     w("}")
-    row_bytes = K * max([ir.ELEM_BYTES[ir.canon_dtype(dtypes.get(n))] for n in plan.streamed] or [0])
     per_row = vec and row_bytes >= ROW_PER_CTA_BYTES
-    grid = max(1, min(plan.rows, 0x7FFFFFFF if per_row else SM_COUNT * 8))
-    launch = LaunchPlan(grid=(grid, 1, 1), block=(T, 1, 1), smem=dyn, range_total=plan.rows, range_align=1,
-                        range_bytes=range_bytes(plan, args, scalars, dtypes, shapes), grid_units=per_row)
-    if plan.rows >= SM_COUNT * 8 and not per_row:
+    # warps whose row fills their registers (16 float4 per lane) take two rows each: measured
+    # 6.6 against 6.2 TB/s at 65536 x 2048 (rmsnorm, 154 registers, one CTA per SM)
+    wr_rounds = 2 if wr and -(-nvec4 // 32) >= 16 else 1
+    if wr:
+        grid = max(1, min(-(-plan.rows // (WR_ROWS * wr_rounds)), 0x7FFFFFFF))
+    else:
+        grid = max(1, min(plan.rows, 0x7FFFFFFF if per_row else SM_COUNT * 8))
+    launch = LaunchPlan(grid=(grid, 1, 1), block=(CT, 1, 1), smem=dyn, range_total=plan.rows, range_align=1,
+                        range_bytes=range_bytes(plan, args, scalars, dtypes, shapes), grid_units=per_row or wr)
+    if wr:
+        launch.grid_quantum = WR_ROWS * wr_rounds   # units (rows) per CTA for the range-sized grid
+    if plan.rows >= SM_COUNT * 8 and not per_row and not wr:
         launch.fill_waves = 1
     lines.append(launch_record_source("rownorm", launch, params))
     nvec = -(-K // 4) if vec else K
     ept = -(-nvec // T)
-    notes = {"kernel": "row_fused", "threads": T, "vector": vec, "passes": sum(isinstance(p, Pass) for p in plan.steps),
+    notes = {"kernel": "row_fused", "threads": CT, "threads_per_row": T,
+             "rows_per_cta": WR_ROWS * wr_rounds if wr else 1,
+             "vector": vec, "passes": sum(isinstance(p, Pass) for p in plan.steps),
              "reductions": nred, "elems_per_thread": ept * (4 if vec else 1),
              "cached": ept * (4 if vec else 1) * max(1, len(plan.streamed)) <= CACHE_FLOATS,
-             "bulk_prefetch": bool(bulk), "cta_per_row": per_row}
+             "bulk_prefetch": bool(bulk), "cta_per_row": per_row, "warp_per_row": wr}
     return KernelSource(entry=kop.name, source="\n".join(lines), launch=launch, params=params, family="rownorm",
                         notes=notes)
 
@@ -459,7 +487,7 @@ def _stage_bytes(plan: RowPlan, dtypes) -> int:
 
 
 def _row_loop(plan: RowPlan, shapes, dtypes, ptrs, scalar_env, fus, VW: int, T: int, ind: str,
-              bulk: bool = False, reuse_values: bool = True) -> list[str]:
+              bulk: bool = False, reuse_values: bool = True, wr: bool = False) -> list[str]:
     """The persistent loop over this CTA's rows, every pass inside it, for
     vector width VW (4: float4 per access, 1: scalar).  With ``bulk`` the next
     row of every streamed tensor is brought into shared memory by one bulk
@@ -481,7 +509,11 @@ def _row_loop(plan: RowPlan, shapes, dtypes, ptrs, scalar_env, fus, VW: int, T: 
             o(f"{ind}    emmy::bulk_load(stage_{_c(n)}, {ptrs[n]} + (RB + (long long)blockIdx.x) * K, "
               f"{K * ir.ELEM_BYTES[dt]}u, rn_bar);")
         o(f"{ind}}}")
-    o(f"{ind}for (long long row = RB + blockIdx.x; row < RE; row += gridDim.x) {{")
+    if wr:
+        o(f"{ind}for (long long row = RB + (long long)blockIdx.x * {WR_ROWS} + wrow; row < RE; "
+          f"row += (long long)gridDim.x * {WR_ROWS}) {{")
+    else:
+        o(f"{ind}for (long long row = RB + blockIdx.x; row < RE; row += gridDim.x) {{")
     i2 = ind + "    "
     # row axes decoded from the flat row index
     rem = "row"
@@ -653,16 +685,19 @@ def _row_loop(plan: RowPlan, shapes, dtypes, ptrs, scalar_env, fus, VW: int, T: 
                 o(f"{i2}#pragma unroll")
                 o(f"{i2}for (int off = 16; off > 0; off >>= 1)")
                 o(f"{i2}    {var} = {combine_code(op, var, f'__shfl_xor_sync(0xffffffffu, {var}, off)')};")
-                o(f"{i2}if (lane == 0) red_smem[{slot}][warp] = {var};")
+                if not wr:
+                    o(f"{i2}if (lane == 0) red_smem[{slot}][warp] = {var};")
                 slot_a = slot
                 slot += 1
                 acc_vars[a] = (var, slot_a, op)
-            if step.accs:
+            if step.accs and not wr:
                 o(f"{i2}__syncthreads();")
             for a, (var, sl, op) in acc_vars.items():
-                o(f"{i2}{var} = red_smem[{sl}][0];")
-                o(f"{i2}#pragma unroll")
-                o(f"{i2}for (int w2 = 1; w2 < {T // 32}; ++w2) {var} = {combine_code(op, var, f'red_smem[{sl}][w2]')};")
+                if not wr:
+                    # one warp per row: the butterfly left the row's value in every lane
+                    o(f"{i2}{var} = red_smem[{sl}][0];")
+                    o(f"{i2}#pragma unroll")
+                    o(f"{i2}for (int w2 = 1; w2 < {T // 32}; ++w2) {var} = {combine_code(op, var, f'red_smem[{sl}][w2]')};")
                 row_env[a] = ("f32", var)
                 declared_row[f"{a}|f32"] = var
                 if a in divisors:
@@ -688,6 +723,9 @@ def _row_loop(plan: RowPlan, shapes, dtypes, ptrs, scalar_env, fus, VW: int, T: 
             out.extend(em.lines)
             row_env.update({k: v for k, v in em.env.items()})
             declared_row.update(em.declared)
-    o(f"{i2}__syncthreads();  // shared partials are reused by the next row")
+    if wr:
+        o(f"{i2}__syncwarp();")
+    else:
+        o(f"{i2}__syncthreads();  // shared partials are reused by the next row")
     o(f"{ind}}}")
     return out

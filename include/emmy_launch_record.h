@@ -71,9 +71,10 @@ enum EmmyParamKind { EMMY_PARAM_PTR = 0, EMMY_PARAM_F32 = 1, EMMY_PARAM_I32 = 2 
  * extent is the launch's unit count (the kernel addresses it relative to
  * range_begin). */
 #define EMMY_LR_RANGE 0x200u
-/* EMMY_LR_GRID_UNITS (with EMMY_LR_RANGE): one CTA per unit of the launch's
- * range, at most grid[0] CTAs (the kernel strides over any units beyond its
- * grid).  A launch that passes its own grid keeps it. */
+/* EMMY_LR_GRID_UNITS (with EMMY_LR_RANGE): one CTA per grid_quantum units
+ * (0 = 1) of the launch's range, at most grid[0] CTAs (the kernel strides
+ * over any units beyond its grid).  A launch that passes its own grid keeps
+ * it. */
 #define EMMY_LR_GRID_UNITS 0x400u
 /* EMMY_LR_COOPERATIVE: launched as a cooperative grid (every CTA resident at
  * once, or the launch fails): the kernel's CTAs wait on one another through
@@ -103,7 +104,7 @@ typedef struct EmmyLaunchRecord {
     uint32_t nparams;
     uint32_t param_kind[EMMY_LR_MAX_PARAMS];
     uint32_t ntmaps;
-    uint32_t grid_quantum; /* with EMMY_LR_FILL_GRID: grid[0] is a multiple of this (0 = 1) */
+    uint32_t grid_quantum; /* EMMY_LR_FILL_GRID: grid[0] is a multiple of this; EMMY_LR_GRID_UNITS: units per CTA (0 = 1) */
     EmmyTmapSpec tmaps[EMMY_LR_MAX_TMAPS];
     /* version 2: unit ranges (EMMY_LR_RANGE) */
     uint64_t range_total;

@@ -254,24 +254,32 @@ def test_plain_copy_staging_is_proven_only_when_right(swap):
     assert (got is None) == swap
 
 
-@pytest.mark.parametrize("cid, per_row", [("f_rmsnorm_bench_16384x8192", True), ("f_softmax_bench_16384x8192", True),
-                                          ("f_rmsnorm_64x1000", False), ("f_l2norm_7x4096", True)])
-def test_row_fused_grid_follows_the_row_range_for_wide_rows(cid, per_row):
-    """Rows of 16 KiB or more get one CTA each: the record asks for
-    EMMY_LR_GRID_UNITS with grid[0] = rows (a range launch then runs one CTA
-    per row of its range); shorter rows keep the occupancy-filled grid."""
+@pytest.mark.parametrize("cid, mode", [("f_rmsnorm_bench_16384x8192", "cta"), ("f_softmax_bench_16384x8192", "cta"),
+                                       ("f_l2norm_7x4096", "cta"), ("f_rmsnorm_64x1000", "warp"),
+                                       ("f_softmax_64x1000", "warp"), ("f_rmsnorm_33x130", "persistent"),
+                                       ("f_softmax_bf16_33x4096", "persistent")])
+def test_row_fused_grid_follows_the_row_range(cid, mode):
+    """Rows of 16 KiB or more get one CTA each; rows that fit a warp's registers
+    one warp each, 8 rows per CTA.  Both records ask for EMMY_LR_GRID_UNITS
+    (grid_quantum = rows per CTA), so that a range launch sizes its grid from
+    its rows.  Other rows (unaligned widths, too few rows) keep the
+    occupancy-filled or fixed grid."""
     from emmy_ptx_compiler_b200.families import rownorm
     from emmy_ptx_compiler_b200.families.common import FLAG_GRID_UNITS, launch_record_source
     kop, shapes, dtypes, args = _plan_inputs(cid)
     plan = rownorm.match(kop, shapes, dtypes)
     ks = rownorm.generate(kop, plan, shapes, dtypes, args, {}, set(plan.outputs))
-    assert ks.notes["cta_per_row"] is per_row
-    assert ks.launch.grid_units is per_row
+    assert ks.notes["cta_per_row"] is (mode == "cta")
+    assert ks.notes["warp_per_row"] is (mode == "warp")
     rec = launch_record_source("rownorm", ks.launch, ks.params)
     flags = int(rec.split("EMMY_LR_VERSION, 4u, ")[1].split("u")[0])
-    assert bool(flags & FLAG_GRID_UNITS) is per_row
-    if per_row:
-        assert ks.launch.grid[0] == plan.rows and not ks.launch.fill_waves
+    assert bool(flags & FLAG_GRID_UNITS) is (mode != "persistent")
+    if mode == "cta":
+        assert ks.launch.grid[0] == plan.rows and ks.launch.grid_quantum == 1 and not ks.launch.fill_waves
+    if mode == "warp":
+        assert ks.launch.block[0] == 32 * rownorm.WR_ROWS and ks.notes["threads_per_row"] == 32
+        assert ks.launch.grid[0] == -(-plan.rows // ks.launch.grid_quantum)
+        assert "__syncthreads" not in ks.source.split("emmy_launch_record")[0].split("__launch_bounds__")[1]
 
 
 def test_attention_exchange_choice_and_launch_record():
