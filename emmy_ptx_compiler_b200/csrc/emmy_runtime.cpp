@@ -767,10 +767,34 @@ int run_pipeline(emmy_module *m, void *const *host_ptrs, const size_t *bytes, co
     // kernel (`stream`) and copy-out (d2h stream), so chunk k's copy-in, chunk
     // k-1's kernel and chunk k-2's copy-out overlap, and both host-link
     // directions are busy at once.
-    uint64_t nchunks = std::max<uint64_t>(2, std::min<uint64_t>(kMaxPipelineChunks, streamed / chunk_bytes));
+    uint64_t nchunks = std::max<uint64_t>(2, std::min<uint64_t>(kMaxPipelineChunks / 2, streamed / chunk_bytes));
     uint64_t per = (total + nchunks - 1) / nchunks;
     per = (per + align - 1) / align * align;
-    nchunks = (total + per - 1) / per;
+    // Chunk boundaries (in units of `align`): the first chunks grow from per / 16 to per and the
+    // last ones shrink back, so that the copy-in before the first kernel and the copy-out after
+    // the last one (while one link direction idles) are short.
+    std::vector<uint64_t> cut{0};
+    {
+        const uint64_t U = (total + align - 1) / align, P = std::max<uint64_t>(1, per / align);
+        std::vector<uint64_t> ramp;
+        uint64_t ramp_units = 0;
+        for (uint64_t sz = std::max<uint64_t>(1, P / 16); sz < P; sz *= 2) {
+            ramp.push_back(sz);
+            ramp_units += sz;
+        }
+        if (U < 2 * ramp_units + 2 * P) {
+            ramp.clear();
+            ramp_units = 0;
+        }
+        uint64_t u = 0;
+        for (uint64_t sz : ramp) cut.push_back((u += sz) * align);
+        const uint64_t mid_end = U - ramp_units;
+        while (u + P < mid_end) cut.push_back((u += P) * align);
+        if (mid_end > u) cut.push_back((u = mid_end) * align);
+        for (auto it = ramp.rbegin(); it != ramp.rend(); ++it) cut.push_back((u += *it) * align);
+        cut.back() = total;   // the last unit may be partial
+    }
+    nchunks = cut.size() - 1;
     if ((rc = ensure_pipeline(m, nchunks))) return rc;
     CU(g_drv.cuEventRecord(m->ev_start, s), "cuEventRecord");
     CU(g_drv.cuStreamWaitEvent(m->h2d, m->ev_start, 0), "cuStreamWaitEvent");
@@ -785,7 +809,7 @@ int run_pipeline(emmy_module *m, void *const *host_ptrs, const size_t *bytes, co
     CU(g_drv.cuEventRecord(m->ev_whole, m->h2d), "cuEventRecord");
     CU(g_drv.cuStreamWaitEvent(s, m->ev_whole, 0), "cuStreamWaitEvent");
     for (uint64_t k = 0; k < nchunks; ++k) {
-        const uint64_t b = k * per, e = std::min(total, b + per);
+        const uint64_t b = cut[k], e = cut[k + 1];
         for (int i = 0; i < nargs; ++i) {
             if (roles[i] == EMMY_ROLE_SCALAR || !is_in(roles[i]) || !m->rec.range_bytes[i]) continue;
             size_t lo, hi;
