@@ -53,7 +53,7 @@ def _pointwise_tune(tune: dict | None) -> dict:
     """The pointwise generator's schedule knobs a caller may set (every value
     gives the same results)."""
     tune = dict(tune or {})
-    bad = set(tune) - {"unroll", "pipeline", "min_blocks"}
+    bad = set(tune) - {"unroll", "pipeline", "min_blocks", "order", "tile_u"}
     if bad:
         raise ValueError(f"unknown pointwise_tune keys: {sorted(bad)}")
     return tune
@@ -67,7 +67,7 @@ def lower(kop: ir.KernelOp, shapes: dict, dtypes: dict, args: list[str], meta: d
     it): ``{"gemm_variant": "auto" | "pair" | "single", "gemm_tune": {...}
     (families/gemm.py PAIR_TUNE),
     "pointwise_pair": "auto" | True | False, "pointwise_tune": {"unroll", "pipeline",
-    "min_blocks"}, "attention_first_pass": "auto" | "tiled",
+    "min_blocks", "order", "tile_u"}, "attention_first_pass": "auto" | "tiled",
     "attention_kernel": "auto" | "tc" | "exact", "attention_exchange": "auto" | "cluster" | "grid",
     "attention_tune": {...} (families/attention_tc.py TC_TUNE),
     "family": "schedule"}``; the

@@ -16,8 +16,9 @@ Such a module carries two entries:
   block shape (and dynamic shared memory), and otherwise a path that is
   correct under any launch of the reference's contract:
 
-  - pointwise kernels are grid-stride loops, correct under every launch, so
-    the drop-in always runs the fast body;
+  - pointwise kernels are correct under every launch (vector tiles under the
+    record's 256-thread blocks, a scalar grid-stride loop under any other), so
+    the drop-in always runs the module's body;
   - row-fused and attention kernels fall back to the IR's own schedule
     (the schedule family: the reference's thread model, compiled for
     sm_100a), which is what meta.json's geometry was written for; a fast

@@ -16,6 +16,7 @@ import re
 import shutil
 import subprocess
 import tempfile
+import threading
 from functools import lru_cache
 from pathlib import Path
 
@@ -77,7 +78,8 @@ def build(source: str, kind: str = "ptx", extra: list[str] | None = None, name: 
         if proc.returncode != 0:
             raise ToolchainError(f"nvcc failed ({proc.returncode}) on {name}:\n{proc.stderr[-4000:]}")
         data = dst.read_bytes()
-    tmp = out_path.with_suffix(out_path.suffix + f".tmp{os.getpid()}")
+    # unique per process and thread: two threads may build the same source at once
+    tmp = out_path.with_suffix(out_path.suffix + f".tmp{os.getpid()}.{threading.get_ident()}")
     tmp.write_bytes(data)
     os.replace(tmp, out_path)
     return data
@@ -121,7 +123,7 @@ def register_usage(source: str, name: str = "kernel") -> dict:
         m = re.search(r"(\d+) bytes spill stores, (\d+) bytes spill loads", line)
         if m:
             cur["spill_stores"], cur["spill_loads"] = int(m.group(1)), int(m.group(2))
-    tmp = path.with_suffix(path.suffix + f".tmp{os.getpid()}")
+    tmp = path.with_suffix(path.suffix + f".tmp{os.getpid()}.{threading.get_ident()}")
     tmp.write_text(json.dumps(out))
     os.replace(tmp, path)
     return out
