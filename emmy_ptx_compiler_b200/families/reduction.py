@@ -262,15 +262,16 @@ def _vector_layout(plan: ReductionPlan, shapes, dtypes) -> tuple[bool, list[str]
 
 
 def _pick_chunks(rows: int, klen: int) -> tuple[int, int]:
-    """Chunks per row: one CTA per row when the rows fill two waves of CTAs;
-    two chunks from half a wave of rows up (1024 and 2048 rows of 65536 f32:
-    5.9 and 6.2 TB/s, against 5.4 and 5.8 with one CTA per row); below that as
-    many chunks as fill one wave, each at least MIN_CHUNK long."""
+    """Chunks per row: rows of at least two MIN_CHUNKs split in two from half
+    a wave of rows up (8192, 4096, 2048 and 1024 rows of 65536 f32: 6.9, 6.7,
+    6.2 and 5.9 TB/s against 6.5, 6.5, 5.8 and 5.4 with one CTA per row; four
+    chunks measured below two); fewer rows split into as many chunks as fill
+    one wave, each at least MIN_CHUNK long."""
     target = SM_COUNT * BLOCKS_PER_SM
-    if rows >= 2 * target or klen <= MIN_CHUNK:
+    if klen <= MIN_CHUNK:
         return 1, klen
     if rows >= target // 2:
-        ch = min(2, max(1, klen // MIN_CHUNK))
+        ch = min(2, klen // MIN_CHUNK)
         if ch == 1:
             return 1, klen
     else:
