@@ -354,3 +354,29 @@ def test_cooperative_attention_without_a_schedule_still_compiles(monkeypatch):
     assert b["family"] == "attention" and b["notes"]["exchange"] == "grid"
     assert b["notes"]["entries"]["drop_in_path"].startswith("reports EMMY_STATUS_BAD_LAUNCH")
     assert b["cubin"][:4] == b"\x7fELF"
+
+
+def test_reduction_chunking_rule():
+    """Rows of two MIN_CHUNKs or more split in two chunks from half a wave of
+    rows up; a full-array reduction splits into one chunk per CTA slot; short
+    rows stay whole."""
+    from emmy_ptx_compiler_b200.families import reduction
+    assert reduction._pick_chunks(8192, 65536) == (2, 32768)     # C3
+    assert reduction._pick_chunks(1024, 65536) == (2, 32768)     # C3's 8-GPU shard
+    assert reduction._pick_chunks(65536, 4096) == (1, 4096)      # rows too short to split
+    ch, length = reduction._pick_chunks(1, 1 << 31)              # C4
+    assert ch == 1184 and ch * length >= 1 << 31 and length % 128 == 0
+
+
+def test_pointwise_tiles_size_the_grid_from_the_range():
+    """The vector path runs one CTA per 4 x 256 float4 tile: the record asks for
+    EMMY_LR_GRID_UNITS with 4096 cells per CTA (a range launch gets one CTA per
+    tile of its range), 256-thread blocks, and no occupancy fill."""
+    from emmy_ptx_compiler_b200 import compiler
+    from emmy_ptx_compiler_b200.families.common import FLAG_GRID_UNITS
+    b = compiler.compile_bundle(next((CASES / "c2_gelu_full").glob("*.ir.json")))
+    assert b["notes"]["order"] == "tile"
+    assert b["launch"]["block"] == [256, 1, 1] and b["launch"]["grid"][0] == (1 << 28) // 4096
+    flags = int(b["source"].split("EMMY_LR_VERSION, 1u, ")[1].split("u")[0])
+    assert flags & FLAG_GRID_UNITS and not flags & 0x100
+    assert "4096u," in b["source"].split("emmy_launch_record = {")[1]
