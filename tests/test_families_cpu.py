@@ -380,3 +380,17 @@ def test_pointwise_tiles_size_the_grid_from_the_range():
     flags = int(b["source"].split("EMMY_LR_VERSION, 1u, ")[1].split("u")[0])
     assert flags & FLAG_GRID_UNITS and not flags & 0x100
     assert "4096u," in b["source"].split("emmy_launch_record = {")[1]
+
+
+def test_launch_record_flags_match_the_header():
+    """The flag bits the Python side emits are the ones the C header defines."""
+    import re
+    from emmy_ptx_compiler_b200.families import common
+    hdr = (REPO / "include" / "emmy_launch_record.h").read_text()
+    defs = {m.group(1): int(m.group(2), 16) for m in re.finditer(r"#define EMMY_LR_(\w+) 0x([0-9A-Fa-f]+)u", hdr)}
+    assert defs["FILL_GRID"] == common.FLAG_FILL_GRID
+    assert defs["RANGE"] == common.FLAG_RANGE
+    assert defs["GRID_UNITS"] == common.FLAG_GRID_UNITS
+    assert defs["COOPERATIVE"] == common.FLAG_COOPERATIVE
+    flags = [common.FLAG_FILL_GRID, common.FLAG_RANGE, common.FLAG_GRID_UNITS, common.FLAG_COOPERATIVE]
+    assert all(f & 0xFF == 0 for f in flags) and len(set(flags)) == len(flags)   # clear of the cluster-size byte
